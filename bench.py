@@ -1,0 +1,175 @@
+"""Headline benchmark: decode output tokens/s per box with k=5 hybrid speculation.
+
+Workload: Llama-3-8B-shaped decoder, bf16 random init
+N(0, 0.02), a 1-layer EAGLE-style draft head of the same width, k = 5 greedy
+hybrid speculation (native drafts mixed with the suffix corpus by the native
+mixer), 64 concurrent requests with synthetic 2048-token prompts (config-0
+span-reuse structure, vocab 128256), up to 512 output tokens each.  On N GPUs
+the model runs tensor-parallel over N ranks (one process per GPU, NCCL).
+
+Timed region: K decode steps after W warm-up steps, bracketed by a barrier
+and a device synchronize.  `value` is output tokens / summed device time of
+the steps (CUDA events from the H2D of a step's inputs to the D2H of its
+results, max over ranks).  `e2e` is the same tokens over the wall clock of
+the K `LLMEngine.step()` calls, which include the host proposer, the H2D of
+each step's inputs from pinned memory and the D2H of its results.  The
+per-step working set (16 GB of weights + the KV cache) is far larger than the
+126 MB L2, so no L2 flush is inserted between steps.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+import argparse
+import json
+import os
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def reference_arm(args):
+    why = ("reference build backend unavailable offline: the reference is a maturin (Rust/PyO3) package and "
+           "neither maturin nor cargo is installed; its native module suffix_hybrid._native cannot be built, "
+           "and the plugin needs vLLM at its pinned revision")
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="llama3-8b")
+    ap.add_argument("--method", default="hybrid")
+    ap.add_argument("--split", default="legacy")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prompt-len", type=int, default=2048)
+    ap.add_argument("--max-new", type=int, default=512)
+    ap.add_argument("--k", type=int, default=5)
+    ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for bench)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from vllm_suffix_hybrid_b200 import ops
+    from vllm_suffix_hybrid_b200.bench.synthetic import make_streams
+    from vllm_suffix_hybrid_b200.engine.config import PRESETS, CacheConfig, EngineConfig, ParallelConfig, SpecConfig
+    from vllm_suffix_hybrid_b200.engine.llm import LLMEngine
+    from vllm_suffix_hybrid_b200.parallel import state as pstate
+    from vllm_suffix_hybrid_b200.utils.clocks import ClockSampler
+
+    st = pstate.init(tp=args.gpus)
+    rank, world = st.rank, st.world
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
+    mcfg = PRESETS[args.config]()
+    if args.layers:
+        mcfg.layers = args.layers
+    cfg = EngineConfig(model=mcfg, spec=SpecConfig(method=args.method, k=args.k, split=args.split),
+                       parallel=ParallelConfig(tp=args.gpus),
+                       cache=CacheConfig(max_model_len=args.prompt_len + args.max_new + 4 * args.k + 64),
+                       max_num_seqs=args.batch, device="cuda", cuda_graphs=not args.no_graphs)
+    if args.split == "diverge":
+        os.environ["SUFFIX_HYBRID_SPLIT"] = "diverge"
+    eng = LLMEngine(cfg)
+    prompts = make_streams(args.batch, args.prompt_len, mcfg.vocab, seed=1234)
+    for p in prompts:
+        eng.add_request(p, args.max_new)
+    t_pf = time.perf_counter()
+    while eng.waiting:
+        eng.step()
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t_pf
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=st.cpu_group)
+
+    for _ in range(args.warmup):
+        eng.step()
+    # Kernel launches of this framework per decode step (one eager step, counted).
+    n_launch_step = 0
+    if cfg.cuda_graphs:
+        r = eng.runner
+        ctr = ops.count_launches(True)
+        r._decode_body(len(eng.running) if len(eng.running) in r.graphs else max(r.graphs))
+        ops.count_launches(False)
+        n_launch_step = ctr.count
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler()
+    if rank == 0:
+        clocks.start()
+    torch.cuda.synchronize()
+    barrier()
+    first = len(eng.stats)
+    t0 = time.perf_counter()
+    dev_ms = 0.0
+    h2d = d2h = 0
+    for _ in range(args.steps):
+        s = eng.step()
+        assert s.kind == "decode", s
+        dev_ms += eng.runner.last_device_ms
+        h2d += eng.runner.h2d_bytes
+        d2h += eng.runner.d2h_bytes
+    torch.cuda.synchronize()
+    barrier()
+    wall = time.perf_counter() - t0
+    clk = clocks.stop(gpus=list(range(world))) if rank == 0 else {}
+    steps = eng.stats[first:]
+    tokens = sum(s.emitted for s in steps)
+    rows = sum(s.num_reqs for s in steps)
+    prop_us = sum(s.proposer_us for s in steps) / len(steps)
+    t = torch.tensor([dev_ms, wall], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=st.group)
+    dev_ms, wall = float(t[0]), float(t[1])
+    if rank == 0:
+        value = tokens / (dev_ms / 1e3)
+        e2e = tokens / wall
+        out = {
+            "metric": "decode out tok/s/box w/ k=5 hybrid spec (max over ranks); mean accept len; us/step",
+            "value": round(value, 1),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dev_ms / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (config-0 span-reuse token streams, vocab 128256); random-init weights N(0,0.02)",
+            "config": {"model": "llama3-8b-shape" if args.config == "llama3-8b" else args.config,
+                       "global_batch": args.batch, "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
+                       "k": args.k, "method": args.method, "split": args.split, "parallelism": f"tp{world}",
+                       "l2": "working set (weights + KV) >> 126 MB L2; no flush",
+                       "layers": mcfg.layers},
+            "mean_accept_len": round(tokens / rows, 4),
+            "proposer_us_per_step": round(prop_us, 2),
+            "prefill_s": round(prefill_s, 2),
+            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d // args.steps,
+                    "d2h_bytes_per_step": d2h // args.steps, "api": "LLMEngine.step"},
+            "gpu_launches": n_launch_step * args.steps,
+            "clocks": clk,
+            "impl": "ours",
+        }
+        if args.layers:
+            out["invalid"] = "layer count overridden (debug run)"
+        print(json.dumps(out))
+    if world > 1:
+        eng.runner.graphs.clear()
+        torch.cuda.synchronize()
+        pstate.shutdown()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+// Greedy sampling and fused draft verification.
+//
+//  * argmax_rows: first-occurrence argmax per logits row (matches
+//    torch.argmax), one CTA per row, 16-byte vector loads.
+//  * spec_verify: the on-device greedy verify + commit step.  For request b
+//    the verify window holds [x_L, d_1..d_k] at positions L..L+k and the
+//    target's argmax t_0..t_k.  accept a = longest prefix with d_i == t_{i-1}
+//    (a -1 pad never matches); emitted tokens are d_1..d_a followed by the
+//    bonus t_a; the committed length becomes L + a + 1 and the next window
+//    starts with t_a.  Stale cache entries past the committed length are
+//    never read (attention is bounded by the sequence length) and are
+//    overwritten by the next window, so no cache copy is needed.  Semantics
+//    of the accept run match the reference's greedy verify oracle
+//    (reference: src/verify_fusion.rs:48-113).
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace shk {
+
+template <typename T, int VEC>
+__global__ void argmax_rows_kernel(int64_t* __restrict__ out, const T* __restrict__ logits, int64_t vocab,
+                                   int64_t stride) {
+  const T* row = logits + (int64_t)blockIdx.x * stride;
+  float best = -INFINITY;
+  int64_t idx = 0x7fffffffffffffffll;
+  const int64_t nvec = vocab / VEC;
+  for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
+    T buf[VEC];
+    *reinterpret_cast<float4*>(buf) = reinterpret_cast<const float4*>(row)[v];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float f = to_f(buf[j]);
+      if (f > best) {  // strict: earliest index wins within a thread's ascending walk
+        best = f;
+        idx = v * VEC + j;
+      }
+    }
+  }
+  for (int64_t v = nvec * VEC + threadIdx.x; v < vocab; v += blockDim.x) {
+    const float f = to_f(row[v]);
+    if (f > best || (f == best && v < idx)) {
+      best = f;
+      idx = v;
+    }
+  }
+  // Reduce (max value, then smallest index).
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ob > best || (ob == best && oi < idx)) {
+      best = ob;
+      idx = oi;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int64_t si[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    sb[warp] = best;
+    si[warp] = idx;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sb[lane] : -INFINITY;
+    idx = lane < nw ? si[lane] : 0x7fffffffffffffffll;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ob > best || (ob == best && oi < idx)) {
+        best = ob;
+        idx = oi;
+      }
+    }
+    if (lane == 0) out[blockIdx.x] = idx == 0x7fffffffffffffffll ? 0 : idx;
+  }
+}
+
+// One thread per request.
+__global__ void spec_verify_kernel(const int64_t* __restrict__ draft, const int64_t* __restrict__ target,
+                                   int64_t* __restrict__ seq_lens, int64_t* __restrict__ out_tokens,
+                                   int32_t* __restrict__ accept, int64_t* __restrict__ next_token, int batch, int k) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const int64_t* d = draft + (int64_t)b * k;
+  const int64_t* t = target + (int64_t)b * (k + 1);
+  int a = 0;
+  while (a < k && d[a] >= 0 && d[a] == t[a]) ++a;
+  int64_t* o = out_tokens + (int64_t)b * (k + 1);
+  for (int i = 0; i < a; ++i) o[i] = d[i];
+  o[a] = t[a];
+  for (int i = a + 1; i <= k; ++i) o[i] = -1;
+  accept[b] = a;
+  next_token[b] = t[a];
+  seq_lens[b] += a + 1;
+}
+
+}  // namespace shk
+
+using namespace shk;
+
+void argmax_rows(torch::Tensor out, torch::Tensor logits) {
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "argmax_rows: logits [T, V]");
+  TORCH_CHECK(out.scalar_type() == at::kLong && out.numel() == logits.size(0), "argmax_rows: out int64 [T]");
+  const int64_t rows = logits.size(0), vocab = logits.size(1);
+  if (rows == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const bool aligned = (reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0) &&
+                       (logits.stride(0) * logits.element_size()) % 16 == 0;
+  TORCH_CHECK(aligned, "argmax_rows: logits rows must start on 16-byte boundaries");
+  if (logits.scalar_type() == at::kBFloat16) {
+    argmax_rows_kernel<__nv_bfloat16, 8><<<rows, 512, 0, stream>>>(
+        out.data_ptr<int64_t>(), (const __nv_bfloat16*)logits.data_ptr(), vocab, logits.stride(0));
+  } else if (logits.scalar_type() == at::kFloat) {
+    argmax_rows_kernel<float, 4><<<rows, 512, 0, stream>>>(out.data_ptr<int64_t>(), logits.data_ptr<float>(), vocab,
+                                                           logits.stride(0));
+  } else {
+    TORCH_CHECK(false, "argmax_rows: bf16 or f32 logits");
+  }
+  SH_CUDA_CHECK(cudaGetLastError());
+}
+
+void spec_verify(torch::Tensor draft, torch::Tensor target, torch::Tensor seq_lens, torch::Tensor out_tokens,
+                 torch::Tensor accept, torch::Tensor next_token) {
+  TORCH_CHECK(draft.scalar_type() == at::kLong && target.scalar_type() == at::kLong, "spec_verify: int64 tokens");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kLong && accept.scalar_type() == at::kInt, "spec_verify: dtypes");
+  TORCH_CHECK(draft.is_contiguous() && target.is_contiguous() && out_tokens.is_contiguous(), "contiguous");
+  const int batch = draft.size(0), k = draft.size(1);
+  TORCH_CHECK(target.size(0) == batch && target.size(1) == k + 1, "target must be [B, k+1]");
+  if (batch == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  spec_verify_kernel<<<(batch + 127) / 128, 128, 0, stream>>>(
+      draft.data_ptr<int64_t>(), target.data_ptr<int64_t>(), seq_lens.data_ptr<int64_t>(),
+      out_tokens.data_ptr<int64_t>(), accept.data_ptr<int32_t>(), next_token.data_ptr<int64_t>(), batch, k);
+  SH_CUDA_CHECK(cudaGetLastError());
+}

@@ -1,0 +1,282 @@
+"""Public engine API: add requests, step, generate.
+
+A step either prefills newly admitted requests (all of them, in chunks of
+``max_prefill_tokens``) or runs one speculative decode step for every
+running request.  After each step the proposer picks the next drafts:
+
+* ``hybrid``  -- native drafts (EAGLE/MTP head) mixed with the suffix corpus
+  by the native HybridMixer (legacy split or diverge), fed the verified
+  accepted lengths;
+* ``native``  -- native drafts only;
+* ``suffix``  -- drafter-free V2SuffixProposer (uniform-k pallet);
+* ``ngram``   -- weight-free Engine (suffix corpus + in-request n-gram);
+* ``none``    -- plain one-token decode.
+
+Running requests occupy rows 0..B-1 of the host token buffer in batch order
+(a finished request's row is back-filled by the last one), so the proposers
+read every context in place.
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+from .. import _native
+from ..models import build_model
+from ..parallel import state as pstate
+from .config import EngineConfig, apply_env
+from .kv_cache import BlockPool, allocate_caches, blocks_for
+from .runner import Runner
+
+
+@dataclass
+class Request:
+    rid: str
+    prompt: np.ndarray
+    max_new_tokens: int
+    output: List[int] = field(default_factory=list)
+    blocks: List[int] = field(default_factory=list)
+    committed: int = 0  # KV positions written and verified
+    next_token: int = -1  # bonus token waiting for the next window
+    drafts: List[int] = field(default_factory=list)
+    accepted_prev: int = -1  # accepted length of the previous proposal (-1 = none)
+    finished: bool = False
+    arrival: float = 0.0
+
+    @property
+    def history_len(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+
+@dataclass
+class StepStats:
+    kind: str
+    num_reqs: int
+    emitted: int
+    accepted: int
+    device_ms: float
+    host_ms: float
+    proposer_us: float
+
+
+class LLMEngine:
+    def __init__(self, cfg: EngineConfig):
+        self.cfg = apply_env(cfg)
+        st = pstate.get()
+        dev = cfg.device
+        if torch.device(dev).type == "cuda":
+            dev = f"cuda:{st.local_rank}" if ":" not in dev else dev
+            torch.cuda.set_device(torch.device(dev))
+        self.device = dev
+        torch.manual_seed(cfg.seed)
+        mcfg = cfg.model
+        spec = cfg.spec
+        self.k = spec.k if spec.method != "none" else 0
+        self.model, self.draft = build_model(mcfg, dev, cfg.seed, with_draft=spec.method in ("hybrid", "native"))
+        if cfg.weights:
+            from .loader import load_weights
+
+            load_weights(self.model, self.draft, cfg.weights)
+        bs = cfg.cache.block_size
+        self.block_size = bs
+        self.max_model_len = cfg.cache.max_model_len
+        self.max_blocks_per_seq = blocks_for(self.max_model_len + 2 * self.k + 2, bs)
+        num_blocks = cfg.cache.num_blocks or self._auto_blocks()
+        self.pool = BlockPool(num_blocks)
+        shape = self.model.kv_cache_shape(num_blocks, bs)
+        self.caches = allocate_caches(mcfg.layers, shape, self.model.dtype, dev)
+        self.dcaches = allocate_caches(1, shape, self.model.dtype, dev)[0] if self.draft is not None else None
+        self.runner = Runner(self.model, self.draft, self.caches, self.dcaches, self.k, cfg.max_num_seqs,
+                             self.max_blocks_per_seq, bs, dev, cfg.cuda_graphs)
+        self.tokens = np.zeros((cfg.max_num_seqs, self.max_model_len + 2 * self.k + 2), dtype=np.int64)
+        self.running: List[Request] = []
+        self.waiting: List[Request] = []
+        self.finished: Dict[str, Request] = {}
+        self._ids = itertools.count()
+        self.stats: List[StepStats] = []
+        self.proposer = None
+        k = max(self.k, 1)
+        if spec.method == "hybrid":
+            self.proposer = _native.HybridMixer(k, self.tokens.shape[1])
+        elif spec.method == "suffix":
+            self.proposer = _native.V2SuffixProposer(k, self.tokens.shape[1], spec.min_len, spec.uniform_k,
+                                                    spec.width_gate)
+        elif spec.method == "ngram":
+            self.proposer = _native.Engine(k, self.tokens.shape[1])
+
+    # ------------------------------------------------------------------ sizing
+    def _auto_blocks(self) -> int:
+        c = self.cfg
+        need = c.max_num_seqs * (self.max_blocks_per_seq + 1) + 8
+        if torch.device(self.device).type != "cuda":
+            return need
+        free, _ = torch.cuda.mem_get_info()
+        m = self.model
+        per_block = 2 * self.block_size * m.kv_heads_local * c.model.head_dim * m.embed.element_size()
+        per_block *= c.model.layers + (1 if self.draft is not None else 0)
+        budget = int(free * c.cache.gpu_memory_fraction) - (4 << 30)
+        return max(need, min(budget // per_block, 4 * need))
+
+    # ------------------------------------------------------------------ API
+    def add_request(self, prompt, max_new_tokens: int = 128, rid: Optional[str] = None) -> str:
+        rid = rid if rid is not None else f"req-{next(self._ids)}"
+        p = np.asarray(prompt, dtype=np.int64)
+        if len(p) == 0 or len(p) + max_new_tokens > self.max_model_len:
+            raise ValueError("prompt empty or prompt + max_new_tokens exceeds max_model_len")
+        self.waiting.append(Request(rid, p, max_new_tokens, arrival=time.time()))
+        return rid
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def step(self) -> StepStats:
+        free_rows = self.cfg.max_num_seqs - len(self.running)
+        if self.waiting and free_rows > 0:
+            return self._prefill_step(free_rows)
+        return self._decode_step()
+
+    def generate(self, prompts, max_new_tokens: int = 128) -> List[List[int]]:
+        rids = [self.add_request(p, max_new_tokens) for p in prompts]
+        while self.has_work():
+            self.step()
+        return [self.finished[r].output for r in rids]
+
+    def spec_stats(self) -> dict:
+        dec = [s for s in self.stats if s.kind == "decode"]
+        steps = sum(s.num_reqs for s in dec)
+        emitted = sum(s.emitted for s in dec)
+        return {
+            "decode_steps": len(dec),
+            "mean_accept_len": emitted / steps if steps else 0.0,
+            "proposer_us_per_step": (sum(s.proposer_us for s in dec) / len(dec)) if dec else 0.0,
+        }
+
+    # ------------------------------------------------------------------ internals
+    def _ensure_blocks(self, r: Request, upto_tokens: int) -> None:
+        need = blocks_for(upto_tokens, self.block_size) - len(r.blocks)
+        if need > 0:
+            r.blocks.extend(self.pool.allocate(need))
+
+    def _prefill_step(self, free_rows: int) -> StepStats:
+        t0 = time.perf_counter()
+        batch, budget = [], self.cfg.max_prefill_tokens
+        while self.waiting and len(batch) < free_rows:
+            r = self.waiting[0]
+            if batch and len(r.prompt) > budget:
+                break
+            self.waiting.pop(0)
+            batch.append(r)
+            budget -= len(r.prompt)
+        for r in batch:
+            self._ensure_blocks(r, len(r.prompt) + 2 * self.k + 2)
+        first, natives = self.runner.prefill([r.prompt for r in batch], [r.blocks for r in batch])
+        for i, r in enumerate(batch):
+            row = len(self.running)
+            self.running.append(r)
+            self.tokens[row, :len(r.prompt)] = r.prompt
+            r.committed = len(r.prompt)
+            self._emit(r, row, [int(first[i])])
+            r.drafts = [int(x) for x in natives[i][: self.k]]
+        t1 = time.perf_counter()
+        prop_us = self._propose(batch_native=True)
+        self._retire()
+        st = StepStats("prefill", len(batch), len(batch), 0, (t1 - t0) * 1e3, 0.0, prop_us)
+        self.stats.append(st)
+        return st
+
+    def _emit(self, r: Request, row: int, toks: List[int]) -> None:
+        room = r.max_new_tokens - len(r.output)
+        toks = toks[:room]
+        n0 = r.history_len
+        self.tokens[row, n0:n0 + len(toks)] = toks
+        r.output.extend(toks)
+        r.next_token = toks[-1] if toks else r.next_token
+        if len(r.output) >= r.max_new_tokens or r.history_len + 2 * self.k + 2 >= self.max_model_len:
+            r.finished = True
+
+    def _propose(self, batch_native: bool) -> float:
+        """Replace each running request's drafts by the proposer's choice."""
+        t0 = time.perf_counter_ns()
+        n = len(self.running)
+        if n == 0 or self.proposer is None or self.k == 0:
+            return 0.0
+        method = self.cfg.spec.method
+        ids = [r.rid for r in self.running]
+        counts = np.fromiter((r.history_len for r in self.running), dtype=np.int64, count=n)
+        if method == "hybrid":
+            acc = [r.accepted_prev for r in self.running]
+            drafts = self.proposer.mix_numpy(ids, counts, self.tokens, [r.drafts for r in self.running],
+                                             acc if any(a >= 0 for a in acc) else None)
+        elif method == "suffix":
+            packed, widths = self.proposer.propose_suffix_only(ids, np.arange(n, dtype=np.int64), counts,
+                                                               self.tokens)
+            drafts = [list(packed[i, : widths[i]]) for i in range(n)]
+        else:  # ngram
+            drafts = self.proposer.propose([[1]] * n, counts, self.tokens)
+        for r, d in zip(self.running, drafts):
+            r.drafts = [int(x) for x in d]
+        return (time.perf_counter_ns() - t0) / 1e3
+
+    def _decode_step(self) -> StepStats:
+        t0 = time.perf_counter()
+        n = len(self.running)
+        if n == 0:
+            return StepStats("idle", 0, 0, 0, 0.0, 0.0, 0.0)
+        k, W = self.k, self.k + 1
+        win = np.full((n, W), 0, dtype=np.int64)
+        seq = np.empty(n, dtype=np.int64)
+        mb = self.max_blocks_per_seq
+        bt = np.zeros((n, mb), dtype=np.int32)
+        for i, r in enumerate(self.running):
+            self._ensure_blocks(r, r.committed + 2 * k + 2)
+            win[i, 0] = r.next_token
+            d = r.drafts[:k]
+            win[i, 1:1 + len(d)] = d
+            if len(d) < k:
+                win[i, 1 + len(d):] = -1
+            seq[i] = r.committed
+            bt[i, :len(r.blocks)] = r.blocks
+        t1 = time.perf_counter()
+        out, acc, nat = self.runner.decode(n, win, seq, bt)
+        t2 = time.perf_counter()
+        emitted = 0
+        accepted = 0
+        for i, r in enumerate(self.running):
+            a = int(acc[i])
+            toks = out[i, : a + 1].tolist()
+            r.committed += a + 1
+            r.accepted_prev = a
+            self._emit(r, i, toks)
+            emitted += min(a + 1, len(toks))
+            accepted += a
+            if self.draft is not None and k > 0:
+                r.drafts = nat[i, :k].tolist()
+        prop_us = self._propose(batch_native=False)
+        self._retire()
+        t3 = time.perf_counter()
+        st = StepStats("decode", n, emitted, accepted, (t2 - t1) * 1e3, (t3 - t2 + t1 - t0) * 1e3, prop_us)
+        self.stats.append(st)
+        return st
+
+    def _retire(self) -> None:
+        """Move finished requests out; back-fill their token rows."""
+        i = 0
+        while i < len(self.running):
+            r = self.running[i]
+            if not r.finished:
+                i += 1
+                continue
+            self.pool.release(r.blocks)
+            r.blocks = []
+            self.finished[r.rid] = r
+            last = len(self.running) - 1
+            if i != last:
+                mv = self.running[last]
+                self.tokens[i, : mv.history_len] = self.tokens[last, : mv.history_len]
+                self.running[i] = mv
+            self.running.pop()

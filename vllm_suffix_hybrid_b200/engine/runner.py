@@ -1,0 +1,225 @@
+"""Model runner: prefill and the fused verify + draft decode step.
+
+Decode step for a batch of B requests, each with a verify window
+[t_prev, d_1..d_k] at positions L..L+k (L = committed cache length):
+
+  1. target forward over the B*(k+1) window tokens (writes their KV);
+  2. greedy target tokens (vocab-parallel argmax, no logits gather);
+  3. spec_verify kernel: accept run, emitted tokens, bonus, L += a + 1;
+  4. draft pass 1 over the same window (features = target pre-norm hidden,
+     tokens = the verified next tokens) -> first native draft from row a;
+  5. k-1 single-token draft steps -> native drafts [B, k].
+
+Everything after the host upload is static-shape per batch bucket, so the
+whole step is captured once per bucket as a CUDA graph and replayed.
+Padded rows of a bucket point at the reserved scratch block 0.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..models.common import AttnMeta
+from .kv_cache import blocks_for
+
+BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+
+
+def bucket_for(n: int, max_batch: int) -> int:
+    for b in BUCKETS:
+        if b >= n and b <= max_batch:
+            return b
+    return max_batch
+
+
+class Runner:
+    def __init__(self, model, draft, caches, draft_caches, k: int, max_batch: int, max_blocks: int,
+                 block_size: int, device, use_graphs: bool):
+        self.model, self.draft = model, draft
+        self.caches, self.dcaches = caches, draft_caches
+        self.k = k
+        self.W = k + 1
+        self.max_batch = max_batch
+        self.max_blocks = max_blocks
+        self.bs = block_size
+        self.device = device
+        self.use_graphs = use_graphs and torch.device(device).type == "cuda"
+        self.group = model.cfg.heads // model.cfg.kv_heads
+        B, W = max_batch, self.W
+        L = dict(dtype=torch.long, device=device)
+        # Static device inputs / outputs of the decode step.
+        self.win = torch.zeros(B, W, **L)
+        self.seq = torch.zeros(B, **L)  # committed length L before the window
+        self.bt = torch.zeros(B, max_blocks, dtype=torch.int32, device=device)
+        self.target = torch.zeros(B, W, **L)
+        self.out_tokens = torch.zeros(B, W, **L)
+        self.accept = torch.zeros(B, dtype=torch.int32, device=device)
+        self.next_tok = torch.zeros(B, **L)
+        self.native = torch.zeros(B, max(k, 1), **L)
+        self.seq_new = torch.zeros(B, **L)
+        self.ar_w = torch.arange(W, **L)
+        self.ar_b = torch.arange(B, **L)
+        pin = torch.device(device).type == "cuda"
+        # Pinned host staging (H2D inputs, D2H results).
+        self.h_win = torch.zeros(B, W, dtype=torch.long, pin_memory=pin)
+        self.h_seq = torch.zeros(B, dtype=torch.long, pin_memory=pin)
+        self.h_bt = torch.zeros(B, max_blocks, dtype=torch.int32, pin_memory=pin)
+        self.h_out = torch.zeros(B, W, dtype=torch.long, pin_memory=pin)
+        self.h_acc = torch.zeros(B, dtype=torch.int32, pin_memory=pin)
+        self.h_nat = torch.zeros(B, max(k, 1), dtype=torch.long, pin_memory=pin)
+        self._tiles: Dict[tuple, tuple] = {}
+        self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        self.event = torch.cuda.Event() if pin else None
+        # Device time of the last decode step (H2D of its inputs .. D2H of its results).
+        self.ev0 = torch.cuda.Event(enable_timing=True) if pin else None
+        self.ev1 = torch.cuda.Event(enable_timing=True) if pin else None
+        self.last_device_ms = 0.0
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+
+    # ------------------------------------------------------------------ helpers
+    def _tile_tensors(self, nb: int, qlen: int):
+        key = (nb, qlen)
+        if key not in self._tiles:
+            req, row0 = ops.plan_attention_tiles([qlen] * nb, self.group // max(1, 1))
+            qs = torch.arange(nb + 1, dtype=torch.long, device=self.device) * qlen
+            self._tiles[key] = (torch.tensor(req, dtype=torch.int32, device=self.device),
+                                torch.tensor(row0, dtype=torch.int32, device=self.device), qs)
+        return self._tiles[key]
+
+    def _slots(self, bt: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """pos [B, n] -> cache slots via the block table."""
+        blk = bt.long().gather(1, torch.div(pos, self.bs, rounding_mode="floor"))
+        return blk * self.bs + pos % self.bs
+
+    def _meta(self, nb: int, qlen: int, pos: torch.Tensor, bt: torch.Tensor, seq_lens: torch.Tensor) -> AttnMeta:
+        tr, t0, qs = self._tile_tensors(nb, qlen)
+        return AttnMeta(positions=pos.reshape(-1), slot_mapping=self._slots(bt, pos).reshape(-1), block_tables=bt,
+                        seq_lens=seq_lens, q_start=qs, tile_req=tr, tile_row0=t0, num_tokens=nb * qlen)
+
+    def _draft_steps(self, d1: torch.Tensor, f1: torch.Tensor, lnew: torch.Tensor, bt: torch.Tensor, nb: int):
+        """Draft tokens 2..k at positions lnew + s - 2 (s = 2..k)."""
+        drafts = [d1]
+        d, f = d1, f1
+        for s in range(2, self.k + 1):
+            pos = (lnew + (s - 2))[:, None]
+            meta = self._meta(nb, 1, pos, bt, pos[:, 0] + 1)
+            h, f = self.draft.forward(d, f, meta, self.dcaches)
+            d = self.model.greedy(h)
+            drafts.append(d)
+        return torch.stack(drafts, 1)
+
+    # ------------------------------------------------------------------ decode
+    def _decode_body(self, nb: int) -> None:
+        W = self.W
+        win, L, bt = self.win[:nb], self.seq[:nb], self.bt[:nb]
+        pos = L[:, None] + self.ar_w[None, :]
+        meta = self._meta(nb, W, pos, bt, L + W)
+        hid, pre = self.model.forward(win.reshape(-1), meta, self.caches)
+        self.target[:nb].copy_(self.model.greedy(hid).view(nb, W))
+        lnew = self.seq_new[:nb]
+        lnew.copy_(L)
+        if self.k > 0:
+            ops.spec_verify(win[:, 1:].contiguous(), self.target[:nb], lnew, self.out_tokens[:nb],
+                            self.accept[:nb], self.next_tok[:nb])
+        else:
+            self.out_tokens[:nb].copy_(self.target[:nb])
+            self.accept[:nb].zero_()
+            self.next_tok[:nb].copy_(self.target[:nb, 0])
+            lnew.add_(1)
+        if self.draft is not None and self.k > 0:
+            tok_in = self.out_tokens[:nb].clamp_min(0)
+            dh, dpre = self.draft.forward(tok_in.reshape(-1), pre, meta, self.dcaches)
+            sel = self.ar_b[:nb] * W + self.accept[:nb].long()
+            d1 = self.model.greedy(dh.index_select(0, sel))
+            f1 = dpre.index_select(0, sel)
+            self.native[:nb].copy_(self._draft_steps(d1, f1, lnew, bt, nb))
+
+    def decode(self, nb_real: int, win: np.ndarray, seq: np.ndarray, bt: np.ndarray):
+        """Run one decode step; returns host views (out_tokens, accept, native)."""
+        nb = bucket_for(nb_real, self.max_batch)
+        self.h_win[:nb_real].numpy()[:] = win
+        self.h_seq[:nb_real].numpy()[:] = seq
+        self.h_bt[:nb_real].numpy()[:, :bt.shape[1]] = bt
+        if nb > nb_real:  # padded rows: scratch block 0, a k+1 window at position 0
+            self.h_win[nb_real:nb] = 0
+            self.h_seq[nb_real:nb] = 0
+            self.h_bt[nb_real:nb] = 0
+        nbt = self.max_blocks
+        if self.ev0 is not None:
+            self.ev0.record()
+        self.win[:nb].copy_(self.h_win[:nb], non_blocking=True)
+        self.seq[:nb].copy_(self.h_seq[:nb], non_blocking=True)
+        self.bt[:nb, :nbt].copy_(self.h_bt[:nb, :nbt], non_blocking=True)
+        if self.use_graphs:
+            g = self.graphs.get(nb)
+            if g is None:
+                g = self._capture(nb)
+            g.replay()
+        else:
+            self._decode_body(nb)
+        self.h_out[:nb].copy_(self.out_tokens[:nb], non_blocking=True)
+        self.h_acc[:nb].copy_(self.accept[:nb], non_blocking=True)
+        if self.draft is not None and self.k > 0:
+            self.h_nat[:nb].copy_(self.native[:nb], non_blocking=True)
+        if self.ev1 is not None:
+            self.ev1.record()
+            self.ev1.synchronize()
+            self.last_device_ms = self.ev0.elapsed_time(self.ev1)
+        self.h2d_bytes = nb * (self.W * 8 + 8 + self.max_blocks * 4)
+        self.d2h_bytes = nb * (self.W * 8 + 4 + (self.k * 8 if self.draft is not None and self.k > 0 else 0))
+        return self.h_out[:nb_real].numpy(), self.h_acc[:nb_real].numpy(), self.h_nat[:nb_real].numpy()
+
+    def _capture(self, nb: int):
+        # Warm up outside capture (allocator pools, lazy module state), then capture.
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._decode_body(nb)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._decode_body(nb)
+        self.graphs[nb] = g
+        return g
+
+    # ------------------------------------------------------------------ prefill
+    def prefill(self, prompts: List[np.ndarray], block_tables: List[List[int]], start: Optional[List[int]] = None):
+        """Prefill a batch of prompts (each fully). Returns (first tokens [n], native drafts [n, k])."""
+        dev = self.device
+        n = len(prompts)
+        lens = [len(p) for p in prompts]
+        ids = torch.from_numpy(np.concatenate(prompts).astype(np.int64)).to(dev, non_blocking=True)
+        pos = torch.from_numpy(np.concatenate([np.arange(l) for l in lens]).astype(np.int64)).to(dev)
+        mb = max(len(b) for b in block_tables)
+        btn = np.zeros((n, mb), dtype=np.int32)
+        for i, b in enumerate(block_tables):
+            btn[i, :len(b)] = b
+        bt = torch.from_numpy(btn).to(dev)
+        req_of_tok = torch.from_numpy(np.concatenate([np.full(l, i) for i, l in enumerate(lens)])).to(dev)
+        blk = bt.long()[req_of_tok, torch.div(pos, self.bs, rounding_mode="floor")]
+        slots = blk * self.bs + pos % self.bs
+        seq_lens = torch.tensor(lens, dtype=torch.long, device=dev)
+        qs = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.long, device=dev)
+        tr, t0 = ops.plan_attention_tiles(lens, self.group)
+        meta = AttnMeta(positions=pos, slot_mapping=slots, block_tables=bt, seq_lens=seq_lens, q_start=qs,
+                        tile_req=torch.tensor(tr, dtype=torch.int32, device=dev),
+                        tile_row0=torch.tensor(t0, dtype=torch.int32, device=dev), num_tokens=int(sum(lens)))
+        hid, pre = self.model.forward(ids, meta, self.caches)
+        last = qs[1:] - 1
+        first = self.model.greedy(hid.index_select(0, last))
+        natives = torch.zeros(n, max(self.k, 1), dtype=torch.long, device=dev)
+        if self.draft is not None and self.k > 0:
+            nxt = torch.empty_like(ids)
+            nxt[:-1] = ids[1:]
+            nxt[last] = first  # the token after each prompt's last position
+            dh, dpre = self.draft.forward(nxt, pre, meta, self.dcaches)
+            d1 = self.model.greedy(dh.index_select(0, last))
+            f1 = dpre.index_select(0, last)
+            natives = self._draft_steps(d1, f1, seq_lens, bt, n)
+        return first.cpu().numpy(), natives.cpu().numpy()

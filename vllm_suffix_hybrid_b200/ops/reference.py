@@ -1,0 +1,103 @@
+"""Plain PyTorch (fp32-accumulating) statements of every kernel's math.
+
+These are the numerics oracles for the CUDA kernels and the execution path
+of the CPU-only toy configuration.  They are written for clarity, not speed.
+"""
+from __future__ import annotations
+
+import torch
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (xf * inv * w.float()).to(x.dtype)
+
+
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> None:
+    s = (x.float() + residual.float()).to(residual.dtype)
+    residual.copy_(s)
+    x.copy_(rms_norm(s, w, eps))
+
+
+def rope_cos_sin(max_pos: int, rot: int, theta: float, device=None) -> torch.Tensor:
+    """[max_pos, rot] float32: cos in the first rot/2 columns, sin in the rest."""
+    inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.float64) / rot))
+    t = torch.arange(max_pos, dtype=torch.float64)
+    f = torch.outer(t, inv)
+    return torch.cat([f.cos(), f.sin()], dim=-1).float().to(device)
+
+
+def apply_rope(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+    """x: [T, H, D]; rotate-half rotary on the first `rot` dims."""
+    rot = cos_sin.shape[1]
+    half = rot // 2
+    cs = cos_sin[positions]
+    c, s = cs[:, None, :half], cs[:, None, half:]
+    xf = x.float()
+    x1, x2 = xf[..., :half], xf[..., half:rot]
+    out = xf.clone()
+    out[..., :half] = x1 * c - x2 * s
+    out[..., half:rot] = x2 * c + x1 * s
+    return out.to(x.dtype)
+
+
+def rope_kv_write(qkv, positions, cos_sin, k_cache, v_cache, slot_mapping, hq, hk, d, rot) -> None:
+    t = qkv.shape[0]
+    q = qkv[:, : hq * d].view(t, hq, d)
+    k = qkv[:, hq * d:(hq + hk) * d].view(t, hk, d)
+    v = qkv[:, (hq + hk) * d:(hq + 2 * hk) * d].view(t, hk, d)
+    q.copy_(apply_rope(q, positions, cos_sin))
+    k.copy_(apply_rope(k, positions, cos_sin))
+    bs = k_cache.shape[2]
+    ok = slot_mapping >= 0
+    slots = slot_mapping[ok]
+    blk, off = slots // bs, slots % bs
+    k_cache[blk, :, off, :] = k[ok]
+    v_cache[blk, :, off, :] = v[ok]
+
+
+def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, hq, scale) -> torch.Tensor:
+    """q: [T, hq, D]; caches [blocks, hk, bs, D]; returns [T, hq, D]."""
+    hk, bs, d = k_cache.shape[1], k_cache.shape[2], k_cache.shape[3]
+    g = hq // hk
+    out = torch.zeros_like(q)
+    for b in range(seq_lens.shape[0]):
+        s0, s1 = int(q_start[b]), int(q_start[b + 1])
+        ql, sl = s1 - s0, int(seq_lens[b])
+        if ql == 0:
+            continue
+        nblk = (sl + bs - 1) // bs
+        blocks = block_tables[b, :nblk].long()
+        k = k_cache[blocks].permute(1, 0, 2, 3).reshape(hk, nblk * bs, d)[:, :sl].float()
+        v = v_cache[blocks].permute(1, 0, 2, 3).reshape(hk, nblk * bs, d)[:, :sl].float()
+        qq = q[s0:s1].float().view(ql, hk, g, d).permute(1, 2, 0, 3)  # [hk, g, ql, d]
+        sc = torch.einsum("hgqd,hkd->hgqk", qq, k) * scale
+        qpos = torch.arange(sl - ql, sl)
+        kpos = torch.arange(sl)
+        mask = kpos[None, :] > qpos[:, None]
+        sc = sc.masked_fill(mask, float("-inf"))
+        p = sc.softmax(-1)
+        o = torch.einsum("hgqk,hkd->hgqd", p, v)  # [hk, g, ql, d]
+        out[s0:s1] = o.permute(2, 0, 1, 3).reshape(ql, hq, d).to(q.dtype)
+    return out
+
+
+def silu_mul(x: torch.Tensor) -> torch.Tensor:
+    f = x.shape[-1] // 2
+    xf = x.float()
+    return (torch.nn.functional.silu(xf[..., :f]) * xf[..., f:]).to(x.dtype)
+
+
+def spec_verify(draft, target, seq_lens):
+    """Greedy accept + commit. Returns (out_tokens, accept, next_token, new_seq_lens)."""
+    b, k = draft.shape
+    eq = (draft == target[:, :k]) & (draft >= 0)
+    accept = torch.cumprod(eq.int(), dim=1).sum(1).int()
+    out = torch.full((b, k + 1), -1, dtype=torch.long, device=draft.device)
+    idx = torch.arange(k + 1, device=draft.device)
+    keep = idx[None, :k] < accept[:, None].long()
+    out[:, :k] = torch.where(keep, draft, out[:, :k])
+    nxt = target.gather(1, accept.long()[:, None])[:, 0]
+    out.scatter_(1, accept.long()[:, None], nxt[:, None])
+    return out, accept, nxt, seq_lens + accept.long() + 1
