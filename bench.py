@@ -51,6 +51,9 @@ def main():
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for bench)")
+    ap.add_argument("--profile", action="store_true",
+                    help="profile one eager decode step between cudaProfilerStart/Stop (for ncu) and exit")
+    ap.add_argument("--dump-tokens", type=int, default=0, help="print the first N generated tokens of row 0")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -95,6 +98,16 @@ def main():
 
     for _ in range(args.warmup):
         eng.step()
+    if args.profile:
+        eng.runner.use_graphs = False
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        eng.step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"profiled_step": True, "num_reqs": len(eng.running)}))
+        return
     # Kernel launches of this framework per decode step (one eager step, counted).
     n_launch_step = 0
     if cfg.cuda_graphs:
@@ -164,6 +177,9 @@ def main():
         }
         if args.layers:
             out["invalid"] = "layer count overridden (debug run)"
+        if args.dump_tokens:
+            r0 = eng.running[0]
+            out["sample_tokens"] = r0.output[: args.dump_tokens]
         print(json.dumps(out))
     if world > 1:
         eng.runner.graphs.clear()

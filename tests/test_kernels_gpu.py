@@ -19,7 +19,7 @@ def _need_cuda():
 
 
 def close(a, b, tol):
-    err = (a.float() - b.float()).abs().max().item()
+    err = (a.detach().float().cpu() - b.detach().float().cpu()).abs().max().item()
     assert err <= tol, f"max abs err {err} > {tol}"
 
 
@@ -43,12 +43,13 @@ def test_fused_add_rms_norm(hidden):
     close(x, x2, 0.06)
 
 
-def _paged_setup(q_lens, ctx_lens, hq, hk, d, nblocks=64, bs=64, dtype=torch.bfloat16):
+def _paged_setup(q_lens, ctx_lens, hq, hk, d, bs=64, dtype=torch.bfloat16):
     B = len(q_lens)
-    k_cache = torch.randn(nblocks, hk, bs, d, device="cuda", dtype=dtype)
-    v_cache = torch.randn(nblocks, hk, bs, d, device="cuda", dtype=dtype)
     seq = [c + q for c, q in zip(ctx_lens, q_lens)]
     maxb = max((s + bs - 1) // bs for s in seq)
+    nblocks = B * maxb + 1
+    k_cache = torch.randn(nblocks, hk, bs, d, device="cuda", dtype=dtype)
+    v_cache = torch.randn(nblocks, hk, bs, d, device="cuda", dtype=dtype)
     perm = torch.randperm(nblocks - 1)[: B * maxb] + 1
     bt = perm.view(B, maxb).int().cuda()
     qs = torch.tensor([0] + list(np.cumsum(q_lens)), dtype=torch.long, device="cuda")

@@ -178,31 +178,21 @@ def spec_verify(draft, target, seq_lens, out_tokens, accept, next_token) -> None
 
 
 # ----------------------------------------------------------------------------- GEMM
+_GEMM_BACKEND = os.environ.get("SH_GEMM", "tcgen05")  # "cublas": library baseline for A/B runs
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """y = x @ w.T for w [N, K] (bf16 on GPU)."""
-    gemm = _gemm_impl()
-    if x.is_cuda and gemm is not None:
-        return gemm(x, w, out)
+    """y = x @ w.T for w [N, K].
+
+    bf16 on a CUDA device runs the tcgen05 GEMM (K must be a multiple of 64);
+    other dtypes (the fp32 toy model) and the CPU use the library matmul.
+    """
+    if x.is_cuda and x.dtype == torch.bfloat16 and _GEMM_BACKEND == "tcgen05":
+        from .gemm import tcgen05_linear
+
+        return tcgen05_linear(x, w, out)
     y = torch.matmul(x, w.t())
     if out is not None:
         out.copy_(y)
         return out
     return y
-
-
-_GEMM = None
-
-
-def _gemm_impl():
-    """The tcgen05 GEMM when built (None -> library matmul, used for the CPU path)."""
-    global _GEMM
-    if _GEMM is None:
-        _GEMM = False
-        if os.environ.get("SH_GEMM", "tcgen05") == "tcgen05":
-            try:
-                from .gemm import tcgen05_linear
-
-                _GEMM = tcgen05_linear
-            except Exception:
-                _GEMM = False
-    return _GEMM or None
