@@ -3,6 +3,7 @@
 #include <torch/extension.h>
 
 #include "gemm_tcgen05.h"
+#include "paged_attention.h"
 
 void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
 void fused_add_rms_norm(torch::Tensor x, torch::Tensor residual, torch::Tensor w, double eps);
@@ -13,9 +14,57 @@ void embedding(torch::Tensor out, torch::Tensor ids, torch::Tensor table);
 void argmax_rows(torch::Tensor out, torch::Tensor logits);
 void spec_verify(torch::Tensor draft, torch::Tensor target, torch::Tensor seq_lens, torch::Tensor out_tokens,
                  torch::Tensor accept, torch::Tensor next_token);
+
+// out[T, hq*D] <- paged GQA attention of the q rows (a view into the QKV
+// projection output) over the [blocks, hk, 64, D] cache.  nsplit > 1 needs
+// part_o [T*hq*nsplit*D] and part_ml [T*hq*nsplit*2] fp32 workspaces.
 void paged_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                      torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
-                     torch::Tensor tile_req, torch::Tensor tile_row0, int64_t hq, double scale);
+                     torch::Tensor tile_req, torch::Tensor tile_row0, int64_t hq, double scale, int64_t nsplit,
+                     c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_ml,
+                     c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16, "paged_attention: bf16 tensors");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == 64 && k_cache.is_contiguous() && v_cache.is_contiguous() &&
+                  v_cache.sizes() == k_cache.sizes(), "paged_attention: caches [blocks, hk, 64, D] contiguous");
+  TORCH_CHECK(q.stride(-1) == 1 && out.stride(-1) == 1 && q.dim() == 2 && out.dim() == 2, "q/out [T, width]");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kLong &&
+                  q_start.scalar_type() == at::kLong && tile_req.scalar_type() == at::kInt &&
+                  tile_row0.scalar_type() == at::kInt, "paged_attention: index dtypes");
+  const int hk = k_cache.size(1), d = k_cache.size(3);
+  TORCH_CHECK(hq % hk == 0 && q.size(1) >= hq * d && out.size(1) >= hq * d, "paged_attention: head layout");
+  TORCH_CHECK((q.stride(0) * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(q.data_ptr()) % 16) == 0,
+              "paged_attention: q rows must be 16-byte aligned");
+  AttnParams p{};
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.out_stride = out.stride(0);
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.q_stride = q.stride(0);
+  p.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  p.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  p.block_tables = block_tables.data_ptr<int32_t>();
+  p.bt_stride = block_tables.stride(0);
+  p.seq_lens = seq_lens.data_ptr<int64_t>();
+  p.q_start = q_start.data_ptr<int64_t>();
+  p.tile_req = tile_req.data_ptr<int32_t>();
+  p.tile_row0 = tile_row0.data_ptr<int32_t>();
+  p.num_tokens = q.size(0);
+  p.hq = static_cast<int>(hq);
+  p.hk = hk;
+  p.nsplit = static_cast<int>(nsplit);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  if (nsplit > 1) {
+    TORCH_CHECK(part_o.has_value() && part_ml.has_value(), "paged_attention: split-KV needs workspaces");
+    TORCH_CHECK(part_o->numel() >= p.num_tokens * hq * nsplit * d && part_ml->numel() >= p.num_tokens * hq * nsplit * 2,
+                "paged_attention: workspace too small");
+    p.part_o = part_o->data_ptr<float>();
+    p.part_ml = part_ml->data_ptr<float>();
+  }
+  p.err = err.has_value() ? err->data_ptr<int>() : nullptr;
+  const int r = sh_paged_attention(&p, static_cast<int>(tile_req.numel()), static_cast<int>(k_cache.size(0)), d,
+                                   at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_paged_attention failed with code ", r);
+}
 
 // y[M, N] = x[M, K] @ w[N, K]^T via the tcgen05 GEMM.  swap: weights take the
 // MMA's 128-row side (small M).  ws: fp32 split-K workspace (>= splits*M*N).
@@ -56,7 +105,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &embedding);
   m.def("argmax_rows", &argmax_rows);
   m.def("spec_verify", &spec_verify);
-  m.def("paged_attention", &paged_attention);
+  m.def("paged_attention", &paged_attention, "paged GQA attention", py::arg("out"), py::arg("q"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("block_tables"), py::arg("seq_lens"), py::arg("q_start"), py::arg("tile_req"),
+        py::arg("tile_row0"), py::arg("hq"), py::arg("scale"), py::arg("nsplit") = 1, py::arg("part_o") = py::none(),
+        py::arg("part_ml") = py::none(), py::arg("err") = py::none());
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM", py::arg("y"), py::arg("x"), py::arg("w"), py::arg("swap"),
         py::arg("bn"), py::arg("splits"), py::arg("ws") = py::none(), py::arg("err") = py::none());
 }

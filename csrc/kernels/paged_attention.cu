@@ -1,35 +1,90 @@
 // Paged GQA attention for prefill, decode and speculative verify.
 //
-// One CTA owns one (request, kv head, 64-row query tile).  A query tile packs
+// Work unit = (64-row query tile, kv head, kv split).  A query tile packs
 // (token, q-head-of-this-group) rows: row r -> token r / G, head h*G + r % G,
-// so the G query heads sharing a kv head (and the k+1 verify tokens of a
-// request) read every K/V page exactly once.  K/V pages are 64 tokens of a
-// [num_blocks, kv_heads, 64, D] cache, streamed through a two-stage cp.async
-// ring into XOR-swizzled shared memory; QK^T and PV run on bf16 tensor-core
-// tiles with fp32 accumulation and an exp2 online softmax.  Causality is by
-// absolute position: the query token at position p sees keys [0, p].
-// Query rows are read in place from the fused QKV projection output.
-#include <ATen/cuda/CUDAContext.h>
-#include <torch/extension.h>
+// so the G query heads sharing a kv head and the k+1 verify tokens of a
+// request read every K/V page once per split.  Each request's pages are cut
+// into `nsplit` equal chunks (split-KV) so short batches still fill the SMs;
+// with nsplit > 1 every unit writes an fp32 partial (normalised O, row max,
+// row sum) to a workspace and attn_merge combines them in split order.
+//
+// Per CTA: warp 0 is a TMA producer streaming 64-token K and V pages of the
+// [num_blocks, kv_heads, 64, D] cache (viewed as 2-D rows of D) in 128-byte
+// swizzled 64-column boxes into a 4-stage mbarrier ring; warps 1..4 each own
+// 16 query rows and run QK^T / PV on bf16 tensor-core tiles (mma.sync
+// m16n8k16, fp32 accumulate) with an exp2 online softmax.  Causality is by
+// absolute position: the query token at position p sees keys [0, p].  Every
+// mbarrier wait is bounded and reports a timeout through *err.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
 
-#include "common.cuh"
+#include "paged_attention.h"
 
 namespace shk {
+namespace attn {
 
-constexpr int kAttnRows = 64;  // query rows per CTA (4 warps x 16)
-constexpr int kAttnKeys = 64;  // keys per page / tile
+constexpr int ROWS = 64;   // query rows per unit
+constexpr int KEYS = 64;   // keys per page
+constexpr int THREADS = 160;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+__device__ __forceinline__ uint32_t saddr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t c) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(c));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t par) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(par)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t par, volatile int* abort_flag) {
+  if (mbar_try(b, par)) return true;
+  const uint64_t t0 = now_ns();
+  while (true) {
+    if (mbar_try(b, par)) return true;
+    if (*abort_flag) return false;
+    if (now_ns() - t0 > kTimeoutNs) return false;
+  }
+}
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* m, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(saddr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* g, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr(smem)), "l"(g), "r"(pred ? 16 : 0));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
+               : "r"(a));
 }
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+__device__ __forceinline__ void ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
+               : "r"(a));
 }
-__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -37,141 +92,164 @@ __device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uin
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Byte offset of 16-byte chunk `c` of row `r` in a swizzled [rows][D] bf16 tile.
-template <int D>
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-  return static_cast<uint32_t>(r * D * 2 + ((c ^ (r & 7)) << 4));
+// A [64 rows][D] bf16 tile stored as D/64 column slabs of [64 rows][128 B],
+// each slab in the TMA 128-byte swizzle: 16-byte chunk c of row r sits at
+// chunk position c ^ (r & 7).  `cc` is the logical 16-byte chunk (0..D/8-1).
+__device__ __forceinline__ uint32_t swz(int r, int cc) {
+  return static_cast<uint32_t>((cc >> 3) * (64 * 128) + r * 128 + (((cc & 7) ^ (r & 7)) << 4));
 }
 
 template <int D>
-__device__ __forceinline__ void load_page(uint8_t* dst, const __nv_bfloat16* src, int valid_keys) {
-  constexpr int CH = D / 8;  // 16-byte chunks per row
-  for (int c = threadIdx.x; c < kAttnKeys * CH; c += blockDim.x) {
-    const int r = c / CH, ch = c % CH;
-    cp_async16(dst + swz<D>(r, ch), src + r * D + ch * 8, r < valid_keys);
-  }
-}
+struct Stages {
+  static constexpr int value = D == 64 ? 8 : (D == 128 ? 4 : 2);  // K/V page ring depth
+};
 
 template <int D>
-__global__ void __launch_bounds__(128) paged_attention_kernel(
-    __nv_bfloat16* __restrict__ out, int64_t out_stride_tok, const __nv_bfloat16* __restrict__ q,
-    int64_t q_stride_tok, const __nv_bfloat16* __restrict__ k_cache, const __nv_bfloat16* __restrict__ v_cache,
-    const int32_t* __restrict__ block_tables, int64_t bt_stride, const int64_t* __restrict__ seq_lens,
-    const int64_t* __restrict__ q_start, const int32_t* __restrict__ tile_req, const int32_t* __restrict__ tile_row0,
-    int hq, int hk, float scale_log2) {
-  constexpr int CH = D / 8;
+__global__ void __launch_bounds__(THREADS, 1)
+    paged_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  constexpr int TILE_BYTES = 64 * D * 2;  // one [64][D] bf16 tile
+  constexpr int STAGES = Stages<D>::value;
   constexpr int KSTEPS = D / 16;
   constexpr int DT = D / 8;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK[2] = {smem + kAttnRows * D * 2, smem + kAttnRows * D * 2 + kAttnKeys * D * 2};
-  uint8_t* sV[2] = {smem + kAttnRows * D * 2 + 2 * kAttnKeys * D * 2,
-                    smem + kAttnRows * D * 2 + 3 * kAttnKeys * D * 2};
+  uint8_t* sKV = smem + TILE_BYTES;  // stage s: K at s*2*TILE, V at s*2*TILE + TILE
+  uint64_t* full = reinterpret_cast<uint64_t*>(sKV + STAGES * 2 * TILE_BYTES);
+  uint64_t* empty = full + STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
 
-  const int b = tile_req[blockIdx.x];
-  const int row0 = tile_row0[blockIdx.x];
-  const int h = blockIdx.y;
-  const int G = hq / hk;
-  const int64_t qs = q_start[b];
-  const int q_len = static_cast<int>(q_start[b + 1] - qs);
-  const int64_t seq_len = seq_lens[b];
-  const int64_t ctx0 = seq_len - q_len;  // absolute position of the first query token
-  const int rows_valid = min(kAttnRows, q_len * G - row0);
+  const int tile = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
+  const int b = p.tile_req[tile];
+  const int row0 = p.tile_row0[tile];
+  const int G = p.hq / p.hk;
+  const int64_t qs = p.q_start[b];
+  const int q_len = static_cast<int>(p.q_start[b + 1] - qs);
+  const int64_t seq_len = p.seq_lens[b];
+  const int64_t ctx0 = seq_len - q_len;
+  const int rows_valid = min(ROWS, q_len * G - row0);
+  const int64_t kv_end = min(seq_len, ctx0 + (row0 + rows_valid - 1) / G + 1);
+  const int npages = static_cast<int>((kv_end + KEYS - 1) / KEYS);
+  const int per = (npages + p.nsplit - 1) / p.nsplit;
+  const int pg0 = min(split * per, npages), pg1 = min(pg0 + per, npages);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t4 = lane & 3;
 
-  // Query rows -> smem (zero-filled past the valid rows).
-  for (int c = threadIdx.x; c < kAttnRows * CH; c += blockDim.x) {
-    const int r = c / CH, ch = c % CH;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 4);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // Query rows -> smem (zero-filled past the valid rows), all threads.
+  for (int c = threadIdx.x; c < ROWS * (D / 8); c += THREADS) {
+    const int r = c / (D / 8), cc = c % (D / 8);
     const bool ok = r < rows_valid;
     const int rr = ok ? row0 + r : row0;
     const int tok = rr / G, head = h * G + rr % G;
-    cp_async16(sQ + swz<D>(r, ch), q + (qs + tok) * q_stride_tok + (int64_t)head * D + ch * 8, ok);
+    cp_async16(sQ + swz(r, cc), p.q + (qs + tok) * p.q_stride + static_cast<int64_t>(head) * D + cc * 8, ok);
   }
-  const int last_row = row0 + rows_valid - 1;
-  const int64_t kv_end = min(seq_len, ctx0 + last_row / G + 1);  // keys any row of this tile may see
-  const int ntiles = static_cast<int>((kv_end + kAttnKeys - 1) / kAttnKeys);
-  const int32_t* bt = block_tables + (int64_t)b * bt_stride;
-  auto page_ptr = [&](const __nv_bfloat16* cache, int j) {
-    return cache + ((int64_t)bt[j] * hk + h) * (int64_t)kAttnKeys * D;
-  };
-  if (ntiles > 0) {
-    const int vk = static_cast<int>(kv_end < kAttnKeys ? kv_end : (int64_t)kAttnKeys);
-    load_page<D>(sK[0], page_ptr(k_cache, 0), vk);
-    load_page<D>(sV[0], page_ptr(v_cache, 0), vk);
-  }
-  cp_async_commit();
-  cp_async_wait<0>();
+  asm volatile("cp.async.commit_group;\n" ::);
+  asm volatile("cp.async.wait_group 0;\n" ::);
   __syncthreads();
 
-  const bool warp_active = warp * 16 < rows_valid;
-  uint32_t qf[KSTEPS][4];
-  if (warp_active) {
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
+      int issued = 0;
+      for (int j = pg0; j < pg1; ++j, ++issued) {
+        const int s = issued % STAGES;
+        const uint32_t ph = (issued / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+          if (p.err) atomicCAS(p.err, 0, 11);
+          *abort_flag = 1;
+          break;
+        }
+        const int y = (bt[j] * p.hk + h) * KEYS;
+        uint8_t* dk = sKV + s * 2 * TILE_BYTES;
+        mbar_expect_tx(&full[s], 2 * TILE_BYTES);
 #pragma unroll
-    for (int kk = 0; kk < KSTEPS; ++kk) {
-      const int r = warp * 16 + (lane & 15);
-      const int ch = 2 * kk + (lane >> 4);
-      ldsm_x4(smem_u32(sQ) + swz<D>(r, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+        for (int slab = 0; slab < D / 64; ++slab) {
+          tma_2d(dk + slab * 64 * 128, &tmK, slab * 64, y, &full[s]);
+          tma_2d(dk + TILE_BYTES + slab * 64 * 128, &tmV, slab * 64, y, &full[s]);
+        }
+      }
+      if (*abort_flag) {  // let every issued load land before exit (bounded)
+        for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i) {
+          const uint64_t t0 = now_ns();
+          while (!mbar_try(&full[i % STAGES], (i / STAGES) & 1))
+            if (now_ns() - t0 > kTimeoutNs) break;
+        }
+      }
     }
+    return;
   }
-  // Absolute positions of this thread's two rows (-1 = padding row).
-  const int ra = warp * 16 + g, rb = ra + 8;
+  // -------------------------------------------------------------- compute
+  const int cw = warp - 1;  // rows cw*16 .. +15
+  const int g = lane >> 2, t4 = lane & 3;
+  const bool active = cw * 16 < rows_valid;
+  uint32_t qf[KSTEPS][4];
+  if (active) {
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk)
+      ldsm_x4(saddr(sQ) + swz(cw * 16 + (lane & 15), 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2],
+              qf[kk][3]);
+  }
+  const int ra = cw * 16 + g, rb = ra + 8;
   const int64_t pa = ra < rows_valid ? ctx0 + (row0 + ra) / G : -1;
   const int64_t pb = rb < rows_valid ? ctx0 + (row0 + rb) / G : -1;
-
   float o[DT][4];
 #pragma unroll
   for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-
-  for (int j = 0; j < ntiles; ++j) {
-    const int buf = j & 1;
-    if (j + 1 < ntiles) {
-      const int vk = static_cast<int>(min((int64_t)kAttnKeys, kv_end - (int64_t)(j + 1) * kAttnKeys));
-      load_page<D>(sK[buf ^ 1], page_ptr(k_cache, j + 1), vk);
-      load_page<D>(sV[buf ^ 1], page_ptr(v_cache, j + 1), vk);
+  int it = 0;
+  for (int j = pg0; j < pg1; ++j, ++it) {
+    const int s = it % STAGES;
+    if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
+      if (p.err && lane == 0) atomicCAS(p.err, 0, 12);
+      *abort_flag = 1;
+      break;
     }
-    cp_async_commit();
-    if (warp_active) {
-      float s[8][4];
+    const uint32_t kb = saddr(sKV + s * 2 * TILE_BYTES);
+    const uint32_t vb = kb + TILE_BYTES;
+    if (active) {
+      float sc[8][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-      const uint32_t kb = smem_u32(sK[buf]);
+      for (int i = 0; i < 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < KSTEPS; ++kk) {
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
           uint32_t b0, b1, b2, b3;
-          const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
-          const int ch = 2 * kk + ((lane >> 3) & 1);
-          ldsm_x4(kb + swz<D>(key, ch), b0, b1, b2, b3);
-          mma_bf16(s[2 * np], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
-          mma_bf16(s[2 * np + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
+          ldsm_x4(kb + swz(np * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0, b1, b2, b3);
+          mma16816(sc[2 * np], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
+          mma16816(sc[2 * np + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
         }
       }
-      // Scale, mask, online softmax.
-      const int64_t kbase = (int64_t)j * kAttnKeys;
-      const bool edge = kbase + kAttnKeys - 1 > min(pa, pb) || pa < 0 || pb < 0;
+      const int64_t kbase = static_cast<int64_t>(j) * KEYS;
+      const bool edge = kbase + KEYS - 1 > min(pa, pb) || pa < 0 || pb < 0;
       float mx_a = m_a, mx_b = m_b;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int64_t kp = kbase + nt * 8 + 2 * t4 + e;
-          float va = s[nt][e] * scale_log2, vb = s[nt][2 + e] * scale_log2;
+          float va = sc[nt][e] * p.scale_log2, vb2 = sc[nt][2 + e] * p.scale_log2;
           if (edge) {
             if (kp > pa) va = -INFINITY;
-            if (kp > pb) vb = -INFINITY;
+            if (kp > pb) vb2 = -INFINITY;
           }
-          s[nt][e] = va;
-          s[nt][2 + e] = vb;
+          sc[nt][e] = va;
+          sc[nt][2 + e] = vb2;
           mx_a = fmaxf(mx_a, va);
-          mx_b = fmaxf(mx_b, vb);
+          mx_b = fmaxf(mx_b, vb2);
         }
       }
       mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
@@ -180,114 +258,189 @@ __global__ void __launch_bounds__(128) paged_attention_kernel(
       mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
       const float base_a = mx_a == -INFINITY ? 0.f : mx_a;
       const float base_b = mx_b == -INFINITY ? 0.f : mx_b;
-      const float alpha_a = exp2f(m_a - base_a), alpha_b = exp2f(m_b - base_b);
+      const float al_a = exp2f(m_a - base_a), al_b = exp2f(m_b - base_b);
       m_a = mx_a;
       m_b = mx_b;
       float sum_a = 0.f, sum_b = 0.f;
       uint32_t pf[4][4];
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-        const float p0 = exp2f(s[nt][0] - base_a), p1 = exp2f(s[nt][1] - base_a);
-        const float p2 = exp2f(s[nt][2] - base_b), p3 = exp2f(s[nt][3] - base_b);
+        const float p0 = exp2f(sc[nt][0] - base_a), p1 = exp2f(sc[nt][1] - base_a);
+        const float p2 = exp2f(sc[nt][2] - base_b), p3 = exp2f(sc[nt][3] - base_b);
         sum_a += p0 + p1;
         sum_b += p2 + p3;
-        const int kc = nt >> 1, hi = nt & 1;
-        pf[kc][hi * 2 + 0] = pack_bf16(p0, p1);
-        pf[kc][hi * 2 + 1] = pack_bf16(p2, p3);
+        pf[nt >> 1][(nt & 1) * 2 + 0] = pack2(p0, p1);
+        pf[nt >> 1][(nt & 1) * 2 + 1] = pack2(p2, p3);
       }
-      l_a = l_a * alpha_a + sum_a;
-      l_b = l_b * alpha_b + sum_b;
+      l_a = l_a * al_a + sum_a;
+      l_b = l_b * al_b + sum_b;
 #pragma unroll
       for (int dt = 0; dt < DT; ++dt) {
-        o[dt][0] *= alpha_a;
-        o[dt][1] *= alpha_a;
-        o[dt][2] *= alpha_b;
-        o[dt][3] *= alpha_b;
+        o[dt][0] *= al_a;
+        o[dt][1] *= al_a;
+        o[dt][2] *= al_b;
+        o[dt][3] *= al_b;
       }
-      const uint32_t vb_ = smem_u32(sV[buf]);
 #pragma unroll
       for (int kc = 0; kc < 4; ++kc) {
-        // A fragment order: a0 (row g, keys lo), a1 (row g+8, keys lo), a2 (row g, keys hi), a3 (row g+8, hi).
-        const uint32_t a0 = pf[kc][0], a1 = pf[kc][1], a2 = pf[kc][2], a3 = pf[kc][3];
 #pragma unroll
         for (int dp = 0; dp < DT / 2; ++dp) {
           uint32_t b0, b1, b2, b3;
-          const int key = kc * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
-          const int ch = 2 * dp + (lane >> 4);
-          ldsm_x4_t(vb_ + swz<D>(key, ch), b0, b1, b2, b3);
-          mma_bf16(o[2 * dp], a0, a1, a2, a3, b0, b1);
-          mma_bf16(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
+          ldsm_x4_t(vb + swz(kc * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), 2 * dp + (lane >> 4)), b0, b1, b2, b3);
+          mma16816(o[2 * dp], pf[kc][0], pf[kc][1], pf[kc][2], pf[kc][3], b0, b1);
+          mma16816(o[2 * dp + 1], pf[kc][0], pf[kc][1], pf[kc][2], pf[kc][3], b2, b3);
         }
       }
     }
-    cp_async_wait<0>();
-    __syncthreads();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (!warp_active) return;
+  if (!active) return;
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
   const float inv_a = l_a > 0.f ? 1.f / l_a : 0.f;
   const float inv_b = l_b > 0.f ? 1.f / l_b : 0.f;
-  if (ra < rows_valid) {
-    const int rr = row0 + ra;
-    __nv_bfloat16* dst = out + (qs + rr / G) * out_stride_tok + (int64_t)(h * G + rr % G) * D;
 #pragma unroll
-    for (int dt = 0; dt < DT; ++dt)
-      *reinterpret_cast<__nv_bfloat162*>(dst + dt * 8 + 2 * t4) =
-          __floats2bfloat162_rn(o[dt][0] * inv_a, o[dt][1] * inv_a);
-  }
-  if (rb < rows_valid) {
-    const int rr = row0 + rb;
-    __nv_bfloat16* dst = out + (qs + rr / G) * out_stride_tok + (int64_t)(h * G + rr % G) * D;
+  for (int half = 0; half < 2; ++half) {
+    const int r = half ? rb : ra;
+    if (r >= rows_valid) continue;
+    const int rr = row0 + r;
+    const int64_t tok = qs + rr / G;
+    const int head = h * G + rr % G;
+    const float inv = half ? inv_b : inv_a;
+    if (p.nsplit == 1) {
+      __nv_bfloat16* dst = p.out + tok * p.out_stride + static_cast<int64_t>(head) * D;
 #pragma unroll
-    for (int dt = 0; dt < DT; ++dt)
-      *reinterpret_cast<__nv_bfloat162*>(dst + dt * 8 + 2 * t4) =
-          __floats2bfloat162_rn(o[dt][2] * inv_b, o[dt][3] * inv_b);
+      for (int dt = 0; dt < DT; ++dt)
+        *reinterpret_cast<__nv_bfloat162*>(dst + dt * 8 + 2 * t4) =
+            __floats2bfloat162_rn(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
+    } else {
+      // Partial: normalised O and (max, sum) in log2 units, per (row, split).
+      const int64_t prow = (tok * p.hq + head) * p.nsplit + split;
+      float* dst = p.part_o + prow * D;
+#pragma unroll
+      for (int dt = 0; dt < DT; ++dt)
+        *reinterpret_cast<float2*>(dst + dt * 8 + 2 * t4) =
+            make_float2(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
+      if (t4 == 0) {
+        p.part_ml[prow * 2] = half ? m_b : m_a;
+        p.part_ml[prow * 2 + 1] = half ? l_b : l_a;
+      }
+    }
   }
 }
 
+// One warp per (token, q head): combine nsplit partials in split order.
+template <int D>
+__global__ void attn_merge_kernel(__nv_bfloat16* __restrict__ out, int64_t out_stride, const float* __restrict__ part_o,
+                                  const float* __restrict__ part_ml, int64_t rows, int hq, int nsplit) {
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= rows) return;
+  const float* ml = part_ml + w * nsplit * 2;
+  float mx = -INFINITY;
+  for (int s = 0; s < nsplit; ++s)
+    if (ml[2 * s + 1] > 0.f) mx = fmaxf(mx, ml[2 * s]);
+  float acc[D / 32];
+#pragma unroll
+  for (int i = 0; i < D / 32; ++i) acc[i] = 0.f;
+  float den = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float l = ml[2 * s + 1];
+    if (!(l > 0.f)) continue;
+    const float wgt = exp2f(ml[2 * s] - mx) * l;
+    den += wgt;
+    const float* po = part_o + (w * nsplit + s) * D;
+#pragma unroll
+    for (int i = 0; i < D / 32; ++i) acc[i] += wgt * po[lane + 32 * i];
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  const int64_t tok = w / hq;
+  const int head = static_cast<int>(w % hq);
+  __nv_bfloat16* dst = out + tok * out_stride + static_cast<int64_t>(head) * D;
+#pragma unroll
+  for (int i = 0; i < D / 32; ++i) dst[lane + 32 * i] = __float2bfloat16(acc[i] * inv);
+}
+
+}  // namespace attn
 }  // namespace shk
 
-using namespace shk;
+using namespace shk::attn;
 
-// q: [T, >= hq*D] view (row stride q_stride), out: [T, hq*D] (row stride).
-// tile_req / tile_row0: int32 [num_tiles] q-tile schedule (see plan_attention_tiles).
-void paged_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
-                     torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
-                     torch::Tensor tile_req, torch::Tensor tile_row0, int64_t hq, double scale) {
-  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16, "bf16 attention");
-  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == kAttnKeys, "cache must be [blocks, hk, 64, D]");
-  TORCH_CHECK(q.stride(-1) == 1 && out.stride(-1) == 1, "q/out innermost stride 1");
-  TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kLong &&
-                  q_start.scalar_type() == at::kLong && tile_req.scalar_type() == at::kInt,
-              "attention index dtypes");
-  const int hk = k_cache.size(1), d = k_cache.size(3);
-  TORCH_CHECK(hq % hk == 0, "hq must be a multiple of hk");
-  const int ntiles = tile_req.numel();
-  if (ntiles == 0) return;
-  const float scale_log2 = static_cast<float>(scale * 1.4426950408889634);
-  auto stream = at::cuda::getCurrentCUDAStream();
-  dim3 grid(ntiles, hk);
-  auto launch = [&](auto kernel, int D) {
-    const int smem = (kAttnRows + 4 * kAttnKeys) * D * 2;
-    SH_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kernel<<<grid, 128, smem, stream>>>((__nv_bfloat16*)out.data_ptr(), out.stride(0),
-                                        (const __nv_bfloat16*)q.data_ptr(), q.stride(0),
-                                        (const __nv_bfloat16*)k_cache.data_ptr(),
-                                        (const __nv_bfloat16*)v_cache.data_ptr(), block_tables.data_ptr<int32_t>(),
-                                        block_tables.stride(0), seq_lens.data_ptr<int64_t>(),
-                                        q_start.data_ptr<int64_t>(), tile_req.data_ptr<int32_t>(),
-                                        tile_row0.data_ptr<int32_t>(), (int)hq, hk, scale_log2);
-  };
-  if (d == 128)
-    launch(paged_attention_kernel<128>, 128);
-  else if (d == 64)
-    launch(paged_attention_kernel<64>, 64);
-  else if (d == 256)
-    launch(paged_attention_kernel<256>, 256);
-  else
-    TORCH_CHECK(false, "paged_attention: head_dim must be 64, 128 or 256");
-  SH_CUDA_CHECK(cudaGetLastError());
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// Cache viewed as rows of D bf16: dims {D, rows}, box {64, 64}, 128-byte swizzle.
+int cache_map(CUtensorMap* m, const void* base, int64_t rows, int d) {
+  auto enc = encoder();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(d) * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
+}
+
+template <int D>
+int launch(const AttnParams& p, int ntiles, int cache_rows, cudaStream_t st) {
+  CUtensorMap mk, mv;
+  int r = cache_map(&mk, p.k_cache, cache_rows, D);
+  if (r) return 100 + r;
+  r = cache_map(&mv, p.v_cache, cache_rows, D);
+  if (r) return 200 + r;
+  constexpr int STAGES = Stages<D>::value;
+  const int smem = 1024 + 64 * D * 2 * (1 + 2 * STAGES) + 2 * STAGES * 8 + 16;
+  auto k = paged_attn_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return 300 + static_cast<int>(e);
+  dim3 grid(ntiles, p.hk, p.nsplit);
+  k<<<grid, THREADS, smem, st>>>(mk, mv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return 400 + static_cast<int>(e);
+  if (p.nsplit > 1) {
+    const int64_t rows = p.num_tokens * p.hq;
+    const int64_t threads = rows * 32;
+    attn_merge_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(
+        p.out, p.out_stride, p.part_o, p.part_ml, rows, p.hq, p.nsplit);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return 500 + static_cast<int>(e);
+  }
+  return 0;
+}
+}  // namespace
+
+extern "C" int sh_paged_attention(const AttnParams* params, int ntiles, int num_blocks, int head_dim,
+                                  cudaStream_t stream) {
+  const AttnParams& p = *params;
+  if (ntiles <= 0 || p.num_tokens <= 0) return 0;
+  if (p.nsplit < 1 || p.hq % p.hk != 0) return -1;
+  if (p.nsplit > 1 && (p.part_o == nullptr || p.part_ml == nullptr)) return -2;
+  if ((reinterpret_cast<uintptr_t>(p.k_cache) & 15) || (reinterpret_cast<uintptr_t>(p.v_cache) & 15)) return -3;
+  const int cache_rows = num_blocks * p.hk * KEYS;
+  switch (head_dim) {
+    case 64:
+      return launch<64>(p, ntiles, cache_rows, stream);
+    case 128:
+      return launch<128>(p, ntiles, cache_rows, stream);
+    case 256:
+      return launch<256>(p, ntiles, cache_rows, stream);
+    default:
+      return -4;
+  }
 }

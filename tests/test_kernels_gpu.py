@@ -58,13 +58,14 @@ def _paged_setup(q_lens, ctx_lens, hq, hk, d, bs=64, dtype=torch.bfloat16):
     return k_cache, v_cache, bt, torch.tensor(seq, dtype=torch.long, device="cuda"), qs, qkv
 
 
+@pytest.mark.parametrize("nsplit", [1, 3])
 @pytest.mark.parametrize("d", [64, 128, 256])
 @pytest.mark.parametrize("shape", [
     ([6] * 5, [100, 63, 64, 1, 700]),  # verify windows, k = 5
     ([1] * 7, [5, 64, 129, 300, 2048, 0, 77]),  # plain decode
     ([130, 1, 64], [0, 40, 200]),  # prefill / chunked prefill
 ])
-def test_paged_attention(d, shape):
+def test_paged_attention(d, shape, nsplit):
     q_lens, ctx = shape
     hq, hk = 8, 2
     kc, vc, bt, seq, qs, qkv = _paged_setup(q_lens, ctx, hq, hk, d)
@@ -72,7 +73,7 @@ def test_paged_attention(d, shape):
     out = torch.empty(qkv.shape[0], hq * d, device="cuda", dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(d)
     ops.paged_attention(out, qkv, kc, vc, bt, seq, qs, torch.tensor(tr, dtype=torch.int32, device="cuda"),
-                        torch.tensor(t0, dtype=torch.int32, device="cuda"), hq, scale)
+                        torch.tensor(t0, dtype=torch.int32, device="cuda"), hq, scale, nsplit)
     q = qkv[:, : hq * d].reshape(-1, hq, d)
     want = ref.paged_attention(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), bt.cpu(), seq.cpu(), qs.cpu(),
                                hq, scale)

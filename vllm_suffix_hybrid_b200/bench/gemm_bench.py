@@ -44,17 +44,22 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", action="store_true")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--only", default="", help="comma-separated shape names")
+    ap.add_argument("--no-cublas", action="store_true")
     a = ap.parse_args()
     from vllm_suffix_hybrid_b200.ops.gemm import plan, tcgen05_linear
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     res = []
+    only = set(filter(None, a.only.split(",")))
     for name, M, N, K in SHAPES:
+        if only and name not in only:
+            continue
         x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
         w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
         y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         t_ours = time_fn(lambda: tcgen05_linear(x, w, y), flush, a.iters)
-        t_lib = time_fn(lambda: torch.matmul(x, w.t(), out=y), flush, a.iters)
+        t_lib = float("nan") if a.no_cublas else time_fn(lambda: torch.matmul(x, w.t(), out=y), flush, a.iters)
         ref = (x.float() @ w.float().t())
         tcgen05_linear(x, w, y)
         err = (y.float() - ref).abs().max().item()

@@ -34,6 +34,7 @@ class AttnMeta:
     tile_req: torch.Tensor  # [tiles] int32 (attention schedule)
     tile_row0: torch.Tensor  # [tiles] int32
     num_tokens: int = 0
+    nsplit: int = 1  # KV splits per request (split-KV attention)
 
 
 def init_weight(shape, std: float, dtype, device, gen: Optional[torch.Generator]) -> torch.Tensor:
@@ -110,7 +111,7 @@ class Attention:
                           self.d, self.rot)
         attn = torch.empty(x.shape[0], self.hq * self.d, dtype=x.dtype, device=x.device)
         ops.paged_attention(attn, qkv, k_cache, v_cache, meta.block_tables, meta.seq_lens, meta.q_start,
-                            meta.tile_req, meta.tile_row0, self.hq, self.scale)
+                            meta.tile_req, meta.tile_row0, self.hq, self.scale, meta.nsplit)
         return self.o(attn)  # partial sum under TP (reduced by the caller)
 
 

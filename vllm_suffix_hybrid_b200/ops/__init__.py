@@ -112,7 +112,30 @@ def plan_attention_tiles(q_lens, group: int, rows: int = 64):
     return req, row0
 
 
-def paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, tile_req, tile_row0, hq, scale):
+_ATTN_WS = {}
+
+
+def attention_splits(num_tiles: int, kv_heads: int, max_pages: int, sms: int = 148) -> int:
+    """KV splits per request so the grid covers ~4 waves of SMs (1..16)."""
+    units = max(num_tiles * kv_heads, 1)
+    want = -(-4 * sms // units)
+    return int(max(1, min(16, want, max(1, max_pages // 2))))
+
+
+def _attn_workspace(device, n_o: int, n_ml: int):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _ATTN_WS.get(idx)
+    if ws is None or ws[0].numel() < n_o or ws[1].numel() < n_ml:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("attention split-KV workspace must be sized before CUDA-graph capture")
+        ws = (torch.empty(max(n_o, 1 << 16), dtype=torch.float32, device=device),
+              torch.empty(max(n_ml, 1 << 12), dtype=torch.float32, device=device))
+        _ATTN_WS[idx] = ws
+    return ws
+
+
+def paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, tile_req, tile_row0, hq, scale,
+                    nsplit: int = 1):
     """out[T, hq*D] <- attention of q (rows of the QKV buffer) over the paged cache."""
     if not _cuda(q):
         d = k_cache.shape[3]
@@ -120,7 +143,15 @@ def paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, t
         qv = q[:, : hq * d].reshape(t, hq, d)
         out.view(t, hq, d).copy_(ref.paged_attention(qv, k_cache, v_cache, block_tables, seq_lens, q_start, hq, scale))
         return out
-    native().paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, tile_req, tile_row0, hq, scale)
+    if nsplit > 1:
+        d = k_cache.shape[3]
+        n = q.shape[0] * hq * nsplit
+        po, pml = _attn_workspace(q.device, n * d, n * 2)
+        native().paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, tile_req, tile_row0, hq,
+                                 scale, nsplit, po, pml)
+    else:
+        native().paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, tile_req, tile_row0, hq,
+                                 scale)
     return out
 
 

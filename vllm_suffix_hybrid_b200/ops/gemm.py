@@ -31,32 +31,28 @@ def _waves_eff(units: int, sms: int = NUM_SMS) -> float:
 
 @functools.lru_cache(maxsize=4096)
 def plan(M: int, N: int, K: int):
-    """(swap, bn, splits) for y[M, N] = x[M, K] w[N, K]^T."""
-    kb = K // 64
-    best = None
+    """(swap, bn, splits) for y[M, N] = x[M, K] w[N, K]^T.
+
+    Split-K only when the tile grid is under one wave: its fp32 partials cost
+    extra traffic and a reduce pass, so it must buy idle SMs.
+    """
+    kb = max(K // 64, 1)
     if M <= 256:
-        bns = [bn for bn in (64, 128, 256) if bn >= M] or [256]
-        bn = bns[0]
+        bn = next(b for b in (64, 128, 256) if b >= M)
         tiles = math.ceil(N / 128) * math.ceil(M / bn)
-        for splits in (1, 2, 3, 4, 6, 8):
-            if kb // splits < 4:
-                break
-            eff = _waves_eff(tiles * splits)
-            score = eff - 0.03 * (splits - 1)
-            if best is None or score > best[0]:
-                best = (score, True, bn, splits)
-    else:
-        for bn in (256, 128):
-            tiles = math.ceil(M / 128) * math.ceil(N / bn)
-            for splits in (1, 2, 3, 4):
-                if kb // splits < 4:
-                    break
-                eff = _waves_eff(tiles * splits)
-                score = eff - 0.04 * (splits - 1) + (0.02 if bn == 256 else 0.0)
-                if best is None or score > best[0]:
-                    best = (score, False, bn, splits)
-    _, swap, bn, splits = best
-    return swap, bn, splits
+        splits = 1
+        while tiles * splits < NUM_SMS and kb // (splits * 2) >= 8 and splits < 8:
+            splits *= 2
+        return True, bn, splits
+    bn = 256
+    tiles = math.ceil(M / 128) * math.ceil(N / bn)
+    if tiles < NUM_SMS // 2:
+        bn = 128
+        tiles = math.ceil(M / 128) * math.ceil(N / bn)
+    splits = 1
+    while tiles * splits < NUM_SMS * 0.9 and kb // (splits * 2) >= 8 and splits < 4:
+        splits *= 2
+    return False, bn, splits
 
 
 def workspace(device: torch.device, numel: int) -> torch.Tensor:
