@@ -22,7 +22,7 @@ void paged_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, 
                      torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
                      torch::Tensor tile_req, torch::Tensor tile_row0, int64_t hq, double scale, int64_t nsplit,
                      c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_ml,
-                     c10::optional<torch::Tensor> err) {
+                     c10::optional<torch::Tensor> err, int64_t max_rows) {
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16, "paged_attention: bf16 tensors");
   TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == 64 && k_cache.is_contiguous() && v_cache.is_contiguous() &&
@@ -61,8 +61,9 @@ void paged_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, 
     p.part_ml = part_ml->data_ptr<float>();
   }
   p.err = err.has_value() ? err->data_ptr<int>() : nullptr;
+  TORCH_CHECK(max_rows >= 1 && max_rows <= 64, "paged_attention: max_rows in 1..64");
   const int r = sh_paged_attention(&p, static_cast<int>(tile_req.numel()), static_cast<int>(k_cache.size(0)), d,
-                                   at::cuda::getCurrentCUDAStream());
+                                   static_cast<int>(max_rows), at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_paged_attention failed with code ", r);
 }
 
@@ -108,7 +109,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention", &paged_attention, "paged GQA attention", py::arg("out"), py::arg("q"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("block_tables"), py::arg("seq_lens"), py::arg("q_start"), py::arg("tile_req"),
         py::arg("tile_row0"), py::arg("hq"), py::arg("scale"), py::arg("nsplit") = 1, py::arg("part_o") = py::none(),
-        py::arg("part_ml") = py::none(), py::arg("err") = py::none());
+        py::arg("part_ml") = py::none(), py::arg("err") = py::none(), py::arg("max_rows") = 64);
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM", py::arg("y"), py::arg("x"), py::arg("w"), py::arg("swap"),
         py::arg("bn"), py::arg("splits"), py::arg("ws") = py::none(), py::arg("err") = py::none());
 }

@@ -363,12 +363,36 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// out[(trans ? q : p)] = bf16(sum over splits of ws[s][p][q]) in fixed split order.
+// out[(trans ? q : p)] = bf16(sum over splits of ws[s][p][q]) in fixed split order;
+// four consecutive q per thread (float4 loads) when rows_q % 4 == 0.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ out, int splits,
                                      int rows_p, int rows_q, int ldo, int trans) {
   const int64_t n = static_cast<int64_t>(rows_p) * rows_q;
-  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x); i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if ((rows_q & 3) == 0) {
+    for (int64_t i4 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i4 < n / 4; i4 += stride) {
+      float4 s = reinterpret_cast<const float4*>(ws)[i4];
+      for (int k = 1; k < splits; ++k) {
+        const float4 v = reinterpret_cast<const float4*>(ws + k * n)[i4];
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+      }
+      const int64_t i = i4 * 4;
+      const int p = static_cast<int>(i / rows_q), q = static_cast<int>(i % rows_q);
+      if (!trans) {
+        __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(out + static_cast<int64_t>(p) * ldo + q);
+        o[0] = __floats2bfloat162_rn(s.x, s.y);
+        o[1] = __floats2bfloat162_rn(s.z, s.w);
+      } else {
+        const float v[4] = {s.x, s.y, s.z, s.w};
+        for (int j = 0; j < 4; ++j) out[static_cast<int64_t>(q + j) * ldo + p] = __float2bfloat16(v[j]);
+      }
+    }
+    return;
+  }
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
     float s = 0.f;
     for (int k = 0; k < splits; ++k) s += ws[k * n + i];
     const int p = static_cast<int>(i / rows_q), q = static_cast<int>(i % rows_q);
@@ -477,8 +501,9 @@ extern "C" int sh_gemm_bf16_tcgen05(const void* P, int rows_p, int64_t ldp, cons
   if (r) return 3000 + r;
   if (split) {
     const int64_t n = static_cast<int64_t>(rows_p) * rows_q;
-    int blocks = static_cast<int>((n + 255) / 256);
-    if (blocks > 4 * num_sms) blocks = 4 * num_sms;
+    int blocks = static_cast<int>((n / 4 + 255) / 256);
+    if (blocks > 8 * num_sms) blocks = 8 * num_sms;
+    if (blocks < 1) blocks = 1;
     splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, static_cast<__nv_bfloat16*>(out), splits, rows_p, rows_q,
                                                       static_cast<int>(ldo), trans);
     r = static_cast<int>(cudaGetLastError());

@@ -109,7 +109,7 @@ struct Stages {
   static constexpr int value = D == 64 ? 8 : (D == 128 ? 4 : 2);  // K/V page ring depth
 };
 
-template <int D>
+template <int D, int KS>
 __global__ void __launch_bounds__(THREADS, 1)
     paged_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnParams p) {
   constexpr int TILE_BYTES = 64 * D * 2;  // one [64][D] bf16 tile
@@ -192,19 +192,26 @@ __global__ void __launch_bounds__(THREADS, 1)
     return;
   }
   // -------------------------------------------------------------- compute
-  const int cw = warp - 1;  // rows cw*16 .. +15
+  // 4 compute warps: warp cw owns row block cw / KS (16 rows) and key part
+  // cw % KS (64 / KS keys of every page); the KS partial softmax states of a
+  // row block are merged through shared memory at the end.
+  constexpr int NT = 8 / KS;  // 8-key n-tiles per page per warp
+  constexpr int KC = 4 / KS;  // 16-key PV chunks per page per warp
+  const int cw = warp - 1;
+  const int rbk = cw / KS, kpart = cw % KS;
   const int g = lane >> 2, t4 = lane & 3;
-  const bool active = cw * 16 < rows_valid;
+  const bool active = rbk * 16 < rows_valid;
   uint32_t qf[KSTEPS][4];
   if (active) {
 #pragma unroll
     for (int kk = 0; kk < KSTEPS; ++kk)
-      ldsm_x4(saddr(sQ) + swz(cw * 16 + (lane & 15), 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2],
+      ldsm_x4(saddr(sQ) + swz(rbk * 16 + (lane & 15), 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2],
               qf[kk][3]);
   }
-  const int ra = cw * 16 + g, rb = ra + 8;
+  const int ra = rbk * 16 + g, rb = ra + 8;
   const int64_t pa = ra < rows_valid ? ctx0 + (row0 + ra) / G : -1;
   const int64_t pb = rb < rows_valid ? ctx0 + (row0 + rb) / G : -1;
+  const int key0 = kpart * (KEYS / KS);
   float o[DT][4];
 #pragma unroll
   for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
@@ -220,24 +227,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t kb = saddr(sKV + s * 2 * TILE_BYTES);
     const uint32_t vb = kb + TILE_BYTES;
     if (active) {
-      float sc[8][4];
+      float sc[NT][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+      for (int i = 0; i < NT; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < KSTEPS; ++kk) {
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
+        for (int np = 0; np < NT / 2; ++np) {
           uint32_t b0, b1, b2, b3;
-          ldsm_x4(kb + swz(np * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0, b1, b2, b3);
+          ldsm_x4(kb + swz(key0 + np * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0, b1, b2,
+                  b3);
           mma16816(sc[2 * np], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
           mma16816(sc[2 * np + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
         }
       }
-      const int64_t kbase = static_cast<int64_t>(j) * KEYS;
-      const bool edge = kbase + KEYS - 1 > min(pa, pb) || pa < 0 || pb < 0;
+      const int64_t kbase = static_cast<int64_t>(j) * KEYS + key0;
+      const bool edge = kbase + KEYS / KS - 1 > min(pa, pb) || pa < 0 || pb < 0;
       float mx_a = m_a, mx_b = m_b;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int64_t kp = kbase + nt * 8 + 2 * t4 + e;
@@ -262,9 +270,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       m_a = mx_a;
       m_b = mx_b;
       float sum_a = 0.f, sum_b = 0.f;
-      uint32_t pf[4][4];
+      uint32_t pf[KC][4];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < NT; ++nt) {
         const float p0 = exp2f(sc[nt][0] - base_a), p1 = exp2f(sc[nt][1] - base_a);
         const float p2 = exp2f(sc[nt][2] - base_b), p3 = exp2f(sc[nt][3] - base_b);
         sum_a += p0 + p1;
@@ -282,11 +290,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         o[dt][3] *= al_b;
       }
 #pragma unroll
-      for (int kc = 0; kc < 4; ++kc) {
+      for (int kc = 0; kc < KC; ++kc) {
 #pragma unroll
         for (int dp = 0; dp < DT / 2; ++dp) {
           uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(vb + swz(kc * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), 2 * dp + (lane >> 4)), b0, b1, b2, b3);
+          ldsm_x4_t(vb + swz(key0 + kc * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), 2 * dp + (lane >> 4)), b0, b1,
+                    b2, b3);
           mma16816(o[2 * dp], pf[kc][0], pf[kc][1], pf[kc][2], pf[kc][3], b0, b1);
           mma16816(o[2 * dp + 1], pf[kc][0], pf[kc][1], pf[kc][2], pf[kc][3], b2, b3);
         }
@@ -295,11 +304,49 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (!active) return;
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  if (KS > 1) {
+    // Merge the KS key-part states of each row block (the ring is drained:
+    // every page was consumed by all compute warps before this barrier).
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    float* xs = reinterpret_cast<float*>(sKV) + (cw * 32 + lane) * (DT * 4 + 4);
+    if (kpart != 0 && active) {
+#pragma unroll
+      for (int dt = 0; dt < DT; ++dt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xs[dt * 4 + e] = o[dt][e];
+      xs[DT * 4 + 0] = m_a;
+      xs[DT * 4 + 1] = m_b;
+      xs[DT * 4 + 2] = l_a;
+      xs[DT * 4 + 3] = l_b;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (kpart != 0 || !active) return;
+#pragma unroll
+    for (int q = 1; q < KS; ++q) {
+      const float* ys = reinterpret_cast<const float*>(sKV) + ((cw + q) * 32 + lane) * (DT * 4 + 4);
+      const float mq_a = ys[DT * 4 + 0], mq_b = ys[DT * 4 + 1];
+      const float na = fmaxf(m_a, mq_a), nb = fmaxf(m_b, mq_b);
+      const float ba = na == -INFINITY ? 0.f : na, bb = nb == -INFINITY ? 0.f : nb;
+      const float sa = exp2f(m_a - ba), sb = exp2f(m_b - bb);
+      const float qa = exp2f(mq_a - ba), qb = exp2f(mq_b - bb);
+#pragma unroll
+      for (int dt = 0; dt < DT; ++dt) {
+        o[dt][0] = o[dt][0] * sa + ys[dt * 4 + 0] * qa;
+        o[dt][1] = o[dt][1] * sa + ys[dt * 4 + 1] * qa;
+        o[dt][2] = o[dt][2] * sb + ys[dt * 4 + 2] * qb;
+        o[dt][3] = o[dt][3] * sb + ys[dt * 4 + 3] * qb;
+      }
+      l_a = l_a * sa + ys[DT * 4 + 2] * qa;
+      l_b = l_b * sb + ys[DT * 4 + 3] * qb;
+      m_a = na;
+      m_b = nb;
+    }
+  }
+  if (!active) return;
   const float inv_a = l_a > 0.f ? 1.f / l_a : 0.f;
   const float inv_b = l_b > 0.f ? 1.f / l_b : 0.f;
 #pragma unroll
@@ -397,22 +444,30 @@ int cache_map(CUtensorMap* m, const void* base, int64_t rows, int d) {
   return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
 }
 
-template <int D>
-int launch(const AttnParams& p, int ntiles, int cache_rows, cudaStream_t st) {
-  CUtensorMap mk, mv;
-  int r = cache_map(&mk, p.k_cache, cache_rows, D);
-  if (r) return 100 + r;
-  r = cache_map(&mv, p.v_cache, cache_rows, D);
-  if (r) return 200 + r;
+template <int D, int KS>
+int launch_ks(const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& p, int ntiles, cudaStream_t st) {
   constexpr int STAGES = Stages<D>::value;
   const int smem = 1024 + 64 * D * 2 * (1 + 2 * STAGES) + 2 * STAGES * 8 + 16;
-  auto k = paged_attn_kernel<D>;
+  auto k = paged_attn_kernel<D, KS>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return 300 + static_cast<int>(e);
   dim3 grid(ntiles, p.hk, p.nsplit);
   k<<<grid, THREADS, smem, st>>>(mk, mv, p);
   e = cudaGetLastError();
-  if (e != cudaSuccess) return 400 + static_cast<int>(e);
+  return e == cudaSuccess ? 0 : 400 + static_cast<int>(e);
+}
+
+template <int D>
+int launch(const AttnParams& p, int ntiles, int cache_rows, int max_rows, cudaStream_t st) {
+  CUtensorMap mk, mv;
+  int r = cache_map(&mk, p.k_cache, cache_rows, D);
+  if (r) return 100 + r;
+  r = cache_map(&mv, p.v_cache, cache_rows, D);
+  if (r) return 200 + r;
+  r = max_rows <= 16 ? launch_ks<D, 4>(mk, mv, p, ntiles, st)
+                     : (max_rows <= 32 ? launch_ks<D, 2>(mk, mv, p, ntiles, st) : launch_ks<D, 1>(mk, mv, p, ntiles, st));
+  if (r) return r;
+  cudaError_t e;
   if (p.nsplit > 1) {
     const int64_t rows = p.num_tokens * p.hq;
     const int64_t threads = rows * 32;
@@ -425,7 +480,7 @@ int launch(const AttnParams& p, int ntiles, int cache_rows, cudaStream_t st) {
 }
 }  // namespace
 
-extern "C" int sh_paged_attention(const AttnParams* params, int ntiles, int num_blocks, int head_dim,
+extern "C" int sh_paged_attention(const AttnParams* params, int ntiles, int num_blocks, int head_dim, int max_rows,
                                   cudaStream_t stream) {
   const AttnParams& p = *params;
   if (ntiles <= 0 || p.num_tokens <= 0) return 0;
@@ -435,11 +490,11 @@ extern "C" int sh_paged_attention(const AttnParams* params, int ntiles, int num_
   const int cache_rows = num_blocks * p.hk * KEYS;
   switch (head_dim) {
     case 64:
-      return launch<64>(p, ntiles, cache_rows, stream);
+      return launch<64>(p, ntiles, cache_rows, max_rows, stream);
     case 128:
-      return launch<128>(p, ntiles, cache_rows, stream);
+      return launch<128>(p, ntiles, cache_rows, max_rows, stream);
     case 256:
-      return launch<256>(p, ntiles, cache_rows, stream);
+      return launch<256>(p, ntiles, cache_rows, max_rows, stream);
     default:
       return -4;
   }

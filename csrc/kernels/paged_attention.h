@@ -28,8 +28,11 @@ struct AttnParams {
 #ifdef __cplusplus
 extern "C" {
 #endif
-// Returns 0 on success; head_dim in {64, 128, 256}; block size 64.
-int sh_paged_attention(const AttnParams* params, int ntiles, int num_blocks, int head_dim, cudaStream_t stream);
+// Returns 0 on success; head_dim in {64, 128, 256}; block size 64.  max_rows:
+// the most valid rows any query tile holds (<= 64); tiles of <= 16 / 32 rows
+// let 4 / 2 warps share one row block's pages by key range.
+int sh_paged_attention(const AttnParams* params, int ntiles, int num_blocks, int head_dim, int max_rows,
+                       cudaStream_t stream);
 #ifdef __cplusplus
 }
 #endif

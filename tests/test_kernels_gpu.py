@@ -73,7 +73,8 @@ def test_paged_attention(d, shape, nsplit):
     out = torch.empty(qkv.shape[0], hq * d, device="cuda", dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(d)
     ops.paged_attention(out, qkv, kc, vc, bt, seq, qs, torch.tensor(tr, dtype=torch.int32, device="cuda"),
-                        torch.tensor(t0, dtype=torch.int32, device="cuda"), hq, scale, nsplit)
+                        torch.tensor(t0, dtype=torch.int32, device="cuda"), hq, scale, nsplit,
+                        min(64, max(q_lens) * (hq // hk)))
     q = qkv[:, : hq * d].reshape(-1, hq, d)
     want = ref.paged_attention(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), bt.cpu(), seq.cpu(), qs.cpu(),
                                hq, scale)

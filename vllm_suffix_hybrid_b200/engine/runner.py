@@ -102,7 +102,7 @@ class Runner:
         nsplit = ops.attention_splits(tr.numel(), kvh, self.max_blocks)
         return AttnMeta(positions=pos.reshape(-1), slot_mapping=self._slots(bt, pos).reshape(-1), block_tables=bt,
                         seq_lens=seq_lens, q_start=qs, tile_req=tr, tile_row0=t0, num_tokens=nb * qlen,
-                        nsplit=nsplit)
+                        nsplit=nsplit, max_rows=min(64, qlen * self.group))
 
     def _draft_steps(self, d1: torch.Tensor, f1: torch.Tensor, lnew: torch.Tensor, bt: torch.Tensor, nb: int):
         """Draft tokens 2..k at positions lnew + s - 2 (s = 2..k)."""
@@ -213,7 +213,8 @@ class Runner:
         meta = AttnMeta(positions=pos, slot_mapping=slots, block_tables=bt, seq_lens=seq_lens, q_start=qs,
                         tile_req=torch.tensor(tr, dtype=torch.int32, device=dev),
                         tile_row0=torch.tensor(t0, dtype=torch.int32, device=dev), num_tokens=int(sum(lens)),
-                        nsplit=ops.attention_splits(len(tr), self.model.kv_heads_local, mb))
+                        nsplit=ops.attention_splits(len(tr), self.model.kv_heads_local, mb),
+                        max_rows=min(64, max(lens) * self.group))
         hid, pre = self.model.forward(ids, meta, self.caches)
         last = qs[1:] - 1
         first = self.model.greedy(hid.index_select(0, last))

@@ -35,6 +35,7 @@ class AttnMeta:
     tile_row0: torch.Tensor  # [tiles] int32
     num_tokens: int = 0
     nsplit: int = 1  # KV splits per request (split-KV attention)
+    max_rows: int = 64  # most valid rows in any 64-row query tile
 
 
 def init_weight(shape, std: float, dtype, device, gen: Optional[torch.Generator]) -> torch.Tensor:
@@ -111,7 +112,8 @@ class Attention:
                           self.d, self.rot)
         attn = torch.empty(x.shape[0], self.hq * self.d, dtype=x.dtype, device=x.device)
         ops.paged_attention(attn, qkv, k_cache, v_cache, meta.block_tables, meta.seq_lens, meta.q_start,
-                            meta.tile_req, meta.tile_row0, self.hq, self.scale, meta.nsplit)
+                            meta.tile_req, meta.tile_row0, self.hq, self.scale, meta.nsplit,
+                            meta.max_rows)
         return self.o(attn)  # partial sum under TP (reduced by the caller)
 
 

@@ -135,7 +135,7 @@ def _attn_workspace(device, n_o: int, n_ml: int):
 
 
 def paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, tile_req, tile_row0, hq, scale,
-                    nsplit: int = 1):
+                    nsplit: int = 1, max_rows: int = 64):
     """out[T, hq*D] <- attention of q (rows of the QKV buffer) over the paged cache."""
     if not _cuda(q):
         d = k_cache.shape[3]
@@ -148,10 +148,10 @@ def paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, t
         n = q.shape[0] * hq * nsplit
         po, pml = _attn_workspace(q.device, n * d, n * 2)
         native().paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, tile_req, tile_row0, hq,
-                                 scale, nsplit, po, pml)
+                                 scale, nsplit, po, pml, None, max_rows)
     else:
         native().paged_attention(out, q, k_cache, v_cache, block_tables, seq_lens, q_start, tile_req, tile_row0, hq,
-                                 scale)
+                                 scale, 1, None, None, None, max_rows)
     return out
 
 

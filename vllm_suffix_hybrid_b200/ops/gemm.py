@@ -44,13 +44,12 @@ def plan(M: int, N: int, K: int):
         while tiles * splits < NUM_SMS and kb // (splits * 2) >= 8 and splits < 8:
             splits *= 2
         return True, bn, splits
-    bn = 256
+    bn = 256 if N > 8192 else 128
     tiles = math.ceil(M / 128) * math.ceil(N / bn)
-    if tiles < NUM_SMS // 2:
-        bn = 128
-        tiles = math.ceil(M / 128) * math.ceil(N / bn)
     splits = 1
-    while tiles * splits < NUM_SMS * 0.9 and kb // (splits * 2) >= 8 and splits < 4:
+    # Split only grids that would leave most SMs idle: the fp32 partial
+    # round trip costs more than a partly filled single wave.
+    while tiles * splits < NUM_SMS // 3 and kb // (splits * 2) >= 16 and splits < 4:
         splits *= 2
     return False, bn, splits
 
