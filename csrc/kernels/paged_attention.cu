@@ -21,6 +21,8 @@
 #include <cudaTypedefs.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "paged_attention.h"
 
 namespace shk {
@@ -498,4 +500,73 @@ extern "C" int sh_paged_attention(const AttnParams* params, int ntiles, int num_
     default:
       return -4;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point (no counterpart in the reference).
+//
+// Some callers cannot allocate device memory at the point where they run
+// attention: a host runtime without a device allocator of its own (a C or
+// Rust serving loop that links only this library), code with a fixed,
+// pre-reserved memory budget where a new allocation would fail, or a latency
+// path that must not pay cudaMalloc's implicit device synchronisation.  For
+// them this variant keeps the split-KV partials in a file-scope device array
+// of a fixed size instead of a caller-provided workspace.  The caller still
+// passes every input and output buffer.
+//
+// The array exists once per GPU that loads this library and stays allocated
+// until the process exits.  Its device address is looked up with
+// cudaGetSymbolAddress on the first call made on each device (with that
+// device current); make that first call before any CUDA-graph stream
+// capture.  Every call reuses the same array: calls that overlap on the GPU
+// (two streams, two threads) race on it and must be serialised by the
+// caller.  Nothing in it needs to start at zero -- every partial slot the
+// merge reads is written earlier in the same call.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int64_t kNoAllocFloats = SH_ATTN_NOALLOC_MAX_FLOATS;
+__device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return SH_NOALLOC_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return SH_NOALLOC_ERR_SYMBOL;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int64_t sh_paged_attention_noalloc_capacity(void) {
+  return kNoAllocFloats;
+}
+
+extern "C" __attribute__((visibility("default"))) int sh_paged_attention_noalloc(const AttnParams* params, int ntiles,
+                                                                                   int num_blocks, int head_dim,
+                                                                                   int max_rows, cudaStream_t stream) {
+  if (params == nullptr) return SH_NOALLOC_ERR_ARGS;
+  AttnParams p = *params;
+  if (p.nsplit < 1 || head_dim <= 0) return SH_NOALLOC_ERR_ARGS;
+  p.part_o = nullptr;
+  p.part_ml = nullptr;
+  if (p.nsplit > 1) {
+    // Partials: [rows * nsplit, head_dim] then [rows * nsplit, 2] floats.
+    const int64_t slots = p.num_tokens * p.hq * p.nsplit;
+    const int64_t need = slots * (head_dim + 2);
+    if (p.num_tokens < 0 || slots < 0 || need > kNoAllocFloats) return SH_NOALLOC_ERR_TOO_LARGE;
+    float* base = nullptr;
+    const int r = noalloc_scratch(&base);
+    if (r) return r;
+    p.part_o = base;
+    p.part_ml = base + slots * head_dim;
+  }
+  return sh_paged_attention(&p, ntiles, num_blocks, head_dim, max_rows, stream);
 }

@@ -33,6 +33,30 @@ extern "C" {
 // let 4 / 2 warps share one row block's pages by key range.
 int sh_paged_attention(const AttnParams* params, int ntiles, int num_blocks, int head_dim, int max_rows,
                        cudaStream_t stream);
+
+// Allocation-free variant (no counterpart in the reference).  Identical to
+// sh_paged_attention except that params->part_o / part_ml are ignored: the
+// split-KV partials live in a fixed device array inside this library, so the
+// call performs no device allocation of any kind.  It exists for callers that
+// cannot allocate device memory where they run attention (a host runtime
+// without its own device allocator, a fixed pre-reserved memory budget, or a
+// latency path that must not pay cudaMalloc's implicit synchronisation).
+//   * Limit: num_tokens * hq * nsplit * (head_dim + 2) floats must not exceed
+//     sh_paged_attention_noalloc_capacity() (SH_ATTN_NOALLOC_MAX_FLOATS,
+//     16 MiB of fp32); larger calls return SH_NOALLOC_ERR_TOO_LARGE.
+//   * The first call on each device looks the array up with
+//     cudaGetSymbolAddress (that device must be current); make it before any
+//     CUDA-graph stream capture.
+//   * All calls share the array: calls that overlap on the GPU race.
+//   * Every GPU that loads the library holds the array until process exit.
+#define SH_ATTN_NOALLOC_MAX_FLOATS (4ll * 1024 * 1024)
+#define SH_NOALLOC_ERR_ARGS -101
+#define SH_NOALLOC_ERR_TOO_LARGE -102
+#define SH_NOALLOC_ERR_DEVICE -103
+#define SH_NOALLOC_ERR_SYMBOL -104
+int sh_paged_attention_noalloc(const AttnParams* params, int ntiles, int num_blocks, int head_dim, int max_rows,
+                               cudaStream_t stream);
+int64_t sh_paged_attention_noalloc_capacity(void);
 #ifdef __cplusplus
 }
 #endif
