@@ -50,6 +50,8 @@ def main():
     ap.add_argument("--max-new", type=int, default=512)
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                    help="TP collectives: own NVLink kernels (fused) or the NCCL baseline")
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for bench)")
     ap.add_argument("--profile", action="store_true",
                     help="profile one eager decode step between cudaProfilerStart/Stop (for ncu) and exit")
@@ -77,7 +79,7 @@ def main():
     if args.layers:
         mcfg.layers = args.layers
     cfg = EngineConfig(model=mcfg, spec=SpecConfig(method=args.method, k=args.k, split=args.split),
-                       parallel=ParallelConfig(tp=args.gpus),
+                       parallel=ParallelConfig(tp=args.gpus, comm=args.comm),
                        cache=CacheConfig(max_model_len=args.prompt_len + args.max_new + 4 * args.k + 64),
                        max_num_seqs=args.batch, device="cuda", cuda_graphs=not args.no_graphs)
     if args.split == "diverge":
@@ -163,7 +165,7 @@ def main():
             "data": "synthetic (config-0 span-reuse token streams, vocab 128256); random-init weights N(0,0.02)",
             "config": {"model": "llama3-8b-shape" if args.config == "llama3-8b" else args.config,
                        "global_batch": args.batch, "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
-                       "k": args.k, "method": args.method, "split": args.split, "parallelism": f"tp{world}",
+                       "k": args.k, "method": args.method, "split": args.split, "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
                        "l2": "working set (weights + KV) >> 126 MB L2; no flush",
                        "layers": mcfg.layers},
             "mean_accept_len": round(tokens / rows, 4),

@@ -3,6 +3,7 @@
 #include <torch/extension.h>
 
 #include "gemm_tcgen05.h"
+#include "comm.h"
 #include "paged_attention.h"
 
 void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
@@ -97,6 +98,43 @@ void gemm_bf16(torch::Tensor y, torch::Tensor x, torch::Tensor w, bool swap, int
   TORCH_CHECK(r == 0, "sh_gemm_bf16_tcgen05 failed with code ", r);
 }
 
+// Fused NVLink all-reduce (+ residual add + RMSNorm).  peer_* are device
+// addresses (ints) of every rank's symmetric buffers / signal pads.
+void allreduce_fused(std::vector<int64_t> peer_in, std::vector<int64_t> peer_gather, std::vector<int64_t> peer_flags,
+                     torch::Tensor counters, torch::Tensor out, c10::optional<torch::Tensor> residual,
+                     c10::optional<torch::Tensor> weight, torch::Tensor err, int64_t rank, int64_t T, int64_t H,
+                     double eps, bool two_shot, int64_t num_blocks) {
+  const int world = static_cast<int>(peer_in.size());
+  TORCH_CHECK(world >= 1 && world <= SH_COMM_MAX_WORLD && peer_gather.size() == peer_in.size() &&
+                  peer_flags.size() == peer_in.size(), "allreduce_fused: peer lists");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() >= T * H, "out");
+  TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= SH_COMM_MAX_BLOCKS, "counters");
+  ArParams p{};
+  for (int i = 0; i < world; ++i) {
+    p.peer_in[i] = reinterpret_cast<const __nv_bfloat16*>(peer_in[i]);
+    p.peer_gather[i] = reinterpret_cast<__nv_bfloat16*>(peer_gather[i]);
+    p.peer_flags[i] = reinterpret_cast<uint32_t*>(peer_flags[i]);
+  }
+  p.counters = reinterpret_cast<uint32_t*>(counters.data_ptr<int>());
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.fuse_norm = residual.has_value() ? 1 : 0;
+  if (p.fuse_norm) {
+    TORCH_CHECK(weight.has_value() && residual->is_contiguous() && residual->scalar_type() == at::kBFloat16,
+                "allreduce_fused: residual/weight");
+    p.residual = reinterpret_cast<__nv_bfloat16*>(residual->data_ptr());
+    p.weight = reinterpret_cast<const __nv_bfloat16*>(weight->data_ptr());
+  }
+  p.err = err.data_ptr<int>();
+  p.rank = static_cast<int>(rank);
+  p.world = world;
+  p.T = static_cast<int>(T);
+  p.H = static_cast<int>(H);
+  p.eps = static_cast<float>(eps);
+  p.two_shot = two_shot ? 1 : 0;
+  const int r = sh_allreduce(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_allreduce failed with code ", r);
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200 (sm_100a) kernels: fused norms, RoPE+cache write, paged attention, GEMMs, verify, comm";
   m.def("rms_norm", &rms_norm);
@@ -110,6 +148,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_cache"), py::arg("block_tables"), py::arg("seq_lens"), py::arg("q_start"), py::arg("tile_req"),
         py::arg("tile_row0"), py::arg("hq"), py::arg("scale"), py::arg("nsplit") = 1, py::arg("part_o") = py::none(),
         py::arg("part_ml") = py::none(), py::arg("err") = py::none(), py::arg("max_rows") = 64);
+  m.def("allreduce_fused", &allreduce_fused);
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM", py::arg("y"), py::arg("x"), py::arg("w"), py::arg("swap"),
         py::arg("bn"), py::arg("splits"), py::arg("ws") = py::none(), py::arg("err") = py::none());
 }

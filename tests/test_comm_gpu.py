@@ -1,0 +1,85 @@
+"""Fused NVLink all-reduce + residual add + RMSNorm on 2+ GPUs.
+
+Each rank writes a random partial into its symmetric buffer; the fused
+kernel's one-shot and two-shot paths must match an fp32 reference of
+rms_norm(residual + sum of partials) and be bit-identical on every rank.
+Skipped on hosts with fewer than two GPUs.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from vllm_suffix_hybrid_b200.parallel import state
+    from vllm_suffix_hybrid_b200.parallel.symm import SymmComm
+
+    state.init(tp=world, backend="nccl", timeout_s=60)
+    try:
+        H, T = 4096, 384
+        comm = SymmComm(H, T)
+        results = {}
+        for mode, thresh in (("one_shot", 1 << 30), ("two_shot", 0)):
+            comm.one_shot_max_bytes = thresh
+            g = torch.Generator(device="cuda").manual_seed(100 + rank)
+            part = comm.partial(T)
+            part.copy_(torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16))
+            gw = torch.Generator(device="cuda").manual_seed(7)
+            resid = torch.randn(T, H, device="cuda", generator=gw).to(torch.bfloat16)
+            w = torch.randn(H, device="cuda", generator=gw).to(torch.bfloat16)
+            full = part.float().clone()
+            dist.all_reduce(full)
+            r_ref = (resid.float() + full).to(torch.bfloat16).float()
+            x_ref = r_ref * torch.rsqrt(r_ref.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+            resid_k = resid.clone()
+            dist.barrier()
+            x = comm.all_reduce_add_rms_norm(part, resid_k, w, 1e-5)
+            torch.cuda.synchronize()
+            comm.check()
+            err_x = (x.float() - x_ref).abs().max().item()
+            err_r = (resid_k.float() - r_ref).abs().max().item()
+            gathered = [torch.empty_like(x) for _ in range(world)]
+            dist.all_gather(gathered, x)
+            same = all(torch.equal(gathered[0], t) for t in gathered)
+            results[mode] = (err_x, err_r, same)
+        q.put((rank, results))
+    finally:
+        torch.cuda.synchronize()
+        state.shutdown()
+
+
+def test_fused_allreduce_rmsnorm_multi_gpu():
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs >= 2 GPUs")
+    world = min(world, 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, modes in res.items():
+        for mode, (ex, er, same) in modes.items():
+            assert ex < 0.1 and er < 0.1 and same, (rank, mode, ex, er, same)

@@ -78,6 +78,12 @@ class LLMEngine:
         spec = cfg.spec
         self.k = spec.k if spec.method != "none" else 0
         self.model, self.draft = build_model(mcfg, dev, cfg.seed, with_draft=spec.method in ("hybrid", "native"))
+        if st.tp > 1 and cfg.parallel.comm == "fused" and torch.device(dev).type == "cuda":
+            from ..parallel import comm as pcomm
+            from ..parallel.symm import SymmComm
+
+            max_tok = max(cfg.max_prefill_tokens, cfg.max_num_seqs * (spec.k + 1))
+            pcomm.set_fused(SymmComm(mcfg.hidden, max_tok))
         if cfg.weights:
             from .loader import load_weights
 

@@ -74,6 +74,8 @@ class Linear:
         self.out_f, self.in_f = full.shape
 
     def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None and self.parallel == "row":
+            out = comm.partial_out(x.shape[0], self.out_f, x)  # symmetric buffer under fused TP comm
         return ops.linear(x, self.weight, out)
 
 
@@ -137,7 +139,7 @@ class DecoderLayer:
     def __call__(self, x: torch.Tensor, residual: torch.Tensor, meta: AttnMeta, kv, first: bool):
         """x: the normalised input of this layer (residual holds the stream)."""
         h = self.attn(x, meta, kv)
-        comm.all_reduce_add_rms_norm(h, residual, self.post_norm.weight, self.post_norm.eps)
+        h = comm.all_reduce_add_rms_norm(h, residual, self.post_norm.weight, self.post_norm.eps)
         m = self.mlp(h)
         return m  # partial; the next layer's input norm reduces + adds it
 

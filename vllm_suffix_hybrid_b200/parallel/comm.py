@@ -37,16 +37,24 @@ def all_reduce(x: torch.Tensor) -> torch.Tensor:
     return x
 
 
-def all_reduce_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> None:
-    """x <- rms_norm(residual + allreduce(x)) * w, residual <- residual + allreduce(x)."""
+def partial_out(tokens: int, hidden: int, like: torch.Tensor) -> Optional[torch.Tensor]:
+    """Where a row-parallel GEMM should write its partial (the symmetric buffer when fused comm is on)."""
+    if _FUSED is not None and state.get().tp > 1 and hidden == _FUSED.hidden and tokens <= _FUSED.max_tokens:
+        return _FUSED.partial(tokens)
+    return None
+
+
+def all_reduce_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """residual += allreduce(x); returns rms_norm(residual) * w (x may be reused as the output)."""
     from .. import ops
 
     st = state.get()
     if st.tp > 1 and _FUSED is not None and _FUSED.can_all_reduce(x):
-        _FUSED.all_reduce_add_rms_norm(x, residual, w, eps)
-        return
-    all_reduce(x)
+        return _FUSED.all_reduce_add_rms_norm(x, residual, w, eps)
+    if st.tp > 1:
+        dist.all_reduce(x, group=st.group)
     ops.fused_add_rms_norm(x, residual, w, eps)
+    return x
 
 
 def vocab_parallel_argmax(local_logits: torch.Tensor, vocab_offset: int, out: Optional[torch.Tensor] = None):
@@ -59,8 +67,13 @@ def vocab_parallel_argmax(local_logits: torch.Tensor, vocab_offset: int, out: Op
         return idx
     val = local_logits.gather(1, idx[:, None]).float()[:, 0]
     pair = torch.stack([val, (idx + vocab_offset).float()], dim=1)  # exact for ids < 2^24
-    gathered = torch.empty(st.tp, *pair.shape, dtype=pair.dtype, device=pair.device)
-    dist.all_gather_into_tensor(gathered, pair, group=st.group)
+    if pair.is_cuda:
+        gathered = torch.empty(st.tp, *pair.shape, dtype=pair.dtype, device=pair.device)
+        dist.all_gather_into_tensor(gathered, pair, group=st.group)
+    else:
+        parts = [torch.empty_like(pair) for _ in range(st.tp)]
+        dist.all_gather(parts, pair, group=st.group)
+        gathered = torch.stack(parts)
     vals, ids = gathered[..., 0], gathered[..., 1]
     best = vals.max(0, keepdim=True).values
     # Lowest global id among the maxima (first-occurrence semantics).

@@ -1,0 +1,92 @@
+"""Symmetric-memory communicator for tensor parallelism over NVLink.
+
+Buffers come from torch's symmetric-memory allocator (one mapping of every
+rank's buffer in every process); the data path is this framework's own
+kernel (``_C.allreduce_fused``): row-parallel GEMMs write their partial sums
+straight into ``partial(T)``, and one kernel reduces them across ranks over
+NVLink peer loads/stores and applies the residual add + RMSNorm.
+
+Routing by message size (the reference routes its all-reduce by size bands
+too, reference: suffix_hybrid/nccl_split.py:63-77): one-shot below
+``one_shot_max_bytes`` (latency), two-shot reduce-scatter/all-gather above it
+(bandwidth).  Device-side waits time out into ``err``; ``check()`` raises on
+the host if any collective failed.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import state
+
+MAX_BLOCKS = 160
+
+
+class SymmComm:
+    def __init__(self, hidden: int, max_tokens: int, dtype=torch.bfloat16, group=None,
+                 one_shot_max_bytes: Optional[int] = None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        st = state.get()
+        self.rank, self.world = st.rank, st.world
+        self.group = group or st.group
+        self.hidden, self.max_tokens = hidden, max_tokens
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.partial_buf = symm_mem.empty(max_tokens, hidden, dtype=dtype, device=dev)
+        self.gather_buf = symm_mem.empty(max_tokens, hidden, dtype=dtype, device=dev)
+        name = self.group.group_name if hasattr(self.group, "group_name") else dist.group.WORLD.group_name
+        h_in = symm_mem.rendezvous(self.partial_buf, name)
+        h_g = symm_mem.rendezvous(self.gather_buf, name)
+        self.peer_in = [int(x) for x in h_in.buffer_ptrs]
+        self.peer_gather = [int(x) for x in h_g.buffer_ptrs]
+        self.peer_flags = [int(x) for x in h_in.signal_pad_ptrs]
+        self._handles = (h_in, h_g)
+        self.counters = torch.zeros(MAX_BLOCKS, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.max_blocks = min(MAX_BLOCKS, sms)
+        env = os.environ.get("SH_ONE_SHOT_MAX_BYTES")
+        self.one_shot_max_bytes = int(env) if env else (one_shot_max_bytes or (1 << 20))
+        dist.barrier(group=self.group)
+
+    # -- buffers --------------------------------------------------------------
+    def partial(self, tokens: int) -> torch.Tensor:
+        """The [tokens, hidden] slice a row-parallel GEMM writes its partial into."""
+        if tokens > self.max_tokens:
+            raise ValueError(f"{tokens} tokens exceed the symmetric buffer ({self.max_tokens})")
+        return self.partial_buf[:tokens]
+
+    def owns(self, x: torch.Tensor) -> bool:
+        return x.data_ptr() == self.partial_buf.data_ptr() and x.shape[-1] == self.hidden
+
+    def can_all_reduce(self, x: torch.Tensor) -> bool:
+        return self.owns(x) and x.shape[0] <= self.max_tokens
+
+    # -- collectives ----------------------------------------------------------
+    def _launch(self, x: torch.Tensor, out: torch.Tensor, residual=None, weight=None, eps: float = 0.0) -> None:
+        from .. import ops
+
+        T, H = x.shape
+        two_shot = T * H * x.element_size() > self.one_shot_max_bytes and T >= self.world
+        blocks = max(1, min(self.max_blocks, T))
+        ops.native().allreduce_fused(self.peer_in, self.peer_gather, self.peer_flags, self.counters, out, residual,
+                                     weight, self.err, self.rank, T, H, eps, two_shot, blocks)
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        out = torch.empty_like(x)
+        self._launch(x, out)
+        return out
+
+    def all_reduce_add_rms_norm(self, x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
+                                eps: float) -> torch.Tensor:
+        out = torch.empty_like(x)
+        self._launch(x, out, residual, w, eps)
+        return out
+
+    def check(self) -> None:
+        code = int(self.err.item())
+        if code:
+            raise RuntimeError(f"symmetric-memory collective timed out or failed (code {code}) on rank {self.rank}")
