@@ -4,6 +4,8 @@
 
 #include "gemm_tcgen05.h"
 #include "comm.h"
+#include "gdn.h"
+#include "moe.h"
 #include "paged_attention.h"
 
 void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
@@ -135,6 +137,140 @@ void allreduce_fused(std::vector<int64_t> peer_in, std::vector<int64_t> peer_gat
   TORCH_CHECK(r == 0, "sh_allreduce failed with code ", r);
 }
 
+template <typename T>
+static T* ptr(const torch::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+#define SH_CHECK_RC(rc, what) TORCH_CHECK((rc) == 0, what " failed with code ", (rc))
+
+// --- Gated DeltaNet -----------------------------------------------------------
+void gdn_conv(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor state, torch::Tensor rec_x,
+              torch::Tensor pending, torch::Tensor slots, torch::Tensor q_start, int64_t W, int64_t mode) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kFloat &&
+                  state.scalar_type() == at::kFloat && rec_x.scalar_type() == at::kFloat, "gdn_conv dtypes");
+  GdnConvParams p{};
+  p.x = ptr<const __nv_bfloat16>(x);
+  p.x_stride = x.stride(0);
+  p.w = ptr<const float>(w);
+  p.y = ptr<__nv_bfloat16>(y);
+  p.state = ptr<float>(state);
+  p.rec_x = ptr<float>(rec_x);
+  p.pending = ptr<const int32_t>(pending);
+  p.slots = ptr<const int64_t>(slots);
+  p.q_start = ptr<const int64_t>(q_start);
+  p.C = static_cast<int>(w.size(0));
+  p.KW = static_cast<int>(w.size(1));
+  p.W = static_cast<int>(W);
+  p.mode = static_cast<int>(mode);
+  SH_CHECK_RC(sh_gdn_conv(&p, static_cast<int>(slots.numel()), at::cuda::getCurrentCUDAStream()), "sh_gdn_conv");
+}
+
+void gdn_recurrent(torch::Tensor qkv, torch::Tensor z, torch::Tensor ba, torch::Tensor a_log, torch::Tensor dt_bias,
+                   torch::Tensor norm_w, torch::Tensor state, torch::Tensor rec_k, torch::Tensor rec_v,
+                   torch::Tensor rec_g, torch::Tensor rec_b, torch::Tensor pending, torch::Tensor slots,
+                   torch::Tensor q_start, torch::Tensor out, int64_t H, int64_t HV, int64_t K, int64_t W,
+                   int64_t mode, double eps) {
+  TORCH_CHECK(state.scalar_type() == at::kFloat && qkv.scalar_type() == at::kBFloat16, "gdn_recurrent dtypes");
+  GdnParams p{};
+  p.qkv = ptr<const __nv_bfloat16>(qkv);
+  p.qkv_stride = qkv.stride(0);
+  p.z = ptr<const __nv_bfloat16>(z);
+  p.z_stride = z.stride(0);
+  p.ba = ptr<const __nv_bfloat16>(ba);
+  p.ba_stride = ba.stride(0);
+  p.a_log = ptr<const float>(a_log);
+  p.dt_bias = ptr<const float>(dt_bias);
+  p.norm_w = ptr<const __nv_bfloat16>(norm_w);
+  p.state = ptr<float>(state);
+  p.rec_k = ptr<float>(rec_k);
+  p.rec_v = ptr<float>(rec_v);
+  p.rec_g = ptr<float>(rec_g);
+  p.rec_b = ptr<float>(rec_b);
+  p.pending = ptr<const int32_t>(pending);
+  p.slots = ptr<const int64_t>(slots);
+  p.q_start = ptr<const int64_t>(q_start);
+  p.out = ptr<__nv_bfloat16>(out);
+  p.out_stride = out.stride(0);
+  p.H = static_cast<int>(H);
+  p.HV = static_cast<int>(HV);
+  p.K = static_cast<int>(K);
+  p.V = static_cast<int>(K);
+  p.W = static_cast<int>(W);
+  p.mode = static_cast<int>(mode);
+  p.eps = static_cast<float>(eps);
+  SH_CHECK_RC(sh_gdn_recurrent(&p, static_cast<int>(slots.numel()), at::cuda::getCurrentCUDAStream()),
+              "sh_gdn_recurrent");
+}
+
+// --- MoE -------------------------------------------------------------------------
+void moe_route(torch::Tensor logits, c10::optional<torch::Tensor> bias, torch::Tensor ids, torch::Tensor weights,
+               int64_t k, bool sigmoid_grouped, int64_t n_groups, int64_t topk_groups, bool renorm, double scale) {
+  RouteParams p{};
+  p.logits = logits.data_ptr();
+  p.logits_bf16 = logits.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(p.logits_bf16 || logits.scalar_type() == at::kFloat, "router logits bf16/f32");
+  p.bias = bias.has_value() ? ptr<const float>(*bias) : nullptr;
+  p.ids = ptr<int32_t>(ids);
+  p.weights = ptr<float>(weights);
+  p.T = static_cast<int>(logits.size(0));
+  p.E = static_cast<int>(logits.size(1));
+  p.k = static_cast<int>(k);
+  p.sigmoid_grouped = sigmoid_grouped;
+  p.n_groups = static_cast<int>(n_groups);
+  p.topk_groups = static_cast<int>(topk_groups);
+  p.renorm = renorm;
+  p.scale = static_cast<float>(scale);
+  SH_CHECK_RC(sh_moe_route(&p, at::cuda::getCurrentCUDAStream()), "sh_moe_route");
+}
+
+void moe_align(torch::Tensor ids, torch::Tensor rank, torch::Tensor offsets, torch::Tensor sorted_pos,
+               torch::Tensor sorted_token, torch::Tensor groups, torch::Tensor num_groups, int64_t E, int64_t bn,
+               int64_t rows_per_expert) {
+  AlignParams p{};
+  p.ids = ptr<const int32_t>(ids);
+  p.rank = ptr<int32_t>(rank);
+  p.offsets = ptr<int32_t>(offsets);
+  p.sorted_pos = ptr<int32_t>(sorted_pos);
+  p.sorted_token = ptr<int32_t>(sorted_token);
+  p.groups = ptr<int4>(groups);
+  p.num_groups = ptr<int>(num_groups);
+  p.T = static_cast<int>(ids.size(0));
+  p.k = static_cast<int>(ids.size(1));
+  p.E = static_cast<int>(E);
+  p.bn = static_cast<int>(bn);
+  p.max_groups = static_cast<int>(groups.size(0));
+  p.rows_per_expert = static_cast<int>(rows_per_expert);
+  SH_CHECK_RC(sh_moe_align(&p, at::cuda::getCurrentCUDAStream()), "sh_moe_align");
+}
+
+void moe_gather(torch::Tensor out, torch::Tensor x, torch::Tensor sorted_token, torch::Tensor total) {
+  SH_CHECK_RC(sh_moe_gather(ptr<__nv_bfloat16>(out), ptr<const __nv_bfloat16>(x), ptr<const int32_t>(sorted_token),
+                            ptr<const int>(total), static_cast<int>(out.size(0)), static_cast<int>(x.size(1)),
+                            at::cuda::getCurrentCUDAStream()),
+              "sh_moe_gather");
+}
+
+void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor sorted_pos, torch::Tensor w, bool accumulate) {
+  SH_CHECK_RC(sh_moe_combine(ptr<__nv_bfloat16>(out), ptr<const __nv_bfloat16>(y), ptr<const int32_t>(sorted_pos),
+                             ptr<const float>(w), static_cast<int>(out.size(0)), static_cast<int>(w.size(1)),
+                             static_cast<int>(out.size(1)), accumulate, at::cuda::getCurrentCUDAStream()),
+              "sh_moe_combine");
+}
+
+// Grouped expert GEMM: out[q_total, rows_p] over device-side tiles (see gemm_tcgen05.h).
+void gemm_grouped(torch::Tensor out, torch::Tensor q, torch::Tensor w_stacked, int64_t rows_p, torch::Tensor groups,
+                  torch::Tensor num_groups, int64_t bn) {
+  static int num_sms = 0;
+  if (!num_sms) num_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  TORCH_CHECK(q.is_contiguous() && w_stacked.is_contiguous() && out.is_contiguous(), "gemm_grouped: contiguous");
+  SH_CHECK_RC(sh_gemm_bf16_grouped(w_stacked.data_ptr(), static_cast<int>(w_stacked.size(0)), static_cast<int>(rows_p),
+                                   q.data_ptr(), static_cast<int>(q.size(0)), static_cast<int>(q.size(1)),
+                                   out.data_ptr(), out.stride(0), ptr<const int4>(groups), ptr<const int>(num_groups),
+                                   static_cast<int>(groups.size(0)), static_cast<int>(bn), nullptr, num_sms,
+                                   at::cuda::getCurrentCUDAStream()),
+              "sh_gemm_bf16_grouped");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200 (sm_100a) kernels: fused norms, RoPE+cache write, paged attention, GEMMs, verify, comm";
   m.def("rms_norm", &rms_norm);
@@ -149,6 +285,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("tile_row0"), py::arg("hq"), py::arg("scale"), py::arg("nsplit") = 1, py::arg("part_o") = py::none(),
         py::arg("part_ml") = py::none(), py::arg("err") = py::none(), py::arg("max_rows") = 64);
   m.def("allreduce_fused", &allreduce_fused);
+  m.def("gdn_conv", &gdn_conv);
+  m.def("gdn_recurrent", &gdn_recurrent);
+  m.def("moe_route", &moe_route);
+  m.def("moe_align", &moe_align);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_combine", &moe_combine);
+  m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM", py::arg("y"), py::arg("x"), py::arg("w"), py::arg("swap"),
         py::arg("bn"), py::arg("splits"), py::arg("ws") = py::none(), py::arg("err") = py::none());
 }

@@ -151,10 +151,25 @@ struct Smem {
 
 struct Work {
   int tp, tq, sp;
+  int p_y, q_y;       // TMA row coordinates of the P and Q tiles
+  int p_lim, q_lim;   // valid rows: p < p_lim (tile-local base tp*BM), q in [q_y, q_lim)
+  int q_base;         // output row base for q
 };
 
-__device__ __forceinline__ Work decode_work(int w, const GemmParams& g) {
+__device__ __forceinline__ Work decode_work(int w, const GemmParams& g, int bn) {
   Work r;
+  if (g.groups) {
+    const int4 e = g.groups[w / g.tiles_p];
+    r.sp = 0;
+    r.tp = w % g.tiles_p;
+    r.tq = 0;
+    r.p_y = e.z + r.tp * BM;
+    r.q_y = e.x;
+    r.p_lim = g.rows_p;
+    r.q_lim = e.x + e.y;
+    r.q_base = e.x;
+    return r;
+  }
   const int tiles = g.tiles_p * g.tiles_q;
   r.sp = w / tiles;
   const int t = w % tiles;
@@ -165,6 +180,11 @@ __device__ __forceinline__ Work decode_work(int w, const GemmParams& g) {
     r.tq = t % g.tiles_q;
     r.tp = t / g.tiles_q;
   }
+  r.p_y = r.tp * BM;
+  r.q_y = r.tq * bn;
+  r.p_lim = g.rows_p;
+  r.q_lim = g.rows_q;
+  r.q_base = r.tq * bn;
   return r;
 }
 
@@ -208,7 +228,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int total_work = g.tiles_p * g.tiles_q * g.splits;
+  const int total_work = g.groups ? (*g.num_groups) * g.tiles_p : g.tiles_p * g.tiles_q * g.splits;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -218,7 +238,7 @@ __global__ void __launch_bounds__(192, 1)
       int64_t issued = 0;
       bool aborted = false;
       for (int w = blockIdx.x; w < total_work && !aborted; w += gridDim.x) {
-        const Work wk = decode_work(w, g);
+        const Work wk = decode_work(w, g, BN);
         const int kb0 = wk.sp * g.kb_per_split;
         const int kb1 = min(kb0 + g.kb_per_split, g.kb_total);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -230,8 +250,8 @@ __global__ void __launch_bounds__(192, 1)
           }
           mbar_expect_tx(&full[stage], S::STAGE_BYTES);
           uint8_t* sp = smem + stage * S::STAGE_BYTES;
-          tma_load_2d(sp, &tmP, kb * BK, wk.tp * BM, &full[stage]);
-          tma_load_2d(sp + S::P_BYTES, &tmQ, kb * BK, wk.tq * BN, &full[stage]);
+          tma_load_2d(sp, &tmP, kb * BK, wk.p_y, &full[stage]);
+          tma_load_2d(sp + S::P_BYTES, &tmQ, kb * BK, wk.q_y, &full[stage]);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -254,7 +274,7 @@ __global__ void __launch_bounds__(192, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int w = blockIdx.x; w < total_work; w += gridDim.x) {
-        const Work wk = decode_work(w, g);
+        const Work wk = decode_work(w, g, BN);
         const int kb0 = wk.sp * g.kb_per_split;
         const int kb1 = min(kb0 + g.kb_per_split, g.kb_total);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
@@ -306,7 +326,7 @@ __global__ void __launch_bounds__(192, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int w = blockIdx.x; w < total_work; w += gridDim.x) {
-      const Work wk = decode_work(w, g);
+      const Work wk = decode_work(w, g, BN);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
         if (g.err && lane == 0) atomicCAS(g.err, 0, 4);
         *abort_flag = 1;
@@ -320,19 +340,19 @@ __global__ void __launch_bounds__(192, 1)
         float v[16];
         __syncwarp();
         tmem_ld16(tbase + c, v);
-        const int q0 = wk.tq * BN + c;
-        if (p >= g.rows_p) {
+        const int q0 = wk.q_base + c;
+        if (p >= wk.p_lim) {
         } else if (SPLIT) {
           float* dst = g.ws + (static_cast<int64_t>(wk.sp) * g.rows_p + p) * g.rows_q + q0;
-          if (q0 + 16 <= g.rows_q && (g.rows_q & 3) == 0) {
+          if (q0 + 16 <= wk.q_lim && (g.rows_q & 3) == 0) {
 #pragma unroll
             for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
           } else {
-            for (int i = 0; i < 16 && q0 + i < g.rows_q; ++i) dst[i] = v[i];
+            for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i) dst[i] = v[i];
           }
         } else if (!TRANS) {
           __nv_bfloat16* dst = g.out + static_cast<int64_t>(p) * g.ldo + q0;
-          if (q0 + 16 <= g.rows_q && (g.ldo & 7) == 0) {
+          if (q0 + 16 <= wk.q_lim && (g.ldo & 7) == 0) {
             uint4 pk[2];
             __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(pk);
 #pragma unroll
@@ -340,10 +360,10 @@ __global__ void __launch_bounds__(192, 1)
             reinterpret_cast<uint4*>(dst)[0] = pk[0];
             reinterpret_cast<uint4*>(dst)[1] = pk[1];
           } else {
-            for (int i = 0; i < 16 && q0 + i < g.rows_q; ++i) dst[i] = __float2bfloat16(v[i]);
+            for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i) dst[i] = __float2bfloat16(v[i]);
           }
         } else {
-          for (int i = 0; i < 16 && q0 + i < g.rows_q; ++i)
+          for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i)
             g.out[static_cast<int64_t>(q0 + i) * g.ldo + p] = __float2bfloat16(v[i]);
         }
       }
@@ -510,4 +530,41 @@ extern "C" int sh_gemm_bf16_tcgen05(const void* P, int rows_p, int64_t ldp, cons
     if (r) return 4000 + r;
   }
   return 0;
+}
+
+extern "C" int sh_gemm_bf16_grouped(const void* P, int p_total_rows, int rows_p, const void* Q, int q_total, int K,
+                                    void* out, int64_t ldo, const int4* groups, const int* num_groups, int max_groups,
+                                    int bn, int* err, int num_sms, cudaStream_t stream) {
+  if (K % BK != 0 || K <= 0) return -2;
+  if (p_total_rows <= 0 || q_total <= 0 || max_groups <= 0) return 0;
+  if ((reinterpret_cast<uintptr_t>(P) & 15) || (reinterpret_cast<uintptr_t>(Q) & 15)) return -3;
+  if (bn != 64 && bn != 128 && bn != 256) return -4;
+  CUtensorMap mp, mq;
+  int r = make_map(&mp, P, p_total_rows, K, K, BM);
+  if (r) return 1000 + r;
+  r = make_map(&mq, Q, q_total, K, K, bn);
+  if (r) return 2000 + r;
+  GemmParams g{};
+  g.rows_p = rows_p;
+  g.rows_q = q_total;
+  g.tiles_p = (rows_p + BM - 1) / BM;
+  g.tiles_q = 1;
+  g.splits = 1;
+  g.kb_total = K / BK;
+  g.kb_per_split = K / BK;
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.ldo = static_cast<int>(ldo);
+  g.err = err;
+  g.p_fast = 1;
+  g.groups = groups;
+  g.num_groups = num_groups;
+  const int work = max_groups * g.tiles_p;
+  const int grid = work < num_sms ? work : num_sms;
+  if (bn == 256)
+    r = launch_bn<256, 4>(mp, mq, g, grid, true, false, stream);
+  else if (bn == 128)
+    r = launch_bn<128, 6>(mp, mq, g, grid, true, false, stream);
+  else
+    r = launch_bn<64, 8>(mp, mq, g, grid, true, false, stream);
+  return r ? 3000 + r : 0;
 }

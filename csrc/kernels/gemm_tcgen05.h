@@ -13,6 +13,12 @@ struct GemmParams {
   float* ws;
   int* err;
   int p_fast;
+  // Grouped (MoE) mode when groups != nullptr: work unit = (group entry, P
+  // tile).  Entry = {q_row0, q_rows, p_row_offset, unused}: the Q tile starts at
+  // sorted row q_row0 and holds q_rows valid rows; P tiles start at row
+  // p_row_offset (the expert's first weight row) and span rows_p rows.
+  const int4* groups;
+  const int* num_groups;
 };
 
 #ifdef __cplusplus
@@ -26,6 +32,14 @@ extern "C" {
 int sh_gemm_bf16_tcgen05(const void* P, int rows_p, int64_t ldp, const void* Q, int rows_q, int64_t ldq, int K,
                          void* out, int64_t ldo, int trans, int bn, int splits, float* ws, int* err, int num_sms,
                          cudaStream_t stream);
+// Grouped swap-AB GEMM for MoE experts: for every device-side group entry g
+// (see GemmParams::groups), out[q, :] = sum_k Q[q, k] * P[p_row_offset + n, k]
+// for the q_rows sorted rows of the entry and n < rows_p.  P stacks the
+// experts' [rows_p, K] weights; Q holds the expert-sorted activations
+// [q_total, K]; out is [q_total, ldo].  max_groups bounds the list length.
+int sh_gemm_bf16_grouped(const void* P, int p_total_rows, int rows_p, const void* Q, int q_total, int K, void* out,
+                         int64_t ldo, const int4* groups, const int* num_groups, int max_groups, int bn, int* err,
+                         int num_sms, cudaStream_t stream);
 #ifdef __cplusplus
 }
 #endif

@@ -10,6 +10,8 @@ running request.  After each step the proposer picks the next drafts:
 * ``native``  -- native drafts only;
 * ``suffix``  -- drafter-free V2SuffixProposer (uniform-k pallet);
 * ``ngram``   -- weight-free Engine (suffix corpus + in-request n-gram);
+* ``external``-- drafts from a user callable ``engine.external_proposer(requests)
+  -> list[list[int]]`` (a custom drafter hook);
 * ``none``    -- plain one-token decode.
 
 Running requests occupy rows 0..B-1 of the host token buffer in batch order
@@ -47,6 +49,7 @@ class Request:
     accepted_prev: int = -1  # accepted length of the previous proposal (-1 = none)
     finished: bool = False
     arrival: float = 0.0
+    slot: int = 0  # recurrent-state slot (hybrid GDN models)
 
     @property
     def history_len(self) -> int:
@@ -94,9 +97,18 @@ class LLMEngine:
         self.max_blocks_per_seq = blocks_for(self.max_model_len + 2 * self.k + 2, bs)
         num_blocks = cfg.cache.num_blocks or self._auto_blocks()
         self.pool = BlockPool(num_blocks)
-        shape = self.model.kv_cache_shape(num_blocks, bs)
-        self.caches = allocate_caches(mcfg.layers, shape, self.model.dtype, dev)
-        self.dcaches = allocate_caches(1, shape, self.model.dtype, dev)[0] if self.draft is not None else None
+        if hasattr(self.model, "allocate_caches"):
+            self.caches = self.model.allocate_caches(num_blocks, bs, cfg.max_num_seqs + 1, self.k + 1)
+        else:
+            self.caches = allocate_caches(mcfg.layers, self.model.kv_cache_shape(num_blocks, bs), self.model.dtype,
+                                          dev)
+        if self.draft is None:
+            self.dcaches = None
+        elif hasattr(self.draft, "allocate_caches"):
+            self.dcaches = self.draft.allocate_caches(num_blocks, bs)
+        else:
+            self.dcaches = allocate_caches(1, self.model.kv_cache_shape(num_blocks, bs), self.model.dtype, dev)[0]
+        self._free_slots = list(range(cfg.max_num_seqs, 0, -1))
         self.runner = Runner(self.model, self.draft, self.caches, self.dcaches, self.k, cfg.max_num_seqs,
                              self.max_blocks_per_seq, bs, dev, cfg.cuda_graphs)
         self.tokens = np.zeros((cfg.max_num_seqs, self.max_model_len + 2 * self.k + 2), dtype=np.int64)
@@ -106,6 +118,7 @@ class LLMEngine:
         self._ids = itertools.count()
         self.stats: List[StepStats] = []
         self.proposer = None
+        self.external_proposer = None  # callable(list[Request]) -> list[list[int]] for method "external"
         k = max(self.k, 1)
         if spec.method == "hybrid":
             self.proposer = _native.HybridMixer(k, self.tokens.shape[1])
@@ -124,7 +137,8 @@ class LLMEngine:
         free, _ = torch.cuda.mem_get_info()
         m = self.model
         per_block = 2 * self.block_size * m.kv_heads_local * c.model.head_dim * m.embed.element_size()
-        per_block *= c.model.layers + (1 if self.draft is not None else 0)
+        kv_layers = getattr(m, "num_kv_layers", c.model.layers)
+        per_block *= kv_layers + (1 if self.draft is not None else 0)
         budget = int(free * c.cache.gpu_memory_fraction) - (4 << 30)
         return max(need, min(budget // per_block, 4 * need))
 
@@ -180,7 +194,9 @@ class LLMEngine:
             budget -= len(r.prompt)
         for r in batch:
             self._ensure_blocks(r, len(r.prompt) + 2 * self.k + 2)
-        first, natives = self.runner.prefill([r.prompt for r in batch], [r.blocks for r in batch])
+            r.slot = self._free_slots.pop()
+        first, natives = self.runner.prefill([r.prompt for r in batch], [r.blocks for r in batch],
+                                             [r.slot for r in batch])
         for i, r in enumerate(batch):
             row = len(self.running)
             self.running.append(r)
@@ -209,7 +225,7 @@ class LLMEngine:
         """Replace each running request's drafts by the proposer's choice."""
         t0 = time.perf_counter_ns()
         n = len(self.running)
-        if n == 0 or self.proposer is None or self.k == 0:
+        if n == 0 or self.k == 0 or (self.proposer is None and self.cfg.spec.method != "external"):
             return 0.0
         method = self.cfg.spec.method
         ids = [r.rid for r in self.running]
@@ -222,6 +238,8 @@ class LLMEngine:
             packed, widths = self.proposer.propose_suffix_only(ids, np.arange(n, dtype=np.int64), counts,
                                                                self.tokens)
             drafts = [list(packed[i, : widths[i]]) for i in range(n)]
+        elif method == "external":
+            drafts = self.external_proposer(self.running) if self.external_proposer else [[] for _ in range(n)]
         else:  # ngram
             drafts = self.proposer.propose([[1]] * n, counts, self.tokens)
         for r, d in zip(self.running, drafts):
@@ -238,6 +256,7 @@ class LLMEngine:
         seq = np.empty(n, dtype=np.int64)
         mb = self.max_blocks_per_seq
         bt = np.zeros((n, mb), dtype=np.int32)
+        slots = np.fromiter((r.slot for r in self.running), dtype=np.int64, count=n)
         for i, r in enumerate(self.running):
             self._ensure_blocks(r, r.committed + 2 * k + 2)
             win[i, 0] = r.next_token
@@ -248,7 +267,7 @@ class LLMEngine:
             seq[i] = r.committed
             bt[i, :len(r.blocks)] = r.blocks
         t1 = time.perf_counter()
-        out, acc, nat = self.runner.decode(n, win, seq, bt)
+        out, acc, nat = self.runner.decode(n, win, seq, bt, slots)
         t2 = time.perf_counter()
         emitted = 0
         accepted = 0
@@ -279,6 +298,9 @@ class LLMEngine:
                 continue
             self.pool.release(r.blocks)
             r.blocks = []
+            if r.slot:
+                self._free_slots.append(r.slot)
+                r.slot = 0
             self.finished[r.rid] = r
             last = len(self.running) - 1
             if i != last:

@@ -61,6 +61,9 @@ class Runner:
         self.next_tok = torch.zeros(B, **L)
         self.native = torch.zeros(B, max(k, 1), **L)
         self.seq_new = torch.zeros(B, **L)
+        self.slots = torch.zeros(B, **L)  # recurrent-state slot per row (0 = scratch)
+        self.pending = torch.zeros(max_batch + 1, dtype=torch.int32, device=device)
+        self.recurrent = bool(getattr(model, "has_recurrent_state", False))
         self.ar_w = torch.arange(W, **L)
         self.ar_b = torch.arange(B, **L)
         pin = torch.device(device).type == "cuda"
@@ -71,6 +74,7 @@ class Runner:
         self.h_out = torch.zeros(B, W, dtype=torch.long, pin_memory=pin)
         self.h_acc = torch.zeros(B, dtype=torch.int32, pin_memory=pin)
         self.h_nat = torch.zeros(B, max(k, 1), dtype=torch.long, pin_memory=pin)
+        self.h_slots = torch.zeros(B, dtype=torch.long, pin_memory=pin)
         self._tiles: Dict[tuple, tuple] = {}
         self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self.event = torch.cuda.Event() if pin else None
@@ -122,6 +126,7 @@ class Runner:
         win, L, bt = self.win[:nb], self.seq[:nb], self.bt[:nb]
         pos = L[:, None] + self.ar_w[None, :]
         meta = self._meta(nb, W, pos, bt, L + W)
+        meta.state_slots, meta.pending, meta.window = self.slots[:nb], self.pending, W
         hid, pre = self.model.forward(win.reshape(-1), meta, self.caches)
         self.target[:nb].copy_(self.model.greedy(hid).view(nb, W))
         lnew = self.seq_new[:nb]
@@ -134,6 +139,8 @@ class Runner:
             self.accept[:nb].zero_()
             self.next_tok[:nb].copy_(self.target[:nb, 0])
             lnew.add_(1)
+        if self.recurrent:  # deferred commit: the next window replays accept+1 records
+            self.pending.index_copy_(0, self.slots[:nb], (self.accept[:nb] + 1).to(torch.int32))
         if self.draft is not None and self.k > 0:
             tok_in = self.out_tokens[:nb].clamp_min(0)
             dh, dpre = self.draft.forward(tok_in.reshape(-1), pre, meta, self.dcaches)
@@ -142,22 +149,25 @@ class Runner:
             f1 = dpre.index_select(0, sel)
             self.native[:nb].copy_(self._draft_steps(d1, f1, lnew, bt, nb))
 
-    def decode(self, nb_real: int, win: np.ndarray, seq: np.ndarray, bt: np.ndarray):
+    def decode(self, nb_real: int, win: np.ndarray, seq: np.ndarray, bt: np.ndarray, slots: np.ndarray = None):
         """Run one decode step; returns host views (out_tokens, accept, native)."""
         nb = bucket_for(nb_real, self.max_batch)
         self.h_win[:nb_real].numpy()[:] = win
         self.h_seq[:nb_real].numpy()[:] = seq
         self.h_bt[:nb_real].numpy()[:, :bt.shape[1]] = bt
-        if nb > nb_real:  # padded rows: scratch block 0, a k+1 window at position 0
+        self.h_slots[:nb_real].numpy()[:] = slots if slots is not None else 0
+        if nb > nb_real:  # padded rows: scratch block 0 and scratch state slot 0
             self.h_win[nb_real:nb] = 0
             self.h_seq[nb_real:nb] = 0
             self.h_bt[nb_real:nb] = 0
+            self.h_slots[nb_real:nb] = 0
         nbt = self.max_blocks
         if self.ev0 is not None:
             self.ev0.record()
         self.win[:nb].copy_(self.h_win[:nb], non_blocking=True)
         self.seq[:nb].copy_(self.h_seq[:nb], non_blocking=True)
         self.bt[:nb, :nbt].copy_(self.h_bt[:nb, :nbt], non_blocking=True)
+        self.slots[:nb].copy_(self.h_slots[:nb], non_blocking=True)
         if self.use_graphs:
             g = self.graphs.get(nb)
             if g is None:
@@ -173,7 +183,7 @@ class Runner:
             self.ev1.record()
             self.ev1.synchronize()
             self.last_device_ms = self.ev0.elapsed_time(self.ev1)
-        self.h2d_bytes = nb * (self.W * 8 + 8 + self.max_blocks * 4)
+        self.h2d_bytes = nb * (self.W * 8 + 8 + 8 + self.max_blocks * 4)
         self.d2h_bytes = nb * (self.W * 8 + 4 + (self.k * 8 if self.draft is not None and self.k > 0 else 0))
         return self.h_out[:nb_real].numpy(), self.h_acc[:nb_real].numpy(), self.h_nat[:nb_real].numpy()
 
@@ -192,7 +202,8 @@ class Runner:
         return g
 
     # ------------------------------------------------------------------ prefill
-    def prefill(self, prompts: List[np.ndarray], block_tables: List[List[int]], start: Optional[List[int]] = None):
+    def prefill(self, prompts: List[np.ndarray], block_tables: List[List[int]],
+                state_slots: Optional[List[int]] = None):
         """Prefill a batch of prompts (each fully). Returns (first tokens [n], native drafts [n, k])."""
         dev = self.device
         n = len(prompts)
@@ -215,7 +226,11 @@ class Runner:
                         tile_row0=torch.tensor(t0, dtype=torch.int32, device=dev), num_tokens=int(sum(lens)),
                         nsplit=ops.attention_splits(len(tr), self.model.kv_heads_local, mb),
                         max_rows=min(64, max(lens) * self.group))
+        slot_t = torch.tensor(state_slots if state_slots is not None else [0] * n, dtype=torch.long, device=dev)
+        meta.state_slots, meta.pending, meta.window = slot_t, self.pending, 0
         hid, pre = self.model.forward(ids, meta, self.caches)
+        if self.recurrent:
+            self.pending.index_fill_(0, slot_t, 0)
         last = qs[1:] - 1
         first = self.model.greedy(hid.index_select(0, last))
         natives = torch.zeros(n, max(self.k, 1), dtype=torch.long, device=dev)

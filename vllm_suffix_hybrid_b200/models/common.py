@@ -36,6 +36,9 @@ class AttnMeta:
     num_tokens: int = 0
     nsplit: int = 1  # KV splits per request (split-KV attention)
     max_rows: int = 64  # most valid rows in any 64-row query tile
+    state_slots: Optional[torch.Tensor] = None  # [B] int64 recurrent-state slot per request
+    pending: Optional[torch.Tensor] = None  # [slots] int32 accepted window records to replay
+    window: int = 0  # verify-window length (0: prefill from an empty state)
 
 
 def init_weight(shape, std: float, dtype, device, gen: Optional[torch.Generator]) -> torch.Tensor:

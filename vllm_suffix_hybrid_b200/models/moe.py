@@ -1,0 +1,65 @@
+"""Mixture-of-experts feed-forward block (Qwen3-Next, DeepSeek-V3.2, Kimi-K2).
+
+Router -> top-k experts (softmax top-k, or sigmoid group-limited top-k with a
+score-correction bias) -> expert-sorted grouped SwiGLU GEMMs on the tcgen05
+tensor cores (device-side tile list, no host sync) -> weighted combine, plus
+an optional shared expert (sigmoid-gated in Qwen3-Next).
+
+Expert parallelism: with EP = N every rank holds E/N experts; tokens routed
+to remote experts are handled by the all-to-all dispatch/combine of
+:mod:`..parallel.ep` (the weights here are then this rank's local experts).
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from ..parallel import comm, state
+from .common import MLP, Linear, init_weight
+
+
+class MoEBlock:
+    def __init__(self, cfg, dtype, device, gen):
+        st = state.get()
+        self.cfg = cfg
+        self.E = cfg.num_experts
+        self.k = cfg.top_k
+        self.F = cfg.expert_ffn
+        self.H = cfg.hidden
+        self.ep = st.ep
+        self.E_local = self.E // max(self.ep, 1)
+        self.gate = init_weight((self.E, cfg.hidden), cfg.init_std, dtype, device, gen)
+        self.bias = (torch.zeros(self.E, dtype=torch.float32, device=device)
+                     if cfg.router == "sigmoid_grouped" else None)
+        # Experts stacked: w13 [E*2F, H] (gate rows then up rows), w2 [E*H, F].
+        self.w13 = init_weight((self.E_local * 2 * self.F, cfg.hidden), cfg.init_std, dtype, device, gen)
+        self.w2 = init_weight((self.E_local * cfg.hidden, self.F), cfg.init_std, dtype, device, gen)
+        self.shared = MLP(cfg.hidden, cfg.shared_ffn, dtype, device, gen) if cfg.shared_experts else None
+        self.shared_gate = (init_weight((1, cfg.hidden), cfg.init_std, dtype, device, gen)
+                            if cfg.shared_experts and cfg.arch == "qwen3_next" else None)
+
+    def route(self, x: torch.Tensor):
+        logits = ops.linear(x, self.gate).float() if not x.is_cuda else ops.linear(x, self.gate)
+        if self.cfg.router == "sigmoid_grouped":
+            return ops.moe_route(logits, self.k, True, self.bias, self.cfg.n_groups, self.cfg.topk_groups, True,
+                                 self.cfg.routed_scale)
+        return ops.moe_route(logits, self.k, False, renorm=True)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """x: normalised input [T, H]; returns the (TP-partial-free) FFN output [T, H]."""
+        ids, w = self.route(x)
+        if self.ep > 1:
+            from ..parallel import ep
+
+            out = ep.dispatch_combine(self, x, ids, w)
+        else:
+            out = ops.moe_experts(x, ids, w, self.w13, self.w2, self.E, self.F)
+        if self.shared is not None:
+            s = self.shared(x)
+            if state.get().tp > 1:
+                s = comm.all_reduce(s)
+            if self.shared_gate is not None:
+                g = torch.sigmoid(ops.linear(x, self.shared_gate).float())
+                s = (s.float() * g).to(s.dtype)
+            out = out + s
+        return out

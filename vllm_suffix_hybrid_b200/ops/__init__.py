@@ -227,3 +227,159 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) ->
         out.copy_(y)
         return out
     return y
+
+
+# ----------------------------------------------------------------------------- Gated DeltaNet
+def gdn_conv(x, w, y, state, rec_x, pending, slots, q_start, W: int, mode: int) -> None:
+    """SiLU(causal depthwise conv) of x [T, >=C] into y [T, C]; mode 0 prefill (commits the taps),
+    mode 1 verify window (replays `pending` records first, records this window's inputs)."""
+    if x.is_cuda:
+        native().gdn_conv(x, w, y, state, rec_x, pending, slots, q_start, W, mode)
+        return
+    C = w.shape[0]
+    for b in range(slots.shape[0]):
+        s = int(slots[b])
+        t0, t1 = int(q_start[b]), int(q_start[b + 1])
+        if mode == 0:
+            st = torch.zeros(C, 3)
+        else:
+            st = state[s].clone()
+            n = int(pending[s])
+            if n:
+                hist = torch.cat([st.t(), rec_x[s, :n]], 0)
+                st = hist[-3:].t().contiguous()
+                state[s] = st
+        yb, new_st = ref.gdn_conv(x[t0:t1, :C], w, st)
+        y[t0:t1] = yb.to(y.dtype)
+        if mode == 0:
+            state[s] = new_st
+        else:
+            rec_x[s, : t1 - t0] = x[t0:t1, :C].float()
+
+
+def gdn_recurrent(qkv, z, ba, a_log, dt_bias, norm_w, state, rec, pending, slots, q_start, out, H, HV, K, W, mode,
+                  eps) -> None:
+    """Gated delta rule over each request's token run (see csrc/kernels/gdn.cu for the math)."""
+    rec_k, rec_v, rec_g, rec_b = rec
+    if qkv.is_cuda:
+        native().gdn_recurrent(qkv, z, ba, a_log, dt_bias, norm_w, state, rec_k, rec_v, rec_g, rec_b, pending, slots,
+                               q_start, out, H, HV, K, W, mode, eps)
+        return
+    rep = HV // H
+    for b in range(slots.shape[0]):
+        s = int(slots[b])
+        t0, t1 = int(q_start[b]), int(q_start[b + 1])
+        if mode == 0:
+            S = torch.zeros(HV, K, K)
+        else:
+            S = state[s].clone()
+            for r in range(int(pending[s])):
+                ref.gdn_step(S, torch.zeros(HV, K), rec_k[s, r], rec_v[s, r], rec_g[s, r], rec_b[s, r])
+            if int(pending[s]):
+                state[s] = S
+            S = S.clone()
+        for t in range(t0, t1):
+            row = qkv[t].float()
+            q = ref.l2norm(row[: H * K].view(H, K)).repeat_interleave(rep, 0) * K ** -0.5
+            k = ref.l2norm(row[H * K:2 * H * K].view(H, K)).repeat_interleave(rep, 0)
+            v = row[2 * H * K:2 * H * K + HV * K].view(HV, K)
+            g, beta = ref.gdn_gates(ba[t, HV:2 * HV], ba[t, :HV], a_log, dt_bias)
+            o = ref.gdn_step(S, q, k, v, g, beta)
+            if mode == 1:
+                i = t - t0
+                rec_k[s, i], rec_v[s, i], rec_g[s, i], rec_b[s, i] = k, v, g, beta
+            out[t, : HV * K] = ref.gated_rms_norm(o, z[t, : HV * K].view(HV, K), norm_w, eps).reshape(-1).to(out.dtype)
+        if mode == 0:
+            state[s] = S
+
+
+# ----------------------------------------------------------------------------- MoE
+def moe_route(logits, k: int, sigmoid_grouped: bool = False, bias=None, n_groups: int = 1, topk_groups: int = 1,
+              renorm: bool = True, scale: float = 1.0):
+    """(ids int32 [T, k], weights f32 [T, k]) of the chosen experts."""
+    T, E = logits.shape
+    if logits.is_cuda:
+        ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+        w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+        native().moe_route(logits, bias, ids, w, k, sigmoid_grouped, n_groups, topk_groups, renorm, scale)
+        return ids, w
+    lf = logits.float()
+    if not sigmoid_grouped:
+        p = lf.softmax(-1)
+        w, ids = p.topk(k, dim=-1)
+    else:
+        sc = torch.sigmoid(lf)
+        sb = sc + (bias.float() if bias is not None else 0.0)
+        if n_groups > 1:
+            g = sb.view(T, n_groups, -1)
+            gs = g.topk(min(2, g.shape[-1]), dim=-1).values.sum(-1)
+            keep = gs.topk(topk_groups, dim=-1).indices
+            mask = torch.ones(T, n_groups, dtype=torch.bool)
+            mask.scatter_(1, keep, False)
+            sb = sb.masked_fill(mask.repeat_interleave(E // n_groups, 1), float("-inf"))
+        ids = sb.topk(k, dim=-1).indices
+        w = sc.gather(1, ids)
+    if renorm:
+        w = w / w.sum(-1, keepdim=True)
+    return ids.int(), (w * scale).float()
+
+
+def moe_experts(x, ids, weights, w13, w2, E: int, F: int, out=None, accumulate: bool = False):
+    """sum_j weights[t, j] * FFN_{ids[t, j]}(x[t]) with SwiGLU experts.
+
+    w13: stacked [E*2F, H] (gate rows then up rows per expert), w2: [E*H, F]."""
+    T, H = x.shape
+    k = ids.shape[1]
+    if not x.is_cuda:
+        res = torch.zeros(T, H, dtype=torch.float32)
+        for e in ids.unique().tolist():
+            tok, slot = (ids == e).nonzero(as_tuple=True)
+            xe = x[tok].float()
+            gu = xe @ w13[e * 2 * F:(e + 1) * 2 * F].float().t()
+            a = torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
+            ye = a.to(x.dtype).float() @ w2[e * H:(e + 1) * H].float().t()
+            res.index_add_(0, tok, ye.to(x.dtype).float() * weights[tok, slot][:, None].float())
+        if out is None:
+            return res.to(x.dtype)
+        if accumulate:
+            out.copy_((out.float() + res).to(out.dtype))
+        else:
+            out.copy_(res.to(out.dtype))
+        return out
+    dev = x.device
+    pairs = T * k
+    bn = 64 if pairs <= E * 64 else 128
+    max_groups = E + pairs // bn + 1
+    C = native()
+    rank = torch.empty(pairs, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    sorted_pos = torch.empty(pairs, dtype=torch.int32, device=dev)
+    sorted_token = torch.zeros(pairs, dtype=torch.int32, device=dev)
+    groups = torch.empty(max_groups, 4, dtype=torch.int32, device=dev)
+    ngroups = torch.empty(1, dtype=torch.int32, device=dev)
+    C.moe_align(ids, rank, offsets, sorted_pos, sorted_token, groups, ngroups, E, bn, 2 * F)
+    xs = torch.empty(pairs, H, dtype=x.dtype, device=dev)
+    C.moe_gather(xs, x, sorted_token, offsets[E:])
+    gu = torch.empty(pairs, 2 * F, dtype=x.dtype, device=dev)
+    C.gemm_grouped(gu, xs, w13, 2 * F, groups, ngroups, bn)
+    a = silu_mul(gu)
+    groups2 = groups.clone()
+    groups2[:, 2] = groups[:, 3] * H  # down-projection weight row offsets
+    ys = torch.empty(pairs, H, dtype=x.dtype, device=dev)
+    C.gemm_grouped(ys, a, w2, H, groups2, ngroups, bn)
+    if out is None:
+        out = torch.empty(T, H, dtype=x.dtype, device=dev)
+        accumulate = False
+    C.moe_combine(out, ys, sorted_pos, weights, accumulate)
+    return out
+
+
+def rms_norm_heads(x3: torch.Tensor, w: torch.Tensor, eps: float) -> None:
+    """In-place RMSNorm over the last dim of a [T, heads, D] strided view (q/k norms)."""
+    if not x3.is_cuda:
+        x3.copy_(ref.rms_norm(x3, w, eps))
+        return
+    T, nh, d = x3.shape
+    tmp = x3.reshape(T * nh, d) if x3.is_contiguous() else x3.contiguous().view(T * nh, d)
+    res = rms_norm(tmp, w, eps)
+    x3.copy_(res.view(T, nh, d))

@@ -101,3 +101,45 @@ def spec_verify(draft, target, seq_lens):
     nxt = target.gather(1, accept.long()[:, None])[:, 0]
     out.scatter_(1, accept.long()[:, None], nxt[:, None])
     return out, accept, nxt, seq_lens + accept.long() + 1
+
+
+# ----------------------------------------------------------------------------- Gated DeltaNet
+def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    xf = x.float()
+    return xf / torch.sqrt((xf * xf).sum(-1, keepdim=True) + eps)
+
+
+def gdn_gates(a: torch.Tensor, b: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor):
+    """g = -exp(a_log) * softplus(a + dt_bias) (softplus(x) = x above 20), beta = sigmoid(b)."""
+    x = a.float() + dt_bias.float()
+    sp = torch.where(x > 20.0, x, torch.log1p(torch.exp(torch.clamp(x, max=20.0))))
+    return -torch.exp(a_log.float()) * sp, torch.sigmoid(b.float())
+
+
+def gdn_step(S: torch.Tensor, q, k, v, g, beta):
+    """One recurrent step for all heads. S [HV, V, K] fp32 (updated in place); q,k [HV, K] (normed,
+    q pre-scaled); v [HV, V]; g, beta [HV].  Returns o [HV, V]."""
+    S.mul_(torch.exp(g)[:, None, None])
+    sk = torch.einsum("hvk,hk->hv", S, k)
+    vp = beta[:, None] * (v - sk)
+    S.add_(vp[:, :, None] * k[:, None, :])
+    return torch.einsum("hvk,hk->hv", S, q)
+
+
+def gdn_conv(x: torch.Tensor, w: torch.Tensor, state: torch.Tensor):
+    """Causal depthwise conv + SiLU over a token run. x [T, C], w [C, KW], state [C, KW-1]
+    (the previous KW-1 inputs). Returns (y [T, C], new_state)."""
+    kw = w.shape[1]
+    xs = torch.cat([state.t().float(), x.float()], 0)  # [KW-1+T, C]
+    T = x.shape[0]
+    y = torch.zeros(T, x.shape[1], dtype=torch.float32)
+    for j in range(kw):
+        y += xs[j:j + T] * w[:, j].float()
+    return torch.nn.functional.silu(y), xs[-(kw - 1):].t().contiguous()
+
+
+def gated_rms_norm(o: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """rms_norm(o) over the last dim * w * silu(z)."""
+    of = o.float()
+    inv = torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + eps)
+    return of * inv * w.float() * torch.nn.functional.silu(z.float())
