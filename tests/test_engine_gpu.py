@@ -26,3 +26,36 @@ def test_spec_modes_match_greedy():
             got, eng = run(method, graphs, prompts)
             agree = np.mean([a == b for a, b in zip(got, base)])
             assert agree == 1.0, (method, graphs, got, base)
+
+
+def test_qwen3_next_oracle_drafts_on_gpu():
+    from vllm_suffix_hybrid_b200.engine.config import qwen3_next_config
+
+    m = shrink(qwen3_next_config(), layers=4, hidden=256, vocab=1024)
+    rng = np.random.default_rng(2)
+    prompts = [rng.integers(0, 1024, int(n)) for n in (40, 23, 64)]
+    base_cfg = EngineConfig(model=m, spec=SpecConfig(method="none"), cache=CacheConfig(max_model_len=512),
+                            max_num_seqs=4, device="cuda", cuda_graphs=False)
+    base = LLMEngine(base_cfg).generate(prompts, max_new_tokens=16)
+    truth = {f"req-{i}": b for i, b in enumerate(base)}
+    cfg = EngineConfig(model=m, spec=SpecConfig(method="external", k=4), cache=CacheConfig(max_model_len=512),
+                       max_num_seqs=4, device="cuda", cuda_graphs=True)
+    eng = LLMEngine(cfg)
+    r = np.random.default_rng(5)
+
+    def oracle(reqs):
+        out = []
+        for q in reqs:
+            cont = list(truth[q.rid][len(q.output):len(q.output) + 4]) + [0] * 4
+            cont = cont[:4]
+            bad = int(r.integers(0, 6))
+            if bad < 4:
+                cont[bad] = (cont[bad] + 1) % 1024
+            out.append(cont)
+        return out
+
+    eng.external_proposer = oracle
+    got = eng.generate(prompts, max_new_tokens=16)
+    agree = np.mean([a == b for a, b in zip(got, base)])
+    assert agree == 1.0, (got, base)
+    assert eng.spec_stats()["mean_accept_len"] > 1.5
