@@ -143,17 +143,19 @@ __global__ void route_sigmoid_grouped_kernel(RouteParams p) {
       gscore[gi] = b1 + (per > 1 ? b2 : 0.f);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {  // keep the top `topk_groups` groups, mask the rest
+    __shared__ int kept[64];
+    if (threadIdx.x == 0) {  // keep the top `topk_groups` groups (ties -> lower index), mask the rest
+      for (int gi = 0; gi < p.n_groups; ++gi) kept[gi] = 0;
       for (int j = 0; j < p.topk_groups; ++j) {
         int best = -1;
         for (int gi = 0; gi < p.n_groups; ++gi)
-          if (gscore[gi] > -INFINITY && (best < 0 || gscore[gi] > gscore[best])) best = gi;
-        if (best >= 0) gscore[best] = INFINITY;  // mark kept
+          if (!kept[gi] && (best < 0 || gscore[gi] > gscore[best])) best = gi;
+        if (best >= 0) kept[best] = 1;
       }
     }
     __syncthreads();
     for (int e = threadIdx.x; e < p.E; e += blockDim.x)
-      if (gscore[e / per] != INFINITY) sb[e] = -INFINITY;
+      if (!kept[e / per]) sb[e] = -INFINITY;
     __syncthreads();
   }
   for (int j = 0; j < p.k; ++j) {

@@ -28,7 +28,8 @@ def test_spec_modes_match_greedy():
             assert agree == 1.0, (method, graphs, got, base)
 
 
-def test_qwen3_next_oracle_drafts_on_gpu():
+@pytest.mark.parametrize("graphs", [False, True])
+def test_qwen3_next_oracle_drafts_on_gpu(graphs):
     from vllm_suffix_hybrid_b200.engine.config import qwen3_next_config
 
     m = shrink(qwen3_next_config(), layers=4, hidden=256, vocab=1024)
@@ -39,7 +40,7 @@ def test_qwen3_next_oracle_drafts_on_gpu():
     base = LLMEngine(base_cfg).generate(prompts, max_new_tokens=16)
     truth = {f"req-{i}": b for i, b in enumerate(base)}
     cfg = EngineConfig(model=m, spec=SpecConfig(method="external", k=4), cache=CacheConfig(max_model_len=512),
-                       max_num_seqs=4, device="cuda", cuda_graphs=True)
+                       max_num_seqs=4, device="cuda", cuda_graphs=graphs)
     eng = LLMEngine(cfg)
     r = np.random.default_rng(5)
 

@@ -188,7 +188,13 @@ class Runner:
         return self.h_out[:nb_real].numpy(), self.h_acc[:nb_real].numpy(), self.h_nat[:nb_real].numpy()
 
     def _capture(self, nb: int):
-        # Warm up outside capture (allocator pools, lazy module state), then capture.
+        # Warm-up and capture run on scratch rows only (block 0, state slot 0):
+        # a warm-up iteration really executes, and state that is committed
+        # rather than rewritten (deferred recurrent commit) must not see it.
+        self.win[:nb].zero_()
+        self.seq[:nb].zero_()
+        self.bt[:nb].zero_()
+        self.slots[:nb].zero_()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -199,6 +205,12 @@ class Runner:
         with torch.cuda.graph(g):
             self._decode_body(nb)
         self.graphs[nb] = g
+        # Restore this step's real inputs (still in the pinned staging buffers).
+        nbt = self.max_blocks
+        self.win[:nb].copy_(self.h_win[:nb], non_blocking=True)
+        self.seq[:nb].copy_(self.h_seq[:nb], non_blocking=True)
+        self.bt[:nb, :nbt].copy_(self.h_bt[:nb, :nbt], non_blocking=True)
+        self.slots[:nb].copy_(self.h_slots[:nb], non_blocking=True)
         return g
 
     # ------------------------------------------------------------------ prefill
