@@ -108,82 +108,101 @@ __device__ __forceinline__ uint32_t swz(int r, int cc) {
 
 template <int D>
 struct Stages {
-  static constexpr int value = D == 64 ? 8 : (D == 128 ? 4 : 2);  // K/V page ring depth
+  static constexpr int value = D == 64 ? 8 : (D == 128 ? 4 : 2);  // K/V page ring depth (fits with the merge area)
 };
 
+// Geometry of one work unit, computed identically by the producer and the
+// compute warps.
+struct Unit {
+  int b, row0, h, split;
+  int64_t qs, seq_len, ctx0;
+  int q_len, rows_valid, pg0, pg1;
+};
+
+__device__ __forceinline__ Unit unit_of(const AttnParams& p, int u, int ntiles) {
+  Unit w;
+  const int per_tile = p.hk * p.nsplit;
+  const int tile = u / per_tile;
+  const int rem = u % per_tile;
+  w.h = rem / p.nsplit;
+  w.split = rem % p.nsplit;
+  w.b = p.tile_req[tile];
+  w.row0 = p.tile_row0[tile];
+  const int G = p.hq / p.hk;
+  w.qs = p.q_start[w.b];
+  w.q_len = static_cast<int>(p.q_start[w.b + 1] - w.qs);
+  w.seq_len = p.seq_lens[w.b];
+  w.ctx0 = w.seq_len - w.q_len;
+  w.rows_valid = min(ROWS, w.q_len * G - w.row0);
+  const int64_t kv_end = min(w.seq_len, w.ctx0 + (w.row0 + w.rows_valid - 1) / G + 1);
+  const int npages = static_cast<int>((kv_end + KEYS - 1) / KEYS);
+  const int per = (npages + p.nsplit - 1) / p.nsplit;
+  w.pg0 = min(w.split * per, npages);
+  w.pg1 = min(w.pg0 + per, npages);
+  return w;
+}
+
+// Persistent: gridDim.x CTAs loop over units u = blockIdx.x + i * gridDim.x;
+// the producer's page ring runs continuously across unit boundaries.
 template <int D, int KS>
 __global__ void __launch_bounds__(THREADS, 1)
-    paged_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+    paged_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnParams p,
+                      int ntiles) {
   constexpr int TILE_BYTES = 64 * D * 2;  // one [64][D] bf16 tile
   constexpr int STAGES = Stages<D>::value;
   constexpr int KSTEPS = D / 16;
   constexpr int DT = D / 8;
+  constexpr int NT = 8 / KS;  // 8-key n-tiles per page per warp
+  constexpr int KC = 4 / KS;  // 16-key PV chunks per page per warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + TILE_BYTES;  // stage s: K at s*2*TILE, V at s*2*TILE + TILE
-  uint64_t* full = reinterpret_cast<uint64_t*>(sKV + STAGES * 2 * TILE_BYTES);
+  float* sMerge = reinterpret_cast<float*>(sKV + STAGES * 2 * TILE_BYTES);  // [4 warps][32][DT*4+4]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sMerge + (KS > 1 ? 4 * 32 * (DT * 4 + 4) : 0));
   uint64_t* empty = full + STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
 
-  const int tile = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
-  const int b = p.tile_req[tile];
-  const int row0 = p.tile_row0[tile];
-  const int G = p.hq / p.hk;
-  const int64_t qs = p.q_start[b];
-  const int q_len = static_cast<int>(p.q_start[b + 1] - qs);
-  const int64_t seq_len = p.seq_lens[b];
-  const int64_t ctx0 = seq_len - q_len;
-  const int rows_valid = min(ROWS, q_len * G - row0);
-  const int64_t kv_end = min(seq_len, ctx0 + (row0 + rows_valid - 1) / G + 1);
-  const int npages = static_cast<int>((kv_end + KEYS - 1) / KEYS);
-  const int per = (npages + p.nsplit - 1) / p.nsplit;
-  const int pg0 = min(split * per, npages), pg1 = min(pg0 + per, npages);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
+  const int G = p.hq / p.hk;
+  const int units = ntiles * p.hk * p.nsplit;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 4);
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 4);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // Query rows -> smem (zero-filled past the valid rows), all threads.
-  for (int c = threadIdx.x; c < ROWS * (D / 8); c += THREADS) {
-    const int r = c / (D / 8), cc = c % (D / 8);
-    const bool ok = r < rows_valid;
-    const int rr = ok ? row0 + r : row0;
-    const int tok = rr / G, head = h * G + rr % G;
-    cp_async16(sQ + swz(r, cc), p.q + (qs + tok) * p.q_stride + static_cast<int64_t>(head) * D + cc * 8, ok);
-  }
-  asm volatile("cp.async.commit_group;\n" ::);
-  asm volatile("cp.async.wait_group 0;\n" ::);
   __syncthreads();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
       int issued = 0;
-      for (int j = pg0; j < pg1; ++j, ++issued) {
-        const int s = issued % STAGES;
-        const uint32_t ph = (issued / STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
-          if (p.err) atomicCAS(p.err, 0, 11);
-          *abort_flag = 1;
-          break;
-        }
-        const int y = (bt[j] * p.hk + h) * KEYS;
-        uint8_t* dk = sKV + s * 2 * TILE_BYTES;
-        mbar_expect_tx(&full[s], 2 * TILE_BYTES);
+      bool aborted = false;
+      for (int u = blockIdx.x; u < units && !aborted; u += gridDim.x) {
+        const Unit w = unit_of(p, u, ntiles);
+        const int32_t* bt = p.block_tables + static_cast<int64_t>(w.b) * p.bt_stride;
+        for (int j = w.pg0; j < w.pg1; ++j, ++issued) {
+          const int st = issued % STAGES;
+          if (!mbar_wait(&empty[st], ((issued / STAGES) & 1) ^ 1, abort_flag)) {
+            if (p.err) atomicCAS(p.err, 0, 11);
+            *abort_flag = 1;
+            aborted = true;
+            break;
+          }
+          const int y = (bt[j] * p.hk + w.h) * KEYS;
+          uint8_t* dk = sKV + st * 2 * TILE_BYTES;
+          mbar_expect_tx(&full[st], 2 * TILE_BYTES);
 #pragma unroll
-        for (int slab = 0; slab < D / 64; ++slab) {
-          tma_2d(dk + slab * 64 * 128, &tmK, slab * 64, y, &full[s]);
-          tma_2d(dk + TILE_BYTES + slab * 64 * 128, &tmV, slab * 64, y, &full[s]);
+          for (int slab = 0; slab < D / 64; ++slab) {
+            tma_2d(dk + slab * 64 * 128, &tmK, slab * 64, y, &full[st]);
+            tma_2d(dk + TILE_BYTES + slab * 64 * 128, &tmV, slab * 64, y, &full[st]);
+          }
         }
       }
-      if (*abort_flag) {  // let every issued load land before exit (bounded)
+      if (aborted) {  // let every issued load land before exit (bounded)
         for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i) {
           const uint64_t t0 = now_ns();
           while (!mbar_try(&full[i % STAGES], (i / STAGES) & 1))
@@ -194,188 +213,203 @@ __global__ void __launch_bounds__(THREADS, 1)
     return;
   }
   // -------------------------------------------------------------- compute
-  // 4 compute warps: warp cw owns row block cw / KS (16 rows) and key part
-  // cw % KS (64 / KS keys of every page); the KS partial softmax states of a
-  // row block are merged through shared memory at the end.
-  constexpr int NT = 8 / KS;  // 8-key n-tiles per page per warp
-  constexpr int KC = 4 / KS;  // 16-key PV chunks per page per warp
+  // Warp cw owns row block cw / KS (16 rows) and key part cw % KS (64 / KS
+  // keys of every page); the KS partial softmax states of a row block are
+  // merged through shared memory at the end of each unit.
   const int cw = warp - 1;
   const int rbk = cw / KS, kpart = cw % KS;
   const int g = lane >> 2, t4 = lane & 3;
-  const bool active = rbk * 16 < rows_valid;
-  uint32_t qf[KSTEPS][4];
-  if (active) {
-#pragma unroll
-    for (int kk = 0; kk < KSTEPS; ++kk)
-      ldsm_x4(saddr(sQ) + swz(rbk * 16 + (lane & 15), 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2],
-              qf[kk][3]);
-  }
-  const int ra = rbk * 16 + g, rb = ra + 8;
-  const int64_t pa = ra < rows_valid ? ctx0 + (row0 + ra) / G : -1;
-  const int64_t pb = rb < rows_valid ? ctx0 + (row0 + rb) / G : -1;
   const int key0 = kpart * (KEYS / KS);
-  float o[DT][4];
-#pragma unroll
-  for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-  int it = 0;
-  for (int j = pg0; j < pg1; ++j, ++it) {
-    const int s = it % STAGES;
-    if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
-      if (p.err && lane == 0) atomicCAS(p.err, 0, 12);
-      *abort_flag = 1;
-      break;
+  int it = 0;  // pages consumed by this CTA so far (ring position)
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const Unit w = unit_of(p, u, ntiles);
+    // Query rows of this unit -> smem (compute warps only; sQ is free once
+    // every compute warp has copied its fragments of the previous unit).
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    for (int c = threadIdx.x - 32; c < ROWS * (D / 8); c += 128) {
+      const int r = c / (D / 8), cc = c % (D / 8);
+      const bool ok = r < w.rows_valid;
+      const int rr = ok ? w.row0 + r : w.row0;
+      const int tok = rr / G, head = w.h * G + rr % G;
+      cp_async16(sQ + swz(r, cc), p.q + (w.qs + tok) * p.q_stride + static_cast<int64_t>(head) * D + cc * 8, ok);
     }
-    const uint32_t kb = saddr(sKV + s * 2 * TILE_BYTES);
-    const uint32_t vb = kb + TILE_BYTES;
+    asm volatile("cp.async.commit_group;\n" ::);
+    asm volatile("cp.async.wait_group 0;\n" ::);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const bool active = rbk * 16 < w.rows_valid;
+    uint32_t qf[KSTEPS][4];
     if (active) {
-      float sc[NT][4];
 #pragma unroll
-      for (int i = 0; i < NT; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+      for (int kk = 0; kk < KSTEPS; ++kk)
+        ldsm_x4(saddr(sQ) + swz(rbk * 16 + (lane & 15), 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2],
+                qf[kk][3]);
+    }
+    const int ra = rbk * 16 + g, rb = ra + 8;
+    const int64_t pa = ra < w.rows_valid ? w.ctx0 + (w.row0 + ra) / G : -1;
+    const int64_t pb = rb < w.rows_valid ? w.ctx0 + (w.row0 + rb) / G : -1;
+    float o[DT][4];
 #pragma unroll
-      for (int kk = 0; kk < KSTEPS; ++kk) {
-#pragma unroll
-        for (int np = 0; np < NT / 2; ++np) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(kb + swz(key0 + np * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0, b1, b2,
-                  b3);
-          mma16816(sc[2 * np], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
-          mma16816(sc[2 * np + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
-        }
+    for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+    bool bad = false;
+    for (int j = w.pg0; j < w.pg1 && !*abort_flag; ++j, ++it) {
+      const int st = it % STAGES;
+      if (!mbar_wait(&full[st], (it / STAGES) & 1, abort_flag)) {
+        if (p.err && lane == 0) atomicCAS(p.err, 0, 12);
+        *abort_flag = 1;
+        bad = true;
+        break;
       }
-      const int64_t kbase = static_cast<int64_t>(j) * KEYS + key0;
-      const bool edge = kbase + KEYS / KS - 1 > min(pa, pb) || pa < 0 || pb < 0;
-      float mx_a = m_a, mx_b = m_b;
+      const uint32_t kb = saddr(sKV + st * 2 * TILE_BYTES);
+      const uint32_t vb = kb + TILE_BYTES;
+      if (active) {
+        float sc[NT][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
+        for (int i = 0; i < NT; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int64_t kp = kbase + nt * 8 + 2 * t4 + e;
-          float va = sc[nt][e] * p.scale_log2, vb2 = sc[nt][2 + e] * p.scale_log2;
-          if (edge) {
-            if (kp > pa) va = -INFINITY;
-            if (kp > pb) vb2 = -INFINITY;
-          }
-          sc[nt][e] = va;
-          sc[nt][2 + e] = vb2;
-          mx_a = fmaxf(mx_a, va);
-          mx_b = fmaxf(mx_b, vb2);
-        }
-      }
-      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
-      const float base_a = mx_a == -INFINITY ? 0.f : mx_a;
-      const float base_b = mx_b == -INFINITY ? 0.f : mx_b;
-      const float al_a = exp2f(m_a - base_a), al_b = exp2f(m_b - base_b);
-      m_a = mx_a;
-      m_b = mx_b;
-      float sum_a = 0.f, sum_b = 0.f;
-      uint32_t pf[KC][4];
+        for (int kk = 0; kk < KSTEPS; ++kk) {
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const float p0 = exp2f(sc[nt][0] - base_a), p1 = exp2f(sc[nt][1] - base_a);
-        const float p2 = exp2f(sc[nt][2] - base_b), p3 = exp2f(sc[nt][3] - base_b);
-        sum_a += p0 + p1;
-        sum_b += p2 + p3;
-        pf[nt >> 1][(nt & 1) * 2 + 0] = pack2(p0, p1);
-        pf[nt >> 1][(nt & 1) * 2 + 1] = pack2(p2, p3);
-      }
-      l_a = l_a * al_a + sum_a;
-      l_b = l_b * al_b + sum_b;
-#pragma unroll
-      for (int dt = 0; dt < DT; ++dt) {
-        o[dt][0] *= al_a;
-        o[dt][1] *= al_a;
-        o[dt][2] *= al_b;
-        o[dt][3] *= al_b;
-      }
-#pragma unroll
-      for (int kc = 0; kc < KC; ++kc) {
-#pragma unroll
-        for (int dp = 0; dp < DT / 2; ++dp) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(vb + swz(key0 + kc * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), 2 * dp + (lane >> 4)), b0, b1,
+          for (int np = 0; np < NT / 2; ++np) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(kb + swz(key0 + np * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0, b1,
                     b2, b3);
-          mma16816(o[2 * dp], pf[kc][0], pf[kc][1], pf[kc][2], pf[kc][3], b0, b1);
-          mma16816(o[2 * dp + 1], pf[kc][0], pf[kc][1], pf[kc][2], pf[kc][3], b2, b3);
+            mma16816(sc[2 * np], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
+            mma16816(sc[2 * np + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
+          }
+        }
+        const int64_t kbase = static_cast<int64_t>(j) * KEYS + key0;
+        const bool edge = kbase + KEYS / KS - 1 > min(pa, pb) || pa < 0 || pb < 0;
+        float mx_a = m_a, mx_b = m_b;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int64_t kp = kbase + nt * 8 + 2 * t4 + e;
+            float va = sc[nt][e] * p.scale_log2, vb2 = sc[nt][2 + e] * p.scale_log2;
+            if (edge) {
+              if (kp > pa) va = -INFINITY;
+              if (kp > pb) vb2 = -INFINITY;
+            }
+            sc[nt][e] = va;
+            sc[nt][2 + e] = vb2;
+            mx_a = fmaxf(mx_a, va);
+            mx_b = fmaxf(mx_b, vb2);
+          }
+        }
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        const float base_a = mx_a == -INFINITY ? 0.f : mx_a;
+        const float base_b = mx_b == -INFINITY ? 0.f : mx_b;
+        const float al_a = exp2f(m_a - base_a), al_b = exp2f(m_b - base_b);
+        m_a = mx_a;
+        m_b = mx_b;
+        float sum_a = 0.f, sum_b = 0.f;
+        uint32_t pf[KC][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float p0 = exp2f(sc[nt][0] - base_a), p1 = exp2f(sc[nt][1] - base_a);
+          const float p2 = exp2f(sc[nt][2] - base_b), p3 = exp2f(sc[nt][3] - base_b);
+          sum_a += p0 + p1;
+          sum_b += p2 + p3;
+          pf[nt >> 1][(nt & 1) * 2 + 0] = pack2(p0, p1);
+          pf[nt >> 1][(nt & 1) * 2 + 1] = pack2(p2, p3);
+        }
+        l_a = l_a * al_a + sum_a;
+        l_b = l_b * al_b + sum_b;
+#pragma unroll
+        for (int dt = 0; dt < DT; ++dt) {
+          o[dt][0] *= al_a;
+          o[dt][1] *= al_a;
+          o[dt][2] *= al_b;
+          o[dt][3] *= al_b;
+        }
+#pragma unroll
+        for (int kc = 0; kc < KC; ++kc) {
+#pragma unroll
+          for (int dp = 0; dp < DT / 2; ++dp) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(vb + swz(key0 + kc * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), 2 * dp + (lane >> 4)), b0,
+                      b1, b2, b3);
+            mma16816(o[2 * dp], pf[kc][0], pf[kc][1], pf[kc][2], pf[kc][3], b0, b1);
+            mma16816(o[2 * dp + 1], pf[kc][0], pf[kc][1], pf[kc][2], pf[kc][3], b2, b3);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    (void)bad;  // an aborted unit still takes part in every named barrier below; its stores are skipped
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+    if (KS > 1) {
+      float* xs = sMerge + (cw * 32 + lane) * (DT * 4 + 4);
+      if (kpart != 0 && active) {
+#pragma unroll
+        for (int dt = 0; dt < DT; ++dt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xs[dt * 4 + e] = o[dt][e];
+        xs[DT * 4 + 0] = m_a;
+        xs[DT * 4 + 1] = m_b;
+        xs[DT * 4 + 2] = l_a;
+        xs[DT * 4 + 3] = l_b;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (kpart == 0 && active) {
+#pragma unroll
+        for (int q = 1; q < KS; ++q) {
+          const float* ys = sMerge + ((cw + q) * 32 + lane) * (DT * 4 + 4);
+          const float mq_a = ys[DT * 4 + 0], mq_b = ys[DT * 4 + 1];
+          const float na = fmaxf(m_a, mq_a), nb = fmaxf(m_b, mq_b);
+          const float ba = na == -INFINITY ? 0.f : na, bb = nb == -INFINITY ? 0.f : nb;
+          const float sa = exp2f(m_a - ba), sb = exp2f(m_b - bb);
+          const float qa = exp2f(mq_a - ba), qb = exp2f(mq_b - bb);
+#pragma unroll
+          for (int dt = 0; dt < DT; ++dt) {
+            o[dt][0] = o[dt][0] * sa + ys[dt * 4 + 0] * qa;
+            o[dt][1] = o[dt][1] * sa + ys[dt * 4 + 1] * qa;
+            o[dt][2] = o[dt][2] * sb + ys[dt * 4 + 2] * qb;
+            o[dt][3] = o[dt][3] * sb + ys[dt * 4 + 3] * qb;
+          }
+          l_a = l_a * sa + ys[DT * 4 + 2] * qa;
+          l_b = l_b * sb + ys[DT * 4 + 3] * qb;
+          m_a = na;
+          m_b = nb;
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-  if (KS > 1) {
-    // Merge the KS key-part states of each row block (the ring is drained:
-    // every page was consumed by all compute warps before this barrier).
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    float* xs = reinterpret_cast<float*>(sKV) + (cw * 32 + lane) * (DT * 4 + 4);
-    if (kpart != 0 && active) {
+    if (kpart != 0 || !active || *abort_flag) continue;
+    const float inv_a = l_a > 0.f ? 1.f / l_a : 0.f;
+    const float inv_b = l_b > 0.f ? 1.f / l_b : 0.f;
 #pragma unroll
-      for (int dt = 0; dt < DT; ++dt)
+    for (int half = 0; half < 2; ++half) {
+      const int r = half ? rb : ra;
+      if (r >= w.rows_valid) continue;
+      const int rr = w.row0 + r;
+      const int64_t tok = w.qs + rr / G;
+      const int head = w.h * G + rr % G;
+      const float inv = half ? inv_b : inv_a;
+      if (p.nsplit == 1) {
+        __nv_bfloat16* dst = p.out + tok * p.out_stride + static_cast<int64_t>(head) * D;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) xs[dt * 4 + e] = o[dt][e];
-      xs[DT * 4 + 0] = m_a;
-      xs[DT * 4 + 1] = m_b;
-      xs[DT * 4 + 2] = l_a;
-      xs[DT * 4 + 3] = l_b;
-    }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (kpart != 0 || !active) return;
+        for (int dt = 0; dt < DT; ++dt)
+          *reinterpret_cast<__nv_bfloat162*>(dst + dt * 8 + 2 * t4) =
+              __floats2bfloat162_rn(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
+      } else {
+        // Partial: normalised O and (max, sum) in log2 units, per (row, split).
+        const int64_t prow = (tok * p.hq + head) * p.nsplit + w.split;
+        float* dst = p.part_o + prow * D;
 #pragma unroll
-    for (int q = 1; q < KS; ++q) {
-      const float* ys = reinterpret_cast<const float*>(sKV) + ((cw + q) * 32 + lane) * (DT * 4 + 4);
-      const float mq_a = ys[DT * 4 + 0], mq_b = ys[DT * 4 + 1];
-      const float na = fmaxf(m_a, mq_a), nb = fmaxf(m_b, mq_b);
-      const float ba = na == -INFINITY ? 0.f : na, bb = nb == -INFINITY ? 0.f : nb;
-      const float sa = exp2f(m_a - ba), sb = exp2f(m_b - bb);
-      const float qa = exp2f(mq_a - ba), qb = exp2f(mq_b - bb);
-#pragma unroll
-      for (int dt = 0; dt < DT; ++dt) {
-        o[dt][0] = o[dt][0] * sa + ys[dt * 4 + 0] * qa;
-        o[dt][1] = o[dt][1] * sa + ys[dt * 4 + 1] * qa;
-        o[dt][2] = o[dt][2] * sb + ys[dt * 4 + 2] * qb;
-        o[dt][3] = o[dt][3] * sb + ys[dt * 4 + 3] * qb;
-      }
-      l_a = l_a * sa + ys[DT * 4 + 2] * qa;
-      l_b = l_b * sb + ys[DT * 4 + 3] * qb;
-      m_a = na;
-      m_b = nb;
-    }
-  }
-  if (!active) return;
-  const float inv_a = l_a > 0.f ? 1.f / l_a : 0.f;
-  const float inv_b = l_b > 0.f ? 1.f / l_b : 0.f;
-#pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const int r = half ? rb : ra;
-    if (r >= rows_valid) continue;
-    const int rr = row0 + r;
-    const int64_t tok = qs + rr / G;
-    const int head = h * G + rr % G;
-    const float inv = half ? inv_b : inv_a;
-    if (p.nsplit == 1) {
-      __nv_bfloat16* dst = p.out + tok * p.out_stride + static_cast<int64_t>(head) * D;
-#pragma unroll
-      for (int dt = 0; dt < DT; ++dt)
-        *reinterpret_cast<__nv_bfloat162*>(dst + dt * 8 + 2 * t4) =
-            __floats2bfloat162_rn(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
-    } else {
-      // Partial: normalised O and (max, sum) in log2 units, per (row, split).
-      const int64_t prow = (tok * p.hq + head) * p.nsplit + split;
-      float* dst = p.part_o + prow * D;
-#pragma unroll
-      for (int dt = 0; dt < DT; ++dt)
-        *reinterpret_cast<float2*>(dst + dt * 8 + 2 * t4) =
-            make_float2(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
-      if (t4 == 0) {
-        p.part_ml[prow * 2] = half ? m_b : m_a;
-        p.part_ml[prow * 2 + 1] = half ? l_b : l_a;
+        for (int dt = 0; dt < DT; ++dt)
+          *reinterpret_cast<float2*>(dst + dt * 8 + 2 * t4) =
+              make_float2(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
+        if (t4 == 0) {
+          p.part_ml[prow * 2] = half ? m_b : m_a;
+          p.part_ml[prow * 2 + 1] = half ? l_b : l_a;
+        }
       }
     }
   }
@@ -449,12 +483,20 @@ int cache_map(CUtensorMap* m, const void* base, int64_t rows, int d) {
 template <int D, int KS>
 int launch_ks(const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& p, int ntiles, cudaStream_t st) {
   constexpr int STAGES = Stages<D>::value;
-  const int smem = 1024 + 64 * D * 2 * (1 + 2 * STAGES) + 2 * STAGES * 8 + 16;
+  constexpr int MERGE = KS > 1 ? 4 * 32 * (D / 8 * 4 + 4) * 4 : 0;
+  const int smem = 1024 + 64 * D * 2 * (1 + 2 * STAGES) + MERGE + 2 * STAGES * 8 + 16;
   auto k = paged_attn_kernel<D, KS>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return 300 + static_cast<int>(e);
-  dim3 grid(ntiles, p.hk, p.nsplit);
-  k<<<grid, THREADS, smem, st>>>(mk, mv, p);
+  static int num_sms = 0;
+  if (!num_sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int units = ntiles * p.hk * p.nsplit;
+  const int grid = units < num_sms ? units : num_sms;
+  k<<<grid, THREADS, smem, st>>>(mk, mv, p, ntiles);
   e = cudaGetLastError();
   return e == cudaSuccess ? 0 : 400 + static_cast<int>(e);
 }
