@@ -484,7 +484,9 @@ template <int D, int KS>
 int launch_ks(const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& p, int ntiles, cudaStream_t st) {
   constexpr int STAGES = Stages<D>::value;
   constexpr int MERGE = KS > 1 ? 4 * 32 * (D / 8 * 4 + 4) * 4 : 0;
-  const int smem = 1024 + 64 * D * 2 * (1 + 2 * STAGES) + MERGE + 2 * STAGES * 8 + 16;
+  constexpr int SMEM = 1024 + 64 * D * 2 * (1 + 2 * STAGES) + MERGE + 2 * STAGES * 8 + 16;
+  static_assert(SMEM <= 227 * 1024, "paged attention shared-memory budget exceeds 227 KB per block");
+  const int smem = SMEM;
   auto k = paged_attn_kernel<D, KS>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return 300 + static_cast<int>(e);
@@ -508,8 +510,13 @@ int launch(const AttnParams& p, int ntiles, int cache_rows, int max_rows, cudaSt
   if (r) return 100 + r;
   r = cache_map(&mv, p.v_cache, cache_rows, D);
   if (r) return 200 + r;
-  r = max_rows <= 16 ? launch_ks<D, 4>(mk, mv, p, ntiles, st)
-                     : (max_rows <= 32 ? launch_ks<D, 2>(mk, mv, p, ntiles, st) : launch_ks<D, 1>(mk, mv, p, ntiles, st));
+  if constexpr (D == 256) {
+    // The key-split merge area does not fit next to a 256-wide page ring.
+    r = launch_ks<D, 1>(mk, mv, p, ntiles, st);
+  } else {
+    r = max_rows <= 16 ? launch_ks<D, 4>(mk, mv, p, ntiles, st)
+                       : (max_rows <= 32 ? launch_ks<D, 2>(mk, mv, p, ntiles, st) : launch_ks<D, 1>(mk, mv, p, ntiles, st));
+  }
   if (r) return r;
   cudaError_t e;
   if (p.nsplit > 1) {
