@@ -271,6 +271,29 @@ void gemm_grouped(torch::Tensor out, torch::Tensor q, torch::Tensor w_stacked, i
               "sh_gemm_bf16_grouped");
 }
 
+// --- NVFP4 ---------------------------------------------------------------------
+extern "C" int sh_nvfp4_dequant(__nv_bfloat16* out, const uint8_t* packed, const uint8_t* scales, const float* global,
+                                int64_t N, int K, cudaStream_t stream);
+extern "C" int sh_nvfp4_quant(uint8_t* packed, uint8_t* scales, const __nv_bfloat16* w, const float* global, int64_t N,
+                              int K, cudaStream_t stream);
+
+void nvfp4_dequant(torch::Tensor out, torch::Tensor packed, torch::Tensor scales, torch::Tensor global) {
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && packed.is_contiguous() &&
+                  scales.is_contiguous(), "nvfp4_dequant: contiguous bf16 out / uint8 packed / e4m3 scales");
+  SH_CHECK_RC(sh_nvfp4_dequant(ptr<__nv_bfloat16>(out), ptr<const uint8_t>(packed), ptr<const uint8_t>(scales),
+                               ptr<const float>(global), out.size(0), static_cast<int>(out.size(1)),
+                               at::cuda::getCurrentCUDAStream()),
+              "sh_nvfp4_dequant");
+}
+
+void nvfp4_quant(torch::Tensor packed, torch::Tensor scales, torch::Tensor w, torch::Tensor global) {
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous(), "nvfp4_quant: contiguous bf16 weight");
+  SH_CHECK_RC(sh_nvfp4_quant(ptr<uint8_t>(packed), ptr<uint8_t>(scales), ptr<const __nv_bfloat16>(w),
+                             ptr<const float>(global), w.size(0), static_cast<int>(w.size(1)),
+                             at::cuda::getCurrentCUDAStream()),
+              "sh_nvfp4_quant");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200 (sm_100a) kernels: fused norms, RoPE+cache write, paged attention, GEMMs, verify, comm";
   m.def("rms_norm", &rms_norm);
@@ -292,6 +315,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
   m.def("gemm_grouped", &gemm_grouped);
+  m.def("nvfp4_dequant", &nvfp4_dequant);
+  m.def("nvfp4_quant", &nvfp4_quant);
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM", py::arg("y"), py::arg("x"), py::arg("w"), py::arg("swap"),
         py::arg("bn"), py::arg("splits"), py::arg("ws") = py::none(), py::arg("err") = py::none());
 }

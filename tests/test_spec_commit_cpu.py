@@ -8,21 +8,26 @@ Gated DeltaNet state) are exercised with real acceptances.
 import numpy as np
 import pytest
 
-from vllm_suffix_hybrid_b200.engine.config import (CacheConfig, EngineConfig, SpecConfig, llama3_8b_config,
-                                                   qwen3_next_config, shrink)
+from vllm_suffix_hybrid_b200.engine.config import (CacheConfig, EngineConfig, SpecConfig, deepseek_v32_config,
+                                                   kimi_k2_config, llama3_8b_config, qwen3_next_config, shrink)
 from vllm_suffix_hybrid_b200.engine.llm import LLMEngine
 
 
 def _model(name):
     if name == "llama":
         m = shrink(llama3_8b_config(), layers=2, hidden=128, vocab=512)
-    else:
+    elif name == "qwen3_next":
         m = shrink(qwen3_next_config(), layers=4, hidden=128, vocab=512)
+    elif name == "deepseek_v32":
+        m = shrink(deepseek_v32_config(), layers=3, hidden=128, vocab=512)
+    else:
+        m = shrink(kimi_k2_config(), layers=3, hidden=128, vocab=512)
     m.dtype = "float32"
+    m.weight_format = "bf16"
     return m
 
 
-@pytest.mark.parametrize("name", ["llama", "qwen3_next"])
+@pytest.mark.parametrize("name", ["llama", "qwen3_next", "deepseek_v32", "kimi_k2"])
 def test_oracle_drafts_match_plain_decode(name):
     rng = np.random.default_rng(3)
     prompts = [rng.integers(0, 512, int(rng.integers(8, 30))) for _ in range(3)]

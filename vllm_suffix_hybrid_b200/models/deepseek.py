@@ -1,0 +1,214 @@
+"""DeepSeek-V3.2-style sparse-MLA MoE (config 3) and Kimi-K2 (config 4).
+
+* MLA in its absorbed form: the cache holds the normalised latent c_kv
+  (kv_lora) and the rotary key k_pe (rope) per token; queries are projected
+  into the latent space with W_UK, attention runs over the latent rows, and
+  W_UV maps the latent output back to per-head values.
+* DSA lightning indexer (V3.2): per-token index keys are cached; every query
+  scores its context with sum_h relu(q_h . k) * w_h and attends only to the
+  top-k positions.
+* MoE: sigmoid group-limited router with score-correction bias, routed
+  scaling, one shared expert; the first `first_dense_layers` layers are dense.
+* Weights may be NVFP4 (ModelOpt layout: packed e2m1, e4m3 block-16 scales,
+  fp32 global scale); dense NVFP4 linears dequantise into a scratch tile and
+  run the tcgen05 GEMM.
+"""
+from __future__ import annotations
+
+import math
+from typing import List, Optional
+
+import torch
+
+from .. import ops
+from ..parallel import comm, state
+from .common import MLP, AttnMeta, Linear, RMSNorm, dtype_of, init_weight
+from .moe import MoEBlock
+
+
+class QLinear:
+    """y = x W^T with W in bf16 or NVFP4.
+
+    NVFP4 weights are dequantised into one scratch tile per device that all
+    NVFP4 linears share (calls are ordered on the stream, so a captured graph
+    replays them correctly) and then run the bf16 tcgen05 GEMM.
+    """
+
+    _scratch: dict = {}
+
+    def __init__(self, in_f: int, out_f: int, dtype, device, gen, fmt: str = "bf16", std: float = 0.02):
+        w = init_weight((out_f, in_f), std, dtype, device, gen)
+        self.fmt = fmt if in_f % 16 == 0 else "bf16"
+        self.out_f, self.in_f, self.dtype = out_f, in_f, dtype
+        if self.fmt == "nvfp4":
+            self.packed, self.scales, self.gscale = ops.nvfp4_quantize(w)
+            self._w = None
+            if self.packed.is_cuda:
+                key = self.packed.device
+                buf = QLinear._scratch.get(key)
+                if buf is None or buf.numel() < out_f * in_f:
+                    QLinear._scratch[key] = torch.empty(out_f * in_f, dtype=torch.bfloat16, device=key)
+        else:
+            self._w = w
+
+    @property
+    def weight(self) -> torch.Tensor:
+        if self.fmt != "nvfp4":
+            return self._w
+        if not self.packed.is_cuda:
+            return ops.nvfp4_dequantize(self.packed, self.scales, self.gscale).to(self.dtype)
+        out = QLinear._scratch[self.packed.device][: self.out_f * self.in_f].view(self.out_f, self.in_f)
+        return ops.nvfp4_dequantize(self.packed, self.scales, self.gscale, out=out)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.linear(x, self.weight)
+
+
+class MLAttention:
+    def __init__(self, cfg, dtype, device, gen, cos_sin, fmt: str):
+        assert state.get().tp == 1, "MLA runs data-parallel (attention DP) with experts sharded by EP"
+        self.cfg = cfg
+        self.H = cfg.heads
+        self.nope, self.rope, self.vd, self.lora = cfg.qk_nope, cfg.qk_rope, cfg.v_head, cfg.kv_lora
+        self.scale = 1.0 / math.sqrt(self.nope + self.rope)
+        h = cfg.hidden
+        self.q_a = QLinear(h, cfg.q_lora, dtype, device, gen, fmt) if cfg.q_lora else None
+        self.q_a_norm = RMSNorm(cfg.q_lora, cfg.norm_eps, dtype, device) if cfg.q_lora else None
+        self.q_b = QLinear(cfg.q_lora or h, self.H * (self.nope + self.rope), dtype, device, gen, fmt)
+        self.kv_a = QLinear(h, self.lora + self.rope, dtype, device, gen, fmt)
+        self.kv_a_norm = RMSNorm(self.lora, cfg.norm_eps, dtype, device)
+        self.kv_b = QLinear(self.lora, self.H * (self.nope + self.vd), dtype, device, gen, fmt)
+        self.o = QLinear(self.H * self.vd, h, dtype, device, gen, fmt)
+        self.cos_sin = cos_sin
+        self.dsa = cfg.dsa_topk > 0
+        if self.dsa:
+            self.ih, self.idim, self.itopk = cfg.dsa_heads, cfg.dsa_head_dim, cfg.dsa_topk
+            self.idx_q = QLinear(cfg.q_lora or h, self.ih * self.idim, dtype, device, gen, fmt)
+            self.idx_k = QLinear(h, self.idim, dtype, device, gen, fmt)
+            self.idx_w = init_weight((self.ih, h), cfg.init_std, dtype, device, gen)
+
+    def cache_width(self) -> int:
+        return self.lora + self.rope
+
+    def __call__(self, x: torch.Tensor, meta: AttnMeta, cache) -> torch.Tensor:
+        latent, icache = cache
+        T = x.shape[0]
+        qa = self.q_a_norm(self.q_a(x)) if self.q_a is not None else x
+        q = self.q_b(qa).view(T, self.H, self.nope + self.rope)
+        ckv = self.kv_a(x)
+        c = ops.rms_norm(ckv[:, : self.lora].contiguous(), self.kv_a_norm.weight, self.kv_a_norm.eps)
+        kpe = ops.ref.apply_rope(ckv[:, self.lora:].reshape(T, 1, self.rope), meta.positions, self.cos_sin)[:, 0]
+        q_pe = ops.ref.apply_rope(q[..., self.nope:], meta.positions, self.cos_sin)
+        bs = latent.shape[1]
+        ok = meta.slot_mapping >= 0
+        slots = meta.slot_mapping[ok]
+        latent[slots // bs, slots % bs] = torch.cat([c, kpe.to(c.dtype)], -1)[ok]
+        wkv = self.kv_b.weight.view(self.H, self.nope + self.vd, self.lora)
+        w_uk, w_uv = wkv[:, : self.nope], wkv[:, self.nope:]
+        q_lat = torch.einsum("thn,hnc->thc", q[..., : self.nope].float(), w_uk.float())
+        topk = None
+        if self.dsa:
+            qi = self.idx_q(qa).view(T, self.ih, self.idim)
+            ki = self.idx_k(x)
+            icache[slots // bs, slots % bs] = ki[ok]
+            wt = ops.linear(x, self.idx_w).float() * (self.ih ** -0.5) * (self.idim ** -0.5)
+            topk = ops.ref.dsa_topk(qi, wt, icache, meta.block_tables, meta.seq_lens, meta.q_start, self.itopk)
+        o_lat = ops.ref.mla_attention(q_lat, q_pe, latent, meta.block_tables, meta.seq_lens, meta.q_start, self.scale,
+                                      self.lora, topk)
+        o = torch.einsum("thc,hvc->thv", o_lat, w_uv.float()).to(x.dtype)
+        return self.o(o.reshape(T, self.H * self.vd))
+
+
+class DeepseekLayer:
+    def __init__(self, cfg, i: int, dtype, device, gen, cos_sin, fmt):
+        self.input_norm = RMSNorm(cfg.hidden, cfg.norm_eps, dtype, device)
+        self.attn = MLAttention(cfg, dtype, device, gen, cos_sin, fmt)
+        self.post_norm = RMSNorm(cfg.hidden, cfg.norm_eps, dtype, device)
+        self.ffn = MoEBlock(cfg, dtype, device, gen) if cfg.layer_is_moe(i) else MLP(cfg.hidden, cfg.ffn, dtype,
+                                                                                   device, gen)
+
+    def __call__(self, x, residual, meta, cache):
+        h = self.attn(x, meta, cache)
+        ops.fused_add_rms_norm(h, residual, self.post_norm.weight, self.post_norm.eps)
+        return self.ffn(h)
+
+
+class DeepseekModel:
+    def __init__(self, cfg, device="cuda", seed: int = 0):
+        self.cfg = cfg
+        self.device = device
+        self.dtype = dtype_of(cfg.dtype)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self.gen = gen
+        fmt = "nvfp4" if cfg.weight_format == "nvfp4" else "bf16"
+        self.cos_sin = ops.ref.rope_cos_sin(cfg.max_position, cfg.qk_rope, cfg.rope_theta, device=device)
+        self.embed = init_weight((cfg.vocab, cfg.hidden), cfg.init_std, self.dtype, device, gen)
+        self.layers = [DeepseekLayer(cfg, i, self.dtype, device, gen, self.cos_sin, fmt) for i in range(cfg.layers)]
+        self.norm = RMSNorm(cfg.hidden, cfg.norm_eps, self.dtype, device)
+        self.lm_head = Linear(cfg.hidden, cfg.vocab, self.dtype, device, gen)
+        self.vocab_offset = 0
+        self.num_kv_layers = cfg.layers
+
+    @property
+    def kv_heads_local(self) -> int:
+        return 1
+
+    def kv_cache_shape(self, num_blocks: int, block_size: int):
+        return (num_blocks, block_size, self.cfg.kv_lora + self.cfg.qk_rope)
+
+    def allocate_caches(self, num_blocks: int, block_size: int, slots: int, window: int) -> List:
+        caches = []
+        for _ in self.layers:
+            lat = torch.zeros(num_blocks, block_size, self.cfg.kv_lora + self.cfg.qk_rope, dtype=self.dtype,
+                              device=self.device)
+            idx = (torch.zeros(num_blocks, block_size, self.cfg.dsa_head_dim, dtype=self.dtype, device=self.device)
+                   if self.cfg.dsa_topk else None)
+            caches.append((lat, idx))
+        return caches
+
+    def forward(self, ids, meta: AttnMeta, caches, embeds=None):
+        residual = ops.embedding(ids, self.embed) if embeds is None else embeds
+        x = ops.rms_norm(residual, self.layers[0].input_norm.weight, self.cfg.norm_eps)
+        for i, layer in enumerate(self.layers):
+            m = layer(x, residual, meta, caches[i])
+            nxt = self.layers[i + 1].input_norm if i + 1 < len(self.layers) else self.norm
+            ops.fused_add_rms_norm(m, residual, nxt.weight, nxt.eps)
+            x = m
+        return x, residual
+
+    def logits(self, hidden):
+        return self.lm_head(hidden)
+
+    def greedy(self, hidden, out=None):
+        return comm.vocab_parallel_argmax(self.logits(hidden), self.vocab_offset, out)
+
+
+class DeepseekMtp:
+    """One MTP layer (MLA + MoE) on [enorm(embed(token)), hnorm(feature)]; shares embedding and head."""
+
+    def __init__(self, cfg, target: DeepseekModel, device="cuda"):
+        self.cfg, self.target = cfg, target
+        dt, gen = target.dtype, target.gen
+        self.enorm = RMSNorm(cfg.hidden, cfg.norm_eps, dt, device)
+        self.hnorm = RMSNorm(cfg.hidden, cfg.norm_eps, dt, device)
+        self.eh_proj = init_weight((cfg.hidden, 2 * cfg.hidden), cfg.init_std, dt, device, gen)
+        fmt = "nvfp4" if cfg.weight_format == "nvfp4" else "bf16"
+        self.layer = DeepseekLayer(cfg, cfg.layers, dt, device, gen, target.cos_sin, fmt)
+        self.norm = RMSNorm(cfg.hidden, cfg.norm_eps, dt, device)
+
+    def allocate_caches(self, num_blocks: int, block_size: int):
+        return self.target.allocate_caches(num_blocks, block_size, 0, 0)[0]
+
+    def forward(self, tokens, feature, meta, cache):
+        e = self.enorm(ops.embedding(tokens, self.target.embed))
+        residual = ops.linear(torch.cat([e, self.hnorm(feature)], -1), self.eh_proj)
+        x = ops.rms_norm(residual, self.layer.input_norm.weight, self.cfg.norm_eps)
+        m = self.layer(x, residual, meta, cache)
+        ops.fused_add_rms_norm(m, residual, self.norm.weight, self.norm.eps)
+        return m, residual
+
+
+def build(cfg, device, seed, with_draft):
+    m = DeepseekModel(cfg, device, seed)
+    return m, (DeepseekMtp(cfg, m, device) if with_draft else None)

@@ -383,3 +383,32 @@ def rms_norm_heads(x3: torch.Tensor, w: torch.Tensor, eps: float) -> None:
     tmp = x3.reshape(T * nh, d) if x3.is_contiguous() else x3.contiguous().view(T * nh, d)
     res = rms_norm(tmp, w, eps)
     x3.copy_(res.view(T, nh, d))
+
+
+# ----------------------------------------------------------------------------- NVFP4
+def nvfp4_quantize(w: torch.Tensor, global_scale: torch.Tensor | None = None):
+    """bf16 [N, K] -> (packed uint8 [N, K/2], e4m3 scales [N, K/16], fp32 global [1])."""
+    if global_scale is None:
+        global_scale = ref.nvfp4_global_scale(w).to(w.device)
+    if not w.is_cuda:
+        p, s = ref.nvfp4_quantize(w, global_scale)
+        return p, s, global_scale
+    N, K = w.shape
+    packed = torch.empty(N, K // 2, dtype=torch.uint8, device=w.device)
+    scales = torch.empty(N, K // 16, dtype=torch.float8_e4m3fn, device=w.device)
+    native().nvfp4_quant(packed, scales.view(torch.uint8), w.contiguous(), global_scale.float())
+    return packed, scales, global_scale
+
+
+def nvfp4_dequantize(packed, scales, global_scale, out: torch.Tensor | None = None) -> torch.Tensor:
+    if not packed.is_cuda:
+        r = ref.nvfp4_dequantize(packed, scales, global_scale)
+        if out is not None:
+            out.copy_(r)
+            return out
+        return r
+    N, K = packed.shape[0], packed.shape[1] * 2
+    if out is None:
+        out = torch.empty(N, K, dtype=torch.bfloat16, device=packed.device)
+    native().nvfp4_dequant(out, packed, scales.view(torch.uint8), global_scale.float())
+    return out

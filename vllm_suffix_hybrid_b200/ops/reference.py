@@ -143,3 +143,96 @@ def gated_rms_norm(o: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float
     of = o.float()
     inv = torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + eps)
     return of * inv * w.float() * torch.nn.functional.silu(z.float())
+
+
+# ----------------------------------------------------------------------------- NVFP4
+E2M1 = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+
+
+def nvfp4_global_scale(w: torch.Tensor) -> torch.Tensor:
+    return (w.float().abs().max() / (6.0 * 448.0)).reshape(1).clamp_min(1e-12)
+
+
+def nvfp4_quantize(w: torch.Tensor, global_scale: torch.Tensor):
+    """(packed uint8 [N, K/2], scales e4m3 [N, K/16]) in the ModelOpt NVFP4 layout."""
+    N, K = w.shape
+    wf = w.float().view(N, K // 16, 16)
+    g = float(global_scale.reshape(-1)[0])
+    amax = wf.abs().amax(-1)
+    sc = (amax / 6.0 / g).to(torch.float8_e4m3fn)
+    s = sc.float() * g
+    x = wf / torch.where(s > 0, s, torch.ones_like(s))[..., None]
+    a = x.abs()
+    mids = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])
+    code = torch.bucketize(a, mids, right=False).to(torch.uint8)  # a <= mid -> lower code
+    code = torch.where((x < 0) & (code > 0), code | 8, code)
+    code = code.view(N, K)
+    packed = (code[:, 0::2] | (code[:, 1::2] << 4)).to(torch.uint8)
+    return packed.contiguous(), sc.contiguous()
+
+
+def nvfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor, global_scale: torch.Tensor) -> torch.Tensor:
+    N = packed.shape[0]
+    K = packed.shape[1] * 2
+    lo = (packed & 15).long()
+    hi = (packed >> 4).long()
+    codes = torch.stack([lo, hi], -1).view(N, K)
+    mag = E2M1[codes & 7]
+    val = torch.where(codes & 8 > 0, -mag, mag)
+    s = scales.float().repeat_interleave(16, dim=1) * float(global_scale.reshape(-1)[0])
+    return (val * s).to(torch.bfloat16)
+
+
+# ----------------------------------------------------------------------------- MLA / DSA
+def mla_attention(q_lat, q_pe, latent, block_tables, seq_lens, q_start, scale, kv_lora, topk=None):
+    """Absorbed MLA over a latent cache [blocks, bs, kv_lora + rope].
+
+    q_lat [T, H, kv_lora], q_pe [T, H, rope]; returns o_lat [T, H, kv_lora] (fp32).
+    topk [T, K] (absolute positions, -1 = unused) restricts each query to those keys (DSA)."""
+    bs = latent.shape[1]
+    T, H, _ = q_lat.shape
+    out = torch.zeros(T, H, kv_lora, dtype=torch.float32, device=q_lat.device)
+    for b in range(seq_lens.shape[0]):
+        s0, s1 = int(q_start[b]), int(q_start[b + 1])
+        ql, sl = s1 - s0, int(seq_lens[b])
+        if ql == 0:
+            continue
+        nblk = (sl + bs - 1) // bs
+        C = latent[block_tables[b, :nblk].long()].reshape(nblk * bs, -1)[:sl].float()
+        sc = (torch.einsum("thc,sc->ths", q_lat[s0:s1].float(), C[:, :kv_lora]) +
+              torch.einsum("thr,sr->ths", q_pe[s0:s1].float(), C[:, kv_lora:])) * scale
+        qpos = torch.arange(sl - ql, sl, device=q_lat.device)
+        mask = torch.arange(sl, device=q_lat.device)[None, :] > qpos[:, None]
+        if topk is not None:
+            sel = torch.zeros(ql, sl + 1, dtype=torch.bool, device=q_lat.device)
+            idx = topk[s0:s1].long().clamp(-1, sl - 1)
+            sel.scatter_(1, torch.where(idx < 0, torch.full_like(idx, sl), idx), True)
+            mask = mask | ~sel[:, :sl]
+        sc = sc.masked_fill(mask[:, None, :], float("-inf"))
+        out[s0:s1] = torch.einsum("ths,sc->thc", sc.softmax(-1), C[:, :kv_lora])
+    return out
+
+
+def dsa_topk(qi, w, kcache, block_tables, seq_lens, q_start, k):
+    """Lightning indexer: logits[t, s] = sum_h relu(qi[t,h] . k[s]) * w[t,h]; causal top-k positions
+    per query ([T, k] int64, -1 padded; equal logits prefer the later position)."""
+    bs = kcache.shape[1]
+    T = qi.shape[0]
+    out = torch.full((T, k), -1, dtype=torch.long, device=qi.device)
+    for b in range(seq_lens.shape[0]):
+        s0, s1 = int(q_start[b]), int(q_start[b + 1])
+        ql, sl = s1 - s0, int(seq_lens[b])
+        if ql == 0:
+            continue
+        nblk = (sl + bs - 1) // bs
+        Kc = kcache[block_tables[b, :nblk].long()].reshape(nblk * bs, -1)[:sl].float()
+        lg = (torch.relu(torch.einsum("thd,sd->ths", qi[s0:s1].float(), Kc)) * w[s0:s1].float()[..., None]).sum(1)
+        qpos = torch.arange(sl - ql, sl, device=qi.device)
+        lg = lg.masked_fill(torch.arange(sl, device=qi.device)[None, :] > qpos[:, None], float("-inf"))
+        kk = min(k, sl)
+        # Ties (relu makes exact zeros common) prefer the most recent position: sort the reversed row stably.
+        vals, idx = torch.sort(lg.flip(-1), dim=-1, descending=True, stable=True)
+        vals, idx = vals[:, :kk], sl - 1 - idx[:, :kk]
+        idx = torch.where(torch.isinf(vals), torch.full_like(idx, -1), idx)
+        out[s0:s1, :kk] = idx
+    return out
