@@ -73,7 +73,7 @@ void paged_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, 
 // y[M, N] = x[M, K] @ w[N, K]^T via the tcgen05 GEMM.  swap: weights take the
 // MMA's 128-row side (small M).  ws: fp32 split-K workspace (>= splits*M*N).
 void gemm_bf16(torch::Tensor y, torch::Tensor x, torch::Tensor w, bool swap, int64_t bn, int64_t splits,
-               c10::optional<torch::Tensor> ws, c10::optional<torch::Tensor> err) {
+               c10::optional<torch::Tensor> ws, c10::optional<torch::Tensor> err, bool pair) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && y.is_cuda(), "gemm_bf16: CUDA tensors");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
               "gemm_bf16: bf16 tensors");
@@ -90,14 +90,15 @@ void gemm_bf16(torch::Tensor y, torch::Tensor x, torch::Tensor w, bool swap, int
   }
   int* errp = err.has_value() ? err->data_ptr<int>() : nullptr;
   auto stream = at::cuda::getCurrentCUDAStream();
+  auto fn = pair ? sh_gemm_bf16_pair : sh_gemm_bf16_tcgen05;
   int r;
   if (swap)
-    r = sh_gemm_bf16_tcgen05(w.data_ptr(), N, w.stride(0), x.data_ptr(), M, x.stride(0), K, y.data_ptr(), y.stride(0),
-                             1, bn, splits, wsp, errp, num_sms, stream);
+    r = fn(w.data_ptr(), N, w.stride(0), x.data_ptr(), M, x.stride(0), K, y.data_ptr(), y.stride(0), 1, bn, splits, wsp,
+           errp, num_sms, stream);
   else
-    r = sh_gemm_bf16_tcgen05(x.data_ptr(), M, x.stride(0), w.data_ptr(), N, w.stride(0), K, y.data_ptr(), y.stride(0),
-                             0, bn, splits, wsp, errp, num_sms, stream);
-  TORCH_CHECK(r == 0, "sh_gemm_bf16_tcgen05 failed with code ", r);
+    r = fn(x.data_ptr(), M, x.stride(0), w.data_ptr(), N, w.stride(0), K, y.data_ptr(), y.stride(0), 0, bn, splits, wsp,
+           errp, num_sms, stream);
+  TORCH_CHECK(r == 0, pair ? "sh_gemm_bf16_pair" : "sh_gemm_bf16_tcgen05", " failed with code ", r);
 }
 
 // Fused NVLink all-reduce (+ residual add + RMSNorm).  peer_* are device
@@ -318,5 +319,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_dequant", &nvfp4_dequant);
   m.def("nvfp4_quant", &nvfp4_quant);
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM", py::arg("y"), py::arg("x"), py::arg("w"), py::arg("swap"),
-        py::arg("bn"), py::arg("splits"), py::arg("ws") = py::none(), py::arg("err") = py::none());
+        py::arg("bn"), py::arg("splits"), py::arg("ws") = py::none(), py::arg("err") = py::none(), py::arg("pair") = false);
 }

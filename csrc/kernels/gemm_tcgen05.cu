@@ -11,7 +11,7 @@
 // Structure (one CTA per SM, persistent over work units):
 //   warp 0      : TMA producer -- 128B-swizzled [rows][64] bf16 tiles of P and
 //                 Q into a STAGES-deep smem ring, completion via mbarrier tx
-//                 counts.  No cluster multicast anywhere.
+//                 counts.  No TMA load uses cluster multicast.
 //   warp 1      : TMEM allocator and single-thread MMA issuer:
 //                 tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) x4
 //                 per 64-wide k-block into one of two TMEM accumulators,
@@ -30,110 +30,16 @@
 #include <stdint.h>
 
 #include "gemm_tcgen05.h"
+#include "tcgen05_common.cuh"
 
 namespace shk {
 namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t now_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: false on timeout or when another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = now_ns();
-  while (true) {
-    if (mbar_try(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (now_ns() - t0 > kTimeoutNs) return false;
-  }
-}
-
-__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = now_ns();
-  while (!mbar_try(bar, parity))
-    if (now_ns() - t0 > kTimeoutNs) return false;
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (SBO), LBO unused (1), descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
-  d |= static_cast<uint64_t>(1) << 16;             // LBO (16 B units)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;     // SBO
-  d |= static_cast<uint64_t>(1) << 46;             // version
-  d |= static_cast<uint64_t>(2) << 61;             // SWIZZLE_128B
-  return d;
-}
 
 // Instruction descriptor: D f32, A/B bf16, both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) { return idesc_bf16_mn(BM, n); }
 
 template <int BN>
 __host__ __device__ constexpr int tmem_cols() {
@@ -383,6 +289,257 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ============================================================================
+// CTA-pair GEMM (cta_group::2).  A cluster of two CTAs on neighbouring SMs
+// computes a 256 x BN tile: CTA r loads P rows [256 tp + 128 r, +128) and Q
+// rows [BN tq + r BN/2, +BN/2) with its own TMA loads (no multicast); both
+// loads count on the LEADER CTA's full barrier.  The leader's single MMA
+// thread issues tcgen05.mma.cta_group::2 (M = 256, N = BN): the tensor cores
+// of both SMs read A from their own CTA and B from both, and each CTA's TMEM
+// receives its 128 rows.  Per SM and 64-wide k-block that is 16 KB of A plus
+// BN/2 x 128 B of B for 128 x BN x 64 MACs -- half the B traffic of a
+// one-CTA 128 x BN tile, which is what the L2 -> SM path needs at M >= 256.
+//
+// Barriers (all counts per phase):
+//   full[s]   leader only: 1 arrive.expect_tx (both CTAs' bytes) + TMA tx
+//   empty[s]  each CTA: 1 commit from the leader's MMA thread
+//   tfull[a]  each CTA: 1 commit from the leader's MMA thread
+//   tempty[a] leader only: 8 arrives (4 epilogue warps x 2 CTAs)
+// Aborts (bounded waits) are mirrored into the peer's flag; before exit both
+// CTAs give in-flight loads time to land, meet at a cluster barrier and free
+// TMEM together.
+// ============================================================================
+constexpr int PAIR_ROWS = 128;  // P rows per CTA; the pair tile is 256 rows
+
+// TMEM columns between the two accumulators (a power of two, so N = 192 tiles start 256-aligned).
+template <int BN>
+__host__ __device__ constexpr int pair_acc_cols() {
+  return BN <= 128 ? 128 : 256;
+}
+template <int BN>
+__host__ __device__ constexpr int pair_tmem_cols() {
+  return 2 * pair_acc_cols<BN>();
+}
+
+template <int BN, int STAGES>
+struct PairSmem {
+  static constexpr int A_BYTES = PAIR_ROWS * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 5) * 8 + 16 + 1024;
+  static_assert(B_BYTES % 1024 == 0, "B half tile must keep the 1024-byte swizzle alignment");
+  static_assert(TOTAL <= 227 * 1024, "shared memory budget");
+};
+
+template <int BN, int STAGES, bool TRANS, bool SPLIT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                     GemmParams g) {
+  using S = PairSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int TCOLS = pair_tmem_cols<BN>();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmP)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(TCOLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers are initialised before any remote arrive / complete_tx
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  const int total_work = g.tiles_p * g.tiles_q * g.splits;
+  const uint32_t peer_abort = map_to_rank(const_cast<int*>(abort_flag), rank ^ 1);
+  auto raise = [&](int code) {
+    if (g.err) atomicCAS(g.err, 0, code);
+    *abort_flag = 1;
+    st_cluster_u32(peer_abort, 1);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int w = cid; w < total_work; w += ncl) {
+        const Work wk = decode_work(w, g, BN);
+        int p_y = wk.tp * (2 * PAIR_ROWS) + static_cast<int>(rank) * PAIR_ROWS;
+        int q_y = wk.tq * BN + static_cast<int>(rank) * (BN / 2);
+        if (p_y >= g.rows_p) p_y = 0;  // fully outside: load valid rows that are never stored
+        if (q_y >= g.rows_q) q_y = 0;
+        const int kb0 = wk.sp * g.kb_per_split;
+        const int kb1 = min(kb0 + g.kb_per_split, g.kb_total);
+        bool stop = false;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            raise(1);
+            stop = true;
+            break;
+          }
+          if (leader) mbar_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
+          uint8_t* sp = smem + stage * S::STAGE_BYTES;
+          const uint32_t bar = map_to_rank(&full[stage], 0);
+          tma_load_2d_pair(sp, &tmP, kb * BK, p_y, bar);
+          tma_load_2d_pair(sp + S::A_BYTES, &tmQ, kb * BK, q_y, bar);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (stop) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t IDESC = idesc_bf16_mn(2 * PAIR_ROWS, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int w = cid; w < total_work; w += ncl) {
+        const Work wk = decode_work(w, g, BN);
+        const int kb0 = wk.sp * g.kb_per_split;
+        const int kb1 = min(kb0 + g.kb_per_split, g.kb_total);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
+          raise(2);
+          break;
+        }
+        fence_after();
+        const uint32_t tmem_d = tmem_base + acc * pair_acc_cols<BN>();
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t sa = smem_addr(smem + stage * S::STAGE_BYTES);
+          const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_bf16_pair(tmem_d, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), IDESC,
+                          (kb > kb0 || kk > 0) ? 1u : 0u);
+          mma_commit_pair_both(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) {
+          raise(3);
+          mma_commit_pair_local(mma_done);
+          (void)mbar_wait_drain(mma_done, 0);
+          break;
+        }
+        mma_commit_pair_both(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int w = cid; w < total_work; w += ncl) {
+      const Work wk = decode_work(w, g, BN);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+        if (lane == 0) raise(4);
+        break;
+      }
+      fence_after();
+      const int p = wk.tp * (2 * PAIR_ROWS) + static_cast<int>(rank) * PAIR_ROWS + row;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * pair_acc_cols<BN>();
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        __syncwarp();
+        tmem_ld16(tbase + c, v);
+        const int q0 = wk.q_base + c;
+        if (p >= wk.p_lim) {
+        } else if (SPLIT) {
+          float* dst = g.ws + (static_cast<int64_t>(wk.sp) * g.rows_p + p) * g.rows_q + q0;
+          if (q0 + 16 <= wk.q_lim && (g.rows_q & 3) == 0) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+            for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i) dst[i] = v[i];
+          }
+        } else if (!TRANS) {
+          __nv_bfloat16* dst = g.out + static_cast<int64_t>(p) * g.ldo + q0;
+          if (q0 + 16 <= wk.q_lim && (g.ldo & 7) == 0) {
+            uint4 pk[2];
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(pk);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            reinterpret_cast<uint4*>(dst)[0] = pk[0];
+            reinterpret_cast<uint4*>(dst)[1] = pk[1];
+          } else {
+            for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i) dst[i] = __float2bfloat16(v[i]);
+          }
+        } else {
+          for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i)
+            g.out[static_cast<int64_t>(q0 + i) * g.ldo + p] = __float2bfloat16(v[i]);
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(&tempty[acc], 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  if (warp == 0 && lane == 0 && *abort_flag) {
+    // Loads issued before the abort complete within microseconds; give them 200 us.
+    const uint64_t t0 = now_ns();
+    while (now_ns() - t0 < 200000) {
+    }
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TCOLS));
+  }
+}
+
 // out[(trans ? q : p)] = bf16(sum over splits of ws[s][p][q]) in fixed split order;
 // four consecutive q per thread (float4 loads) when rows_q % 4 == 0.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ out, int splits,
@@ -455,12 +612,27 @@ int make_map(CUtensorMap* m, const void* base, int rows, int K, int64_t row_stri
   return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
 }
 
+constexpr int kMaxDevices = 64;
+
+// Opt a kernel into its dynamic shared-memory size once per device (the
+// attribute call costs microseconds of host time on every launch otherwise).
+int set_smem_once(const void* k, int bytes, bool* ready) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+  if (ready[dev]) return 0;
+  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  ready[dev] = true;
+  return 0;
+}
+
 template <int BN, int STAGES, bool TRANS, bool SPLIT>
 int launch_t(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g, int grid, cudaStream_t st) {
   using S = Smem<BN, STAGES>;
   auto k = gemm_kernel<BN, STAGES, TRANS, SPLIT>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
-  if (e != cudaSuccess) return static_cast<int>(e);
+  static bool ready[kMaxDevices] = {false};
+  const int e = set_smem_once(reinterpret_cast<const void*>(k), S::TOTAL, ready);
+  if (e) return e;
   k<<<grid, 192, S::TOTAL, st>>>(mp, mq, g);
   return static_cast<int>(cudaGetLastError());
 }
@@ -472,6 +644,48 @@ int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g,
                           : launch_t<BN, STAGES, false, true>(mp, mq, g, grid, st);
   return trans ? launch_t<BN, STAGES, true, false>(mp, mq, g, grid, st)
                : launch_t<BN, STAGES, false, false>(mp, mq, g, grid, st);
+}
+
+template <int BN, int STAGES, bool TRANS, bool SPLIT>
+int launch_pair_t(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g, int grid, cudaStream_t st) {
+  using S = PairSmem<BN, STAGES>;
+  auto k = gemm_pair_kernel<BN, STAGES, TRANS, SPLIT>;
+  static bool ready[kMaxDevices] = {false};
+  const int e = set_smem_once(reinterpret_cast<const void*>(k), S::TOTAL, ready);
+  if (e) return e;
+  k<<<grid, 192, S::TOTAL, st>>>(mp, mq, g);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int BN, int STAGES>
+int launch_pair_bn(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g, int grid, bool trans,
+                   bool split, cudaStream_t st) {
+  if (split) return trans ? launch_pair_t<BN, STAGES, true, true>(mp, mq, g, grid, st)
+                          : launch_pair_t<BN, STAGES, false, true>(mp, mq, g, grid, st);
+  return trans ? launch_pair_t<BN, STAGES, true, false>(mp, mq, g, grid, st)
+               : launch_pair_t<BN, STAGES, false, false>(mp, mq, g, grid, st);
+}
+
+// Co-resident CTA pairs on this device for the pair kernel (cached per device).
+int pair_clusters(int num_sms) {
+  static int cached[16] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return num_sms / 2;
+  if (cached[dev]) return cached[dev];
+  using S = PairSmem<256, 6>;
+  auto k = gemm_pair_kernel<256, 6, false, false>;
+  int n = num_sms / 2;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms, 1, 1);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = S::TOTAL;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, k, &cfg) == cudaSuccess && c > 0) n = c < n ? c : n;
+  }
+  (void)cudaGetLastError();
+  cached[dev] = n;
+  return n;
 }
 
 }  // namespace
@@ -567,4 +781,61 @@ extern "C" int sh_gemm_bf16_grouped(const void* P, int p_total_rows, int rows_p,
   else
     r = launch_bn<64, 8>(mp, mq, g, grid, true, false, stream);
   return r ? 3000 + r : 0;
+}
+
+extern "C" int sh_gemm_bf16_pair(const void* P, int rows_p, int64_t ldp, const void* Q, int rows_q, int64_t ldq,
+                                 int K, void* out, int64_t ldo, int trans, int bn, int splits, float* ws, int* err,
+                                 int num_sms, cudaStream_t stream) {
+  if (K % BK != 0 || K <= 0) return -2;
+  if (rows_p <= 0 || rows_q <= 0) return 0;
+  if ((reinterpret_cast<uintptr_t>(P) & 15) || (reinterpret_cast<uintptr_t>(Q) & 15) || (ldp * 2) % 16 ||
+      (ldq * 2) % 16)
+    return -3;
+  if (bn != 128 && bn != 192 && bn != 256) return -4;
+  splits = splits < 1 ? 1 : splits;
+  const int kb_total = K / BK;
+  if (splits > kb_total) splits = kb_total;
+  const int kb_per_split = (kb_total + splits - 1) / splits;
+  splits = (kb_total + kb_per_split - 1) / kb_per_split;
+  if (splits > 1 && ws == nullptr) return -5;
+  CUtensorMap mp, mq;
+  int r = make_map(&mp, P, rows_p, K, ldp, PAIR_ROWS);
+  if (r) return 1000 + r;
+  r = make_map(&mq, Q, rows_q, K, ldq, bn / 2);
+  if (r) return 2000 + r;
+  GemmParams g{};
+  g.rows_p = rows_p;
+  g.rows_q = rows_q;
+  g.tiles_p = (rows_p + 2 * PAIR_ROWS - 1) / (2 * PAIR_ROWS);
+  g.tiles_q = (rows_q + bn - 1) / bn;
+  g.splits = splits;
+  g.kb_total = kb_total;
+  g.kb_per_split = kb_per_split;
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.ldo = static_cast<int>(ldo);
+  g.ws = ws;
+  g.err = err;
+  g.p_fast = trans ? 0 : 1;
+  const int work = g.tiles_p * g.tiles_q * splits;
+  const int clusters = pair_clusters(num_sms);
+  const int grid = 2 * (work < clusters ? work : clusters);
+  const bool split = splits > 1;
+  if (bn == 256)
+    r = launch_pair_bn<256, 6>(mp, mq, g, grid, trans, split, stream);
+  else if (bn == 192)
+    r = launch_pair_bn<192, 7>(mp, mq, g, grid, trans, split, stream);
+  else
+    r = launch_pair_bn<128, 8>(mp, mq, g, grid, trans, split, stream);
+  if (r) return 3000 + r;
+  if (split) {
+    const int64_t n = static_cast<int64_t>(rows_p) * rows_q;
+    int blocks = static_cast<int>((n / 4 + 255) / 256);
+    if (blocks > 8 * num_sms) blocks = 8 * num_sms;
+    if (blocks < 1) blocks = 1;
+    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, static_cast<__nv_bfloat16*>(out), splits, rows_p, rows_q,
+                                                      static_cast<int>(ldo), trans);
+    r = static_cast<int>(cudaGetLastError());
+    if (r) return 4000 + r;
+  }
+  return 0;
 }

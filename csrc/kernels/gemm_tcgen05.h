@@ -32,6 +32,10 @@ extern "C" {
 int sh_gemm_bf16_tcgen05(const void* P, int rows_p, int64_t ldp, const void* Q, int rows_q, int64_t ldq, int K,
                          void* out, int64_t ldo, int trans, int bn, int splits, float* ws, int* err, int num_sms,
                          cudaStream_t stream);
+// Same contract on CTA pairs (cta_group::2, 256-row P tiles; bn in {128, 192, 256}).
+int sh_gemm_bf16_pair(const void* P, int rows_p, int64_t ldp, const void* Q, int rows_q, int64_t ldq, int K,
+                      void* out, int64_t ldo, int trans, int bn, int splits, float* ws, int* err, int num_sms,
+                      cudaStream_t stream);
 // Grouped swap-AB GEMM for MoE experts: for every device-side group entry g
 // (see GemmParams::groups), out[q, :] = sum_k Q[q, k] * P[p_row_offset + n, k]
 // for the q_rows sorted rows of the entry and n < rows_p.  P stacks the

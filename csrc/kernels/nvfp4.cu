@@ -74,14 +74,18 @@ __global__ void quant_kernel(uint8_t* __restrict__ packed, uint8_t* __restrict__
     v[j] = __bfloat162float(src[j]);
     amax = fmaxf(amax, fabsf(v[j]));
   }
+  // IEEE round-to-nearest divisions (not the fast-math approximations): values
+  // that land exactly on a rounding midpoint are common with bf16 inputs, and
+  // the tie rule only holds with exact quotients.
   const float g = global[0];
-  const uint8_t sc = f_to_e4m3(g > 0.f ? amax / 6.f / g : 0.f);
+  const uint8_t sc = f_to_e4m3(g > 0.f ? __fdiv_rn(__fdiv_rn(amax, 6.f), g) : 0.f);
   scales[i] = sc;
   const float s = e4m3_to_f(sc) * g;
-  const float inv = s > 0.f ? 1.f / s : 0.f;
+  const float d = s > 0.f ? s : 1.f;
   uint8_t out[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) out[j] = e2m1_code(v[2 * j] * inv) | (e2m1_code(v[2 * j + 1] * inv) << 4);
+  for (int j = 0; j < 8; ++j)
+    out[j] = e2m1_code(__fdiv_rn(v[2 * j], d)) | (e2m1_code(__fdiv_rn(v[2 * j + 1], d)) << 4);
   *reinterpret_cast<uint2*>(packed + row * (K / 2) + blk * 8) = *reinterpret_cast<const uint2*>(out);
 }
 

@@ -59,3 +59,21 @@ def test_gemm_strided_input_and_graph_capture():
     g.replay()
     torch.cuda.synchronize()
     check(y, x, w)
+
+
+@pytest.mark.parametrize("swap", [False, True])
+@pytest.mark.parametrize("bn", [128, 192, 256])
+@pytest.mark.parametrize("splits", [1, 3])
+@pytest.mark.parametrize("M,N,K", [(300, 520, 1536), (384, 6144, 4096), (96, 640, 1536), (1000, 136, 512)])
+def test_gemm_pair_variants(swap, bn, splits, M, N, K):
+    """CTA-pair (cta_group::2) kernel: partial and fully out-of-range half tiles, both orientations."""
+    torch.manual_seed(bn + splits + M)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    y = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    ws = torch.empty(splits * M * N, device="cuda", dtype=torch.float32) if splits > 1 else None
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.native().gemm_bf16(y, x, w, swap, bn, splits, ws, err, True)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    check(y, x, w)

@@ -41,6 +41,7 @@ def _worker(rank, world, port, method, out_q):
     from vllm_suffix_hybrid_b200.engine.llm import LLMEngine
     from vllm_suffix_hybrid_b200.parallel import state
 
+    torch.set_num_threads(1)  # fixed CPU reduction order in every process
     state.init(tp=world, backend="gloo", timeout_s=60)
     try:
         eng = LLMEngine(_cfg(method))
@@ -55,7 +56,12 @@ def test_tp2_matches_tp1(method):
     from vllm_suffix_hybrid_b200.parallel import state
 
     state._STATE = state.ParallelState()
-    base = LLMEngine(_cfg(method)).generate(_prompts(), max_new_tokens=12)
+    threads = torch.get_num_threads()
+    torch.set_num_threads(1)
+    try:
+        base = LLMEngine(_cfg(method)).generate(_prompts(), max_new_tokens=12)
+    finally:
+        torch.set_num_threads(threads)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()

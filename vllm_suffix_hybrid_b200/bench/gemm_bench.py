@@ -1,7 +1,8 @@
 """tcgen05 GEMM vs cuBLAS (torch.matmul) on the decode/verify GEMM shapes.
 
-Times each shape with CUDA events after warm-up; between timed iterations a
-256 MB buffer is rewritten so every iteration starts with a cold L2.
+Times each shape on the device from CUDA-graph replays (no host launch cost in
+the number); between iterations a 256 MB buffer is rewritten so every
+iteration starts with a cold L2.
 Reports microseconds, TFLOP/s and weight-stream GB/s per implementation.
 Run: python -m vllm_suffix_hybrid_b200.bench.gemm_bench [--json]
 """
@@ -25,19 +26,58 @@ SHAPES = [  # (name, M, N, K) -- Llama-3-8B decode with a k=5 verify window over
 
 
 def time_fn(fn, flush, iters=20, warmup=5):
+    """Device time of fn in microseconds, free of host launch cost.
+
+    Captures `iters` x (L2 flush, fn) in one CUDA graph and `iters` x (flush)
+    in another, replays both and returns the difference per iteration: what
+    the kernels cost when replayed from a graph, as in the decode step.
+    """
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    total = 0.0
-    for _ in range(iters):
-        flush.zero_()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        fn()
-        e.record()
-        e.synchronize()
-        total += s.elapsed_time(e)
-    return total / iters * 1e3  # us
+    g1, g0 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g1):
+        for _ in range(iters):
+            flush.zero_()
+            fn()
+    with torch.cuda.graph(g0):
+        for _ in range(iters):
+            flush.zero_()
+
+    def run(g):
+        g.replay()
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(3):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            g.replay()
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e))
+        return best
+
+    return max(run(g1) - run(g0), 0.0) / iters * 1e3  # us
+
+
+def sweep(name, x, w, y, flush, iters):
+    """Every (pair, swap, bn, splits) configuration of the tcgen05 kernels on one shape."""
+    from vllm_suffix_hybrid_b200 import ops
+    from vllm_suffix_hybrid_b200.ops.gemm import workspace
+
+    M, K = x.shape
+    N = w.shape[0]
+    rows = []
+    for pair in (False, True):
+        for swap in (False, True):
+            for bn in ((128, 192, 256) if pair else (64, 128, 256)):
+                for splits in (1, 2, 4):
+                    ws = workspace(x.device, splits * M * N) if splits > 1 else None
+                    fn = lambda: ops.native().gemm_bf16(y, x, w, swap, bn, splits, ws, None, pair)
+                    rows.append((time_fn(fn, flush, iters, 2), pair, swap, bn, splits))
+    rows.sort()
+    print(json.dumps({"sweep": name, "best": [dict(us=round(t, 2), pair=p, swap=s, bn=b, splits=k)
+                                              for t, p, s, b, k in rows[:6]]}))
 
 
 def main():
@@ -46,6 +86,10 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", default="", help="comma-separated shape names")
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="time every kernel configuration per shape")
+    ap.add_argument("--once", action="store_true",
+                    help="no timing: two eager launches of ours then cuBLAS per shape (for ncu captures)")
+    ap.add_argument("--config", default="", help="force pair,swap,bn,splits (e.g. 1,0,256,1)")
     a = ap.parse_args()
     from vllm_suffix_hybrid_b200.ops.gemm import plan, tcgen05_linear
 
@@ -58,14 +102,33 @@ def main():
         x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
         w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
         y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        t_ours = time_fn(lambda: tcgen05_linear(x, w, y), flush, a.iters)
+        if a.sweep:
+            sweep(name, x, w, y, flush, a.iters)
+        ours = lambda: tcgen05_linear(x, w, y)
+        if a.config:
+            from vllm_suffix_hybrid_b200 import ops
+            from vllm_suffix_hybrid_b200.ops.gemm import workspace
+
+            pr, sw, bn, sp = (int(v) for v in a.config.split(","))
+            ws = workspace(x.device, sp * M * N) if sp > 1 else None
+            ours = lambda: ops.native().gemm_bf16(y, x, w, bool(sw), bn, sp, ws, None, bool(pr))
+        if a.once:
+            for _ in range(2):
+                flush.zero_()
+                ours()
+                flush.zero_()
+                torch.matmul(x, w.t(), out=y)
+            torch.cuda.synchronize()
+            print(json.dumps({"once": name}))
+            continue
+        t_ours = time_fn(ours, flush, a.iters)
         t_lib = float("nan") if a.no_cublas else time_fn(lambda: torch.matmul(x, w.t(), out=y), flush, a.iters)
         ref = (x.float() @ w.float().t())
         tcgen05_linear(x, w, y)
         err = (y.float() - ref).abs().max().item()
         flops = 2.0 * M * N * K
         wbytes = N * K * 2
-        r = {"shape": name, "M": M, "N": N, "K": K, "plan": list(plan(M, N, K)), "tcgen05_us": round(t_ours, 2),
+        r = {"shape": name, "M": M, "N": N, "K": K, "plan": list(plan(M, N, K, x, w, y)), "tcgen05_us": round(t_ours, 2),
              "cublas_us": round(t_lib, 2), "speedup": round(t_lib / t_ours, 3),
              "tcgen05_tflops": round(flops / t_ours / 1e6, 1), "tcgen05_weight_gbs": round(wbytes / t_ours / 1e3, 1),
              "max_abs_err": err}

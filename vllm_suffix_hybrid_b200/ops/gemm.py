@@ -1,12 +1,20 @@
-"""Dispatcher of the tcgen05 GEMM: y = x @ w^T for bf16 x [M, K], w [N, K].
+"""Dispatcher of the tcgen05 GEMMs: y = x @ w^T for bf16 x [M, K], w [N, K].
 
-Chooses per shape (cached) the orientation, the N-tile of the MMA and a
-split-K factor so that the persistent grid fills the 148 SMs in whole waves:
+Two kernels (csrc/kernels/gemm_tcgen05.cu): one CTA per 128-row tile, and a
+CTA pair (cta_group::2) per 256-row tile that halves each SM's share of the
+B operand.  A configuration is (pair, swap, bn, splits):
 
-* M <= 256: swap-AB -- the weight rows take the MMA's 128-row side and the
-  tokens are the MMA N dimension (BN = 64/128/256), so a decode batch pays
-  no padding to 128 rows;
-* M > 256: activations on the 128-row side, weights tiled by BN = 128/256.
+* swap: the weight rows take the MMA's M side and the tokens become the MMA
+  N dimension (bn), so a decode batch pays no padding to 128 rows;
+* bn: MMA N tile (one CTA: 64/128/256, pair: 128/192/256);
+* splits: split-K factor (fp32 partials + a deterministic reduce pass).
+
+By default every new (M, N, K) is autotuned once, on its first eager call:
+the candidate configurations are timed on the device with a cold L2 and the
+fastest is kept for the process (SH_GEMM_TUNE=0 uses the static heuristic;
+SH_GEMM_TUNE_FILE=path loads and saves the choices as JSON, which pins them
+across runs).  Calls during CUDA-graph capture never tune: they use the
+recorded choice or the heuristic.
 
 Split-K partials go to one fp32 workspace per device that grows on demand
 and is reused by every call on that device's stream.
@@ -14,8 +22,10 @@ and is reused by every call on that device's stream.
 from __future__ import annotations
 
 import functools
+import json
 import math
-from typing import Dict, Optional
+import os
+from typing import Dict, Optional, Tuple
 
 import torch
 
@@ -25,33 +35,120 @@ NUM_SMS = 148
 _WS: Dict[int, torch.Tensor] = {}
 
 
-def _waves_eff(units: int, sms: int = NUM_SMS) -> float:
-    return units / (math.ceil(units / sms) * sms)
-
-
 @functools.lru_cache(maxsize=4096)
-def plan(M: int, N: int, K: int):
-    """(swap, bn, splits) for y[M, N] = x[M, K] w[N, K]^T.
+def heuristic(M: int, N: int, K: int) -> Tuple[bool, bool, int, int]:
+    """(pair, swap, bn, splits) without measurement.
 
-    Split-K only when the tile grid is under one wave: its fp32 partials cost
-    extra traffic and a reduce pass, so it must buy idle SMs.
+    Decode sizes (M <= 256) are weight-streaming: one-CTA swap-AB tiles,
+    split-K only while it at most fills one wave.  Larger M is bound by the
+    L2 -> SM operand stream, where the CTA pair's 256 x 256 tile moves the
+    fewest bytes per MAC.
     """
     kb = max(K // 64, 1)
     if M <= 256:
         bn = next(b for b in (64, 128, 256) if b >= M)
         tiles = math.ceil(N / 128) * math.ceil(M / bn)
         splits = 1
-        while tiles * splits < NUM_SMS and kb // (splits * 2) >= 8 and splits < 8:
+        while tiles * splits * 2 <= NUM_SMS and kb // (splits * 2) >= 8 and splits < 8:
             splits *= 2
-        return True, bn, splits
-    bn = 256 if N > 8192 else 128
-    tiles = math.ceil(M / 128) * math.ceil(N / bn)
+        return False, True, bn, splits
+    tiles = math.ceil(M / 256) * math.ceil(N / 256)
     splits = 1
-    # Split only grids that would leave most SMs idle: the fp32 partial
-    # round trip costs more than a partly filled single wave.
-    while tiles * splits < NUM_SMS // 3 and kb // (splits * 2) >= 16 and splits < 4:
+    while tiles * splits < NUM_SMS // 4 and kb // (splits * 2) >= 16 and splits < 4:
         splits *= 2
-    return False, bn, splits
+    return True, False, 256, splits
+
+
+def candidates(M: int, N: int, K: int):
+    kb = max(K // 64, 1)
+    out = []
+    for pair in (False, True):
+        for swap in (False, True):
+            for bn in ((128, 192, 256) if pair else (64, 128, 256)):
+                if bn >= 2 * max(M if swap else N, 64) and bn > 64:
+                    continue  # tile far wider than the operand
+                for splits in (1, 2, 4):
+                    if splits > 1 and kb // splits < 4:
+                        continue
+                    out.append((pair, swap, bn, splits))
+    return out
+
+
+_CHOICE: Dict[Tuple[int, int, int], Tuple[bool, bool, int, int]] = {}
+_FLUSH: Dict[int, torch.Tensor] = {}
+_LOADED = [False]
+
+
+def _tune_file() -> Optional[str]:
+    return os.environ.get("SH_GEMM_TUNE_FILE") or None
+
+
+def _load():
+    if _LOADED[0]:
+        return
+    _LOADED[0] = True
+    f = _tune_file()
+    if f and os.path.exists(f):
+        with open(f) as fh:
+            for key, val in json.load(fh).items():
+                M, N, K = (int(v) for v in key.split(","))
+                _CHOICE[(M, N, K)] = (bool(val[0]), bool(val[1]), int(val[2]), int(val[3]))
+
+
+def _save():
+    f = _tune_file()
+    if not f:
+        return
+    data = {f"{M},{N},{K}": list(v) for (M, N, K), v in sorted(_CHOICE.items())}
+    tmp = f + ".tmp"
+    with open(tmp, "w") as fh:
+        json.dump(data, fh, indent=0)
+    os.replace(tmp, f)
+
+
+def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> Tuple[bool, bool, int, int]:
+    M, K = x2.shape
+    N = w.shape[0]
+    dev = x2.device
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    flush = _FLUSH.get(idx)
+    if flush is None:
+        flush = _FLUSH[idx] = torch.empty(160 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    lib = native()
+    best, best_t = None, float("inf")
+    for cfg in candidates(M, N, K):
+        pair, swap, bn, splits = cfg
+        ws = workspace(dev, splits * M * N) if splits > 1 else None
+        lib.gemm_bf16(y, x2, w, swap, bn, splits, ws, None, pair)  # first launch: no timing
+        t = float("inf")
+        for _ in range(2):
+            flush.zero_()  # cold L2, and keeps the GPU busy while the timed launch is enqueued
+            torch.cuda._sleep(50_000)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            lib.gemm_bf16(y, x2, w, swap, bn, splits, ws, None, pair)
+            e.record()
+            e.synchronize()
+            t = min(t, s.elapsed_time(e))
+        if t < best_t:
+            best, best_t = cfg, t
+    return best
+
+
+def plan(M: int, N: int, K: int, x2: Optional[torch.Tensor] = None, w: Optional[torch.Tensor] = None,
+         y: Optional[torch.Tensor] = None) -> Tuple[bool, bool, int, int]:
+    """Configuration for y[M, N] = x[M, K] w[N, K]^T (see the module docstring)."""
+    _load()
+    key = (M, N, K)
+    got = _CHOICE.get(key)
+    if got is not None:
+        return got
+    if (x2 is None or os.environ.get("SH_GEMM_TUNE", "1") == "0" or torch.cuda.is_current_stream_capturing()):
+        return heuristic(M, N, K)
+    got = _autotune(x2, w, y)
+    _CHOICE[key] = got
+    _save()
+    return got
 
 
 def workspace(device: torch.device, numel: int) -> torch.Tensor:
@@ -77,7 +174,7 @@ def tcgen05_linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor]
     y = out.view(M, N) if out is not None else torch.empty(M, N, dtype=x.dtype, device=x.device)
     if M == 0:
         return y.view(*lead, N)
-    swap, bn, splits = plan(M, N, K)
+    pair, swap, bn, splits = plan(M, N, K, x2, w, y)
     ws = workspace(x.device, splits * M * N) if splits > 1 else None
-    native().gemm_bf16(y, x2, w, swap, bn, splits, ws)
+    native().gemm_bf16(y, x2, w, swap, bn, splits, ws, None, pair)
     return y.view(*lead, N)
