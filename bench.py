@@ -36,6 +36,43 @@ def reference_arm(args):
         print(json.dumps({"impl": "reference", "unavailable": why}))
 
 
+def trace_steps(eng, path, rank, barrier):
+    """Per-kernel device time of 2 decode steps (torch.profiler / CUPTI), summed by kernel name."""
+    import collections
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    barrier()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(2):
+            eng.step()
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    spans = []
+    for ev in prof.events():
+        if ev.device_type is not None and str(ev.device_type).endswith("CUDA") and ev.device_time_total > 0:
+            name = ev.name
+            agg[name][0] += 1
+            agg[name][1] += ev.device_time_total
+            spans.append((ev.time_range.start, ev.time_range.end))
+    total = sum(v[1] for v in agg.values())
+    busy, end = 0.0, None
+    for a, b in sorted(spans):
+        if end is None or a > end:
+            busy += b - a
+            end = b
+        elif b > end:
+            busy += b - end
+            end = b
+    wall = (max(b for _, b in spans) - min(a for a, _ in spans)) if spans else 0.0
+    with open(f"{path}_rank{rank}.txt", "w") as fh:
+        fh.write(f"# 2 decode steps; kernel time {total:.1f} us; device busy {busy:.1f} us of {wall:.1f} us span\n")
+        for name, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
+            fh.write(f"{t:10.1f} us {n:6d}  {100 * t / max(total, 1e-9):5.1f}%  {name[:150]}\n")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -56,6 +93,9 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="profile one eager decode step between cudaProfilerStart/Stop (for ncu) and exit")
     ap.add_argument("--dump-tokens", type=int, default=0, help="print the first N generated tokens of row 0")
+    ap.add_argument("--trace", default="",
+                    help="after the timed steps, run 2 untimed steps under torch.profiler and write a per-kernel "
+                         "device-time summary per rank to <trace>_rank<R>.txt")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -120,7 +160,7 @@ def main():
         n_launch_step = ctr.count
     torch.cuda.synchronize()
     barrier()
-    clocks = ClockSampler()
+    clocks = ClockSampler(gpus=list(range(world)))
     if rank == 0:
         clocks.start()
     torch.cuda.synchronize()
@@ -138,7 +178,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     wall = time.perf_counter() - t0
-    clk = clocks.stop(gpus=list(range(world))) if rank == 0 else {}
+    clk = clocks.stop() if rank == 0 else {}
     steps = eng.stats[first:]
     tokens = sum(s.emitted for s in steps)
     rows = sum(s.num_reqs for s in steps)
@@ -183,6 +223,11 @@ def main():
             r0 = eng.running[0]
             out["sample_tokens"] = r0.output[: args.dump_tokens]
         print(json.dumps(out))
+    if args.trace:
+        try:
+            trace_steps(eng, args.trace, rank, barrier)
+        except Exception as e:  # diagnostics only; never fail the benchmark
+            print(f"trace failed on rank {rank}: {e!r}", file=sys.stderr)
     if world > 1:
         eng.runner.graphs.clear()
         torch.cuda.synchronize()

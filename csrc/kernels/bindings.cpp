@@ -102,19 +102,25 @@ void gemm_bf16(torch::Tensor y, torch::Tensor x, torch::Tensor w, bool swap, int
 }
 
 // Fused NVLink all-reduce (+ residual add + RMSNorm).  peer_* are device
-// addresses (ints) of every rank's symmetric buffers / signal pads.
-void allreduce_fused(std::vector<int64_t> peer_in, std::vector<int64_t> peer_gather, std::vector<int64_t> peer_flags,
-                     torch::Tensor counters, torch::Tensor out, c10::optional<torch::Tensor> residual,
-                     c10::optional<torch::Tensor> weight, torch::Tensor err, int64_t rank, int64_t T, int64_t H,
-                     double eps, bool two_shot, int64_t num_blocks) {
-  const int world = static_cast<int>(peer_in.size());
-  TORCH_CHECK(world >= 1 && world <= SH_COMM_MAX_WORLD && peer_gather.size() == peer_in.size() &&
-                  peer_flags.size() == peer_in.size(), "allreduce_fused: peer lists");
+// addresses (ints) of every rank's symmetric receive / gather buffers and
+// flag arrays; `partial` is this rank's [T, H] partial in local memory.
+void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std::vector<int64_t> peer_gather,
+                     std::vector<int64_t> peer_flags, torch::Tensor counters, torch::Tensor out,
+                     c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, torch::Tensor err,
+                     int64_t rank, int64_t T, int64_t H, int64_t max_T, double eps, bool two_shot,
+                     int64_t num_blocks) {
+  const int world = static_cast<int>(peer_recv.size());
+  TORCH_CHECK(world >= 1 && world <= SH_COMM_MAX_WORLD && peer_gather.size() == peer_recv.size() &&
+                  peer_flags.size() == peer_recv.size(), "allreduce_fused: peer lists");
+  TORCH_CHECK(partial.is_cuda() && partial.scalar_type() == at::kBFloat16 && partial.is_contiguous() &&
+                  partial.numel() >= T * H, "allreduce_fused: partial");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() >= T * H, "out");
   TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= SH_COMM_MAX_BLOCKS, "counters");
+  TORCH_CHECK(T <= max_T, "allreduce_fused: T exceeds the receive slots");
   ArParams p{};
+  p.partial = reinterpret_cast<const __nv_bfloat16*>(partial.data_ptr());
   for (int i = 0; i < world; ++i) {
-    p.peer_in[i] = reinterpret_cast<const __nv_bfloat16*>(peer_in[i]);
+    p.peer_recv[i] = reinterpret_cast<__nv_bfloat16*>(peer_recv[i]);
     p.peer_gather[i] = reinterpret_cast<__nv_bfloat16*>(peer_gather[i]);
     p.peer_flags[i] = reinterpret_cast<uint32_t*>(peer_flags[i]);
   }
@@ -132,6 +138,7 @@ void allreduce_fused(std::vector<int64_t> peer_in, std::vector<int64_t> peer_gat
   p.world = world;
   p.T = static_cast<int>(T);
   p.H = static_cast<int>(H);
+  p.max_T = static_cast<int>(max_T);
   p.eps = static_cast<float>(eps);
   p.two_shot = two_shot ? 1 : 0;
   const int r = sh_allreduce(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());

@@ -1,25 +1,30 @@
 // Tensor-parallel all-reduce over NVLink peer memory, fused with the next
 // layer's residual add + RMSNorm.
 //
-// Every rank's row-parallel GEMM writes its [T, H] partial straight into its
-// symmetric buffer; this kernel then
-//   one-shot (small T*H): every rank reads all peers' partials for its rows
-//     (P2P loads over NVLink), sums them in rank order in fp32;
-//   two-shot (large T*H): rank q reduces the rows it owns and stores the
-//     bf16 sum into every rank's gather buffer (P2P stores), then each rank
-//     reads the gathered sums from its own memory;
-// and finishes with residual += sum, out = rms_norm(residual) * weight (or
-// writes the plain sum).  Summation order is the same on every rank, so all
-// ranks hold bit-identical results.
+// The row-parallel GEMM writes its [T, H] partial into local memory; this
+// kernel moves data only with P2P STORES (posted writes, no round trip):
+//   one-shot (small T*H): every rank pushes its partial rows into a receive
+//     slot of every peer, waits for the peers' pushes, and sums the world
+//     partials in rank order from its own memory;
+//   two-shot (large T*H): rows are split into world contiguous chunks; every
+//     rank pushes each chunk to its owner, the owner sums its chunk in rank
+//     order and pushes the bf16 sums into every rank's gather buffer, and each
+//     rank reads the gathered sums from its own memory;
+// then residual += sum, out = rms_norm(residual) * weight (or out = sum) on
+// every rank.  The summation order is the same everywhere, so all ranks hold
+// bit-identical results.
 //
 // Synchronisation: block b of every rank handles the same rows, so ranks only
-// synchronise block-to-block.  A barrier is: __syncthreads, system-scope
-// release store of the block's epoch into each peer's signal pad, then
-// acquire loads of the peers' flags.  Epochs live in per-block device
-// counters, so CUDA-graph replays stay aligned across ranks.  Each wait gives
-// up after a time limit, records an error code in *err and skips the data
-// phase (the step is then failed by the host; no trap, no hang).  The grid is
-// at most one block per SM so every block is resident while it waits.
+// synchronise block-to-block: a system-scope release store of the block's
+// epoch into each peer's flag slot, then acquire loads of the peers' slots.
+// Receive and gather buffers are double-buffered by epoch parity, which makes
+// a trailing "peers are done reading" barrier unnecessary: before a rank can
+// write a slot of parity e again (call e + 2) it must pass call e + 1's wait,
+// which every peer signals only after finishing call e.  The grid is the same
+// for every call of a communicator, so all blocks of a call share one epoch
+// (and one parity), and at most one block per SM so every block is resident
+// while it waits.  Each wait gives up after a time limit, records an error
+// code in *err and skips the remaining data phases (no trap, no hang).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -30,7 +35,6 @@ namespace shk {
 namespace comm {
 
 constexpr uint64_t kTimeoutNs = 5000000000ull;  // 5 s
-constexpr int kPhases = 3;
 
 __device__ __forceinline__ uint64_t now_ns() {
   uint64_t t;
@@ -47,6 +51,7 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
 }
 __device__ __forceinline__ uint32_t* flag_slot(uint32_t* pad, int phase, int block, int src) {
   return pad + (static_cast<size_t>(phase) * SH_COMM_MAX_BLOCKS + block) * SH_COMM_MAX_WORLD + src;
+  static_assert(SH_COMM_PHASES == 2, "flag layout");
 }
 
 // Cross-rank barrier between same-index blocks. Returns false on timeout.
@@ -156,6 +161,26 @@ __device__ void finish_row(const ArParams& p, int64_t r, float (*acc)[8], float*
 }
 
 template <int VPT>
+__device__ __forceinline__ void zero_acc(float (*acc)[8]) {
+#pragma unroll
+  for (int k = 0; k < VPT; ++k)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
+}
+
+// dst[v] = src[v] for this thread's vectors of one row, to every rank in `mask` but `skip`.
+template <int VPT>
+__device__ __forceinline__ void push_row(const uint4* src, uint4* const* dst, int ndst, int nv) {
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int v = threadIdx.x + k * blockDim.x;
+    if (v >= nv) continue;
+    const uint4 val = src[v];
+    for (int d = 0; d < ndst; ++d) dst[d][v] = val;
+  }
+}
+
+template <int VPT>
 __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
   __shared__ float red[32];
   __shared__ uint32_t s_epoch;
@@ -166,18 +191,33 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
   }
   __syncthreads();
   const uint32_t epoch = s_epoch;
+  const size_t par = epoch & 1u;
   const int nv = p.H / 8;
   const int nb = gridDim.x;
-  if (!barrier(p, 0, epoch, &bail)) return;  // every partial is written
+  const int W = p.world;
+  const size_t H = static_cast<size_t>(p.H);
+  // Receive slot of source `src` in rank `dst`'s buffer for row r.
+  auto recv_row = [&](int dst, int src, int64_t r) {
+    return reinterpret_cast<uint4*>(p.peer_recv[dst] + ((par * W + src) * p.max_T + r) * H);
+  };
+  auto gather_row = [&](int dst, int64_t r) {
+    return reinterpret_cast<uint4*>(p.peer_gather[dst] + (par * p.max_T + r) * H);
+  };
+  const uint4* partial = reinterpret_cast<const uint4*>(p.partial);
+  uint4* dsts[SH_COMM_MAX_WORLD];
+
   if (!p.two_shot) {
     for (int64_t r = blockIdx.x; r < p.T; r += nb) {
+      int n = 0;
+      for (int i = 1; i < W; ++i) dsts[n++] = recv_row((p.rank + i) % W, p.rank, r);
+      push_row<VPT>(partial + r * (H / 8), dsts, n, nv);
+    }
+    if (!barrier(p, 0, epoch, &bail)) return;  // every peer's partial has landed here
+    for (int64_t r = blockIdx.x; r < p.T; r += nb) {
       float acc[VPT][8];
-#pragma unroll
-      for (int k = 0; k < VPT; ++k)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
-      for (int src = 0; src < p.world; ++src) {
-        const uint4* in = reinterpret_cast<const uint4*>(p.peer_in[src] + r * p.H);
+      zero_acc<VPT>(acc);
+      for (int src = 0; src < W; ++src) {
+        const uint4* in = src == p.rank ? partial + r * (H / 8) : recv_row(p.rank, src, r);
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
           const int v = threadIdx.x + k * blockDim.x;
@@ -186,45 +226,57 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
       }
       finish_row<VPT>(p, r, acc, red);
     }
-    barrier(p, 2, epoch, &bail);  // peers are done reading this rank's partial
     return;
   }
-  // Two-shot: rows r with r % nb == block; owner rank = (r / nb) % world.
-  for (int64_t r = blockIdx.x; r < p.T; r += nb) {
-    if ((r / nb) % p.world != p.rank) continue;
-    float acc[VPT][8];
+  // Two-shot.  Owner o holds rows [o*Tc, min(T, (o+1)*Tc)); block b handles
+  // local row indices j = b, b + nb, ... of every chunk.
+  const int Tc = (p.T + W - 1) / W;
+  for (int i = 1; i < W; ++i) {
+    const int o = (p.rank + i) % W;
+    const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(o + 1) * Tc);
+    for (int64_t r = static_cast<int64_t>(o) * Tc + blockIdx.x; r < r1; r += nb) {
+      dsts[0] = recv_row(o, p.rank, r);
+      push_row<VPT>(partial + r * (H / 8), dsts, 1, nv);
+    }
+  }
+  if (!barrier(p, 0, epoch, &bail)) return;  // every chunk this rank owns has landed
+  {
+    const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(p.rank + 1) * Tc);
+    for (int64_t r = static_cast<int64_t>(p.rank) * Tc + blockIdx.x; r < r1; r += nb) {
+      float acc[VPT][8];
+      zero_acc<VPT>(acc);
+      for (int src = 0; src < W; ++src) {
+        const uint4* in = src == p.rank ? partial + r * (H / 8) : recv_row(p.rank, src, r);
 #pragma unroll
-    for (int k = 0; k < VPT; ++k)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
-    for (int src = 0; src < p.world; ++src) {
-      const uint4* in = reinterpret_cast<const uint4*>(p.peer_in[src] + r * p.H);
+        for (int k = 0; k < VPT; ++k) {
+          const int v = threadIdx.x + k * blockDim.x;
+          if (v < nv) add8(acc[k], in[v]);
+        }
+      }
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
         const int v = threadIdx.x + k * blockDim.x;
-        if (v < nv) add8(acc[k], in[v]);
+        if (v >= nv) continue;
+        const uint4 packed = pack8(acc[k]);
+        for (int i = 0; i < W; ++i) gather_row((p.rank + i) % W, r)[v] = packed;
       }
     }
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int v = threadIdx.x + k * blockDim.x;
-      if (v >= nv) continue;
-      const uint4 packed = pack8(acc[k]);
-      for (int dst = 0; dst < p.world; ++dst) reinterpret_cast<uint4*>(p.peer_gather[dst] + r * p.H)[v] = packed;
-    }
   }
-  if (!barrier(p, 1, epoch, &bail)) return;  // every gathered sum has landed
-  for (int64_t r = blockIdx.x; r < p.T; r += nb) {
-    float acc[VPT][8];
-    const uint4* g = reinterpret_cast<const uint4*>(p.peer_gather[p.rank] + r * p.H);
+  if (!barrier(p, 1, epoch, &bail)) return;  // every owner's sums have landed here
+  for (int o = 0; o < W; ++o) {
+    const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(o + 1) * Tc);
+    for (int64_t r = static_cast<int64_t>(o) * Tc + blockIdx.x; r < r1; r += nb) {
+      float acc[VPT][8];
+      const uint4* g = gather_row(p.rank, r);
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
+      for (int k = 0; k < VPT; ++k) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
-      const int v = threadIdx.x + k * blockDim.x;
-      if (v < nv) add8(acc[k], g[v]);
+        for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
+        const int v = threadIdx.x + k * blockDim.x;
+        if (v < nv) add8(acc[k], g[v]);
+      }
+      finish_row<VPT>(p, r, acc, red);
     }
-    finish_row<VPT>(p, r, acc, red);
   }
 }
 
@@ -235,7 +287,7 @@ using namespace shk::comm;
 
 extern "C" int sh_allreduce(const ArParams* params, int num_blocks, cudaStream_t stream) {
   const ArParams& p = *params;
-  if (p.world < 1 || p.world > SH_COMM_MAX_WORLD || p.H % 8 != 0 || p.T < 0) return -1;
+  if (p.world < 1 || p.world > SH_COMM_MAX_WORLD || p.H % 8 != 0 || p.T < 0 || p.T > p.max_T) return -1;
   if (p.fuse_norm && (p.residual == nullptr || p.weight == nullptr)) return -2;
   if (p.T == 0) return 0;
   if (num_blocks < 1) num_blocks = 1;

@@ -1,4 +1,11 @@
-"""Engine on a B200: speculative decoding (eager and CUDA-graph) reproduces plain greedy decoding."""
+"""Engine on a B200: speculative decoding (eager and CUDA-graph) reproduces plain greedy decoding.
+
+Runs in batch-invariant mode: bit-exact agreement between a k+1-token verify
+window and one-token decoding needs kernels whose per-row reduction order
+does not depend on the number of rows in the call.
+"""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -7,6 +14,11 @@ from vllm_suffix_hybrid_b200.engine.config import CacheConfig, EngineConfig, Spe
 from vllm_suffix_hybrid_b200.engine.llm import LLMEngine
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _batch_invariant(monkeypatch):
+    monkeypatch.setenv("SH_BATCH_INVARIANT", "1")
 
 
 def run(method, graphs, prompts, k=5, new=24):

@@ -116,7 +116,14 @@ _ATTN_WS = {}
 
 
 def attention_splits(num_tiles: int, kv_heads: int, max_pages: int, sms: int = 148) -> int:
-    """KV splits per request so the grid covers ~4 waves of SMs (1..16)."""
+    """KV splits per request so the grid covers ~4 waves of SMs (1..16).
+
+    In batch-invariant mode (SH_BATCH_INVARIANT=1) the count depends on
+    max_pages only, so a query row's merge order does not change with the
+    number of other rows in the call.
+    """
+    if os.environ.get("SH_BATCH_INVARIANT", "0") == "1":
+        return int(max(1, min(8, max_pages // 2)))
     units = max(num_tiles * kv_heads, 1)
     want = -(-4 * sms // units)
     return int(max(1, min(16, want, max(1, max_pages // 2))))

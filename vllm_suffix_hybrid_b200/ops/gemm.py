@@ -16,6 +16,13 @@ SH_GEMM_TUNE_FILE=path loads and saves the choices as JSON, which pins them
 across runs).  Calls during CUDA-graph capture never tune: they use the
 recorded choice or the heuristic.
 
+Batch-invariant mode (SH_BATCH_INVARIANT=1): the split-K factor -- the only
+choice that changes a row's fp32 summation order -- becomes a function of
+(N, K) alone, so a token's output does not depend on how many other tokens
+share the call (a k+1-token verify window gives the same logits as plain
+decoding).  Orientation, pair and N tile do not change the per-element
+order and stay free.
+
 Split-K partials go to one fp32 workspace per device that grows on demand
 and is reused by every call on that device's stream.
 """
@@ -59,7 +66,17 @@ def heuristic(M: int, N: int, K: int) -> Tuple[bool, bool, int, int]:
     return True, False, 256, splits
 
 
-def candidates(M: int, N: int, K: int):
+def batch_invariant() -> bool:
+    return os.environ.get("SH_BATCH_INVARIANT", "0") == "1"
+
+
+@functools.lru_cache(maxsize=4096)
+def invariant_splits(N: int, K: int) -> int:
+    """Split-K factor of (N, K) used for every M in batch-invariant mode (the decode-size choice)."""
+    return heuristic(64, N, K)[3]
+
+
+def candidates(M: int, N: int, K: int, splits_only: Optional[int] = None):
     kb = max(K // 64, 1)
     out = []
     for pair in (False, True):
@@ -67,8 +84,8 @@ def candidates(M: int, N: int, K: int):
             for bn in ((128, 192, 256) if pair else (64, 128, 256)):
                 if bn >= 2 * max(M if swap else N, 64) and bn > 64:
                     continue  # tile far wider than the operand
-                for splits in (1, 2, 4):
-                    if splits > 1 and kb // splits < 4:
+                for splits in ((splits_only,) if splits_only else (1, 2, 4)):
+                    if splits_only is None and splits > 1 and kb // splits < 4:
                         continue
                     out.append((pair, swap, bn, splits))
     return out
@@ -106,7 +123,8 @@ def _save():
     os.replace(tmp, f)
 
 
-def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> Tuple[bool, bool, int, int]:
+def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor,
+              splits_only: Optional[int] = None) -> Tuple[bool, bool, int, int]:
     M, K = x2.shape
     N = w.shape[0]
     dev = x2.device
@@ -115,8 +133,9 @@ def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> Tuple[bool,
     if flush is None:
         flush = _FLUSH[idx] = torch.empty(160 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
     lib = native()
-    best, best_t = None, float("inf")
-    for cfg in candidates(M, N, K):
+    cands = candidates(M, N, K, splits_only)
+    times = []
+    for cfg in cands:
         pair, swap, bn, splits = cfg
         ws = workspace(dev, splits * M * N) if splits > 1 else None
         lib.gemm_bf16(y, x2, w, swap, bn, splits, ws, None, pair)  # first launch: no timing
@@ -130,24 +149,50 @@ def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> Tuple[bool,
             e.record()
             e.synchronize()
             t = min(t, s.elapsed_time(e))
-        if t < best_t:
-            best, best_t = cfg, t
-    return best
+        times.append(t)
+    times = _agree(times)
+    return cands[min(range(len(cands)), key=times.__getitem__)]
+
+
+def _agree(times):
+    """Sum the candidates' times over the tensor-parallel ranks so every rank picks the same configuration.
+
+    Ranks that chose differently would run different kernels per layer and
+    wait for each other at every all-reduce.  Every rank autotunes the same
+    shapes in the same order (the TP-sharded model is identical per rank).
+    """
+    try:
+        import torch.distributed as dist
+
+        from ..parallel import state
+
+        st = state.get()
+        if not dist.is_initialized() or st.tp <= 1 or st.tp != st.world or st.cpu_group is None:
+            return times
+        t = torch.tensor(times, dtype=torch.float64)
+        dist.all_reduce(t, group=st.cpu_group)
+        return t.tolist()
+    except Exception:
+        return times
 
 
 def plan(M: int, N: int, K: int, x2: Optional[torch.Tensor] = None, w: Optional[torch.Tensor] = None,
          y: Optional[torch.Tensor] = None) -> Tuple[bool, bool, int, int]:
     """Configuration for y[M, N] = x[M, K] w[N, K]^T (see the module docstring)."""
     _load()
-    key = (M, N, K)
+    inv = batch_invariant()
+    key = (M, N, K) if not inv else (-M, N, K)
     got = _CHOICE.get(key)
     if got is not None:
         return got
+    fixed = invariant_splits(N, K) if inv else None
     if (x2 is None or os.environ.get("SH_GEMM_TUNE", "1") == "0" or torch.cuda.is_current_stream_capturing()):
-        return heuristic(M, N, K)
-    got = _autotune(x2, w, y)
+        h = heuristic(M, N, K)
+        return h if fixed is None else (h[0], h[1], h[2], fixed)
+    got = _autotune(x2, w, y, fixed)
     _CHOICE[key] = got
-    _save()
+    if not inv:
+        _save()
     return got
 
 

@@ -3,14 +3,18 @@
 Buffers come from torch's symmetric-memory allocator (one mapping of every
 rank's buffer in every process); the data path is this framework's own
 kernel (``_C.allreduce_fused``): row-parallel GEMMs write their partial sums
-straight into ``partial(T)``, and one kernel reduces them across ranks over
-NVLink peer loads/stores and applies the residual add + RMSNorm.
+into the local ``partial(T)`` buffer, and one kernel pushes them to the
+peers with NVLink stores into double-buffered receive slots, reduces in rank
+order and applies the residual add + RMSNorm.
 
-Routing by message size (the reference routes its all-reduce by size bands
-too, reference: suffix_hybrid/nccl_split.py:63-77): one-shot below
-``one_shot_max_bytes`` (latency), two-shot reduce-scatter/all-gather above it
-(bandwidth).  Device-side waits time out into ``err``; ``check()`` raises on
-the host if any collective failed.
+Routing by the bytes each rank sends (the reference routes its all-reduce by
+size bands too, reference: suffix_hybrid/nccl_split.py:63-77): one-shot
+(push the whole partial to every peer, one cross-GPU wait) while
+(world - 1) * T * H * 2 bytes stay under ``one_shot_max_bytes``, two-shot
+(reduce-scatter to row owners, all-gather of the sums, two waits) above it.
+Every call uses the same grid (all blocks then share one epoch parity).
+Device-side waits time out into ``err``; ``check()`` raises on the host if
+any collective failed.
 """
 from __future__ import annotations
 
@@ -23,6 +27,8 @@ import torch.distributed as dist
 from . import state
 
 MAX_BLOCKS = 160
+PHASES = 2
+MAX_WORLD = 8
 
 
 class SymmComm:
@@ -32,24 +38,31 @@ class SymmComm:
 
         st = state.get()
         self.rank, self.world = st.rank, st.world
+        if self.world > MAX_WORLD:
+            raise ValueError(f"fused NVLink collectives support up to {MAX_WORLD} ranks")
         self.group = group or st.group
         self.hidden, self.max_tokens = hidden, max_tokens
         dev = torch.device("cuda", torch.cuda.current_device())
-        self.partial_buf = symm_mem.empty(max_tokens, hidden, dtype=dtype, device=dev)
-        self.gather_buf = symm_mem.empty(max_tokens, hidden, dtype=dtype, device=dev)
+        self.partial_buf = torch.empty(max_tokens, hidden, dtype=dtype, device=dev)
+        self.recv_buf = symm_mem.empty(2 * self.world * max_tokens * hidden, dtype=dtype, device=dev)
+        self.gather_buf = symm_mem.empty(2 * max_tokens * hidden, dtype=dtype, device=dev)
+        self.flag_buf = symm_mem.empty(PHASES * MAX_BLOCKS * MAX_WORLD, dtype=torch.int32, device=dev)
+        self.flag_buf.zero_()
+        torch.cuda.synchronize()
         name = self.group.group_name if hasattr(self.group, "group_name") else dist.group.WORLD.group_name
-        h_in = symm_mem.rendezvous(self.partial_buf, name)
+        h_r = symm_mem.rendezvous(self.recv_buf, name)
         h_g = symm_mem.rendezvous(self.gather_buf, name)
-        self.peer_in = [int(x) for x in h_in.buffer_ptrs]
+        h_f = symm_mem.rendezvous(self.flag_buf, name)
+        self.peer_recv = [int(x) for x in h_r.buffer_ptrs]
         self.peer_gather = [int(x) for x in h_g.buffer_ptrs]
-        self.peer_flags = [int(x) for x in h_in.signal_pad_ptrs]
-        self._handles = (h_in, h_g)
+        self.peer_flags = [int(x) for x in h_f.buffer_ptrs]
+        self._handles = (h_r, h_g, h_f)
         self.counters = torch.zeros(MAX_BLOCKS, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        self.max_blocks = min(MAX_BLOCKS, sms)
+        self.blocks = min(MAX_BLOCKS, sms)
         env = os.environ.get("SH_ONE_SHOT_MAX_BYTES")
-        self.one_shot_max_bytes = int(env) if env else (one_shot_max_bytes or (1 << 20))
+        self.one_shot_max_bytes = int(env) if env else (one_shot_max_bytes or (4 << 20))
         dist.barrier(group=self.group)
 
     # -- buffers --------------------------------------------------------------
@@ -70,10 +83,11 @@ class SymmComm:
         from .. import ops
 
         T, H = x.shape
-        two_shot = T * H * x.element_size() > self.one_shot_max_bytes and T >= self.world
-        blocks = max(1, min(self.max_blocks, T))
-        ops.native().allreduce_fused(self.peer_in, self.peer_gather, self.peer_flags, self.counters, out, residual,
-                                     weight, self.err, self.rank, T, H, eps, two_shot, blocks)
+        sent = (self.world - 1) * T * H * x.element_size()
+        two_shot = sent > self.one_shot_max_bytes and T >= self.world
+        ops.native().allreduce_fused(x, self.peer_recv, self.peer_gather, self.peer_flags, self.counters, out,
+                                     residual, weight, self.err, self.rank, T, H, self.max_tokens, eps, two_shot,
+                                     self.blocks)
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         out = torch.empty_like(x)
