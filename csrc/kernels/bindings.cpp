@@ -108,7 +108,7 @@ void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std:
                      std::vector<int64_t> peer_flags, torch::Tensor counters, torch::Tensor out,
                      c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, torch::Tensor err,
                      int64_t rank, int64_t T, int64_t H, int64_t max_T, double eps, bool two_shot,
-                     int64_t num_blocks) {
+                     int64_t num_blocks, c10::optional<torch::Tensor> timing) {
   const int world = static_cast<int>(peer_recv.size());
   TORCH_CHECK(world >= 1 && world <= SH_COMM_MAX_WORLD && peer_gather.size() == peer_recv.size() &&
                   peer_flags.size() == peer_recv.size(), "allreduce_fused: peer lists");
@@ -141,6 +141,10 @@ void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std:
   p.max_T = static_cast<int>(max_T);
   p.eps = static_cast<float>(eps);
   p.two_shot = two_shot ? 1 : 0;
+  if (timing.has_value()) {
+    TORCH_CHECK(timing->scalar_type() == at::kLong && timing->numel() >= 256, "allreduce_fused: timing [64, 4] int64");
+    p.timing = reinterpret_cast<unsigned long long*>(timing->data_ptr<int64_t>());
+  }
   const int r = sh_allreduce(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_allreduce failed with code ", r);
 }
@@ -315,7 +319,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_cache"), py::arg("block_tables"), py::arg("seq_lens"), py::arg("q_start"), py::arg("tile_req"),
         py::arg("tile_row0"), py::arg("hq"), py::arg("scale"), py::arg("nsplit") = 1, py::arg("part_o") = py::none(),
         py::arg("part_ml") = py::none(), py::arg("err") = py::none(), py::arg("max_rows") = 64);
-  m.def("allreduce_fused", &allreduce_fused);
+  m.def("allreduce_fused", &allreduce_fused, py::arg("partial"), py::arg("peer_recv"), py::arg("peer_gather"),
+        py::arg("peer_flags"), py::arg("counters"), py::arg("out"), py::arg("residual"), py::arg("weight"),
+        py::arg("err"), py::arg("rank"), py::arg("T"), py::arg("H"), py::arg("max_T"), py::arg("eps"),
+        py::arg("two_shot"), py::arg("num_blocks"), py::arg("timing") = py::none());
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("moe_route", &moe_route);

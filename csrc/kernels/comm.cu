@@ -58,7 +58,8 @@ __device__ __forceinline__ uint32_t* flag_slot(uint32_t* pad, int phase, int blo
 __device__ bool barrier(const ArParams& p, int phase, uint32_t epoch, volatile int* bail) {
   __syncthreads();
   if (threadIdx.x < p.world) {
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    // st.release orders every store the block made before the bar.sync above
+    // (cumulativity) ahead of the flag, at system scope.
     st_release(flag_slot(p.peer_flags[threadIdx.x], phase, blockIdx.x, p.rank), epoch);
   }
   if (threadIdx.x < p.world) {
@@ -192,6 +193,9 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
   __syncthreads();
   const uint32_t epoch = s_epoch;
   const size_t par = epoch & 1u;
+  unsigned long long* stamp =
+      (p.timing && blockIdx.x == 0 && threadIdx.x == 0) ? p.timing + 4 * (epoch % 64u) : nullptr;
+  if (stamp) stamp[0] = now_ns();
   const int nv = p.H / 8;
   const int nb = gridDim.x;
   const int W = p.world;
@@ -212,7 +216,9 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
       for (int i = 1; i < W; ++i) dsts[n++] = recv_row((p.rank + i) % W, p.rank, r);
       push_row<VPT>(partial + r * (H / 8), dsts, n, nv);
     }
+    if (stamp) stamp[1] = now_ns();
     if (!barrier(p, 0, epoch, &bail)) return;  // every peer's partial has landed here
+    if (stamp) stamp[2] = now_ns();
     for (int64_t r = blockIdx.x; r < p.T; r += nb) {
       float acc[VPT][8];
       zero_acc<VPT>(acc);
@@ -226,6 +232,7 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
       }
       finish_row<VPT>(p, r, acc, red);
     }
+    if (stamp) stamp[3] = now_ns();
     return;
   }
   // Two-shot.  Owner o holds rows [o*Tc, min(T, (o+1)*Tc)); block b handles
@@ -239,7 +246,9 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
       push_row<VPT>(partial + r * (H / 8), dsts, 1, nv);
     }
   }
+  if (stamp) stamp[1] = now_ns();
   if (!barrier(p, 0, epoch, &bail)) return;  // every chunk this rank owns has landed
+  if (stamp) stamp[2] = now_ns();
   {
     const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(p.rank + 1) * Tc);
     for (int64_t r = static_cast<int64_t>(p.rank) * Tc + blockIdx.x; r < r1; r += nb) {
@@ -278,6 +287,7 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
       finish_row<VPT>(p, r, acc, red);
     }
   }
+  if (stamp) stamp[3] = now_ns();
 }
 
 }  // namespace comm

@@ -23,6 +23,9 @@ struct ArParams {
   float eps;
   int two_shot;
   int fuse_norm;
+  // Optional phase timestamps (%globaltimer, ns) of block 0: [64 calls][4] =
+  // entry, pushes issued, first wait passed, exit; slot = epoch % 64.
+  unsigned long long* timing;
 };
 
 #ifdef __cplusplus

@@ -90,6 +90,17 @@ def main():
                 best = min(best, s.elapsed_time(e) * 1e3 / a.iters)
             return best
 
+        # phase stamps of block 0 over 32 un-graphed back-to-back calls
+        comm.timing = torch.zeros(64, 4, dtype=torch.int64, device=dev)
+        for _ in range(32):
+            ours()
+        torch.cuda.synchronize()
+        st_ = comm.timing.cpu().double()
+        comm.timing = None
+        ok = (st_[:, 3] > 0)
+        d = st_[ok]
+        phases = ((d[:, 1] - d[:, 0]).median().item() / 1e3, (d[:, 2] - d[:, 1]).median().item() / 1e3,
+                  (d[:, 3] - d[:, 2]).median().item() / 1e3)
         cp = torch.empty_like(x0)
         t_copy = timed(lambda: cp.copy_(x0), True)  # the input copy both paths pay
         t_ours = timed(ours, False) - t_copy
@@ -97,6 +108,9 @@ def main():
         t = torch.tensor([t_ours, t_nccl, err], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=st.group)
         t_ours, t_nccl, err = (float(v) for v in t)
+        ph = torch.tensor(phases, device=dev, dtype=torch.float64)
+        allph = [torch.empty_like(ph) for _ in range(W)]
+        dist.all_gather(allph, ph, group=st.group)
         nbytes = T * H * 2
         link = 2 * (W - 1) / W * nbytes
         target_us = link / (LINK_GBS * 1e3)
@@ -105,7 +119,8 @@ def main():
         rows.append({"world": W, "T": T, "H": H, "bytes": nbytes, "mode": mode, "ours_us": round(t_ours, 2),
                      "nccl_us": round(t_nccl, 2), "speedup_vs_nccl": round(t_nccl / max(t_ours, 1e-9), 2),
                      "roofline_us": round(target_us, 2), "frac_ours": round(target_us / max(t_ours, 1e-9), 3),
-                     "frac_nccl": round(target_us / max(t_nccl, 1e-9), 3), "max_abs_diff_vs_nccl": err})
+                     "frac_nccl": round(target_us / max(t_nccl, 1e-9), 3), "max_abs_diff_vs_nccl": err,
+                     "block0_phase_us_push_wait_finish": [[round(v, 2) for v in x.tolist()] for x in allph]})
     comm.check()
     if rank == 0:
         for r in rows:

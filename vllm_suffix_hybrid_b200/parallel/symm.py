@@ -58,6 +58,7 @@ class SymmComm:
         self.peer_flags = [int(x) for x in h_f.buffer_ptrs]
         self._handles = (h_r, h_g, h_f)
         self.counters = torch.zeros(MAX_BLOCKS, dtype=torch.int32, device=dev)
+        self.timing = None  # set to an int64 [64, 4] tensor to record per-call phase stamps
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
         self.blocks = min(MAX_BLOCKS, sms)
@@ -87,7 +88,7 @@ class SymmComm:
         two_shot = sent > self.one_shot_max_bytes and T >= self.world
         ops.native().allreduce_fused(x, self.peer_recv, self.peer_gather, self.peer_flags, self.counters, out,
                                      residual, weight, self.err, self.rank, T, H, self.max_tokens, eps, two_shot,
-                                     self.blocks)
+                                     self.blocks, self.timing)
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         out = torch.empty_like(x)
