@@ -34,6 +34,7 @@ from ..parallel import state as pstate
 from .config import EngineConfig, apply_env
 from .kv_cache import BlockPool, allocate_caches, blocks_for
 from .runner import Runner
+from .telemetry import Telemetry
 
 
 @dataclass
@@ -50,6 +51,9 @@ class Request:
     finished: bool = False
     arrival: float = 0.0
     slot: int = 0  # recurrent-state slot (hybrid GDN models)
+    stop_ids: frozenset = frozenset()  # generation ends after the first of these tokens
+    finish_reason: str = ""  # "length" | "stop" | "abort"
+    polled: int = 0  # output tokens already handed out by poll()
 
     @property
     def history_len(self) -> int:
@@ -118,6 +122,7 @@ class LLMEngine:
         self._ids = itertools.count()
         self.stats: List[StepStats] = []
         self.proposer = None
+        self.telemetry = Telemetry.from_env()
         self.external_proposer = None  # callable(list[Request]) -> list[list[int]] for method "external"
         k = max(self.k, 1)
         if spec.method == "hybrid":
@@ -143,13 +148,60 @@ class LLMEngine:
         return max(need, min(budget // per_block, 4 * need))
 
     # ------------------------------------------------------------------ API
-    def add_request(self, prompt, max_new_tokens: int = 128, rid: Optional[str] = None) -> str:
+    def add_request(self, prompt, max_new_tokens: int = 128, rid: Optional[str] = None,
+                    stop_token_ids=None) -> str:
         rid = rid if rid is not None else f"req-{next(self._ids)}"
         p = np.asarray(prompt, dtype=np.int64)
         if len(p) == 0 or len(p) + max_new_tokens > self.max_model_len:
             raise ValueError("prompt empty or prompt + max_new_tokens exceeds max_model_len")
-        self.waiting.append(Request(rid, p, max_new_tokens, arrival=time.time()))
+        if rid in self.finished or any(r.rid == rid for r in self.running) or any(r.rid == rid for r in self.waiting):
+            raise ValueError(f"duplicate request id {rid}")
+        self.waiting.append(Request(rid, p, max_new_tokens, arrival=time.time(),
+                                    stop_ids=frozenset(int(t) for t in (stop_token_ids or ()))))
         return rid
+
+    def abort_request(self, rid: str) -> bool:
+        """Stop a request; a running one leaves at this step boundary. False if unknown or done."""
+        for i, r in enumerate(self.waiting):
+            if r.rid == rid:
+                self.waiting.pop(i)
+                r.finished, r.finish_reason = True, "abort"
+                self.finished[rid] = r
+                return True
+        for r in self.running:
+            if r.rid == rid and not r.finished:
+                r.finished, r.finish_reason = True, "abort"
+                self._retire()
+                return True
+        return False
+
+    def poll(self, rid: str):
+        """(new output tokens since the last poll, finished, finish_reason) of a request."""
+        r = self.finished.get(rid)
+        if r is None:
+            r = next((q for q in self.running if q.rid == rid), None)
+        if r is None:
+            r = next((q for q in self.waiting if q.rid == rid), None)
+        if r is None:
+            raise KeyError(rid)
+        new = r.output[r.polled:]
+        r.polled = len(r.output)
+        return new, r.finished, r.finish_reason
+
+    def warm_start(self, sequences) -> int:
+        """Pre-fill the proposer's suffix corpus with token histories (same path as a departing request)."""
+        cache = getattr(self.proposer, "suffix_cache", None)
+        if cache is None:
+            raise RuntimeError(f"warm start needs a suffix-corpus proposer (method {self.cfg.spec.method!r})")
+        n = 0
+        for seq in sequences:
+            cache.add_sequence([int(t) for t in seq])
+            n += 1
+        return n
+
+    def proposer_stats(self) -> dict:
+        get = getattr(self.proposer, "get_stats", None)
+        return dict(get()) if get else {}
 
     def has_work(self) -> bool:
         return bool(self.waiting or self.running)
@@ -214,12 +266,20 @@ class LLMEngine:
     def _emit(self, r: Request, row: int, toks: List[int]) -> None:
         room = r.max_new_tokens - len(r.output)
         toks = toks[:room]
+        stopped = False
+        if r.stop_ids:
+            for j, t in enumerate(toks):
+                if t in r.stop_ids:
+                    toks, stopped = toks[: j + 1], True
+                    break
         n0 = r.history_len
         self.tokens[row, n0:n0 + len(toks)] = toks
         r.output.extend(toks)
         r.next_token = toks[-1] if toks else r.next_token
-        if len(r.output) >= r.max_new_tokens or r.history_len + 2 * self.k + 2 >= self.max_model_len:
-            r.finished = True
+        if stopped:
+            r.finished, r.finish_reason = True, "stop"
+        elif len(r.output) >= r.max_new_tokens or r.history_len + 2 * self.k + 2 >= self.max_model_len:
+            r.finished, r.finish_reason = True, "length"
 
     def _propose(self, batch_native: bool) -> float:
         """Replace each running request's drafts by the proposer's choice."""
@@ -286,6 +346,7 @@ class LLMEngine:
         t3 = time.perf_counter()
         st = StepStats("decode", n, emitted, accepted, (t2 - t1) * 1e3, (t3 - t2 + t1 - t0) * 1e3, prop_us)
         self.stats.append(st)
+        self.telemetry.record(self, st)
         return st
 
     def _retire(self) -> None:
