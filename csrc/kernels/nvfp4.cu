@@ -8,8 +8,8 @@
 // 2, 3, 4, 6; bit 3 is the sign.
 //
 // quantize: global = amax(W) / (6 * 448); block scale = e4m3(block_amax / 6 /
-// global); code = nearest e2m1 to w / (scale * global) (ties toward the
-// smaller magnitude).  One thread per 16-element block, vectorised I/O.
+// global); code = nearest e2m1 to w / (scale * global) (ties to the even
+// code).  One thread per 16-element block, vectorised I/O.
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -32,9 +32,10 @@ __device__ __forceinline__ uint8_t f_to_e4m3(float f) {
 
 __device__ __forceinline__ uint8_t e2m1_code(float x) {
   const float a = fabsf(x);
-  // Midpoints between consecutive magnitudes; ties go to the smaller one.
-  uint8_t c = a <= 0.25f ? 0 : a <= 0.75f ? 1 : a <= 1.25f ? 2 : a <= 1.75f ? 3 : a <= 2.5f ? 4 : a <= 3.5f ? 5 : a <= 5.f ? 6 : 7;
-  return (x < 0.f && c) ? static_cast<uint8_t>(c | 8) : c;
+  // Nearest magnitude; a value exactly between two goes to the even code
+  // (round half to even on the code grid, as the ModelOpt / vLLM quantiser).
+  uint8_t c = a <= 0.25f ? 0 : a < 0.75f ? 1 : a <= 1.25f ? 2 : a < 1.75f ? 3 : a <= 2.5f ? 4 : a < 3.5f ? 5 : a <= 5.f ? 6 : 7;
+  return x < 0.f ? static_cast<uint8_t>(c | 8) : c;  // negative values keep the sign bit (-0 included)
 }
 
 __global__ void dequant_kernel(__nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ packed,

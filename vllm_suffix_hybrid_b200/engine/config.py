@@ -26,7 +26,9 @@ class ModelConfig:
     ffn: int = 14336
     vocab: int = 128256
     rope_theta: float = 500000.0
+    rope_scaling: Optional[dict] = None  # HF rope_scaling / rope_parameters (llama3, yarn)
     norm_eps: float = 1e-5
+    norm_offset: float = 0.0  # checkpoint RMSNorm gains are stored as (gain - offset), e.g. 1 for Qwen3-Next
     max_position: int = 131072
     tie_embeddings: bool = False
     dtype: str = "bfloat16"

@@ -59,22 +59,35 @@ class Linear:
     def __init__(self, in_f: int, out_f: int, dtype, device, gen=None, std=0.02, parallel=None, sections=None):
         st = state.get()
         self.parallel = parallel if st.tp > 1 else None
-        full = init_weight((out_f, in_f), std, dtype, device, gen)
+        self.sections = sections
+        self.full_shape = (out_f, in_f)
+        self.weight = self.shard(init_weight((out_f, in_f), std, dtype, device, gen))
+        self.out_f, self.in_f = self.weight.shape
+
+    def shard(self, full: torch.Tensor) -> torch.Tensor:
+        """This rank's slice of a full [out, in] matrix (identity without TP)."""
+        st = state.get()
+        out_f, in_f = full.shape
         if self.parallel == "col":
-            secs = sections or [out_f]
+            secs = self.sections or [out_f]
             assert sum(secs) == out_f and all(s % st.tp == 0 for s in secs)
             parts, o = [], 0
             for s in secs:
                 w = s // st.tp
                 parts.append(full[o + st.tp_rank * w:o + (st.tp_rank + 1) * w])
                 o += s
-            full = torch.cat(parts, 0).contiguous()
-        elif self.parallel == "row":
+            return torch.cat(parts, 0).contiguous()
+        if self.parallel == "row":
             assert in_f % st.tp == 0
             w = in_f // st.tp
-            full = full[:, st.tp_rank * w:(st.tp_rank + 1) * w].contiguous()
-        self.weight = full
-        self.out_f, self.in_f = full.shape
+            return full[:, st.tp_rank * w:(st.tp_rank + 1) * w].contiguous()
+        return full.contiguous()
+
+    def load(self, full: torch.Tensor) -> None:
+        """Replace the weight by this rank's slice of a full [out, in] checkpoint matrix."""
+        if tuple(full.shape) != tuple(self.full_shape):
+            raise ValueError(f"checkpoint matrix {tuple(full.shape)} != expected {self.full_shape}")
+        self.weight.copy_(self.shard(full.to(self.weight.device)).to(self.weight.dtype))
 
     def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if out is None and self.parallel == "row":

@@ -63,6 +63,18 @@ class QLinear:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         return ops.linear(x, self.weight)
 
+    def load(self, full: torch.Tensor) -> None:
+        """Replace the weight by a full [out, in] matrix (re-quantised when the layer is NVFP4)."""
+        if tuple(full.shape) != (self.out_f, self.in_f):
+            raise ValueError(f"checkpoint matrix {tuple(full.shape)} != expected {(self.out_f, self.in_f)}")
+        if self.fmt == "nvfp4":
+            p, sc, g = ops.nvfp4_quantize(full.to(self.packed.device, self.dtype))
+            self.packed.copy_(p)
+            self.scales.copy_(sc)
+            self.gscale.copy_(g)
+        else:
+            self._w.copy_(full.to(self._w.device, self._w.dtype))
+
 
 class MLAttention:
     def __init__(self, cfg, dtype, device, gen, cos_sin, fmt: str):
@@ -70,7 +82,7 @@ class MLAttention:
         self.cfg = cfg
         self.H = cfg.heads
         self.nope, self.rope, self.vd, self.lora = cfg.qk_nope, cfg.qk_rope, cfg.v_head, cfg.kv_lora
-        self.scale = 1.0 / math.sqrt(self.nope + self.rope)
+        self.scale = ops.ref.yarn_softmax_mscale(cfg.rope_scaling) / math.sqrt(self.nope + self.rope)
         h = cfg.hidden
         self.q_a = QLinear(h, cfg.q_lora, dtype, device, gen, fmt) if cfg.q_lora else None
         self.q_a_norm = RMSNorm(cfg.q_lora, cfg.norm_eps, dtype, device) if cfg.q_lora else None
@@ -142,7 +154,8 @@ class DeepseekModel:
         gen.manual_seed(seed)
         self.gen = gen
         fmt = "nvfp4" if cfg.weight_format == "nvfp4" else "bf16"
-        self.cos_sin = ops.ref.rope_cos_sin(cfg.max_position, cfg.qk_rope, cfg.rope_theta, device=device)
+        self.cos_sin = ops.ref.rope_cos_sin(cfg.max_position, cfg.qk_rope, cfg.rope_theta, device=device,
+                                              scaling=cfg.rope_scaling)
         self.embed = init_weight((cfg.vocab, cfg.hidden), cfg.init_std, self.dtype, device, gen)
         self.layers = [DeepseekLayer(cfg, i, self.dtype, device, gen, self.cos_sin, fmt) for i in range(cfg.layers)]
         self.norm = RMSNorm(cfg.hidden, cfg.norm_eps, self.dtype, device)

@@ -24,7 +24,7 @@ class LlamaModel:
         gen.manual_seed(seed)
         self.gen = gen
         rot = int(cfg.head_dim * cfg.partial_rotary) // 2 * 2
-        self.cos_sin = ops.ref.rope_cos_sin(cfg.max_position, rot, cfg.rope_theta, device=device)
+        self.cos_sin = ops.ref.rope_cos_sin(cfg.max_position, rot, cfg.rope_theta, device=device, scaling=cfg.rope_scaling)
         self.embed = init_weight((cfg.vocab, cfg.hidden), cfg.init_std, self.dtype, device, gen)
         self.layers = [DecoderLayer(cfg, self.dtype, device, gen, self.cos_sin) for _ in range(cfg.layers)]
         self.norm = RMSNorm(cfg.hidden, cfg.norm_eps, self.dtype, device)

@@ -131,7 +131,7 @@ class Qwen3NextModel:
         gen.manual_seed(seed)
         self.gen = gen
         rot = int(cfg.head_dim * cfg.partial_rotary) // 2 * 2
-        self.cos_sin = ops.ref.rope_cos_sin(cfg.max_position, rot, cfg.rope_theta, device=device)
+        self.cos_sin = ops.ref.rope_cos_sin(cfg.max_position, rot, cfg.rope_theta, device=device, scaling=cfg.rope_scaling)
         self.embed = init_weight((cfg.vocab, cfg.hidden), cfg.init_std, self.dtype, device, gen)
         self.layers = [HybridLayer(cfg, cfg.layer_kind(i), self.dtype, device, gen, self.cos_sin)
                        for i in range(cfg.layers)]

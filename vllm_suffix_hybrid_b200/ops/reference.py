@@ -5,6 +5,9 @@ of the CPU-only toy configuration.  They are written for clarity, not speed.
 """
 from __future__ import annotations
 
+import math
+from typing import Optional
+
 import torch
 
 
@@ -20,12 +23,77 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
     x.copy_(rms_norm(s, w, eps))
 
 
-def rope_cos_sin(max_pos: int, rot: int, theta: float, device=None) -> torch.Tensor:
-    """[max_pos, rot] float32: cos in the first rot/2 columns, sin in the rest."""
+def rope_inv_freq(rot: int, theta: float, scaling: Optional[dict] = None):
+    """(inverse frequencies [rot/2] float64, cos/sin attention factor) for plain, llama3 or YaRN RoPE.
+
+    llama3: wavelengths above original_ctx / low_freq_factor are divided by
+    `factor`, those below original_ctx / high_freq_factor kept, a linear blend
+    in between.  YaRN (Peng et al. 2023, arXiv:2309.00071): per-dimension blend
+    of interpolated (/factor) and extrapolated frequencies with a linear ramp
+    between the correction dims of beta_fast and beta_slow rotations, and
+    cos/sin scaled by 0.1 * mscale * ln(factor) + 1 (ratio of the mscale and
+    mscale_all_dim terms when both are given).
+    """
     inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.float64) / rot))
+    kind = (scaling or {}).get("rope_type", (scaling or {}).get("type", "default"))
+    if kind in (None, "default"):
+        return inv, 1.0
+    factor = float(scaling["factor"])
+    if kind == "llama3":
+        old = float(scaling["original_max_position_embeddings"])
+        lo, hi = float(scaling["low_freq_factor"]), float(scaling["high_freq_factor"])
+        wl = 2 * math.pi / inv
+        smooth = ((old / wl) - lo) / (hi - lo)
+        out = torch.where(wl > old / lo, inv / factor, inv)
+        mid = (wl <= old / lo) & (wl >= old / hi)
+        return torch.where(mid, (1 - smooth) * inv / factor + smooth * inv, out), 1.0
+    if kind == "yarn":
+        old = float(scaling["original_max_position_embeddings"])
+        beta_fast = float(scaling.get("beta_fast") or 32)
+        beta_slow = float(scaling.get("beta_slow") or 1)
+
+        def corr_dim(rotations):
+            return (rot * math.log(old / (rotations * 2 * math.pi))) / (2 * math.log(theta))
+
+        lo, hi = math.floor(corr_dim(beta_fast)), math.ceil(corr_dim(beta_slow))
+        if scaling.get("truncate", True) is False:
+            lo, hi = corr_dim(beta_fast), corr_dim(beta_slow)
+        lo, hi = max(lo, 0), min(hi, rot - 1)
+        if lo == hi:
+            hi += 0.001
+        ramp = ((torch.arange(rot // 2, dtype=torch.float64) - lo) / (hi - lo)).clamp(0, 1)
+        extrap = 1 - ramp
+        inv = (inv / factor) * (1 - extrap) + inv * extrap
+
+        def mscale(s, m=1.0):
+            return 1.0 if s <= 1 else 0.1 * m * math.log(s) + 1.0
+
+        att = scaling.get("attention_factor")
+        if att is None:
+            m, mad = scaling.get("mscale"), scaling.get("mscale_all_dim")
+            att = mscale(factor, m) / mscale(factor, mad) if (m and mad) else mscale(factor)
+        return inv, float(att)
+    raise ValueError(f"unsupported rope scaling {kind!r}")
+
+
+def rope_cos_sin(max_pos: int, rot: int, theta: float, device=None, scaling: Optional[dict] = None) -> torch.Tensor:
+    """[max_pos, rot] float32: cos in the first rot/2 columns, sin in the rest (scaled RoPE supported)."""
+    inv, att = rope_inv_freq(rot, theta, scaling)
     t = torch.arange(max_pos, dtype=torch.float64)
     f = torch.outer(t, inv)
-    return torch.cat([f.cos(), f.sin()], dim=-1).float().to(device)
+    return (torch.cat([f.cos(), f.sin()], dim=-1) * att).float().to(device)
+
+
+def yarn_softmax_mscale(scaling: Optional[dict]) -> float:
+    """DeepSeek-style extra softmax scale factor (mscale_all_dim term squared) under YaRN."""
+    if not scaling or scaling.get("rope_type", scaling.get("type")) != "yarn":
+        return 1.0
+    mad = scaling.get("mscale_all_dim")
+    factor = float(scaling["factor"])
+    if not mad or factor <= 1:
+        return 1.0
+    m = 0.1 * float(mad) * math.log(factor) + 1.0
+    return m * m
 
 
 def apply_rope(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
@@ -164,8 +232,10 @@ def nvfp4_quantize(w: torch.Tensor, global_scale: torch.Tensor):
     x = wf / torch.where(s > 0, s, torch.ones_like(s))[..., None]
     a = x.abs()
     mids = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])
-    code = torch.bucketize(a, mids, right=False).to(torch.uint8)  # a <= mid -> lower code
-    code = torch.where((x < 0) & (code > 0), code | 8, code)
+    odd = torch.tensor([False, True, False, True, False, True, False])
+    # nearest e2m1 magnitude; exact midpoints go to the even code
+    code = ((a[..., None] > mids).sum(-1) + ((a[..., None] == mids) & odd).sum(-1)).to(torch.uint8)
+    code = torch.where(x < 0, code | 8, code)  # negative values keep the sign bit (-0 included)
     code = code.view(N, K)
     packed = (code[:, 0::2] | (code[:, 1::2] << 4)).to(torch.uint8)
     return packed.contiguous(), sc.contiguous()

@@ -3,7 +3,7 @@
   python -m vllm_suffix_hybrid_b200.serve --model llama3-8b --port 8000
   torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m vllm_suffix_hybrid_b200.serve --model llama3-8b --tp 8
 
---model is a preset (toy, llama3-8b, qwen3-next, deepseek-v3.2, kimi-k2);
+--model is a preset (toy, llama3-8b, qwen3-next, deepseek-v3.2, kimi-k2) or "auto" (config.json of --weights);
 --weights loads a safetensors checkpoint directory into it (random init
 otherwise); --tokenizer is a local Hugging Face tokenizer directory (byte
 tokenizer otherwise).  Under torchrun rank 0 serves HTTP and the other ranks
@@ -42,7 +42,14 @@ def main(argv=None):
     from .tokenizer import load_tokenizer
 
     st = state.init(tp=a.tp, backend=None if a.device == "cuda" else "gloo")
-    mcfg = PRESETS[a.model]()
+    if a.model == "auto":
+        if not a.weights:
+            raise SystemExit("--model auto needs --weights <checkpoint dir>")
+        from ..engine.loader import config_from_hf
+
+        mcfg = config_from_hf(a.weights)
+    else:
+        mcfg = PRESETS[a.model]()
     if a.shrink:
         mcfg = shrink(mcfg)
         if a.device != "cuda":
