@@ -85,7 +85,7 @@ class LLMEngine:
         spec = cfg.spec
         self.k = spec.k if spec.method != "none" else 0
         self.model, self.draft = build_model(mcfg, dev, cfg.seed, with_draft=spec.method in ("hybrid", "native"))
-        if st.tp > 1 and cfg.parallel.comm == "fused" and torch.device(dev).type == "cuda":
+        if (st.tp > 1 or st.ep > 1) and cfg.parallel.comm == "fused" and torch.device(dev).type == "cuda":
             from ..parallel import comm as pcomm
             from ..parallel.symm import SymmComm
 

@@ -31,9 +31,20 @@ class MoEBlock:
         self.gate = init_weight((self.E, cfg.hidden), cfg.init_std, dtype, device, gen)
         self.bias = (torch.zeros(self.E, dtype=torch.float32, device=device)
                      if cfg.router == "sigmoid_grouped" else None)
-        # Experts stacked: w13 [E*2F, H] (gate rows then up rows), w2 [E*H, F].
-        self.w13 = init_weight((self.E_local * 2 * self.F, cfg.hidden), cfg.init_std, dtype, device, gen)
-        self.w2 = init_weight((self.E_local * cfg.hidden, self.F), cfg.init_std, dtype, device, gen)
+        # Experts stacked: w13 [E_local*2F, H] (gate rows then up rows), w2 [E_local*H, F].  Each
+        # expert is drawn from its own seed, so the model is the same function for every EP size
+        # and a rank only materialises its own experts.
+        base = int(torch.randint(0, 2 ** 62, (1,), generator=gen, device=gen.device).item())
+        e0 = st.ep_rank * self.E_local if self.ep > 1 else 0
+        self.w13 = torch.empty(self.E_local * 2 * self.F, cfg.hidden, dtype=dtype, device=device)
+        self.w2 = torch.empty(self.E_local * cfg.hidden, self.F, dtype=dtype, device=device)
+        for j in range(self.E_local):
+            g = torch.Generator(device=device)
+            g.manual_seed(base + e0 + j)
+            self.w13[j * 2 * self.F:(j + 1) * 2 * self.F] = init_weight((2 * self.F, cfg.hidden), cfg.init_std,
+                                                                          dtype, device, g)
+            self.w2[j * cfg.hidden:(j + 1) * cfg.hidden] = init_weight((cfg.hidden, self.F), cfg.init_std, dtype,
+                                                                         device, g)
         self.shared = MLP(cfg.hidden, cfg.shared_ffn, dtype, device, gen) if cfg.shared_experts else None
         self.shared_gate = (init_weight((1, cfg.hidden), cfg.init_std, dtype, device, gen)
                             if cfg.shared_experts and cfg.arch == "qwen3_next" else None)

@@ -340,6 +340,8 @@ def moe_experts(x, ids, weights, w13, w2, E: int, F: int, out=None, accumulate: 
     if not x.is_cuda:
         res = torch.zeros(T, H, dtype=torch.float32)
         for e in ids.unique().tolist():
+            if e < 0 or e >= E:  # routed to another rank's experts
+                continue
             tok, slot = (ids == e).nonzero(as_tuple=True)
             xe = x[tok].float()
             gu = xe @ w13[e * 2 * F:(e + 1) * 2 * F].float().t()

@@ -27,9 +27,16 @@ def fused():
     return _FUSED
 
 
-def all_reduce(x: torch.Tensor) -> torch.Tensor:
+def _reduces(force: bool) -> bool:
+    """Whether this process takes part in a world-wide reduction (TP, or EP when forced)."""
     st = state.get()
-    if st.tp == 1:
+    return st.world > 1 and (st.tp > 1 or (force and st.ep > 1))
+
+
+def all_reduce(x: torch.Tensor, force: bool = False) -> torch.Tensor:
+    """Sum over the ranks under TP (and under EP with force=True, for the MoE combine)."""
+    st = state.get()
+    if not _reduces(force):
         return x
     if _FUSED is not None and _FUSED.can_all_reduce(x):
         return _FUSED.all_reduce(x)
@@ -37,9 +44,10 @@ def all_reduce(x: torch.Tensor) -> torch.Tensor:
     return x
 
 
-def partial_out(tokens: int, hidden: int, like: torch.Tensor) -> Optional[torch.Tensor]:
-    """Where a row-parallel GEMM should write its partial (the symmetric buffer when fused comm is on)."""
-    if _FUSED is not None and state.get().tp > 1 and hidden == _FUSED.hidden and tokens <= _FUSED.max_tokens:
+def partial_out(tokens: int, hidden: int, like: torch.Tensor, force: bool = False) -> Optional[torch.Tensor]:
+    """Where a row-parallel GEMM (or the EP expert sum) should write its partial: the
+    communicator's buffer when the fused comm runtime is on."""
+    if _FUSED is not None and _reduces(force) and hidden == _FUSED.hidden and tokens <= _FUSED.max_tokens:
         return _FUSED.partial(tokens)
     return None
 

@@ -55,6 +55,8 @@ def init(tp: int = 1, ep: int = 1, backend: Optional[str] = None, timeout_s: int
         cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=timeout_s))
     if tp > 1 and tp != world:
         raise ValueError(f"tensor parallel size {tp} must equal the world size {world} on one box")
+    if ep > 1 and ep != world:
+        raise ValueError(f"expert parallel size {ep} must equal the world size {world} on one box")
     _STATE = ParallelState(rank=rank, world=world, local_rank=local, tp=tp, tp_rank=rank if tp > 1 else 0, ep=ep,
                            ep_rank=rank if ep > 1 else 0, group=group, cpu_group=cpu_group)
     return _STATE
