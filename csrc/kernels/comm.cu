@@ -95,56 +95,71 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
   return r;
 }
 
-__device__ float block_sum(float v, float* red) {
+// Rows are processed by groups of kGroupThreads threads (four warps); a block
+// runs blockDim.x / kGroupThreads groups on different rows at once, so decode
+// sizes (tens to hundreds of rows) are handled in one pass instead of one row
+// per block at a time.  Thread t of a group owns the 8-element vectors
+// v = t + k * kGroupThreads (k < VPT) of its row.
+constexpr int kGroupThreads = 128;
+
+// Sum over the threads of this thread's group (shuffles + one named barrier per group).
+__device__ __forceinline__ float group_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  float t = 0.f;
-  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) t += red[i];
-  __syncthreads();
+  const int g = threadIdx.x / kGroupThreads, w = (threadIdx.x % kGroupThreads) >> 5;
+  if ((threadIdx.x & 31) == 0) red[g * 4 + w] = v;
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(kGroupThreads) : "memory");
+  const float t = red[g * 4] + red[g * 4 + 1] + red[g * 4 + 2] + red[g * 4 + 3];
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(kGroupThreads) : "memory");
   return t;
 }
 
-// residual += sum (bf16), out = rms_norm(residual) * w for one row; each
-// thread owns the 8-element vectors v = threadIdx.x + k * blockDim.x.
+// residual += sum (bf16), out = rms_norm(residual) * w for one row (or out = sum).
 template <int VPT>
 __device__ void finish_row(const ArParams& p, int64_t r, float (*acc)[8], float* red) {
   const int nv = p.H / 8;
+  const int lt = threadIdx.x % kGroupThreads;
+  if (!p.fuse_norm) {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int v = lt + k * kGroupThreads;
+      if (v < nv) reinterpret_cast<uint4*>(p.out + r * p.H)[v] = pack8(acc[k]);
+    }
+    return;
+  }
   float ss = 0.f;
   uint4 res[VPT];
+  uint4 rv[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int v = threadIdx.x + k * blockDim.x;
-    if (v >= nv) continue;
-    if (p.fuse_norm) {
-      uint4 rv = reinterpret_cast<const uint4*>(p.residual + r * p.H)[v];
-      float s[8];
-      const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rv);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(rh[i]);
-        s[2 * i] = f.x + acc[k][2 * i];
-        s[2 * i + 1] = f.y + acc[k][2 * i + 1];
-      }
-      res[k] = pack8(s);  // the residual stream is stored in bf16
-      const __nv_bfloat162* q = reinterpret_cast<const __nv_bfloat162*>(&res[k]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(q[i]);
-        ss += f.x * f.x + f.y * f.y;
-      }
-      reinterpret_cast<uint4*>(p.residual + r * p.H)[v] = res[k];
-    } else {
-      reinterpret_cast<uint4*>(p.out + r * p.H)[v] = pack8(acc[k]);
-    }
+    const int v = lt + k * kGroupThreads;
+    if (v < nv) rv[k] = reinterpret_cast<const uint4*>(p.residual + r * p.H)[v];
   }
-  if (!p.fuse_norm) return;
-  const float inv = rsqrtf(block_sum(ss, red) / p.H + p.eps);
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int v = threadIdx.x + k * blockDim.x;
+    const int v = lt + k * kGroupThreads;
+    if (v >= nv) continue;
+    float sum[8];
+    const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rv[k]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(rh[i]);
+      sum[2 * i] = f.x + acc[k][2 * i];
+      sum[2 * i + 1] = f.y + acc[k][2 * i + 1];
+    }
+    res[k] = pack8(sum);  // the residual stream is stored in bf16
+    const __nv_bfloat162* q = reinterpret_cast<const __nv_bfloat162*>(&res[k]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(q[i]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+    reinterpret_cast<uint4*>(p.residual + r * p.H)[v] = res[k];
+  }
+  const float inv = rsqrtf(group_sum(ss, red) / p.H + p.eps);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int v = lt + k * kGroupThreads;
     if (v >= nv) continue;
     const uint4 wv = reinterpret_cast<const uint4*>(p.weight)[v];
     const __nv_bfloat162* q = reinterpret_cast<const __nv_bfloat162*>(&res[k]);
@@ -169,20 +184,40 @@ __device__ __forceinline__ void zero_acc(float (*acc)[8]) {
     for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
 }
 
-// dst[v] = src[v] for this thread's vectors of one row, to every rank in `mask` but `skip`.
+// acc += the row's vectors (all loads of the row issued before any use).
 template <int VPT>
-__device__ __forceinline__ void push_row(const uint4* src, uint4* const* dst, int ndst, int nv) {
+__device__ __forceinline__ void add_row(float (*acc)[8], const uint4* src, int nv) {
+  const int lt = threadIdx.x % kGroupThreads;
+  uint4 val[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
-    const int v = threadIdx.x + k * blockDim.x;
-    if (v >= nv) continue;
-    const uint4 val = src[v];
-    for (int d = 0; d < ndst; ++d) dst[d][v] = val;
+    const int v = lt + k * kGroupThreads;
+    val[k] = v < nv ? src[v] : make_uint4(0, 0, 0, 0);
   }
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) add8(acc[k], val[k]);
+}
+
+// dst[d][v] = src[v] for this thread's vectors of one row.
+template <int VPT>
+__device__ __forceinline__ void push_row(const uint4* src, uint4* const* dst, int ndst, int nv) {
+  const int lt = threadIdx.x % kGroupThreads;
+  uint4 val[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int v = lt + k * kGroupThreads;
+    if (v < nv) val[k] = src[v];
+  }
+  for (int d = 0; d < ndst; ++d)
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int v = lt + k * kGroupThreads;
+      if (v < nv) dst[d][v] = val[k];
+    }
 }
 
 template <int VPT>
-__global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
+__global__ void __launch_bounds__(512) allreduce_kernel(ArParams p) {
   __shared__ float red[32];
   __shared__ uint32_t s_epoch;
   __shared__ volatile int bail;
@@ -197,10 +232,12 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
       (p.timing && blockIdx.x == 0 && threadIdx.x == 0) ? p.timing + 4 * (epoch % 64u) : nullptr;
   if (stamp) stamp[0] = now_ns();
   const int nv = p.H / 8;
-  const int nb = gridDim.x;
+  const int G = blockDim.x / kGroupThreads;            // row groups per block
+  const int g = threadIdx.x / kGroupThreads;
+  const int64_t slots = static_cast<int64_t>(gridDim.x) * G;  // rows in flight per pass
+  const int64_t slot0 = static_cast<int64_t>(blockIdx.x) * G + g;
   const int W = p.world;
   const size_t H = static_cast<size_t>(p.H);
-  // Receive slot of source `src` in rank `dst`'s buffer for row r.
   auto recv_row = [&](int dst, int src, int64_t r) {
     return reinterpret_cast<uint4*>(p.peer_recv[dst] + ((par * W + src) * p.max_T + r) * H);
   };
@@ -211,7 +248,7 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
   uint4* dsts[SH_COMM_MAX_WORLD];
 
   if (!p.two_shot) {
-    for (int64_t r = blockIdx.x; r < p.T; r += nb) {
+    for (int64_t r = slot0; r < p.T; r += slots) {
       int n = 0;
       for (int i = 1; i < W; ++i) dsts[n++] = recv_row((p.rank + i) % W, p.rank, r);
       push_row<VPT>(partial + r * (H / 8), dsts, n, nv);
@@ -219,29 +256,23 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
     if (stamp) stamp[1] = now_ns();
     if (!barrier(p, 0, epoch, &bail)) return;  // every peer's partial has landed here
     if (stamp) stamp[2] = now_ns();
-    for (int64_t r = blockIdx.x; r < p.T; r += nb) {
+    for (int64_t r = slot0; r < p.T; r += slots) {
       float acc[VPT][8];
       zero_acc<VPT>(acc);
-      for (int src = 0; src < W; ++src) {
-        const uint4* in = src == p.rank ? partial + r * (H / 8) : recv_row(p.rank, src, r);
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-          const int v = threadIdx.x + k * blockDim.x;
-          if (v < nv) add8(acc[k], in[v]);
-        }
-      }
+      for (int src = 0; src < W; ++src)
+        add_row<VPT>(acc, src == p.rank ? partial + r * (H / 8) : recv_row(p.rank, src, r), nv);
       finish_row<VPT>(p, r, acc, red);
     }
     if (stamp) stamp[3] = now_ns();
     return;
   }
-  // Two-shot.  Owner o holds rows [o*Tc, min(T, (o+1)*Tc)); block b handles
-  // local row indices j = b, b + nb, ... of every chunk.
+  // Two-shot.  Owner o holds rows [o*Tc, min(T, (o+1)*Tc)); slot s of every
+  // rank handles local row indices j = s, s + slots, ... of every chunk.
   const int Tc = (p.T + W - 1) / W;
   for (int i = 1; i < W; ++i) {
     const int o = (p.rank + i) % W;
     const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(o + 1) * Tc);
-    for (int64_t r = static_cast<int64_t>(o) * Tc + blockIdx.x; r < r1; r += nb) {
+    for (int64_t r = static_cast<int64_t>(o) * Tc + slot0; r < r1; r += slots) {
       dsts[0] = recv_row(o, p.rank, r);
       push_row<VPT>(partial + r * (H / 8), dsts, 1, nv);
     }
@@ -251,39 +282,32 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(ArParams p) {
   if (stamp) stamp[2] = now_ns();
   {
     const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(p.rank + 1) * Tc);
-    for (int64_t r = static_cast<int64_t>(p.rank) * Tc + blockIdx.x; r < r1; r += nb) {
+    for (int64_t r = static_cast<int64_t>(p.rank) * Tc + slot0; r < r1; r += slots) {
       float acc[VPT][8];
       zero_acc<VPT>(acc);
-      for (int src = 0; src < W; ++src) {
-        const uint4* in = src == p.rank ? partial + r * (H / 8) : recv_row(p.rank, src, r);
+      for (int src = 0; src < W; ++src)
+        add_row<VPT>(acc, src == p.rank ? partial + r * (H / 8) : recv_row(p.rank, src, r), nv);
+      const int lt = threadIdx.x % kGroupThreads;
+      uint4 packed[VPT];
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) packed[k] = pack8(acc[k]);
+      for (int i = 0; i < W; ++i) {
+        uint4* dst = gather_row((p.rank + i) % W, r);
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
-          const int v = threadIdx.x + k * blockDim.x;
-          if (v < nv) add8(acc[k], in[v]);
+          const int v = lt + k * kGroupThreads;
+          if (v < nv) dst[v] = packed[k];
         }
-      }
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        const int v = threadIdx.x + k * blockDim.x;
-        if (v >= nv) continue;
-        const uint4 packed = pack8(acc[k]);
-        for (int i = 0; i < W; ++i) gather_row((p.rank + i) % W, r)[v] = packed;
       }
     }
   }
   if (!barrier(p, 1, epoch, &bail)) return;  // every owner's sums have landed here
   for (int o = 0; o < W; ++o) {
     const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(o + 1) * Tc);
-    for (int64_t r = static_cast<int64_t>(o) * Tc + blockIdx.x; r < r1; r += nb) {
+    for (int64_t r = static_cast<int64_t>(o) * Tc + slot0; r < r1; r += slots) {
       float acc[VPT][8];
-      const uint4* g = gather_row(p.rank, r);
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
-        const int v = threadIdx.x + k * blockDim.x;
-        if (v < nv) add8(acc[k], g[v]);
-      }
+      zero_acc<VPT>(acc);
+      add_row<VPT>(acc, gather_row(p.rank, r), nv);
       finish_row<VPT>(p, r, acc, red);
     }
   }
@@ -303,16 +327,17 @@ extern "C" int sh_allreduce(const ArParams* params, int num_blocks, cudaStream_t
   if (num_blocks < 1) num_blocks = 1;
   if (num_blocks > SH_COMM_MAX_BLOCKS) num_blocks = SH_COMM_MAX_BLOCKS;
   const int nv = p.H / 8;
-  int threads = 32;
-  while (threads < nv && threads < 1024) threads <<= 1;
-  const int vpt = (nv + threads - 1) / threads;
+  const int vpt = (nv + kGroupThreads - 1) / kGroupThreads;
+  const int threads = 4 * kGroupThreads;  // four rows per block
   if (vpt == 1)
     allreduce_kernel<1><<<num_blocks, threads, 0, stream>>>(p);
   else if (vpt == 2)
     allreduce_kernel<2><<<num_blocks, threads, 0, stream>>>(p);
   else if (vpt <= 4)
     allreduce_kernel<4><<<num_blocks, threads, 0, stream>>>(p);
+  else if (vpt <= 8)
+    allreduce_kernel<8><<<num_blocks, threads, 0, stream>>>(p);
   else
-    return -3;  // H > 32768
+    return -3;  // H > 8192
   return static_cast<int>(cudaGetLastError());
 }
