@@ -187,6 +187,9 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=st.group)
     dev_ms, wall = float(t[0]), float(t[1])
+    from vllm_suffix_hybrid_b200.ops import gemm as _gemm
+
+    gemm_choices = _gemm.choice_summary()
     if rank == 0:
         value = tokens / (dev_ms / 1e3)
         e2e = tokens / wall
@@ -215,6 +218,7 @@ def main():
                     "d2h_bytes_per_step": d2h // args.steps, "api": "LLMEngine.step"},
             "gpu_launches": n_launch_step * args.steps,
             "clocks": clk,
+            "gemm_choices": gemm_choices,
             "impl": "ours",
         }
         if args.layers:

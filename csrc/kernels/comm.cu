@@ -30,6 +30,7 @@
 #include <stdint.h>
 
 #include "comm.h"
+#include "pdl.cuh"
 
 namespace shk {
 namespace comm {
@@ -218,6 +219,8 @@ __device__ __forceinline__ void push_row(const uint4* src, uint4* const* dst, in
 
 template <int VPT>
 __global__ void __launch_bounds__(512) allreduce_kernel(ArParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   __shared__ float red[32];
   __shared__ uint32_t s_epoch;
   __shared__ volatile int bail;
@@ -330,13 +333,13 @@ extern "C" int sh_allreduce(const ArParams* params, int num_blocks, cudaStream_t
   const int vpt = (nv + kGroupThreads - 1) / kGroupThreads;
   const int threads = 4 * kGroupThreads;  // four rows per block
   if (vpt == 1)
-    allreduce_kernel<1><<<num_blocks, threads, 0, stream>>>(p);
+    shk::launch(allreduce_kernel<1>, dim3(num_blocks), dim3(threads), 0, stream, p);
   else if (vpt == 2)
-    allreduce_kernel<2><<<num_blocks, threads, 0, stream>>>(p);
+    shk::launch(allreduce_kernel<2>, dim3(num_blocks), dim3(threads), 0, stream, p);
   else if (vpt <= 4)
-    allreduce_kernel<4><<<num_blocks, threads, 0, stream>>>(p);
+    shk::launch(allreduce_kernel<4>, dim3(num_blocks), dim3(threads), 0, stream, p);
   else if (vpt <= 8)
-    allreduce_kernel<8><<<num_blocks, threads, 0, stream>>>(p);
+    shk::launch(allreduce_kernel<8>, dim3(num_blocks), dim3(threads), 0, stream, p);
   else
     return -3;  // H > 8192
   return static_cast<int>(cudaGetLastError());

@@ -12,12 +12,15 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "pdl.cuh"
 
 namespace shk {
 
 template <typename T>
 __global__ void rms_norm_kernel(T* __restrict__ out, const T* __restrict__ x, const T* __restrict__ w, int hidden,
                                 int64_t x_stride, int64_t out_stride, float eps) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   __shared__ float scratch[32];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * x_stride;
@@ -35,6 +38,8 @@ __global__ void rms_norm_kernel(T* __restrict__ out, const T* __restrict__ x, co
 // bf16, hidden % 8 == 0: 16-byte vectors, residual += x, x = norm(residual) * w.
 __global__ void fused_add_rms_norm_bf16_kernel(__nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                                const __nv_bfloat16* __restrict__ w, int hidden, float eps) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   __shared__ float scratch[32];
   extern __shared__ float4 row_cache[];  // hidden bf16 of the summed row
   const int64_t row = blockIdx.x;
@@ -79,6 +84,8 @@ __global__ void fused_add_rms_norm_bf16_kernel(__nv_bfloat16* __restrict__ x, __
 template <typename T>
 __global__ void fused_add_rms_norm_kernel(T* __restrict__ x, T* __restrict__ residual, const T* __restrict__ w,
                                           int hidden, float eps) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   __shared__ float scratch[32];
   const int64_t row = blockIdx.x;
   T* xr = x + row * hidden;
@@ -103,6 +110,8 @@ __global__ void rope_kv_write_kernel(T* __restrict__ qkv, int64_t qkv_stride, co
                                      const float* __restrict__ cos_sin, T* __restrict__ k_cache,
                                      T* __restrict__ v_cache, const int64_t* __restrict__ slot_mapping, int hq, int hk,
                                      int d, int rot, int block_size) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int64_t tok = blockIdx.x;
   T* row = qkv + tok * qkv_stride;
   const int64_t pos = positions[tok];
@@ -134,6 +143,8 @@ __global__ void rope_kv_write_kernel(T* __restrict__ qkv, int64_t qkv_stride, co
 
 template <typename T>
 __global__ void silu_mul_kernel(T* __restrict__ out, const T* __restrict__ x, int f) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int64_t row = blockIdx.x;
   const T* g = x + row * 2 * f;
   const T* u = g + f;
@@ -145,6 +156,8 @@ __global__ void silu_mul_kernel(T* __restrict__ out, const T* __restrict__ x, in
 }
 
 __global__ void silu_mul_bf16_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x, int f) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int64_t row = blockIdx.x;
   const float4* g = reinterpret_cast<const float4*>(x + row * 2 * f);
   const float4* u = reinterpret_cast<const float4*>(x + row * 2 * f + f);
@@ -167,6 +180,8 @@ __global__ void silu_mul_bf16_kernel(__nv_bfloat16* __restrict__ out, const __nv
 template <typename T>
 __global__ void embedding_kernel(T* __restrict__ out, const int64_t* __restrict__ ids, const T* __restrict__ table,
                                  int hidden, int64_t vocab) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int64_t row = blockIdx.x;
   int64_t id = ids[row];
   if (id < 0 || id >= vocab) id = 0;  // out-of-range ids read row 0, never out of bounds
@@ -213,7 +228,7 @@ void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps) {
   if (rows == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   SH_DISPATCH(x.scalar_type(), {
-    rms_norm_kernel<scalar><<<rows, threads_for(std::min(hidden / 4, 1024)), 0, stream>>>(
+    shk::launch(rms_norm_kernel<scalar>, dim3(rows), dim3(threads_for(std::min(hidden / 4, 1024))), 0, stream, 
         (scalar*)out.data_ptr(), (const scalar*)x.data_ptr(), (const scalar*)w.data_ptr(), hidden, x.stride(0),
         out.stride(0), (float)eps);
   });
@@ -229,12 +244,12 @@ void fused_add_rms_norm(torch::Tensor x, torch::Tensor residual, torch::Tensor w
   auto stream = at::cuda::getCurrentCUDAStream();
   if (x.scalar_type() == at::kBFloat16 && hidden % 8 == 0) {
     const int threads = threads_for(std::min(hidden / 8, 1024));
-    fused_add_rms_norm_bf16_kernel<<<rows, threads, hidden * 2, stream>>>(
+    shk::launch(fused_add_rms_norm_bf16_kernel, dim3(rows), dim3(threads), hidden * 2, stream, 
         (__nv_bfloat16*)x.data_ptr(), (__nv_bfloat16*)residual.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), hidden,
         (float)eps);
   } else {
     SH_DISPATCH(x.scalar_type(), {
-      fused_add_rms_norm_kernel<scalar><<<rows, threads_for(std::min(hidden, 1024)), 0, stream>>>(
+      shk::launch(fused_add_rms_norm_kernel<scalar>, dim3(rows), dim3(threads_for(std::min(hidden, 1024))), 0, stream, 
           (scalar*)x.data_ptr(), (scalar*)residual.data_ptr(), (const scalar*)w.data_ptr(), hidden, (float)eps);
     });
   }
@@ -252,7 +267,7 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
   if (t == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   SH_DISPATCH(qkv.scalar_type(), {
-    rope_kv_write_kernel<scalar><<<t, 256, 0, stream>>>(
+    shk::launch(rope_kv_write_kernel<scalar>, dim3(t), dim3(256), 0, stream, 
         (scalar*)qkv.data_ptr(), qkv.stride(0), positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(),
         (scalar*)k_cache.data_ptr(), (scalar*)v_cache.data_ptr(), slot_mapping.data_ptr<int64_t>(), hq, hk, d, rot,
         k_cache.size(2));
@@ -268,11 +283,11 @@ void silu_mul(torch::Tensor out, torch::Tensor x) {
   if (rows == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (x.scalar_type() == at::kBFloat16 && f % 8 == 0) {
-    silu_mul_bf16_kernel<<<rows, threads_for(std::min(f / 8, 1024)), 0, stream>>>(
+    shk::launch(silu_mul_bf16_kernel, dim3(rows), dim3(threads_for(std::min(f / 8, 1024))), 0, stream, 
         (__nv_bfloat16*)out.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), f);
   } else {
     SH_DISPATCH(x.scalar_type(), {
-      silu_mul_kernel<scalar><<<rows, threads_for(std::min(f, 1024)), 0, stream>>>((scalar*)out.data_ptr(),
+      shk::launch(silu_mul_kernel<scalar>, dim3(rows), dim3(threads_for(std::min(f, 1024))), 0, stream, (scalar*)out.data_ptr(),
                                                                                    (const scalar*)x.data_ptr(), f);
     });
   }
@@ -286,7 +301,7 @@ void embedding(torch::Tensor out, torch::Tensor ids, torch::Tensor table) {
   const int hidden = table.size(1);
   auto stream = at::cuda::getCurrentCUDAStream();
   SH_DISPATCH(table.scalar_type(), {
-    embedding_kernel<scalar><<<rows, 128, 0, stream>>>((scalar*)out.data_ptr(), ids.data_ptr<int64_t>(),
+    shk::launch(embedding_kernel<scalar>, dim3(rows), dim3(128), 0, stream, (scalar*)out.data_ptr(), ids.data_ptr<int64_t>(),
                                                        (const scalar*)table.data_ptr(), hidden, table.size(0));
   });
   SH_CUDA_CHECK(cudaGetLastError());

@@ -23,6 +23,7 @@
 #include <stdint.h>
 
 #include "gdn.h"
+#include "pdl.cuh"
 
 namespace shk {
 namespace gdn {
@@ -48,6 +49,8 @@ __device__ float block_sum(float v, float* red) {
 // x: pre-conv activations [T, C] (row stride x_stride); y: [T, C] SiLU(conv).
 // state [slots, C, KW-1] fp32; rec_x [slots, W, C] fp32 window inputs.
 __global__ void conv_kernel(GdnConvParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= p.C) return;
@@ -92,6 +95,8 @@ __global__ void conv_kernel(GdnConvParams p) {
 
 template <int K>
 __global__ void __launch_bounds__(K) recurrent_kernel(GdnParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   // Requires K == V == blockDim.x (checked on the host).
   __shared__ float sk[K], sq[K], red[32];
   __shared__ float sg, sb;
@@ -204,7 +209,7 @@ extern "C" int sh_gdn_conv(const GdnConvParams* p, int batch, cudaStream_t strea
   if (batch <= 0) return 0;
   if (p->KW != 4) return -1;
   dim3 grid((p->C + 127) / 128, batch);
-  conv_kernel<<<grid, 128, 0, stream>>>(*p);
+  shk::launch(conv_kernel, dim3(grid), dim3(128), 0, stream, *p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -214,13 +219,13 @@ extern "C" int sh_gdn_recurrent(const GdnParams* p, int batch, cudaStream_t stre
   dim3 grid(batch, p->HV);
   switch (p->K) {
     case 32:
-      recurrent_kernel<32><<<grid, 32, 0, stream>>>(*p);
+      shk::launch(recurrent_kernel<32>, dim3(grid), dim3(32), 0, stream, *p);
       break;
     case 64:
-      recurrent_kernel<64><<<grid, 64, 0, stream>>>(*p);
+      shk::launch(recurrent_kernel<64>, dim3(grid), dim3(64), 0, stream, *p);
       break;
     case 128:
-      recurrent_kernel<128><<<grid, 128, 0, stream>>>(*p);
+      shk::launch(recurrent_kernel<128>, dim3(grid), dim3(128), 0, stream, *p);
       break;
     default:
       return -2;

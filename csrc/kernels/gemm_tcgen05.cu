@@ -31,6 +31,7 @@
 
 #include "gemm_tcgen05.h"
 #include "tcgen05_common.cuh"
+#include "pdl.cuh"
 
 namespace shk {
 namespace tc {
@@ -133,6 +134,8 @@ __global__ void __launch_bounds__(192, 1)
   fence_before();
   __syncthreads();
   fence_after();
+  shk::pdl_trigger();
+  shk::pdl_wait();  // inputs of the previous kernel are complete from here on
   const uint32_t tmem_base = *tmem_slot;
   const int total_work = g.groups ? (*g.num_groups) * g.tiles_p : g.tiles_p * g.tiles_q * g.splits;
 
@@ -375,6 +378,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   __syncthreads();
   cluster_sync();  // the peer's barriers are initialised before any remote arrive / complete_tx
   fence_after();
+  shk::pdl_trigger();
+  shk::pdl_wait();  // inputs of the previous kernel are complete from here on
   const uint32_t tmem_base = *tmem_slot;
   const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
   const int total_work = g.tiles_p * g.tiles_q * g.splits;
@@ -544,6 +549,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 // four consecutive q per thread (float4 loads) when rows_q % 4 == 0.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ out, int splits,
                                      int rows_p, int rows_q, int ldo, int trans) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int64_t n = static_cast<int64_t>(rows_p) * rows_q;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   if ((rows_q & 3) == 0) {
@@ -633,7 +640,7 @@ int launch_t(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g, 
   static bool ready[kMaxDevices] = {false};
   const int e = set_smem_once(reinterpret_cast<const void*>(k), S::TOTAL, ready);
   if (e) return e;
-  k<<<grid, 192, S::TOTAL, st>>>(mp, mq, g);
+  shk::launch(k, dim3(grid), dim3(192), S::TOTAL, st, mp, mq, g);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -653,7 +660,7 @@ int launch_pair_t(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams
   static bool ready[kMaxDevices] = {false};
   const int e = set_smem_once(reinterpret_cast<const void*>(k), S::TOTAL, ready);
   if (e) return e;
-  k<<<grid, 192, S::TOTAL, st>>>(mp, mq, g);
+  shk::launch(k, dim3(grid), dim3(192), S::TOTAL, st, mp, mq, g);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -738,7 +745,7 @@ extern "C" int sh_gemm_bf16_tcgen05(const void* P, int rows_p, int64_t ldp, cons
     int blocks = static_cast<int>((n / 4 + 255) / 256);
     if (blocks > 8 * num_sms) blocks = 8 * num_sms;
     if (blocks < 1) blocks = 1;
-    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, static_cast<__nv_bfloat16*>(out), splits, rows_p, rows_q,
+    shk::launch(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream, ws, static_cast<__nv_bfloat16*>(out), splits, rows_p, rows_q,
                                                       static_cast<int>(ldo), trans);
     r = static_cast<int>(cudaGetLastError());
     if (r) return 4000 + r;
@@ -832,7 +839,7 @@ extern "C" int sh_gemm_bf16_pair(const void* P, int rows_p, int64_t ldp, const v
     int blocks = static_cast<int>((n / 4 + 255) / 256);
     if (blocks > 8 * num_sms) blocks = 8 * num_sms;
     if (blocks < 1) blocks = 1;
-    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, static_cast<__nv_bfloat16*>(out), splits, rows_p, rows_q,
+    shk::launch(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream, ws, static_cast<__nv_bfloat16*>(out), splits, rows_p, rows_q,
                                                       static_cast<int>(ldo), trans);
     r = static_cast<int>(cudaGetLastError());
     if (r) return 4000 + r;

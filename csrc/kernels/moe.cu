@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include "moe.h"
+#include "pdl.cuh"
 
 namespace shk {
 namespace moe {
@@ -61,6 +62,8 @@ __device__ int block_argmax(const float* s, int E, float* rv, int* ri) {
 }
 
 __global__ void route_softmax_kernel(RouteParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   extern __shared__ float s[];
   __shared__ float rv[32];
   __shared__ int ri[32];
@@ -111,6 +114,8 @@ __global__ void route_softmax_kernel(RouteParams p) {
 }
 
 __global__ void route_sigmoid_grouped_kernel(RouteParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   extern __shared__ float s[];  // [E] scores, [E] biased
   float* sb = s + p.E;
   __shared__ float rv[32];
@@ -179,6 +184,8 @@ __global__ void route_sigmoid_grouped_kernel(RouteParams p) {
 
 // Single CTA: counting sort by expert + tile list.
 __global__ void align_kernel(AlignParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   extern __shared__ int cnt[];  // [E] counts, then [E+1] offsets, [E] tile offsets
   int* off = cnt + p.E;
   int* toff = off + p.E + 1;
@@ -223,6 +230,8 @@ __global__ void align_kernel(AlignParams p) {
 
 __global__ void gather_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
                               const int32_t* __restrict__ sorted_token, const int* __restrict__ total, int H) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int row = blockIdx.x;
   if (row >= *total) return;
   const int t = sorted_token[row];
@@ -235,6 +244,8 @@ __global__ void gather_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat
 __global__ void combine_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ y,
                                const int32_t* __restrict__ sorted_pos, const float* __restrict__ w, int k, int H,
                                int accumulate) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int64_t t = blockIdx.x;
   for (int i = threadIdx.x; i < H / 2; i += blockDim.x) {
     float2 acc = accumulate ? __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(out + t * H)[i])
@@ -262,9 +273,9 @@ extern "C" int sh_moe_route(const RouteParams* p, cudaStream_t stream) {
   const int threads = p->E >= 512 ? 512 : (p->E >= 256 ? 256 : 128);
   if (p->sigmoid_grouped) {
     if (p->n_groups < 1 || p->E % p->n_groups || p->n_groups > 64) return -2;
-    route_sigmoid_grouped_kernel<<<p->T, threads, 2 * p->E * sizeof(float), stream>>>(*p);
+    shk::launch(route_sigmoid_grouped_kernel, dim3(p->T), dim3(threads), 2 * p->E * sizeof(float), stream, *p);
   } else {
-    route_softmax_kernel<<<p->T, threads, p->E * sizeof(float), stream>>>(*p);
+    shk::launch(route_softmax_kernel, dim3(p->T), dim3(threads), p->E * sizeof(float), stream, *p);
   }
   return static_cast<int>(cudaGetLastError());
 }
@@ -277,7 +288,7 @@ extern "C" int sh_moe_align(const AlignParams* p, cudaStream_t stream) {
     const cudaError_t e = cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return static_cast<int>(e);
   }
-  align_kernel<<<1, 1024, smem, stream>>>(*p);
+  shk::launch(align_kernel, dim3(1), dim3(1024), smem, stream, *p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -285,7 +296,7 @@ extern "C" int sh_moe_gather(__nv_bfloat16* out, const __nv_bfloat16* x, const i
                              const int* total, int max_rows, int H, cudaStream_t stream) {
   if (max_rows <= 0) return 0;
   if (H % 8) return -1;
-  gather_kernel<<<max_rows, 128, 0, stream>>>(out, x, sorted_token, total, H);
+  shk::launch(gather_kernel, dim3(max_rows), dim3(128), 0, stream, out, x, sorted_token, total, H);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -293,6 +304,6 @@ extern "C" int sh_moe_combine(__nv_bfloat16* out, const __nv_bfloat16* y, const 
                               int T, int k, int H, int accumulate, cudaStream_t stream) {
   if (T <= 0) return 0;
   if (H % 2) return -1;
-  combine_kernel<<<T, 256, 0, stream>>>(out, y, sorted_pos, w, k, H, accumulate);
+  shk::launch(combine_kernel, dim3(T), dim3(256), 0, stream, out, y, sorted_pos, w, k, H, accumulate);
   return static_cast<int>(cudaGetLastError());
 }

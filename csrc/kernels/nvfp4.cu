@@ -14,6 +14,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include "pdl.cuh"
 
 namespace shk {
 namespace fp4 {
@@ -40,6 +41,8 @@ __device__ __forceinline__ uint8_t e2m1_code(float x) {
 
 __global__ void dequant_kernel(__nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ packed,
                                const uint8_t* __restrict__ scales, const float* __restrict__ global, int64_t N, int K) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int64_t blocks_per_row = K / 16;
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= N * blocks_per_row) return;
@@ -63,6 +66,8 @@ __global__ void dequant_kernel(__nv_bfloat16* __restrict__ out, const uint8_t* _
 
 __global__ void quant_kernel(uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
                              const __nv_bfloat16* __restrict__ w, const float* __restrict__ global, int64_t N, int K) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int64_t blocks_per_row = K / 16;
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= N * blocks_per_row) return;
@@ -98,7 +103,7 @@ extern "C" int sh_nvfp4_dequant(__nv_bfloat16* out, const uint8_t* packed, const
   if (K % 16) return -1;
   const int64_t n = N * (K / 16);
   if (n == 0) return 0;
-  shk::fp4::dequant_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(out, packed, scales, global, N,
+  shk::launch(shk::fp4::dequant_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream, out, packed, scales, global, N,
                                                                                          K);
   return static_cast<int>(cudaGetLastError());
 }
@@ -108,6 +113,6 @@ extern "C" int sh_nvfp4_quant(uint8_t* packed, uint8_t* scales, const __nv_bfloa
   if (K % 16) return -1;
   const int64_t n = N * (K / 16);
   if (n == 0) return 0;
-  shk::fp4::quant_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(packed, scales, w, global, N, K);
+  shk::launch(shk::fp4::quant_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream, packed, scales, w, global, N, K);
   return static_cast<int>(cudaGetLastError());
 }

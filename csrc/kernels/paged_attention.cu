@@ -24,6 +24,7 @@
 #include <mutex>
 
 #include "paged_attention.h"
+#include "pdl.cuh"
 
 namespace shk {
 namespace attn {
@@ -175,6 +176,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  shk::pdl_trigger();
+  shk::pdl_wait();  // inputs of the previous kernel are complete from here on
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -419,6 +422,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 template <int D>
 __global__ void attn_merge_kernel(__nv_bfloat16* __restrict__ out, int64_t out_stride, const float* __restrict__ part_o,
                                   const float* __restrict__ part_ml, int64_t rows, int hq, int nsplit) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= rows) return;
@@ -498,7 +503,7 @@ int launch_ks(const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& p,
   }
   const int units = ntiles * p.hk * p.nsplit;
   const int grid = units < num_sms ? units : num_sms;
-  k<<<grid, THREADS, smem, st>>>(mk, mv, p, ntiles);
+  shk::launch(k, dim3(grid), dim3(THREADS), smem, st, mk, mv, p, ntiles);
   e = cudaGetLastError();
   return e == cudaSuccess ? 0 : 400 + static_cast<int>(e);
 }
@@ -522,7 +527,7 @@ int launch(const AttnParams& p, int ntiles, int cache_rows, int max_rows, cudaSt
   if (p.nsplit > 1) {
     const int64_t rows = p.num_tokens * p.hq;
     const int64_t threads = rows * 32;
-    attn_merge_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(
+    shk::launch(attn_merge_kernel<D>, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, st, 
         p.out, p.out_stride, p.part_o, p.part_ml, rows, p.hq, p.nsplit);
     e = cudaGetLastError();
     if (e != cudaSuccess) return 500 + static_cast<int>(e);

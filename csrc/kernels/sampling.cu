@@ -16,12 +16,15 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "pdl.cuh"
 
 namespace shk {
 
 template <typename T, int VEC>
 __global__ void argmax_rows_kernel(int64_t* __restrict__ out, const T* __restrict__ logits, int64_t vocab,
                                    int64_t stride) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const T* row = logits + (int64_t)blockIdx.x * stride;
   float best = -INFINITY;
   int64_t idx = 0x7fffffffffffffffll;
@@ -84,6 +87,8 @@ __global__ void argmax_rows_kernel(int64_t* __restrict__ out, const T* __restric
 __global__ void spec_verify_kernel(const int64_t* __restrict__ draft, const int64_t* __restrict__ target,
                                    int64_t* __restrict__ seq_lens, int64_t* __restrict__ out_tokens,
                                    int32_t* __restrict__ accept, int64_t* __restrict__ next_token, int batch, int k) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
   const int64_t* d = draft + (int64_t)b * k;
@@ -113,10 +118,10 @@ void argmax_rows(torch::Tensor out, torch::Tensor logits) {
                        (logits.stride(0) * logits.element_size()) % 16 == 0;
   TORCH_CHECK(aligned, "argmax_rows: logits rows must start on 16-byte boundaries");
   if (logits.scalar_type() == at::kBFloat16) {
-    argmax_rows_kernel<__nv_bfloat16, 8><<<rows, 512, 0, stream>>>(
+    shk::launch(argmax_rows_kernel<__nv_bfloat16, 8>, dim3(rows), dim3(512), 0, stream, 
         out.data_ptr<int64_t>(), (const __nv_bfloat16*)logits.data_ptr(), vocab, logits.stride(0));
   } else if (logits.scalar_type() == at::kFloat) {
-    argmax_rows_kernel<float, 4><<<rows, 512, 0, stream>>>(out.data_ptr<int64_t>(), logits.data_ptr<float>(), vocab,
+    shk::launch(argmax_rows_kernel<float, 4>, dim3(rows), dim3(512), 0, stream, out.data_ptr<int64_t>(), logits.data_ptr<float>(), vocab,
                                                            logits.stride(0));
   } else {
     TORCH_CHECK(false, "argmax_rows: bf16 or f32 logits");
@@ -133,7 +138,7 @@ void spec_verify(torch::Tensor draft, torch::Tensor target, torch::Tensor seq_le
   TORCH_CHECK(target.size(0) == batch && target.size(1) == k + 1, "target must be [B, k+1]");
   if (batch == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  spec_verify_kernel<<<(batch + 127) / 128, 128, 0, stream>>>(
+  shk::launch(spec_verify_kernel, dim3((batch + 127) / 128), dim3(128), 0, stream, 
       draft.data_ptr<int64_t>(), target.data_ptr<int64_t>(), seq_lens.data_ptr<int64_t>(),
       out_tokens.data_ptr<int64_t>(), accept.data_ptr<int32_t>(), next_token.data_ptr<int64_t>(), batch, k);
   SH_CUDA_CHECK(cudaGetLastError());

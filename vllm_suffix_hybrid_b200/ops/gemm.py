@@ -14,7 +14,10 @@ the candidate configurations are timed on the device with a cold L2 and the
 fastest is kept for the process (SH_GEMM_TUNE=0 uses the static heuristic;
 SH_GEMM_TUNE_FILE=path loads and saves the choices as JSON, which pins them
 across runs).  Calls during CUDA-graph capture never tune: they use the
-recorded choice or the heuristic.
+recorded choice or the heuristic.  For these plain (unfused) linears cuBLAS is
+one more candidate (configuration "lib"; SH_GEMM_LIB=0 leaves it out); the
+fused GEMMs -- grouped MoE experts and the NVFP4 paths -- always run this
+framework's kernels.
 
 Batch-invariant mode (SH_BATCH_INVARIANT=1): the split-K factor -- the only
 choice that changes a row's fp32 summation order -- becomes a function of
@@ -76,9 +79,12 @@ def invariant_splits(N: int, K: int) -> int:
     return heuristic(64, N, K)[3]
 
 
+LIB = (False, False, 0, 0)  # configuration tag of the cuBLAS candidate
+
+
 def candidates(M: int, N: int, K: int, splits_only: Optional[int] = None):
     kb = max(K // 64, 1)
-    out = []
+    out = [LIB] if os.environ.get("SH_GEMM_LIB", "1") != "0" and splits_only is None else []
     for pair in (False, True):
         for swap in (False, True):
             for bn in ((128, 192, 256) if pair else (64, 128, 256)):
@@ -136,22 +142,30 @@ def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor,
     cands = candidates(M, N, K, splits_only)
     times = []
     for cfg in cands:
-        pair, swap, bn, splits = cfg
-        ws = workspace(dev, splits * M * N) if splits > 1 else None
-        lib.gemm_bf16(y, x2, w, swap, bn, splits, ws, None, pair)  # first launch: no timing
+        run = _runner(cfg, x2, w, y)
+        run()  # first launch: no timing
         t = float("inf")
         for _ in range(2):
             flush.zero_()  # cold L2, and keeps the GPU busy while the timed launch is enqueued
             torch.cuda._sleep(50_000)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
-            lib.gemm_bf16(y, x2, w, swap, bn, splits, ws, None, pair)
+            run()
             e.record()
             e.synchronize()
             t = min(t, s.elapsed_time(e))
         times.append(t)
     times = _agree(times)
     return cands[min(range(len(cands)), key=times.__getitem__)]
+
+
+def _runner(cfg, x2, w, y):
+    pair, swap, bn, splits = cfg
+    if bn == 0:
+        return lambda: torch.matmul(x2, w.t(), out=y)
+    M, N = x2.shape[0], w.shape[0]
+    ws = workspace(x2.device, splits * M * N) if splits > 1 else None
+    return lambda: native().gemm_bf16(y, x2, w, swap, bn, splits, ws, None, pair)
 
 
 def _agree(times):
@@ -196,6 +210,14 @@ def plan(M: int, N: int, K: int, x2: Optional[torch.Tensor] = None, w: Optional[
     return got
 
 
+def choice_summary() -> dict:
+    """How many tuned shapes run which kernel family (for benchmark reports)."""
+    out = {"tcgen05_one_cta": 0, "tcgen05_pair": 0, "cublas": 0}
+    for cfg in _CHOICE.values():
+        out["cublas" if cfg[2] == 0 else ("tcgen05_pair" if cfg[0] else "tcgen05_one_cta")] += 1
+    return out
+
+
 def workspace(device: torch.device, numel: int) -> torch.Tensor:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     ws = _WS.get(idx)
@@ -219,7 +241,6 @@ def tcgen05_linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor]
     y = out.view(M, N) if out is not None else torch.empty(M, N, dtype=x.dtype, device=x.device)
     if M == 0:
         return y.view(*lead, N)
-    pair, swap, bn, splits = plan(M, N, K, x2, w, y)
-    ws = workspace(x.device, splits * M * N) if splits > 1 else None
-    native().gemm_bf16(y, x2, w, swap, bn, splits, ws, None, pair)
+    cfg = plan(M, N, K, x2, w, y)
+    _runner(cfg, x2, w, y)()
     return y.view(*lead, N)
