@@ -149,6 +149,85 @@ void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std:
   TORCH_CHECK(r == 0, "sh_allreduce failed with code ", r);
 }
 
+// Row-parallel GEMM y = x w^T whose epilogue pushes output rows to their owner
+// ranks' receive slots (reduce-scatter inside the GEMM), see GemmParams::push.
+void gemm_bf16_push(torch::Tensor x, torch::Tensor w, bool swap, int64_t bn, std::vector<int64_t> peer_recv,
+                    std::vector<int64_t> peer_cnt, torch::Tensor counters, int64_t rank, int64_t push_rows,
+                    int64_t max_T, c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+              "gemm_bf16_push: bf16 CUDA tensors");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1, "gemm_bf16_push: 2-D row-major");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && M <= max_T, "gemm_bf16_push: shapes");
+  const int world = static_cast<int>(peer_recv.size());
+  TORCH_CHECK(world >= 1 && world <= 8 && peer_cnt.size() == peer_recv.size(), "gemm_bf16_push: peer lists");
+  TORCH_CHECK(counters.scalar_type() == at::kInt, "gemm_bf16_push: counters");
+  static int num_sms = 0;
+  if (!num_sms) num_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  GemmParams g{};
+  for (int i = 0; i < world; ++i) {
+    g.push_recv[i] = reinterpret_cast<__nv_bfloat16*>(peer_recv[i]);
+    g.push_cnt[i] = reinterpret_cast<uint32_t*>(peer_cnt[i]);
+  }
+  g.push_epoch = reinterpret_cast<const uint32_t*>(counters.data_ptr<int>());
+  g.push_rank = static_cast<int>(rank);
+  g.push_world = world;
+  g.push_rows = static_cast<int>(push_rows);
+  g.push_max_T = static_cast<int>(max_T);
+  g.push_n = static_cast<int>(N);
+  int* errp = err.has_value() ? err->data_ptr<int>() : nullptr;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int r;
+  if (swap)
+    r = sh_gemm_bf16_push(w.data_ptr(), N, w.stride(0), x.data_ptr(), M, x.stride(0), K, 1, bn, &g, errp, num_sms,
+                          stream);
+  else
+    r = sh_gemm_bf16_push(x.data_ptr(), M, x.stride(0), w.data_ptr(), N, w.stride(0), K, 0, bn, &g, errp, num_sms,
+                          stream);
+  TORCH_CHECK(r == 0, "sh_gemm_bf16_push failed with code ", r);
+}
+
+void rs_norm_ag(int64_t recv, std::vector<int64_t> peer_gather, std::vector<int64_t> peer_gather_res,
+                std::vector<int64_t> peer_flags, int64_t rs_cnt, torch::Tensor targets, torch::Tensor counters,
+                torch::Tensor residual, torch::Tensor out, torch::Tensor weight, torch::Tensor err, int64_t rank,
+                int64_t T, int64_t H, int64_t max_T, int64_t Tc, int64_t expected, double eps, bool gather_res,
+                int64_t num_blocks, c10::optional<torch::Tensor> timing) {
+  const int world = static_cast<int>(peer_gather.size());
+  TORCH_CHECK(world >= 1 && world <= SH_COMM_MAX_WORLD && peer_flags.size() == peer_gather.size() &&
+                  peer_gather_res.size() == peer_gather.size(), "rs_norm_ag: peer lists");
+  TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && residual.is_contiguous() && residual.numel() >= T * H &&
+                  out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() >= T * H &&
+                  weight.scalar_type() == at::kBFloat16 && weight.numel() == H, "rs_norm_ag: tensors");
+  TORCH_CHECK(targets.scalar_type() == at::kInt && targets.numel() >= 2 * SH_COMM_MAX_BLOCKS &&
+                  counters.scalar_type() == at::kInt && counters.numel() >= SH_COMM_MAX_BLOCKS, "rs_norm_ag: state");
+  RsParams p{};
+  p.recv = reinterpret_cast<const __nv_bfloat16*>(recv);
+  for (int i = 0; i < world; ++i) {
+    p.peer_gather[i] = reinterpret_cast<__nv_bfloat16*>(peer_gather[i]);
+    p.peer_gather_res[i] = reinterpret_cast<__nv_bfloat16*>(peer_gather_res[i]);
+    p.peer_flags[i] = reinterpret_cast<uint32_t*>(peer_flags[i]);
+  }
+  p.rs_cnt = reinterpret_cast<uint32_t*>(rs_cnt);
+  p.targets = reinterpret_cast<uint32_t*>(targets.data_ptr<int>());
+  p.counters = reinterpret_cast<uint32_t*>(counters.data_ptr<int>());
+  p.residual = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.weight = reinterpret_cast<const __nv_bfloat16*>(weight.data_ptr());
+  p.err = err.data_ptr<int>();
+  p.rank = static_cast<int>(rank);
+  p.world = world;
+  p.T = static_cast<int>(T);
+  p.H = static_cast<int>(H);
+  p.max_T = static_cast<int>(max_T);
+  p.Tc = static_cast<int>(Tc);
+  p.expected = static_cast<uint32_t>(expected);
+  p.eps = static_cast<float>(eps);
+  p.gather_res = gather_res ? 1 : 0;
+  if (timing.has_value()) p.timing = reinterpret_cast<unsigned long long*>(timing->data_ptr<int64_t>());
+  const int r = sh_rs_norm_ag(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_rs_norm_ag failed with code ", r);
+}
+
 template <typename T>
 static T* ptr(const torch::Tensor& t) {
   return reinterpret_cast<T*>(t.data_ptr());
@@ -323,6 +402,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("peer_flags"), py::arg("counters"), py::arg("out"), py::arg("residual"), py::arg("weight"),
         py::arg("err"), py::arg("rank"), py::arg("T"), py::arg("H"), py::arg("max_T"), py::arg("eps"),
         py::arg("two_shot"), py::arg("num_blocks"), py::arg("timing") = py::none());
+  m.def("gemm_bf16_push", &gemm_bf16_push);
+  m.def("rs_norm_ag", &rs_norm_ag, py::arg("recv"), py::arg("peer_gather"), py::arg("peer_gather_res"),
+        py::arg("peer_flags"), py::arg("rs_cnt"), py::arg("targets"), py::arg("counters"), py::arg("residual"),
+        py::arg("out"), py::arg("weight"), py::arg("err"), py::arg("rank"), py::arg("T"), py::arg("H"),
+        py::arg("max_T"), py::arg("Tc"), py::arg("expected"), py::arg("eps"), py::arg("gather_res"),
+        py::arg("num_blocks"), py::arg("timing") = py::none());
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("moe_route", &moe_route);

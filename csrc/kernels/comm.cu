@@ -52,30 +52,35 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
 }
 __device__ __forceinline__ uint32_t* flag_slot(uint32_t* pad, int phase, int block, int src) {
   return pad + (static_cast<size_t>(phase) * SH_COMM_MAX_BLOCKS + block) * SH_COMM_MAX_WORLD + src;
-  static_assert(SH_COMM_PHASES == 2, "flag layout");
+  static_assert(SH_COMM_PHASES == 3, "flag layout");
 }
 
 // Cross-rank barrier between same-index blocks. Returns false on timeout.
-__device__ bool barrier(const ArParams& p, int phase, uint32_t epoch, volatile int* bail) {
+__device__ bool barrier_flags(uint32_t* const* peer_flags, int world, int rank, int* err, int phase, uint32_t epoch,
+                              volatile int* bail) {
   __syncthreads();
-  if (threadIdx.x < p.world) {
+  if (threadIdx.x < world) {
     // st.release orders every store the block made before the bar.sync above
     // (cumulativity) ahead of the flag, at system scope.
-    st_release(flag_slot(p.peer_flags[threadIdx.x], phase, blockIdx.x, p.rank), epoch);
+    st_release(flag_slot(peer_flags[threadIdx.x], phase, blockIdx.x, rank), epoch);
   }
-  if (threadIdx.x < p.world) {
-    const uint32_t* f = flag_slot(p.peer_flags[p.rank], phase, blockIdx.x, threadIdx.x);
+  if (threadIdx.x < world) {
+    const uint32_t* f = flag_slot(peer_flags[rank], phase, blockIdx.x, threadIdx.x);
     const uint64_t t0 = now_ns();
     while (static_cast<int32_t>(ld_acquire(f) - epoch) < 0) {
       if (*bail || now_ns() - t0 > kTimeoutNs) {
         *bail = 1;
-        if (p.err) atomicCAS(p.err, 0, 100 + phase);
+        if (err) atomicCAS(err, 0, 100 + phase);
         break;
       }
     }
   }
   __syncthreads();
   return *bail == 0;
+}
+
+__device__ __forceinline__ bool barrier(const ArParams& p, int phase, uint32_t epoch, volatile int* bail) {
+  return barrier_flags(p.peer_flags, p.world, p.rank, p.err, phase, epoch, bail);
 }
 
 __device__ __forceinline__ void add8(float* acc, uint4 v) {
@@ -317,6 +322,142 @@ __global__ void __launch_bounds__(512) allreduce_kernel(ArParams p) {
   if (stamp) stamp[3] = now_ns();
 }
 
+
+template <int VPT>
+__global__ void __launch_bounds__(512) rs_norm_ag_kernel(RsParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  __shared__ float red[32];
+  __shared__ uint32_t s_epoch, s_target;
+  __shared__ volatile int bail;
+  if (threadIdx.x == 0) {
+    s_epoch = ++p.counters[blockIdx.x];
+    const uint32_t par = s_epoch & 1u;
+    s_target = p.targets[2 * blockIdx.x + par] + p.expected;
+    p.targets[2 * blockIdx.x + par] = s_target;
+    bail = 0;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const size_t par = epoch & 1u;
+  unsigned long long* stamp =
+      (p.timing && blockIdx.x == 0 && threadIdx.x == 0) ? p.timing + 4 * (epoch % 64u) : nullptr;
+  if (stamp) stamp[0] = now_ns();
+  if (threadIdx.x == 0) {  // every rank's pushed rows for this rank have landed
+    const uint32_t* cnt = p.rs_cnt + par;
+    const uint64_t t0 = now_ns();
+    while (static_cast<int32_t>(ld_acquire(cnt) - s_target) < 0) {
+      if (now_ns() - t0 > kTimeoutNs) {
+        bail = 1;
+        if (p.err) atomicCAS(p.err, 0, 200);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (bail) return;
+  if (stamp) stamp[1] = now_ns();
+  const int nv = p.H / 8;
+  const int G = blockDim.x / kGroupThreads;
+  const int g = threadIdx.x / kGroupThreads;
+  const int lt = threadIdx.x % kGroupThreads;
+  const int64_t slots = static_cast<int64_t>(gridDim.x) * G;
+  const int64_t slot0 = static_cast<int64_t>(blockIdx.x) * G + g;
+  const int W = p.world;
+  const size_t H = static_cast<size_t>(p.H);
+  const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(p.rank + 1) * p.Tc);
+  for (int64_t r = static_cast<int64_t>(p.rank) * p.Tc + slot0; r < r1; r += slots) {
+    float acc[VPT][8];
+    zero_acc<VPT>(acc);
+    for (int src = 0; src < W; ++src)
+      add_row<VPT>(acc, reinterpret_cast<const uint4*>(p.recv + ((par * W + src) * p.max_T + r) * H), nv);
+    uint4 rv[VPT], res[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int v = lt + k * kGroupThreads;
+      if (v < nv) rv[k] = reinterpret_cast<const uint4*>(p.residual + r * H)[v];
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int v = lt + k * kGroupThreads;
+      if (v >= nv) continue;
+      float sum[8];
+      const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rv[k]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(rh[i]);
+        sum[2 * i] = f.x + acc[k][2 * i];
+        sum[2 * i + 1] = f.y + acc[k][2 * i + 1];
+      }
+      res[k] = pack8(sum);
+      const __nv_bfloat162* q = reinterpret_cast<const __nv_bfloat162*>(&res[k]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(q[i]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+      reinterpret_cast<uint4*>(p.residual + r * H)[v] = res[k];
+    }
+    const float inv = rsqrtf(group_sum(ss, red) / p.H + p.eps);
+    uint4 y[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int v = lt + k * kGroupThreads;
+      if (v >= nv) continue;
+      const uint4 wv = reinterpret_cast<const uint4*>(p.weight)[v];
+      const __nv_bfloat162* q = reinterpret_cast<const __nv_bfloat162*>(&res[k]);
+      const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wv);
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(q[i]);
+        const float2 w2 = __bfloat1622float2(wh[i]);
+        o[2 * i] = f.x * inv * w2.x;
+        o[2 * i + 1] = f.y * inv * w2.y;
+      }
+      y[k] = pack8(o);
+    }
+    for (int i = 0; i < W; ++i) {
+      const int d = (p.rank + i) % W;
+      uint4* dy = reinterpret_cast<uint4*>(p.peer_gather[d] + (par * p.max_T + r) * H);
+      uint4* dr = p.gather_res ? reinterpret_cast<uint4*>(p.peer_gather_res[d] + (par * p.max_T + r) * H) : nullptr;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int v = lt + k * kGroupThreads;
+        if (v >= nv) continue;
+        dy[v] = y[k];
+        if (dr) dr[v] = res[k];
+      }
+    }
+  }
+  if (stamp) stamp[2] = now_ns();
+  if (!barrier_flags(p.peer_flags, W, p.rank, p.err, 2, epoch, &bail)) return;  // every owner's rows landed
+  for (int o = 0; o < W; ++o) {
+    const int64_t e1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(o + 1) * p.Tc);
+    for (int64_t r = static_cast<int64_t>(o) * p.Tc + slot0; r < e1; r += slots) {
+      const uint4* gy = reinterpret_cast<const uint4*>(p.peer_gather[p.rank] + (par * p.max_T + r) * H);
+      const uint4* gr = reinterpret_cast<const uint4*>(p.peer_gather_res[p.rank] + (par * p.max_T + r) * H);
+      uint4 a[VPT], b[VPT];
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int v = lt + k * kGroupThreads;
+        if (v >= nv) continue;
+        a[k] = gy[v];
+        if (p.gather_res && o != p.rank) b[k] = gr[v];
+      }
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int v = lt + k * kGroupThreads;
+        if (v >= nv) continue;
+        reinterpret_cast<uint4*>(p.out + r * H)[v] = a[k];
+        if (p.gather_res && o != p.rank) reinterpret_cast<uint4*>(p.residual + r * H)[v] = b[k];
+      }
+    }
+  }
+  if (stamp) stamp[3] = now_ns();
+}
+
 }  // namespace comm
 }  // namespace shk
 
@@ -342,5 +483,29 @@ extern "C" int sh_allreduce(const ArParams* params, int num_blocks, cudaStream_t
     shk::launch(allreduce_kernel<8>, dim3(num_blocks), dim3(threads), 0, stream, p);
   else
     return -3;  // H > 8192
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int sh_rs_norm_ag(const RsParams* params, int num_blocks, cudaStream_t stream) {
+  const RsParams& p = *params;
+  if (p.world < 1 || p.world > SH_COMM_MAX_WORLD || p.H % 8 != 0 || p.T < 0 || p.T > p.max_T || p.Tc < 1) return -1;
+  if (!p.residual || !p.weight || !p.out || !p.rs_cnt || !p.targets || !p.counters) return -2;
+  if (p.gather_res && !p.peer_gather_res[p.rank]) return -4;
+  if (p.T == 0) return 0;
+  if (num_blocks < 1) num_blocks = 1;
+  if (num_blocks > SH_COMM_MAX_BLOCKS) num_blocks = SH_COMM_MAX_BLOCKS;
+  const int nv = p.H / 8;
+  const int vpt = (nv + kGroupThreads - 1) / kGroupThreads;
+  const int threads = 4 * kGroupThreads;
+  if (vpt == 1)
+    shk::launch(rs_norm_ag_kernel<1>, dim3(num_blocks), dim3(threads), 0, stream, p);
+  else if (vpt == 2)
+    shk::launch(rs_norm_ag_kernel<2>, dim3(num_blocks), dim3(threads), 0, stream, p);
+  else if (vpt <= 4)
+    shk::launch(rs_norm_ag_kernel<4>, dim3(num_blocks), dim3(threads), 0, stream, p);
+  else if (vpt <= 8)
+    shk::launch(rs_norm_ag_kernel<8>, dim3(num_blocks), dim3(threads), 0, stream, p);
+  else
+    return -3;
   return static_cast<int>(cudaGetLastError());
 }

@@ -6,7 +6,7 @@
 
 #define SH_COMM_MAX_WORLD 8
 #define SH_COMM_MAX_BLOCKS 160
-#define SH_COMM_PHASES 2
+#define SH_COMM_PHASES 3
 
 struct ArParams {
   const __nv_bfloat16* partial;                    // [T, H] this rank's partial sum (local memory)
@@ -28,6 +28,32 @@ struct ArParams {
   unsigned long long* timing;
 };
 
+// Reduce-scatter tail of a row-parallel GEMM whose epilogue pushed its output
+// rows into the owners' receive slots (GemmParams::push): the owner waits until
+// `expected` tile arrivals were counted on rs_cnt[par], sums its rows in rank
+// order, residual += sum, y = rms_norm(residual) * weight, and pushes y (and,
+// with gather_res, the residual rows) to every rank's gather buffer; after a
+// cross-rank barrier every rank copies all T rows into out (and residual).
+struct RsParams {
+  const __nv_bfloat16* recv;                          // this rank's receive buffer [2][world][max_T][H]
+  __nv_bfloat16* peer_gather[SH_COMM_MAX_WORLD];      // per rank: [2][max_T][H] normalised rows
+  __nv_bfloat16* peer_gather_res[SH_COMM_MAX_WORLD];  // per rank: [2][max_T][H] residual rows
+  uint32_t* peer_flags[SH_COMM_MAX_WORLD];            // per rank: barrier flags (phase 2)
+  uint32_t* rs_cnt;                                   // this rank's arrival counters [2]
+  uint32_t* targets;                                  // [SH_COMM_MAX_BLOCKS][2] running targets (block-local)
+  uint32_t* counters;                                 // [SH_COMM_MAX_BLOCKS] epochs (shared with sh_allreduce)
+  __nv_bfloat16* residual;                            // [T, H]: owned rows updated; all rows with gather_res
+  __nv_bfloat16* out;                                 // [T, H] normalised rows
+  const __nv_bfloat16* weight;                        // [H]
+  int* err;
+  int rank, world;
+  int T, H, max_T, Tc;
+  uint32_t expected;
+  float eps;
+  int gather_res;
+  unsigned long long* timing;  // optional [64][4] phase stamps of block 0
+};
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -36,6 +62,8 @@ extern "C" {
 // with identical T, H, mode and grid (every call of a communicator uses the
 // same grid) in the same order.  Returns 0 on launch.
 int sh_allreduce(const ArParams* p, int num_blocks, cudaStream_t stream);
+// Launch of the reduce-scatter tail (same grid as every sh_allreduce call).
+int sh_rs_norm_ag(const RsParams* p, int num_blocks, cudaStream_t stream);
 #ifdef __cplusplus
 }
 #endif

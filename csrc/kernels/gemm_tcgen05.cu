@@ -234,6 +234,7 @@ __global__ void __launch_bounds__(192, 1)
     const int row = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
+    const uint32_t push_par = g.push ? ((*g.push_epoch + 1u) & 1u) : 0u;
     for (int w = blockIdx.x; w < total_work; w += gridDim.x) {
       const Work wk = decode_work(w, g, BN);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
@@ -251,6 +252,31 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld16(tbase + c, v);
         const int q0 = wk.q_base + c;
         if (p >= wk.p_lim) {
+        } else if (g.push) {
+          // token t, output column n: non-TRANS rows are tokens, TRANS columns are tokens
+          if (!TRANS) {
+            const int o = p / g.push_rows;
+            __nv_bfloat16* dst = g.push_recv[o] +
+                                 ((static_cast<int64_t>(push_par) * g.push_world + g.push_rank) * g.push_max_T + p) *
+                                     g.push_n + q0;
+            if (q0 + 16 <= wk.q_lim && (g.push_n & 7) == 0) {
+              uint4 pk[2];
+              __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(pk);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+              reinterpret_cast<uint4*>(dst)[0] = pk[0];
+              reinterpret_cast<uint4*>(dst)[1] = pk[1];
+            } else {
+              for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i) dst[i] = __float2bfloat16(v[i]);
+            }
+          } else {
+            for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i) {
+              const int t = q0 + i;
+              const int o = t / g.push_rows;
+              g.push_recv[o][((static_cast<int64_t>(push_par) * g.push_world + g.push_rank) * g.push_max_T + t) *
+                                 g.push_n + p] = __float2bfloat16(v[i]);
+            }
+          }
         } else if (SPLIT) {
           float* dst = g.ws + (static_cast<int64_t>(wk.sp) * g.rows_p + p) * g.rows_q + q0;
           if (q0 + 16 <= wk.q_lim && (g.rows_q & 3) == 0) {
@@ -278,6 +304,24 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_before();
       mbar_arrive(&tempty[acc]);
+      if (g.push) {
+        // Each warp counts its own stores: the warp's lanes' stores precede the
+        // arrival counts (__syncwarp + release cumulativity at system scope).
+        // Non-TRANS: the warp's 32 token rows; TRANS: the tile's token columns.
+        __syncwarp();
+        if (lane == 0) {
+          int t0, t1;
+          if (!TRANS) {
+            t0 = wk.tp * BM + quad * 32;
+            t1 = min(t0 + 32, wk.p_lim);
+          } else {
+            t0 = wk.q_base;
+            t1 = min(wk.q_base + BN, wk.q_lim);
+          }
+          for (int o = t0 / g.push_rows; t0 < t1 && o <= (t1 - 1) / g.push_rows && o < g.push_world; ++o)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(g.push_cnt[o] + push_par) : "memory");
+        }
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -845,4 +889,46 @@ extern "C" int sh_gemm_bf16_pair(const void* P, int rows_p, int64_t ldp, const v
     if (r) return 4000 + r;
   }
   return 0;
+}
+
+extern "C" int sh_gemm_bf16_push(const void* P, int rows_p, int64_t ldp, const void* Q, int rows_q, int64_t ldq,
+                                 int K, int trans, int bn, const GemmParams* push, int* err, int num_sms,
+                                 cudaStream_t stream) {
+  if (K % BK != 0 || K <= 0) return -2;
+  if (rows_p <= 0 || rows_q <= 0) return 0;
+  if ((reinterpret_cast<uintptr_t>(P) & 15) || (reinterpret_cast<uintptr_t>(Q) & 15) || (ldp * 2) % 16 ||
+      (ldq * 2) % 16)
+    return -3;
+  if (bn != 64 && bn != 128 && bn != 256) return -4;
+  if (!push || push->push_world < 1 || push->push_world > 8 || push->push_rows <= 0 || !push->push_epoch) return -6;
+  CUtensorMap mp, mq;
+  int r = make_map(&mp, P, rows_p, K, ldp, BM);
+  if (r) return 1000 + r;
+  r = make_map(&mq, Q, rows_q, K, ldq, bn);
+  if (r) return 2000 + r;
+  GemmParams g = *push;
+  g.push = 1;
+  g.rows_p = rows_p;
+  g.rows_q = rows_q;
+  g.tiles_p = (rows_p + BM - 1) / BM;
+  g.tiles_q = (rows_q + bn - 1) / bn;
+  g.splits = 1;
+  g.kb_total = K / BK;
+  g.kb_per_split = K / BK;
+  g.out = nullptr;
+  g.ldo = 0;
+  g.ws = nullptr;
+  g.err = err;
+  g.p_fast = trans ? 0 : 1;
+  g.groups = nullptr;
+  g.num_groups = nullptr;
+  const int work = g.tiles_p * g.tiles_q;
+  const int grid = work < num_sms ? work : num_sms;
+  if (bn == 256)
+    r = launch_bn<256, 4>(mp, mq, g, grid, trans, false, stream);
+  else if (bn == 128)
+    r = launch_bn<128, 6>(mp, mq, g, grid, trans, false, stream);
+  else
+    r = launch_bn<64, 8>(mp, mq, g, grid, trans, false, stream);
+  return r ? 3000 + r : 0;
 }

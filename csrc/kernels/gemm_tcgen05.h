@@ -19,6 +19,18 @@ struct GemmParams {
   // p_row_offset (the expert's first weight row) and span rows_p rows.
   const int4* groups;
   const int* num_groups;
+  // Reduce-scatter push (row-parallel GEMM under tensor parallelism, push != 0):
+  // output row t (a token) is stored into rank o = t / push_rows's receive slot
+  // push_recv[o] + ((par * push_world + push_rank) * push_max_T + t) * N + n
+  // (N = the output width, par = parity of the next comm call = (*push_epoch + 1) & 1),
+  // and after each tile every epilogue warp adds 1, with release semantics, to
+  // push_cnt[o][par] of every owner o whose token rows it stored (non-TRANS:
+  // the warp's 32 rows of the tile; TRANS: the tile's token columns).
+  int push;
+  __nv_bfloat16* push_recv[8];
+  uint32_t* push_cnt[8];
+  const uint32_t* push_epoch;
+  int push_rank, push_world, push_rows, push_max_T, push_n;
 };
 
 #ifdef __cplusplus
@@ -36,6 +48,11 @@ int sh_gemm_bf16_tcgen05(const void* P, int rows_p, int64_t ldp, const void* Q, 
 int sh_gemm_bf16_pair(const void* P, int rows_p, int64_t ldp, const void* Q, int rows_q, int64_t ldq, int K,
                       void* out, int64_t ldo, int trans, int bn, int splits, float* ws, int* err, int num_sms,
                       cudaStream_t stream);
+// Row-parallel GEMM whose epilogue pushes output rows to their owner ranks (see
+// GemmParams::push*).  One CTA per 128-row P tile, splits = 1.  `push` holds the
+// push fields (other members ignored).  Returns 0 on success.
+int sh_gemm_bf16_push(const void* P, int rows_p, int64_t ldp, const void* Q, int rows_q, int64_t ldq, int K,
+                      int trans, int bn, const GemmParams* push, int* err, int num_sms, cudaStream_t stream);
 // Grouped swap-AB GEMM for MoE experts: for every device-side group entry g
 // (see GemmParams::groups), out[q, :] = sum_k Q[q, k] * P[p_row_offset + n, k]
 // for the q_rows sorted rows of the entry and n < rows_p.  P stacks the

@@ -89,8 +89,12 @@ class Linear:
             raise ValueError(f"checkpoint matrix {tuple(full.shape)} != expected {self.full_shape}")
         self.weight.copy_(self.shard(full.to(self.weight.device)).to(self.weight.dtype))
 
-    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    push = True  # row-parallel: may push its rows to the owner ranks (finished by all_reduce_add_rms_norm)
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None):
         if out is None and self.parallel == "row":
+            if self.push and comm.can_push(x.shape[0], self.out_f, x):
+                return comm.push_gemm(x, self.weight)  # reduce-scatter inside the GEMM epilogue
             out = comm.partial_out(x.shape[0], self.out_f, x)  # symmetric buffer under fused TP comm
         return ops.linear(x, self.weight, out)
 

@@ -49,7 +49,8 @@ class LlamaModel:
         for i, layer in enumerate(self.layers):
             m = layer(x, residual, meta, kv_caches[i], i == 0)
             nxt = self.layers[i + 1].input_norm if i + 1 < len(self.layers) else self.norm
-            x = comm.all_reduce_add_rms_norm(m, residual, nxt.weight, nxt.eps)
+            x = comm.all_reduce_add_rms_norm(m, residual, nxt.weight, nxt.eps,
+                                             gather_residual=i + 1 == len(self.layers))
         return x, residual
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
@@ -88,5 +89,5 @@ class DraftHead:
         residual = ops.linear(torch.cat([e, feature], dim=-1), self.fc)
         x = ops.rms_norm(residual, self.layer.input_norm.weight, self.cfg.norm_eps)
         m = self.layer(x, residual, meta, kv, True)
-        x = comm.all_reduce_add_rms_norm(m, residual, self.norm.weight, self.norm.eps)
+        x = comm.all_reduce_add_rms_norm(m, residual, self.norm.weight, self.norm.eps, gather_residual=True)
         return x, residual  # (normed, pre-norm feature for the next step)

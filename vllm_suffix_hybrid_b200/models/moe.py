@@ -46,6 +46,8 @@ class MoEBlock:
             self.w2[j * cfg.hidden:(j + 1) * cfg.hidden] = init_weight((cfg.hidden, self.F), cfg.init_std, dtype,
                                                                          device, g)
         self.shared = MLP(cfg.hidden, cfg.shared_ffn, dtype, device, gen) if cfg.shared_experts else None
+        if self.shared is not None:
+            self.shared.down.push = False  # reduced by a plain all-reduce below
         self.shared_gate = (init_weight((1, cfg.hidden), cfg.init_std, dtype, device, gen)
                             if cfg.shared_experts and cfg.arch == "qwen3_next" else None)
 

@@ -33,8 +33,22 @@ def _reduces(force: bool) -> bool:
     return st.world > 1 and (st.tp > 1 or (force and st.ep > 1))
 
 
+def can_push(tokens: int, hidden: int, like: torch.Tensor) -> bool:
+    """Whether a row-parallel GEMM of this shape runs with the reduce-scatter in its epilogue."""
+    f = _FUSED
+    return (f is not None and getattr(f, "push_enabled", False) and state.get().tp > 1 and like.is_cuda
+            and like.dtype == torch.bfloat16 and hidden == f.hidden and 0 < tokens <= f.max_tokens
+            and like.shape[-1] % 64 == 0)
+
+
+def push_gemm(x: torch.Tensor, w: torch.Tensor):
+    return _FUSED.push_gemm(x, w)
+
+
 def all_reduce(x: torch.Tensor, force: bool = False) -> torch.Tensor:
     """Sum over the ranks under TP (and under EP with force=True, for the MoE combine)."""
+    if not isinstance(x, torch.Tensor):
+        raise TypeError("a pushed row-parallel partial can only be finished by all_reduce_add_rms_norm")
     st = state.get()
     if not _reduces(force):
         return x
@@ -52,10 +66,18 @@ def partial_out(tokens: int, hidden: int, like: torch.Tensor, force: bool = Fals
     return None
 
 
-def all_reduce_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """residual += allreduce(x); returns rms_norm(residual) * w (x may be reused as the output)."""
+def all_reduce_add_rms_norm(x, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                            gather_residual: bool = False) -> torch.Tensor:
+    """residual += allreduce(x); returns rms_norm(residual) * w (x may be reused as the output).
+
+    x is a tensor partial, or the handle of a GEMM that pushed its rows to their owners: then each
+    rank updates only the residual rows it owns (sequence-parallel residual) and every rank gets all
+    normalised rows; gather_residual=True also brings every residual row up to date.
+    """
     from .. import ops
 
+    if not isinstance(x, torch.Tensor):
+        return x.comm.finish_push(x, residual, w, eps, gather_residual)
     st = state.get()
     if st.tp > 1 and _FUSED is not None and _FUSED.can_all_reduce(x):
         return _FUSED.all_reduce_add_rms_norm(x, residual, w, eps)

@@ -27,7 +27,7 @@ import torch.distributed as dist
 from . import state
 
 MAX_BLOCKS = 160
-PHASES = 2
+PHASES = 3
 MAX_WORLD = 8
 
 
@@ -46,17 +46,28 @@ class SymmComm:
         self.partial_buf = torch.empty(max_tokens, hidden, dtype=dtype, device=dev)
         self.recv_buf = symm_mem.empty(2 * self.world * max_tokens * hidden, dtype=dtype, device=dev)
         self.gather_buf = symm_mem.empty(2 * max_tokens * hidden, dtype=dtype, device=dev)
-        self.flag_buf = symm_mem.empty(PHASES * MAX_BLOCKS * MAX_WORLD, dtype=torch.int32, device=dev)
+        self.gather_res_buf = symm_mem.empty(2 * max_tokens * hidden, dtype=dtype, device=dev)
+        # flags [PHASES][MAX_BLOCKS][MAX_WORLD] then the reduce-scatter arrival counters [2]
+        self.flag_buf = symm_mem.empty(PHASES * MAX_BLOCKS * MAX_WORLD + 64, dtype=torch.int32, device=dev)
         self.flag_buf.zero_()
         torch.cuda.synchronize()
         name = self.group.group_name if hasattr(self.group, "group_name") else dist.group.WORLD.group_name
         h_r = symm_mem.rendezvous(self.recv_buf, name)
         h_g = symm_mem.rendezvous(self.gather_buf, name)
         h_f = symm_mem.rendezvous(self.flag_buf, name)
+        h_gr = symm_mem.rendezvous(self.gather_res_buf, name)
         self.peer_recv = [int(x) for x in h_r.buffer_ptrs]
         self.peer_gather = [int(x) for x in h_g.buffer_ptrs]
+        self.peer_gather_res = [int(x) for x in h_gr.buffer_ptrs]
         self.peer_flags = [int(x) for x in h_f.buffer_ptrs]
-        self._handles = (h_r, h_g, h_f)
+        cnt_off = PHASES * MAX_BLOCKS * MAX_WORLD * 4
+        self.peer_rs_cnt = [p + cnt_off for p in self.peer_flags]
+        self._handles = (h_r, h_g, h_f, h_gr)
+        self.targets = torch.zeros(2 * MAX_BLOCKS, dtype=torch.int32, device=dev)
+        # Row-parallel GEMMs push their rows straight to the owners (reduce-scatter in
+        # the GEMM epilogue) and rs_norm_ag finishes; SH_TP_PUSH=0 keeps the
+        # GEMM -> all-reduce kernel path.
+        self.push_enabled = os.environ.get("SH_TP_PUSH", "1") != "0"
         self.counters = torch.zeros(MAX_BLOCKS, dtype=torch.int32, device=dev)
         self.timing = None  # set to an int64 [64, 4] tensor to record per-call phase stamps
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -101,7 +112,57 @@ class SymmComm:
         self._launch(x, out, residual, w, eps)
         return out
 
+    # -- reduce-scatter in the GEMM epilogue -----------------------------------
+    def owner_rows(self, T: int) -> int:
+        return max(1, -(-T // self.world))
+
+    def push_expected(self, T: int, N: int, swap: bool, bn: int) -> int:
+        """Arrival counts this rank receives for one push GEMM (mirrors the epilogue's per-warp counting)."""
+        Tc = self.owner_rows(T)
+        lo, hi = self.rank * Tc, min(T, (self.rank + 1) * Tc)
+        if lo >= hi:
+            return 0
+        if swap:  # every warp of every (weight tile, token tile) counts the tile's token range
+            tiles_w = -(-N // 128)
+            n = sum(1 for t0 in range(0, T, bn) if t0 < hi and min(t0 + bn, T) > lo)
+            return self.world * tiles_w * 4 * n
+        tiles_w = -(-N // bn)  # every warp counts its own 32 token rows
+        n = sum(1 for r0 in range(0, T, 32) if r0 < hi and min(r0 + 32, T) > lo)
+        return self.world * tiles_w * n
+
+    def push_gemm(self, x: torch.Tensor, w: torch.Tensor) -> "PushedPartial":
+        """Row-parallel y = x w^T with the rows pushed to their owner ranks; finish with finish_push()."""
+        from .. import ops
+
+        T, N = x.shape[0], w.shape[0]
+        if N != self.hidden or T > self.max_tokens:
+            raise ValueError("push GEMM: output width must be the hidden size and T <= max_tokens")
+        swap = T <= 256
+        bn = next(b for b in (64, 128, 256) if b >= T) if swap else (256 if N > 8192 else 128)
+        ops.native().gemm_bf16_push(x.contiguous(), w, swap, bn, self.peer_recv, self.peer_rs_cnt, self.counters,
+                                    self.rank, self.owner_rows(T), self.max_tokens, self.err)
+        return PushedPartial(self, T, self.push_expected(T, N, swap, bn))
+
+    def finish_push(self, pp: "PushedPartial", residual: torch.Tensor, w: torch.Tensor, eps: float,
+                    gather_residual: bool = False) -> torch.Tensor:
+        from .. import ops
+
+        out = torch.empty(pp.T, self.hidden, dtype=residual.dtype, device=residual.device)
+        ops.native().rs_norm_ag(self.peer_recv[self.rank], self.peer_gather, self.peer_gather_res, self.peer_flags,
+                                self.peer_rs_cnt[self.rank], self.targets, self.counters, residual, out, w, self.err,
+                                self.rank, pp.T, self.hidden, self.max_tokens, self.owner_rows(pp.T), pp.expected,
+                                eps, gather_residual, self.blocks, self.timing)
+        return out
+
     def check(self) -> None:
         code = int(self.err.item())
         if code:
             raise RuntimeError(f"symmetric-memory collective timed out or failed (code {code}) on rank {self.rank}")
+
+
+class PushedPartial:
+    """A row-parallel GEMM output that was pushed to its owner ranks (not materialised locally)."""
+
+    def __init__(self, comm: SymmComm, T: int, expected: int):
+        self.comm, self.T, self.expected = comm, T, expected
+        self.shape = (T, comm.hidden)
