@@ -151,7 +151,7 @@ void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std:
 
 // Row-parallel GEMM y = x w^T whose epilogue pushes output rows to their owner
 // ranks' receive slots (reduce-scatter inside the GEMM), see GemmParams::push.
-void gemm_bf16_push(torch::Tensor x, torch::Tensor w, bool swap, int64_t bn, std::vector<int64_t> peer_recv,
+void gemm_bf16_push(torch::Tensor x, torch::Tensor w, bool pair, int64_t bn, std::vector<int64_t> peer_recv,
                     std::vector<int64_t> peer_cnt, torch::Tensor counters, int64_t rank, int64_t push_rows,
                     int64_t max_T, c10::optional<torch::Tensor> err) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
@@ -177,13 +177,8 @@ void gemm_bf16_push(torch::Tensor x, torch::Tensor w, bool swap, int64_t bn, std
   g.push_n = static_cast<int>(N);
   int* errp = err.has_value() ? err->data_ptr<int>() : nullptr;
   auto stream = at::cuda::getCurrentCUDAStream();
-  int r;
-  if (swap)
-    r = sh_gemm_bf16_push(w.data_ptr(), N, w.stride(0), x.data_ptr(), M, x.stride(0), K, 1, bn, &g, errp, num_sms,
-                          stream);
-  else
-    r = sh_gemm_bf16_push(x.data_ptr(), M, x.stride(0), w.data_ptr(), N, w.stride(0), K, 0, bn, &g, errp, num_sms,
-                          stream);
+  const int r = sh_gemm_bf16_push(x.data_ptr(), M, x.stride(0), w.data_ptr(), N, w.stride(0), K, 0, bn, pair ? 1 : 0,
+                                  &g, errp, num_sms, stream);
   TORCH_CHECK(r == 0, "sh_gemm_bf16_push failed with code ", r);
 }
 

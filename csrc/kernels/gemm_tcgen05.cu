@@ -47,13 +47,20 @@ __host__ __device__ constexpr int tmem_cols() {
   return (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
 }
 
-template <int BN, int STAGES>
+// Push-epilogue staging: per epilogue warp 32 rows x 64 columns of bf16, rows
+// padded to 72 elements (144 B) so the 32 lanes' row writes spread over banks.
+constexpr int PUSH_LD = 72;
+constexpr int PUSH_STAGE_BYTES = 4 * 32 * PUSH_LD * 2;
+
+template <int BN, int STAGES, bool PUSH = false>
 struct Smem {
   static constexpr int P_BYTES = BM * BK * 2;
   static constexpr int Q_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = P_BYTES + Q_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int PUSH_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = PUSH_OFF + (PUSH ? PUSH_STAGE_BYTES : 0);
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 5) * 8 + 16 + 1024;  // + alignment slack
+  static_assert(TOTAL <= 227 * 1024, "shared memory budget");
 };
 
 struct Work {
@@ -95,10 +102,10 @@ __device__ __forceinline__ Work decode_work(int w, const GemmParams& g, int bn) 
   return r;
 }
 
-template <int BN, int STAGES, bool TRANS, bool SPLIT>
+template <int BN, int STAGES, bool TRANS, bool SPLIT, bool PUSH = false>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ, GemmParams g) {
-  using S = Smem<BN, STAGES>;
+  using S = Smem<BN, STAGES, PUSH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
@@ -245,38 +252,53 @@ __global__ void __launch_bounds__(192, 1)
       fence_after();
       const int p = wk.tp * BM + row;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
+      if constexpr (PUSH) {
+        // Stage this warp's 32 rows x 64 columns in shared memory, then write
+        // 128-byte row segments (16 B per lane) to the rows' owner ranks.
+        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + S::PUSH_OFF) + (warp - 2) * 32 * PUSH_LD;
+        const int64_t slot = (static_cast<int64_t>(push_par) * g.push_world + g.push_rank) * g.push_max_T;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+        for (int c64 = 0; c64 < BN; c64 += 64) {
+#pragma unroll 1
+          for (int c = c64; c < c64 + 64; c += 16) {
+            float v[16];
+            __syncwarp();
+            tmem_ld16(tbase + c, v);
+            uint4 pk[2];
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(pk);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            uint4* d = reinterpret_cast<uint4*>(stg + lane * PUSH_LD + (c - c64));
+            d[0] = pk[0];
+            d[1] = pk[1];
+          }
+          __syncwarp();
+#pragma unroll 1
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3), seg = lane & 7;
+            const int pr = wk.tp * BM + quad * 32 + rr;
+            const int q = wk.q_base + c64 + seg * 8;
+            if (pr >= wk.p_lim || q >= wk.q_lim) continue;
+            __nv_bfloat16* dst = g.push_recv[pr / g.push_rows] + (slot + pr) * g.push_n + q;
+            const __nv_bfloat16* src = stg + rr * PUSH_LD + seg * 8;
+            if (q + 8 <= wk.q_lim && (g.push_n & 7) == 0) {
+              *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+            } else {
+              for (int i = 0; i < 8 && q + i < wk.q_lim; ++i) dst[i] = src[i];
+            }
+          }
+          __syncwarp();
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; c < (PUSH ? 0 : BN); c += 16) {
         float v[16];
         __syncwarp();
         tmem_ld16(tbase + c, v);
         const int q0 = wk.q_base + c;
         if (p >= wk.p_lim) {
-        } else if (g.push) {
-          // token t, output column n: non-TRANS rows are tokens, TRANS columns are tokens
-          if (!TRANS) {
-            const int o = p / g.push_rows;
-            __nv_bfloat16* dst = g.push_recv[o] +
-                                 ((static_cast<int64_t>(push_par) * g.push_world + g.push_rank) * g.push_max_T + p) *
-                                     g.push_n + q0;
-            if (q0 + 16 <= wk.q_lim && (g.push_n & 7) == 0) {
-              uint4 pk[2];
-              __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(pk);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-              reinterpret_cast<uint4*>(dst)[0] = pk[0];
-              reinterpret_cast<uint4*>(dst)[1] = pk[1];
-            } else {
-              for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i) dst[i] = __float2bfloat16(v[i]);
-            }
-          } else {
-            for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i) {
-              const int t = q0 + i;
-              const int o = t / g.push_rows;
-              g.push_recv[o][((static_cast<int64_t>(push_par) * g.push_world + g.push_rank) * g.push_max_T + t) *
-                                 g.push_n + p] = __float2bfloat16(v[i]);
-            }
-          }
+        } else if (PUSH) {
+          // handled below per 64-column chunk
         } else if (SPLIT) {
           float* dst = g.ws + (static_cast<int64_t>(wk.sp) * g.rows_p + p) * g.rows_q + q0;
           if (q0 + 16 <= wk.q_lim && (g.rows_q & 3) == 0) {
@@ -368,22 +390,23 @@ __host__ __device__ constexpr int pair_tmem_cols() {
   return 2 * pair_acc_cols<BN>();
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PUSH = false>
 struct PairSmem {
   static constexpr int A_BYTES = PAIR_ROWS * BK * 2;
   static constexpr int B_BYTES = (BN / 2) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int PUSH_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = PUSH_OFF + (PUSH ? PUSH_STAGE_BYTES : 0);
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 5) * 8 + 16 + 1024;
   static_assert(B_BYTES % 1024 == 0, "B half tile must keep the 1024-byte swizzle alignment");
   static_assert(TOTAL <= 227 * 1024, "shared memory budget");
 };
 
-template <int BN, int STAGES, bool TRANS, bool SPLIT>
+template <int BN, int STAGES, bool TRANS, bool SPLIT, bool PUSH = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                      GemmParams g) {
-  using S = PairSmem<BN, STAGES>;
+  using S = PairSmem<BN, STAGES, PUSH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
@@ -523,6 +546,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const int row = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
+    const uint32_t push_par = PUSH ? ((*g.push_epoch + 1u) & 1u) : 0u;
     for (int w = cid; w < total_work; w += ncl) {
       const Work wk = decode_work(w, g, BN);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
@@ -532,8 +556,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       fence_after();
       const int p = wk.tp * (2 * PAIR_ROWS) + static_cast<int>(rank) * PAIR_ROWS + row;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * pair_acc_cols<BN>();
+      const int row0 = wk.tp * (2 * PAIR_ROWS) + static_cast<int>(rank) * PAIR_ROWS + quad * 32;
+      if constexpr (PUSH) {
+        // as in the one-CTA push epilogue: stage 32 rows x 64 columns, write 128-byte row segments
+        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + S::PUSH_OFF) + (warp - 2) * 32 * PUSH_LD;
+        const int64_t slot = (static_cast<int64_t>(push_par) * g.push_world + g.push_rank) * g.push_max_T;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+        for (int c64 = 0; c64 < BN; c64 += 64) {
+#pragma unroll 1
+          for (int c = c64; c < c64 + 64; c += 16) {
+            float v[16];
+            __syncwarp();
+            tmem_ld16(tbase + c, v);
+            uint4 pk[2];
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(pk);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            uint4* d = reinterpret_cast<uint4*>(stg + lane * PUSH_LD + (c - c64));
+            d[0] = pk[0];
+            d[1] = pk[1];
+          }
+          __syncwarp();
+#pragma unroll 1
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3), seg = lane & 7;
+            const int pr = row0 + rr;
+            const int q = wk.q_base + c64 + seg * 8;
+            if (pr >= wk.p_lim || q >= wk.q_lim) continue;
+            __nv_bfloat16* dst = g.push_recv[pr / g.push_rows] + (slot + pr) * g.push_n + q;
+            const __nv_bfloat16* src = stg + rr * PUSH_LD + seg * 8;
+            if (q + 8 <= wk.q_lim && (g.push_n & 7) == 0) {
+              *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+            } else {
+              for (int i = 0; i < 8 && q + i < wk.q_lim; ++i) dst[i] = src[i];
+            }
+          }
+          __syncwarp();
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; c < (PUSH ? 0 : BN); c += 16) {
         float v[16];
         __syncwarp();
         tmem_ld16(tbase + c, v);
@@ -568,6 +630,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_to_rank(&tempty[acc], 0));
+      if constexpr (PUSH) {  // this warp's 32 token rows are stored: count them at their owners
+        if (lane == 0) {
+          const int t1 = min(row0 + 32, wk.p_lim);
+          for (int o = row0 / g.push_rows; row0 < t1 && o <= (t1 - 1) / g.push_rows && o < g.push_world; ++o)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(g.push_cnt[o] + push_par) : "memory");
+        }
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -689,6 +758,17 @@ int launch_t(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g, 
 }
 
 template <int BN, int STAGES>
+int launch_push(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g, int grid, cudaStream_t st) {
+  using S = Smem<BN, STAGES, true>;
+  auto k = gemm_kernel<BN, STAGES, false, false, true>;
+  static bool ready[kMaxDevices] = {false};
+  const int e = set_smem_once(reinterpret_cast<const void*>(k), S::TOTAL, ready);
+  if (e) return e;
+  shk::launch(k, dim3(grid), dim3(192), S::TOTAL, st, mp, mq, g);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int BN, int STAGES>
 int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g, int grid, bool trans, bool split,
               cudaStream_t st) {
   if (split) return trans ? launch_t<BN, STAGES, true, true>(mp, mq, g, grid, st)
@@ -701,6 +781,17 @@ template <int BN, int STAGES, bool TRANS, bool SPLIT>
 int launch_pair_t(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g, int grid, cudaStream_t st) {
   using S = PairSmem<BN, STAGES>;
   auto k = gemm_pair_kernel<BN, STAGES, TRANS, SPLIT>;
+  static bool ready[kMaxDevices] = {false};
+  const int e = set_smem_once(reinterpret_cast<const void*>(k), S::TOTAL, ready);
+  if (e) return e;
+  shk::launch(k, dim3(grid), dim3(192), S::TOTAL, st, mp, mq, g);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int BN, int STAGES>
+int launch_pair_push(const CUtensorMap& mp, const CUtensorMap& mq, const GemmParams& g, int grid, cudaStream_t st) {
+  using S = PairSmem<BN, STAGES, true>;
+  auto k = gemm_pair_kernel<BN, STAGES, false, false, true>;
   static bool ready[kMaxDevices] = {false};
   const int e = set_smem_once(reinterpret_cast<const void*>(k), S::TOTAL, ready);
   if (e) return e;
@@ -892,25 +983,26 @@ extern "C" int sh_gemm_bf16_pair(const void* P, int rows_p, int64_t ldp, const v
 }
 
 extern "C" int sh_gemm_bf16_push(const void* P, int rows_p, int64_t ldp, const void* Q, int rows_q, int64_t ldq,
-                                 int K, int trans, int bn, const GemmParams* push, int* err, int num_sms,
+                                 int K, int trans, int bn, int pair, const GemmParams* push, int* err, int num_sms,
                                  cudaStream_t stream) {
   if (K % BK != 0 || K <= 0) return -2;
   if (rows_p <= 0 || rows_q <= 0) return 0;
   if ((reinterpret_cast<uintptr_t>(P) & 15) || (reinterpret_cast<uintptr_t>(Q) & 15) || (ldp * 2) % 16 ||
       (ldq * 2) % 16)
     return -3;
-  if (bn != 64 && bn != 128 && bn != 256) return -4;
+  if (pair ? (bn != 128 && bn != 192 && bn != 256) : (bn != 64 && bn != 128 && bn != 256)) return -4;
   if (!push || push->push_world < 1 || push->push_world > 8 || push->push_rows <= 0 || !push->push_epoch) return -6;
+  if (trans) return -7;  // the push epilogue writes token rows: activations on the 128-row side
   CUtensorMap mp, mq;
-  int r = make_map(&mp, P, rows_p, K, ldp, BM);
+  int r = make_map(&mp, P, rows_p, K, ldp, pair ? PAIR_ROWS : BM);
   if (r) return 1000 + r;
-  r = make_map(&mq, Q, rows_q, K, ldq, bn);
+  r = make_map(&mq, Q, rows_q, K, ldq, pair ? bn / 2 : bn);
   if (r) return 2000 + r;
   GemmParams g = *push;
   g.push = 1;
   g.rows_p = rows_p;
   g.rows_q = rows_q;
-  g.tiles_p = (rows_p + BM - 1) / BM;
+  g.tiles_p = (rows_p + (pair ? 2 * PAIR_ROWS : BM) - 1) / (pair ? 2 * PAIR_ROWS : BM);
   g.tiles_q = (rows_q + bn - 1) / bn;
   g.splits = 1;
   g.kb_total = K / BK;
@@ -923,12 +1015,23 @@ extern "C" int sh_gemm_bf16_push(const void* P, int rows_p, int64_t ldp, const v
   g.groups = nullptr;
   g.num_groups = nullptr;
   const int work = g.tiles_p * g.tiles_q;
+  if (pair) {
+    const int clusters = pair_clusters(num_sms);
+    const int pgrid = 2 * (work < clusters ? work : clusters);
+    if (bn == 256)
+      r = launch_pair_push<256, 6>(mp, mq, g, pgrid, stream);
+    else if (bn == 192)
+      r = launch_pair_push<192, 6>(mp, mq, g, pgrid, stream);
+    else
+      r = launch_pair_push<128, 8>(mp, mq, g, pgrid, stream);
+    return r ? 3000 + r : 0;
+  }
   const int grid = work < num_sms ? work : num_sms;
   if (bn == 256)
-    r = launch_bn<256, 4>(mp, mq, g, grid, trans, false, stream);
+    r = launch_push<256, 4>(mp, mq, g, grid, stream);
   else if (bn == 128)
-    r = launch_bn<128, 6>(mp, mq, g, grid, trans, false, stream);
+    r = launch_push<128, 6>(mp, mq, g, grid, stream);
   else
-    r = launch_bn<64, 8>(mp, mq, g, grid, trans, false, stream);
+    r = launch_push<64, 8>(mp, mq, g, grid, stream);
   return r ? 3000 + r : 0;
 }

@@ -49,10 +49,12 @@ int sh_gemm_bf16_pair(const void* P, int rows_p, int64_t ldp, const void* Q, int
                       void* out, int64_t ldo, int trans, int bn, int splits, float* ws, int* err, int num_sms,
                       cudaStream_t stream);
 // Row-parallel GEMM whose epilogue pushes output rows to their owner ranks (see
-// GemmParams::push*).  One CTA per 128-row P tile, splits = 1.  `push` holds the
-// push fields (other members ignored).  Returns 0 on success.
+// GemmParams::push*).  P holds the token rows (trans = 0 only), splits = 1;
+// pair selects the CTA-pair kernel (bn 128/192/256) over the one-CTA kernel
+// (bn 64/128/256).  `push` holds the push fields (other members ignored).
 int sh_gemm_bf16_push(const void* P, int rows_p, int64_t ldp, const void* Q, int rows_q, int64_t ldq, int K,
-                      int trans, int bn, const GemmParams* push, int* err, int num_sms, cudaStream_t stream);
+                      int trans, int bn, int pair, const GemmParams* push, int* err, int num_sms,
+                      cudaStream_t stream);
 // Grouped swap-AB GEMM for MoE experts: for every device-side group entry g
 // (see GemmParams::groups), out[q, :] = sum_k Q[q, k] * P[p_row_offset + n, k]
 // for the q_rows sorted rows of the entry and n < rows_p.  P stacks the

@@ -210,6 +210,51 @@ def plan(M: int, N: int, K: int, x2: Optional[torch.Tensor] = None, w: Optional[
     return got
 
 
+_PUSH: Dict[Tuple[int, int, int], Tuple[bool, int]] = {}
+
+
+def plan_push(x2: torch.Tensor, w: torch.Tensor) -> Tuple[bool, int]:
+    """(pair, bn) of a push (reduce-scatter epilogue) GEMM: tokens on the M side, no split-K.
+
+    Timed on the same tile configurations with the local epilogue (a push run cannot be timed
+    alone: it counts arrivals at the peers); the choice is agreed across ranks like every plan.
+    """
+    M, K = x2.shape
+    N = w.shape[0]
+    key = (M, N, K)
+    got = _PUSH.get(key)
+    if got is not None:
+        return got
+    if torch.cuda.is_current_stream_capturing() or os.environ.get("SH_GEMM_TUNE", "1") == "0":
+        return (M > 128, 256 if M > 128 else 128)
+    y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
+    cands = [(False, False, bn, 1) for bn in (64, 128, 256)] + [(True, False, bn, 1) for bn in (128, 192, 256)]
+    dev = x2.device
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    flush = _FLUSH.get(idx)
+    if flush is None:
+        flush = _FLUSH[idx] = torch.empty(160 << 20, dtype=torch.uint8, device=dev)
+    times = []
+    for cfg in cands:
+        run = _runner(cfg, x2, w, y)
+        run()
+        t = float("inf")
+        for _ in range(2):
+            flush.zero_()
+            torch.cuda._sleep(50_000)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            run()
+            e.record()
+            e.synchronize()
+            t = min(t, s.elapsed_time(e))
+        times.append(t)
+    times = _agree(times)
+    best = cands[min(range(len(cands)), key=times.__getitem__)]
+    _PUSH[key] = (best[0], best[2])
+    return _PUSH[key]
+
+
 def choice_summary() -> dict:
     """How many tuned shapes run which kernel family (for benchmark reports)."""
     out = {"tcgen05_one_cta": 0, "tcgen05_pair": 0, "cublas": 0}

@@ -137,11 +137,15 @@ class SymmComm:
         T, N = x.shape[0], w.shape[0]
         if N != self.hidden or T > self.max_tokens:
             raise ValueError("push GEMM: output width must be the hidden size and T <= max_tokens")
-        swap = T <= 256
-        bn = next(b for b in (64, 128, 256) if b >= T) if swap else (256 if N > 8192 else 128)
-        ops.native().gemm_bf16_push(x.contiguous(), w, swap, bn, self.peer_recv, self.peer_rs_cnt, self.counters,
-                                    self.rank, self.owner_rows(T), self.max_tokens, self.err)
-        return PushedPartial(self, T, self.push_expected(T, N, swap, bn))
+        from ..ops import gemm
+
+        x = x.contiguous()
+        # The push epilogue writes 128-byte token-row segments: tokens on the MMA M side (no swap),
+        # no split-K.  The tile configuration is autotuned on the same GEMM with a local epilogue.
+        pair, bn = gemm.plan_push(x, w)
+        ops.native().gemm_bf16_push(x, w, pair, bn, self.peer_recv, self.peer_rs_cnt, self.counters, self.rank,
+                                    self.owner_rows(T), self.max_tokens, self.err)
+        return PushedPartial(self, T, self.push_expected(T, N, False, bn))
 
     def finish_push(self, pp: "PushedPartial", residual: torch.Tensor, w: torch.Tensor, eps: float,
                     gather_residual: bool = False) -> torch.Tensor:
