@@ -6,6 +6,7 @@
 #include "comm.h"
 #include "gdn.h"
 #include "moe.h"
+#include "mla.h"
 #include "paged_attention.h"
 
 void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
@@ -223,6 +224,87 @@ void rs_norm_ag(int64_t recv, std::vector<int64_t> peer_gather, std::vector<int6
   TORCH_CHECK(r == 0, "sh_rs_norm_ag failed with code ", r);
 }
 
+// --- MLA decode / DSA indexer -----------------------------------------------------
+void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor latent, torch::Tensor block_tables,
+                torch::Tensor seq_lens, torch::Tensor q_start, c10::optional<torch::Tensor> topk, int64_t nsplit,
+                c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_ml, double scale,
+                torch::Tensor err) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.is_contiguous(), "mla: q [T,H,C]");
+  TORCH_CHECK(latent.scalar_type() == at::kBFloat16 && latent.dim() == 3 && latent.size(1) == 64 &&
+                  latent.is_contiguous(), "mla: latent [blocks, 64, C]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.dim() == 3, "mla: out [T,H,V]");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kLong &&
+                  q_start.scalar_type() == at::kLong, "mla: index dtypes");
+  const int C = static_cast<int>(q.size(2)), V = static_cast<int>(out.size(2));
+  TORCH_CHECK(latent.size(2) == C, "mla: latent width");
+  MlaParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.latent = reinterpret_cast<const __nv_bfloat16*>(latent.data_ptr());
+  p.block_tables = block_tables.data_ptr<int32_t>();
+  p.bt_stride = block_tables.stride(0);
+  p.seq_lens = seq_lens.data_ptr<int64_t>();
+  p.q_start = q_start.data_ptr<int64_t>();
+  p.B = static_cast<int>(seq_lens.size(0));
+  if (topk.has_value()) {
+    TORCH_CHECK(topk->scalar_type() == at::kInt && topk->is_contiguous() && topk->size(0) == q.size(0), "mla: topk");
+    p.topk = topk->data_ptr<int32_t>();
+    p.topk_k = static_cast<int>(topk->size(1));
+  }
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.nsplit = static_cast<int>(nsplit);
+  if (nsplit > 1) {
+    TORCH_CHECK(part_o.has_value() && part_ml.has_value() && part_o->numel() >= q.size(0) * q.size(1) * nsplit * V &&
+                    part_ml->numel() >= q.size(0) * q.size(1) * nsplit * 2, "mla: split workspace");
+    p.part_o = part_o->data_ptr<float>();
+    p.part_ml = part_ml->data_ptr<float>();
+  }
+  p.err = err.data_ptr<int>();
+  p.T = static_cast<int>(q.size(0));
+  p.H = static_cast<int>(q.size(1));
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  const int r = sh_mla_decode(&p, C, V, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_mla_decode failed with code ", r, " (C=", C, ", V=", V, ")");
+}
+
+void mla_cache_write(torch::Tensor latent, torch::Tensor c, torch::Tensor kpe, torch::Tensor slots) {
+  TORCH_CHECK(latent.scalar_type() == at::kBFloat16 && c.scalar_type() == at::kBFloat16 &&
+                  kpe.scalar_type() == at::kBFloat16 && slots.scalar_type() == at::kLong, "mla_cache_write: dtypes");
+  TORCH_CHECK(c.stride(1) == 1 && kpe.stride(1) == 1 && latent.size(2) == c.size(1) + kpe.size(1), "mla_cache_write");
+  const int r = sh_mla_cache_write(reinterpret_cast<__nv_bfloat16*>(latent.data_ptr()),
+                                   reinterpret_cast<const __nv_bfloat16*>(c.data_ptr()), c.stride(0),
+                                   reinterpret_cast<const __nv_bfloat16*>(kpe.data_ptr()), kpe.stride(0),
+                                   slots.data_ptr<int64_t>(), static_cast<int>(c.size(0)), static_cast<int>(c.size(1)),
+                                   static_cast<int>(kpe.size(1)), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_mla_cache_write failed with code ", r);
+}
+
+void dsa_topk(torch::Tensor topk, torch::Tensor logits, torch::Tensor q, torch::Tensor w, torch::Tensor kcache,
+              torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.is_contiguous(), "dsa: q [T, IH, ID]");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "dsa: w [T, IH] fp32");
+  TORCH_CHECK(kcache.scalar_type() == at::kBFloat16 && kcache.dim() == 3 && kcache.size(1) == 64, "dsa: kcache");
+  TORCH_CHECK(topk.scalar_type() == at::kInt && topk.is_contiguous() && logits.scalar_type() == at::kFloat,
+              "dsa: outputs");
+  DsaParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.w = w.data_ptr<float>();
+  p.kcache = reinterpret_cast<const __nv_bfloat16*>(kcache.data_ptr());
+  p.block_tables = block_tables.data_ptr<int32_t>();
+  p.bt_stride = block_tables.stride(0);
+  p.seq_lens = seq_lens.data_ptr<int64_t>();
+  p.q_start = q_start.data_ptr<int64_t>();
+  p.B = static_cast<int>(seq_lens.size(0));
+  p.logits = logits.data_ptr<float>();
+  p.topk = topk.data_ptr<int32_t>();
+  p.T = static_cast<int>(q.size(0));
+  p.IH = static_cast<int>(q.size(1));
+  p.ID = static_cast<int>(q.size(2));
+  p.K = static_cast<int>(topk.size(1));
+  p.max_keys = static_cast<int>(logits.size(1));
+  const int r = sh_dsa_topk(&p, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_dsa_topk failed with code ", r, " (IH=", p.IH, ", ID=", p.ID, ")");
+}
+
 template <typename T>
 static T* ptr(const torch::Tensor& t) {
   return reinterpret_cast<T*>(t.data_ptr());
@@ -403,6 +485,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out"), py::arg("weight"), py::arg("err"), py::arg("rank"), py::arg("T"), py::arg("H"),
         py::arg("max_T"), py::arg("Tc"), py::arg("expected"), py::arg("eps"), py::arg("gather_res"),
         py::arg("num_blocks"), py::arg("timing") = py::none());
+  m.def("mla_decode", &mla_decode);
+  m.def("mla_cache_write", &mla_cache_write);
+  m.def("dsa_topk", &dsa_topk);
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("moe_route", &moe_route);

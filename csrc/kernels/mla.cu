@@ -1,0 +1,547 @@
+// Multi-head latent attention (DeepSeek-V3 / Kimi-K2 absorbed form) decode and
+// the DeepSeek-V3.2 lightning indexer with top-k selection.
+//
+// MLA decode.  Queries are already absorbed into the latent space: q[t, h] =
+// [q_nope W_UK | rotated q_pe] (C = kv_lora + rope columns); the paged cache
+// row of a key is [normalised c_kv | rotated k_pe], and the values are the
+// first V = kv_lora columns of the same row.  Work unit = (query token, 64
+// heads, key split): all heads of a token share every key, so a 32-key
+// sub-page gathered once feeds 64 rows of bf16 tensor-core tiles (mma.sync
+// m16n8k16, fp32 accumulate).  8 warps = 4 row groups (16 heads) x 2 halves:
+// for QK^T the two warps of a row group take one half of the 32 keys each
+// (C-deep dot products), exchange row maxima and their probabilities P
+// through shared memory, and for PV each takes one half of the V columns over
+// all 32 keys, so the [16 x V/2] fp32 accumulator of a warp stays in
+// registers.  Keys come from a DSA top-k list (sparse) or every position up to
+// the token's own (dense causal); a key position outside the causal range or
+// -1 is zero-filled and masked.  Sub-pages are gathered row by row with
+// cp.async (two-stage ring), which serves both the contiguous and the sparse
+// case.  Online softmax in the exp2 domain; with nsplit > 1 each split writes
+// normalised O and (max, sum) and mla_merge combines them in split order.
+//
+// DSA indexer.  logits[t, s] = sum_h relu(q[t, h] . k[s]) * w[t, h] over the
+// token's causal keys, computed on tensor-core tiles (16 heads x 64 keys per
+// warp), then the top K positions by a 4-pass radix select on the float
+// bits; ties at the threshold keep the latest positions, and the selected
+// positions are written in ascending order (a deterministic key order for the
+// attention that follows).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "mla.h"
+#include "pdl.cuh"
+
+namespace shk {
+namespace mla {
+
+constexpr int ROWS = 64;  // heads per work unit
+constexpr int KEYS = 32;  // keys per sub-page
+constexpr int THREADS = 256;
+constexpr int P_LD = 40;  // bf16 row stride of the P tile (80 bytes)
+
+__device__ __forceinline__ uint32_t saddr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(pred ? 16 : 0));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a));
+}
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+// [NR rows][C] bf16 tile as C/64 slabs of [NR][128 B]; 16-byte chunk cc of row
+// r sits at chunk position cc ^ (r & 7) of its slab (conflict-free ldmatrix).
+template <int NR>
+__device__ __forceinline__ uint32_t swz(int r, int cc) {
+  return static_cast<uint32_t>((cc >> 3) * (NR * 128) + r * 128 + (((cc & 7) ^ (r & 7)) << 4));
+}
+// Request of query token t: the largest b with q_start[b] <= t.
+__device__ __forceinline__ int request_of(const int64_t* q_start, int B, int t) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (q_start[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+__device__ __forceinline__ void bar_pair(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+
+template <int C, int V>
+struct MlaSmem {
+  static constexpr int Q_BYTES = ROWS * C * 2;
+  static constexpr int KV_BYTES = KEYS * C * 2;
+  static constexpr int P_OFF = Q_BYTES + 2 * KV_BYTES;
+  static constexpr int M_OFF = P_OFF + 4 * 16 * P_LD * 2;
+  static constexpr int L_OFF = M_OFF + 4 * 2 * 16 * 4;
+  static constexpr int I_OFF = L_OFF + 4 * 2 * 16 * 4;
+  static constexpr int TOTAL = I_OFF + 2 * KEYS * 4 + 128;
+  static_assert(TOTAL <= 227 * 1024, "shared memory budget");
+};
+
+template <int C, int V>
+__global__ void __launch_bounds__(THREADS, 1) mla_decode_kernel(MlaParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  using S = MlaSmem<C, V>;
+  constexpr int CH = C / 8;        // 16-byte chunks per row
+  constexpr int KSTEPS = C / 16;
+  constexpr int VH = V / 2;        // value columns per warp
+  constexpr int VT = VH / 8;       // n8 tiles per warp
+  static_assert(C % 64 == 0 && V % 32 == 0 && V <= C, "MLA geometry");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const uint32_t sQ = saddr(smem);
+  const uint32_t sKV = sQ + S::Q_BYTES;
+  __nv_bfloat16* sP = reinterpret_cast<__nv_bfloat16*>(smem + S::P_OFF);
+  float* sM = reinterpret_cast<float*>(smem + S::M_OFF);
+  float* sL = reinterpret_cast<float*>(smem + S::L_OFF);
+  int* sIdx = reinterpret_cast<int*>(smem + S::I_OFF);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rg = warp & 3, vh = warp >> 2, g = lane >> 2, t4 = lane & 3;
+  const int t = blockIdx.x, h0 = blockIdx.y * ROWS, split = blockIdx.z;
+  const int b = request_of(p.q_start, p.B, t);
+  const int64_t qs = p.q_start[b], ql = p.q_start[b + 1] - qs, seq = p.seq_lens[b];
+  const int64_t qpos = seq - ql + (t - qs);
+  const int64_t nkeys = p.topk ? static_cast<int64_t>(p.topk_k) : qpos + 1;
+  const int npages = static_cast<int>((nkeys + KEYS - 1) / KEYS);
+  const int per = (npages + p.nsplit - 1) / p.nsplit;
+  const int pg0 = min(split * per, npages), pg1 = min(pg0 + per, npages);
+  const int rows_valid = min(ROWS, p.H - h0);
+  const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
+
+  auto key_pos = [&](int j, int key) -> int64_t {
+    const int64_t kp = static_cast<int64_t>(j) * KEYS + key;
+    if (kp >= nkeys) return -1;
+    const int64_t pos = p.topk ? static_cast<int64_t>(p.topk[static_cast<int64_t>(t) * p.topk_k + kp]) : kp;
+    return (pos < 0 || pos > qpos) ? -1 : pos;
+  };
+  auto load_page = [&](int j, int st) {
+    for (int c = tid; c < KEYS * CH; c += THREADS) {
+      const int key = c / CH, cc = c % CH;
+      const int64_t pos = key_pos(j, key);
+      const bool ok = pos >= 0;
+      const int64_t row = ok ? static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63) : 0;
+      cp_async16(sKV + st * S::KV_BYTES + swz<KEYS>(key, cc), p.latent + row * C + cc * 8, ok);
+    }
+    if (tid < KEYS) sIdx[st * KEYS + tid] = key_pos(j, tid) >= 0 ? 1 : 0;
+  };
+
+  for (int c = tid; c < ROWS * CH; c += THREADS) {
+    const int r = c / CH, cc = c % CH;
+    const bool ok = r < rows_valid;
+    cp_async16(sQ + swz<ROWS>(r, cc), p.q + (static_cast<int64_t>(t) * p.H + h0 + (ok ? r : 0)) * C + cc * 8, ok);
+  }
+  asm volatile("cp.async.commit_group;\n" ::);
+  if (pg0 < pg1) load_page(pg0, 0);
+  asm volatile("cp.async.commit_group;\n" ::);
+
+  float o[VT][4];
+#pragma unroll
+  for (int i = 0; i < VT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  __nv_bfloat16* myP = sP + rg * 16 * P_LD;
+  const uint32_t sPrg = saddr(myP);
+
+  for (int j = pg0; j < pg1; ++j) {
+    const int st = (j - pg0) & 1;
+    if (j + 1 < pg1) load_page(j + 1, st ^ 1);
+    asm volatile("cp.async.commit_group;\n" ::);
+    asm volatile("cp.async.wait_group 1;\n" ::);
+    __syncthreads();
+    const uint32_t kv = sKV + st * S::KV_BYTES;
+    // S = Q K^T for this warp's 16 heads x 16 keys
+    float sc[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+#pragma unroll 4
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+      ldsm_x4(sQ + swz<ROWS>(rg * 16 + (lane & 15), 2 * kk + (lane >> 4)), a0, a1, a2, a3);
+      ldsm_x4(kv + swz<KEYS>(vh * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0, b1, b2, b3);
+      mma16816(sc[0], a0, a1, a2, a3, b0, b1);
+      mma16816(sc[1], a0, a1, a2, a3, b2, b3);
+    }
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool valid = sIdx[st * KEYS + vh * 16 + nt * 8 + 2 * t4 + e] != 0;
+        const float va = valid ? sc[nt][e] * p.scale_log2 : -INFINITY;
+        const float vb = valid ? sc[nt][2 + e] * p.scale_log2 : -INFINITY;
+        sc[nt][e] = va;
+        sc[nt][2 + e] = vb;
+        mx_a = fmaxf(mx_a, va);
+        mx_b = fmaxf(mx_b, vb);
+      }
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+    if (t4 == 0) {
+      sM[(rg * 2 + vh) * 16 + g] = mx_a;
+      sM[(rg * 2 + vh) * 16 + g + 8] = mx_b;
+    }
+    bar_pair(1 + rg);
+    mx_a = fmaxf(mx_a, sM[(rg * 2 + (vh ^ 1)) * 16 + g]);
+    mx_b = fmaxf(mx_b, sM[(rg * 2 + (vh ^ 1)) * 16 + g + 8]);
+    const float nm_a = fmaxf(m_a, mx_a), nm_b = fmaxf(m_b, mx_b);
+    const float base_a = nm_a == -INFINITY ? 0.f : nm_a, base_b = nm_b == -INFINITY ? 0.f : nm_b;
+    const float al_a = exp2f(m_a - base_a), al_b = exp2f(m_b - base_b);
+    float sum_a = 0.f, sum_b = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const float p0 = exp2f(sc[nt][0] - base_a), p1 = exp2f(sc[nt][1] - base_a);
+      const float p2 = exp2f(sc[nt][2] - base_b), p3 = exp2f(sc[nt][3] - base_b);
+      sum_a += p0 + p1;
+      sum_b += p2 + p3;
+      const int col = vh * 16 + nt * 8 + 2 * t4;
+      *reinterpret_cast<uint32_t*>(myP + g * P_LD + col) = pack2(p0, p1);
+      *reinterpret_cast<uint32_t*>(myP + (g + 8) * P_LD + col) = pack2(p2, p3);
+    }
+    l_a = l_a * al_a + sum_a;  // this warp's keys; the two halves are added at the end
+    l_b = l_b * al_b + sum_b;
+    m_a = nm_a;
+    m_b = nm_b;
+#pragma unroll
+    for (int dt = 0; dt < VT; ++dt) {
+      o[dt][0] *= al_a;
+      o[dt][1] *= al_a;
+      o[dt][2] *= al_b;
+      o[dt][3] *= al_b;
+    }
+    bar_pair(1 + rg);  // both halves of P are written
+    // O[16 x V/2] += P[16 x 32] V[32 x V/2]
+#pragma unroll
+    for (int kc = 0; kc < 2; ++kc) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(sPrg + ((lane & 15) * P_LD + kc * 16 + (lane >> 4) * 8) * 2, a0, a1, a2, a3);
+#pragma unroll
+      for (int dp = 0; dp < VT / 2; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(kv + swz<KEYS>(kc * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), vh * (VH / 8) + 2 * dp + (lane >> 4)),
+                  b0, b1, b2, b3);
+        mma16816(o[2 * dp], a0, a1, a2, a3, b0, b1);
+        mma16816(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    __syncthreads();  // stage st, P and the maxima are free for the next sub-page
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  if (t4 == 0) {
+    sL[(rg * 2 + vh) * 16 + g] = l_a;
+    sL[(rg * 2 + vh) * 16 + g + 8] = l_b;
+  }
+  bar_pair(1 + rg);
+  l_a += sL[(rg * 2 + (vh ^ 1)) * 16 + g];
+  l_b += sL[(rg * 2 + (vh ^ 1)) * 16 + g + 8];
+  const float inv_a = l_a > 0.f ? 1.f / l_a : 0.f, inv_b = l_b > 0.f ? 1.f / l_b : 0.f;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int r = rg * 16 + g + 8 * half;
+    if (r >= rows_valid) continue;
+    const int64_t th = static_cast<int64_t>(t) * p.H + h0 + r;
+    const float inv = half ? inv_b : inv_a;
+    if (p.nsplit == 1) {
+      __nv_bfloat16* dst = p.out + th * V + vh * VH;
+#pragma unroll
+      for (int dt = 0; dt < VT; ++dt)
+        *reinterpret_cast<__nv_bfloat162*>(dst + dt * 8 + 2 * t4) =
+            __floats2bfloat162_rn(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
+    } else {
+      const int64_t prow = th * p.nsplit + split;
+      float* dst = p.part_o + prow * V + vh * VH;
+#pragma unroll
+      for (int dt = 0; dt < VT; ++dt)
+        *reinterpret_cast<float2*>(dst + dt * 8 + 2 * t4) = make_float2(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
+      if (t4 == 0 && vh == 0) {
+        p.part_ml[prow * 2] = half ? m_b : m_a;
+        p.part_ml[prow * 2 + 1] = half ? l_b : l_a;
+      }
+    }
+  }
+}
+
+// out[t, h, :] = sum_s w_s o_s / sum_s w_s, w_s = l_s exp2(m_s - max m), in split order.
+__global__ void mla_merge_kernel(__nv_bfloat16* __restrict__ out, const float* __restrict__ part_o,
+                                 const float* __restrict__ part_ml, int64_t rows, int nsplit, int V) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int per_row = V / 2;
+  if (i >= rows * per_row) return;
+  const int64_t row = i / per_row;
+  const int c = static_cast<int>(i % per_row) * 2;
+  float mx = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, part_ml[(row * nsplit + s) * 2]);
+  const float base = mx == -INFINITY ? 0.f : mx;
+  float acc0 = 0.f, acc1 = 0.f, den = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const int64_t pr = row * nsplit + s;
+    const float w = part_ml[pr * 2 + 1] * exp2f(part_ml[pr * 2] - base);
+    const float2 v = *reinterpret_cast<const float2*>(part_o + pr * V + c);
+    acc0 += w * v.x;
+    acc1 += w * v.y;
+    den += w;
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  *reinterpret_cast<__nv_bfloat162*>(out + row * V + c) = __floats2bfloat162_rn(acc0 * inv, acc1 * inv);
+}
+
+__global__ void cache_write_kernel(__nv_bfloat16* __restrict__ latent, const __nv_bfloat16* __restrict__ c,
+                                   int64_t c_stride, const __nv_bfloat16* __restrict__ kpe, int64_t kpe_stride,
+                                   const int64_t* __restrict__ slots, int Cl, int R) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  const int t = blockIdx.x;
+  const int64_t slot = slots[t];
+  if (slot < 0) return;
+  __nv_bfloat16* dst = latent + slot * (Cl + R);
+  for (int i = threadIdx.x; i < Cl + R; i += blockDim.x)
+    dst[i] = i < Cl ? c[t * c_stride + i] : kpe[t * kpe_stride + (i - Cl)];
+}
+
+// ------------------------------------------------------------------------- DSA indexer
+constexpr int IDX_KEYS = 64;     // keys per indexer tile
+constexpr int IDX_THREADS = 512;  // 16 warps: 4 head groups x 4 key quarters
+
+__device__ __forceinline__ uint32_t ordered_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // larger float -> larger unsigned
+}
+
+// One CTA per query token: logits over its causal keys, then the top-K positions.
+template <int IH, int ID>
+__global__ void __launch_bounds__(IDX_THREADS, 1) dsa_topk_kernel(DsaParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  static_assert(IH % 16 == 0 && IH <= 64 && ID % 64 == 0, "indexer geometry");
+  constexpr int CH = ID / 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const uint32_t sQ = saddr(smem);                       // [64][ID] (rows >= IH zero)
+  const uint32_t sK = sQ + 64 * ID * 2;                  // [IDX_KEYS][ID]
+  float* sW = reinterpret_cast<float*>(smem + 64 * ID * 2 + IDX_KEYS * ID * 2);  // [64] head weights
+  float* sPart = sW + 64;                                 // [4 head groups][IDX_KEYS]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(sPart + 4 * IDX_KEYS);  // [256]
+  uint32_t* misc = hist + 256;                           // [8]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t = blockIdx.x;
+  const int b = request_of(p.q_start, p.B, t);
+  const int64_t qs = p.q_start[b], ql = p.q_start[b + 1] - qs, seq = p.seq_lens[b];
+  const int64_t qpos = seq - ql + (t - qs);
+  const int nkeys = static_cast<int>(qpos + 1);
+  int32_t* out = p.topk + static_cast<int64_t>(t) * p.K;
+  if (nkeys <= p.K) {  // every causal key is selected
+    for (int i = tid; i < p.K; i += IDX_THREADS) out[i] = i < nkeys ? i : -1;
+    return;
+  }
+  const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
+  float* lg = p.logits + static_cast<int64_t>(t) * p.max_keys;
+  for (int c = tid; c < 64 * CH; c += IDX_THREADS) {
+    const int r = c / CH, cc = c % CH;
+    const bool ok = r < IH;
+    cp_async16(sQ + swz<64>(r, cc), p.q + (static_cast<int64_t>(t) * IH + (ok ? r : 0)) * ID + cc * 8, ok);
+  }
+  if (tid < 64) sW[tid] = tid < IH ? p.w[static_cast<int64_t>(t) * IH + tid] : 0.f;
+  asm volatile("cp.async.commit_group;\n" ::);
+  const int hg = warp & 3, kq = warp >> 2;  // 16 heads x 16 keys per warp
+  for (int k0 = 0; k0 < nkeys; k0 += IDX_KEYS) {
+    __syncthreads();
+    for (int c = tid; c < IDX_KEYS * CH; c += IDX_THREADS) {
+      const int key = c / CH, cc = c % CH;
+      const int pos = k0 + key;
+      const bool ok = pos < nkeys;
+      const int64_t row = ok ? static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63) : 0;
+      cp_async16(sK + swz<IDX_KEYS>(key, cc), p.kcache + row * ID + cc * 8, ok);
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+    asm volatile("cp.async.wait_group 0;\n" ::);
+    __syncthreads();
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (hg * 16 < IH) {
+#pragma unroll
+      for (int kk = 0; kk < ID / 16; ++kk) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        ldsm_x4(sQ + swz<64>(hg * 16 + (lane & 15), 2 * kk + (lane >> 4)), a0, a1, a2, a3);
+        ldsm_x4(sK + swz<IDX_KEYS>(kq * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0, b1, b2,
+                b3);
+        mma16816(sc[0], a0, a1, a2, a3, b0, b1);
+        mma16816(sc[1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // relu * w over this warp's 16 heads, summed over the heads -> per key partial
+    const float wa = sW[hg * 16 + (lane >> 2)], wb = sW[hg * 16 + (lane >> 2) + 8];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = fmaxf(sc[nt][e], 0.f) * wa + fmaxf(sc[nt][2 + e], 0.f) * wb;
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        if ((lane >> 2) == 0) sPart[hg * IDX_KEYS + kq * 16 + nt * 8 + 2 * (lane & 3) + e] = v;
+      }
+    __syncthreads();
+    for (int key = tid; key < IDX_KEYS; key += IDX_THREADS) {
+      const int pos = k0 + key;
+      if (pos < nkeys)
+        lg[pos] = sPart[key] + sPart[IDX_KEYS + key] + sPart[2 * IDX_KEYS + key] + sPart[3 * IDX_KEYS + key];
+    }
+  }
+  __syncthreads();
+  // radix select of the K-th largest ordered key (4 passes of 8 bits, most significant first)
+  uint32_t prefix = 0, mask = 0;
+  int remaining = p.K;  // how many of the top K lie at or below the current prefix bucket
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += IDX_THREADS) hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < nkeys; i += IDX_THREADS) {
+      const uint32_t u = ordered_bits(lg[i]);
+      if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 255], 1u);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0, d = 255;
+      for (; d > 0; --d) {
+        if (acc + static_cast<int>(hist[d]) >= remaining) break;
+        acc += hist[d];
+      }
+      misc[0] = static_cast<uint32_t>(d);
+      misc[1] = static_cast<uint32_t>(remaining - acc);
+    }
+    __syncthreads();
+    prefix |= misc[0] << shift;
+    mask |= 255u << shift;
+    remaining = static_cast<int>(misc[1]);
+    __syncthreads();
+  }
+  // threshold = prefix: take every key above it and the `remaining` latest keys equal to it
+  // (skip the first eq_total - remaining equal keys in position order), written in ascending order
+  const uint32_t thr = prefix;
+  if (tid == 0) misc[2] = 0;
+  __syncthreads();
+  {
+    uint32_t eq = 0;
+    for (int i = tid; i < nkeys; i += IDX_THREADS) eq += ordered_bits(lg[i]) == thr ? 1u : 0u;
+    if (eq) atomicAdd(&misc[2], eq);
+  }
+  __syncthreads();
+  const int skip = static_cast<int>(misc[2]) - remaining;
+  uint32_t* wsel = misc + 8;        // [16] per-warp selected counts
+  uint32_t* weq = wsel + 16;        // [16] per-warp equal counts
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  int base = 0, base_eq = 0;
+  for (int c0 = 0; c0 < nkeys; c0 += IDX_THREADS) {
+    const int i = c0 + tid;
+    const uint32_t u = i < nkeys ? ordered_bits(lg[i]) : 0u;
+    const bool gt = i < nkeys && u > thr, eqk = i < nkeys && u == thr;
+    const uint32_t beq = __ballot_sync(0xffffffffu, eqk);
+    if (lane == 0) weq[warp] = __popc(beq);
+    __syncthreads();
+    int eq_before = base_eq;
+    for (int w = 0; w < warp; ++w) eq_before += weq[w];
+    eq_before += __popc(beq & lt_mask);
+    const bool sel = gt || (eqk && eq_before >= skip);
+    const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
+    if (lane == 0) wsel[warp] = __popc(bsel);
+    __syncthreads();
+    int pos = base;
+    for (int w = 0; w < warp; ++w) pos += wsel[w];
+    pos += __popc(bsel & lt_mask);
+    if (sel && pos < p.K) out[pos] = i;
+    for (int w = 0; w < IDX_THREADS / 32; ++w) {
+      base += wsel[w];
+      base_eq += weq[w];
+    }
+    __syncthreads();
+  }
+  for (int i = base + tid; i < p.K; i += IDX_THREADS) out[i] = -1;
+}
+
+}  // namespace mla
+}  // namespace shk
+
+using namespace shk::mla;
+
+namespace {
+template <int C, int V>
+int launch_mla(const MlaParams& p, cudaStream_t st) {
+  using S = MlaSmem<C, V>;
+  auto k = mla_decode_kernel<C, V>;
+  static bool ready = false;
+  if (!ready) {
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    ready = true;
+  }
+  shk::launch(k, dim3(p.T, (p.H + ROWS - 1) / ROWS, p.nsplit), dim3(THREADS), S::TOTAL, st, p);
+  int r = static_cast<int>(cudaGetLastError());
+  if (r || p.nsplit == 1) return r;
+  const int64_t rows = static_cast<int64_t>(p.T) * p.H;
+  const int64_t n = rows * (V / 2);
+  shk::launch(mla_merge_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, st, p.out, p.part_o,
+              p.part_ml, rows, p.nsplit, V);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int IH, int ID>
+int launch_dsa(const DsaParams& p, cudaStream_t st) {
+  const int smem = 64 * ID * 2 + IDX_KEYS * ID * 2 + (64 + 4 * IDX_KEYS) * 4 + (256 + 8 + 32) * 4 + 128;
+  auto k = dsa_topk_kernel<IH, ID>;
+  static bool ready = false;
+  if (!ready) {
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    ready = true;
+  }
+  shk::launch(k, dim3(p.T), dim3(IDX_THREADS), smem, st, p);
+  return static_cast<int>(cudaGetLastError());
+}
+}  // namespace
+
+extern "C" int sh_mla_decode(const MlaParams* p, int C, int V, cudaStream_t stream) {
+  if (p->T <= 0) return 0;
+  if (p->nsplit < 1 || (p->nsplit > 1 && (!p->part_o || !p->part_ml))) return -1;
+  if (C == 576 && V == 512) return launch_mla<576, 512>(*p, stream);
+  if (C == 128 && V == 64) return launch_mla<128, 64>(*p, stream);
+  return -2;
+}
+
+extern "C" int sh_mla_cache_write(__nv_bfloat16* latent, const __nv_bfloat16* c, int64_t c_stride,
+                                  const __nv_bfloat16* kpe, int64_t kpe_stride, const int64_t* slots, int T, int Cl,
+                                  int R, cudaStream_t stream) {
+  if (T <= 0) return 0;
+  shk::launch(cache_write_kernel, dim3(T), dim3(128), 0, stream, latent, c, c_stride, kpe, kpe_stride, slots, Cl, R);
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int sh_dsa_topk(const DsaParams* p, cudaStream_t stream) {
+  if (p->T <= 0) return 0;
+  if (p->K <= 0 || !p->topk || !p->logits) return -1;
+  if (p->IH == 64 && p->ID == 128) return launch_dsa<64, 128>(*p, stream);
+  if (p->IH == 16 && p->ID == 64) return launch_dsa<16, 64>(*p, stream);
+  return -2;
+}

@@ -1,0 +1,50 @@
+// C ABI of the MLA (multi-head latent attention) decode kernels and the DSA indexer.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+struct MlaParams {
+  const __nv_bfloat16* q;       // [T, H, C] absorbed queries: [q_nope W_UK | rotated q_pe]
+  const __nv_bfloat16* latent;  // paged cache [num_blocks, 64, C]: [normalised c_kv | rotated k_pe]
+  const int32_t* block_tables;  // [B, bt_stride]
+  int64_t bt_stride;
+  const int64_t* seq_lens;      // [B] keys of the request including its new tokens
+  const int64_t* q_start;       // [B+1] query start offsets (a token's request is found by binary search)
+  int B;
+  const int32_t* topk;          // [T, topk_k] absolute key positions (-1 unused) or nullptr (dense causal)
+  int topk_k;
+  __nv_bfloat16* out;           // [T, H, V] (nsplit == 1)
+  float* part_o;                // [T, H, nsplit, V]  (nsplit > 1)
+  float* part_ml;               // [T, H, nsplit, 2]  (log2-domain max, sum)
+  int* err;
+  int T, H, nsplit;
+  float scale_log2;             // softmax scale * log2(e)
+};
+
+struct DsaParams {
+  const __nv_bfloat16* q;       // [T, IH, ID] indexer queries
+  const float* w;               // [T, IH] head weights (scales folded in)
+  const __nv_bfloat16* kcache;  // paged [num_blocks, 64, ID] indexer keys
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  const int64_t* seq_lens;
+  const int64_t* q_start;
+  int B;
+  float* logits;                // scratch [T, max_keys]
+  int32_t* topk;                // [T, K] selected positions in ascending order, -1 padded
+  int T, IH, ID, K, max_keys;
+};
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+// C % 64 == 0 and V % 64 == 0 (V <= C); supported (C, V): (576, 512), (128, 64).
+int sh_mla_decode(const MlaParams* p, int C, int V, cudaStream_t stream);
+// latent[slot[t]] = cat(c[t], kpe[t]) for slot[t] >= 0 (C = Cl + R).
+int sh_mla_cache_write(__nv_bfloat16* latent, const __nv_bfloat16* c, int64_t c_stride, const __nv_bfloat16* kpe,
+                       int64_t kpe_stride, const int64_t* slots, int T, int Cl, int R, cudaStream_t stream);
+int sh_dsa_topk(const DsaParams* p, cudaStream_t stream);
+#ifdef __cplusplus
+}
+#endif

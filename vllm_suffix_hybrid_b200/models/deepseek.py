@@ -111,20 +111,27 @@ class MLAttention:
         c = ops.rms_norm(ckv[:, : self.lora].contiguous(), self.kv_a_norm.weight, self.kv_a_norm.eps)
         kpe = ops.ref.apply_rope(ckv[:, self.lora:].reshape(T, 1, self.rope), meta.positions, self.cos_sin)[:, 0]
         q_pe = ops.ref.apply_rope(q[..., self.nope:], meta.positions, self.cos_sin)
-        bs = latent.shape[1]
-        ok = meta.slot_mapping >= 0
-        slots = meta.slot_mapping[ok]
-        latent[slots // bs, slots % bs] = torch.cat([c, kpe.to(c.dtype)], -1)[ok]
+        ops.mla_cache_write(latent, c, kpe.to(c.dtype), meta.slot_mapping)
         wkv = self.kv_b.weight.view(self.H, self.nope + self.vd, self.lora)
         w_uk, w_uv = wkv[:, : self.nope], wkv[:, self.nope:]
-        q_lat = torch.einsum("thn,hnc->thc", q[..., : self.nope].float(), w_uk.float())
         topk = None
         if self.dsa:
             qi = self.idx_q(qa).view(T, self.ih, self.idim)
             ki = self.idx_k(x)
-            icache[slots // bs, slots % bs] = ki[ok]
+            ops.mla_cache_write(icache, ki.contiguous(), ki[:, :0], meta.slot_mapping)
             wt = ops.linear(x, self.idx_w).float() * (self.ih ** -0.5) * (self.idim ** -0.5)
-            topk = ops.ref.dsa_topk(qi, wt, icache, meta.block_tables, meta.seq_lens, meta.q_start, self.itopk)
+            topk = ops.dsa_topk(qi, wt, icache, meta.block_tables, meta.seq_lens, meta.q_start, self.itopk)
+        if x.is_cuda:
+            # absorb W_UK into the queries (plain batched GEMMs), attention over the latent cache on this
+            # framework's MLA kernel, then W_UV back to per-head values
+            q_lat = torch.bmm(q[..., : self.nope].transpose(0, 1), w_uk).transpose(0, 1)
+            qf = torch.cat([q_lat, q_pe.to(q_lat.dtype)], -1).contiguous()
+            keys = meta.block_tables.shape[1] * latent.shape[1]
+            o_lat = ops.mla_decode(qf, latent, meta.block_tables, meta.seq_lens, meta.q_start, self.scale, self.lora,
+                                   topk, ops.mla_splits(T, self.H, self.itopk if self.dsa else keys))
+            o = torch.bmm(o_lat.transpose(0, 1), w_uv.transpose(1, 2)).transpose(0, 1)
+            return self.o(o.reshape(T, self.H * self.vd).contiguous())
+        q_lat = torch.einsum("thn,hnc->thc", q[..., : self.nope].float(), w_uk.float())
         o_lat = ops.ref.mla_attention(q_lat, q_pe, latent, meta.block_tables, meta.seq_lens, meta.q_start, self.scale,
                                       self.lora, topk)
         o = torch.einsum("thc,hvc->thv", o_lat, w_uv.float()).to(x.dtype)

@@ -421,3 +421,73 @@ def nvfp4_dequantize(packed, scales, global_scale, out: torch.Tensor | None = No
         out = torch.empty(N, K, dtype=torch.bfloat16, device=packed.device)
     native().nvfp4_dequant(out, packed, scales.view(torch.uint8), global_scale.float())
     return out
+
+
+# ----------------------------------------------------------------------------- MLA / DSA
+_MLA_WS = {}
+
+
+def mla_cache_write(latent: torch.Tensor, c: torch.Tensor, kpe: torch.Tensor, slots: torch.Tensor) -> None:
+    """latent[slot] = [c | kpe] for every token with slot >= 0 (paged [blocks, 64, C] cache)."""
+    if not latent.is_cuda:
+        bs = latent.shape[1]
+        ok = slots >= 0
+        s = slots[ok]
+        latent[s // bs, s % bs] = torch.cat([c, kpe.to(c.dtype)], -1)[ok].to(latent.dtype)
+        return
+    native().mla_cache_write(latent, c, kpe, slots)
+
+
+def mla_decode(q: torch.Tensor, latent: torch.Tensor, block_tables, seq_lens, q_start, scale: float, kv_lora: int,
+               topk: torch.Tensor | None = None, nsplit: int = 1) -> torch.Tensor:
+    """Absorbed MLA over the latent cache: q [T, H, C] -> o_lat [T, H, kv_lora] (bf16 on CUDA)."""
+    if not q.is_cuda:
+        return ref.mla_attention(q[..., :kv_lora], q[..., kv_lora:], latent, block_tables, seq_lens, q_start, scale,
+                                 kv_lora, topk)
+    T, H, C = q.shape
+    out = torch.empty(T, H, kv_lora, dtype=torch.bfloat16, device=q.device)
+    part_o = part_ml = None
+    if nsplit > 1:
+        idx = q.device.index if q.device.index is not None else torch.cuda.current_device()
+        need_o, need_ml = T * H * nsplit * kv_lora, T * H * nsplit * 2
+        ws = _MLA_WS.get(idx)
+        if ws is None or ws[0].numel() < need_o or ws[1].numel() < need_ml:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("MLA split workspace must be sized before CUDA-graph capture")
+            ws = (torch.empty(max(need_o, 1 << 16), dtype=torch.float32, device=q.device),
+                  torch.empty(max(need_ml, 1 << 12), dtype=torch.float32, device=q.device))
+            _MLA_WS[idx] = ws
+        part_o, part_ml = ws
+    err = torch.zeros(1, dtype=torch.int32, device=q.device)
+    native().mla_decode(out, q.contiguous(), latent, block_tables, seq_lens, q_start,
+                        None if topk is None else topk.to(torch.int32).contiguous(), nsplit, part_o, part_ml, scale,
+                        err)
+    return out
+
+
+def mla_splits(num_tokens: int, heads: int, max_keys: int, sms: int = 148) -> int:
+    if os.environ.get("SH_BATCH_INVARIANT", "0") == "1":
+        return int(max(1, min(8, max_keys // 256)))
+    units = max(num_tokens * -(-heads // 64), 1)
+    return int(max(1, min(16, -(-sms // units), max(1, max_keys // 64))))
+
+
+def dsa_topk(qi: torch.Tensor, w: torch.Tensor, kcache: torch.Tensor, block_tables, seq_lens, q_start,
+             k: int) -> torch.Tensor:
+    """Lightning-indexer top-k positions per query token ([T, k], -1 padded)."""
+    if not qi.is_cuda:
+        return ref.dsa_topk(qi, w, kcache, block_tables, seq_lens, q_start, k)
+    T = qi.shape[0]
+    max_keys = block_tables.shape[1] * kcache.shape[1]
+    idx = qi.device.index if qi.device.index is not None else torch.cuda.current_device()
+    key = ("dsa", idx)
+    ws = _MLA_WS.get(key)
+    if ws is None or ws.shape[0] < T or ws.shape[1] < max_keys:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("indexer scratch must be sized before CUDA-graph capture")
+        ws = torch.empty(max(T, 64), max_keys, dtype=torch.float32, device=qi.device)
+        _MLA_WS[key] = ws
+    out = torch.empty(T, k, dtype=torch.int32, device=qi.device)
+    native().dsa_topk(out, ws[:T, :max_keys], qi.contiguous(), w.float().contiguous(), kcache, block_tables,
+                      seq_lens, q_start)
+    return out
