@@ -90,8 +90,8 @@ struct MlaSmem {
   static constexpr int P_OFF = Q_BYTES + 2 * KV_BYTES;
   static constexpr int M_OFF = P_OFF + 4 * 16 * P_LD * 2;
   static constexpr int L_OFF = M_OFF + 4 * 2 * 16 * 4;
-  static constexpr int I_OFF = L_OFF + 4 * 2 * 16 * 4;
-  static constexpr int TOTAL = I_OFF + 2 * KEYS * 4 + 128;
+  static constexpr int I_OFF = L_OFF + 4 * 2 * 16 * 4;  // [3][KEYS] physical cache rows (-1: masked key)
+  static constexpr int TOTAL = I_OFF + 3 * KEYS * 8 + 128;
   static_assert(TOTAL <= 227 * 1024, "shared memory budget");
 };
 
@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(THREADS, 1) mla_decode_kernel(MlaParams p) {
   __nv_bfloat16* sP = reinterpret_cast<__nv_bfloat16*>(smem + S::P_OFF);
   float* sM = reinterpret_cast<float*>(smem + S::M_OFF);
   float* sL = reinterpret_cast<float*>(smem + S::L_OFF);
-  int* sIdx = reinterpret_cast<int*>(smem + S::I_OFF);
+  int64_t* sRow = reinterpret_cast<int64_t*>(smem + S::I_OFF);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rg = warp & 3, vh = warp >> 2, g = lane >> 2, t4 = lane & 3;
@@ -127,29 +127,37 @@ __global__ void __launch_bounds__(THREADS, 1) mla_decode_kernel(MlaParams p) {
   const int rows_valid = min(ROWS, p.H - h0);
   const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
 
+  // Key position of entry `key` of sub-page j (-1: past the list, unused or outside the causal range).
   auto key_pos = [&](int j, int key) -> int64_t {
     const int64_t kp = static_cast<int64_t>(j) * KEYS + key;
-    if (kp >= nkeys) return -1;
+    if (j >= pg1 || kp >= nkeys) return -1;
     const int64_t pos = p.topk ? static_cast<int64_t>(p.topk[static_cast<int64_t>(t) * p.topk_k + kp]) : kp;
     return (pos < 0 || pos > qpos) ? -1 : pos;
   };
+  auto row_of = [&](int64_t pos) -> int64_t {
+    return pos < 0 ? -1 : static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63);
+  };
+  // Issue the cp.async gather of sub-page j (rows already in sRow[j % 3]) into stage st.
   auto load_page = [&](int j, int st) {
+    const int64_t* rows = sRow + (j % 3) * KEYS;
     for (int c = tid; c < KEYS * CH; c += THREADS) {
       const int key = c / CH, cc = c % CH;
-      const int64_t pos = key_pos(j, key);
-      const bool ok = pos >= 0;
-      const int64_t row = ok ? static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63) : 0;
-      cp_async16(sKV + st * S::KV_BYTES + swz<KEYS>(key, cc), p.latent + row * C + cc * 8, ok);
+      const int64_t row = rows[key];
+      cp_async16(sKV + st * S::KV_BYTES + swz<KEYS>(key, cc), p.latent + (row < 0 ? 0 : row) * C + cc * 8, row >= 0);
     }
-    if (tid < KEYS) sIdx[st * KEYS + tid] = key_pos(j, tid) >= 0 ? 1 : 0;
   };
 
+  if (warp == 0) {  // rows of the first two sub-pages
+    sRow[(pg0 % 3) * KEYS + lane] = row_of(key_pos(pg0, lane));
+    sRow[((pg0 + 1) % 3) * KEYS + lane] = row_of(key_pos(pg0 + 1, lane));
+  }
   for (int c = tid; c < ROWS * CH; c += THREADS) {
     const int r = c / CH, cc = c % CH;
     const bool ok = r < rows_valid;
     cp_async16(sQ + swz<ROWS>(r, cc), p.q + (static_cast<int64_t>(t) * p.H + h0 + (ok ? r : 0)) * C + cc * 8, ok);
   }
   asm volatile("cp.async.commit_group;\n" ::);
+  __syncthreads();
   if (pg0 < pg1) load_page(pg0, 0);
   asm volatile("cp.async.commit_group;\n" ::);
 
@@ -164,27 +172,45 @@ __global__ void __launch_bounds__(THREADS, 1) mla_decode_kernel(MlaParams p) {
     const int st = (j - pg0) & 1;
     if (j + 1 < pg1) load_page(j + 1, st ^ 1);
     asm volatile("cp.async.commit_group;\n" ::);
+    // warp 0 fetches sub-page j+2's positions now and resolves its rows after the QK^T below,
+    // so both dependent global loads overlap this sub-page's tensor-core work
+    int64_t nxt_pos = -1;
+    if (warp == 0) nxt_pos = key_pos(j + 2, lane);
     asm volatile("cp.async.wait_group 1;\n" ::);
     __syncthreads();
     const uint32_t kv = sKV + st * S::KV_BYTES;
-    // S = Q K^T for this warp's 16 heads x 16 keys
-    float sc[2][4];
+    const int64_t* rows_j = sRow + (j % 3) * KEYS;
+    // S = Q K^T for this warp's 16 heads x 16 keys (even and odd k-steps accumulate apart: 4 chains)
+    float sc[2][4], sd[2][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+    for (int i = 0; i < 2; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = sd[i][0] = sd[i][1] = sd[i][2] = sd[i][3] = 0.f;
 #pragma unroll 4
-    for (int kk = 0; kk < KSTEPS; ++kk) {
+    for (int kk = 0; kk < KSTEPS; kk += 2) {
       uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
       ldsm_x4(sQ + swz<ROWS>(rg * 16 + (lane & 15), 2 * kk + (lane >> 4)), a0, a1, a2, a3);
       ldsm_x4(kv + swz<KEYS>(vh * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0, b1, b2, b3);
       mma16816(sc[0], a0, a1, a2, a3, b0, b1);
       mma16816(sc[1], a0, a1, a2, a3, b2, b3);
+      ldsm_x4(sQ + swz<ROWS>(rg * 16 + (lane & 15), 2 * (kk + 1) + (lane >> 4)), a0, a1, a2, a3);
+      ldsm_x4(kv + swz<KEYS>(vh * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * (kk + 1) + ((lane >> 3) & 1)), b0, b1, b2,
+              b3);
+      mma16816(sd[0], a0, a1, a2, a3, b0, b1);
+      mma16816(sd[1], a0, a1, a2, a3, b2, b3);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[i][e] += sd[i][e];
+    if (warp == 0) {
+      const int64_t r = row_of(nxt_pos);
+      sRow[((j + 2) % 3) * KEYS + lane] = r;  // read by load_page(j + 2) after the next __syncthreads
     }
     float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const bool valid = sIdx[st * KEYS + vh * 16 + nt * 8 + 2 * t4 + e] != 0;
+        const bool valid = rows_j[vh * 16 + nt * 8 + 2 * t4 + e] >= 0;
         const float va = valid ? sc[nt][e] * p.scale_log2 : -INFINITY;
         const float vb = valid ? sc[nt][2 + e] * p.scale_log2 : -INFINITY;
         sc[nt][e] = va;
