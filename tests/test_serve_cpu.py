@@ -171,3 +171,20 @@ def test_tp2_lockstep_serving():
     finally:
         torch.set_num_threads(threads)
     assert got == want
+
+
+def test_step_profiler_windows(tmp_path, monkeypatch):
+    """SUFFIX_HYBRID_STEP_PROFILE writes a trace and a kernel/op summary per batch bucket."""
+    monkeypatch.setenv("SUFFIX_HYBRID_STEP_PROFILE", str(tmp_path))
+    monkeypatch.setenv("SUFFIX_HYBRID_STEP_PROFILE_SKIP", "1")
+    monkeypatch.setenv("SUFFIX_HYBRID_STEP_PROFILE_STEPS", "2")
+    monkeypatch.setenv("SUFFIX_HYBRID_STEP_PROFILE_BUCKETS", "2,8")
+    from vllm_suffix_hybrid_b200.engine.llm import LLMEngine
+    from vllm_suffix_hybrid_b200.parallel import state
+
+    state._STATE = state.ParallelState()
+    eng = LLMEngine(_cfg("hybrid"))
+    eng.generate([list(range(5, 25)), list(range(40, 60))], 8)
+    files = sorted(os.listdir(tmp_path))
+    assert "step_b2_r0.txt" in files and "step_b2_r0.json" in files, files
+    assert open(tmp_path / "step_b2_r0.txt").read().startswith("# 2 decode steps")

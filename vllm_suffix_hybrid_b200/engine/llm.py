@@ -123,6 +123,9 @@ class LLMEngine:
         self.stats: List[StepStats] = []
         self.proposer = None
         self.telemetry = Telemetry.from_env()
+        from ..utils.step_profiler import StepProfiler
+
+        self.step_profiler = StepProfiler.from_env(st.rank)
         self.external_proposer = None  # callable(list[Request]) -> list[list[int]] for method "external"
         k = max(self.k, 1)
         if spec.method == "hybrid":
@@ -210,6 +213,13 @@ class LLMEngine:
         free_rows = self.cfg.max_num_seqs - len(self.running)
         if self.waiting and free_rows > 0:
             return self._prefill_step(free_rows)
+        sp = self.step_profiler
+        if sp is not None:
+            sp.before("decode", len(self.running))
+            try:
+                return self._decode_step()
+            finally:
+                sp.after()
         return self._decode_step()
 
     def generate(self, prompts, max_new_tokens: int = 128) -> List[List[int]]:
