@@ -7,6 +7,7 @@
 #include "gdn.h"
 #include "moe.h"
 #include "mla.h"
+#include "gemm_nvfp4.h"
 #include "paged_attention.h"
 
 void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
@@ -305,6 +306,40 @@ void dsa_topk(torch::Tensor topk, torch::Tensor logits, torch::Tensor q, torch::
   TORCH_CHECK(r == 0, "sh_dsa_topk failed with code ", r, " (IH=", p.IH, ", ID=", p.ID, ")");
 }
 
+// NVFP4-weight GEMM (W4A16): y[t, n] = x[t] . dequant(W[n]); grouped MoE mode with `groups`.
+void gemm_nvfp4(torch::Tensor y, torch::Tensor x, torch::Tensor packed, torch::Tensor scales, torch::Tensor gscale,
+                int64_t bn, c10::optional<torch::Tensor> groups, c10::optional<torch::Tensor> num_groups,
+                int64_t rows_p, c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "gemm_nvfp4: x");
+  TORCH_CHECK(packed.scalar_type() == at::kByte && packed.is_contiguous() && scales.is_contiguous() &&
+                  scales.element_size() == 1 && gscale.scalar_type() == at::kFloat, "gemm_nvfp4: weights");
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.stride(1) == 1, "gemm_nvfp4: y");
+  const int64_t K = x.size(1);
+  TORCH_CHECK(packed.size(1) * 2 == K && scales.size(1) * 16 == K && packed.size(0) == scales.size(0),
+              "gemm_nvfp4: shapes");
+  static int num_sms = 0;
+  if (!num_sms) num_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  Fp4GemmParams g{};
+  g.packed = packed.data_ptr<uint8_t>();
+  g.scales = reinterpret_cast<const uint8_t*>(scales.data_ptr());
+  g.global_scale = gscale.data_ptr<float>();
+  g.out = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  g.ldo = y.stride(0);
+  g.rows_total = static_cast<int>(packed.size(0));
+  g.K = static_cast<int>(K);
+  g.err = err.has_value() ? err->data_ptr<int>() : nullptr;
+  if (groups.has_value()) {
+    TORCH_CHECK(num_groups.has_value() && groups->scalar_type() == at::kInt && groups->size(1) == 4, "gemm_nvfp4: groups");
+    g.groups = reinterpret_cast<const int4*>(groups->data_ptr<int>());
+    g.num_groups = num_groups->data_ptr<int>();
+    g.max_groups = static_cast<int>(groups->size(0));
+    g.rows_p = static_cast<int>(rows_p);
+  }
+  const int r = sh_gemm_nvfp4(&g, x.data_ptr(), static_cast<int>(x.size(0)), x.stride(0), static_cast<int>(bn),
+                              num_sms, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_gemm_nvfp4 failed with code ", r);
+}
+
 template <typename T>
 static T* ptr(const torch::Tensor& t) {
   return reinterpret_cast<T*>(t.data_ptr());
@@ -488,6 +523,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_decode", &mla_decode);
   m.def("mla_cache_write", &mla_cache_write);
   m.def("dsa_topk", &dsa_topk);
+  m.def("gemm_nvfp4", &gemm_nvfp4, py::arg("y"), py::arg("x"), py::arg("packed"), py::arg("scales"),
+        py::arg("gscale"), py::arg("bn"), py::arg("groups") = py::none(), py::arg("num_groups") = py::none(),
+        py::arg("rows_p") = 0, py::arg("err") = py::none());
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("moe_route", &moe_route);

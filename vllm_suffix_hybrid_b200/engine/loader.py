@@ -192,9 +192,13 @@ def _moe(ck: Checkpoint, pre: str, moe, shared_name: str) -> None:
     e0 = st.ep_rank * moe.E_local if moe.ep > 1 else 0
     for j in range(moe.E_local):
         e = e0 + j
-        g = ck.matrix(f"{pre}experts.{e}.gate_proj")
-        u = ck.matrix(f"{pre}experts.{e}.up_proj")
-        d = ck.matrix(f"{pre}experts.{e}.down_proj")
+        base = f"{pre}experts.{e}."
+        if getattr(moe, "fp4", None) is not None:
+            _fp4_expert(ck, moe, j, base)
+            continue
+        g = ck.matrix(base + "gate_proj")
+        u = ck.matrix(base + "up_proj")
+        d = ck.matrix(base + "down_proj")
         _copy(moe.w13[j * 2 * F:(j + 1) * 2 * F], torch.cat([g, u], 0), f"{pre}experts.{e}.gate|up")
         _copy(moe.w2[j * H:(j + 1) * H], d, f"{pre}experts.{e}.down")
     if moe.shared is not None:
@@ -203,6 +207,33 @@ def _moe(ck: Checkpoint, pre: str, moe, shared_name: str) -> None:
         moe.shared.down.load(ck.matrix(sp + "down_proj"))
     if moe.shared_gate is not None:
         _copy(moe.shared_gate, ck.get(pre + "shared_expert_gate.weight").float(), pre + "shared_expert_gate")
+
+
+def _fp4_expert(ck: Checkpoint, moe, j: int, base: str) -> None:
+    """Fill NVFP4 expert j: copy ModelOpt-packed tensors when gate and up share one global scale,
+    otherwise quantise the (dequantised) full matrices."""
+    from .. import ops
+
+    F, H = moe.F, moe.H
+    (p13, s13, g13), (p2, s2, g2) = moe.fp4
+    gname, uname, dname = base + "gate_proj", base + "up_proj", base + "down_proj"
+    if ck.is_nvfp4(gname) and ck.is_nvfp4(uname) and \
+            float(ck.get(gname + ".weight_scale_2")) == float(ck.get(uname + ".weight_scale_2")):
+        pg, sg, gg = ck.nvfp4(gname)
+        pu, su, _ = ck.nvfp4(uname)
+        p13[j * 2 * F:(j + 1) * 2 * F] = torch.cat([pg, pu]).to(p13.device)
+        s13[j * 2 * F:(j + 1) * 2 * F] = torch.cat([sg, su]).to(s13.device)
+        g13[j] = gg.to(g13.device)[0]
+    else:
+        w = torch.cat([ck.matrix(gname), ck.matrix(uname)]).to(p13.device, torch.bfloat16)
+        p, sc, g = ops.nvfp4_quantize(w)
+        p13[j * 2 * F:(j + 1) * 2 * F], s13[j * 2 * F:(j + 1) * 2 * F], g13[j] = p, sc, g.reshape(-1)[0]
+    if ck.is_nvfp4(dname):
+        pd, sd, gd = ck.nvfp4(dname)
+        p2[j * H:(j + 1) * H], s2[j * H:(j + 1) * H], g2[j] = pd.to(p2.device), sd.to(s2.device), gd.to(g2.device)[0]
+    else:
+        p, sc, g = ops.nvfp4_quantize(ck.matrix(dname).to(p2.device, torch.bfloat16))
+        p2[j * H:(j + 1) * H], s2[j * H:(j + 1) * H], g2[j] = p, sc, g.reshape(-1)[0]
 
 
 def _mlp(ck: Checkpoint, pre: str, mlp) -> None:

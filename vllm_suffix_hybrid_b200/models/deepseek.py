@@ -29,9 +29,11 @@ from .moe import MoEBlock
 class QLinear:
     """y = x W^T with W in bf16 or NVFP4.
 
-    NVFP4 weights are dequantised into one scratch tile per device that all
-    NVFP4 linears share (calls are ordered on the stream, so a captured graph
-    replays them correctly) and then run the bf16 tcgen05 GEMM.
+    NVFP4 linears run the W4A16 tcgen05 kernel (packed weights streamed and
+    decoded in shared memory).  `weight` (the dequantised matrix, for the MLA
+    absorption of kv_b) decodes into one scratch tile per device shared by all
+    NVFP4 layers (calls are ordered on the stream, so a captured graph replays
+    them correctly).
     """
 
     _scratch: dict = {}
@@ -61,6 +63,8 @@ class QLinear:
         return ops.nvfp4_dequantize(self.packed, self.scales, self.gscale, out=out)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fmt == "nvfp4" and x.is_cuda and x.dtype == torch.bfloat16 and self.in_f % 64 == 0:
+            return ops.nvfp4_linear(x, self.packed, self.scales, self.gscale)  # W4A16 tcgen05 kernel
         return ops.linear(x, self.weight)
 
     def load(self, full: torch.Tensor) -> None:

@@ -45,11 +45,28 @@ class MoEBlock:
                                                                           dtype, device, g)
             self.w2[j * cfg.hidden:(j + 1) * cfg.hidden] = init_weight((cfg.hidden, self.F), cfg.init_std, dtype,
                                                                          device, g)
+        # NVFP4 experts (weight_format nvfp4 on CUDA): packed codes + block scales + one global
+        # scale per expert matrix; the grouped GEMMs run the W4A16 tcgen05 kernel.
+        self.fp4 = None
+        if cfg.weight_format == "nvfp4" and torch.device(device).type == "cuda" and dtype == torch.bfloat16 \
+                and cfg.hidden % 64 == 0 and self.F % 64 == 0:
+            self.fp4 = (self._quant(self.w13, self.E_local, 2 * self.F), self._quant(self.w2, self.E_local, cfg.hidden))
+            self.w13 = self.w2 = None  # the bf16 copies are dropped
         self.shared = MLP(cfg.hidden, cfg.shared_ffn, dtype, device, gen) if cfg.shared_experts else None
         if self.shared is not None:
             self.shared.down.push = False  # reduced by a plain all-reduce below
         self.shared_gate = (init_weight((1, cfg.hidden), cfg.init_std, dtype, device, gen)
                             if cfg.shared_experts and cfg.arch == "qwen3_next" else None)
+
+    @staticmethod
+    def _quant(w: torch.Tensor, n_mat: int, rows: int):
+        packed, scales, gs = [], [], []
+        for e in range(n_mat):
+            p, sc, g = ops.nvfp4_quantize(w[e * rows:(e + 1) * rows])
+            packed.append(p)
+            scales.append(sc)
+            gs.append(g.reshape(1).float())
+        return torch.cat(packed), torch.cat(scales), torch.cat(gs)
 
     def route(self, x: torch.Tensor):
         logits = ops.linear(x, self.gate).float() if not x.is_cuda else ops.linear(x, self.gate)
@@ -65,6 +82,8 @@ class MoEBlock:
             from ..parallel import ep
 
             out = ep.dispatch_combine(self, x, ids, w)
+        elif self.fp4 is not None:
+            out = ops.moe_experts_nvfp4(x, ids, w, self.fp4[0], self.fp4[1], self.E, self.F)
         else:
             out = ops.moe_experts(x, ids, w, self.w13, self.w2, self.E, self.F)
         if self.shared is not None:

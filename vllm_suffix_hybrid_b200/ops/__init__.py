@@ -491,3 +491,62 @@ def dsa_topk(qi: torch.Tensor, w: torch.Tensor, kcache: torch.Tensor, block_tabl
     native().dsa_topk(out, ws[:T, :max_keys], qi.contiguous(), w.float().contiguous(), kcache, block_tables,
                       seq_lens, q_start)
     return out
+
+
+def nvfp4_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, global_scale: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x W^T with W in NVFP4 (tcgen05 W4A16 kernel on CUDA; dequantised reference on CPU)."""
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    N = packed.shape[0]
+    if not x.is_cuda:
+        w = ref.nvfp4_dequantize(packed, scales, global_scale).to(x.dtype)
+        y = x2 @ w.t()
+        return y.view(*lead, N)
+    if x2.stride(-1) != 1 or (x2.stride(0) * 2) % 16 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    y = out.view(M, N) if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    if M:
+        bn = 64 if M <= 64 else (128 if M <= 128 else 256)
+        native().gemm_nvfp4(y, x2, packed, scales.view(torch.uint8), global_scale.float().reshape(-1), bn)
+    return y.view(*lead, N)
+
+
+def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
+    """moe_experts with NVFP4 expert weights: w13q = (packed [E*2F, H/2], scales [E*2F, H/16], global [E]),
+    w2q = (packed [E*H, F/2], scales [E*H, F/16], global [E]); the grouped GEMMs run the W4A16 tcgen05
+    kernel, each expert's rows scaled by its global scale."""
+    T, H = x.shape
+    if not x.is_cuda:
+        w13 = torch.cat([ref.nvfp4_dequantize(w13q[0][e * 2 * F:(e + 1) * 2 * F], w13q[1][e * 2 * F:(e + 1) * 2 * F],
+                                              w13q[2][e:e + 1]) for e in range(E)]).to(x.dtype)
+        w2 = torch.cat([ref.nvfp4_dequantize(w2q[0][e * H:(e + 1) * H], w2q[1][e * H:(e + 1) * H], w2q[2][e:e + 1])
+                        for e in range(E)]).to(x.dtype)
+        return moe_experts(x, ids, weights, w13, w2, E, F, out=out)
+    k = ids.shape[1]
+    dev = x.device
+    pairs = T * k
+    bn = 64 if pairs <= E * 64 else 128
+    max_groups = E + pairs // bn + 1
+    C = native()
+    rank = torch.empty(pairs, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    sorted_pos = torch.empty(pairs, dtype=torch.int32, device=dev)
+    sorted_token = torch.zeros(pairs, dtype=torch.int32, device=dev)
+    groups = torch.empty(max_groups, 4, dtype=torch.int32, device=dev)
+    ngroups = torch.empty(1, dtype=torch.int32, device=dev)
+    C.moe_align(ids, rank, offsets, sorted_pos, sorted_token, groups, ngroups, E, bn, 2 * F)
+    xs = torch.empty(pairs, H, dtype=x.dtype, device=dev)
+    C.moe_gather(xs, x, sorted_token, offsets[E:])
+    gu = torch.empty(pairs, 2 * F, dtype=x.dtype, device=dev)
+    C.gemm_nvfp4(gu, xs, w13q[0], w13q[1].view(torch.uint8), w13q[2], bn, groups, ngroups, 2 * F)
+    a = silu_mul(gu)
+    groups2 = groups.clone()
+    groups2[:, 2] = groups[:, 3] * H
+    ys = torch.empty(pairs, H, dtype=x.dtype, device=dev)
+    C.gemm_nvfp4(ys, a, w2q[0], w2q[1].view(torch.uint8), w2q[2], bn, groups2, ngroups, H)
+    if out is None:
+        out = torch.empty(T, H, dtype=x.dtype, device=dev)
+    C.moe_combine(out, ys, sorted_pos, weights, False)
+    return out

@@ -28,5 +28,8 @@ def dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -
     T, H = x.shape
     ids_l, w_l = local_routes(ids, w, st.ep_rank * moe.E_local, moe.E_local)
     out = comm.partial_out(T, H, x, force=True)
-    out = ops.moe_experts(x, ids_l, w_l, moe.w13, moe.w2, moe.E_local, moe.F, out=out)
+    if moe.fp4 is not None:
+        out = ops.moe_experts_nvfp4(x, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F, out=out)
+    else:
+        out = ops.moe_experts(x, ids_l, w_l, moe.w13, moe.w2, moe.E_local, moe.F, out=out)
     return comm.all_reduce(out, force=True)
