@@ -80,6 +80,48 @@ def sweep(name, x, w, y, flush, iters):
                                               for t, p, s, b, k in rows[:6]]}))
 
 
+NVFP4_SHAPES = [  # (name, M, N, K): DeepSeek-V3-style decode projections and one expert
+    ("q_b_m192", 192, 24576, 1536),
+    ("o_m192", 192, 7168, 16384),
+    ("expert_gate_up_m64", 64, 4096, 7168),
+    ("expert_down_m64", 64, 7168, 2048),
+    ("dense_gate_up_m192", 192, 36864, 7168),
+]
+
+
+def nvfp4_main(a):
+    from vllm_suffix_hybrid_b200 import ops
+    from vllm_suffix_hybrid_b200.ops.gemm import tcgen05_linear
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    only = set(filter(None, a.only.split(",")))
+    for name, M, N, K in NVFP4_SHAPES:
+        if only and name not in only:
+            continue
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02)
+        p, s, g = ops.nvfp4_quantize(w)
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        run = lambda: ops.nvfp4_linear(x, p, s, g, out=y)
+        if a.once:
+            run()
+            run()
+            torch.cuda.synchronize()
+            print(json.dumps({"once": name}))
+            continue
+        t4 = time_fn(run, flush, a.iters)
+        wd = ops.nvfp4_dequantize(p, s, g)
+        t16 = time_fn(lambda: tcgen05_linear(x, wd, y), flush, a.iters)
+        tlib = time_fn(lambda: torch.matmul(x, wd.t(), out=y), flush, a.iters)
+        ref = x.float() @ wd.float().t()
+        err = (ops.nvfp4_linear(x, p, s, g).float() - ref).abs().max().item()
+        packed = N * K // 2 + N * K // 16
+        print(json.dumps({"shape": name, "M": M, "N": N, "K": K, "nvfp4_us": round(t4, 2),
+                          "bf16_tcgen05_us": round(t16, 2), "cublas_bf16_us": round(tlib, 2),
+                          "packed_weight_gbs": round(packed / t4 / 1e3, 1), "speedup_vs_cublas_bf16": round(tlib / t4, 2),
+                          "max_abs_err_vs_dequantised": err}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", action="store_true")
@@ -90,7 +132,11 @@ def main():
     ap.add_argument("--once", action="store_true",
                     help="no timing: two eager launches of ours then cuBLAS per shape (for ncu captures)")
     ap.add_argument("--config", default="", help="force pair,swap,bn,splits (e.g. 1,0,256,1)")
+    ap.add_argument("--nvfp4", action="store_true",
+                    help="NVFP4-weight (W4A16) kernel vs the bf16 paths on decode shapes (packed-weight GB/s)")
     a = ap.parse_args()
+    if a.nvfp4:
+        return nvfp4_main(a)
     from vllm_suffix_hybrid_b200.ops.gemm import plan, tcgen05_linear
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
