@@ -309,14 +309,15 @@ void dsa_topk(torch::Tensor topk, torch::Tensor logits, torch::Tensor q, torch::
 // NVFP4-weight GEMM (W4A16): y[t, n] = x[t] . dequant(W[n]); grouped MoE mode with `groups`.
 void gemm_nvfp4(torch::Tensor y, torch::Tensor x, torch::Tensor packed, torch::Tensor scales, torch::Tensor gscale,
                 int64_t bn, c10::optional<torch::Tensor> groups, c10::optional<torch::Tensor> num_groups,
-                int64_t rows_p, c10::optional<torch::Tensor> err) {
+                int64_t rows_p, c10::optional<torch::Tensor> err, int64_t splits, c10::optional<torch::Tensor> ws) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "gemm_nvfp4: x");
   TORCH_CHECK(packed.scalar_type() == at::kByte && packed.is_contiguous() && scales.is_contiguous() &&
                   scales.element_size() == 1 && gscale.scalar_type() == at::kFloat, "gemm_nvfp4: weights");
   TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.stride(1) == 1, "gemm_nvfp4: y");
   const int64_t K = x.size(1);
-  TORCH_CHECK(packed.size(1) * 2 == K && scales.size(1) * 16 == K && packed.size(0) == scales.size(0),
-              "gemm_nvfp4: shapes");
+  // scales: k-block-major [K/64, rows_pad, 4] (see ops.nvfp4_kmajor_scales)
+  TORCH_CHECK(packed.size(1) * 2 == K && scales.dim() == 3 && scales.size(0) * 64 == K && scales.size(2) == 4 &&
+                  scales.size(1) >= packed.size(0) && scales.size(1) % 128 == 0, "gemm_nvfp4: shapes");
   static int num_sms = 0;
   if (!num_sms) num_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
   Fp4GemmParams g{};
@@ -326,6 +327,7 @@ void gemm_nvfp4(torch::Tensor y, torch::Tensor x, torch::Tensor packed, torch::T
   g.out = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
   g.ldo = y.stride(0);
   g.rows_total = static_cast<int>(packed.size(0));
+  g.rows_pad = static_cast<int>(scales.size(1));
   g.K = static_cast<int>(K);
   g.err = err.has_value() ? err->data_ptr<int>() : nullptr;
   if (groups.has_value()) {
@@ -335,8 +337,13 @@ void gemm_nvfp4(torch::Tensor y, torch::Tensor x, torch::Tensor packed, torch::T
     g.max_groups = static_cast<int>(groups->size(0));
     g.rows_p = static_cast<int>(rows_p);
   }
+  if (splits > 1) {
+    TORCH_CHECK(ws.has_value() && ws->scalar_type() == at::kFloat && ws->numel() >= splits * x.size(0) * packed.size(0),
+                "gemm_nvfp4: split workspace");
+    g.ws = ws->data_ptr<float>();
+  }
   const int r = sh_gemm_nvfp4(&g, x.data_ptr(), static_cast<int>(x.size(0)), x.stride(0), static_cast<int>(bn),
-                              num_sms, at::cuda::getCurrentCUDAStream());
+                              static_cast<int>(splits), num_sms, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_gemm_nvfp4 failed with code ", r);
 }
 
@@ -525,7 +532,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dsa_topk", &dsa_topk);
   m.def("gemm_nvfp4", &gemm_nvfp4, py::arg("y"), py::arg("x"), py::arg("packed"), py::arg("scales"),
         py::arg("gscale"), py::arg("bn"), py::arg("groups") = py::none(), py::arg("num_groups") = py::none(),
-        py::arg("rows_p") = 0, py::arg("err") = py::none());
+        py::arg("rows_p") = 0, py::arg("err") = py::none(), py::arg("splits") = 1, py::arg("ws") = py::none());
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("moe_route", &moe_route);

@@ -58,11 +58,21 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t par) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread in hardware (up to hint_ns) until the phase completes.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* b, uint32_t par, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(par), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t par, volatile int* abort_flag) {
   if (mbar_try(b, par)) return true;
   const uint64_t t0 = now_ns();
   while (true) {
-    if (mbar_try(b, par)) return true;
+    if (mbar_try_sleep(b, par, 10000)) return true;
     if (*abort_flag) return false;
     if (now_ns() - t0 > kTimeoutNs) return false;
   }

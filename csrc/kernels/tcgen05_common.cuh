@@ -39,19 +39,31 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: false on timeout or when another role already aborted.
+// try_wait that may suspend the thread in hardware for up to `hint_ns` until the
+// phase completes: a waiting role issues no instructions while it sleeps.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false on timeout or when another role already aborted.  The
+// loop sleeps in try_wait (10 us hint) between the abort / timer checks.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = now_ns();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_sleep(bar, parity, 10000)) return true;
     if (*abort_flag) return false;
     if (now_ns() - t0 > kTimeoutNs) return false;
   }
 }
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = now_ns();
-  while (!mbar_try(bar, parity))
+  while (!mbar_try_sleep(bar, parity, 10000))
     if (now_ns() - t0 > kTimeoutNs) return false;
   return true;
 }

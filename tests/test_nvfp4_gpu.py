@@ -75,3 +75,19 @@ def test_nvfp4_moe_experts_match_bf16_path():
     torch.cuda.synchronize()
     err = (got.float() - want.float()).abs().max().item()
     assert err <= 0.03 * want.float().abs().max().item() + 0.02, err
+
+
+def test_nvfp4_linear_decodes_every_code_exactly():
+    """One-hot activations read single dequantised weights back: every e2m1 code (the subnormal 0.5
+    included) times every block scale must come out exact."""
+    torch.manual_seed(5)
+    N, K = 256, 128
+    w = (torch.randn(N, K) * 0.05).to(torch.bfloat16)
+    w[0, :16] = torch.tensor([0.0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.0, -0.5, -1, -1.5, -2, -3, -4, -6]) * 0.01
+    g = ref.nvfp4_global_scale(w)
+    p, s = ref.nvfp4_quantize(w, g)
+    want = ref.nvfp4_dequantize(p, s, torch.ones(1)).float()  # code * block scale (global applied below)
+    x = torch.eye(K).to(torch.bfloat16)
+    got = ops.nvfp4_linear(x.cuda(), p.cuda(), s.cuda(), torch.ones(1).cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(got.float().cpu(), want.t()), (got.float().cpu() - want.t()).abs().max()

@@ -201,6 +201,8 @@ def _moe(ck: Checkpoint, pre: str, moe, shared_name: str) -> None:
         d = ck.matrix(base + "down_proj")
         _copy(moe.w13[j * 2 * F:(j + 1) * 2 * F], torch.cat([g, u], 0), f"{pre}experts.{e}.gate|up")
         _copy(moe.w2[j * H:(j + 1) * H], d, f"{pre}experts.{e}.down")
+    if getattr(moe, "fp4", None) is not None:
+        moe.refresh()
     if moe.shared is not None:
         sp = pre + shared_name + "."
         moe.shared.gate_up.load(torch.cat([ck.matrix(sp + "gate_proj"), ck.matrix(sp + "up_proj")], 0))
@@ -215,7 +217,7 @@ def _fp4_expert(ck: Checkpoint, moe, j: int, base: str) -> None:
     from .. import ops
 
     F, H = moe.F, moe.H
-    (p13, s13, g13), (p2, s2, g2) = moe.fp4
+    (p13, s13, g13), (p2, s2, g2) = moe.fp4[0][:3], moe.fp4[1][:3]
     gname, uname, dname = base + "gate_proj", base + "up_proj", base + "down_proj"
     if ck.is_nvfp4(gname) and ck.is_nvfp4(uname) and \
             float(ck.get(gname + ".weight_scale_2")) == float(ck.get(uname + ".weight_scale_2")):
@@ -337,6 +339,7 @@ def _qlinear(ck: Checkpoint, base: str, lin, transform=None) -> None:
         lin.packed.copy_(p.to(lin.packed.device))
         lin.scales.copy_(s.to(lin.scales.device))
         lin.gscale.copy_(g.to(lin.gscale.device))
+        lin.refresh()
         return
     full = ck.matrix(base)
     if transform is not None:

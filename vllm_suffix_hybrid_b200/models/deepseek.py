@@ -44,6 +44,7 @@ class QLinear:
         self.out_f, self.in_f, self.dtype = out_f, in_f, dtype
         if self.fmt == "nvfp4":
             self.packed, self.scales, self.gscale = ops.nvfp4_quantize(w)
+            self.scales_k = ops.nvfp4_kmajor_scales(self.scales) if self.packed.is_cuda else None
             self._w = None
             if self.packed.is_cuda:
                 key = self.packed.device
@@ -64,8 +65,13 @@ class QLinear:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         if self.fmt == "nvfp4" and x.is_cuda and x.dtype == torch.bfloat16 and self.in_f % 64 == 0:
-            return ops.nvfp4_linear(x, self.packed, self.scales, self.gscale)  # W4A16 tcgen05 kernel
+            return ops.nvfp4_linear(x, self.packed, self.scales, self.gscale, scales_k=self.scales_k)  # W4A16 kernel
         return ops.linear(x, self.weight)
+
+    def refresh(self) -> None:
+        """Rebuild the kernels' k-block-major scale copy after the packed weights changed."""
+        if self.fmt == "nvfp4" and self.packed.is_cuda:
+            self.scales_k = ops.nvfp4_kmajor_scales(self.scales)
 
     def load(self, full: torch.Tensor) -> None:
         """Replace the weight by a full [out, in] matrix (re-quantised when the layer is NVFP4)."""
@@ -76,6 +82,7 @@ class QLinear:
             self.packed.copy_(p)
             self.scales.copy_(sc)
             self.gscale.copy_(g)
+            self.refresh()
         else:
             self._w.copy_(full.to(self._w.device, self._w.dtype))
 

@@ -66,7 +66,13 @@ class MoEBlock:
             packed.append(p)
             scales.append(sc)
             gs.append(g.reshape(1).float())
-        return torch.cat(packed), torch.cat(scales), torch.cat(gs)
+        sc = torch.cat(scales)
+        return torch.cat(packed), sc, torch.cat(gs), ops.nvfp4_kmajor_scales(sc)
+
+    def refresh(self) -> None:
+        """Rebuild the k-block-major scale copies after the NVFP4 experts changed (checkpoint load)."""
+        if self.fp4 is not None:
+            self.fp4 = tuple(q[:3] + (ops.nvfp4_kmajor_scales(q[1]),) for q in self.fp4)
 
     def route(self, x: torch.Tensor):
         logits = ops.linear(x, self.gate).float() if not x.is_cuda else ops.linear(x, self.gate)

@@ -493,9 +493,23 @@ def dsa_topk(qi: torch.Tensor, w: torch.Tensor, kcache: torch.Tensor, block_tabl
     return out
 
 
+def nvfp4_kmajor_scales(scales: torch.Tensor) -> torch.Tensor:
+    """ModelOpt block scales [N, K/16] -> the kernels' k-block-major layout [K/64, N_pad, 4] (N_pad: next
+    multiple of 128), so one 64-wide k-block's scales of a 128-row tile are one contiguous 512-byte copy."""
+    N, kb16 = scales.shape
+    n_pad = -(-N // 128) * 128
+    s8 = scales.view(torch.uint8).view(N, kb16 // 4, 4).permute(1, 0, 2)
+    out = torch.zeros(kb16 // 4, n_pad, 4, dtype=torch.uint8, device=scales.device)
+    out[:, :N] = s8
+    return out
+
+
 def nvfp4_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, global_scale: torch.Tensor,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
-    """y = x W^T with W in NVFP4 (tcgen05 W4A16 kernel on CUDA; dequantised reference on CPU)."""
+                 out: torch.Tensor | None = None, scales_k: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x W^T with W in NVFP4 (tcgen05 W4A16 kernel on CUDA; dequantised reference on CPU).
+
+    The kernel reads the block scales in the k-block-major layout (`nvfp4_kmajor_scales`); layers keep
+    that copy with their weights and pass it as scales_k (computed here otherwise)."""
     lead = x.shape[:-1]
     x2 = x.reshape(-1, x.shape[-1])
     N = packed.shape[0]
@@ -509,13 +523,23 @@ def nvfp4_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, gl
     y = out.view(M, N) if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
     if M:
         bn = 64 if M <= 64 else (128 if M <= 128 else 256)
-        native().gemm_nvfp4(y, x2, packed, scales.view(torch.uint8), global_scale.float().reshape(-1), bn)
+        # split-K while the (weight tile x token tile) grid covers under half the SMs
+        tiles = -(-N // 128) * -(-M // bn)
+        kb = x2.shape[1] // 64
+        splits = 1
+        while tiles * splits * 2 <= 148 and kb // (splits * 2) >= 4 and splits < 16:
+            splits *= 2
+        from .gemm import workspace
+
+        ws = workspace(x.device, splits * M * N) if splits > 1 else None
+        sk = scales_k if scales_k is not None else nvfp4_kmajor_scales(scales)
+        native().gemm_nvfp4(y, x2, packed, sk, global_scale.float().reshape(-1), bn, splits=splits, ws=ws)
     return y.view(*lead, N)
 
 
 def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
-    """moe_experts with NVFP4 expert weights: w13q = (packed [E*2F, H/2], scales [E*2F, H/16], global [E]),
-    w2q = (packed [E*H, F/2], scales [E*H, F/16], global [E]); the grouped GEMMs run the W4A16 tcgen05
+    """moe_experts with NVFP4 expert weights: w13q = (packed [E*2F, H/2], scales [E*2F, H/16], global [E],
+    optional k-block-major scales), w2q likewise for [E*H, F]; the grouped GEMMs run the W4A16 tcgen05
     kernel, each expert's rows scaled by its global scale."""
     T, H = x.shape
     if not x.is_cuda:
@@ -540,12 +564,14 @@ def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
     xs = torch.empty(pairs, H, dtype=x.dtype, device=dev)
     C.moe_gather(xs, x, sorted_token, offsets[E:])
     gu = torch.empty(pairs, 2 * F, dtype=x.dtype, device=dev)
-    C.gemm_nvfp4(gu, xs, w13q[0], w13q[1].view(torch.uint8), w13q[2], bn, groups, ngroups, 2 * F)
+    sk13 = w13q[3] if len(w13q) > 3 else nvfp4_kmajor_scales(w13q[1])
+    sk2 = w2q[3] if len(w2q) > 3 else nvfp4_kmajor_scales(w2q[1])
+    C.gemm_nvfp4(gu, xs, w13q[0], sk13, w13q[2], bn, groups, ngroups, 2 * F)
     a = silu_mul(gu)
     groups2 = groups.clone()
     groups2[:, 2] = groups[:, 3] * H
     ys = torch.empty(pairs, H, dtype=x.dtype, device=dev)
-    C.gemm_nvfp4(ys, a, w2q[0], w2q[1].view(torch.uint8), w2q[2], bn, groups2, ngroups, H)
+    C.gemm_nvfp4(ys, a, w2q[0], sk2, w2q[2], bn, groups2, ngroups, H)
     if out is None:
         out = torch.empty(T, H, dtype=x.dtype, device=dev)
     C.moe_combine(out, ys, sorted_pos, weights, False)
