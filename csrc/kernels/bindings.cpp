@@ -7,6 +7,7 @@
 #include "gdn.h"
 #include "moe.h"
 #include "mla.h"
+#include "gemm_fp4mma.h"
 #include "gemm_nvfp4.h"
 #include "paged_attention.h"
 
@@ -347,6 +348,93 @@ void gemm_nvfp4(torch::Tensor y, torch::Tensor x, torch::Tensor packed, torch::T
   TORCH_CHECK(r == 0, "sh_gemm_nvfp4 failed with code ", r);
 }
 
+// NVFP4 activation quantiser (see sh_nvfp4_quant_act): x bf16 [rows, K] ->
+// xq uint8 [rows, K/2], x_sf uint8 [tiles, kc4, 512], a_scale fp32 [rows].
+void nvfp4_quant_act(torch::Tensor x, torch::Tensor xq, torch::Tensor x_sf, torch::Tensor a_scale, int64_t tile_rows,
+                     double static_g, c10::optional<torch::Tensor> groups, c10::optional<torch::Tensor> num_groups) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
+              "nvfp4_quant_act: x bf16 [rows, K]");
+  const int64_t rows = x.size(0), K = x.size(1);
+  TORCH_CHECK(xq.scalar_type() == at::kByte && xq.is_contiguous() && xq.size(0) >= rows && xq.size(1) * 2 == K,
+              "nvfp4_quant_act: xq uint8 [rows, K/2]");
+  const int64_t kc4 = (K + 255) / 256 * 4;
+  TORCH_CHECK(x_sf.element_size() == 1 && x_sf.is_contiguous() && x_sf.dim() == 3 && x_sf.size(1) == kc4 &&
+                  x_sf.size(2) == 512, "nvfp4_quant_act: x_sf [tiles, kc4, 512]");
+  TORCH_CHECK(a_scale.scalar_type() == at::kFloat && a_scale.numel() >= rows, "nvfp4_quant_act: a_scale");
+  const int4* gp = nullptr;
+  const int* ng = nullptr;
+  int64_t max_tiles = (rows + tile_rows - 1) / tile_rows;
+  if (groups.has_value()) {
+    TORCH_CHECK(num_groups.has_value() && groups->scalar_type() == at::kInt && groups->size(1) == 4,
+                "nvfp4_quant_act: groups");
+    gp = reinterpret_cast<const int4*>(groups->data_ptr<int>());
+    ng = num_groups->data_ptr<int>();
+    max_tiles = groups->size(0);
+  }
+  TORCH_CHECK(x_sf.size(0) >= max_tiles, "nvfp4_quant_act: x_sf has too few tiles");
+  const int r = sh_nvfp4_quant_act(x.data_ptr(), x.stride(0), static_cast<int>(rows), static_cast<int>(K), gp, ng,
+                                   static_cast<int>(max_tiles), static_cast<int>(tile_rows),
+                                   static_cast<float>(static_g), xq.data_ptr<uint8_t>(),
+                                   reinterpret_cast<uint8_t*>(x_sf.data_ptr()), a_scale.data_ptr<float>(),
+                                   at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_nvfp4_quant_act failed with code ", r);
+}
+
+// Block-scaled W4A4 GEMM (see sh_gemm_fp4mma): y[t, n] = alpha_w * a_scale[t] * (xq sx) . (w sw).
+void gemm_fp4mma(torch::Tensor y, torch::Tensor xq, torch::Tensor x_sf, torch::Tensor a_scale, torch::Tensor w,
+                 torch::Tensor w_sf, torch::Tensor alpha_w, int64_t bn, c10::optional<torch::Tensor> groups,
+                 c10::optional<torch::Tensor> num_groups, int64_t rows_p, c10::optional<torch::Tensor> err,
+                 int64_t splits, c10::optional<torch::Tensor> ws, c10::optional<torch::Tensor> counters) {
+  TORCH_CHECK(xq.is_cuda() && xq.scalar_type() == at::kByte && xq.is_contiguous() && xq.dim() == 2, "gemm_fp4mma: xq");
+  TORCH_CHECK(w.scalar_type() == at::kByte && w.is_contiguous() && w.size(1) == xq.size(1), "gemm_fp4mma: w");
+  const int64_t K = xq.size(1) * 2, kc4 = (K + 255) / 256 * 4;
+  TORCH_CHECK(w_sf.element_size() == 1 && w_sf.is_contiguous() && w_sf.dim() == 3 && w_sf.size(1) == kc4 &&
+                  w_sf.size(2) == 512 && x_sf.element_size() == 1 && x_sf.is_contiguous() && x_sf.dim() == 3 &&
+                  x_sf.size(1) == kc4, "gemm_fp4mma: scale tiles [tiles, kc4, 512]");
+  TORCH_CHECK(alpha_w.scalar_type() == at::kFloat && a_scale.scalar_type() == at::kFloat &&
+                  a_scale.numel() >= xq.size(0), "gemm_fp4mma: scales");
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.stride(1) == 1 && y.size(0) >= xq.size(0), "gemm_fp4mma: y");
+  static int num_sms = 0;
+  if (!num_sms) num_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  Fp4MmaParams g{};
+  g.w = w.data_ptr<uint8_t>();
+  g.w_sf = reinterpret_cast<const uint8_t*>(w_sf.data_ptr());
+  g.alpha_w = alpha_w.data_ptr<float>();
+  g.x_sf = reinterpret_cast<const uint8_t*>(x_sf.data_ptr());
+  g.a_scale = a_scale.data_ptr<float>();
+  g.out = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  g.ldo = y.stride(0);
+  g.rows_total = static_cast<int>(w.size(0));
+  g.K = static_cast<int>(K);
+  g.err = err.has_value() ? err->data_ptr<int>() : nullptr;
+  const int64_t rows_m = groups.has_value() ? rows_p : w.size(0);
+  TORCH_CHECK(w_sf.size(0) >= (groups.has_value() ? (w.size(0) / rows_p) : 1) * ((rows_m + 127) / 128),
+              "gemm_fp4mma: w_sf has too few tiles");
+  if (groups.has_value()) {
+    TORCH_CHECK(num_groups.has_value() && groups->scalar_type() == at::kInt && groups->size(1) == 4 && rows_p > 0 &&
+                    w.size(0) % rows_p == 0, "gemm_fp4mma: groups");
+    TORCH_CHECK(x_sf.size(0) >= groups->size(0), "gemm_fp4mma: one activation scale tile per group entry");
+    g.groups = reinterpret_cast<const int4*>(groups->data_ptr<int>());
+    g.num_groups = num_groups->data_ptr<int>();
+    g.max_groups = static_cast<int>(groups->size(0));
+    g.rows_p = static_cast<int>(rows_p);
+  } else {
+    TORCH_CHECK(x_sf.size(0) >= (xq.size(0) + bn - 1) / bn, "gemm_fp4mma: activation scale tiles of bn rows");
+  }
+  if (splits > 1 && !groups.has_value()) {
+    const int64_t tiles = ((w.size(0) + 127) / 128) * ((xq.size(0) + bn - 1) / bn);
+    TORCH_CHECK(ws.has_value() && ws->scalar_type() == at::kFloat && ws->numel() >= splits * tiles * 128 * bn,
+                "gemm_fp4mma: split workspace of splits * tiles * 128 * bn floats");
+    TORCH_CHECK(counters.has_value() && counters->scalar_type() == at::kInt && counters->numel() >= tiles,
+                "gemm_fp4mma: split tickets (zeroed int32 per output tile)");
+    g.ws = ws->data_ptr<float>();
+    g.counters = counters->data_ptr<int>();
+  }
+  const int r = sh_gemm_fp4mma(&g, xq.data_ptr(), static_cast<int>(xq.size(0)), static_cast<int>(bn),
+                               static_cast<int>(splits), num_sms, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_gemm_fp4mma failed with code ", r);
+}
+
 template <typename T>
 static T* ptr(const torch::Tensor& t) {
   return reinterpret_cast<T*>(t.data_ptr());
@@ -533,6 +621,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_nvfp4", &gemm_nvfp4, py::arg("y"), py::arg("x"), py::arg("packed"), py::arg("scales"),
         py::arg("gscale"), py::arg("bn"), py::arg("groups") = py::none(), py::arg("num_groups") = py::none(),
         py::arg("rows_p") = 0, py::arg("err") = py::none(), py::arg("splits") = 1, py::arg("ws") = py::none());
+  m.def("nvfp4_quant_act", &nvfp4_quant_act, py::arg("x"), py::arg("xq"), py::arg("x_sf"), py::arg("a_scale"),
+        py::arg("tile_rows"), py::arg("static_g") = 0.0, py::arg("groups") = py::none(),
+        py::arg("num_groups") = py::none());
+  m.def("gemm_fp4mma", &gemm_fp4mma, py::arg("y"), py::arg("xq"), py::arg("x_sf"), py::arg("a_scale"), py::arg("w"),
+        py::arg("w_sf"), py::arg("alpha_w"), py::arg("bn"), py::arg("groups") = py::none(),
+        py::arg("num_groups") = py::none(), py::arg("rows_p") = 0, py::arg("err") = py::none(),
+        py::arg("splits") = 1, py::arg("ws") = py::none(), py::arg("counters") = py::none());
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("moe_route", &moe_route);

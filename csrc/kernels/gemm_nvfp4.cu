@@ -241,7 +241,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     // (exponent 0 gives the bf16 subnormal m * 2^-127); two exact bf16x2 multiplies, by 2^63 and by
     // block_scale * 2^63, restore code_value * block_scale (at most 7 significant bits: exact in bf16).
     const int ct = threadIdx.x - 6 * 32;
-    const int row = ct & (BM - 1), part = ct >> 7;  // part p: elements 16p .. 16p+15 of the k-block
+    // four consecutive lanes share a row (part p: elements 16p .. 16p+15 of the k-block), so a warp
+    // reads 256 contiguous packed bytes and its 16-byte stores hit distinct banks per quarter-warp
+    const int row = ct >> 2, part = ct & 3;
     const __nv_bfloat162 two63 = __halves2bfloat162(__float2bfloat16(9.223372036854775808e18f),
                                                     __float2bfloat16(9.223372036854775808e18f));
     int ps = 0, ws = 0;
@@ -320,10 +322,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int q0 = wk.q_base + c;
         if (g.splits > 1) {
           float* dst = g.ws + (static_cast<int64_t>(wk.sp) * g.rows_q) * g.rows_total + n;
-          for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i) dst[static_cast<int64_t>(q0 + i) * g.rows_total] = v[i] * gs;
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (q0 + i < wk.q_lim) dst[static_cast<int64_t>(q0 + i) * g.rows_total] = v[i] * gs;
         } else {
-          for (int i = 0; i < 16 && q0 + i < wk.q_lim; ++i)
-            g.out[static_cast<int64_t>(q0 + i) * g.ldo + n] = __float2bfloat16(v[i] * gs);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (q0 + i < wk.q_lim) g.out[static_cast<int64_t>(q0 + i) * g.ldo + n] = __float2bfloat16(v[i] * gs);
         }
       }
       fence_before();

@@ -98,3 +98,27 @@ def test_deepseek_engines_on_gpu(name):
         agree = np.mean([a == b for a, b in zip(got, base)])
         assert agree >= 2 / 3, (key, got, base)  # bf16 verify vs one-token decode may flip a near-tie
         assert all(len(g) == 12 for g in got)
+
+
+@pytest.mark.parametrize("act", ["fp4", "bf16"])
+def test_deepseek_nvfp4_spec_is_exact_in_batch_invariant_mode(monkeypatch, act):
+    """NVFP4 DeepSeek on the block-scaled W4A4 path (act=fp4: per-token NVFP4 activations) and on the
+    W4A16 path: in batch-invariant mode a k+1-token verify window reproduces one-token decoding exactly,
+    eager and CUDA-graph."""
+    from vllm_suffix_hybrid_b200.engine.config import (CacheConfig, EngineConfig, SpecConfig, deepseek_v32_config,
+                                                       shrink)
+    from vllm_suffix_hybrid_b200.engine.llm import LLMEngine
+
+    monkeypatch.setenv("SH_BATCH_INVARIANT", "1")
+    monkeypatch.setenv("SH_NVFP4_ACT", act)
+    m = shrink(deepseek_v32_config(), layers=3, hidden=256, vocab=1024)
+    rng = np.random.default_rng(6)
+    prompts = [rng.integers(0, 1024, int(n)) for n in (90, 40, 130)]
+    outs = {}
+    for method, graphs in (("none", False), ("hybrid", False), ("hybrid", True)):
+        cfg = EngineConfig(model=m, spec=SpecConfig(method=method, k=3), cache=CacheConfig(max_model_len=512),
+                           max_num_seqs=4, device="cuda", cuda_graphs=graphs)
+        outs[(method, graphs)] = LLMEngine(cfg).generate(prompts, max_new_tokens=12)
+    base = outs[("none", False)]
+    for key, got in outs.items():
+        assert got == base, (key, got, base)

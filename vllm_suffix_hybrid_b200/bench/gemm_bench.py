@@ -86,6 +86,7 @@ NVFP4_SHAPES = [  # (name, M, N, K): DeepSeek-V3-style decode projections and on
     ("expert_gate_up_m64", 64, 4096, 7168),
     ("expert_down_m64", 64, 7168, 2048),
     ("dense_gate_up_m192", 192, 36864, 7168),
+    ("one_kblock_m64", 64, 4096, 256),  # launch + prologue + epilogue floor
 ]
 
 
@@ -102,24 +103,46 @@ def nvfp4_main(a):
         w = (torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02)
         p, s, g = ops.nvfp4_quantize(w)
         y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        w_sf = ops.nvfp4_scale_tiles(s)
         run = lambda: ops.nvfp4_linear(x, p, s, g, out=y)
+        run44 = lambda: ops.nvfp4_linear_w4a4(x, p, w_sf, s, g, out=y)
         if a.once:
-            run()
-            run()
+            (run44 if a.w4a4 else run)()
+            (run44 if a.w4a4 else run)()
             torch.cuda.synchronize()
-            print(json.dumps({"once": name}))
+            print(json.dumps({"once": name, "w4a4": bool(a.w4a4)}))
             continue
         t4 = time_fn(run, flush, a.iters)
+        t44 = time_fn(run44, flush, a.iters)  # includes the activation quantiser launch
+        bn44 = 64 if M <= 64 else 128
+        xq, x_sf, a_sc = ops.nvfp4_quant_act(x, bn44)
+        xq, x_sf, a_sc = xq.clone(), x_sf.clone(), a_sc.clone()
+        tq = time_fn(lambda: ops.nvfp4_quant_act(x, bn44), flush, a.iters)
+        gsc = g.float().reshape(-1)
+        t_g1 = time_fn(lambda: ops.native().gemm_fp4mma(y, xq, x_sf, a_sc, p, w_sf, gsc, bn44), flush, a.iters)
+        from vllm_suffix_hybrid_b200.ops.gemm import workspace
+        ntile = -(-N // 128) * -(-M // bn44)
+        wsp = workspace(x.device, 8 * ntile * 128 * bn44)
+        cnt = ops.split_tickets(x.device, ntile)
+        t_split = {sp: round(time_fn(lambda: ops.native().gemm_fp4mma(y, xq, x_sf, a_sc, p, w_sf, gsc, bn44,
+                                                                      splits=sp, ws=wsp, counters=cnt),
+                                     flush, a.iters), 2)
+                   for sp in (2, 4, 8)}
         wd = ops.nvfp4_dequantize(p, s, g)
         t16 = time_fn(lambda: tcgen05_linear(x, wd, y), flush, a.iters)
         tlib = time_fn(lambda: torch.matmul(x, wd.t(), out=y), flush, a.iters)
         ref = x.float() @ wd.float().t()
         err = (ops.nvfp4_linear(x, p, s, g).float() - ref).abs().max().item()
+        ref44 = ops.reference.nvfp4_w4a4_linear(x.cpu(), p.cpu(), s.cpu(), g.cpu()) if M * N * K <= (1 << 31) else None
+        err44 = None if ref44 is None else (ops.nvfp4_linear_w4a4(x, p, w_sf, s, g).float().cpu() - ref44).abs().max().item()
         packed = N * K // 2 + N * K // 16
-        print(json.dumps({"shape": name, "M": M, "N": N, "K": K, "nvfp4_us": round(t4, 2),
+        print(json.dumps({"shape": name, "M": M, "N": N, "K": K, "w4a16_us": round(t4, 2), "w4a4_us": round(t44, 2), "w4a4_quant_us": round(tq, 2),
+                          "w4a4_gemm_nosplit_us": round(t_g1, 2), "w4a4_gemm_split_us": t_split,
                           "bf16_tcgen05_us": round(t16, 2), "cublas_bf16_us": round(tlib, 2),
-                          "packed_weight_gbs": round(packed / t4 / 1e3, 1), "speedup_vs_cublas_bf16": round(tlib / t4, 2),
-                          "max_abs_err_vs_dequantised": err}))
+                          "w4a4_packed_weight_gbs": round(packed / t44 / 1e3, 1),
+                          "w4a4_speedup_vs_cublas_bf16": round(tlib / t44, 2),
+                          "w4a16_speedup_vs_cublas_bf16": round(tlib / t4, 2),
+                          "w4a16_max_abs_err_vs_dequantised": err, "w4a4_max_abs_err_vs_fp32_oracle": err44}))
 
 
 def main():
@@ -132,6 +155,7 @@ def main():
     ap.add_argument("--once", action="store_true",
                     help="no timing: two eager launches of ours then cuBLAS per shape (for ncu captures)")
     ap.add_argument("--config", default="", help="force pair,swap,bn,splits (e.g. 1,0,256,1)")
+    ap.add_argument("--w4a4", action="store_true", help="with --nvfp4 --once: launch the W4A4 kernel")
     ap.add_argument("--nvfp4", action="store_true",
                     help="NVFP4-weight (W4A16) kernel vs the bf16 paths on decode shapes (packed-weight GB/s)")
     a = ap.parse_args()

@@ -339,6 +339,9 @@ def _qlinear(ck: Checkpoint, base: str, lin, transform=None) -> None:
         lin.packed.copy_(p.to(lin.packed.device))
         lin.scales.copy_(s.to(lin.scales.device))
         lin.gscale.copy_(g.to(lin.gscale.device))
+        if ck.has(base + ".input_scale"):  # static activation scale of the W4A4 path
+            isc = float(ck.get(base + ".input_scale").float().reshape(-1).max())
+            lin.static_g = 1.0 / isc if isc > 0 else 0.0
         lin.refresh()
         return
     full = ck.matrix(base)

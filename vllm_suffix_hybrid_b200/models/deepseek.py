@@ -29,8 +29,10 @@ from .moe import MoEBlock
 class QLinear:
     """y = x W^T with W in bf16 or NVFP4.
 
-    NVFP4 linears run the W4A16 tcgen05 kernel (packed weights streamed and
-    decoded in shared memory).  `weight` (the dequantised matrix, for the MLA
+    NVFP4 linears run the block-scaled W4A4 tcgen05 kernel on per-token NVFP4
+    activations (static_g: the checkpoint's 1 / input_scale when it has one,
+    else a per-token dynamic scale); SH_NVFP4_ACT=bf16 selects the W4A16
+    kernel (packed weights decoded in shared memory).  `weight` (the dequantised matrix, for the MLA
     absorption of kv_b) decodes into one scratch tile per device shared by all
     NVFP4 layers (calls are ordered on the stream, so a captured graph replays
     them correctly).
@@ -45,6 +47,8 @@ class QLinear:
         if self.fmt == "nvfp4":
             self.packed, self.scales, self.gscale = ops.nvfp4_quantize(w)
             self.scales_k = ops.nvfp4_kmajor_scales(self.scales) if self.packed.is_cuda else None
+            self.w_sf = ops.nvfp4_scale_tiles(self.scales) if self.packed.is_cuda else None
+            self.static_g = 0.0
             self._w = None
             if self.packed.is_cuda:
                 key = self.packed.device
@@ -64,14 +68,18 @@ class QLinear:
         return ops.nvfp4_dequantize(self.packed, self.scales, self.gscale, out=out)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fmt == "nvfp4" and self.in_f % 64 == 0 and x.dtype == torch.bfloat16 and ops.nvfp4_act_mode() == "fp4":
+            return ops.nvfp4_linear_w4a4(x, self.packed, self.w_sf, self.scales, self.gscale, self.static_g)
         if self.fmt == "nvfp4" and x.is_cuda and x.dtype == torch.bfloat16 and self.in_f % 64 == 0:
             return ops.nvfp4_linear(x, self.packed, self.scales, self.gscale, scales_k=self.scales_k)  # W4A16 kernel
         return ops.linear(x, self.weight)
 
     def refresh(self) -> None:
-        """Rebuild the kernels' k-block-major scale copy after the packed weights changed."""
+        """Rebuild the kernels' scale copies (k-block-major, block-scaled MMA tiles) after the packed
+        weights changed."""
         if self.fmt == "nvfp4" and self.packed.is_cuda:
             self.scales_k = ops.nvfp4_kmajor_scales(self.scales)
+            self.w_sf = ops.nvfp4_scale_tiles(self.scales)
 
     def load(self, full: torch.Tensor) -> None:
         """Replace the weight by a full [out, in] matrix (re-quantised when the layer is NVFP4)."""

@@ -46,7 +46,8 @@ class MoEBlock:
             self.w2[j * cfg.hidden:(j + 1) * cfg.hidden] = init_weight((cfg.hidden, self.F), cfg.init_std, dtype,
                                                                          device, g)
         # NVFP4 experts (weight_format nvfp4 on CUDA): packed codes + block scales + one global
-        # scale per expert matrix; the grouped GEMMs run the W4A16 tcgen05 kernel.
+        # scale per expert matrix; the grouped GEMMs run the block-scaled W4A4 tcgen05 kernel
+        # (SH_NVFP4_ACT=bf16: the W4A16 kernel).
         self.fp4 = None
         if cfg.weight_format == "nvfp4" and torch.device(device).type == "cuda" and dtype == torch.bfloat16 \
                 and cfg.hidden % 64 == 0 and self.F % 64 == 0:
@@ -67,12 +68,15 @@ class MoEBlock:
             scales.append(sc)
             gs.append(g.reshape(1).float())
         sc = torch.cat(scales)
-        return torch.cat(packed), sc, torch.cat(gs), ops.nvfp4_kmajor_scales(sc)
+        return (torch.cat(packed), sc, torch.cat(gs), ops.nvfp4_kmajor_scales(sc), ops.nvfp4_scale_tiles(sc, rows))
 
     def refresh(self) -> None:
-        """Rebuild the k-block-major scale copies after the NVFP4 experts changed (checkpoint load)."""
+        """Rebuild the kernels' scale copies (k-block-major for W4A16, block-scaled MMA tiles for W4A4)
+        after the NVFP4 experts changed (checkpoint load)."""
         if self.fp4 is not None:
-            self.fp4 = tuple(q[:3] + (ops.nvfp4_kmajor_scales(q[1]),) for q in self.fp4)
+            rows = (2 * self.F, self.H)
+            self.fp4 = tuple(q[:3] + (ops.nvfp4_kmajor_scales(q[1]), ops.nvfp4_scale_tiles(q[1], r))
+                             for q, r in zip(self.fp4, rows))
 
     def route(self, x: torch.Tensor):
         logits = ops.linear(x, self.gate).float() if not x.is_cuda else ops.linear(x, self.gate)

@@ -522,9 +522,12 @@ def nvfp4_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, gl
     M = x2.shape[0]
     y = out.view(M, N) if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
     if M:
+        from .gemm import batch_invariant
+
         bn = 64 if M <= 64 else (128 if M <= 128 else 256)
-        # split-K while the (weight tile x token tile) grid covers under half the SMs
-        tiles = -(-N // 128) * -(-M // bn)
+        # split-K while the (weight tile x token tile) grid covers under half the SMs; in batch-invariant
+        # mode the split count (which sets the fp32 summation order) is the one-token-tile choice for every M
+        tiles = -(-N // 128) * (1 if batch_invariant() else -(-M // bn))
         kb = x2.shape[1] // 64
         splits = 1
         while tiles * splits * 2 <= 148 and kb // (splits * 2) >= 4 and splits < 16:
@@ -537,11 +540,143 @@ def nvfp4_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, gl
     return y.view(*lead, N)
 
 
+def nvfp4_act_mode() -> str:
+    """How NVFP4 linears treat activations: "fp4" (default) quantises them to NVFP4 per token and runs
+    the block-scaled W4A4 tensor-core GEMM (the serving math of ModelOpt NVFP4 checkpoints); "bf16"
+    keeps bf16 activations (W4A16 kernel, weights decoded in shared memory).  SH_NVFP4_ACT selects."""
+    return "bf16" if os.environ.get("SH_NVFP4_ACT", "fp4") == "bf16" else "fp4"
+
+
+def nvfp4_scale_tiles(scales: torch.Tensor, rows_per_matrix: int | None = None) -> torch.Tensor:
+    """ModelOpt block scales [R, K/16] -> the block-scaled MMA's scale tiles [R/rows_per_matrix * tiles,
+    kc4, 512] (tiles = ceil(rows_per_matrix / 128) per matrix, kc4 = 4 * ceil(K / 256)): byte
+    (r % 32) * 16 + (r / 32) * 4 + b % 4 of chunk b / 4 holds the scale of row r, 16-block b (zero padded)."""
+    R, kb16 = scales.shape
+    rp = rows_per_matrix or R
+    nm = R // rp
+    tp = -(-rp // 128)
+    kc4 = -(-kb16 // 16) * 4
+    buf = torch.zeros(nm, tp * 128, kc4 * 4, dtype=torch.uint8, device=scales.device)
+    buf[:, :rp, :kb16] = scales.view(torch.uint8).reshape(nm, rp, kb16)
+    return buf.view(nm * tp, 4, 32, kc4, 4).permute(0, 3, 2, 1, 4).contiguous().view(nm * tp, kc4, 512)
+
+
+_FP4_ACT: dict = {}
+
+
+def _fp4_act_buffers(dev, rows: int, K: int, tiles: int):
+    """Per-device scratch of the activation quantiser (grown on demand, reused by every call)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    kc4 = -(-K // 256) * 4
+    b = _FP4_ACT.get(idx)
+    if b is None or b[0].numel() < rows * K // 2 or b[1].numel() < tiles * kc4 * 512 or b[2].numel() < rows:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("NVFP4 activation scratch must be sized before CUDA-graph capture (run once eagerly)")
+        old = (0, 0, 0) if b is None else (b[0].numel(), b[1].numel(), b[2].numel())
+        b = (torch.empty(max(rows * K // 2, old[0], 1 << 20), dtype=torch.uint8, device=dev),
+             torch.empty(max(tiles * kc4 * 512, old[1], 1 << 18), dtype=torch.uint8, device=dev),
+             torch.empty(max(rows, old[2], 4096), dtype=torch.float32, device=dev))
+        _FP4_ACT[idx] = b
+    return (b[0][: rows * K // 2].view(rows, K // 2), b[1][: tiles * kc4 * 512].view(tiles, kc4, 512),
+            b[2][:rows])
+
+
+def nvfp4_quant_act(x: torch.Tensor, tile_rows: int, static_g: float = 0.0, groups=None, num_groups=None):
+    """(xq [R, K/2], x_sf scale tiles, a_scale [R]) of bf16 activations x [R, K] (see
+    reference.nvfp4_quant_act); CUDA buffers are per-device scratch reused by the next call."""
+    R, K = x.shape
+    tiles = groups.shape[0] if groups is not None else -(-R // tile_rows)
+    xq, x_sf, a_scale = _fp4_act_buffers(x.device, R, K, tiles)
+    native().nvfp4_quant_act(x, xq, x_sf, a_scale, tile_rows, float(static_g), groups, num_groups)
+    return xq, x_sf, a_scale
+
+
+def nvfp4_linear_w4a4(x: torch.Tensor, packed: torch.Tensor, w_sf: torch.Tensor, scales: torch.Tensor,
+                      global_scale: torch.Tensor, static_g: float = 0.0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x W^T with NVFP4 W and per-token NVFP4-quantised x (block-scaled tcgen05 MMA on CUDA; the fp32
+    oracle of the same quantisation on CPU).  w_sf: `nvfp4_scale_tiles(scales)` kept with the weights."""
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    N = packed.shape[0]
+    if not x.is_cuda:
+        return ref.nvfp4_w4a4_linear(x2, packed, scales, global_scale, static_g).to(x.dtype).view(*lead, N)
+    if x2.stride(-1) != 1 or (x2.stride(0) * 2) % 16 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M, K = x2.shape
+    y = out.view(M, N) if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    if M:
+        from .gemm import batch_invariant
+
+        bn = 64 if M <= 64 else 128
+        xq, x_sf, a_scale = nvfp4_quant_act(x2, bn, static_g)
+        tiles = -(-N // 128) * -(-M // bn)
+        nkb = -(-K // 256)
+        # split-K (SH_FP4_SPLITK=1): while the grid covers under half the SMs (batch-invariant mode: the
+        # one-token-tile choice for every M).  Off by default: on B200 the last-split reduction tail
+        # measured neutral to slower than one split on every decode shape tried.
+        t_split = -(-N // 128) if batch_invariant() else tiles
+        splits = 1
+        while os.environ.get("SH_FP4_SPLITK", "0") == "1" and t_split * splits * 2 <= 148 \
+                and nkb // (splits * 2) >= 2 and splits < 16:
+            splits *= 2
+        ws = cnt = None
+        if splits > 1:
+            from .gemm import workspace
+
+            ws = workspace(x.device, splits * tiles * 128 * bn)
+            cnt = split_tickets(x.device, tiles)
+        native().gemm_fp4mma(y, xq, x_sf, a_scale, packed, w_sf, global_scale.float().reshape(-1), bn,
+                             splits=splits, ws=ws, counters=cnt)
+    return y.view(*lead, N)
+
+
+_TICKETS: dict = {}
+
+
+def split_tickets(dev, n: int) -> torch.Tensor:
+    """Per-device zeroed int32 tickets of the in-kernel split-K reduction (each launch leaves them zero)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    t = _TICKETS.get(idx)
+    if t is None or t.numel() < n:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("split-K tickets must be sized before CUDA-graph capture (run once eagerly)")
+        t = torch.zeros(max(n, 4096), dtype=torch.int32, device=dev)
+        _TICKETS[idx] = t
+    return t
+
+
+def _moe_w4a4_cpu(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
+    """CPU oracle of the W4A4 expert path: per (token, expert) pair, quantise the input row, gate/up
+    GEMM, SiLU * up in bf16, quantise again, down GEMM, weighted sum over the token's experts."""
+    T, H = x.shape
+    y = torch.zeros(T, H, dtype=torch.float32)
+    for t in range(T):
+        for j in range(ids.shape[1]):
+            e = int(ids[t, j])
+            if e < 0 or e >= E:
+                continue
+            r13 = slice(e * 2 * F, (e + 1) * 2 * F)
+            gu = ref.nvfp4_w4a4_linear(x[t:t + 1], w13q[0][r13], w13q[1][r13], w13q[2][e:e + 1]).to(x.dtype)
+            a = (torch.nn.functional.silu(gu[:, :F].float()) * gu[:, F:].float()).to(x.dtype)
+            r2 = slice(e * H, (e + 1) * H)
+            d = ref.nvfp4_w4a4_linear(a, w2q[0][r2], w2q[1][r2], w2q[2][e:e + 1]).to(x.dtype)
+            y[t] += float(weights[t, j]) * d[0].float()
+    y = y.to(x.dtype)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
 def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
     """moe_experts with NVFP4 expert weights: w13q = (packed [E*2F, H/2], scales [E*2F, H/16], global [E],
-    optional k-block-major scales), w2q likewise for [E*H, F]; the grouped GEMMs run the W4A16 tcgen05
-    kernel, each expert's rows scaled by its global scale."""
+    optional k-block-major scales, optional block-scaled MMA scale tiles), w2q likewise for [E*H, F].
+    The grouped GEMMs run the block-scaled W4A4 tcgen05 kernel on per-token NVFP4 activations (or the
+    W4A16 kernel with SH_NVFP4_ACT=bf16), each expert's rows scaled by its global scale.  On CPU the
+    W4A4 mode quantises the activations like the kernel and multiplies dequantised values in fp32."""
     T, H = x.shape
+    if not x.is_cuda and nvfp4_act_mode() == "fp4":
+        return _moe_w4a4_cpu(x, ids, weights, w13q, w2q, E, F, out)
     if not x.is_cuda:
         w13 = torch.cat([ref.nvfp4_dequantize(w13q[0][e * 2 * F:(e + 1) * 2 * F], w13q[1][e * 2 * F:(e + 1) * 2 * F],
                                               w13q[2][e:e + 1]) for e in range(E)]).to(x.dtype)
@@ -564,14 +699,24 @@ def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
     xs = torch.empty(pairs, H, dtype=x.dtype, device=dev)
     C.moe_gather(xs, x, sorted_token, offsets[E:])
     gu = torch.empty(pairs, 2 * F, dtype=x.dtype, device=dev)
-    sk13 = w13q[3] if len(w13q) > 3 else nvfp4_kmajor_scales(w13q[1])
-    sk2 = w2q[3] if len(w2q) > 3 else nvfp4_kmajor_scales(w2q[1])
-    C.gemm_nvfp4(gu, xs, w13q[0], sk13, w13q[2], bn, groups, ngroups, 2 * F)
-    a = silu_mul(gu)
     groups2 = groups.clone()
     groups2[:, 2] = groups[:, 3] * H
     ys = torch.empty(pairs, H, dtype=x.dtype, device=dev)
-    C.gemm_nvfp4(ys, a, w2q[0], sk2, w2q[2], bn, groups2, ngroups, H)
+    if nvfp4_act_mode() == "fp4":
+        # W4A4: each group entry's activation rows are quantised into the entry's own scale tile
+        t13 = w13q[4] if len(w13q) > 4 else nvfp4_scale_tiles(w13q[1], 2 * F)
+        t2 = w2q[4] if len(w2q) > 4 else nvfp4_scale_tiles(w2q[1], H)
+        xq, x_sf, a_sc = nvfp4_quant_act(xs, bn, 0.0, groups, ngroups)
+        C.gemm_fp4mma(gu, xq, x_sf, a_sc, w13q[0], t13, w13q[2], bn, groups, ngroups, 2 * F)
+        a = silu_mul(gu)
+        xq, x_sf, a_sc = nvfp4_quant_act(a, bn, 0.0, groups, ngroups)
+        C.gemm_fp4mma(ys, xq, x_sf, a_sc, w2q[0], t2, w2q[2], bn, groups2, ngroups, H)
+    else:
+        sk13 = w13q[3] if len(w13q) > 3 and w13q[3] is not None else nvfp4_kmajor_scales(w13q[1])
+        sk2 = w2q[3] if len(w2q) > 3 and w2q[3] is not None else nvfp4_kmajor_scales(w2q[1])
+        C.gemm_nvfp4(gu, xs, w13q[0], sk13, w13q[2], bn, groups, ngroups, 2 * F)
+        a = silu_mul(gu)
+        C.gemm_nvfp4(ys, a, w2q[0], sk2, w2q[2], bn, groups2, ngroups, H)
     if out is None:
         out = torch.empty(T, H, dtype=x.dtype, device=dev)
     C.moe_combine(out, ys, sorted_pos, weights, False)

@@ -253,6 +253,60 @@ def nvfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor, global_scale: t
     return (val * s).to(torch.bfloat16)
 
 
+def e2m1_codes(x: torch.Tensor) -> torch.Tensor:
+    """Nearest e2m1 code of each value (exact midpoints to the even code; bit 3 = sign, -0 included)."""
+    a = x.abs()
+    mids = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], device=x.device)
+    odd = torch.tensor([False, True, False, True, False, True, False], device=x.device)
+    code = ((a[..., None] > mids).sum(-1) + ((a[..., None] == mids) & odd).sum(-1)).to(torch.uint8)
+    return torch.where(x < 0, code | 8, code)
+
+
+def nvfp4_quant_act(x: torch.Tensor, static_g: float = 0.0):
+    """NVFP4 quantisation of activations [R, K] with a per-row global multiplier g.
+
+    g = static_g when given (the checkpoint's 1 / input_scale), else 2688 / amax(|row|) (1 for a zero
+    row); block scale s = e4m3(amax16 * (g / 6)) (saturating at 448); code = e2m1(x * (g / s)).
+    Returns (packed uint8 [R, K/2], scales uint8 (e4m3 bits) [R, K/16], a_scale fp32 [R] = 1 / g).
+    Reference semantics: suffix_hybrid/helion_kernels/nvfp4_gemm.py:213-240 (`nvfp4_quant_act_body`,
+    there with a static g)."""
+    xf = x.float()
+    R, K = xf.shape
+    if static_g > 0:
+        g = torch.full((R,), float(static_g), dtype=torch.float32, device=x.device)
+    else:
+        amax = xf.abs().amax(1)
+        g = torch.where(amax > 0, torch.tensor(2688.0, device=x.device) / torch.where(amax > 0, amax, 1.0),
+                        torch.ones_like(amax))
+    g6 = g / 6.0
+    blocks = xf.view(R, K // 16, 16)
+    s = (blocks.abs().amax(-1) * g6[:, None]).clamp(max=448.0).to(torch.float8_e4m3fn)
+    sf = s.float()
+    inv = torch.where(sf > 0, g[:, None] / torch.where(sf > 0, sf, 1.0), torch.zeros_like(sf))
+    code = e2m1_codes(blocks * inv[..., None]).view(R, K)
+    packed = (code[:, 0::2] | (code[:, 1::2] << 4)).to(torch.uint8)
+    return packed.contiguous(), s.view(torch.uint8).contiguous(), 1.0 / g
+
+
+def nvfp4_codes_value(packed: torch.Tensor) -> torch.Tensor:
+    """e2m1 values [R, K] (fp32) of packed codes [R, K/2]."""
+    R = packed.shape[0]
+    lo = (packed & 15).long()
+    hi = (packed >> 4).long()
+    codes = torch.stack([lo, hi], -1).view(R, -1)
+    mag = E2M1.to(packed.device)[codes & 7]
+    return torch.where(codes & 8 > 0, -mag, mag)
+
+
+def nvfp4_w4a4_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, global_scale: torch.Tensor,
+                      static_g: float = 0.0) -> torch.Tensor:
+    """fp32 oracle of the block-scaled W4A4 GEMM: quantise x, then sum of dequantised products."""
+    xq, xs, a_scale = nvfp4_quant_act(x, static_g)
+    xa = nvfp4_codes_value(xq) * xs.view(torch.float8_e4m3fn).float().repeat_interleave(16, dim=1)
+    wv = nvfp4_codes_value(packed) * scales.view(torch.uint8).view(torch.float8_e4m3fn).float().repeat_interleave(16, dim=1)
+    return (xa @ wv.t()) * a_scale[:, None] * float(global_scale.reshape(-1)[0])
+
+
 # ----------------------------------------------------------------------------- MLA / DSA
 def mla_attention(q_lat, q_pe, latent, block_tables, seq_lens, q_start, scale, kv_lora, topk=None):
     """Absorbed MLA over a latent cache [blocks, bs, kv_lora + rope].
