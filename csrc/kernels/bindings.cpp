@@ -20,6 +20,9 @@ void embedding(torch::Tensor out, torch::Tensor ids, torch::Tensor table);
 void argmax_rows(torch::Tensor out, torch::Tensor logits);
 void spec_verify(torch::Tensor draft, torch::Tensor target, torch::Tensor seq_lens, torch::Tensor out_tokens,
                  torch::Tensor accept, torch::Tensor next_token);
+void spec_advance(torch::Tensor out_tokens, torch::Tensor accept, torch::Tensor next_token, torch::Tensor seq_new,
+                  torch::Tensor cand, torch::Tensor clen, c10::optional<torch::Tensor> native, torch::Tensor win,
+                  torch::Tensor seq, torch::Tensor real, int64_t hyb_min, int64_t real_batch);
 
 // out[T, hq*D] <- paged GQA attention of the q rows (a view into the QKV
 // projection output) over the [blocks, hk, 64, D] cache.  nsplit > 1 needs
@@ -628,6 +631,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("w_sf"), py::arg("alpha_w"), py::arg("bn"), py::arg("groups") = py::none(),
         py::arg("num_groups") = py::none(), py::arg("rows_p") = 0, py::arg("err") = py::none(),
         py::arg("splits") = 1, py::arg("ws") = py::none(), py::arg("counters") = py::none());
+  m.def("spec_advance", &spec_advance);
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("moe_route", &moe_route);

@@ -104,9 +104,82 @@ __global__ void spec_verify_kernel(const int64_t* __restrict__ draft, const int6
   seq_lens[b] += a + 1;
 }
 
+// Async-scheduling advance (one thread per request): builds the next verify
+// window on the device from this step's results and a host candidate computed
+// one step earlier.  cand [B, L] (row b: C_b[0:clen_b]) was anchored at the
+// history length before this step; the step accepted a_b drafts and appended
+// o = a_b + 1 tokens out[b, 0:o].  If C_b[0:o] == out[b, 0:o] the next drafts
+// are C_b[o : o+k] (positions < clen_b; -1 = no draft), else none.  With
+// native != nullptr (hybrid) the native drafts native[b, 0:k] are used unless
+// at least hyb_min candidate drafts are real.  win[b] = [next_token[b],
+// drafts]; seq[b] = seq_new[b]; real[b] = number of candidate drafts used.
+// Rows b >= real_batch (bucket padding) are reset to the scratch window
+// (zeros, length 0).
+__global__ void spec_advance_kernel(const int64_t* __restrict__ out_tokens, const int32_t* __restrict__ accept,
+                                    const int64_t* __restrict__ next_token, const int64_t* __restrict__ seq_new,
+                                    const int64_t* __restrict__ cand, const int32_t* __restrict__ clen,
+                                    const int64_t* __restrict__ native, int64_t* __restrict__ win,
+                                    int64_t* __restrict__ seq, int32_t* __restrict__ real, int batch, int k, int L,
+                                    int hyb_min, int real_batch) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  if (b >= real_batch) {
+    for (int j = 0; j <= k; ++j) win[(int64_t)b * (k + 1) + j] = 0;
+    seq[b] = 0;
+    real[b] = 0;
+    return;
+  }
+  const int o = accept[b] + 1;
+  const int64_t* c = cand + (int64_t)b * L;
+  const int64_t* ot = out_tokens + (int64_t)b * (k + 1);
+  const int cl = clen[b];
+  bool aligned = o <= cl;
+  for (int j = 0; j < o && aligned; ++j) aligned = c[j] == ot[j];
+  int n_real = 0;
+  if (aligned)
+    while (n_real < k && o + n_real < cl) ++n_real;
+  int64_t* w = win + (int64_t)b * (k + 1);
+  w[0] = next_token[b];
+  const bool use_native = native != nullptr && n_real < hyb_min;
+  for (int j = 0; j < k; ++j)
+    w[1 + j] = use_native ? native[(int64_t)b * k + j] : (j < n_real ? c[o + j] : -1);
+  seq[b] = seq_new[b];
+  real[b] = use_native ? 0 : n_real;
+}
+
 }  // namespace shk
 
 using namespace shk;
+
+void spec_advance(torch::Tensor out_tokens, torch::Tensor accept, torch::Tensor next_token, torch::Tensor seq_new,
+                  torch::Tensor cand, torch::Tensor clen, c10::optional<torch::Tensor> native, torch::Tensor win,
+                  torch::Tensor seq, torch::Tensor real, int64_t hyb_min, int64_t real_batch) {
+  TORCH_CHECK(out_tokens.scalar_type() == at::kLong && cand.scalar_type() == at::kLong && win.scalar_type() == at::kLong &&
+                  seq.scalar_type() == at::kLong && seq_new.scalar_type() == at::kLong &&
+                  next_token.scalar_type() == at::kLong, "spec_advance: int64 tokens");
+  TORCH_CHECK(accept.scalar_type() == at::kInt && clen.scalar_type() == at::kInt && real.scalar_type() == at::kInt,
+              "spec_advance: int32 counts");
+  TORCH_CHECK(out_tokens.is_contiguous() && cand.is_contiguous() && win.is_contiguous(), "spec_advance: contiguous");
+  const int batch = win.size(0), k = win.size(1) - 1, L = cand.size(1);
+  TORCH_CHECK(out_tokens.size(0) >= batch && out_tokens.size(1) == k + 1 && cand.size(0) >= batch,
+              "spec_advance: shapes");
+  const int64_t* nat = nullptr;
+  if (native.has_value()) {
+    TORCH_CHECK(native->scalar_type() == at::kLong && native->is_contiguous() && native->size(1) == k,
+                "spec_advance: native [B, k]");
+    nat = native->data_ptr<int64_t>();
+  }
+  if (batch == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  shk::launch(spec_advance_kernel, dim3((batch + 127) / 128), dim3(128), 0, stream, out_tokens.data_ptr<int64_t>(),
+              accept.data_ptr<int32_t>(), next_token.data_ptr<int64_t>(), seq_new.data_ptr<int64_t>(),
+              cand.data_ptr<int64_t>(), clen.data_ptr<int32_t>(), nat, win.data_ptr<int64_t>(),
+              seq.data_ptr<int64_t>(), real.data_ptr<int32_t>(), batch, k, L, static_cast<int>(hyb_min),
+              static_cast<int>(real_batch));
+  SH_CUDA_CHECK(cudaGetLastError());
+}
 
 void argmax_rows(torch::Tensor out, torch::Tensor logits) {
   TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "argmax_rows: logits [T, V]");

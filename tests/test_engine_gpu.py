@@ -72,3 +72,20 @@ def test_qwen3_next_oracle_drafts_on_gpu(graphs):
     agree = np.mean([a == b for a, b in zip(got, base)])
     assert agree == 1.0, (got, base)
     assert eng.spec_stats()["mean_accept_len"] > 1.5
+
+
+@pytest.mark.parametrize("method", ["suffix", "hybrid"])
+@pytest.mark.parametrize("graphs", [False, True])
+def test_async_scheduling_matches_greedy_on_gpu(method, graphs):
+    """Lag-1 drafting with the device-side resolve (spec_advance kernel) inside the pipelined step."""
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, 4096, int(n)) for n in (100, 70, 130, 64, 33)]
+    base, _ = run("none", False, prompts, new=32)
+    m = shrink(llama3_8b_config(), layers=2, hidden=512, vocab=4096)
+    cfg = EngineConfig(model=m, spec=SpecConfig(method=method, k=5, async_scheduling=True),
+                       cache=CacheConfig(max_model_len=1024), max_num_seqs=4, device="cuda", cuda_graphs=graphs)
+    eng = LLMEngine(cfg)
+    eng.warm_start([np.concatenate([p, b]) for p, b in zip(prompts, base)])
+    got = eng.generate(prompts, max_new_tokens=32)
+    assert got == base
+    assert eng.spec_stats()["mean_accept_len"] > 1.5

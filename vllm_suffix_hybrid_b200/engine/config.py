@@ -181,6 +181,8 @@ class SpecConfig:
     uniform_k: bool = True  # suffix-only: publish width k for every row (static verify shape)
     width_gate: bool = False  # SUFFIX_HYBRID_EWMA_WIDTH
     min_len: int = 1  # SUFFIX_HYBRID_SUFFIX_MIN
+    async_scheduling: bool = False  # SUFFIX_HYBRID_ASYNC: lag-1 host candidates, drafts resolved on the device
+    async_hyb_min: int = 0  # SUFFIX_HYBRID_ASYNC_HYB_MIN (0 = k): real suffix drafts that replace native ones
 
 
 @dataclass
@@ -231,6 +233,11 @@ def apply_env(cfg: EngineConfig) -> EngineConfig:
     v = _env("SUFFIX_MIN")
     if v is not None and v.isdigit():
         cfg.spec.min_len = max(1, int(v))
+    if _env("ASYNC") == "1":
+        cfg.spec.async_scheduling = True
+    v = _env("ASYNC_HYB_MIN")
+    if v is not None and v.isdigit():
+        cfg.spec.async_hyb_min = int(v)
     v = _env("MAX_SPEC_TOKENS")
     if v is not None and v.isdigit() and int(v) > 0:
         cfg.spec.k = int(v)

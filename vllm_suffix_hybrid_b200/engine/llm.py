@@ -21,6 +21,7 @@ read every context in place.
 from __future__ import annotations
 
 import itertools
+import logging
 import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
@@ -35,6 +36,20 @@ from .config import EngineConfig, apply_env
 from .kv_cache import BlockPool, allocate_caches, blocks_for
 from .runner import Runner
 from .telemetry import Telemetry
+
+logger = logging.getLogger(__name__)
+
+
+def _trace_budget(name: str) -> list:
+    """[remaining traced steps] of SUFFIX_HYBRID_<name> (0 = off; _MAX sets the budget, default 24)."""
+    import os
+
+    if not os.environ.get("SUFFIX_HYBRID_" + name, "").strip():
+        return [0]
+    try:
+        return [max(0, int(os.environ.get("SUFFIX_HYBRID_" + name + "_MAX", "") or 24))]
+    except ValueError:
+        return [24]
 
 
 @dataclass
@@ -135,6 +150,19 @@ class LLMEngine:
                                                     spec.width_gate)
         elif spec.method == "ngram":
             self.proposer = _native.Engine(k, self.tokens.shape[1])
+        # Async scheduling (lag-1 drafting, SUFFIX_HYBRID_ASYNC=1): suffix / hybrid only; other methods keep
+        # synchronous scheduling (the reference's sched_sync rule, sched_sync.py:85).
+        self._pipe = None
+        self._async = bool(spec.async_scheduling and self.k > 0 and spec.method in ("suffix", "hybrid"))
+        if spec.async_scheduling and not self._async:
+            logger.warning("SUFFIX_HYBRID_ASYNC ignored for method %r: synchronous scheduling", spec.method)
+        self._cand_len = 2 * self.k + 1
+        self.async_proposer = (_native.V2SuffixProposer(self._cand_len, self.tokens.shape[1], spec.min_len, False,
+                                                        False) if self._async else None)
+        self._hyb_min = (spec.async_hyb_min or self.k) if spec.method == "hybrid" else 0
+        self._lag = self.k + 1 if self._async else 0  # tokens a lagged step may add beyond the host's view
+        self._trace_verify = _trace_budget("TRACE_VERIFY2")
+        self._trace_sched = _trace_budget("SCHEDTRACE")
 
     # ------------------------------------------------------------------ sizing
     def _auto_blocks(self) -> int:
@@ -173,6 +201,7 @@ class LLMEngine:
                 return True
         for r in self.running:
             if r.rid == rid and not r.finished:
+                self._drain()
                 r.finished, r.finish_reason = True, "abort"
                 self._retire()
                 return True
@@ -193,12 +222,15 @@ class LLMEngine:
 
     def warm_start(self, sequences) -> int:
         """Pre-fill the proposer's suffix corpus with token histories (same path as a departing request)."""
-        cache = getattr(self.proposer, "suffix_cache", None)
-        if cache is None:
+        caches = [c for c in (getattr(self.proposer, "suffix_cache", None),
+                              getattr(self.async_proposer, "suffix_cache", None)) if c is not None]
+        if not caches:
             raise RuntimeError(f"warm start needs a suffix-corpus proposer (method {self.cfg.spec.method!r})")
         n = 0
         for seq in sequences:
-            cache.add_sequence([int(t) for t in seq])
+            toks = [int(t) for t in seq]
+            for c in caches:
+                c.add_sequence(toks)
             n += 1
         return n
 
@@ -207,20 +239,22 @@ class LLMEngine:
         return dict(get()) if get else {}
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self._pipe is not None)
 
     def step(self) -> StepStats:
         free_rows = self.cfg.max_num_seqs - len(self.running)
         if self.waiting and free_rows > 0:
-            return self._prefill_step(free_rows)
+            self._drain()
+            return self._prefill_step(self.cfg.max_num_seqs - len(self.running))
+        decode = self._decode_step_async if self._async else self._decode_step
         sp = self.step_profiler
         if sp is not None:
             sp.before("decode", len(self.running))
             try:
-                return self._decode_step()
+                return decode()
             finally:
                 sp.after()
-        return self._decode_step()
+        return decode()
 
     def generate(self, prompts, max_new_tokens: int = 128) -> List[List[int]]:
         rids = [self.add_request(p, max_new_tokens) for p in prompts]
@@ -288,7 +322,7 @@ class LLMEngine:
         r.next_token = toks[-1] if toks else r.next_token
         if stopped:
             r.finished, r.finish_reason = True, "stop"
-        elif len(r.output) >= r.max_new_tokens or r.history_len + 2 * self.k + 2 >= self.max_model_len:
+        elif len(r.output) >= r.max_new_tokens or r.history_len + 2 * self.k + 2 + 2 * self._lag >= self.max_model_len:
             r.finished, r.finish_reason = True, "length"
 
     def _propose(self, batch_native: bool) -> float:
@@ -355,6 +389,109 @@ class LLMEngine:
         self._retire()
         t3 = time.perf_counter()
         st = StepStats("decode", n, emitted, accepted, (t2 - t1) * 1e3, (t3 - t2 + t1 - t0) * 1e3, prop_us)
+        self.stats.append(st)
+        self.telemetry.record(self, st)
+        return st
+
+    # ------------------------------------------------------------------ async scheduling
+    def _take(self, out, acc, used, real, pub=None) -> tuple:
+        """Commit one collected pipelined step: emit for rows still running; (emitted, accepted)."""
+        emitted = accepted = 0
+        for i, r in enumerate(self.running):
+            a = int(acc[i])
+            if r.finished:  # finished at an earlier step: the lagged step's tokens are dropped
+                continue
+            toks = out[i, : a + 1].tolist()
+            r.committed += a + 1
+            r.accepted_prev = a
+            self._emit(r, i, toks)
+            emitted += min(a + 1, len(toks))
+            accepted += a
+        if self._trace_verify[0] > 0:
+            self._trace_verify[0] -= 1
+            for i, r in enumerate(self.running):
+                w = self.k
+                graded = [int(x) for x in used[i, 1:1 + w]]
+                p = pub[i] if pub is not None else graded
+                m = sum(1 for x, y in zip(p, graded) if x == y)
+                logger.warning("VTRACE2 rid=%r w=%d pubmatch=%d/%d graded=%s pub=%s accrow=%s nacc=%d real=%d", r.rid,
+                               w, m, w, graded[:8], list(p)[:8], out[i, :8].tolist(), int(acc[i]), int(real[i]))
+        return emitted, accepted
+
+    def _drain(self) -> None:
+        """Collect the in-flight pipelined step (before the running set changes)."""
+        if self._pipe is None:
+            return
+        n = len(self.running)
+        out, acc, nat, used, real = self.runner.collect(self._pipe["parity"], n)
+        em, ac = self._take(out, acc, used, real)
+        self._pipe = None
+        if self.draft is not None:
+            for i, r in enumerate(self.running):
+                r.drafts = nat[i, : self.k].tolist()
+        self._propose(batch_native=False)  # host drafts for the next synchronous step
+        st = StepStats("decode", n, em, ac, 0.0, 0.0, 0.0)
+        self.stats.append(st)
+        self.telemetry.record(self, st)
+        self._retire()
+
+    def _decode_step_async(self) -> StepStats:
+        """Pipelined decode: launch step N (window advanced on the device from step N-1's results and a
+        candidate looked up on the host from the history before step N-1), then collect step N-1.
+
+        Reference behaviour: suffix_hybrid/async_spec.py:1-120 (lag-1 host lookup, device resolve,
+        hybrid replacement threshold); here the resolve checks the candidate against the in-flight
+        step's accepted tokens, so no device copy of the token history is needed."""
+        t0 = time.perf_counter()
+        n = len(self.running)
+        if n == 0:
+            self._drain()
+            return StepStats("idle", 0, 0, 0, 0.0, 0.0, 0.0)
+        ids = [r.rid for r in self.running]
+        if self._pipe is not None and self._pipe["rows"] != ids:
+            self._drain()
+            return self._decode_step()
+        if self._pipe is None and not self.runner.has_graph(n):
+            return self._decode_step()  # captures the bucket's graph synchronously
+        k, W = self.k, self.k + 1
+        mb = self.max_blocks_per_seq
+        bt = np.zeros((n, mb), dtype=np.int32)
+        slots = np.fromiter((r.slot for r in self.running), dtype=np.int64, count=n)
+        for i, r in enumerate(self.running):
+            self._ensure_blocks(r, r.committed + 2 * k + 2 + 2 * self._lag)
+            bt[i, :len(r.blocks)] = r.blocks
+        if self._pipe is None:  # pipeline start: host window (drafts from the synchronous proposer)
+            win = np.full((n, W), -1, dtype=np.int64)
+            seq = np.fromiter((r.committed for r in self.running), dtype=np.int64, count=n)
+            for i, r in enumerate(self.running):
+                win[i, 0] = r.next_token
+                d = r.drafts[:k]
+                win[i, 1:1 + len(d)] = d
+            self.runner.launch(0, n, bt, slots, win=win, seq=seq, cand_len=self._cand_len)
+            self._pipe = {"parity": 0, "rows": ids}
+            st = StepStats("launch", n, 0, 0, 0.0, (time.perf_counter() - t0) * 1e3, 0.0)
+            self.stats.append(st)
+            return st
+        tp = time.perf_counter_ns()
+        counts = np.fromiter((r.history_len for r in self.running), dtype=np.int64, count=n)
+        cand, clen = self.async_proposer.propose_suffix_only(ids, np.arange(n, dtype=np.int64), counts, self.tokens)
+        prop_us = (time.perf_counter_ns() - tp) / 1e3
+        p = self._pipe["parity"]
+        q = p ^ 1
+        self.runner.launch(q, n, bt, slots, cand=cand, clen=np.asarray(clen, dtype=np.int32), hyb_min=self._hyb_min,
+                           cand_len=self._cand_len)
+        if self._trace_sched[0] > 0:
+            self._trace_sched[0] -= 1
+            logger.warning("SCHEDTRACE step rows=%d host_widths=%s", n,
+                           [int(min(k, max(int(c) - 1, 0))) for c in clen][:16])
+        t1 = time.perf_counter()
+        out, acc, nat, used, real = self.runner.collect(p, n)
+        t2 = time.perf_counter()
+        em, ac = self._take(out, acc, used, real, pub=self._pipe.get("pub"))
+        self._pipe = {"parity": q, "rows": ids, "pub": [list(cand[i, 1:1 + k]) for i in range(n)]}
+        if any(r.finished for r in self.running):
+            self._drain()
+        st = StepStats("decode", n, em, ac, (t2 - t1) * 1e3, (t1 - t0) * 1e3, prop_us)
         self.stats.append(st)
         self.telemetry.record(self, st)
         return st

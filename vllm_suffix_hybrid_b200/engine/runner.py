@@ -84,6 +84,95 @@ class Runner:
         self.last_device_ms = 0.0
         self.h2d_bytes = 0
         self.d2h_bytes = 0
+        self._async = None  # buffers of the pipelined (async-scheduling) step, made on first use
+
+    # ------------------------------------------------------------------ async scheduling
+    def _async_buffers(self, cand_len: int):
+        """Parity-double-buffered pinned staging + device candidate buffers of the pipelined step."""
+        if self._async is not None and self._async["L"] == cand_len:
+            return self._async
+        B, W, pin = self.max_batch, self.W, torch.device(self.device).type == "cuda"
+        P = lambda *shape, dt=torch.long: [torch.zeros(*shape, dtype=dt, pin_memory=pin) for _ in range(2)]
+        self._async = dict(
+            L=cand_len, h_win=P(B, W), h_seq=P(B), h_bt=P(B, self.max_blocks, dt=torch.int32), h_slots=P(B),
+            h_cand=P(B, cand_len), h_clen=P(B, dt=torch.int32), h_out=P(B, W), h_acc=P(B, dt=torch.int32),
+            h_nat=P(B, max(self.k, 1)), h_used=P(B, W), h_real=P(B, dt=torch.int32),
+            cand=torch.zeros(B, cand_len, dtype=torch.long, device=self.device),
+            clen=torch.zeros(B, dtype=torch.int32, device=self.device),
+            real=torch.zeros(B, dtype=torch.int32, device=self.device),
+            ev=[torch.cuda.Event() if pin else None for _ in range(2)], nb=None)
+        return self._async
+
+    def launch(self, parity: int, nb_real: int, bt: np.ndarray, slots: np.ndarray, win: np.ndarray = None,
+               seq: np.ndarray = None, cand: np.ndarray = None, clen: np.ndarray = None, hyb_min: int = 0,
+               cand_len: int = 1) -> None:
+        """Enqueue one decode step without waiting for it (async scheduling).
+
+        win/seq given: the window comes from the host (pipeline start).  Otherwise the window is built on
+        the device by `spec_advance` from the previous launch's results (same rows, same bucket) and the
+        host candidates cand [n, cand_len] / clen [n] computed one step earlier.  Results land in the
+        parity's pinned buffers; `collect(parity)` waits for them.  Staging is double-buffered by parity:
+        a parity is reused only after its previous step was collected.
+        """
+        A = self._async_buffers(cand_len)
+        nb = bucket_for(nb_real, self.max_batch)
+        if win is None and A["nb"] != nb:
+            raise RuntimeError("device-advanced launch needs the previous launch's bucket")
+        A["nb"] = nb
+        nbt = self.max_blocks
+        A["h_bt"][parity][:nb_real, : bt.shape[1]].numpy()[:] = bt
+        A["h_bt"][parity][nb_real:nb] = 0
+        A["h_slots"][parity][:nb_real].numpy()[:] = slots
+        A["h_slots"][parity][nb_real:nb] = 0
+        self.bt[:nb, :nbt].copy_(A["h_bt"][parity][:nb, :nbt], non_blocking=True)
+        self.slots[:nb].copy_(A["h_slots"][parity][:nb], non_blocking=True)
+        if win is not None:
+            A["h_win"][parity][:nb_real].numpy()[:] = win
+            A["h_seq"][parity][:nb_real].numpy()[:] = seq
+            A["h_win"][parity][nb_real:nb] = 0
+            A["h_seq"][parity][nb_real:nb] = 0
+            self.win[:nb].copy_(A["h_win"][parity][:nb], non_blocking=True)
+            self.seq[:nb].copy_(A["h_seq"][parity][:nb], non_blocking=True)
+            A["real"][:nb].zero_()
+        else:
+            A["h_cand"][parity][:nb_real].numpy()[:] = cand
+            A["h_clen"][parity][:nb_real].numpy()[:] = clen
+            A["cand"][:nb].copy_(A["h_cand"][parity][:nb], non_blocking=True)
+            A["clen"][:nb].copy_(A["h_clen"][parity][:nb], non_blocking=True)
+            nat = self.native[:nb] if (self.draft is not None and self.k > 0 and hyb_min > 0) else None
+            ops.spec_advance(self.out_tokens[:nb], self.accept[:nb], self.next_tok[:nb], self.seq_new[:nb],
+                             A["cand"][:nb], A["clen"][:nb], nat, self.win[:nb], self.seq[:nb], A["real"][:nb],
+                             hyb_min, nb_real)
+        A["h_used"][parity][:nb].copy_(self.win[:nb], non_blocking=True)
+        A["h_real"][parity][:nb].copy_(A["real"][:nb], non_blocking=True)
+        if self.use_graphs:
+            g = self.graphs.get(nb)
+            if g is None:
+                raise RuntimeError("capture the bucket's graph with a synchronous step first")
+            g.replay()
+        else:
+            self._decode_body(nb)
+        A["h_out"][parity][:nb].copy_(self.out_tokens[:nb], non_blocking=True)
+        A["h_acc"][parity][:nb].copy_(self.accept[:nb], non_blocking=True)
+        if self.draft is not None and self.k > 0:
+            A["h_nat"][parity][:nb].copy_(self.native[:nb], non_blocking=True)
+        if A["ev"][parity] is not None:
+            A["ev"][parity].record()
+        self.h2d_bytes = nb * (self.max_blocks * 4 + 8) + (nb * (self.W * 8 + 8) if win is not None
+                                                           else nb * (cand_len * 8 + 4))
+        self.d2h_bytes = nb * (2 * self.W * 8 + 8 + (self.k * 8 if self.draft is not None and self.k > 0 else 0))
+
+    def collect(self, parity: int, nb_real: int):
+        """Wait for a launched step; host views (out_tokens, accept, native, window used, real drafts)."""
+        A = self._async
+        if A["ev"][parity] is not None:
+            A["ev"][parity].synchronize()
+        return (A["h_out"][parity][:nb_real].numpy(), A["h_acc"][parity][:nb_real].numpy(),
+                A["h_nat"][parity][:nb_real].numpy(), A["h_used"][parity][:nb_real].numpy(),
+                A["h_real"][parity][:nb_real].numpy())
+
+    def has_graph(self, nb_real: int) -> bool:
+        return not self.use_graphs or bucket_for(nb_real, self.max_batch) in self.graphs
 
     # ------------------------------------------------------------------ helpers
     def _tile_tensors(self, nb: int, qlen: int):

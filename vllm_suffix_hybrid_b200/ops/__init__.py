@@ -215,6 +215,26 @@ def spec_verify(draft, target, seq_lens, out_tokens, accept, next_token) -> None
     native().spec_verify(draft, target, seq_lens, out_tokens, accept, next_token)
 
 
+def spec_advance(out_tokens, accept, next_token, seq_new, cand, clen, native_drafts, win, seq, real,
+                 hyb_min: int, real_batch: int) -> None:
+    """Next verify window from this step's results and a lag-1 host candidate (async scheduling); in place
+    into win [B, k+1], seq [B], real [B]; rows >= real_batch reset to the scratch window (see
+    reference.spec_advance)."""
+    if not _cuda(win):
+        w, sq, rl = ref.spec_advance(out_tokens[: win.shape[0]], accept, next_token, seq_new, cand, clen,
+                                     native_drafts, hyb_min)
+        w[real_batch:] = 0
+        sq[real_batch:] = 0
+        rl[real_batch:] = 0
+        win.copy_(w)
+        seq.copy_(sq)
+        real.copy_(rl)
+        return
+    nd = native_drafts.contiguous() if native_drafts is not None else None
+    native().spec_advance(out_tokens, accept, next_token, seq_new, cand, clen, nd, win, seq, real, hyb_min,
+                          real_batch)
+
+
 # ----------------------------------------------------------------------------- GEMM
 _GEMM_BACKEND = os.environ.get("SH_GEMM", "tcgen05")  # "cublas": library baseline for A/B runs
 

@@ -213,6 +213,28 @@ def gated_rms_norm(o: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float
     return of * inv * w.float() * torch.nn.functional.silu(z.float())
 
 
+def spec_advance(out_tokens, accept, next_token, seq_new, cand, clen, native, hyb_min: int):
+    """Async-scheduling advance (restates the reference's device `resolve`, async_spec.py:102-120, for a
+    candidate checked against this step's accepted tokens): returns (win [B, k+1], seq [B], real [B])."""
+    B, W = out_tokens.shape[0], out_tokens.shape[1]
+    k = W - 1
+    win = torch.full((B, W), -1, dtype=torch.long)
+    real = torch.zeros(B, dtype=torch.int32)
+    for b in range(B):
+        o = int(accept[b]) + 1
+        cl = int(clen[b])
+        aligned = o <= cl and all(int(cand[b, j]) == int(out_tokens[b, j]) for j in range(o))
+        n_real = min(k, max(cl - o, 0)) if aligned else 0
+        win[b, 0] = next_token[b]
+        if native is not None and n_real < hyb_min:
+            win[b, 1:] = native[b, :k]
+        else:
+            for j in range(n_real):
+                win[b, 1 + j] = cand[b, o + j]
+            real[b] = n_real
+    return win, seq_new[:B].clone(), real
+
+
 # ----------------------------------------------------------------------------- NVFP4
 E2M1 = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
 
