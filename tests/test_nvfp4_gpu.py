@@ -221,3 +221,20 @@ def test_w4a4_split_k_last_arriver_reduction(splits):
         torch.testing.assert_close(ys.float(), y1.float(), rtol=2e-2, atol=2e-3)
     want = ref.nvfp4_w4a4_linear(x.cpu(), p, s, g)
     assert (ys.float().cpu() - want).abs().max().item() <= 0.01 * want.abs().max().item() + 1e-3
+
+
+def test_screened_lm_head_on_gpu():
+    """W4A4 screen + exact re-score of 64 candidates picks the bf16 head's greedy token (rows whose bf16
+    maxima differ only by the fp32 summation order may flip; at most one here)."""
+    from vllm_suffix_hybrid_b200.models.lm_head import ScreenedHead
+
+    torch.manual_seed(12)
+    V, H, M = 32000, 1024, 48
+    w = (torch.randn(V, H, device="cuda") * 0.05).to(torch.bfloat16)
+    x = torch.randn(M, H, device="cuda").to(torch.bfloat16)
+    head = ScreenedHead(w)
+    val, ids = head.best(x)
+    want = (x.float() @ w.float().t()).bfloat16().float()
+    torch.cuda.synchronize()
+    assert int((ids != want.argmax(-1)).sum()) <= 1
+    assert torch.allclose(val, want.max(-1).values, rtol=1e-2, atol=1e-3)

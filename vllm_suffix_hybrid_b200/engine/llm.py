@@ -110,6 +110,11 @@ class LLMEngine:
             from .loader import load_weights
 
             load_weights(self.model, self.draft, cfg.weights)
+        from ..models import lm_head
+
+        if lm_head.enabled() and lm_head.install(self.model) is not None:
+            logger.warning("NVFP4-screened LM head active (max M %d, re-score %d)", self.model.lm_screen.max_m,
+                           self.model.lm_screen.rescore)
         bs = cfg.cache.block_size
         self.block_size = bs
         self.max_model_len = cfg.cache.max_model_len

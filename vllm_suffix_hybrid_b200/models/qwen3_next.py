@@ -177,6 +177,9 @@ class Qwen3NextModel:
         return self.lm_head(hidden)
 
     def greedy(self, hidden, out=None):
+        scr = getattr(self, "lm_screen", None)
+        if scr is not None and scr.applies(hidden):  # NVFP4 screen + exact re-score (SUFFIX_NVFP4_LMHEAD)
+            return comm.vocab_parallel_best(*scr.best(hidden), self.vocab_offset, out)
         return comm.vocab_parallel_argmax(self.logits(hidden), self.vocab_offset, out)
 
 

@@ -96,7 +96,19 @@ def vocab_parallel_argmax(local_logits: torch.Tensor, vocab_offset: int, out: Op
     if st.tp == 1:
         return idx
     val = local_logits.gather(1, idx[:, None]).float()[:, 0]
-    pair = torch.stack([val, (idx + vocab_offset).float()], dim=1)  # exact for ids < 2^24
+    return vocab_parallel_best(val, idx, vocab_offset, out)
+
+
+def vocab_parallel_best(val: torch.Tensor, idx: torch.Tensor, vocab_offset: int,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Global id of the best (value, local id) pair per row over the vocab shards (lowest id on ties)."""
+    st = state.get()
+    if st.tp == 1:
+        if out is not None:
+            out.copy_(idx)
+            return out
+        return idx
+    pair = torch.stack([val.float(), (idx + vocab_offset).float()], dim=1)  # exact for ids < 2^24
     if pair.is_cuda:
         gathered = torch.empty(st.tp, *pair.shape, dtype=pair.dtype, device=pair.device)
         dist.all_gather_into_tensor(gathered, pair, group=st.group)
