@@ -31,8 +31,22 @@ def main(argv=None):
     ap.add_argument("--shrink", action="store_true", help="test-size model of the same architecture")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--async-scheduling", action="store_true", help="lag-1 drafting (SUFFIX_HYBRID_ASYNC=1)")
+    import sys
+
+    from . import dev_args
+
+    argv = list(sys.argv[1:] if argv is None else argv)
+    applied = dev_args.apply(argv)  # SUFFIX_HYBRID_DEV_ARGS=1: splice a reviewed flag delta
     a = ap.parse_args(argv)
     logging.basicConfig(level=logging.INFO)
+    if applied:
+        logging.getLogger(__name__).warning("dev args applied: %s -> argv %s", applied, argv)
+    from ..utils.gpu_mon import GpuMonitor
+
+    mon = GpuMonitor.from_env()  # SUFFIX_HYBRID_GPU_MON=<seconds>
+    if mon is not None:
+        mon.start()
 
     from ..engine.config import PRESETS, CacheConfig, EngineConfig, ParallelConfig, SpecConfig, shrink
     from ..engine.llm import LLMEngine
@@ -54,7 +68,8 @@ def main(argv=None):
         mcfg = shrink(mcfg)
         if a.device != "cuda":
             mcfg.dtype = "float32"
-    cfg = EngineConfig(model=mcfg, spec=SpecConfig(method=a.method, k=a.k), parallel=ParallelConfig(tp=a.tp, comm=a.comm),
+    cfg = EngineConfig(model=mcfg, spec=SpecConfig(method=a.method, k=a.k, async_scheduling=a.async_scheduling),
+                       parallel=ParallelConfig(tp=a.tp, comm=a.comm),
                        cache=CacheConfig(max_model_len=a.max_model_len), max_num_seqs=a.max_num_seqs, device=a.device,
                        cuda_graphs=(a.device == "cuda" and not a.no_graphs), weights=a.weights)
     engine = LLMEngine(cfg)
