@@ -17,6 +17,7 @@
 #include <string>
 #include <string_view>
 
+#include "decider.h"
 #include "engine.h"
 #include "mixer.h"
 #include "suffix_cache.h"
@@ -486,6 +487,22 @@ PYBIND11_MODULE(_native, m) {
         return d;
       });
 
+  // Decision-endpoint helpers (reference: src/lib.rs:431-443); malformed requests raise ValueError.
+  m.def(
+      "decider_prepare",
+      [](const std::string& request_json, const std::string& codes_json, const std::string& profile) {
+        py::gil_scoped_release nogil;
+        return decider_prepare(request_json, codes_json, profile);
+      },
+      py::arg("request_json"), py::arg("codes_json"), py::arg("profile") = "pplx");
+  m.def(
+      "decider_answer",
+      [](const std::string& request_json, const std::string& logits_json, double temperature,
+         const std::string& profile) {
+        py::gil_scoped_release nogil;
+        return decider_answer(request_json, logits_json, temperature, profile);
+      },
+      py::arg("request_json"), py::arg("logits_json"), py::arg("temperature"), py::arg("profile") = "pplx");
   m.def(
       "rejection_greedy_accept",
       [](py::handle draft_token_ids, py::handle target_argmax, py::handle cu_num_draft_tokens, size_t max_spec_len) {

@@ -239,6 +239,22 @@ class LLMEngine:
             n += 1
         return n
 
+    def readout(self, prompt, rows: torch.Tensor) -> List[float]:
+        """Score one prompt: rows [R, H] . final hidden state at the prompt's last position (fp32).
+
+        Runs between decode steps on scratch KV blocks (released afterwards) and the scratch recurrent
+        slot, so running requests are unaffected.  Used by the decision endpoint."""
+        self._drain()
+        prompt = np.asarray(prompt, dtype=np.int64)
+        if len(prompt) == 0 or len(prompt) > self.max_model_len:
+            raise ValueError("decision input must fit the model length without truncation")
+        blocks = self.pool.allocate(blocks_for(len(prompt), self.block_size))
+        try:
+            hid = self.runner.prefill([prompt], [blocks], [0], hidden_only=True)
+            return (hid.float() @ rows.to(hid.device).float().t())[0].tolist()
+        finally:
+            self.pool.release(blocks)
+
     def proposer_stats(self) -> dict:
         get = getattr(self.proposer, "get_stats", None)
         return dict(get()) if get else {}

@@ -304,8 +304,9 @@ class Runner:
 
     # ------------------------------------------------------------------ prefill
     def prefill(self, prompts: List[np.ndarray], block_tables: List[List[int]],
-                state_slots: Optional[List[int]] = None):
-        """Prefill a batch of prompts (each fully). Returns (first tokens [n], native drafts [n, k])."""
+                state_slots: Optional[List[int]] = None, hidden_only: bool = False):
+        """Prefill a batch of prompts (each fully). Returns (first tokens [n], native drafts [n, k]), or with
+        hidden_only the final normalised hidden state at each prompt's last position [n, H] (scoring)."""
         dev = self.device
         n = len(prompts)
         lens = [len(p) for p in prompts]
@@ -333,6 +334,8 @@ class Runner:
         if self.recurrent:
             self.pending.index_fill_(0, slot_t, 0)
         last = qs[1:] - 1
+        if hidden_only:
+            return hid.index_select(0, last)
         first = self.model.greedy(hid.index_select(0, last))
         natives = torch.zeros(n, max(self.k, 1), dtype=torch.long, device=dev)
         if self.draft is not None and self.k > 0:

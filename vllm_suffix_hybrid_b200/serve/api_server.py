@@ -163,4 +163,13 @@ def build_app(aeng, tokenizer, model_name: str) -> FastAPI:
                 return JSONResponse(status_code=409, content={"error": str(ex)})
             return {"ingested": n}
 
+    if os.environ.get("SUFFIX_PPLX_DECIDER", "0") == "1":
+        from .decider import DeciderContext, attach
+
+        root = os.environ.get("SUFFIX_PPLX_DECIDER_DIR") or getattr(aeng.engine.cfg, "weights", None)
+        ctx = None
+        if root and os.path.exists(os.path.join(root, "decision_config.json")):
+            ctx = DeciderContext.load(root, aeng.engine.model, {model_name})
+        attach(app, aeng, tokenizer, ctx, aeng.engine.max_model_len)
+
     return app

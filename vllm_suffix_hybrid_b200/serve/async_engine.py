@@ -27,12 +27,13 @@ logger = logging.getLogger("suffix_hybrid.serve")
 
 @dataclass
 class EngineOp:
-    kind: str  # "add" | "abort" | "warm" | "stop"
+    kind: str  # "add" | "abort" | "warm" | "readout" | "stop"
     rid: str = ""
     prompt: List[int] = field(default_factory=list)
     max_new_tokens: int = 0
     stop_token_ids: List[int] = field(default_factory=list)
     sequences: List[List[int]] = field(default_factory=list)
+    payload: Any = None  # readout rows (single-rank engines only)
 
 
 class AsyncEngine:
@@ -101,6 +102,18 @@ class AsyncEngine:
         self._ops.put(EngineOp("warm", key, sequences=[[int(t) for t in s] for s in sequences]))
         return await fut
 
+    async def readout(self, prompt: List[int], rows) -> List[float]:
+        """Score one prompt on the engine thread (LLMEngine.readout); single-rank engines only."""
+        if self.world > 1:
+            raise ValueError("the decision endpoint runs on single-rank engines")
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        key = f"readout-{self.new_rid()}"
+        with self._lock:
+            self._futures[key] = (loop, fut)
+        self._ops.put(EngineOp("readout", key, sequences=[[int(t) for t in prompt]], payload=rows))
+        return await fut
+
     def stats(self) -> dict:
         e = self.engine
         out = dict(self.metrics)
@@ -143,6 +156,11 @@ class AsyncEngine:
             elif op.kind == "abort":
                 if e.abort_request(op.rid):
                     self.metrics["requests_aborted"] += 1
+            elif op.kind == "readout":
+                try:
+                    self._resolve(op.rid, e.readout(op.sequences[0], op.payload))
+                except Exception as ex:
+                    self._resolve(op.rid, ex)
             elif op.kind == "warm":
                 try:
                     n = e.warm_start(op.sequences)
