@@ -168,6 +168,9 @@ class LLMEngine:
         self._lag = self.k + 1 if self._async else 0  # tokens a lagged step may add beyond the host's view
         self._trace_verify = _trace_budget("TRACE_VERIFY2")
         self._trace_sched = _trace_budget("SCHEDTRACE")
+        from ..tune.mtp_tune import MtpTuner
+
+        self.tuner = MtpTuner.from_env(self)  # SUFFIX_MTP_TUNE=1: adapters attach before any graph capture
 
     # ------------------------------------------------------------------ sizing
     def _auto_blocks(self) -> int:
@@ -238,6 +241,24 @@ class LLMEngine:
                 c.add_sequence(toks)
             n += 1
         return n
+
+    @torch.no_grad()
+    def features(self, seq) -> torch.Tensor:
+        """The target's pre-norm hidden state at every position of a token sequence (scratch KV blocks and
+        the scratch recurrent slot; running requests are unaffected)."""
+        self._drain()
+        seq = np.asarray(seq, dtype=np.int64)
+        blocks = self.pool.allocate(blocks_for(len(seq), self.block_size))
+        try:
+            return self.runner.prefill([seq], [blocks], [0], features=True)
+        finally:
+            self.pool.release(blocks)
+
+    def idle_step(self) -> bool:
+        """One bounded slice of idle-time work (online draft-head tuning); False when nothing ran."""
+        if self.tuner is None or self.has_work():
+            return False
+        return self.tuner.micro_step()
 
     def readout(self, prompt, rows: torch.Tensor) -> List[float]:
         """Score one prompt: rows [R, H] . final hidden state at the prompt's last position (fp32).
@@ -525,6 +546,9 @@ class LLMEngine:
             if not r.finished:
                 i += 1
                 continue
+            if self.tuner is not None and r.finish_reason != "abort":
+                self.tuner.capture(r.rid, np.concatenate([np.asarray(r.prompt, dtype=np.int64),
+                                                          np.asarray(r.output, dtype=np.int64)]))
             self.pool.release(r.blocks)
             r.blocks = []
             if r.slot:

@@ -304,9 +304,11 @@ class Runner:
 
     # ------------------------------------------------------------------ prefill
     def prefill(self, prompts: List[np.ndarray], block_tables: List[List[int]],
-                state_slots: Optional[List[int]] = None, hidden_only: bool = False):
-        """Prefill a batch of prompts (each fully). Returns (first tokens [n], native drafts [n, k]), or with
-        hidden_only the final normalised hidden state at each prompt's last position [n, H] (scoring)."""
+                state_slots: Optional[List[int]] = None, hidden_only: bool = False, features: bool = False):
+        """Prefill a batch of prompts (each fully). Returns (first tokens [n], native drafts [n, k]); with
+        hidden_only the final normalised hidden state at each prompt's last position [n, H] (scoring);
+        with features the target's pre-norm hidden state at every prompt position [sum(len), H] (the draft
+        head's input features, for its training replay)."""
         dev = self.device
         n = len(prompts)
         lens = [len(p) for p in prompts]
@@ -334,6 +336,8 @@ class Runner:
         if self.recurrent:
             self.pending.index_fill_(0, slot_t, 0)
         last = qs[1:] - 1
+        if features:
+            return pre
         if hidden_only:
             return hid.index_select(0, last)
         first = self.model.greedy(hid.index_select(0, last))

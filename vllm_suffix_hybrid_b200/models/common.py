@@ -90,8 +90,18 @@ class Linear:
         self.weight.copy_(self.shard(full.to(self.weight.device)).to(self.weight.dtype))
 
     push = True  # row-parallel: may push its rows to the owner ranks (finished by all_reduce_add_rms_norm)
+    # Low-rank adapter (A [r, in_local], B [out_local, r], scale) of online draft tuning: y += scale * x A^T B^T,
+    # added to this rank's (partial) output before any reduction; updated in place so captured graphs see it.
+    lora = None
 
     def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None):
+        if self.lora is not None:
+            if out is None and self.parallel == "row":
+                out = comm.partial_out(x.shape[0], self.out_f, x)
+            y = ops.linear(x, self.weight, out)
+            a, b, scale = self.lora
+            y.add_(torch.matmul(torch.matmul(x, a.t()), b.t()), alpha=scale)
+            return y
         if out is None and self.parallel == "row":
             if self.push and comm.can_push(x.shape[0], self.out_f, x):
                 return comm.push_gemm(x, self.weight)  # reduce-scatter inside the GEMM epilogue

@@ -156,6 +156,8 @@ class AsyncEngine:
             elif op.kind == "abort":
                 if e.abort_request(op.rid):
                     self.metrics["requests_aborted"] += 1
+            elif op.kind == "tune":
+                e.idle_step()
             elif op.kind == "readout":
                 try:
                     self._resolve(op.rid, e.readout(op.sequences[0], op.payload))
@@ -222,6 +224,12 @@ class AsyncEngine:
         while alive:
             idle = not e.has_work()
             ops = self._drain(block=idle) if self.rank == 0 else []
+            tuner = getattr(e, "tuner", None)
+            if tuner is not None and self.rank == 0:
+                if not idle or ops:
+                    tuner.note_work()
+                elif tuner.wants_step():
+                    ops.append(EngineOp("tune"))  # every rank runs the same idle micro-step
             if self.world > 1:
                 ops = self._sync_ops(ops)
             alive = self._apply(ops)
