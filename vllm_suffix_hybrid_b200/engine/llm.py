@@ -158,7 +158,9 @@ class LLMEngine:
         # Async scheduling (lag-1 drafting, SUFFIX_HYBRID_ASYNC=1): suffix / hybrid only; other methods keep
         # synchronous scheduling (the reference's sched_sync rule, sched_sync.py:85).
         self._pipe = None
-        self._async = bool(spec.async_scheduling and self.k > 0 and spec.method in ("suffix", "hybrid"))
+        self.dp = st.dp
+        self._async = bool(spec.async_scheduling and self.k > 0 and spec.method in ("suffix", "hybrid")
+                           and self.dp == 1)
         if spec.async_scheduling and not self._async:
             logger.warning("SUFFIX_HYBRID_ASYNC ignored for method %r: synchronous scheduling", spec.method)
         self._cand_len = 2 * self.k + 1
@@ -281,9 +283,38 @@ class LLMEngine:
         return dict(get()) if get else {}
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running or self._pipe is not None)
+        local = bool(self.waiting or self.running or self._pipe is not None)
+        if self.dp > 1:  # data-parallel attention: every rank steps while any rank has work
+            return bool(self._dp_gather([int(local)]).max())
+        return local
+
+    def _dp_gather(self, values) -> torch.Tensor:
+        """[world, len(values)] of every rank's values (control plane, gloo)."""
+        import torch.distributed as dist
+
+        st = pstate.get()
+        t = torch.tensor(values, dtype=torch.long)
+        out = [torch.empty_like(t) for _ in range(st.world)]
+        dist.all_gather(out, t, group=st.cpu_group)
+        return torch.stack(out)
+
+    def _dp_step(self) -> StepStats:
+        """Lockstep step under data-parallel attention: all ranks run the same kind of step with the same
+        padded shapes (every MoE layer exchanges equal token counts), idle ranks run padding only."""
+        free = self.cfg.max_num_seqs - len(self.running)
+        batch = self._select_prefill(free) if (self.waiting and free > 0) else []
+        info = self._dp_gather([len(batch), sum(len(r.prompt) for r in batch), len(self.running)])
+        if int(info[:, 0].max()) > 0:
+            n_max = int(info[:, 0].max())
+            t_max = int((info[:, 1] + (n_max - info[:, 0])).max())
+            return self._prefill_step(0, batch=batch, pad=(n_max, t_max))
+        if int(info[:, 2].max()) > 0:
+            return self._decode_step(nb_min=int(info[:, 2].max()))
+        return StepStats("idle", 0, 0, 0, 0.0, 0.0, 0.0)
 
     def step(self) -> StepStats:
+        if self.dp > 1:
+            return self._dp_step()
         free_rows = self.cfg.max_num_seqs - len(self.running)
         if self.waiting and free_rows > 0:
             self._drain()
@@ -320,8 +351,7 @@ class LLMEngine:
         if need > 0:
             r.blocks.extend(self.pool.allocate(need))
 
-    def _prefill_step(self, free_rows: int) -> StepStats:
-        t0 = time.perf_counter()
+    def _select_prefill(self, free_rows: int) -> list:
         batch, budget = [], self.cfg.max_prefill_tokens
         while self.waiting and len(batch) < free_rows:
             r = self.waiting[0]
@@ -330,11 +360,30 @@ class LLMEngine:
             self.waiting.pop(0)
             batch.append(r)
             budget -= len(r.prompt)
+        return batch
+
+    def _prefill_step(self, free_rows: int, batch: Optional[list] = None, pad: Optional[tuple] = None) -> StepStats:
+        """Prefill a batch; pad = (prompts, tokens) adds padding prompts on the scratch block and slot so every
+        data-parallel rank runs the same shapes (their results are dropped)."""
+        t0 = time.perf_counter()
+        if batch is None:
+            batch = self._select_prefill(free_rows)
         for r in batch:
             self._ensure_blocks(r, len(r.prompt) + 2 * self.k + 2)
             r.slot = self._free_slots.pop()
-        first, natives = self.runner.prefill([r.prompt for r in batch], [r.blocks for r in batch],
-                                             [r.slot for r in batch])
+        prompts = [r.prompt for r in batch]
+        tables = [r.blocks for r in batch]
+        slots = [r.slot for r in batch]
+        if pad is not None:
+            n_pad = pad[0] - len(batch)
+            left = pad[1] - sum(len(p) for p in prompts)
+            for j in range(n_pad):
+                ln = left - (n_pad - 1 - j) if j == 0 else 1
+                left -= ln
+                prompts.append(np.zeros(ln, dtype=np.int64))
+                tables.append([0] * blocks_for(ln + 2 * self.k + 2, self.block_size))
+                slots.append(0)
+        first, natives = self.runner.prefill(prompts, tables, slots)
         for i, r in enumerate(batch):
             row = len(self.running)
             self.running.append(r)
@@ -392,10 +441,10 @@ class LLMEngine:
             r.drafts = [int(x) for x in d]
         return (time.perf_counter_ns() - t0) / 1e3
 
-    def _decode_step(self) -> StepStats:
+    def _decode_step(self, nb_min: int = 0) -> StepStats:
         t0 = time.perf_counter()
         n = len(self.running)
-        if n == 0:
+        if n == 0 and nb_min == 0:
             return StepStats("idle", 0, 0, 0, 0.0, 0.0, 0.0)
         k, W = self.k, self.k + 1
         win = np.full((n, W), 0, dtype=np.int64)
@@ -413,7 +462,7 @@ class LLMEngine:
             seq[i] = r.committed
             bt[i, :len(r.blocks)] = r.blocks
         t1 = time.perf_counter()
-        out, acc, nat = self.runner.decode(n, win, seq, bt, slots)
+        out, acc, nat = self.runner.decode(n, win, seq, bt, slots, nb_min=nb_min)
         t2 = time.perf_counter()
         emitted = 0
         accepted = 0

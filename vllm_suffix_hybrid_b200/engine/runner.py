@@ -238,9 +238,11 @@ class Runner:
             f1 = dpre.index_select(0, sel)
             self.native[:nb].copy_(self._draft_steps(d1, f1, lnew, bt, nb))
 
-    def decode(self, nb_real: int, win: np.ndarray, seq: np.ndarray, bt: np.ndarray, slots: np.ndarray = None):
-        """Run one decode step; returns host views (out_tokens, accept, native)."""
-        nb = bucket_for(nb_real, self.max_batch)
+    def decode(self, nb_real: int, win: np.ndarray, seq: np.ndarray, bt: np.ndarray, slots: np.ndarray = None,
+               nb_min: int = 0):
+        """Run one decode step; returns host views (out_tokens, accept, native).  nb_min raises the batch
+        bucket (data-parallel ranks run the same bucket; rows past nb_real are scratch padding)."""
+        nb = bucket_for(max(nb_real, nb_min, 1), self.max_batch)
         self.h_win[:nb_real].numpy()[:] = win
         self.h_seq[:nb_real].numpy()[:] = seq
         self.h_bt[:nb_real].numpy()[:, :bt.shape[1]] = bt

@@ -18,6 +18,10 @@ from ..parallel import comm, state
 from .common import MLP, Linear, init_weight
 
 
+def st_dp() -> int:
+    return state.get().dp
+
+
 class MoEBlock:
     def __init__(self, cfg, dtype, device, gen):
         st = state.get()
@@ -91,7 +95,7 @@ class MoEBlock:
         if self.ep > 1:
             from ..parallel import ep
 
-            out = ep.dispatch_combine(self, x, ids, w)
+            out = ep.dp_dispatch_combine(self, x, ids, w) if st_dp() > 1 else ep.dispatch_combine(self, x, ids, w)
         elif self.fp4 is not None:
             out = ops.moe_experts_nvfp4(x, ids, w, self.fp4[0], self.fp4[1], self.E, self.F)
         else:

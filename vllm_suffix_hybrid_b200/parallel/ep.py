@@ -1,5 +1,11 @@
 """Expert parallelism: each of the N ranks holds E/N routed experts.
 
+Two layouts.  With replicated (or tensor-parallel) attention every rank sees every token:
+`dispatch_combine` below.  With data-parallel attention (state.dp > 1) every rank holds different
+tokens: `dp_dispatch_combine` gathers all ranks' tokens and routes, runs this rank's experts over them
+and reduce-scatters the partial outputs back to their owners (the engine pads every rank to the same
+token count per call).
+
 Layout of the reference's EP (reference: suffix_hybrid/kernels/nvfp4_moe.py:78-84,449-457 and
 docs/dsv41-comms.md:54-58): every rank sees every token (attention is replicated or tensor
 parallel), the router runs on every rank, each rank computes only the (token, expert) pairs of its
@@ -33,3 +39,47 @@ def dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -
     else:
         out = ops.moe_experts(x, ids_l, w_l, moe.w13, moe.w2, moe.E_local, moe.F, out=out)
     return comm.all_reduce(out, force=True)
+
+
+def _all_gather(x: torch.Tensor) -> torch.Tensor:
+    import torch.distributed as dist
+
+    st = state.get()
+    x = x.contiguous()
+    if x.is_cuda:
+        out = torch.empty((st.world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(out, x, group=st.group)
+        return out
+    parts = [torch.empty_like(x) for _ in range(st.world)]
+    dist.all_gather(parts, x, group=st.group)
+    return torch.cat(parts, 0)
+
+
+def _reduce_scatter(y: torch.Tensor) -> torch.Tensor:
+    import torch.distributed as dist
+
+    st = state.get()
+    T = y.shape[0] // st.world
+    if y.is_cuda:
+        out = torch.empty((T,) + tuple(y.shape[1:]), dtype=y.dtype, device=y.device)
+        dist.reduce_scatter_tensor(out, y.contiguous(), group=st.group)
+        return out
+    y = y.contiguous().clone()
+    dist.all_reduce(y, group=st.group)  # gloo has no reduce-scatter
+    return y[st.rank * T:(st.rank + 1) * T].contiguous()
+
+
+def dp_dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Data-parallel attention: every rank's tokens through this rank's experts; each rank keeps its own rows.
+
+    x [T, H] (T equal on every rank), ids / w [T, k] from the local router; returns [T, H]."""
+    st = state.get()
+    xs = _all_gather(x)
+    ids_a = _all_gather(ids)
+    w_a = _all_gather(w)
+    ids_l, w_l = local_routes(ids_a, w_a, st.ep_rank * moe.E_local, moe.E_local)
+    if moe.fp4 is not None:
+        part = ops.moe_experts_nvfp4(xs, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F)
+    else:
+        part = ops.moe_experts(xs, ids_l, w_l, moe.w13, moe.w2, moe.E_local, moe.F)
+    return _reduce_scatter(part)

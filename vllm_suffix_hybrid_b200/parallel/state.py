@@ -24,6 +24,8 @@ class ParallelState:
     tp_rank: int = 0
     ep: int = 1
     ep_rank: int = 0
+    dp: int = 1  # data-parallel attention: each rank serves its own requests (MoE experts shared by EP)
+    dp_rank: int = 0
     group: Optional[object] = None  # device collectives
     cpu_group: Optional[object] = None  # control plane
 
@@ -35,8 +37,11 @@ def get() -> ParallelState:
     return _STATE
 
 
-def init(tp: int = 1, ep: int = 1, backend: Optional[str] = None, timeout_s: int = 300) -> ParallelState:
-    """Initialise from torchrun env vars (RANK/WORLD_SIZE/LOCAL_RANK/MASTER_*)."""
+def init(tp: int = 1, ep: int = 1, backend: Optional[str] = None, timeout_s: int = 300, dp: int = 1) -> ParallelState:
+    """Initialise from torchrun env vars (RANK/WORLD_SIZE/LOCAL_RANK/MASTER_*).
+
+    dp = world (with tp = 1) selects data-parallel attention: every rank runs attention and dense layers for
+    its own requests, and MoE layers exchange tokens with the other ranks (expert parallel over the world)."""
     global _STATE
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -57,8 +62,11 @@ def init(tp: int = 1, ep: int = 1, backend: Optional[str] = None, timeout_s: int
         raise ValueError(f"tensor parallel size {tp} must equal the world size {world} on one box")
     if ep > 1 and ep != world:
         raise ValueError(f"expert parallel size {ep} must equal the world size {world} on one box")
+    if dp > 1 and (dp != world or tp > 1):
+        raise ValueError(f"data-parallel attention needs dp == world size ({world}) and tp == 1")
     _STATE = ParallelState(rank=rank, world=world, local_rank=local, tp=tp, tp_rank=rank if tp > 1 else 0, ep=ep,
-                           ep_rank=rank if ep > 1 else 0, group=group, cpu_group=cpu_group)
+                           ep_rank=rank if ep > 1 else 0, dp=dp, dp_rank=rank if dp > 1 else 0, group=group,
+                           cpu_group=cpu_group)
     return _STATE
 
 
