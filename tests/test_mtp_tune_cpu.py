@@ -56,7 +56,11 @@ def test_replay_matches_the_serving_draft_chain(tune_env):
     assert toks[0].tolist() == natives[0][:4].tolist()
 
 
-def test_training_gate_promotion_and_rollback(tune_env):
+def test_training_gate_promotion_and_rollback(tune_env, monkeypatch):
+    monkeypatch.setenv("SUFFIX_MTP_TUNE_LR", "3e-3")
+    monkeypatch.setenv("SUFFIX_MTP_TUNE_ACCUM", "2")
+    monkeypatch.setenv("SUFFIX_MTP_TUNE_STEP_MS", "1")  # one sequence per micro-step: load-independent
+    monkeypatch.setenv("SUFFIX_MTP_TUNE_EVAL_EVERY", "100000")
     eng = LLMEngine(_cfg())
     tuner = eng.tuner
     rng = np.random.default_rng(3)
@@ -66,12 +70,12 @@ def test_training_gate_promotion_and_rollback(tune_env):
         tuner.capture(f"req-{i}", seq)
     assert len(tuner.train) >= 2 and len(tuner.heldout) >= 1
     first = None
-    for _ in range(40):
+    while tuner.stats["opt_steps"] < 60:
         tuner.micro_step()
         first = first if first is not None else tuner.stats["last_loss"]
-    assert tuner.stats["opt_steps"] >= 5 and tuner.stats["last_loss"] < first
+    assert tuner.stats["last_loss"] < first
     live, cand, anchors, _ = tuner.evaluate()
-    assert anchors > 0 and cand >= live
+    assert anchors > 0 and cand > live
     tuner.promote()
     for n, (a, b) in tuner.live.items():
         assert torch.equal(b, tuner.cand[n][1].detach().to(b.dtype))
