@@ -173,6 +173,9 @@ class LLMEngine:
         from ..tune.mtp_tune import MtpTuner
 
         self.tuner = MtpTuner.from_env(self)  # SUFFIX_MTP_TUNE=1: adapters attach before any graph capture
+        from ..tune.sft import SftTrainer
+
+        self.sft = SftTrainer.from_env(self)  # SUFFIX_SFT=1: adapters on the served model, before capture
 
     # ------------------------------------------------------------------ sizing
     def _auto_blocks(self) -> int:

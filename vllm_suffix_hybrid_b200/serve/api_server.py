@@ -163,6 +163,11 @@ def build_app(aeng, tokenizer, model_name: str) -> FastAPI:
                 return JSONResponse(status_code=409, content={"error": str(ex)})
             return {"ingested": n}
 
+    if getattr(aeng.engine, "sft", None) is not None:
+        from .sft_api import attach as attach_sft
+
+        attach_sft(app, aeng, tokenizer)
+
     if os.environ.get("SUFFIX_PPLX_DECIDER", "0") == "1":
         from .decider import DeciderContext, attach
 

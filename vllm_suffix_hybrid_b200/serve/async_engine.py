@@ -114,6 +114,17 @@ class AsyncEngine:
         self._ops.put(EngineOp("readout", key, sequences=[[int(t) for t in prompt]], payload=rows))
         return await fut
 
+    async def sft_call(self, kind: str, payload) -> Any:
+        """Run an SFT control op on the engine thread (every rank, in step order): "sft_begin" (returns the
+        run id; training then proceeds between serving steps) or "sft_load"."""
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        key = f"{kind}-{self.new_rid()}"
+        with self._lock:
+            self._futures[key] = (loop, fut)
+        self._ops.put(EngineOp(kind, key, payload=payload))
+        return await fut
+
     def stats(self) -> dict:
         e = self.engine
         out = dict(self.metrics)
@@ -156,6 +167,19 @@ class AsyncEngine:
             elif op.kind == "abort":
                 if e.abort_request(op.rid):
                     self.metrics["requests_aborted"] += 1
+            elif op.kind in ("sft_begin", "sft_load", "sft_step"):
+                try:
+                    if e.sft is None:
+                        raise RuntimeError("SFT is not enabled (SUFFIX_SFT=1)")
+                    if op.kind == "sft_begin":
+                        res = e.sft.begin(**op.payload)
+                    elif op.kind == "sft_load":
+                        res = e.sft.load(op.payload)
+                    else:
+                        res = e.sft.micro()
+                    self._resolve(op.rid, res)
+                except Exception as ex:
+                    self._resolve(op.rid, ex)
             elif op.kind == "tune":
                 e.idle_step()
             elif op.kind == "readout":
@@ -224,6 +248,9 @@ class AsyncEngine:
         while alive:
             idle = not e.has_work()
             ops = self._drain(block=idle) if self.rank == 0 else []
+            sft = getattr(e, "sft", None)
+            if sft is not None and self.rank == 0 and sft.wants_step(busy=not idle):
+                ops.append(EngineOp("sft_step"))  # one optimizer step of the active run, on every rank
             tuner = getattr(e, "tuner", None)
             if tuner is not None and self.rank == 0:
                 if not idle or ops:

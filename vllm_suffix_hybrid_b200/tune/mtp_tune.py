@@ -94,12 +94,12 @@ class MtpTuner:
         for n, lin in self.lin.items():
             out_f, in_f = lin.weight.shape
             a0 = torch.randn(self.cfg.rank, in_f, generator=g) / math.sqrt(in_f)
-            a = a0.to(lin.weight.device, lin.weight.dtype)
+            a = a0.to(lin.weight.device, lin.weight.dtype, copy=True)  # live and candidate never share storage
             b = torch.zeros(out_f, self.cfg.rank, device=lin.weight.device, dtype=lin.weight.dtype)
             lin.lora = (a, b, self.scale)
             lin.push = False  # the adapter adds to the materialised partial output
             self.live[n] = (a, b)
-            ca = torch.nn.Parameter(a0.to(lin.weight.device).float())
+            ca = torch.nn.Parameter(a0.to(lin.weight.device, torch.float32, copy=True))
             cb = torch.nn.Parameter(torch.zeros(out_f, self.cfg.rank, device=lin.weight.device))
             self.cand[n] = (ca, cb)
             params += [ca, cb]

@@ -159,3 +159,55 @@ def train_loss(draft, ad, seq: torch.Tensor, feats: torch.Tensor, start: int = 0
     logits, _, _, _ = teacher_forced(draft, ad, seq[1:n + 1], feats[:n], pos)
     loss = F.cross_entropy(logits[start:], seq[start + 2:n + 2])
     return loss, n - start
+
+
+# ---------------------------------------------------------------------------------------- target model
+def layer_linears(layer, prefix: str) -> Dict[str, object]:
+    return {prefix + "qkv": layer.attn.qkv, prefix + "o": layer.attn.o, prefix + "gate_up": layer.mlp.gate_up,
+            prefix + "down": layer.mlp.down}
+
+
+def target_linears(model) -> Dict[str, object]:
+    out = {}
+    for i, L in enumerate(model.layers):
+        out.update(layer_linears(L, f"layers.{i}."))
+    return out
+
+
+def _layer(L, ad: dict, prefix: str, residual: torch.Tensor, positions: torch.Tensor, eps: float) -> torch.Tensor:
+    """One decoder layer (models/common.py DecoderLayer) on the residual stream, causal over the sequence."""
+    A = L.attn
+    x = copy_to_tp(_rms(residual, L.input_norm.weight, eps))
+    qkv = _lin(x, A.qkv, ad.get(prefix + "qkv"))
+    t = qkv.shape[0]
+    q = ref.apply_rope(qkv[:, : A.hq * A.d].view(t, A.hq, A.d), positions, A.cos_sin)
+    k = ref.apply_rope(qkv[:, A.hq * A.d:(A.hq + A.hk) * A.d].view(t, A.hk, A.d), positions, A.cos_sin)
+    v = qkv[:, (A.hq + A.hk) * A.d:].view(t, A.hk, A.d)
+    g = A.hq // A.hk
+    attn = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0),
+                                          k.repeat_interleave(g, dim=1).transpose(0, 1).unsqueeze(0),
+                                          v.repeat_interleave(g, dim=1).transpose(0, 1).unsqueeze(0),
+                                          is_causal=True, scale=A.scale)[0].transpose(0, 1)
+    residual = residual + reduce_from_tp(_lin(attn.reshape(t, -1), A.o, ad.get(prefix + "o")))
+    h = copy_to_tp(_rms(residual, L.post_norm.weight, L.post_norm.eps))
+    gu = _lin(h, L.mlp.gate_up, ad.get(prefix + "gate_up"))
+    gg, u = gu.chunk(2, dim=-1)
+    return residual + reduce_from_tp(_lin(F.silu(gg) * u, L.mlp.down, ad.get(prefix + "down")))
+
+
+def target_logits(model, ad: Optional[dict], tokens: torch.Tensor, checkpoint: bool = True) -> torch.Tensor:
+    """Full target forward (Llama family) over one sequence: logits [T, V] (vocab gathered under TP).
+    checkpoint recomputes each layer in the backward pass (activation memory of one layer)."""
+    ad = ad or {}
+    eps = model.cfg.norm_eps
+    positions = torch.arange(tokens.shape[0], device=tokens.device)
+    residual = model.embed[tokens].float()
+    for i, L in enumerate(model.layers):
+        fn = lambda r, L=L, i=i: _layer(L, ad, f"layers.{i}.", r, positions, eps)
+        if checkpoint and residual.requires_grad:
+            residual = torch.utils.checkpoint.checkpoint(fn, residual, use_reentrant=False)
+        else:
+            residual = fn(residual)
+    normed = _rms(residual, model.norm.weight, model.norm.eps)
+    lm = model.lm_head
+    return gather_from_tp(F.linear(copy_to_tp(normed).to(lm.weight.dtype), lm.weight).float())
