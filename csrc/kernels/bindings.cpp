@@ -235,16 +235,20 @@ void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor latent, torch:
                 c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_ml, double scale,
                 torch::Tensor err) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.is_contiguous(), "mla: q [T,H,C]");
-  TORCH_CHECK(latent.scalar_type() == at::kBFloat16 && latent.dim() == 3 && latent.size(1) == 64 &&
-                  latent.is_contiguous(), "mla: latent [blocks, 64, C]");
+  const bool fp4 = latent.scalar_type() == at::kByte;
+  TORCH_CHECK((fp4 || latent.scalar_type() == at::kBFloat16) && latent.dim() == 3 && latent.size(1) == 64 &&
+                  latent.is_contiguous(), "mla: latent [blocks, 64, C] bf16 or NVFP4 rows [blocks, 64, row_bytes]");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.dim() == 3, "mla: out [T,H,V]");
   TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kLong &&
                   q_start.scalar_type() == at::kLong, "mla: index dtypes");
   const int C = static_cast<int>(q.size(2)), V = static_cast<int>(out.size(2));
-  TORCH_CHECK(latent.size(2) == C, "mla: latent width");
+  TORCH_CHECK(latent.size(2) == (fp4 ? sh_mla_fp4_row_bytes(V, C - V) : C), "mla: latent width");
   MlaParams p{};
   p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
-  p.latent = reinterpret_cast<const __nv_bfloat16*>(latent.data_ptr());
+  if (fp4)
+    p.latent_fp4 = latent.data_ptr<uint8_t>();
+  else
+    p.latent = reinterpret_cast<const __nv_bfloat16*>(latent.data_ptr());
   p.block_tables = block_tables.data_ptr<int32_t>();
   p.bt_stride = block_tables.stride(0);
   p.seq_lens = seq_lens.data_ptr<int64_t>();
@@ -272,6 +276,19 @@ void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor latent, torch:
 }
 
 void mla_cache_write(torch::Tensor latent, torch::Tensor c, torch::Tensor kpe, torch::Tensor slots) {
+  if (latent.scalar_type() == at::kByte) {  // NVFP4 latent rows
+    TORCH_CHECK(c.scalar_type() == at::kBFloat16 && kpe.scalar_type() == at::kBFloat16 &&
+                    slots.scalar_type() == at::kLong && c.stride(1) == 1 && kpe.stride(1) == 1 &&
+                    latent.is_contiguous() && latent.size(2) == sh_mla_fp4_row_bytes(c.size(1), kpe.size(1)),
+                "mla_cache_write: NVFP4 cache rows");
+    const int r = sh_mla_cache_write_fp4(latent.data_ptr<uint8_t>(), reinterpret_cast<const __nv_bfloat16*>(c.data_ptr()),
+                                         c.stride(0), reinterpret_cast<const __nv_bfloat16*>(kpe.data_ptr()),
+                                         kpe.stride(0), slots.data_ptr<int64_t>(), static_cast<int>(c.size(0)),
+                                         static_cast<int>(c.size(1)), static_cast<int>(kpe.size(1)),
+                                         at::cuda::getCurrentCUDAStream());
+    TORCH_CHECK(r == 0, "sh_mla_cache_write_fp4 failed with code ", r);
+    return;
+  }
   TORCH_CHECK(latent.scalar_type() == at::kBFloat16 && c.scalar_type() == at::kBFloat16 &&
                   kpe.scalar_type() == at::kBFloat16 && slots.scalar_type() == at::kLong, "mla_cache_write: dtypes");
   TORCH_CHECK(c.stride(1) == 1 && kpe.stride(1) == 1 && latent.size(2) == c.size(1) + kpe.size(1), "mla_cache_write");
@@ -632,6 +649,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("num_groups") = py::none(), py::arg("rows_p") = 0, py::arg("err") = py::none(),
         py::arg("splits") = 1, py::arg("ws") = py::none(), py::arg("counters") = py::none());
   m.def("spec_advance", &spec_advance);
+  m.def("mla_fp4_row_bytes", [](int64_t cl, int64_t r) { return sh_mla_fp4_row_bytes(cl, r); });
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("moe_route", &moe_route);

@@ -26,6 +26,7 @@
 // positions are written in ascending order (a deterministic key order for the
 // attention that follows).
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -83,11 +84,18 @@ __device__ __forceinline__ int request_of(const int64_t* q_start, int B, int t) 
 }
 __device__ __forceinline__ void bar_pair(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
 
-template <int C, int V>
+__host__ __device__ constexpr int fp4_sc_off(int Cl) { return Cl / 2; }
+__host__ __device__ constexpr int fp4_rope_off(int Cl) { return (Cl / 2 + Cl / 16 + 15) / 16 * 16; }
+__host__ __device__ constexpr int fp4_row_bytes(int Cl, int R) { return (fp4_rope_off(Cl) + 2 * R + 15) / 16 * 16; }
+
+template <int C, int V, bool FP4>
 struct MlaSmem {
   static constexpr int Q_BYTES = ROWS * C * 2;
   static constexpr int KV_BYTES = KEYS * C * 2;
-  static constexpr int P_OFF = Q_BYTES + 2 * KV_BYTES;
+  static constexpr int ROWB = fp4_row_bytes(V, C - V);
+  static constexpr int RAW_BYTES = FP4 ? KEYS * ROWB : 0;  // packed rows of one sub-page (NVFP4 cache)
+  static constexpr int RAW_OFF = Q_BYTES + 2 * KV_BYTES;
+  static constexpr int P_OFF = RAW_OFF + 2 * RAW_BYTES;
   static constexpr int M_OFF = P_OFF + 4 * 16 * P_LD * 2;
   static constexpr int L_OFF = M_OFF + 4 * 2 * 16 * 4;
   static constexpr int I_OFF = L_OFF + 4 * 2 * 16 * 4;  // [3][KEYS] physical cache rows (-1: masked key)
@@ -95,11 +103,19 @@ struct MlaSmem {
   static_assert(TOTAL <= 227 * 1024, "shared memory budget");
 };
 
-template <int C, int V>
+// e2m1 code (bits 0-3) times the e4m3 scale, as bf16 (exact: at most 6 significant bits).  The code's bits
+// placed at bf16 positions 15 / 6..8 read as code_value * 2^-126 (fp32 upper half); two power-of-two
+// multiplies restore the scale without overflow.
+__device__ __forceinline__ float fp4_value(uint32_t code, float scale_x2p63) {
+  const uint32_t bits = ((code & 7u) << 22) | ((code & 8u) << 28);
+  return (__uint_as_float(bits) * 9.223372036854775808e18f) * scale_x2p63;
+}
+
+template <int C, int V, bool FP4>
 __global__ void __launch_bounds__(THREADS, 1) mla_decode_kernel(MlaParams p) {
   shk::pdl_trigger();
   shk::pdl_wait();
-  using S = MlaSmem<C, V>;
+  using S = MlaSmem<C, V, FP4>;
   constexpr int CH = C / 8;        // 16-byte chunks per row
   constexpr int KSTEPS = C / 16;
   constexpr int VH = V / 2;        // value columns per warp
@@ -137,13 +153,57 @@ __global__ void __launch_bounds__(THREADS, 1) mla_decode_kernel(MlaParams p) {
   auto row_of = [&](int64_t pos) -> int64_t {
     return pos < 0 ? -1 : static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63);
   };
-  // Issue the cp.async gather of sub-page j (rows already in sRow[j % 3]) into stage st.
+  // Issue the cp.async gather of sub-page j (rows already in sRow[j % 3]) into stage st (NVFP4: the packed
+  // rows go to the raw ring and are decoded into the stage by `decode_page`).
+  const uint32_t sRaw = sQ + S::RAW_OFF;
   auto load_page = [&](int j, int st) {
     const int64_t* rows = sRow + (j % 3) * KEYS;
-    for (int c = tid; c < KEYS * CH; c += THREADS) {
-      const int key = c / CH, cc = c % CH;
-      const int64_t row = rows[key];
-      cp_async16(sKV + st * S::KV_BYTES + swz<KEYS>(key, cc), p.latent + (row < 0 ? 0 : row) * C + cc * 8, row >= 0);
+    if constexpr (FP4) {
+      constexpr int RCH = S::ROWB / 16;
+      for (int c = tid; c < KEYS * RCH; c += THREADS) {
+        const int key = c / RCH, cc = c % RCH;
+        const int64_t row = rows[key];
+        cp_async16(sRaw + st * S::RAW_BYTES + key * S::ROWB + cc * 16,
+                   p.latent_fp4 + (row < 0 ? 0 : row) * S::ROWB + cc * 16, row >= 0);
+      }
+    } else {
+      for (int c = tid; c < KEYS * CH; c += THREADS) {
+        const int key = c / CH, cc = c % CH;
+        const int64_t row = rows[key];
+        cp_async16(sKV + st * S::KV_BYTES + swz<KEYS>(key, cc), p.latent + (row < 0 ? 0 : row) * C + cc * 8,
+                   row >= 0);
+      }
+    }
+  };
+  // NVFP4: packed latent blocks -> bf16 chunks of the swizzled stage; rope chunks copied as they are.
+  auto decode_page = [&](int st) {
+    constexpr int NB = V / 16;
+    const uint8_t* raw = smem + S::RAW_OFF + st * S::RAW_BYTES;
+    uint8_t* kvp = smem + S::Q_BYTES + st * S::KV_BYTES;
+    for (int i = tid; i < KEYS * NB; i += THREADS) {
+      const int key = i / NB, blk = i % NB;
+      const uint8_t* r = raw + key * S::ROWB;
+      const uint2 pk = *reinterpret_cast<const uint2*>(r + blk * 8);
+      __nv_fp8_e4m3 s8;
+      s8.__x = r[fp4_sc_off(V) + blk];
+      const float sc = static_cast<float>(s8) * 9.223372036854775808e18f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t w = h ? pk.y : pk.x;
+        uint32_t outw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t byte = (w >> (8 * e)) & 0xFFu;
+          outw[e] = pack2(fp4_value(byte & 15u, sc), fp4_value(byte >> 4, sc));
+        }
+        *reinterpret_cast<uint4*>(kvp + swz<KEYS>(key, blk * 2 + h)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+      }
+    }
+    constexpr int RC = (C - V) * 2 / 16;
+    for (int i = tid; i < KEYS * RC; i += THREADS) {
+      const int key = i / RC, rc = i % RC;
+      *reinterpret_cast<uint4*>(kvp + swz<KEYS>(key, V / 8 + rc)) =
+          *reinterpret_cast<const uint4*>(raw + key * S::ROWB + fp4_rope_off(V) + rc * 16);
     }
   };
 
@@ -178,6 +238,10 @@ __global__ void __launch_bounds__(THREADS, 1) mla_decode_kernel(MlaParams p) {
     if (warp == 0) nxt_pos = key_pos(j + 2, lane);
     asm volatile("cp.async.wait_group 1;\n" ::);
     __syncthreads();
+    if constexpr (FP4) {
+      decode_page(st);
+      __syncthreads();
+    }
     const uint32_t kv = sKV + st * S::KV_BYTES;
     const int64_t* rows_j = sRow + (j % 3) * KEYS;
     // S = Q K^T for this warp's 16 heads x 16 keys (even and odd k-steps accumulate apart: 4 chains)
@@ -349,6 +413,51 @@ __global__ void cache_write_kernel(__nv_bfloat16* __restrict__ latent, const __n
     dst[i] = i < Cl ? c[t * c_stride + i] : kpe[t * kpe_stride + (i - Cl)];
 }
 
+// NVFP4 latent row writer (layout: sh_mla_fp4_row_bytes): one CTA of 64 threads per token; thread i
+// quantises latent block i (16 values) and threads copy the rope values.
+__device__ __forceinline__ uint32_t e2m1x8(const float* v) {
+  uint32_t out;
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
+      " mov.b32 %0, {b0, b1, b2, b3};\n}"
+      : "=r"(out)
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+  return out;
+}
+
+__global__ void cache_write_fp4_kernel(uint8_t* __restrict__ cache, const __nv_bfloat16* __restrict__ c,
+                                       int64_t c_stride, const __nv_bfloat16* __restrict__ kpe, int64_t kpe_stride,
+                                       const int64_t* __restrict__ slots, int Cl, int R) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  const int t = blockIdx.x;
+  const int64_t slot = slots[t];
+  if (slot < 0) return;
+  uint8_t* row = cache + slot * fp4_row_bytes(Cl, R);
+  const int blk = threadIdx.x;
+  if (blk < Cl / 16) {
+    float v[16];
+    float am = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      v[j] = __bfloat162float(c[t * c_stride + blk * 16 + j]);
+      am = fmaxf(am, fabsf(v[j]));
+    }
+    const __nv_fp8_e4m3 s(am / 6.f);  // round to nearest even, saturating
+    const float sv = static_cast<float>(s);
+    const float inv = sv > 0.f ? 1.f / sv : 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] *= inv;
+    *reinterpret_cast<uint2*>(row + blk * 8) = make_uint2(e2m1x8(v), e2m1x8(v + 8));
+    row[fp4_sc_off(Cl) + blk] = s.__x;
+  }
+  __nv_bfloat16* rope = reinterpret_cast<__nv_bfloat16*>(row + fp4_rope_off(Cl));
+  for (int i = threadIdx.x; i < R; i += blockDim.x) rope[i] = kpe[t * kpe_stride + i];
+}
+
 // ------------------------------------------------------------------------- DSA indexer
 constexpr int IDX_KEYS = 64;     // keys per indexer tile
 constexpr int IDX_THREADS = 512;  // 16 warps: 4 head groups x 4 key quarters
@@ -513,10 +622,10 @@ __global__ void __launch_bounds__(IDX_THREADS, 1) dsa_topk_kernel(DsaParams p) {
 using namespace shk::mla;
 
 namespace {
-template <int C, int V>
+template <int C, int V, bool FP4>
 int launch_mla(const MlaParams& p, cudaStream_t st) {
-  using S = MlaSmem<C, V>;
-  auto k = mla_decode_kernel<C, V>;
+  using S = MlaSmem<C, V, FP4>;
+  auto k = mla_decode_kernel<C, V, FP4>;
   static bool ready = false;
   if (!ready) {
     const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
@@ -551,9 +660,22 @@ int launch_dsa(const DsaParams& p, cudaStream_t st) {
 extern "C" int sh_mla_decode(const MlaParams* p, int C, int V, cudaStream_t stream) {
   if (p->T <= 0) return 0;
   if (p->nsplit < 1 || (p->nsplit > 1 && (!p->part_o || !p->part_ml))) return -1;
-  if (C == 576 && V == 512) return launch_mla<576, 512>(*p, stream);
-  if (C == 128 && V == 64) return launch_mla<128, 64>(*p, stream);
+  const bool fp4 = p->latent_fp4 != nullptr;
+  if (C == 576 && V == 512) return fp4 ? launch_mla<576, 512, true>(*p, stream) : launch_mla<576, 512, false>(*p, stream);
+  if (C == 128 && V == 64) return fp4 ? launch_mla<128, 64, true>(*p, stream) : launch_mla<128, 64, false>(*p, stream);
   return -2;
+}
+
+extern "C" int sh_mla_fp4_row_bytes(int Cl, int R) { return fp4_row_bytes(Cl, R); }
+
+extern "C" int sh_mla_cache_write_fp4(uint8_t* cache, const __nv_bfloat16* c, int64_t c_stride,
+                                      const __nv_bfloat16* kpe, int64_t kpe_stride, const int64_t* slots, int T,
+                                      int Cl, int R, cudaStream_t stream) {
+  if (T <= 0) return 0;
+  if (Cl % 16 != 0 || Cl / 16 > 64) return -2;
+  shk::launch(cache_write_fp4_kernel, dim3(T), dim3(64), 0, stream, cache, c, c_stride, kpe, kpe_stride, slots, Cl,
+              R);
+  return static_cast<int>(cudaGetLastError());
 }
 
 extern "C" int sh_mla_cache_write(__nv_bfloat16* latent, const __nv_bfloat16* c, int64_t c_stride,

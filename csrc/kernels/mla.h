@@ -7,6 +7,7 @@
 struct MlaParams {
   const __nv_bfloat16* q;       // [T, H, C] absorbed queries: [q_nope W_UK | rotated q_pe]
   const __nv_bfloat16* latent;  // paged cache [num_blocks, 64, C]: [normalised c_kv | rotated k_pe]
+  const uint8_t* latent_fp4;    // or the NVFP4 cache [num_blocks, 64, row_bytes] (see sh_mla_fp4_row_bytes)
   const int32_t* block_tables;  // [B, bt_stride]
   int64_t bt_stride;
   const int64_t* seq_lens;      // [B] keys of the request including its new tokens
@@ -41,6 +42,13 @@ extern "C" {
 #endif
 // C % 64 == 0 and V % 64 == 0 (V <= C); supported (C, V): (576, 512), (128, 64).
 int sh_mla_decode(const MlaParams* p, int C, int V, cudaStream_t stream);
+// NVFP4 latent cache row (Cl latent + R rope values): Cl/2 bytes of e2m1 pairs (low nibble first), Cl/16
+// e4m3 block scales at byte Cl/2, the R rope values in bf16 at the next 16-byte boundary; rows padded
+// to 16 bytes (Cl 512, R 64: 416 bytes against 1152 in bf16).  Block scale s = e4m3(amax16 / 6),
+// code = e2m1_rne(x / s); the value read back is code * s.
+int sh_mla_fp4_row_bytes(int Cl, int R);
+int sh_mla_cache_write_fp4(uint8_t* cache, const __nv_bfloat16* c, int64_t c_stride, const __nv_bfloat16* kpe,
+                           int64_t kpe_stride, const int64_t* slots, int T, int Cl, int R, cudaStream_t stream);
 // latent[slot[t]] = cat(c[t], kpe[t]) for slot[t] >= 0 (C = Cl + R).
 int sh_mla_cache_write(__nv_bfloat16* latent, const __nv_bfloat16* c, int64_t c_stride, const __nv_bfloat16* kpe,
                        int64_t kpe_stride, const int64_t* slots, int T, int Cl, int R, cudaStream_t stream);

@@ -1,4 +1,6 @@
 """MLA decode and DSA indexer kernels vs the fp32 PyTorch references; DeepSeek/Kimi engines on the GPU."""
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -122,3 +124,38 @@ def test_deepseek_nvfp4_spec_is_exact_in_batch_invariant_mode(monkeypatch, act):
     base = outs[("none", False)]
     for key, got in outs.items():
         assert got == base, (key, got, base)
+
+
+@pytest.mark.parametrize("C,V", [(576, 512), (128, 64)])
+@pytest.mark.parametrize("sparse", [False, True])
+def test_mla_decode_over_nvfp4_cache(C, V, sparse):
+    """NVFP4 latent rows written by the cache kernel and read by the decode kernel == the fp32 oracle
+    over the quantise-dequantised latent (the values the cache stores)."""
+    torch.manual_seed(C + int(sparse))
+    B, q, H, ctx = 3, 4, 64 if C == 576 else 16, 300
+    T = B * q
+    bs = 64
+    nb = -(-ctx // bs)
+    R = C - V
+    c = (torch.randn(B * ctx, V) * 0.7).to(torch.bfloat16).cuda()
+    kpe = (torch.randn(B * ctx, R) * 0.5).to(torch.bfloat16).cuda()
+    bt = (torch.randperm(B * nb) + 1).view(B, nb).int().cuda()
+    pos = torch.arange(ctx).repeat(B).cuda()
+    req = torch.arange(B).repeat_interleave(ctx).cuda()
+    slots = (bt[req, pos // bs].long() * bs + pos % bs)
+    cache = torch.zeros(B * nb + 1, bs, ops.mla_fp4_row_bytes(V, R), dtype=torch.uint8, device="cuda")
+    ops.mla_cache_write(cache, c, kpe, slots)
+    lat_cpu = torch.zeros(B * nb + 1, bs, C, dtype=torch.float32)
+    ops.mla_cache_write(lat_cpu, c.float().cpu(), kpe.float().cpu(), slots.cpu(), fp4=True)
+    seq = torch.full((B,), ctx, dtype=torch.long, device="cuda")
+    qs = (torch.arange(B + 1) * q).long().cuda()
+    qq = (torch.randn(T, H, C) * 0.3).to(torch.bfloat16).cuda()
+    topk = None
+    if sparse:
+        topk = torch.stack([torch.randperm(ctx - q)[:128].sort().values for _ in range(T)]).int().cuda()
+    scale = 1.0 / math.sqrt(192)
+    got = ops.mla_decode(qq, cache, bt, seq, qs, scale, V, topk, 2)
+    want = ref.mla_attention(qq[..., :V].float().cpu(), qq[..., V:].float().cpu(), lat_cpu, bt.cpu(), seq.cpu(),
+                             qs.cpu(), scale, V, None if topk is None else topk.cpu())
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got.float().cpu(), want.float(), rtol=3e-2, atol=3e-2)

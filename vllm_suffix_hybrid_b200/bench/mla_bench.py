@@ -32,6 +32,7 @@ def main():
     ap.add_argument("--ctx", type=int, default=8192)
     ap.add_argument("--topk", type=int, default=2048)
     ap.add_argument("--dense", action="store_true")
+    ap.add_argument("--fp4", action="store_true", help="NVFP4 latent cache rows instead of bf16")
     ap.add_argument("--nsplit", type=int, default=0)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--once", action="store_true", help="two eager launches, no timing (for ncu)")
@@ -53,6 +54,12 @@ def main():
         g = torch.Generator(device="cuda").manual_seed(0)
         topk = torch.stack([torch.randperm(a.ctx - a.q, device="cuda", generator=g)[:K].sort().values
                             for _ in range(T)]).int()
+    if a.fp4:  # same values written through the NVFP4 cache writer
+        flat = latent.view(-1, C)
+        packed = torch.zeros(latent.shape[0], bs, ops.mla_fp4_row_bytes(V, C - V), dtype=torch.uint8, device="cuda")
+        ops.mla_cache_write(packed, flat[:, :V].contiguous(), flat[:, V:].contiguous(),
+                            torch.arange(flat.shape[0], device="cuda"))
+        latent = packed
     nsplit = a.nsplit or ops.mla_splits(T, a.heads, K)
     run = lambda: ops.mla_decode(q, latent, bt, seq, qs, 1.0 / math.sqrt(192), V, topk, nsplit)
     if a.once:
@@ -64,9 +71,10 @@ def main():
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     us = time_fn(run, flush, a.iters)
     flops = 2.0 * T * a.heads * K * (C + V)
-    gathered = T * K * C * 2  # latent rows read per token (requests' tokens share most of them through L2)
+    row_bytes = latent.shape[2] if a.fp4 else C * 2
+    gathered = T * K * row_bytes  # latent rows read per token (requests' tokens share most of them through L2)
     tf, hbm = peaks()
-    print(json.dumps({"us": round(us, 2), "tokens": T, "heads": a.heads, "keys_per_token": K, "dense": a.dense,
+    print(json.dumps({"us": round(us, 2), "tokens": T, "heads": a.heads, "keys_per_token": K, "dense": a.dense, "fp4_cache": a.fp4,
                       "nsplit": nsplit, "tflops": round(flops / us / 1e6, 1),
                       "frac_of_measured_bf16_peak": round(flops / us / 1e6 / tf, 3),
                       "gathered_gb_s": round(gathered / us / 1e3, 1)}))

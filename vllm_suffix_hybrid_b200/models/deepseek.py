@@ -101,6 +101,7 @@ class MLAttention:
         self.cfg = cfg
         self.H = cfg.heads
         self.nope, self.rope, self.vd, self.lora = cfg.qk_nope, cfg.qk_rope, cfg.v_head, cfg.kv_lora
+        self.kv_fp4 = cfg.kv_format == "nvfp4"  # NVFP4 latent cache (CUDA: packed rows; CPU: the same values)
         self.scale = ops.ref.yarn_softmax_mscale(cfg.rope_scaling) / math.sqrt(self.nope + self.rope)
         h = cfg.hidden
         self.q_a = QLinear(h, cfg.q_lora, dtype, device, gen, fmt) if cfg.q_lora else None
@@ -130,7 +131,7 @@ class MLAttention:
         c = ops.rms_norm(ckv[:, : self.lora].contiguous(), self.kv_a_norm.weight, self.kv_a_norm.eps)
         kpe = ops.ref.apply_rope(ckv[:, self.lora:].reshape(T, 1, self.rope), meta.positions, self.cos_sin)[:, 0]
         q_pe = ops.ref.apply_rope(q[..., self.nope:], meta.positions, self.cos_sin)
-        ops.mla_cache_write(latent, c, kpe.to(c.dtype), meta.slot_mapping)
+        ops.mla_cache_write(latent, c, kpe.to(c.dtype), meta.slot_mapping, fp4=self.kv_fp4)
         wkv = self.kv_b.weight.view(self.H, self.nope + self.vd, self.lora)
         w_uk, w_uv = wkv[:, : self.nope], wkv[:, self.nope:]
         topk = None
@@ -198,9 +199,14 @@ class DeepseekModel:
 
     def allocate_caches(self, num_blocks: int, block_size: int, slots: int, window: int) -> List:
         caches = []
+        fp4 = self.cfg.kv_format == "nvfp4" and torch.device(self.device).type == "cuda"
         for _ in self.layers:
-            lat = torch.zeros(num_blocks, block_size, self.cfg.kv_lora + self.cfg.qk_rope, dtype=self.dtype,
-                              device=self.device)
+            if fp4:  # NVFP4 latent rows (2.8x smaller than bf16 at kv_lora 512)
+                lat = torch.zeros(num_blocks, block_size, ops.mla_fp4_row_bytes(self.cfg.kv_lora, self.cfg.qk_rope),
+                                  dtype=torch.uint8, device=self.device)
+            else:
+                lat = torch.zeros(num_blocks, block_size, self.cfg.kv_lora + self.cfg.qk_rope, dtype=self.dtype,
+                                  device=self.device)
             idx = (torch.zeros(num_blocks, block_size, self.cfg.dsa_head_dim, dtype=self.dtype, device=self.device)
                    if self.cfg.dsa_topk else None)
             caches.append((lat, idx))

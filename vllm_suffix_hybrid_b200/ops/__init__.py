@@ -447,15 +447,24 @@ def nvfp4_dequantize(packed, scales, global_scale, out: torch.Tensor | None = No
 _MLA_WS = {}
 
 
-def mla_cache_write(latent: torch.Tensor, c: torch.Tensor, kpe: torch.Tensor, slots: torch.Tensor) -> None:
-    """latent[slot] = [c | kpe] for every token with slot >= 0 (paged [blocks, 64, C] cache)."""
+def mla_cache_write(latent: torch.Tensor, c: torch.Tensor, kpe: torch.Tensor, slots: torch.Tensor,
+                    fp4: bool = False) -> None:
+    """latent[slot] = [c | kpe] for every token with slot >= 0 (paged [blocks, 64, C] cache).  A uint8 cache
+    holds NVFP4 latent rows (mla_fp4_row_bytes); on CPU, fp4=True stores the values such a cache returns."""
     if not latent.is_cuda:
         bs = latent.shape[1]
         ok = slots >= 0
         s = slots[ok]
-        latent[s // bs, s % bs] = torch.cat([c, kpe.to(c.dtype)], -1)[ok].to(latent.dtype)
+        cc = ref.mla_fp4_qdq(c).to(c.dtype) if fp4 else c
+        latent[s // bs, s % bs] = torch.cat([cc, kpe.to(c.dtype)], -1)[ok].to(latent.dtype)
         return
     native().mla_cache_write(latent, c, kpe, slots)
+
+
+def mla_fp4_row_bytes(kv_lora: int, rope: int) -> int:
+    """Bytes of one NVFP4 latent cache row (kv_lora e2m1 values + e4m3 scales + rope in bf16, 16-aligned)."""
+    r0 = (kv_lora // 2 + kv_lora // 16 + 15) // 16 * 16
+    return (r0 + 2 * rope + 15) // 16 * 16
 
 
 def mla_decode(q: torch.Tensor, latent: torch.Tensor, block_tables, seq_lens, q_start, scale: float, kv_lora: int,

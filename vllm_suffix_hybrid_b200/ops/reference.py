@@ -329,6 +329,19 @@ def nvfp4_w4a4_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tenso
     return (xa @ wv.t()) * a_scale[:, None] * float(global_scale.reshape(-1)[0])
 
 
+def mla_fp4_qdq(c: torch.Tensor) -> torch.Tensor:
+    """Latent values as the NVFP4 latent cache returns them: per 16 values s = e4m3(amax / 6), code =
+    e2m1_rne(x * (1 / s)), value = code * s (fp32)."""
+    shape = c.shape
+    x = c.float().reshape(-1, 16)
+    s = (x.abs().amax(-1) / 6.0).to(torch.float8_e4m3fn).float()
+    inv = torch.where(s > 0, 1.0 / torch.where(s > 0, s, torch.ones_like(s)), torch.zeros_like(s))
+    codes = e2m1_codes(x * inv[:, None])
+    mag = E2M1.to(c.device)[(codes & 7).long()]
+    val = torch.where(codes & 8 > 0, -mag, mag) * s[:, None]
+    return val.reshape(shape)
+
+
 # ----------------------------------------------------------------------------- MLA / DSA
 def mla_attention(q_lat, q_pe, latent, block_tables, seq_lens, q_start, scale, kv_lora, topk=None):
     """Absorbed MLA over a latent cache [blocks, bs, kv_lora + rope].
