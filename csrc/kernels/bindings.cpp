@@ -404,10 +404,12 @@ void nvfp4_quant_act(torch::Tensor x, torch::Tensor xq, torch::Tensor x_sf, torc
 void gemm_fp4mma(torch::Tensor y, torch::Tensor xq, torch::Tensor x_sf, torch::Tensor a_scale, torch::Tensor w,
                  torch::Tensor w_sf, torch::Tensor alpha_w, int64_t bn, c10::optional<torch::Tensor> groups,
                  c10::optional<torch::Tensor> num_groups, int64_t rows_p, c10::optional<torch::Tensor> err,
-                 int64_t splits, c10::optional<torch::Tensor> ws, c10::optional<torch::Tensor> counters) {
+                 int64_t splits, c10::optional<torch::Tensor> ws, c10::optional<torch::Tensor> counters,
+                 bool fp8) {
   TORCH_CHECK(xq.is_cuda() && xq.scalar_type() == at::kByte && xq.is_contiguous() && xq.dim() == 2, "gemm_fp4mma: xq");
   TORCH_CHECK(w.scalar_type() == at::kByte && w.is_contiguous() && w.size(1) == xq.size(1), "gemm_fp4mma: w");
-  const int64_t K = xq.size(1) * 2, kc4 = (K + 255) / 256 * 4;
+  // NVFP4: two codes per byte, 4 scale chunks per 256 k; MXFP8: one code per byte, one chunk per 128 k
+  const int64_t K = fp8 ? xq.size(1) : xq.size(1) * 2, kc4 = fp8 ? K / 128 : (K + 255) / 256 * 4;
   TORCH_CHECK(w_sf.element_size() == 1 && w_sf.is_contiguous() && w_sf.dim() == 3 && w_sf.size(1) == kc4 &&
                   w_sf.size(2) == 512 && x_sf.element_size() == 1 && x_sf.is_contiguous() && x_sf.dim() == 3 &&
                   x_sf.size(1) == kc4, "gemm_fp4mma: scale tiles [tiles, kc4, 512]");
@@ -450,9 +452,38 @@ void gemm_fp4mma(torch::Tensor y, torch::Tensor xq, torch::Tensor x_sf, torch::T
     g.ws = ws->data_ptr<float>();
     g.counters = counters->data_ptr<int>();
   }
-  const int r = sh_gemm_fp4mma(&g, xq.data_ptr(), static_cast<int>(xq.size(0)), static_cast<int>(bn),
-                               static_cast<int>(splits), num_sms, at::cuda::getCurrentCUDAStream());
-  TORCH_CHECK(r == 0, "sh_gemm_fp4mma failed with code ", r);
+  const int r = (fp8 ? sh_gemm_mxfp8 : sh_gemm_fp4mma)(&g, xq.data_ptr(), static_cast<int>(xq.size(0)),
+                                                       static_cast<int>(bn), static_cast<int>(splits), num_sms,
+                                                       at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "block-scaled GEMM failed with code ", r);
+}
+
+// MXFP8 activation quantiser (see sh_mxfp8_quant_act): x bf16 [rows, K] -> xq [rows, K] e4m3,
+// x_sf [tiles, K/128, 512] ue8m0, a_scale [rows] = 1.
+void mxfp8_quant_act(torch::Tensor x, torch::Tensor xq, torch::Tensor x_sf, torch::Tensor a_scale, int64_t tile_rows,
+                     c10::optional<torch::Tensor> groups, c10::optional<torch::Tensor> num_groups) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "mxfp8: x");
+  const int64_t rows = x.size(0), K = x.size(1);
+  TORCH_CHECK(xq.scalar_type() == at::kByte && xq.is_contiguous() && xq.size(0) >= rows && xq.size(1) == K,
+              "mxfp8: xq uint8 [rows, K]");
+  TORCH_CHECK(x_sf.element_size() == 1 && x_sf.is_contiguous() && x_sf.dim() == 3 && x_sf.size(1) == K / 128 &&
+                  x_sf.size(2) == 512, "mxfp8: x_sf [tiles, K/128, 512]");
+  TORCH_CHECK(a_scale.scalar_type() == at::kFloat && a_scale.numel() >= rows, "mxfp8: a_scale");
+  const int4* gp = nullptr;
+  const int* ng = nullptr;
+  int64_t tiles = (rows + tile_rows - 1) / tile_rows;
+  if (groups.has_value()) {
+    TORCH_CHECK(num_groups.has_value() && groups->scalar_type() == at::kInt, "mxfp8: groups");
+    gp = reinterpret_cast<const int4*>(groups->data_ptr<int>());
+    ng = num_groups->data_ptr<int>();
+    tiles = groups->size(0);
+  }
+  TORCH_CHECK(x_sf.size(0) >= tiles, "mxfp8: x_sf has too few tiles");
+  const int r = sh_mxfp8_quant_act(x.data_ptr(), x.stride(0), static_cast<int>(rows), static_cast<int>(K), gp, ng,
+                                   static_cast<int>(tile_rows), xq.data_ptr<uint8_t>(),
+                                   reinterpret_cast<uint8_t*>(x_sf.data_ptr()), a_scale.data_ptr<float>(),
+                                   at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_mxfp8_quant_act failed with code ", r);
 }
 
 template <typename T>
@@ -647,7 +678,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp4mma", &gemm_fp4mma, py::arg("y"), py::arg("xq"), py::arg("x_sf"), py::arg("a_scale"), py::arg("w"),
         py::arg("w_sf"), py::arg("alpha_w"), py::arg("bn"), py::arg("groups") = py::none(),
         py::arg("num_groups") = py::none(), py::arg("rows_p") = 0, py::arg("err") = py::none(),
-        py::arg("splits") = 1, py::arg("ws") = py::none(), py::arg("counters") = py::none());
+        py::arg("splits") = 1, py::arg("ws") = py::none(), py::arg("counters") = py::none(),
+        py::arg("fp8") = false);
+  m.def("mxfp8_quant_act", &mxfp8_quant_act, py::arg("x"), py::arg("xq"), py::arg("x_sf"), py::arg("a_scale"),
+        py::arg("tile_rows"), py::arg("groups") = py::none(), py::arg("num_groups") = py::none());
   m.def("spec_advance", &spec_advance);
   m.def("mla_fp4_row_bytes", [](int64_t cl, int64_t r) { return sh_mla_fp4_row_bytes(cl, r); });
   m.def("gdn_conv", &gdn_conv);

@@ -39,16 +39,25 @@ namespace fp4mma {
 using namespace shk::tc;
 
 constexpr int BM = 128;
-constexpr int KB = 256;         // k elements per pipeline stage
-constexpr int ROW_BYTES = KB / 2;
-constexpr int SF_CHUNK = 512;   // scales of 128 rows x 64 k
+constexpr int KB = 256;         // NVFP4: k elements per pipeline stage (128 bytes per row)
+constexpr int ROW_BYTES = 128;  // bytes per operand row per stage (both formats)
+constexpr int SF_CHUNK = 512;   // scales of 128 rows x 4 blocks
 constexpr int THREADS = 192;
 
-template <int BN, int STAGES>
+// Operand formats: NVFP4 (e2m1 pairs, e4m3 scale per 16, MMA K 64, four scale chunks per 256-wide stage,
+// one per MMA) or MXFP8 (e4m3, ue8m0 scale per 32, MMA K 32, one scale chunk per 128-wide stage whose
+// byte j of every row word serves MMA j).
+template <bool FP8>
+struct Fmt {
+  static constexpr int KB = FP8 ? 128 : 256;
+  static constexpr int CPB = FP8 ? 1 : 4;  // scale chunks per stage and operand
+};
+
+template <int BN, int STAGES, bool FP8 = false>
 struct Smem {
   static constexpr int A_BYTES = BM * ROW_BYTES;
   static constexpr int B_BYTES = BN * ROW_BYTES;
-  static constexpr int SF_BYTES = 4 * SF_CHUNK;  // one operand's scales of one k-block
+  static constexpr int SF_BYTES = Fmt<FP8>::CPB * SF_CHUNK;  // one operand's scales of one k-block
   static constexpr int STAGE = A_BYTES + B_BYTES + 2 * SF_BYTES;
   static constexpr int OUT_OFF = STAGES * STAGE;  // epilogue staging tile: bf16 [BN tokens][BM columns]
   static constexpr int SC_OFF = OUT_OFF + BN * BM * 2;  // alpha_w * a_scale of the tile's tokens [BN]
@@ -60,11 +69,12 @@ struct Smem {
 };
 
 // TMEM columns: two fp32 accumulators of BN columns, then two scale buffers of
-// 32 columns (A chunks 0-3 at +0/+4/+8/+12, B chunks at +16..+28).
-template <int BN>
+// 8 * CPB columns (A chunks at +0/+4/..., B chunks after them).
+template <int BN, bool FP8 = false>
 struct Tmem {
   static constexpr int SF_COL = 2 * BN;
-  static constexpr int USED = 2 * BN + 64;
+  static constexpr int SF_BUF = 8 * Fmt<FP8>::CPB;
+  static constexpr int USED = 2 * BN + 2 * SF_BUF;
   static constexpr int COLS = USED <= 128 ? 128 : (USED <= 256 ? 256 : 512);
 };
 
@@ -83,6 +93,20 @@ __device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
 // e4m3 scales (scale format 0), scale ids 0, M x N, dense K = 64.
 __host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
   return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+// Instruction descriptor of kind::mxf8f6f4: A and B e4m3 (format 0), K-major, ue8m0 scales (scale
+// format 1), M x N, K = 32; the scale ids (bits 4-5 for B, 29-30 for A) pick byte `sf` of the scale words.
+__host__ __device__ constexpr uint32_t idesc_mxf8(int m, int n, uint32_t sf) {
+  return (sf << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (1u << 23) | (static_cast<uint32_t>(m >> 4) << 24) |
+         (sf << 29);
+}
+__device__ __forceinline__ void mma_mxf8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t tsfa, uint32_t tsfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb)
+      : "memory");
 }
 __device__ __forceinline__ void mma_nvf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t tsfa, uint32_t tsfb, uint32_t accumulate) {
@@ -156,12 +180,14 @@ __device__ __forceinline__ Work decode_work(int w, const Fp4MmaParams& g, int bn
   return r;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool FP8>
 __global__ void __launch_bounds__(THREADS, 1)
     fp4mma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   Fp4MmaParams g) {
-  using S = Smem<BN, STAGES>;
-  using TM = Tmem<BN>;
+  using S = Smem<BN, STAGES, FP8>;
+  using TM = Tmem<BN, FP8>;
+  constexpr int KB = Fmt<FP8>::KB;
+  constexpr int CPB = Fmt<FP8>::CPB;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base derived from the shared array itself (the compiler keeps the address space)
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -199,7 +225,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   shk::pdl_wait();
   const uint32_t tmem_base = *tmem_slot;
   const int nkb = (g.K + KB - 1) / KB;
-  const int kc4 = nkb * 4;  // scale chunks per tile
+  const int kc4 = nkb * CPB;  // scale chunks per tile
   const int total = g.groups ? (*g.num_groups) * g.tiles_p : g.tiles_p * g.tiles_q * g.splits;
 
   if (warp == 0) {
@@ -233,7 +259,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t IDESC = idesc_nvf4(BM, BN);
+      constexpr uint32_t IDESC = idesc_nvf4(BM, BN);  // (NVFP4)
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;
@@ -259,16 +285,24 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t sb = sa + S::A_BYTES;
           const uint32_t ssfa = sb + S::B_BYTES;
           const uint32_t ssfb = ssfa + S::SF_BYTES;
-          const uint32_t tsf = tmem_base + TM::SF_COL + (kcount & 1) * 32;
+          const uint32_t tsf = tmem_base + TM::SF_COL + (kcount & 1) * TM::SF_BUF;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < CPB; ++j) {
             tmem_cp_sf(tsf + j * 4, sf_desc(ssfa + j * SF_CHUNK));
-            tmem_cp_sf(tsf + 16 + j * 4, sf_desc(ssfb + j * SF_CHUNK));
+            tmem_cp_sf(tsf + 4 * CPB + j * 4, sf_desc(ssfb + j * SF_CHUNK));
           }
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            mma_nvf4(tmem_d, sw128_desc(sa + j * 32), sw128_desc(sb + j * 32), IDESC, tsf + j * 4, tsf + 16 + j * 4,
-                     (kb > wk.kb0 || j > 0) ? 1u : 0u);
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t acc_on = (kb > wk.kb0 || j > 0) ? 1u : 0u;
+            if constexpr (FP8) {
+              const uint32_t byte = static_cast<uint32_t>(j) << 30;  // scale byte j of each row word
+              mma_mxf8(tmem_d, sw128_desc(sa + j * 32), sw128_desc(sb + j * 32), idesc_mxf8(BM, BN, j), tsf | byte,
+                       (tsf + 4) | byte, acc_on);
+            } else {
+              mma_nvf4(tmem_d, sw128_desc(sa + j * 32), sw128_desc(sb + j * 32), IDESC, tsf + j * 4,
+                       tsf + 16 + j * 4, acc_on);
+            }
+          }
           mma_commit(&empty[s]);
           if (++s == STAGES) {
             s = 0;
@@ -537,6 +571,70 @@ __global__ void __launch_bounds__(QUANT_THREADS) quant_act_kernel(
   }
 }
 
+// MXFP8 activations: per 32 values s = 2^e (ue8m0 byte e + 127) with e the smallest exponent that keeps
+// amax / s <= 448, code = e4m3(x / s) (exact scaling, round to nearest even); a_scale = 1.
+__global__ void __launch_bounds__(QUANT_THREADS) quant_act_mx8_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, int rows, int K, const int4* __restrict__ groups,
+    const int* __restrict__ num_groups, int tile_rows, uint8_t* __restrict__ xq, uint8_t* __restrict__ x_sf,
+    float* __restrict__ a_scale) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  const int r = blockIdx.x;
+  int t, slot;
+  if (groups) {
+    int lo = 0, hi = *num_groups - 1;
+    if (hi < 0) return;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (groups[mid].x <= r) lo = mid;
+      else hi = mid - 1;
+    }
+    const int4 e = groups[lo];
+    if (r < e.x || r >= e.x + e.y) return;
+    t = lo;
+    slot = r - e.x;
+  } else {
+    t = r / tile_rows;
+    slot = r - t * tile_rows;
+  }
+  const __nv_bfloat16* xr = x + static_cast<int64_t>(r) * ldx;
+  const int nblk = K / 32;
+  const int chunks = K / 128;
+  if (threadIdx.x == 0) a_scale[r] = 1.f;
+  uint8_t* sf = x_sf + static_cast<int64_t>(t) * chunks * SF_CHUNK + (slot & 31) * 16 + ((slot >> 5) & 3) * 4;
+  uint8_t* q = xq + static_cast<int64_t>(r) * K;
+  for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
+    float v[32];
+    load16(xr + b * 32, v);
+    load16(xr + b * 32 + 16, v + 16);
+    float am = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) am = fmaxf(am, fabsf(v[j]));
+    int e = -127;
+    if (am > 0.f) {
+      int ex;
+      const float m = frexpf(am / 448.f, &ex);  // am / 448 = m * 2^ex, m in [0.5, 1)
+      e = (m == 0.5f) ? ex - 1 : ex;             // smallest e with am / 2^e <= 448
+      e = max(-127, min(127, e));
+    }
+    const float inv = ldexpf(1.f, -e);
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_fp8_e4m3 c(v[4 * j + i] * inv);
+        word |= static_cast<uint32_t>(c.__x) << (8 * i);
+      }
+      w[j] = word;
+    }
+    *reinterpret_cast<uint4*>(q + b * 32) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(q + b * 32 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+    sf[(b >> 2) * SF_CHUNK + (b & 3)] = static_cast<uint8_t>(e + 127);
+  }
+}
+
 }  // namespace fp4mma
 }  // namespace shk
 
@@ -570,10 +668,10 @@ int map_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box
   return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool FP8>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const Fp4MmaParams& g, int grid, cudaStream_t st) {
-  using S = Smem<BN, STAGES>;
-  auto k = fp4mma_kernel<BN, STAGES>;
+  using S = Smem<BN, STAGES, FP8>;
+  auto k = fp4mma_kernel<BN, STAGES, FP8>;
   static bool ready[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -602,25 +700,29 @@ extern "C" int sh_nvfp4_quant_act(const void* x, int64_t ldx, int rows, int K, c
   return static_cast<int>(cudaGetLastError());
 }
 
-extern "C" int sh_gemm_fp4mma(Fp4MmaParams* g, const void* xq, int rows_q, int bn, int splits, int num_sms,
-                              cudaStream_t stream) {
-  if (g->K % 64 != 0 || g->K <= 0) return -2;
+namespace {
+template <bool FP8>
+int run_blockscaled(Fp4MmaParams* g, const void* xq, int rows_q, int bn, int splits, int num_sms,
+                    cudaStream_t stream) {
+  constexpr int KBF = Fmt<FP8>::KB;
+  const int row_bytes = FP8 ? g->K : g->K / 2;
+  if (g->K <= 0 || g->K % (FP8 ? 128 : 64) != 0) return -2;
   if (g->rows_total <= 0 || rows_q <= 0) return 0;
   if ((reinterpret_cast<uintptr_t>(g->w) & 15) || (reinterpret_cast<uintptr_t>(xq) & 15) ||
       (reinterpret_cast<uintptr_t>(g->w_sf) & 15) || (reinterpret_cast<uintptr_t>(g->x_sf) & 15) ||
-      (g->K / 2) % 16 != 0)
+      row_bytes % 16 != 0)
     return -3;
   if (bn != 64 && bn != 128) return -4;
   CUtensorMap a, b;
-  int r = map_u8(&a, g->w, g->rows_total, g->K / 2, BM);
+  int r = map_u8(&a, g->w, g->rows_total, row_bytes, BM);
   if (r) return 1000 + r;
-  r = map_u8(&b, xq, rows_q, g->K / 2, bn);
+  r = map_u8(&b, xq, rows_q, row_bytes, bn);
   if (r) return 2000 + r;
   g->rows_q = rows_q;
   if (!g->groups) g->rows_p = g->rows_total;
   g->tiles_p = (g->rows_p + BM - 1) / BM;
   g->tiles_q = (rows_q + bn - 1) / bn;
-  const int nkb = (g->K + KB - 1) / KB;
+  const int nkb = (g->K + KBF - 1) / KBF;
   splits = (g->groups || splits < 1) ? 1 : (splits > nkb ? nkb : splits);
   g->kb_per_split = (nkb + splits - 1) / splits;
   splits = (nkb + g->kb_per_split - 1) / g->kb_per_split;
@@ -629,7 +731,31 @@ extern "C" int sh_gemm_fp4mma(Fp4MmaParams* g, const void* xq, int rows_q, int b
   g->out_vec = (g->ldo % 8 == 0) && (reinterpret_cast<uintptr_t>(g->out) % 16 == 0);
   const int work = g->groups ? g->max_groups * g->tiles_p : g->tiles_p * g->tiles_q * splits;
   const int grid = work < num_sms ? work : num_sms;
-  r = bn == 128 ? launch<128, 5>(a, b, *g, grid, stream) : launch<64, 7>(a, b, *g, grid, stream);
+  r = bn == 128 ? launch<128, 5, FP8>(a, b, *g, grid, stream) : launch<64, 7, FP8>(a, b, *g, grid, stream);
   if (r) return 3000 + r;
   return 0;
+}
+}  // namespace
+
+extern "C" int sh_gemm_fp4mma(Fp4MmaParams* g, const void* xq, int rows_q, int bn, int splits, int num_sms,
+                              cudaStream_t stream) {
+  return run_blockscaled<false>(g, xq, rows_q, bn, splits, num_sms, stream);
+}
+
+extern "C" int sh_gemm_mxfp8(Fp4MmaParams* g, const void* xq, int rows_q, int bn, int splits, int num_sms,
+                             cudaStream_t stream) {
+  return run_blockscaled<true>(g, xq, rows_q, bn, splits, num_sms, stream);
+}
+
+extern "C" int sh_mxfp8_quant_act(const void* x, int64_t ldx, int rows, int K, const int4* groups,
+                                  const int* num_groups, int tile_rows, uint8_t* xq, uint8_t* x_sf, float* a_scale,
+                                  cudaStream_t stream) {
+  if (K % 128 != 0 || K <= 0 || tile_rows <= 0 || tile_rows > 128) return -2;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(xq) & 15)) return -3;
+  if (rows <= 0) return 0;
+  const int nb = K / 32;
+  const int threads = nb >= QUANT_THREADS ? QUANT_THREADS : (nb + 31) / 32 * 32;
+  shk::launch(quant_act_mx8_kernel, dim3(rows), dim3(threads), 0, stream, static_cast<const __nv_bfloat16*>(x), ldx,
+              rows, K, groups, num_groups, tile_rows, xq, x_sf, a_scale);
+  return static_cast<int>(cudaGetLastError());
 }

@@ -51,6 +51,14 @@ int sh_nvfp4_quant_act(const void* x, int64_t ldx, int rows, int K, const int4* 
 // splits > 1 (dense mode) needs ws (splits * tiles_p * tiles_q * 128 * bn floats) and zeroed counters.
 int sh_gemm_fp4mma(Fp4MmaParams* g, const void* xq, int rows_q, int bn, int splits, int num_sms,
                    cudaStream_t stream);
+// MXFP8 (W8A8) on the same kernel: w [rows_total, K] e4m3, w_sf / x_sf tiles of ue8m0 scales per 32 values
+// (chunk c covers k 128c .. 128c+127; byte (r % 32) * 16 + (r / 32) * 4 + (k / 32) % 4), K % 128 == 0.
+int sh_gemm_mxfp8(Fp4MmaParams* g, const void* xq, int rows_q, int bn, int splits, int num_sms,
+                  cudaStream_t stream);
+// bf16 activations -> e4m3 codes xq [rows, K] with ue8m0 scales per 32 values (scale tiles as above);
+// a_scale[r] = 1.  Grouped rows map to their entry's tile like sh_nvfp4_quant_act.
+int sh_mxfp8_quant_act(const void* x, int64_t ldx, int rows, int K, const int4* groups, const int* num_groups,
+                       int tile_rows, uint8_t* xq, uint8_t* x_sf, float* a_scale, cudaStream_t stream);
 #ifdef __cplusplus
 }
 #endif

@@ -102,8 +102,8 @@ def test_deepseek_engines_on_gpu(name):
         assert all(len(g) == 12 for g in got)
 
 
-@pytest.mark.parametrize("act", ["fp4", "bf16"])
-def test_deepseek_nvfp4_spec_is_exact_in_batch_invariant_mode(monkeypatch, act):
+@pytest.mark.parametrize("fmt,act", [("nvfp4", "fp4"), ("nvfp4", "bf16"), ("fp8_block", "fp4")])
+def test_deepseek_nvfp4_spec_is_exact_in_batch_invariant_mode(monkeypatch, fmt, act):
     """NVFP4 DeepSeek on the block-scaled W4A4 path (act=fp4: per-token NVFP4 activations) and on the
     W4A16 path: in batch-invariant mode a k+1-token verify window reproduces one-token decoding exactly,
     eager and CUDA-graph."""
@@ -114,6 +114,7 @@ def test_deepseek_nvfp4_spec_is_exact_in_batch_invariant_mode(monkeypatch, act):
     monkeypatch.setenv("SH_BATCH_INVARIANT", "1")
     monkeypatch.setenv("SH_NVFP4_ACT", act)
     m = shrink(deepseek_v32_config(), layers=3, hidden=256, vocab=1024)
+    m.weight_format = fmt  # fp8_block: MXFP8 W8A8 linears (and experts where the widths allow)
     rng = np.random.default_rng(6)
     prompts = [rng.integers(0, 1024, int(n)) for n in (90, 40, 130)]
     outs = {}

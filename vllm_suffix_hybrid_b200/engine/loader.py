@@ -156,7 +156,7 @@ def config_from_hf(path_or_dict, dtype: str = "bfloat16"):
                            kv_lora=hf["kv_lora_rank"], qk_nope=hf["qk_nope_head_dim"], qk_rope=hf["qk_rope_head_dim"],
                            v_head=hf["v_head_dim"], dsa_heads=hf.get("index_n_heads", 0) if v32 else 0,
                            dsa_head_dim=hf.get("index_head_dim", 128), dsa_topk=hf.get("index_topk", 0) if v32 else 0,
-                           weight_format=fmt if fmt != "fp8_block" else "bf16", draft="mtp", **common)
+                           weight_format=fmt, draft="mtp", **common)
     raise ValueError(f"unsupported checkpoint architecture {arch or mt!r}")
 
 
@@ -196,6 +196,9 @@ def _moe(ck: Checkpoint, pre: str, moe, shared_name: str) -> None:
         if getattr(moe, "fp4", None) is not None:
             _fp4_expert(ck, moe, j, base)
             continue
+        if getattr(moe, "fp8", None) is not None:
+            _fp8_expert(ck, moe, j, base)
+            continue
         g = ck.matrix(base + "gate_proj")
         u = ck.matrix(base + "up_proj")
         d = ck.matrix(base + "down_proj")
@@ -203,12 +206,30 @@ def _moe(ck: Checkpoint, pre: str, moe, shared_name: str) -> None:
         _copy(moe.w2[j * H:(j + 1) * H], d, f"{pre}experts.{e}.down")
     if getattr(moe, "fp4", None) is not None:
         moe.refresh()
+    if getattr(moe, "fp8", None) is not None:  # scale tiles of the re-quantised experts
+        from .. import ops
+
+        moe.fp8 = tuple((c, sc, ops.mxfp8_scale_tiles(sc, r)) for (c, sc, _), r in zip(moe.fp8, (2 * moe.F, moe.H)))
     if moe.shared is not None:
         sp = pre + shared_name + "."
         moe.shared.gate_up.load(torch.cat([ck.matrix(sp + "gate_proj"), ck.matrix(sp + "up_proj")], 0))
         moe.shared.down.load(ck.matrix(sp + "down_proj"))
     if moe.shared_gate is not None:
         _copy(moe.shared_gate, ck.get(pre + "shared_expert_gate.weight").float(), pre + "shared_expert_gate")
+
+
+def _fp8_expert(ck: Checkpoint, moe, j: int, base: str) -> None:
+    """Fill MXFP8 expert j from the checkpoint's (dequantised) matrices: per-32 e4m3 + ue8m0.  Power-of-two
+    block scales (ue8m0 checkpoints) re-quantise exactly; other block scales round once more."""
+    from .. import ops
+
+    F, H = moe.F, moe.H
+    (c13, s13, _), (c2, s2, _) = moe.fp8
+    w = torch.cat([ck.matrix(base + "gate_proj"), ck.matrix(base + "up_proj")]).to(c13.device)
+    c, sc = ops.mxfp8_quantize(w)
+    c13[j * 2 * F:(j + 1) * 2 * F], s13[j * 2 * F:(j + 1) * 2 * F] = c, sc
+    c, sc = ops.mxfp8_quantize(ck.matrix(base + "down_proj").to(c2.device))
+    c2[j * H:(j + 1) * H], s2[j * H:(j + 1) * H] = c, sc
 
 
 def _fp4_expert(ck: Checkpoint, moe, j: int, base: str) -> None:

@@ -42,9 +42,13 @@ class QLinear:
 
     def __init__(self, in_f: int, out_f: int, dtype, device, gen, fmt: str = "bf16", std: float = 0.02):
         w = init_weight((out_f, in_f), std, dtype, device, gen)
-        self.fmt = fmt if in_f % 16 == 0 else "bf16"
+        self.fmt = fmt if in_f % (128 if fmt == "fp8" else 16) == 0 else "bf16"
         self.out_f, self.in_f, self.dtype = out_f, in_f, dtype
-        if self.fmt == "nvfp4":
+        if self.fmt == "fp8":  # MXFP8: e4m3 codes + ue8m0 scale per 32 (W8A8 block-scaled tcgen05 GEMM)
+            self.codes, self.mx_scales = ops.mxfp8_quantize(w)
+            self.w_sf = ops.mxfp8_scale_tiles(self.mx_scales) if self.codes.is_cuda else None
+            self._w = None
+        elif self.fmt == "nvfp4":
             self.packed, self.scales, self.gscale = ops.nvfp4_quantize(w)
             self.scales_k = ops.nvfp4_kmajor_scales(self.scales) if self.packed.is_cuda else None
             self.w_sf = ops.nvfp4_scale_tiles(self.scales) if self.packed.is_cuda else None
@@ -60,6 +64,8 @@ class QLinear:
 
     @property
     def weight(self) -> torch.Tensor:
+        if self.fmt == "fp8":
+            return ops.ref.mxfp8_dequantize(self.codes, self.mx_scales).to(self.dtype)
         if self.fmt != "nvfp4":
             return self._w
         if not self.packed.is_cuda:
@@ -68,6 +74,8 @@ class QLinear:
         return ops.nvfp4_dequantize(self.packed, self.scales, self.gscale, out=out)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fmt == "fp8" and x.dtype == torch.bfloat16:
+            return ops.mxfp8_linear(x, self.codes, self.w_sf, self.mx_scales)
         if self.fmt == "nvfp4" and self.in_f % 64 == 0 and x.dtype == torch.bfloat16 and ops.nvfp4_act_mode() == "fp4":
             return ops.nvfp4_linear_w4a4(x, self.packed, self.w_sf, self.scales, self.gscale, self.static_g)
         if self.fmt == "nvfp4" and x.is_cuda and x.dtype == torch.bfloat16 and self.in_f % 64 == 0:
@@ -80,12 +88,19 @@ class QLinear:
         if self.fmt == "nvfp4" and self.packed.is_cuda:
             self.scales_k = ops.nvfp4_kmajor_scales(self.scales)
             self.w_sf = ops.nvfp4_scale_tiles(self.scales)
+        if self.fmt == "fp8" and self.codes.is_cuda:
+            self.w_sf = ops.mxfp8_scale_tiles(self.mx_scales)
 
     def load(self, full: torch.Tensor) -> None:
         """Replace the weight by a full [out, in] matrix (re-quantised when the layer is NVFP4)."""
         if tuple(full.shape) != (self.out_f, self.in_f):
             raise ValueError(f"checkpoint matrix {tuple(full.shape)} != expected {(self.out_f, self.in_f)}")
-        if self.fmt == "nvfp4":
+        if self.fmt == "fp8":
+            c, sc = ops.mxfp8_quantize(full.to(self.codes.device, torch.float32))
+            self.codes.copy_(c)
+            self.mx_scales.copy_(sc)
+            self.refresh()
+        elif self.fmt == "nvfp4":
             p, sc, g = ops.nvfp4_quantize(full.to(self.packed.device, self.dtype))
             self.packed.copy_(p)
             self.scales.copy_(sc)
@@ -180,7 +195,7 @@ class DeepseekModel:
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)
         self.gen = gen
-        fmt = "nvfp4" if cfg.weight_format == "nvfp4" else "bf16"
+        fmt = {"nvfp4": "nvfp4", "fp8_block": "fp8"}.get(cfg.weight_format, "bf16")
         self.cos_sin = ops.ref.rope_cos_sin(cfg.max_position, cfg.qk_rope, cfg.rope_theta, device=device,
                                               scaling=cfg.rope_scaling)
         self.embed = init_weight((cfg.vocab, cfg.hidden), cfg.init_std, self.dtype, device, gen)
@@ -241,7 +256,7 @@ class DeepseekMtp:
         self.enorm = RMSNorm(cfg.hidden, cfg.norm_eps, dt, device)
         self.hnorm = RMSNorm(cfg.hidden, cfg.norm_eps, dt, device)
         self.eh_proj = init_weight((cfg.hidden, 2 * cfg.hidden), cfg.init_std, dt, device, gen)
-        fmt = "nvfp4" if cfg.weight_format == "nvfp4" else "bf16"
+        fmt = {"nvfp4": "nvfp4", "fp8_block": "fp8"}.get(cfg.weight_format, "bf16")
         self.layer = DeepseekLayer(cfg, cfg.layers, dt, device, gen, target.cos_sin, fmt)
         self.norm = RMSNorm(cfg.hidden, cfg.norm_eps, dt, device)
 

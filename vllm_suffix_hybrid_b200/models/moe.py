@@ -57,6 +57,12 @@ class MoEBlock:
                 and cfg.hidden % 64 == 0 and self.F % 64 == 0:
             self.fp4 = (self._quant(self.w13, self.E_local, 2 * self.F), self._quant(self.w2, self.E_local, cfg.hidden))
             self.w13 = self.w2 = None  # the bf16 copies are dropped
+        # MXFP8 experts (weight_format fp8_block on CUDA): e4m3 codes + ue8m0 scale per 32, W8A8 grouped GEMMs
+        self.fp8 = None
+        if self.fp4 is None and cfg.weight_format == "fp8_block" and torch.device(device).type == "cuda" \
+                and dtype == torch.bfloat16 and cfg.hidden % 128 == 0 and self.F % 128 == 0:
+            self.fp8 = tuple(self._quant8(w, r) for w, r in ((self.w13, 2 * self.F), (self.w2, cfg.hidden)))
+            self.w13 = self.w2 = None
         self.shared = MLP(cfg.hidden, cfg.shared_ffn, dtype, device, gen) if cfg.shared_experts else None
         if self.shared is not None:
             self.shared.down.push = False  # reduced by a plain all-reduce below
@@ -73,6 +79,11 @@ class MoEBlock:
             gs.append(g.reshape(1).float())
         sc = torch.cat(scales)
         return (torch.cat(packed), sc, torch.cat(gs), ops.nvfp4_kmajor_scales(sc), ops.nvfp4_scale_tiles(sc, rows))
+
+    @staticmethod
+    def _quant8(w: torch.Tensor, rows: int):
+        codes, sc = ops.mxfp8_quantize(w)
+        return codes, sc, ops.mxfp8_scale_tiles(sc, rows)
 
     def refresh(self) -> None:
         """Rebuild the kernels' scale copies (k-block-major for W4A16, block-scaled MMA tiles for W4A4)
@@ -98,6 +109,8 @@ class MoEBlock:
             out = ep.dp_dispatch_combine(self, x, ids, w) if st_dp() > 1 else ep.dispatch_combine(self, x, ids, w)
         elif self.fp4 is not None:
             out = ops.moe_experts_nvfp4(x, ids, w, self.fp4[0], self.fp4[1], self.E, self.F)
+        elif self.fp8 is not None:
+            out = ops.moe_experts_mxfp8(x, ids, w, self.fp8[0], self.fp8[1], self.E, self.F)
         else:
             out = ops.moe_experts(x, ids, w, self.w13, self.w2, self.E, self.F)
         if self.shared is not None:

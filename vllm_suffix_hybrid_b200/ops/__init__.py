@@ -697,6 +697,134 @@ def _moe_w4a4_cpu(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
     return y
 
 
+# ----------------------------------------------------------------------------- MXFP8 (W8A8)
+def _tile_layout(s8: torch.Tensor, rows_per_matrix: int, kc: int) -> torch.Tensor:
+    """Per-row scale bytes [R, nblk] -> tensor-core scale tiles [matrices * tiles, kc, 512] (zero padded)."""
+    R, nblk = s8.shape
+    nm = R // rows_per_matrix
+    tp = -(-rows_per_matrix // 128)
+    buf = torch.zeros(nm, tp * 128, kc * 4, dtype=torch.uint8, device=s8.device)
+    buf[:, :rows_per_matrix, :nblk] = s8.reshape(nm, rows_per_matrix, nblk)
+    return buf.view(nm * tp, 4, 32, kc, 4).permute(0, 3, 2, 1, 4).contiguous().view(nm * tp, kc, 512)
+
+
+def mxfp8_scale_tiles(scales: torch.Tensor, rows_per_matrix: int | None = None) -> torch.Tensor:
+    """ue8m0 scales [R, K/32] -> scale tiles [R/rows_per_matrix * tiles, K/128, 512] of the MXFP8 GEMM."""
+    R, nblk = scales.shape
+    return _tile_layout(scales.view(torch.uint8), rows_per_matrix or R, -(-nblk // 4))
+
+
+def mxfp8_quantize(w: torch.Tensor):
+    """(e4m3 codes uint8 [R, K], ue8m0 scales [R, K/32]) of a matrix (load time; see reference)."""
+    return ref.mxfp8_quantize(w)
+
+
+def mxfp8_quant_act(x: torch.Tensor, tile_rows: int, groups=None, num_groups=None):
+    R, K = x.shape
+    tiles = groups.shape[0] if groups is not None else -(-R // tile_rows)
+    dev = x.device
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = ("mx8", idx)
+    b = _FP4_ACT.get(key)
+    if b is None or b[0].numel() < R * K or b[1].numel() < tiles * (K // 128) * 512 or b[2].numel() < R:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("MXFP8 activation scratch must be sized before CUDA-graph capture (run once eagerly)")
+        old = (0, 0, 0) if b is None else (b[0].numel(), b[1].numel(), b[2].numel())
+        b = (torch.empty(max(R * K, old[0], 1 << 20), dtype=torch.uint8, device=dev),
+             torch.empty(max(tiles * (K // 128) * 512, old[1], 1 << 18), dtype=torch.uint8, device=dev),
+             torch.empty(max(R, old[2], 4096), dtype=torch.float32, device=dev))
+        _FP4_ACT[key] = b
+    xq, x_sf, a_sc = (b[0][: R * K].view(R, K), b[1][: tiles * (K // 128) * 512].view(tiles, K // 128, 512),
+                      b[2][:R])
+    native().mxfp8_quant_act(x, xq, x_sf, a_sc, tile_rows, groups, num_groups)
+    return xq, x_sf, a_sc
+
+
+_ONES: dict = {}
+
+
+def _ones(dev, n: int) -> torch.Tensor:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    t = _ONES.get(idx)
+    if t is None or t.numel() < n:
+        t = torch.ones(max(n, 4096), dtype=torch.float32, device=dev)
+        _ONES[idx] = t
+    return t[:n]
+
+
+def mxfp8_linear(x: torch.Tensor, codes: torch.Tensor, w_sf: torch.Tensor, scales: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x W^T with MXFP8 W (e4m3 + ue8m0 per 32) and per-32 MXFP8 x: block-scaled tcgen05 MMA
+    (kind::mxf8f6f4) on CUDA, the fp32 oracle of the same quantisation on CPU."""
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    N = codes.shape[0]
+    if not x.is_cuda:
+        return ref.mxfp8_linear(x2, codes, scales).to(x.dtype).view(*lead, N)
+    if x2.stride(-1) != 1 or (x2.stride(0) * 2) % 16 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    y = out.view(M, N) if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    if M:
+        bn = 64 if M <= 64 else 128
+        xq, x_sf, a_sc = mxfp8_quant_act(x2, bn)
+        native().gemm_fp4mma(y, xq, x_sf, a_sc, codes, w_sf, _ones(x.device, 1), bn, fp8=True)
+    return y.view(*lead, N)
+
+
+def moe_experts_mxfp8(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
+    """MoE experts with MXFP8 weights: w13q = (codes [E*2F, H], scales [E*2F, H/32], scale tiles), w2q likewise
+    for [E*H, F]; grouped block-scaled W8A8 GEMMs (CPU: fp32 oracle per pair)."""
+    T, H = x.shape
+    if not x.is_cuda:
+        y = torch.zeros(T, H, dtype=torch.float32)
+        for t in range(T):
+            for j in range(ids.shape[1]):
+                e = int(ids[t, j])
+                if e < 0 or e >= E:
+                    continue
+                r13, r2 = slice(e * 2 * F, (e + 1) * 2 * F), slice(e * H, (e + 1) * H)
+                gu = ref.mxfp8_linear(x[t:t + 1], w13q[0][r13], w13q[1][r13]).to(x.dtype)
+                a = (torch.nn.functional.silu(gu[:, :F].float()) * gu[:, F:].float()).to(x.dtype)
+                y[t] += float(weights[t, j]) * ref.mxfp8_linear(a, w2q[0][r2], w2q[1][r2])[0].to(x.dtype).float()
+        y = y.to(x.dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    k = ids.shape[1]
+    dev = x.device
+    pairs = T * k
+    bn = 64 if pairs <= E * 64 else 128
+    max_groups = E + pairs // bn + 1
+    C = native()
+    rank = torch.empty(pairs, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    sorted_pos = torch.empty(pairs, dtype=torch.int32, device=dev)
+    sorted_token = torch.zeros(pairs, dtype=torch.int32, device=dev)
+    groups = torch.empty(max_groups, 4, dtype=torch.int32, device=dev)
+    ngroups = torch.empty(1, dtype=torch.int32, device=dev)
+    C.moe_align(ids, rank, offsets, sorted_pos, sorted_token, groups, ngroups, E, bn, 2 * F)
+    xs = torch.empty(pairs, H, dtype=x.dtype, device=dev)
+    C.moe_gather(xs, x, sorted_token, offsets[E:])
+    gu = torch.empty(pairs, 2 * F, dtype=x.dtype, device=dev)
+    groups2 = groups.clone()
+    groups2[:, 2] = groups[:, 3] * H
+    ys = torch.empty(pairs, H, dtype=x.dtype, device=dev)
+    t13 = w13q[2] if len(w13q) > 2 else mxfp8_scale_tiles(w13q[1], 2 * F)
+    t2 = w2q[2] if len(w2q) > 2 else mxfp8_scale_tiles(w2q[1], H)
+    ones = _ones(dev, E)
+    xq, x_sf, a_sc = mxfp8_quant_act(xs, bn, groups, ngroups)
+    C.gemm_fp4mma(gu, xq, x_sf, a_sc, w13q[0], t13, ones, bn, groups, ngroups, 2 * F, fp8=True)
+    a = silu_mul(gu)
+    xq, x_sf, a_sc = mxfp8_quant_act(a, bn, groups, ngroups)
+    C.gemm_fp4mma(ys, xq, x_sf, a_sc, w2q[0], t2, ones, bn, groups2, ngroups, H, fp8=True)
+    if out is None:
+        out = torch.empty(T, H, dtype=x.dtype, device=dev)
+    C.moe_combine(out, ys, sorted_pos, weights, False)
+    return out
+
+
 def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
     """moe_experts with NVFP4 expert weights: w13q = (packed [E*2F, H/2], scales [E*2F, H/16], global [E],
     optional k-block-major scales, optional block-scaled MMA scale tiles), w2q likewise for [E*H, F].

@@ -342,6 +342,32 @@ def mla_fp4_qdq(c: torch.Tensor) -> torch.Tensor:
     return val.reshape(shape)
 
 
+# ----------------------------------------------------------------------------- MXFP8 (W8A8, block 32)
+def mxfp8_quantize(x: torch.Tensor):
+    """e4m3 codes (uint8 bits) [R, K] and ue8m0 scales [R, K/32]: s = 2^e with the smallest e keeping
+    amax32 / s <= 448, code = e4m3(x / s) (exact power-of-two scaling, round to nearest even)."""
+    R, K = x.shape
+    xf = x.float().view(R, K // 32, 32)
+    am = xf.abs().amax(-1)
+    m, ex = torch.frexp(am / 448.0)
+    e = torch.where(m == 0.5, ex - 1, ex)
+    e = torch.where(am > 0, e, torch.full_like(e, -127)).clamp(-127, 127)
+    codes = (xf * torch.pow(2.0, -e.float())[..., None]).to(torch.float8_e4m3fn)
+    return codes.view(torch.uint8).view(R, K).contiguous(), (e + 127).to(torch.uint8).contiguous()
+
+
+def mxfp8_dequantize(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    R, K = codes.shape
+    v = codes.view(torch.float8_e4m3fn).float().view(R, K // 32, 32)
+    return (v * torch.pow(2.0, scales.float() - 127.0)[..., None]).view(R, K)
+
+
+def mxfp8_linear(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """fp32 oracle of the MXFP8 W8A8 GEMM: quantise x like the kernel, sum dequantised products."""
+    xc, xs = mxfp8_quantize(x)
+    return mxfp8_dequantize(xc, xs) @ mxfp8_dequantize(codes, scales).t()
+
+
 # ----------------------------------------------------------------------------- MLA / DSA
 def mla_attention(q_lat, q_pe, latent, block_tables, seq_lens, q_start, scale, kv_lora, topk=None):
     """Absorbed MLA over a latent cache [blocks, bs, kv_lora + rope].

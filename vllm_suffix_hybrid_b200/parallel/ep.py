@@ -36,6 +36,8 @@ def dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -
     out = comm.partial_out(T, H, x, force=True)
     if moe.fp4 is not None:
         out = ops.moe_experts_nvfp4(x, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F, out=out)
+    elif getattr(moe, "fp8", None) is not None:
+        out = ops.moe_experts_mxfp8(x, ids_l, w_l, moe.fp8[0], moe.fp8[1], moe.E_local, moe.F, out=out)
     else:
         out = ops.moe_experts(x, ids_l, w_l, moe.w13, moe.w2, moe.E_local, moe.F, out=out)
     return comm.all_reduce(out, force=True)
@@ -80,6 +82,8 @@ def dp_dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor
     ids_l, w_l = local_routes(ids_a, w_a, st.ep_rank * moe.E_local, moe.E_local)
     if moe.fp4 is not None:
         part = ops.moe_experts_nvfp4(xs, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F)
+    elif getattr(moe, "fp8", None) is not None:
+        part = ops.moe_experts_mxfp8(xs, ids_l, w_l, moe.fp8[0], moe.fp8[1], moe.E_local, moe.F)
     else:
         part = ops.moe_experts(xs, ids_l, w_l, moe.w13, moe.w2, moe.E_local, moe.F)
     return _reduce_scatter(part)
