@@ -129,6 +129,9 @@ def nvfp4_main(a):
                                      flush, a.iters), 2)
                    for sp in (2, 4, 8)}
         wd = ops.nvfp4_dequantize(p, s, g)
+        c8, s8 = ops.mxfp8_quantize(w)
+        t8sf = ops.mxfp8_scale_tiles(s8)
+        t8 = time_fn(lambda: ops.mxfp8_linear(x, c8, t8sf, s8, out=y), flush, a.iters)
         t16 = time_fn(lambda: tcgen05_linear(x, wd, y), flush, a.iters)
         tlib = time_fn(lambda: torch.matmul(x, wd.t(), out=y), flush, a.iters)
         ref = x.float() @ wd.float().t()
@@ -136,7 +139,7 @@ def nvfp4_main(a):
         ref44 = ops.reference.nvfp4_w4a4_linear(x.cpu(), p.cpu(), s.cpu(), g.cpu()) if M * N * K <= (1 << 31) else None
         err44 = None if ref44 is None else (ops.nvfp4_linear_w4a4(x, p, w_sf, s, g).float().cpu() - ref44).abs().max().item()
         packed = N * K // 2 + N * K // 16
-        print(json.dumps({"shape": name, "M": M, "N": N, "K": K, "w4a16_us": round(t4, 2), "w4a4_us": round(t44, 2), "w4a4_quant_us": round(tq, 2),
+        print(json.dumps({"shape": name, "M": M, "N": N, "K": K, "w4a16_us": round(t4, 2), "w4a4_us": round(t44, 2), "w4a4_quant_us": round(tq, 2), "mxfp8_w8a8_us": round(t8, 2),
                           "w4a4_gemm_nosplit_us": round(t_g1, 2), "w4a4_gemm_split_us": t_split,
                           "bf16_tcgen05_us": round(t16, 2), "cublas_bf16_us": round(tlib, 2),
                           "w4a4_packed_weight_gbs": round(packed / t44 / 1e3, 1),
