@@ -41,6 +41,7 @@ struct GdnParams {
   int H, HV, K, V, W;
   int mode;
   float eps;
+  int async_ok;  // set by sh_gdn_recurrent: token rows may be staged with cp.async
 };
 
 #ifdef __cplusplus

@@ -40,10 +40,10 @@ def _cache(dev, slots, W, C, HV, K):
                 rb=torch.zeros(slots, W, HV, **f))
 
 
-@pytest.mark.parametrize("K", [64, 128])
-def test_gdn_prefill_then_windows_match_reference(K):
-    H, HV, W = 2, 4, 4
-    lens = [11, 5]
+@pytest.mark.parametrize("K,W,lens", [(64, 4, [11, 5]), (128, 4, [11, 5]), (128, 9, [37, 17]), (32, 6, [3, 9])])
+def test_gdn_prefill_then_windows_match_reference(K, W, lens):
+    """Prefill over several token chunks, then verify windows whose replayed records span chunks."""
+    H, HV = 2, 4
     caches = {d: _cache(d, 3, W, 2 * H * K + HV * K, HV, K) for d in ("cpu", "cuda")}
     pend = {d: torch.zeros(3, dtype=torch.int32, device=d) for d in ("cpu", "cuda")}
     slots = {d: torch.tensor([2, 1], device=d) for d in ("cpu", "cuda")}
@@ -54,7 +54,7 @@ def test_gdn_prefill_then_windows_match_reference(K):
             for d in ("cpu", "cuda")}
     assert (outs["cuda"][1].float().cpu() - outs["cpu"][1].float()).abs().max() < 0.05
     # three verify windows with varying accepted counts
-    for step, acc in enumerate([[2, 0], [3, 1], [0, 3]]):
+    for step, acc in enumerate([[min(2, W - 1), 0], [W - 1, 1], [0, W - 1]]):
         x, ba, *_ = _gdn_inputs(2 * W, H, HV, K, 10 + step)
         qs = {d: torch.tensor([0, W, 2 * W], device=d) for d in ("cpu", "cuda")}
         outs = {d: _run(d, x, ba, w, a_log, dt, nw, C, H, HV, K, slots[d], qs[d], W, 1, caches[d], pend[d])
