@@ -551,6 +551,35 @@ void gdn_recurrent(torch::Tensor qkv, torch::Tensor z, torch::Tensor ba, torch::
               "sh_gdn_recurrent");
 }
 
+void gdn_chunk_prefill(torch::Tensor qkv, torch::Tensor z, torch::Tensor ba, torch::Tensor a_log, torch::Tensor dt_bias,
+                       torch::Tensor norm_w, torch::Tensor state, torch::Tensor slots, torch::Tensor q_start,
+                       torch::Tensor out, int64_t H, int64_t HV, int64_t K, double eps, c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(state.scalar_type() == at::kFloat && qkv.scalar_type() == at::kBFloat16, "gdn_chunk_prefill dtypes");
+  GdnParams p{};
+  p.qkv = ptr<const __nv_bfloat16>(qkv);
+  p.qkv_stride = qkv.stride(0);
+  p.z = ptr<const __nv_bfloat16>(z);
+  p.z_stride = z.stride(0);
+  p.ba = ptr<const __nv_bfloat16>(ba);
+  p.ba_stride = ba.stride(0);
+  p.a_log = ptr<const float>(a_log);
+  p.dt_bias = ptr<const float>(dt_bias);
+  p.norm_w = ptr<const __nv_bfloat16>(norm_w);
+  p.state = ptr<float>(state);
+  p.slots = ptr<const int64_t>(slots);
+  p.q_start = ptr<const int64_t>(q_start);
+  p.out = ptr<__nv_bfloat16>(out);
+  p.out_stride = out.stride(0);
+  p.H = static_cast<int>(H);
+  p.HV = static_cast<int>(HV);
+  p.K = static_cast<int>(K);
+  p.V = static_cast<int>(K);
+  p.eps = static_cast<float>(eps);
+  p.err = err.has_value() ? ptr<int32_t>(*err) : nullptr;
+  SH_CHECK_RC(sh_gdn_chunk_prefill(&p, static_cast<int>(slots.numel()), at::cuda::getCurrentCUDAStream()),
+              "sh_gdn_chunk_prefill");
+}
+
 // --- MoE -------------------------------------------------------------------------
 void moe_route(torch::Tensor logits, c10::optional<torch::Tensor> bias, torch::Tensor ids, torch::Tensor weights,
                int64_t k, bool sigmoid_grouped, int64_t n_groups, int64_t topk_groups, bool renorm, double scale) {
@@ -686,6 +715,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_fp4_row_bytes", [](int64_t cl, int64_t r) { return sh_mla_fp4_row_bytes(cl, r); });
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
+  m.def("gdn_chunk_prefill", &gdn_chunk_prefill, "Chunked (64-token, tensor-core) GDN prefill from zero state");
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);

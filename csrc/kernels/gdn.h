@@ -42,6 +42,7 @@ struct GdnParams {
   int mode;
   float eps;
   int async_ok;  // set by sh_gdn_recurrent: token rows may be staged with cp.async
+  int32_t* err;  // chunked prefill: set to 1 when a tensor-core wait gave up (may be null)
 };
 
 #ifdef __cplusplus
@@ -49,6 +50,9 @@ extern "C" {
 #endif
 int sh_gdn_conv(const GdnConvParams* p, int batch, cudaStream_t stream);
 int sh_gdn_recurrent(const GdnParams* p, int batch, cudaStream_t stream);
+// Prefill from zero state in chunks of 64 tokens on the tensor cores (K == V == 128); commits the final
+// state like sh_gdn_recurrent mode 0.  -3: a row of qkv / z / out is not 16-byte aligned.
+int sh_gdn_chunk_prefill(const GdnParams* p, int batch, cudaStream_t stream);
 #ifdef __cplusplus
 }
 #endif

@@ -66,6 +66,40 @@ def test_gdn_prefill_then_windows_match_reference(K, W, lens):
     assert (caches["cuda"]["S"].cpu() - caches["cpu"]["S"]).abs().max() < 1e-2
 
 
+@pytest.mark.parametrize("lens", [[150, 64, 7], [1, 200, 0, 65]])
+def test_gdn_chunk_prefill_matches_recurrence(lens):
+    """Chunked tensor-core prefill (64-token WY form, bf16 products) vs the fp32 recurrence on the CPU."""
+    H, HV, K, W = 2, 4, 128, 4
+    C = 2 * H * K + HV * K
+    nreq = len(lens)
+    x, ba, w, a_log, dt, nw, _ = _gdn_inputs(sum(lens), H, HV, K, 3)
+    g = torch.Generator().manual_seed(5)
+    qkv = (torch.randn(sum(lens), C, generator=g) * 0.7).to(torch.bfloat16)
+    z = x[:, C:]
+    qs = torch.tensor([0] + list(np.cumsum(lens)))
+    slots = torch.arange(1, nreq + 1)
+    st_c = torch.full((nreq + 1, HV, K, K), 7.0)
+    out_c = torch.zeros(sum(lens), HV * K, dtype=torch.bfloat16)
+    ops.gdn_chunk_prefill(qkv, z, ba, a_log, dt, nw, st_c, slots, qs, out_c, H, HV, K, 1e-6)
+    dev = "cuda"
+    st_g = torch.full((nreq + 1, HV, K, K), 7.0, device=dev)
+    out_g = torch.zeros(sum(lens), HV * K, dtype=torch.bfloat16, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    zg = x.to(dev)[:, C:]
+    assert ops.gdn_chunk_ok(qkv.to(dev), zg, out_g, K)
+    ops.gdn_chunk_prefill(qkv.to(dev), zg, ba.to(dev), a_log.to(dev), dt.to(dev), nw.to(dev), st_g, slots.to(dev),
+                          qs.to(dev), out_g, H, HV, K, 1e-6, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    o_ref, o_got = out_c.float(), out_g.float().cpu()
+    scale = o_ref.abs().max().item()
+    assert (o_got - o_ref).abs().max().item() < 0.03 * scale, (o_got - o_ref).abs().max().item() / scale
+    assert (o_got - o_ref).abs().mean().item() < 0.004 * scale
+    s_ref, s_got = st_c, st_g.cpu()
+    assert torch.equal(s_got[0], s_ref[0])  # untouched slot
+    assert (s_got - s_ref).abs().max().item() < 0.03 * s_ref[1:].abs().max().item()
+
+
 @pytest.mark.parametrize("grouped", [False, True])
 def test_moe_route(grouped):
     torch.manual_seed(0)

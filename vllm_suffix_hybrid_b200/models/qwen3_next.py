@@ -15,6 +15,7 @@ commits directly.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import List, Optional, Tuple
 
@@ -27,6 +28,10 @@ from .moe import MoEBlock
 
 
 @dataclass
+
+# Prefill runs through the chunked tensor-core kernel (SH_GDN_CHUNK=0: the recurrent kernel).
+_CHUNKED = os.environ.get("SH_GDN_CHUNK", "1") != "0"
+
 class GdnCache:
     state: torch.Tensor  # [slots, HV, V, K] fp32
     conv: torch.Tensor  # [slots, C, 3] fp32
@@ -68,7 +73,12 @@ class GdnLayer:
         ops.gdn_conv(qkvz, self.conv_w, y, cache.conv, cache.rec_x, meta.pending, meta.state_slots, meta.q_start, W,
                      mode)
         o = torch.empty(T, self.HV * self.K, dtype=x.dtype, device=x.device)
-        ops.gdn_recurrent(y, qkvz[:, self.C:], ba, self.a_log, self.dt_bias, self.norm_w, cache.state,
+        z = qkvz[:, self.C:]
+        if mode == 0 and _CHUNKED and ops.gdn_chunk_ok(y, z, o, self.K):
+            ops.gdn_chunk_prefill(y, z, ba, self.a_log, self.dt_bias, self.norm_w, cache.state, meta.state_slots,
+                                  meta.q_start, o, self.H, self.HV, self.K, self.eps)
+            return self.out(o)
+        ops.gdn_recurrent(y, z, ba, self.a_log, self.dt_bias, self.norm_w, cache.state,
                           (cache.rec_k, cache.rec_v, cache.rec_g, cache.rec_b), meta.pending, meta.state_slots,
                           meta.q_start, o, self.H, self.HV, self.K, W, mode, self.eps)
         return self.out(o)

@@ -320,6 +320,26 @@ def gdn_recurrent(qkv, z, ba, a_log, dt_bias, norm_w, state, rec, pending, slots
             state[s] = S
 
 
+def gdn_chunk_prefill(qkv, z, ba, a_log, dt_bias, norm_w, state, slots, q_start, out, H, HV, K, eps,
+                      err=None) -> None:
+    """Prefill from zero state in 64-token chunks on the tensor cores (K == V == 128, rows 16-byte aligned):
+    the same result as gdn_recurrent mode 0 up to bf16 rounding of the chunk products.  On the CPU it runs
+    the recurrence."""
+    if qkv.is_cuda:
+        native().gdn_chunk_prefill(qkv, z, ba, a_log, dt_bias, norm_w, state, slots, q_start, out, H, HV, K, eps, err)
+        return
+    none = torch.zeros(0)
+    gdn_recurrent(qkv, z, ba, a_log, dt_bias, norm_w, state, (none, none, none, none), None, slots, q_start, out, H,
+                  HV, K, 0, 0, eps)
+
+
+def gdn_chunk_ok(qkv, z, out, K: int) -> bool:
+    """The chunked prefill applies: CUDA tensors, K == 128 and 16-byte aligned rows."""
+    if not qkv.is_cuda or K != 128:
+        return False
+    return all(t.data_ptr() % 16 == 0 and (t.stride(0) * t.element_size()) % 16 == 0 for t in (qkv, z, out))
+
+
 # ----------------------------------------------------------------------------- MoE
 def moe_route(logits, k: int, sigmoid_grouped: bool = False, bias=None, n_groups: int = 1, topk_groups: int = 1,
               renorm: bool = True, scale: float = 1.0):
