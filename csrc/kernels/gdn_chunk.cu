@@ -65,7 +65,9 @@ constexpr int OFF_Z = ((OFF_YF + YF_BYTES + 1023) / 1024) * 1024;  // z rows of 
 constexpr int OFF_GAM = OFF_Z + 64 * 256;
 constexpr int OFF_BV = OFF_GAM + 64 * 4;
 constexpr int OFF_BETA = OFF_BV + 64 * 4;
-constexpr int OFF_BAR = OFF_BETA + 64 * 4;
+constexpr int OFF_NW = OFF_BETA + 64 * 4;   // norm weight, fp32 [128]
+constexpr int OFF_PART = OFF_NW + 128 * 4;  // per-row partial sums of o^2, [2][64]
+constexpr int OFF_BAR = OFF_PART + 2 * 64 * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 64;
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024
 static_assert(OFF_A7 + 128 * 128 <= OFF_Z, "inverse work arrays alias the D^T tiles");
@@ -129,6 +131,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
   float* gam = reinterpret_cast<float*>(sm + OFF_GAM);
   float* bv = reinterpret_cast<float*>(sm + OFF_BV);
   float* betav = reinterpret_cast<float*>(sm + OFF_BETA);
+  float* nw = reinterpret_cast<float*>(sm + OFF_NW);
+  float* part = reinterpret_cast<float*>(sm + OFF_PART);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + OFF_BAR + 16);
@@ -150,6 +154,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (tid < K) nw[tid] = __bfloat162float(p.norm_w[tid]);
   // S0 = 0 for the first chunk.
   for (int i = tid; i < 2 * S_ATOM / 16; i += NT) reinterpret_cast<uint4*>(sm + OFF_S)[i] = make_uint4(0, 0, 0, 0);
   fence_proxy();
@@ -253,7 +258,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
       for (int i = lane; i < n * 16; i += 32) {
         const int t = i >> 4, ch = i & 15;
         const __nv_bfloat16* src = p.z + (t0 + c0 + t) * p.z_stride + hv * K + ch * 8;
-        const uint32_t d = sbase + OFF_Z + t * 256 + ch * 16;
+        const uint32_t d = sbase + OFF_Z + t * 256 + ((ch ^ (t & 7)) << 4);  // swizzled: conflict-free row reads
         asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src));
       }
       asm volatile("cp.async.commit_group;");
@@ -455,34 +460,47 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
       break;
     }
     // ---------------------------------------------------------------- phase 5
-    if (warp < 2) {  // O = b_t Q S0^T + Mq D, gated RMSNorm, bf16 out
-      // Every lane runs the warp-collective TMEM loads; only rows t < n are stored.
+    // O = b_t Q S0^T + Mq D with the gated RMSNorm: rows t = TMEM lanes 0-63 (warps 0, 1, 4, 5; each
+    // warp owns 64 of the 128 columns).  Every lane runs the warp-collective TMEM loads; rows t < n are stored.
+    const int half = warp >> 2;
+    if (quarter < 2) {
       const int t = 32 * quarter + lane;
-      {
-        const float bt = bv[t];
-        float ss = 0.f;
+      const float bt = bv[t];
+      float ss = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 16) {
-          float a[16], d[16];
-          tmem_ld16(tmem + TM_4 + lane_off + c, a);
-          tmem_ld16(tmem + TM_5 + lane_off + c, d);
+      for (int c = 64 * half; c < 64 * half + 64; c += 16) {
+        float a[16], d[16];
+        tmem_ld16(tmem + TM_4 + lane_off + c, a);
+        tmem_ld16(tmem + TM_5 + lane_off + c, d);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float o = bt * a[e] + d[e];
-            ss += o * o;
-          }
+        for (int e = 0; e < 16; ++e) {
+          const float o = bt * a[e] + d[e];
+          ss += o * o;
         }
-        const float inv = rsqrtf(ss / K + p.eps);
-        __nv_bfloat16* dst = p.out + (t0 + c0 + min(t, n - 1)) * p.out_stride + hv * K;
-        const __nv_bfloat16* zr = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_Z + t * 256);
+      }
+      part[half * 64 + t] = ss;
+    }
+    __syncthreads();
+    if (quarter < 2) {
+      const int t = 32 * quarter + lane;
+      const float bt = bv[t];
+      const float inv = rsqrtf((part[t] + part[64 + t]) / K + p.eps);
+      __nv_bfloat16* dst = p.out + (t0 + c0 + min(t, n - 1)) * p.out_stride + hv * K;
+      const uint8_t* zrow = sm + OFF_Z + t * 256;
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 16) {
-          float a[16], d[16], o[16];
-          tmem_ld16(tmem + TM_4 + lane_off + c, a);
-          tmem_ld16(tmem + TM_5 + lane_off + c, d);
+      for (int c = 64 * half; c < 64 * half + 64; c += 16) {
+        float a[16], d[16], o[16];
+        tmem_ld16(tmem + TM_4 + lane_off + c, a);
+        tmem_ld16(tmem + TM_5 + lane_off + c, d);
+        const uint4 z0 = *reinterpret_cast<const uint4*>(zrow + ((((c >> 3)) ^ (t & 7)) << 4));
+        const uint4 z1 = *reinterpret_cast<const uint4*>(zrow + ((((c >> 3) + 1) ^ (t & 7)) << 4));
+        const uint32_t zw[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            o[e] = (bt * a[e] + d[e]) * inv * __bfloat162float(p.norm_w[c + e]) * silu(__bfloat162float(zr[c + e]));
+        for (int e = 0; e < 16; ++e) {
+          const float zv = (e & 1) ? hi(zw[e >> 1]) : lo(zw[e >> 1]);
+          o[e] = (bt * a[e] + d[e]) * inv * nw[c + e] * silu(zv);
+        }
+        if (t < n) {
           uint4 u0, u1;
           u0.x = pack_bf16(o[0], o[1]);
           u0.y = pack_bf16(o[2], o[3]);
@@ -492,22 +510,22 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
           u1.y = pack_bf16(o[10], o[11]);
           u1.z = pack_bf16(o[12], o[13]);
           u1.w = pack_bf16(o[14], o[15]);
-          if (t < n) {
-            reinterpret_cast<uint4*>(dst + c)[0] = u0;
-            reinterpret_cast<uint4*>(dst + c)[1] = u1;
-          }
+          reinterpret_cast<uint4*>(dst + c)[0] = u0;
+          reinterpret_cast<uint4*>(dst + c)[1] = u1;
         }
       }
-    } else if (warp >= 4) {  // state row v: bf16 S0 operand of the next chunk; fp32 to global after the last
+    }
+    {  // state rows v = TMEM lanes (all warps, 64 columns each): bf16 S0 of the next chunk; fp32 to
+       // global after the last chunk
       const int v = 32 * quarter + lane;
       const bool last = ci == nchunks - 1;
       float* srow = p.state + ((slot * p.HV + hv) * K + v) * K;
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 16) {
+      for (int c = 64 * half; c < 64 * half + 64; c += 16) {
         float x[16];
         tmem_ld16(tmem + TM_X + lane_off + c, x);
-        st_chunk(sm + OFF_S + (c >> 6) * S_ATOM, swz(v, c & 63), x);
-        st_chunk(sm + OFF_S + (c >> 6) * S_ATOM, swz(v, (c & 63) + 8), x + 8);
+        st_chunk(sm + OFF_S + half * S_ATOM, swz(v, c & 63), x);
+        st_chunk(sm + OFF_S + half * S_ATOM, swz(v, (c & 63) + 8), x + 8);
         if (last) {
 #pragma unroll
           for (int e = 0; e < 16; e += 4)
