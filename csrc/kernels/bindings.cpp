@@ -4,6 +4,7 @@
 
 #include "gemm_tcgen05.h"
 #include "comm.h"
+#include "ep_a2a.h"
 #include "gdn.h"
 #include "moe.h"
 #include "mla.h"
@@ -551,6 +552,69 @@ void gdn_recurrent(torch::Tensor qkv, torch::Tensor z, torch::Tensor ba, torch::
               "sh_gdn_recurrent");
 }
 
+// --- expert-parallel all-to-all over NVLink peer memory ------------------------
+static EpParams ep_params(torch::Tensor ids, std::vector<int64_t> peer_x, std::vector<int64_t> peer_ids,
+                          std::vector<int64_t> peer_w, std::vector<int64_t> peer_y, std::vector<int64_t> peer_flags,
+                          torch::Tensor counters, torch::Tensor err, int64_t rank, int64_t H, int64_t e_local,
+                          int64_t max_T) {
+  const int world = static_cast<int>(peer_x.size());
+  TORCH_CHECK(world >= 1 && world <= SH_EP_MAX_WORLD && peer_ids.size() == peer_x.size() &&
+                  peer_w.size() == peer_x.size() && peer_y.size() == peer_x.size() &&
+                  peer_flags.size() == peer_x.size(), "ep: peer lists");
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == at::kInt && ids.is_contiguous() && ids.dim() == 2, "ep: ids");
+  TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= SH_EP_MAX_BLOCKS, "ep: counters");
+  TORCH_CHECK(ids.size(0) <= max_T, "ep: T exceeds the receive buffers");
+  EpParams p{};
+  p.ids = ids.data_ptr<int32_t>();
+  for (int i = 0; i < world; ++i) {
+    p.peer_x[i] = reinterpret_cast<__nv_bfloat16*>(peer_x[i]);
+    p.peer_ids[i] = reinterpret_cast<int32_t*>(peer_ids[i]);
+    p.peer_w[i] = reinterpret_cast<float*>(peer_w[i]);
+    p.peer_y[i] = reinterpret_cast<__nv_bfloat16*>(peer_y[i]);
+    p.peer_flags[i] = reinterpret_cast<uint32_t*>(peer_flags[i]);
+  }
+  p.counters = reinterpret_cast<uint32_t*>(counters.data_ptr<int>());
+  p.err = err.data_ptr<int>();
+  p.rank = static_cast<int>(rank);
+  p.world = world;
+  p.T = static_cast<int>(ids.size(0));
+  p.k = static_cast<int>(ids.size(1));
+  p.H = static_cast<int>(H);
+  p.e_local = static_cast<int>(e_local);
+  p.max_T = static_cast<int>(max_T);
+  return p;
+}
+
+void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor w, std::vector<int64_t> peer_x,
+                 std::vector<int64_t> peer_ids, std::vector<int64_t> peer_w, std::vector<int64_t> peer_y,
+                 std::vector<int64_t> peer_flags, torch::Tensor counters, torch::Tensor err, int64_t rank,
+                 int64_t e_local, int64_t max_T, int64_t num_blocks) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.size(0) == ids.size(0),
+              "ep_dispatch: x");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.sizes() == ids.sizes(), "ep_dispatch: w");
+  EpParams p = ep_params(ids, peer_x, peer_ids, peer_w, peer_y, peer_flags, counters, err, rank, x.size(1), e_local,
+                         max_T);
+  p.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  p.w = w.data_ptr<float>();
+  SH_CHECK_RC(sh_ep_dispatch(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream()), "sh_ep_dispatch");
+}
+
+void ep_combine(torch::Tensor y, torch::Tensor ids, torch::Tensor out, std::vector<int64_t> peer_x,
+                std::vector<int64_t> peer_ids, std::vector<int64_t> peer_w, std::vector<int64_t> peer_y,
+                std::vector<int64_t> peer_flags, torch::Tensor counters, torch::Tensor err, int64_t rank,
+                int64_t e_local, int64_t max_T, int64_t num_blocks) {
+  const int64_t world = static_cast<int64_t>(peer_x.size());
+  TORCH_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.is_contiguous() &&
+                  y.size(0) == world * ids.size(0), "ep_combine: y [world*T, H]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(0) == ids.size(0) &&
+                  out.size(1) == y.size(1), "ep_combine: out");
+  EpParams p = ep_params(ids, peer_x, peer_ids, peer_w, peer_y, peer_flags, counters, err, rank, y.size(1), e_local,
+                         max_T);
+  p.y = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr());
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  SH_CHECK_RC(sh_ep_combine(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream()), "sh_ep_combine");
+}
+
 void gdn_chunk_prefill(torch::Tensor qkv, torch::Tensor z, torch::Tensor ba, torch::Tensor a_log, torch::Tensor dt_bias,
                        torch::Tensor norm_w, torch::Tensor state, torch::Tensor slots, torch::Tensor q_start,
                        torch::Tensor out, int64_t H, int64_t HV, int64_t K, double eps, c10::optional<torch::Tensor> err) {
@@ -716,6 +780,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_conv", &gdn_conv);
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("gdn_chunk_prefill", &gdn_chunk_prefill, "Chunked (64-token, tensor-core) GDN prefill from zero state");
+  m.def("ep_dispatch", &ep_dispatch, "Expert-parallel dispatch of token rows over NVLink peer memory");
+  m.def("ep_combine", &ep_combine, "Expert-parallel combine of expert outputs over NVLink peer memory");
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);

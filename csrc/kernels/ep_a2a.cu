@@ -1,0 +1,202 @@
+// Expert-parallel all-to-all over NVLink peer memory: dispatch of token rows
+// to the ranks that hold their experts and combine of the expert outputs back
+// to the token owners, with P2P stores issued from the kernels (replaces an
+// all-gather of every token to every rank + reduce-scatter of the partials:
+// a token row crosses NVLink only to ranks that host one of its top-k experts).
+//
+// dispatch (rank r, block b, tokens i = b, b + nblocks, ...):
+//   for every rank d: route row (local expert id or -1, weight or 0) ->
+//   d.ids / d.w [r*T + i]; for the ranks d hosting one of the token's experts:
+//   x[i] -> d.x[r*T + i]; then a cross-rank barrier between same-index blocks.
+//   When the kernel finishes on d, every rank's rows have landed in d's buffers.
+// experts: the grouped expert GEMMs of this rank over the [world*T, H] rows
+//   (rows routed elsewhere have only -1 ids and are skipped).
+// combine (rank d, block b, tokens i = b, b + nblocks, ...): for every source
+//   rank r whose row r*T + i reached a local expert: y[r*T + i] ->
+//   r.y_ret[d*T + i]; barrier; then out[i] = sum over the token's expert ranks
+//   in rank order of y_ret[d*T + i] (fp32 accumulation, identical order on
+//   every call).  Same-index blocks push and sum the same tokens, so the
+//   block-to-block barrier covers exactly the rows each block reads.
+//
+// Buffers are single: a rank writes a peer's receive rows of call e+1 only
+// after passing a barrier of call e+1 or e that the peer signals after it has
+// finished reading call e's rows (dispatch writes follow the previous call's
+// combine barrier, which each rank signals after its expert GEMMs; combine
+// writes follow this call's dispatch barrier, signalled after the previous
+// combine's sums).  Flags carry the per-block epoch, so no flag reset is
+// needed, and the data pointers are the same every call (CUDA-graph safe).
+// Every wait gives up after a time limit, records an error code and skips the
+// remaining phases (no trap, no hang).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ep_a2a.h"
+#include "pdl.cuh"
+
+namespace shk {
+namespace ep {
+
+constexpr uint64_t kTimeoutNs = 5000000000ull;  // 5 s
+constexpr int kThreads = 512;
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t* flag_slot(uint32_t* base, int phase, int block, int src) {
+  return base + (static_cast<size_t>(phase) * SH_EP_MAX_BLOCKS + block) * SH_EP_MAX_WORLD + src;
+}
+
+// Same-index blocks of all ranks meet; false on timeout (error recorded).
+__device__ bool barrier(const EpParams& p, int phase, uint32_t epoch, volatile int* bail) {
+  __syncthreads();  // every store of this block precedes the release below (cumulativity)
+  if (threadIdx.x < p.world) st_release(flag_slot(p.peer_flags[threadIdx.x], phase, blockIdx.x, p.rank), epoch);
+  if (threadIdx.x < p.world) {
+    const uint32_t* f = flag_slot(p.peer_flags[p.rank], phase, blockIdx.x, threadIdx.x);
+    const uint64_t t0 = now_ns();
+    while (static_cast<int32_t>(ld_acquire(f) - epoch) < 0) {
+      if (*bail || now_ns() - t0 > kTimeoutNs) {
+        *bail = 1;
+        if (p.err) atomicCAS(p.err, 0, 200 + phase);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return *bail == 0;
+}
+
+// Bit d set when one of the token's experts lives on rank d.
+__device__ __forceinline__ uint32_t dest_mask(const EpParams& p, int64_t i) {
+  uint32_t m = 0;
+  for (int j = 0; j < p.k; ++j) {
+    const int id = p.ids[i * p.k + j];
+    if (id >= 0) m |= 1u << (id / p.e_local);
+  }
+  return m;
+}
+
+__global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(EpParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  __shared__ uint32_t s_epoch;
+  __shared__ volatile int bail;
+  if (threadIdx.x == 0) {
+    s_epoch = ++p.counters[blockIdx.x];
+    bail = 0;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int nv = p.H / 8;
+  const int64_t T = p.T;
+  for (int64_t i = blockIdx.x; i < T; i += gridDim.x) {
+    const int64_t row = static_cast<int64_t>(p.rank) * T + i;  // this token's row on every rank
+    if (threadIdx.x < p.world * p.k) {
+      const int d = threadIdx.x / p.k, j = threadIdx.x % p.k;
+      const int id = p.ids[i * p.k + j];
+      const bool mine = id >= 0 && id / p.e_local == d;
+      p.peer_ids[d][row * p.k + j] = mine ? id - d * p.e_local : -1;
+      p.peer_w[d][row * p.k + j] = mine ? p.w[i * p.k + j] : 0.f;
+    }
+    const uint32_t m = dest_mask(p, i);
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + i * p.H);
+    for (int d = 0; d < p.world; ++d) {
+      if (!((m >> d) & 1u)) continue;
+      uint4* dst = reinterpret_cast<uint4*>(p.peer_x[d] + row * p.H);
+      for (int v = threadIdx.x; v < nv; v += kThreads) dst[v] = src[v];
+    }
+  }
+  barrier(p, 0, epoch, &bail);
+}
+
+__global__ void __launch_bounds__(kThreads) ep_combine_kernel(EpParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  __shared__ uint32_t s_epoch;
+  __shared__ volatile int bail;
+  if (threadIdx.x == 0) {
+    s_epoch = p.counters[blockIdx.x];  // the epoch of this call's dispatch
+    bail = 0;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int nv = p.H / 8;
+  const int64_t T = p.T;
+  const int32_t* my_ids = p.peer_ids[p.rank];
+  // Push: row r*T + i of y goes back to its owner r when a local expert served it.
+  for (int64_t i = blockIdx.x; i < T; i += gridDim.x) {
+    for (int r = 0; r < p.world; ++r) {
+      const int64_t row = static_cast<int64_t>(r) * T + i;
+      bool served = false;
+      for (int j = 0; j < p.k; ++j) served |= my_ids[row * p.k + j] >= 0;
+      if (!served) continue;
+      const uint4* src = reinterpret_cast<const uint4*>(p.y + row * p.H);
+      uint4* dst = reinterpret_cast<uint4*>(p.peer_y[r] + (static_cast<int64_t>(p.rank) * T + i) * p.H);
+      for (int v = threadIdx.x; v < nv; v += kThreads) dst[v] = src[v];
+    }
+  }
+  if (!barrier(p, 1, epoch, &bail)) return;
+  // Sum the returned rows of each own token in rank order.
+  const __nv_bfloat16* ret = p.peer_y[p.rank];
+  for (int64_t i = blockIdx.x; i < T; i += gridDim.x) {
+    const uint32_t m = dest_mask(p, i);
+    for (int v = threadIdx.x; v < nv; v += kThreads) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int d = 0; d < p.world; ++d) {
+        if (!((m >> d) & 1u)) continue;
+        const uint4 u = reinterpret_cast<const uint4*>(ret + (static_cast<int64_t>(d) * T + i) * p.H)[v];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          acc[2 * e] += f.x;
+          acc[2 * e + 1] += f.y;
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) oh[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+      reinterpret_cast<uint4*>(p.out + i * p.H)[v] = o;
+    }
+  }
+}
+
+}  // namespace ep
+}  // namespace shk
+
+using namespace shk::ep;
+
+static int ep_check(const EpParams& p) {
+  if (p.world < 1 || p.world > SH_EP_MAX_WORLD || p.H % 8 != 0 || p.T < 0 || p.T > p.max_T) return -1;
+  if (p.k < 1 || p.k > SH_EP_MAX_K || p.world * p.k > kThreads || p.e_local < 1) return -2;
+  return 0;
+}
+
+extern "C" int sh_ep_dispatch(const EpParams* params, int num_blocks, cudaStream_t stream) {
+  const int rc = ep_check(*params);
+  if (rc) return rc;
+  if (params->T == 0) return 0;
+  num_blocks = num_blocks < 1 ? 1 : (num_blocks > SH_EP_MAX_BLOCKS ? SH_EP_MAX_BLOCKS : num_blocks);
+  shk::launch(ep_dispatch_kernel, dim3(num_blocks), dim3(kThreads), 0, stream, *params);
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int sh_ep_combine(const EpParams* params, int num_blocks, cudaStream_t stream) {
+  const int rc = ep_check(*params);
+  if (rc) return rc;
+  if (params->T == 0) return 0;
+  num_blocks = num_blocks < 1 ? 1 : (num_blocks > SH_EP_MAX_BLOCKS ? SH_EP_MAX_BLOCKS : num_blocks);
+  shk::launch(ep_combine_kernel, dim3(num_blocks), dim3(kThreads), 0, stream, *params);
+  return static_cast<int>(cudaGetLastError());
+}

@@ -1,0 +1,39 @@
+// C ABI of the expert-parallel all-to-all over NVLink peer memory (no PyTorch types).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define SH_EP_MAX_WORLD 8
+#define SH_EP_MAX_BLOCKS 160
+#define SH_EP_MAX_K 16
+
+// One call = dispatch, the expert GEMMs on the received rows, combine.  Every
+// rank holds T tokens (T equal on every rank within a call).  Received rows
+// are laid out by source rank: rows [r*T, r*T + T) of a receive buffer hold
+// source rank r's tokens, so the expert GEMMs see one [world*T, H] matrix.
+struct EpParams {
+  const __nv_bfloat16* x;                  // [T, H] this rank's tokens (dispatch)
+  const int32_t* ids;                      // [T, k] global expert ids of this rank's tokens
+  const float* w;                          // [T, k] route weights (dispatch)
+  __nv_bfloat16* peer_x[SH_EP_MAX_WORLD];  // per rank: [world*max_T][H] received token rows
+  int32_t* peer_ids[SH_EP_MAX_WORLD];      // per rank: [world*max_T][k] local expert id, -1 elsewhere
+  float* peer_w[SH_EP_MAX_WORLD];          // per rank: [world*max_T][k] weight, 0 elsewhere
+  const __nv_bfloat16* y;                  // combine: [world*T, H] this rank's expert outputs per received row
+  __nv_bfloat16* peer_y[SH_EP_MAX_WORLD];  // per rank: [world*max_T][H] returned rows, rows [d*T, d*T+T) from rank d
+  __nv_bfloat16* out;                      // combine: [T, H] sum over the expert ranks in rank order
+  uint32_t* peer_flags[SH_EP_MAX_WORLD];   // per rank: [2 phases][SH_EP_MAX_BLOCKS][SH_EP_MAX_WORLD]
+  uint32_t* counters;                      // [SH_EP_MAX_BLOCKS] local epochs (dispatch advances them)
+  int* err;                                // nonzero after a timed-out wait
+  int rank, world, T, H, k, e_local, max_T;
+};
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+// Both use the same grid on every rank and for every call of a communicator.
+int sh_ep_dispatch(const EpParams* p, int num_blocks, cudaStream_t stream);
+int sh_ep_combine(const EpParams* p, int num_blocks, cudaStream_t stream);
+#ifdef __cplusplus
+}
+#endif

@@ -2,9 +2,10 @@
 
 Two layouts.  With replicated (or tensor-parallel) attention every rank sees every token:
 `dispatch_combine` below.  With data-parallel attention (state.dp > 1) every rank holds different
-tokens: `dp_dispatch_combine` gathers all ranks' tokens and routes, runs this rank's experts over them
-and reduce-scatters the partial outputs back to their owners (the engine pads every rank to the same
-token count per call).
+tokens: `dp_dispatch_combine` sends each token row only to the ranks that host its experts and returns
+the expert outputs to the owner, with P2P stores from the kernels of ``parallel/ep_a2a.py`` (CUDA), or
+gathers all ranks' tokens and routes, runs this rank's experts over them and reduce-scatters the partial
+outputs back (NCCL / gloo, ``SH_EP_A2A=0``); the engine pads every rank to the same token count per call.
 
 Layout of the reference's EP (reference: suffix_hybrid/kernels/nvfp4_moe.py:78-84,449-457 and
 docs/dsv41-comms.md:54-58): every rank sees every token (attention is replicated or tensor
@@ -15,6 +16,8 @@ written straight into the communicator's buffer, so the combine is this framewor
 all-reduce kernel (or NCCL with ``comm=nccl``).
 """
 from __future__ import annotations
+
+import os
 
 import torch
 
@@ -71,19 +74,38 @@ def _reduce_scatter(y: torch.Tensor) -> torch.Tensor:
     return y[st.rank * T:(st.rank + 1) * T].contiguous()
 
 
+def _experts(moe, xs: torch.Tensor, ids_l: torch.Tensor, w_l: torch.Tensor) -> torch.Tensor:
+    if moe.fp4 is not None:
+        return ops.moe_experts_nvfp4(xs, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F)
+    if getattr(moe, "fp8", None) is not None:
+        return ops.moe_experts_mxfp8(xs, ids_l, w_l, moe.fp8[0], moe.fp8[1], moe.E_local, moe.F)
+    return ops.moe_experts(xs, ids_l, w_l, moe.w13, moe.w2, moe.E_local, moe.F)
+
+
+A2A_MAX_TOKENS = int(os.environ.get("SH_EP_A2A_MAX_TOKENS", "4096"))
+
+
+def a2a_enabled(x: torch.Tensor) -> bool:
+    """Device all-to-all over NVLink peer memory (SH_EP_A2A=0: NCCL all-gather / reduce-scatter).  The
+    decision depends only on values equal on every rank (device kind, world, T)."""
+    st = state.get()
+    return (x.is_cuda and st.world > 1 and os.environ.get("SH_EP_A2A", "1") != "0"
+            and x.shape[0] <= A2A_MAX_TOKENS)
+
+
 def dp_dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Data-parallel attention: every rank's tokens through this rank's experts; each rank keeps its own rows.
 
     x [T, H] (T equal on every rank), ids / w [T, k] from the local router; returns [T, H]."""
     st = state.get()
+    if a2a_enabled(x):
+        from . import ep_a2a
+
+        comm = ep_a2a.get(x.shape[1], A2A_MAX_TOKENS, ids.shape[1], moe.E_local)
+        xs, ids_l, w_l = comm.dispatch(x, ids, w)
+        return comm.combine(_experts(moe, xs, ids_l, w_l), ids)
     xs = _all_gather(x)
     ids_a = _all_gather(ids)
     w_a = _all_gather(w)
     ids_l, w_l = local_routes(ids_a, w_a, st.ep_rank * moe.E_local, moe.E_local)
-    if moe.fp4 is not None:
-        part = ops.moe_experts_nvfp4(xs, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F)
-    elif getattr(moe, "fp8", None) is not None:
-        part = ops.moe_experts_mxfp8(xs, ids_l, w_l, moe.fp8[0], moe.fp8[1], moe.E_local, moe.F)
-    else:
-        part = ops.moe_experts(xs, ids_l, w_l, moe.w13, moe.w2, moe.E_local, moe.F)
-    return _reduce_scatter(part)
+    return _reduce_scatter(_experts(moe, xs, ids_l, w_l))
