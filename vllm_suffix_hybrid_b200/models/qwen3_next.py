@@ -27,11 +27,11 @@ from .common import AttnMeta, Linear, RMSNorm, dtype_of, init_weight
 from .moe import MoEBlock
 
 
-@dataclass
-
 # Prefill runs through the chunked tensor-core kernel (SH_GDN_CHUNK=0: the recurrent kernel).
 _CHUNKED = os.environ.get("SH_GDN_CHUNK", "1") != "0"
 
+
+@dataclass
 class GdnCache:
     state: torch.Tensor  # [slots, HV, V, K] fp32
     conv: torch.Tensor  # [slots, C, 3] fp32
