@@ -115,7 +115,8 @@ void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std:
                      std::vector<int64_t> peer_flags, torch::Tensor counters, torch::Tensor out,
                      c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, torch::Tensor err,
                      int64_t rank, int64_t T, int64_t H, int64_t max_T, double eps, bool two_shot,
-                     int64_t num_blocks, c10::optional<torch::Tensor> timing) {
+                     int64_t num_blocks, c10::optional<torch::Tensor> timing, int64_t prefetch_ptr,
+                     int64_t prefetch_bytes) {
   const int world = static_cast<int>(peer_recv.size());
   TORCH_CHECK(world >= 1 && world <= SH_COMM_MAX_WORLD && peer_gather.size() == peer_recv.size() &&
                   peer_flags.size() == peer_recv.size(), "allreduce_fused: peer lists");
@@ -152,6 +153,8 @@ void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std:
     TORCH_CHECK(timing->scalar_type() == at::kLong && timing->numel() >= 256, "allreduce_fused: timing [64, 4] int64");
     p.timing = reinterpret_cast<unsigned long long*>(timing->data_ptr<int64_t>());
   }
+  p.prefetch = reinterpret_cast<const void*>(prefetch_ptr);
+  p.prefetch_bytes = static_cast<unsigned long long>(prefetch_bytes > 0 ? prefetch_bytes : 0);
   const int r = sh_allreduce(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_allreduce failed with code ", r);
 }
@@ -193,7 +196,8 @@ void rs_norm_ag(int64_t recv, std::vector<int64_t> peer_gather, std::vector<int6
                 std::vector<int64_t> peer_flags, int64_t rs_cnt, torch::Tensor targets, torch::Tensor counters,
                 torch::Tensor residual, torch::Tensor out, torch::Tensor weight, torch::Tensor err, int64_t rank,
                 int64_t T, int64_t H, int64_t max_T, int64_t Tc, int64_t expected, double eps, bool gather_res,
-                int64_t num_blocks, c10::optional<torch::Tensor> timing) {
+                int64_t num_blocks, c10::optional<torch::Tensor> timing, int64_t prefetch_ptr,
+                int64_t prefetch_bytes) {
   const int world = static_cast<int>(peer_gather.size());
   TORCH_CHECK(world >= 1 && world <= SH_COMM_MAX_WORLD && peer_flags.size() == peer_gather.size() &&
                   peer_gather_res.size() == peer_gather.size(), "rs_norm_ag: peer lists");
@@ -226,6 +230,8 @@ void rs_norm_ag(int64_t recv, std::vector<int64_t> peer_gather, std::vector<int6
   p.eps = static_cast<float>(eps);
   p.gather_res = gather_res ? 1 : 0;
   if (timing.has_value()) p.timing = reinterpret_cast<unsigned long long*>(timing->data_ptr<int64_t>());
+  p.prefetch = reinterpret_cast<const void*>(prefetch_ptr);
+  p.prefetch_bytes = static_cast<unsigned long long>(prefetch_bytes > 0 ? prefetch_bytes : 0);
   const int r = sh_rs_norm_ag(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_rs_norm_ag failed with code ", r);
 }
@@ -752,13 +758,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("allreduce_fused", &allreduce_fused, py::arg("partial"), py::arg("peer_recv"), py::arg("peer_gather"),
         py::arg("peer_flags"), py::arg("counters"), py::arg("out"), py::arg("residual"), py::arg("weight"),
         py::arg("err"), py::arg("rank"), py::arg("T"), py::arg("H"), py::arg("max_T"), py::arg("eps"),
-        py::arg("two_shot"), py::arg("num_blocks"), py::arg("timing") = py::none());
+        py::arg("two_shot"), py::arg("num_blocks"), py::arg("timing") = py::none(), py::arg("prefetch_ptr") = 0,
+        py::arg("prefetch_bytes") = 0);
   m.def("gemm_bf16_push", &gemm_bf16_push);
   m.def("rs_norm_ag", &rs_norm_ag, py::arg("recv"), py::arg("peer_gather"), py::arg("peer_gather_res"),
         py::arg("peer_flags"), py::arg("rs_cnt"), py::arg("targets"), py::arg("counters"), py::arg("residual"),
         py::arg("out"), py::arg("weight"), py::arg("err"), py::arg("rank"), py::arg("T"), py::arg("H"),
         py::arg("max_T"), py::arg("Tc"), py::arg("expected"), py::arg("eps"), py::arg("gather_res"),
-        py::arg("num_blocks"), py::arg("timing") = py::none());
+        py::arg("num_blocks"), py::arg("timing") = py::none(), py::arg("prefetch_ptr") = 0,
+        py::arg("prefetch_bytes") = 0);
   m.def("mla_decode", &mla_decode);
   m.def("mla_cache_write", &mla_cache_write);
   m.def("dsa_topk", &dsa_topk);

@@ -101,6 +101,22 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
   return r;
 }
 
+// L2 prefetch of block b's slice of [base, base + bytes): the weights of the
+// GEMM that follows the collective are static, so the fetch is issued before
+// griddepcontrol.wait and proceeds while the ranks push and wait.
+__device__ __forceinline__ void l2_prefetch_slice(const void* base, unsigned long long bytes) {
+  if (base == nullptr || bytes < 16 || threadIdx.x != 0) return;
+  const unsigned long long per = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+  const unsigned long long lo = static_cast<unsigned long long>(blockIdx.x) * per;
+  const unsigned long long hi = lo + per < bytes ? lo + per : bytes;
+  for (unsigned long long off = lo; off + 16 <= hi; off += (1u << 20)) {
+    const unsigned long long left = hi - off;
+    const uint32_t n = static_cast<uint32_t>(left < (1u << 20) ? left : (1u << 20)) & ~15u;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const char*>(base) + off), "r"(n)
+                 : "memory");
+  }
+}
+
 // Rows are processed by groups of kGroupThreads threads (four warps); a block
 // runs blockDim.x / kGroupThreads groups on different rows at once, so decode
 // sizes (tens to hundreds of rows) are handled in one pass instead of one row
@@ -225,6 +241,7 @@ __device__ __forceinline__ void push_row(const uint4* src, uint4* const* dst, in
 template <int VPT>
 __global__ void __launch_bounds__(512) allreduce_kernel(ArParams p) {
   shk::pdl_trigger();
+  l2_prefetch_slice(p.prefetch, p.prefetch_bytes);
   shk::pdl_wait();
   __shared__ float red[32];
   __shared__ uint32_t s_epoch;
@@ -326,6 +343,7 @@ __global__ void __launch_bounds__(512) allreduce_kernel(ArParams p) {
 template <int VPT>
 __global__ void __launch_bounds__(512) rs_norm_ag_kernel(RsParams p) {
   shk::pdl_trigger();
+  l2_prefetch_slice(p.prefetch, p.prefetch_bytes);
   shk::pdl_wait();
   __shared__ float red[32];
   __shared__ uint32_t s_epoch, s_target;

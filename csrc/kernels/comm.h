@@ -26,6 +26,10 @@ struct ArParams {
   // Optional phase timestamps (%globaltimer, ns) of block 0: [64 calls][4] =
   // entry, pushes issued, first wait passed, exit; slot = epoch % 64.
   unsigned long long* timing;
+  // Optional L2 prefetch of the next GEMM's weights while the ranks wait on
+  // each other (every block takes a slice; nullptr / 0 = none).
+  const void* prefetch;
+  unsigned long long prefetch_bytes;
 };
 
 // Reduce-scatter tail of a row-parallel GEMM whose epilogue pushed its output
@@ -52,6 +56,8 @@ struct RsParams {
   float eps;
   int gather_res;
   unsigned long long* timing;  // optional [64][4] phase stamps of block 0
+  const void* prefetch;        // optional L2 prefetch of the next GEMM's weights (as ArParams)
+  unsigned long long prefetch_bytes;
 };
 
 #ifdef __cplusplus

@@ -169,7 +169,8 @@ class DecoderLayer:
     def __call__(self, x: torch.Tensor, residual: torch.Tensor, meta: AttnMeta, kv, first: bool):
         """x: the normalised input of this layer (residual holds the stream)."""
         h = self.attn(x, meta, kv)
-        h = comm.all_reduce_add_rms_norm(h, residual, self.post_norm.weight, self.post_norm.eps)
+        h = comm.all_reduce_add_rms_norm(h, residual, self.post_norm.weight, self.post_norm.eps,
+                                         prefetch=self.mlp.gate_up.weight)
         m = self.mlp(h)
         return m  # partial; the next layer's input norm reduces + adds it
 

@@ -48,9 +48,10 @@ class LlamaModel:
         x = ops.rms_norm(residual, self.layers[0].input_norm.weight, self.cfg.norm_eps)
         for i, layer in enumerate(self.layers):
             m = layer(x, residual, meta, kv_caches[i], i == 0)
-            nxt = self.layers[i + 1].input_norm if i + 1 < len(self.layers) else self.norm
-            x = comm.all_reduce_add_rms_norm(m, residual, nxt.weight, nxt.eps,
-                                             gather_residual=i + 1 == len(self.layers))
+            last = i + 1 == len(self.layers)
+            nxt = self.norm if last else self.layers[i + 1].input_norm
+            x = comm.all_reduce_add_rms_norm(m, residual, nxt.weight, nxt.eps, gather_residual=last,
+                                             prefetch=None if last else self.layers[i + 1].attn.qkv.weight)
         return x, residual
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:

@@ -67,20 +67,21 @@ def partial_out(tokens: int, hidden: int, like: torch.Tensor, force: bool = Fals
 
 
 def all_reduce_add_rms_norm(x, residual: torch.Tensor, w: torch.Tensor, eps: float,
-                            gather_residual: bool = False) -> torch.Tensor:
+                            gather_residual: bool = False, prefetch: Optional[torch.Tensor] = None) -> torch.Tensor:
     """residual += allreduce(x); returns rms_norm(residual) * w (x may be reused as the output).
 
     x is a tensor partial, or the handle of a GEMM that pushed its rows to their owners: then each
     rank updates only the residual rows it owns (sequence-parallel residual) and every rank gets all
-    normalised rows; gather_residual=True also brings every residual row up to date.
+    normalised rows; gather_residual=True also brings every residual row up to date.  prefetch: the
+    weight of the GEMM that reads the result, pulled into L2 by the fused kernel while the ranks wait.
     """
     from .. import ops
 
     if not isinstance(x, torch.Tensor):
-        return x.comm.finish_push(x, residual, w, eps, gather_residual)
+        return x.comm.finish_push(x, residual, w, eps, gather_residual, prefetch)
     st = state.get()
     if st.tp > 1 and _FUSED is not None and _FUSED.can_all_reduce(x):
-        return _FUSED.all_reduce_add_rms_norm(x, residual, w, eps)
+        return _FUSED.all_reduce_add_rms_norm(x, residual, w, eps, prefetch)
     if st.tp > 1:
         dist.all_reduce(x, group=st.group)
     ops.fused_add_rms_norm(x, residual, w, eps)

@@ -75,6 +75,8 @@ class SymmComm:
         self.blocks = min(MAX_BLOCKS, sms)
         env = os.environ.get("SH_ONE_SHOT_MAX_BYTES")
         self.one_shot_max_bytes = int(env) if env else (one_shot_max_bytes or (4 << 20))
+        # L2 prefetch of the next GEMM's weights from the collective kernels (SH_L2_PREFETCH_MAX_BYTES=0: off)
+        self.l2_prefetch_max_bytes = int(os.environ.get("SH_L2_PREFETCH_MAX_BYTES", str(24 << 20)))
         dist.barrier(group=self.group)
 
     # -- buffers --------------------------------------------------------------
@@ -91,15 +93,26 @@ class SymmComm:
         return self.owns(x) and x.shape[0] <= self.max_tokens
 
     # -- collectives ----------------------------------------------------------
-    def _launch(self, x: torch.Tensor, out: torch.Tensor, residual=None, weight=None, eps: float = 0.0) -> None:
+    def _prefetch(self, nxt: Optional[torch.Tensor]):
+        """(pointer, bytes) of the next GEMM's weight to pull into L2 while the ranks wait (C7: the
+        reference prefetches the next window's weights from its waiting all-reduce blocks, reference:
+        suffix_hybrid/host_ar.py:106-127).  Capped at ``l2_prefetch_max_bytes`` (the head of the weight,
+        which the GEMM's first tile wave reads)."""
+        if nxt is None or not self.l2_prefetch_max_bytes:
+            return 0, 0
+        return nxt.data_ptr(), min(nxt.numel() * nxt.element_size(), self.l2_prefetch_max_bytes)
+
+    def _launch(self, x: torch.Tensor, out: torch.Tensor, residual=None, weight=None, eps: float = 0.0,
+                prefetch: Optional[torch.Tensor] = None) -> None:
         from .. import ops
 
         T, H = x.shape
         sent = (self.world - 1) * T * H * x.element_size()
         two_shot = sent > self.one_shot_max_bytes and T >= self.world
+        pf, pf_bytes = self._prefetch(prefetch)
         ops.native().allreduce_fused(x, self.peer_recv, self.peer_gather, self.peer_flags, self.counters, out,
                                      residual, weight, self.err, self.rank, T, H, self.max_tokens, eps, two_shot,
-                                     self.blocks, self.timing)
+                                     self.blocks, self.timing, pf, pf_bytes)
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         out = torch.empty_like(x)
@@ -107,9 +120,9 @@ class SymmComm:
         return out
 
     def all_reduce_add_rms_norm(self, x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
-                                eps: float) -> torch.Tensor:
+                                eps: float, prefetch: Optional[torch.Tensor] = None) -> torch.Tensor:
         out = torch.empty_like(x)
-        self._launch(x, out, residual, w, eps)
+        self._launch(x, out, residual, w, eps, prefetch)
         return out
 
     # -- reduce-scatter in the GEMM epilogue -----------------------------------
@@ -148,14 +161,15 @@ class SymmComm:
         return PushedPartial(self, T, self.push_expected(T, N, False, bn))
 
     def finish_push(self, pp: "PushedPartial", residual: torch.Tensor, w: torch.Tensor, eps: float,
-                    gather_residual: bool = False) -> torch.Tensor:
+                    gather_residual: bool = False, prefetch: Optional[torch.Tensor] = None) -> torch.Tensor:
         from .. import ops
 
         out = torch.empty(pp.T, self.hidden, dtype=residual.dtype, device=residual.device)
+        pf, pf_bytes = self._prefetch(prefetch)
         ops.native().rs_norm_ag(self.peer_recv[self.rank], self.peer_gather, self.peer_gather_res, self.peer_flags,
                                 self.peer_rs_cnt[self.rank], self.targets, self.counters, residual, out, w, self.err,
                                 self.rank, pp.T, self.hidden, self.max_tokens, self.owner_rows(pp.T), pp.expected,
-                                eps, gather_residual, self.blocks, self.timing)
+                                eps, gather_residual, self.blocks, self.timing, pf, pf_bytes)
         return out
 
     def check(self) -> None:
