@@ -378,10 +378,12 @@ void gemm_nvfp4(torch::Tensor y, torch::Tensor x, torch::Tensor packed, torch::T
 // NVFP4 activation quantiser (see sh_nvfp4_quant_act): x bf16 [rows, K] ->
 // xq uint8 [rows, K/2], x_sf uint8 [tiles, kc4, 512], a_scale fp32 [rows].
 void nvfp4_quant_act(torch::Tensor x, torch::Tensor xq, torch::Tensor x_sf, torch::Tensor a_scale, int64_t tile_rows,
-                     double static_g, c10::optional<torch::Tensor> groups, c10::optional<torch::Tensor> num_groups) {
+                     double static_g, c10::optional<torch::Tensor> groups, c10::optional<torch::Tensor> num_groups,
+                     bool swiglu) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
-              "nvfp4_quant_act: x bf16 [rows, K]");
-  const int64_t rows = x.size(0), K = x.size(1);
+              "nvfp4_quant_act: x bf16 [rows, K] (or [rows, 2K] gate | up with swiglu)");
+  TORCH_CHECK(!swiglu || x.size(1) % 2 == 0, "nvfp4_quant_act: swiglu needs an even width");
+  const int64_t rows = x.size(0), K = swiglu ? x.size(1) / 2 : x.size(1);
   TORCH_CHECK(xq.scalar_type() == at::kByte && xq.is_contiguous() && xq.size(0) >= rows && xq.size(1) * 2 == K,
               "nvfp4_quant_act: xq uint8 [rows, K/2]");
   const int64_t kc4 = (K + 255) / 256 * 4;
@@ -403,7 +405,7 @@ void nvfp4_quant_act(torch::Tensor x, torch::Tensor xq, torch::Tensor x_sf, torc
                                    static_cast<int>(max_tiles), static_cast<int>(tile_rows),
                                    static_cast<float>(static_g), xq.data_ptr<uint8_t>(),
                                    reinterpret_cast<uint8_t*>(x_sf.data_ptr()), a_scale.data_ptr<float>(),
-                                   at::cuda::getCurrentCUDAStream());
+                                   swiglu ? 1 : 0, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_nvfp4_quant_act failed with code ", r);
 }
 
@@ -775,7 +777,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rows_p") = 0, py::arg("err") = py::none(), py::arg("splits") = 1, py::arg("ws") = py::none());
   m.def("nvfp4_quant_act", &nvfp4_quant_act, py::arg("x"), py::arg("xq"), py::arg("x_sf"), py::arg("a_scale"),
         py::arg("tile_rows"), py::arg("static_g") = 0.0, py::arg("groups") = py::none(),
-        py::arg("num_groups") = py::none());
+        py::arg("num_groups") = py::none(), py::arg("swiglu") = false);
   m.def("gemm_fp4mma", &gemm_fp4mma, py::arg("y"), py::arg("xq"), py::arg("x_sf"), py::arg("a_scale"), py::arg("w"),
         py::arg("w_sf"), py::arg("alpha_w"), py::arg("bn"), py::arg("groups") = py::none(),
         py::arg("num_groups") = py::none(), py::arg("rows_p") = 0, py::arg("err") = py::none(),

@@ -500,7 +500,25 @@ __device__ __forceinline__ void load16(const __nv_bfloat16* p, float* v) {
 
 constexpr int QUANT_THREADS = 512;
 
+// Block b (16 values) of an activation row.  SWIGLU: the row is a fused
+// gate | up projection [2K] and the activation is silu(gate) * up rounded to
+// bf16 (the same expression and rounding as silu_mul_bf16_kernel), so the
+// SwiGLU output is quantised without being written out.
+template <bool SWIGLU>
+__device__ __forceinline__ void load_act(const __nv_bfloat16* xr, int K, int b, float* v) {
+  if constexpr (!SWIGLU) {
+    load16(xr + b * 16, v);
+  } else {
+    float g[16], u[16];
+    load16(xr + b * 16, g);
+    load16(xr + K + b * 16, u);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(g[j] / (1.f + __expf(-g[j])) * u[j]));
+  }
+}
+
 // One CTA per activation row, one thread per 16-element block (looping for K > 8192).
+template <bool SWIGLU>
 __global__ void __launch_bounds__(QUANT_THREADS) quant_act_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t ldx, int rows, int K, const int4* __restrict__ groups,
     const int* __restrict__ num_groups, int tile_rows, float static_g, uint8_t* __restrict__ xq,
@@ -535,7 +553,7 @@ __global__ void __launch_bounds__(QUANT_THREADS) quant_act_kernel(
     float amax = 0.f;
     for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
       float v[16];
-      load16(xr + b * 16, v);
+      load_act<SWIGLU>(xr, K, b, v);
 #pragma unroll
       for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
     }
@@ -555,7 +573,7 @@ __global__ void __launch_bounds__(QUANT_THREADS) quant_act_kernel(
     uint8_t s8 = 0;
     if (b < nblk) {
       float v[16];
-      load16(xr + b * 16, v);
+      load_act<SWIGLU>(xr, K, b, v);
       float am = 0.f;
 #pragma unroll
       for (int j = 0; j < 16; ++j) am = fmaxf(am, fabsf(v[j]));
@@ -688,13 +706,14 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const Fp4MmaParams& g, in
 
 extern "C" int sh_nvfp4_quant_act(const void* x, int64_t ldx, int rows, int K, const int4* groups,
                                   const int* num_groups, int max_tiles, int tile_rows, float static_g, uint8_t* xq,
-                                  uint8_t* x_sf, float* a_scale, cudaStream_t stream) {
+                                  uint8_t* x_sf, float* a_scale, int swiglu, cudaStream_t stream) {
   if (K % 64 != 0 || K <= 0 || tile_rows <= 0 || tile_rows > 128) return -2;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(xq) & 7)) return -3;
   if (rows <= 0 || max_tiles <= 0) return 0;
   const int nb = ((K + KB - 1) / KB) * 4 * 4;
   const int threads = nb >= QUANT_THREADS ? QUANT_THREADS : (nb + 31) / 32 * 32;
-  shk::launch(quant_act_kernel, dim3(rows), dim3(threads), 0, stream,
+  if (swiglu && ldx < 2 * static_cast<int64_t>(K)) return -5;
+  shk::launch(swiglu ? quant_act_kernel<true> : quant_act_kernel<false>, dim3(rows), dim3(threads), 0, stream,
               static_cast<const __nv_bfloat16*>(x), ldx, rows, K, groups, num_groups, tile_rows, static_g, xq, x_sf,
               a_scale);
   return static_cast<int>(cudaGetLastError());

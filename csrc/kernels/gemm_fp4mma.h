@@ -44,9 +44,11 @@ extern "C" {
 //   the row: dense (groups == nullptr): tile r / tile_rows, slot r % tile_rows;
 //   grouped: the entry e with q_row0 <= r < q_row0 + q_rows, slot r - q_row0.
 // max_tiles bounds the grid (dense: ceil(rows / tile_rows); grouped: max_groups).
+// swiglu: x rows are a fused gate | up projection [2K] (row stride ldx >= 2K) and the quantised
+// activation is silu(gate) * up (bf16-rounded), i.e. the SwiGLU is fused into the quantiser.
 int sh_nvfp4_quant_act(const void* x, int64_t ldx, int rows, int K, const int4* groups, const int* num_groups,
                        int max_tiles, int tile_rows, float static_g, uint8_t* xq, uint8_t* x_sf, float* a_scale,
-                       cudaStream_t stream);
+                       int swiglu, cudaStream_t stream);
 // out[t, n] = alpha_w * a_scale[t] * sum_k e2m1(xq[t, k]) sx(t, k) e2m1(w[n, k]) sw(n, k); bn in {64, 128}.
 // splits > 1 (dense mode) needs ws (splits * tiles_p * tiles_q * 128 * bn floats) and zeroed counters.
 int sh_gemm_fp4mma(Fp4MmaParams* g, const void* xq, int rows_q, int bn, int splits, int num_sms,

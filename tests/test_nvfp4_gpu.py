@@ -122,6 +122,19 @@ def test_quant_act_matches_reference(rows, K, tile, static_g):
     assert torch.equal(_deswizzle(x_sf, rows, tile, K // 16), ps)
 
 
+@pytest.mark.parametrize("rows,F,tile", [(100, 1024, 64), (37, 2048, 128)])
+def test_quant_act_swiglu_fusion_equals_silu_mul_then_quant(rows, F, tile):
+    """The quantiser's fused SwiGLU reads gate | up and must equal silu_mul followed by the plain quantiser."""
+    torch.manual_seed(rows + F)
+    gu = (torch.randn(rows, 2 * F) * 2).to(torch.bfloat16).cuda()
+    xq, x_sf, a_sc = [t.clone() for t in ops.nvfp4_quant_act(ops.silu_mul(gu), tile)]
+    fq, f_sf, f_sc = ops.nvfp4_quant_act(gu, tile, swiglu=True)
+    torch.cuda.synchronize()
+    assert torch.equal(fq[:rows], xq[:rows])
+    assert torch.equal(f_sc[:rows], a_sc[:rows])
+    assert torch.equal(_deswizzle(f_sf, rows, tile, F // 16), _deswizzle(x_sf, rows, tile, F // 16))
+
+
 def test_scale_tiles_match_the_swizzled_layout():
     """nvfp4_scale_tiles == the 128x4 layout byte (row/128)*kb_pad*128 + (kb/4)*512 + (row%32)*16 +
     ((row/32)%4)*4 + kb%4 for K a multiple of 256 (reference: kernels/nvfp4_gemm.py sf_offset)."""

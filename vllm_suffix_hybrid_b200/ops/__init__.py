@@ -630,13 +630,17 @@ def _fp4_act_buffers(dev, rows: int, K: int, tiles: int):
             b[2][:rows])
 
 
-def nvfp4_quant_act(x: torch.Tensor, tile_rows: int, static_g: float = 0.0, groups=None, num_groups=None):
+def nvfp4_quant_act(x: torch.Tensor, tile_rows: int, static_g: float = 0.0, groups=None, num_groups=None,
+                    swiglu: bool = False):
     """(xq [R, K/2], x_sf scale tiles, a_scale [R]) of bf16 activations x [R, K] (see
-    reference.nvfp4_quant_act); CUDA buffers are per-device scratch reused by the next call."""
+    reference.nvfp4_quant_act); CUDA buffers are per-device scratch reused by the next call.  swiglu: x is a
+    fused gate | up projection [R, 2K] and the quantised activation is silu_mul(x), fused into the kernel."""
     R, K = x.shape
+    if swiglu:
+        K //= 2
     tiles = groups.shape[0] if groups is not None else -(-R // tile_rows)
     xq, x_sf, a_scale = _fp4_act_buffers(x.device, R, K, tiles)
-    native().nvfp4_quant_act(x, xq, x_sf, a_scale, tile_rows, float(static_g), groups, num_groups)
+    native().nvfp4_quant_act(x, xq, x_sf, a_scale, tile_rows, float(static_g), groups, num_groups, swiglu)
     return xq, x_sf, a_scale
 
 
@@ -885,8 +889,7 @@ def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
         t2 = w2q[4] if len(w2q) > 4 else nvfp4_scale_tiles(w2q[1], H)
         xq, x_sf, a_sc = nvfp4_quant_act(xs, bn, 0.0, groups, ngroups)
         C.gemm_fp4mma(gu, xq, x_sf, a_sc, w13q[0], t13, w13q[2], bn, groups, ngroups, 2 * F)
-        a = silu_mul(gu)
-        xq, x_sf, a_sc = nvfp4_quant_act(a, bn, 0.0, groups, ngroups)
+        xq, x_sf, a_sc = nvfp4_quant_act(gu, bn, 0.0, groups, ngroups, swiglu=True)  # SwiGLU fused into the quantiser
         C.gemm_fp4mma(ys, xq, x_sf, a_sc, w2q[0], t2, w2q[2], bn, groups2, ngroups, H)
     else:
         sk13 = w13q[3] if len(w13q) > 3 and w13q[3] is not None else nvfp4_kmajor_scales(w13q[1])
