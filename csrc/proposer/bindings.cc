@@ -142,12 +142,12 @@ std::vector<std::vector<int64_t>> to_token_lists(const py::handle& obj) {
 
 // Request ids: zero-copy UTF-8 views into the caller's str objects (valid
 // for the duration of the call; the caller's list keeps them alive).
-std::vector<std::string_view> to_ids(const py::handle& obj, py::list* keep) {
+void to_ids_into(const py::handle& obj, py::list* keep, std::vector<std::string_view>& ids) {
   PyObject* seq = PySequence_Fast(obj.ptr(), "request ids must be a sequence of str");
   if (!seq) throw py::error_already_set();
   const Py_ssize_t n = PySequence_Fast_GET_SIZE(seq);
   PyObject** items = PySequence_Fast_ITEMS(seq);
-  std::vector<std::string_view> ids(static_cast<size_t>(n));
+  ids.resize(static_cast<size_t>(n));
   for (Py_ssize_t i = 0; i < n; ++i) {
     if (!PyUnicode_Check(items[i])) {
       Py_DECREF(seq);
@@ -162,7 +162,27 @@ std::vector<std::string_view> to_ids(const py::handle& obj, py::list* keep) {
     ids[static_cast<size_t>(i)] = std::string_view(s, static_cast<size_t>(len));
   }
   keep->append(py::reinterpret_steal<py::object>(seq));
+}
+
+std::vector<std::string_view> to_ids(const py::handle& obj, py::list* keep) {
+  std::vector<std::string_view> ids;
+  to_ids_into(obj, keep, ids);
   return ids;
+}
+
+// Accepted lengths (list / tuple / NumPy of ints) into a reused vector.
+void to_tokens_into(const py::handle& obj, std::vector<int64_t>& out) {
+  if (PyList_CheckExact(obj.ptr())) {
+    const Py_ssize_t n = PyList_GET_SIZE(obj.ptr());
+    out.resize(static_cast<size_t>(n));
+    for (Py_ssize_t i = 0; i < n; ++i) {
+      const long long v = PyLong_AsLongLong(PyList_GET_ITEM(obj.ptr(), i));
+      if (v == -1 && PyErr_Occurred()) throw py::error_already_set();
+      out[static_cast<size_t>(i)] = v;
+    }
+    return;
+  }
+  out = to_tokens(obj);
 }
 
 // Drafts in: int64 rows plus the caller's int objects, so published tokens
@@ -172,13 +192,14 @@ struct DraftRows {
   std::vector<std::vector<PyObject*>> objs;  // borrowed; caller keeps them alive
 };
 
-DraftRows to_draft_rows(const py::handle& obj, py::list* keep) {
+// Fills `out` in place: its vectors keep their capacity across calls, so a
+// warm call allocates nothing for the draft rows.
+void to_draft_rows(const py::handle& obj, py::list* keep, DraftRows& out) {
   PyObject* seq = PySequence_Fast(obj.ptr(), "native drafts must be a sequence of token lists");
   if (!seq) throw py::error_already_set();
   keep->append(py::reinterpret_steal<py::object>(seq));
   const Py_ssize_t n = PySequence_Fast_GET_SIZE(seq);
   PyObject** rows = PySequence_Fast_ITEMS(seq);
-  DraftRows out;
   out.values.resize(static_cast<size_t>(n));
   out.objs.resize(static_cast<size_t>(n));
   for (Py_ssize_t i = 0; i < n; ++i) {
@@ -202,7 +223,13 @@ DraftRows to_draft_rows(const py::handle& obj, py::list* keep) {
       out.objs[static_cast<size_t>(i)].assign(out.values[static_cast<size_t>(i)].size(), nullptr);
     }
   }
-  return out;
+}
+
+// Per-thread draft-row scratch of the mixer calls (the borrowed int objects are
+// valid for one call: the caller's lists are kept alive by `keep`).
+DraftRows& draft_scratch() {
+  static thread_local DraftRows rows;
+  return rows;
 }
 
 py::list to_pylist_reuse(const std::vector<std::vector<int64_t>>& rows, const DraftRows& src) {
@@ -358,11 +385,11 @@ PYBIND11_MODULE(_native, m) {
              py::object accepted_lengths, py::object step_time_ns) {
             (void)step_time_ns;
             py::list keep;
-            DraftRows nat;
-            auto drafts = guard("mix", [&] {
+            DraftRows& nat = draft_scratch();
+            const auto& drafts = guard("mix", [&]() -> const std::vector<std::vector<int64_t>>& {
               std::vector<std::string_view> ids = to_ids(request_ids, &keep);
               std::vector<std::vector<int64_t>> ctx = to_token_lists(contexts);
-              nat = to_draft_rows(native_drafts, &keep);
+              to_draft_rows(native_drafts, &keep, nat);
               std::vector<int64_t> acc;
               const bool has_acc = !accepted_lengths.is_none();
               if (has_acc) acc = to_tokens(accepted_lengths);
@@ -378,15 +405,16 @@ PYBIND11_MODULE(_native, m) {
              py::object accepted_lengths, py::object step_time_ns) {
             (void)step_time_ns;
             py::list keep;
-            DraftRows nat;
-            auto drafts = guard("mix_numpy", [&] {
-              std::vector<std::string_view> ids = to_ids(request_ids, &keep);
+            DraftRows& nat = draft_scratch();
+            static thread_local std::vector<std::string_view> ids;
+            static thread_local std::vector<int64_t> acc;
+            const auto& drafts = guard("mix_numpy", [&]() -> const std::vector<std::vector<int64_t>>& {
+              to_ids_into(request_ids, &keep, ids);
               IntVector c = as_vector(counts, "counts must be int32/int64 NumPy");
               IntMatrix t = as_matrix(tokens, "tokens must be int32/int64 NumPy");
-              nat = to_draft_rows(native_drafts, &keep);
-              std::vector<int64_t> acc;
+              to_draft_rows(native_drafts, &keep, nat);
               const bool has_acc = !accepted_lengths.is_none();
-              if (has_acc) acc = to_tokens(accepted_lengths);
+              if (has_acc) to_tokens_into(accepted_lengths, acc);
               return x.mix_matrix(ids, c, t, nat.values, has_acc ? &acc : nullptr);
             });
             return to_pylist_reuse(drafts, nat);

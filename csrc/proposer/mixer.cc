@@ -54,7 +54,8 @@ void HybridMixer::validate(const std::vector<std::string_view>& ids, const std::
   bool bad = n > 4096 || native.size() != n || (accepted && accepted->size() != n);
   if (!bad && n > 1) {
     // Duplicate ids: sort 64-bit hashes, compare strings only on equal hash.
-    std::vector<std::pair<size_t, size_t>> hs(n);
+    std::vector<std::pair<size_t, size_t>>& hs = hashes_;
+    hs.resize(n);
     for (size_t i = 0; i < n; ++i) hs[i] = {StrHash{}(ids[i]), i};
     std::sort(hs.begin(), hs.end());
     for (size_t i = 1; i < n && !bad; ++i)
@@ -177,7 +178,7 @@ std::pair<std::vector<int64_t>, size_t> HybridMixer::diverge_row(SuffixCorpus& c
 }
 
 template <class Decide>
-std::vector<std::vector<int64_t>> HybridMixer::mix_core(const std::vector<std::string_view>& ids,
+const std::vector<std::vector<int64_t>>& HybridMixer::mix_core(const std::vector<std::string_view>& ids,
                                                         const std::vector<std::vector<int64_t>>& native,
                                                         const std::vector<int64_t>* accepted, Decide&& decide) {
   const uint64_t start = now_ns();
@@ -229,17 +230,17 @@ std::vector<std::vector<int64_t>> HybridMixer::mix_core(const std::vector<std::s
     }
   }
   last_native_.clear();
-  std::vector<std::vector<int64_t>> result;
-  result.reserve(n);
+  std::vector<std::vector<int64_t>>& result = result_;
+  result.resize(n);  // inner vectors keep their capacity from earlier calls
   const size_t depth = cache.cfg().depth;
-  std::vector<int64_t> delta;
+  std::vector<int64_t>& delta = delta_;
   for (size_t i = 0; i < n; ++i) {
     const std::vector<int64_t>& nat = native[i];
     if (diverge_) {
       const int64_t a = accepted ? (*accepted)[i] : -1;
       auto dr = diverge_row(cache, ids[i], i, nat, a, decide);
       last_native_.push_back(dr.second);
-      result.push_back(std::move(dr.first));
+      result[i] = std::move(dr.first);
       ++decisions_;
       continue;
     }
@@ -287,7 +288,7 @@ std::vector<std::vector<int64_t>> HybridMixer::mix_core(const std::vector<std::s
     SpecResult sr = cache.speculate(conditioned_.data(), conditioned_.size(), cap);
     const bool has_gate = occupied && it->second.has_gate;
     const double gate = has_gate ? it->second.gate : 0.0;
-    std::vector<int64_t> draft;
+    std::vector<int64_t>& draft = result[i];
     size_t native_count;
     bool had_suffix;
     if (sr.tokens.empty() || fresh_row) {
@@ -353,7 +354,6 @@ std::vector<std::vector<int64_t>> HybridMixer::mix_core(const std::vector<std::s
       fresh.stamp = stamp;
       previous_.emplace(std::string(ids[i]), std::move(fresh));
     }
-    result.push_back(std::move(draft));
     ++decisions_;
   }
   ++calls_;
@@ -361,7 +361,7 @@ std::vector<std::vector<int64_t>> HybridMixer::mix_core(const std::vector<std::s
   return result;
 }
 
-std::vector<std::vector<int64_t>> HybridMixer::mix(const std::vector<std::string_view>& ids,
+const std::vector<std::vector<int64_t>>& HybridMixer::mix(const std::vector<std::string_view>& ids,
                                                    const std::vector<std::vector<int64_t>>& contexts,
                                                    const std::vector<std::vector<int64_t>>& native,
                                                    const std::vector<int64_t>* accepted) {
@@ -385,7 +385,7 @@ std::vector<std::vector<int64_t>> HybridMixer::mix(const std::vector<std::string
   return mix_core(ids, native, accepted, decide);
 }
 
-std::vector<std::vector<int64_t>> HybridMixer::mix_matrix(const std::vector<std::string_view>& ids,
+const std::vector<std::vector<int64_t>>& HybridMixer::mix_matrix(const std::vector<std::string_view>& ids,
                                                           const IntVector& counts, const IntMatrix& tokens,
                                                           const std::vector<std::vector<int64_t>>& native,
                                                           const std::vector<int64_t>* accepted) {

@@ -37,14 +37,15 @@ class HybridMixer {
  public:
   HybridMixer(size_t num_speculative_tokens, size_t max_model_len);
 
-  // List API: full authoritative contexts, exact prefix continuity.
-  std::vector<std::vector<int64_t>> mix(const std::vector<std::string_view>& ids,
+  // List API: full authoritative contexts, exact prefix continuity.  The
+  // returned drafts live in the mixer (reused by the next call).
+  const std::vector<std::vector<int64_t>>& mix(const std::vector<std::string_view>& ids,
                                         const std::vector<std::vector<int64_t>>& contexts,
                                         const std::vector<std::vector<int64_t>>& native,
                                         const std::vector<int64_t>* accepted);
   // Buffer API: rows read from a CPU token matrix, continuity proven with
   // 64-token head/tail windows; only the delta is copied.
-  std::vector<std::vector<int64_t>> mix_matrix(const std::vector<std::string_view>& ids, const IntVector& counts,
+  const std::vector<std::vector<int64_t>>& mix_matrix(const std::vector<std::string_view>& ids, const IntVector& counts,
                                                const IntMatrix& tokens,
                                                const std::vector<std::vector<int64_t>>& native,
                                                const std::vector<int64_t>* accepted);
@@ -91,7 +92,7 @@ class HybridMixer {
   void validate(const std::vector<std::string_view>& ids, const std::vector<std::vector<int64_t>>& native,
                 const std::vector<int64_t>* accepted);
   template <class Decide>
-  std::vector<std::vector<int64_t>> mix_core(const std::vector<std::string_view>& ids,
+  const std::vector<std::vector<int64_t>>& mix_core(const std::vector<std::string_view>& ids,
                                              const std::vector<std::vector<int64_t>>& native,
                                              const std::vector<int64_t>* accepted, Decide&& decide);
   template <class Decide>
@@ -114,6 +115,10 @@ class HybridMixer {
   uint64_t div_observed_ = 0, div_suffix_published_ = 0, self_hits_ = 0;
   std::vector<int64_t> conditioned_;
   std::vector<Table::iterator> found_;
+  // Per-call scratch kept across calls (no allocation once warm).
+  std::vector<std::vector<int64_t>> result_;
+  std::vector<int64_t> delta_;
+  std::vector<std::pair<size_t, size_t>> hashes_;
 };
 
 }  // namespace sh
