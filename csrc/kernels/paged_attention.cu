@@ -117,9 +117,11 @@ __device__ __forceinline__ uint32_t swz(int r, int cc) {
   return static_cast<uint32_t>((cc >> 3) * (64 * 128) + r * 128 + (((cc & 7) ^ (r & 7)) << 4));
 }
 
-template <int D>
+// K/V page ring depth: as deep as the 227 KB block budget allows (the key-split
+// variants also hold the merge area), so more page bytes are in flight per SM.
+template <int D, int KS>
 struct Stages {
-  static constexpr int value = D == 64 ? 8 : (D == 128 ? 4 : 2);  // K/V page ring depth (fits with the merge area)
+  static constexpr int value = D == 64 ? 8 : (D == 128 ? (KS > 1 ? 5 : 6) : 2);
 };
 
 // Geometry of one work unit, computed identically by the producer and the
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     paged_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnParams p,
                       int ntiles) {
   constexpr int TILE_BYTES = 64 * D * 2;  // one [64][D] bf16 tile
-  constexpr int STAGES = Stages<D>::value;
+  constexpr int STAGES = Stages<D, KS>::value;
   constexpr int KSTEPS = D / 16;
   constexpr int DT = D / 8;
   constexpr int NT = 8 / KS;  // 8-key n-tiles per page per warp
@@ -497,7 +499,7 @@ int cache_map(CUtensorMap* m, const void* base, int64_t rows, int d) {
 
 template <int D, int KS>
 int launch_ks(const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& p, int ntiles, cudaStream_t st) {
-  constexpr int STAGES = Stages<D>::value;
+  constexpr int STAGES = Stages<D, KS>::value;
   constexpr int MERGE = KS > 1 ? 4 * 32 * (D / 8 * 4 + 4) * 4 : 0;
   constexpr int SMEM = 1024 + 64 * D * 2 * (1 + 2 * STAGES) + MERGE + 2 * STAGES * 8 + 16;
   static_assert(SMEM <= 227 * 1024, "paged attention shared-memory budget exceeds 227 KB per block");
