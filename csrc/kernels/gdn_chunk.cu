@@ -19,8 +19,10 @@
 //   MMA7  X += (D^T diag(b_C/b)) . K    -> state             (128 columns)
 // The unit lower-triangular inverse T is done in fp32 on the CUDA cores in
 // 16 x 16 blocks.  The state X in TMEM is pre-scaled by b_C of the chunk
-// before MMA7 accumulates into it, and its bf16 copy (the S0 operand of the
-// next chunk) is written after.  Rows past the request's last token are
+// before MMA7 accumulates into it (in the previous chunk's state pass, with
+// that chunk's gates computed ahead), and its bf16 copy (the S0 operand of the
+// next chunk) is written after.  The next chunk's raw rows are prefetched with
+// cp.async while the output phase runs.  Rows past the request's last token are
 // zero: they add nothing to the state and their outputs are not stored.
 //
 // Roles are phase-sequential (all 256 threads, barriers between phases);
@@ -62,10 +64,14 @@ constexpr int OFF_TF = OFF_LF + 64 * LDF * 4;
 constexpr int OFF_YF = OFF_TF + 64 * LDF * 4;
 constexpr int YF_BYTES = 3 * 16 * 17 * 4;
 constexpr int OFF_Z = ((OFF_YF + YF_BYTES + 1023) / 1024) * 1024;  // z rows of the chunk, bf16 [64][128]
-constexpr int OFF_GAM = OFF_Z + 64 * 256;
-constexpr int OFF_BV = OFF_GAM + 64 * 4;
-constexpr int OFF_BETA = OFF_BV + 64 * 4;
-constexpr int OFF_NW = OFF_BETA + 64 * 4;   // norm weight, fp32 [128]
+constexpr int OFF_GAM = OFF_Z + 64 * 256;   // gates of two chunks: [2][64] each
+constexpr int OFF_BV = OFF_GAM + 2 * 64 * 4;
+constexpr int OFF_BETA = OFF_BV + 2 * 64 * 4;
+constexpr int OFF_NW = OFF_BETA + 2 * 64 * 4;  // norm weight, fp32 [128]
+// Raw k | q | v rows of the next chunk (bf16 [3][64][128], 16-byte chunks swizzled by row), prefetched
+// during the output phase into the B12 / Mq / D^T tiles, which are dead from MMA6/7 until the next MMA5.
+constexpr int OFF_STG = OFF_B12;
+static_assert(OFF_STG + 3 * 64 * 256 <= OFF_A7, "staging fits the dead tiles");
 constexpr int OFF_PART = OFF_NW + 128 * 4;  // per-row partial sums of o^2, [2][64]
 constexpr int OFF_BAR = OFF_PART + 2 * 64 * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 64;
@@ -128,9 +134,9 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
   float* Lf = reinterpret_cast<float*>(sm + OFF_LF);
   float* Tf = reinterpret_cast<float*>(sm + OFF_TF);
   float* Yf = reinterpret_cast<float*>(sm + OFF_YF);
-  float* gam = reinterpret_cast<float*>(sm + OFF_GAM);
-  float* bv = reinterpret_cast<float*>(sm + OFF_BV);
-  float* betav = reinterpret_cast<float*>(sm + OFF_BETA);
+  float* gam_all = reinterpret_cast<float*>(sm + OFF_GAM);
+  float* bv_all = reinterpret_cast<float*>(sm + OFF_BV);
+  float* betav_all = reinterpret_cast<float*>(sm + OFF_BETA);
   float* nw = reinterpret_cast<float*>(sm + OFF_NW);
   float* part = reinterpret_cast<float*>(sm + OFF_PART);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
@@ -184,17 +190,82 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
     return *abort_flag == 0;
   };
 
+  // Gates of chunk ci (one warp, two tokens per lane) and their in-chunk cumulative sum -> buffer ci & 1.
+  auto gates = [&](int ci) {
+    const int c0 = ci * C, n = min(C, ntok - c0), bb = (ci & 1) * 64;
+    float g2[2], be2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = 2 * lane + e;
+      g2[e] = 0.f;
+      be2[e] = 0.f;
+      if (t < n) {
+        const __nv_bfloat16* ba = p.ba + (t0 + c0 + t) * p.ba_stride;
+        const float bq = __bfloat162float(ba[hv]), aa = __bfloat162float(ba[p.HV + hv]);
+        g2[e] = -alog * softplus(aa + dtb);
+        be2[e] = 1.f / (1.f + __expf(-bq));
+      }
+    }
+    float s = g2[0] + g2[1];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    const float g1 = s, g0 = s - g2[1];
+    gam_all[bb + 2 * lane] = g0;
+    gam_all[bb + 2 * lane + 1] = g1;
+    bv_all[bb + 2 * lane] = __expf(g0);
+    bv_all[bb + 2 * lane + 1] = __expf(g1);
+    betav_all[bb + 2 * lane] = be2[0];
+    betav_all[bb + 2 * lane + 1] = be2[1];
+  };
+  // cp.async of chunk ci's raw k / q / v rows into the staging tiles (threads of warps 2, 3, 6, 7: 128
+  // threads, 24 copies each); rows past the request are not loaded (phase 0 zeroes them).
+  auto prefetch_rows = [&](int ci, int idx) {
+    const int c0 = ci * C, n = min(C, ntok - c0);
+    for (int i = idx; i < 3 * 64 * 16; i += 128) {
+      const int kind = i / (64 * 16), t = (i / 16) % 64, ch = i % 16;
+      if (t >= n) continue;
+      const __nv_bfloat16* row = p.qkv + (t0 + c0 + t) * p.qkv_stride +
+                                 (kind == 0 ? p.H * K + h * K : kind == 1 ? h * K : 2 * p.H * K + hv * K);
+      const uint32_t d = sbase + OFF_STG + (kind * 64 + t) * 256 + ((ch ^ (t & 7)) << 4);
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(d), "l"(row + ch * 8));
+    }
+    asm volatile("cp.async.commit_group;");
+  };
+  const bool stager = warp == 2 || warp == 3 || warp == 6 || warp == 7;
+  const int stage_idx = (warp & 1) * 32 + (warp >> 2) * 64 + lane;  // 0..127 over the four staging warps
+  if (nchunks > 0) {
+    if (warp == 4) gates(0);
+    if (stager) {
+      prefetch_rows(0, stage_idx);
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+  }
+  __syncthreads();
+
   for (int ci = 0; ci < nchunks && !failed; ++ci) {
     const int c0 = ci * C;
     const int n = min(C, ntok - c0);
+    const float* gam = gam_all + (ci & 1) * 64;
+    const float* bv = bv_all + (ci & 1) * 64;
+    const float* betav = betav_all + (ci & 1) * 64;
     // ---------------------------------------------------------------- phase 0: stage the chunk
     if (warp < 6) {
       const int t = tid & 63, kind = tid >> 6;  // 0: k, 1: q, 2: v
       const bool valid = t < n;
       uint32_t r[64];
-      if (valid) {
-        const __nv_bfloat16* row = p.qkv + (t0 + c0 + t) * p.qkv_stride;
-        load_row(row + (kind == 0 ? p.H * K + h * K : kind == 1 ? h * K : 2 * p.H * K + hv * K), r);
+      if (valid) {  // the row prefetched into the staging tiles
+        const uint8_t* srow = sm + OFF_STG + (kind * 64 + t) * 256;
+#pragma unroll
+        for (int ch = 0; ch < 16; ++ch) {
+          const uint4 u = *reinterpret_cast<const uint4*>(srow + ((ch ^ (t & 7)) << 4));
+          r[4 * ch] = u.x;
+          r[4 * ch + 1] = u.y;
+          r[4 * ch + 2] = u.z;
+          r[4 * ch + 3] = u.w;
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < 64; ++i) r[i] = 0u;
@@ -227,42 +298,14 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
           st_bf16(sm + OFF_KVT, swz(rbase + 2 * i + 1, t), hi(r[i]) * scale);
         }
       }
-    } else if (warp == 6) {  // gates and their in-chunk cumulative sum (two tokens per lane)
-      float g2[2], be2[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int t = 2 * lane + e;
-        g2[e] = 0.f;
-        be2[e] = 0.f;
-        if (t < n) {
-          const __nv_bfloat16* ba = p.ba + (t0 + c0 + t) * p.ba_stride;
-          const float bb = __bfloat162float(ba[hv]), aa = __bfloat162float(ba[p.HV + hv]);
-          g2[e] = -alog * softplus(aa + dtb);
-          be2[e] = 1.f / (1.f + __expf(-bb));
-        }
-      }
-      float s = g2[0] + g2[1];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, s, o);
-        if (lane >= o) s += y;
-      }
-      const float g1 = s, g0 = s - g2[1];
-      gam[2 * lane] = g0;
-      gam[2 * lane + 1] = g1;
-      bv[2 * lane] = __expf(g0);
-      bv[2 * lane + 1] = __expf(g1);
-      betav[2 * lane] = be2[0];
-      betav[2 * lane + 1] = be2[1];
-    } else {  // warp 7: z rows of the chunk -> shared memory (read by phase 5)
+    } else if (warp == 7) {  // z rows of the chunk -> shared memory (read by phase 5)
       for (int i = lane; i < n * 16; i += 32) {
         const int t = i >> 4, ch = i & 15;
         const __nv_bfloat16* src = p.z + (t0 + c0 + t) * p.z_stride + hv * K + ch * 8;
         const uint32_t d = sbase + OFF_Z + t * 256 + ((ch ^ (t & 7)) << 4);  // swizzled: conflict-free row reads
         asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src));
       }
-      asm volatile("cp.async.commit_group;");
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      asm volatile("cp.async.commit_group;");  // waited for in phase 5
     }
     fence_proxy();
     fence_before();
@@ -281,7 +324,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
       failed = true;
       break;
     }
-    const float gC = gam[63], bC = bv[63];
+    const float gC = gam[63];
     // ---------------------------------------------------------------- phase 1
     if (warp < 2) {  // L = beta_t e^{g_t-g_j} G (j < t) into fp32 shared memory
       const int t = 32 * quarter + lane;
@@ -311,16 +354,6 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
         st_chunk(sm + OFF_MQ, swz(t, c), v);
         st_chunk(sm + OFF_MQ, swz(t, c + 8), v + 8);
       }
-    } else if (ci > 0) {  // warps 4-7: X <- b_C X (the S_C = b_C S0 + ... term)
-#pragma unroll 1
-      for (int c = 0; c < 128; c += 16) {
-        float v[16];
-        tmem_ld16(tmem + TM_X + lane_off + c, v);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] *= bC;
-        tmem_st16(tmem + TM_X + lane_off + c, v);
-      }
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
     fence_proxy();
     fence_before();
@@ -422,6 +455,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
       break;
     }
     // ---------------------------------------------------------------- phase 4: D = U - W S0^T, transposed
+    if (warp == 4 && ci + 1 < nchunks) gates(ci + 1);  // the next chunk's gates (b_C pre-scales the state)
     if (quarter >= 2 && (warp == quarter || warp == quarter + 4)) {
       const int t = 32 * quarter + lane - 64, half = warp >> 2;  // half: v 0-63 or 64-127
       const float sc = __expf(gC - gam[t]);
@@ -460,6 +494,10 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
       break;
     }
     // ---------------------------------------------------------------- phase 5
+    // The staging tiles are dead now: fetch the next chunk's rows behind this phase (warp 7 first
+    // completes its z copies of this chunk).
+    if (warp == 7) asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (stager && ci + 1 < nchunks) prefetch_rows(ci + 1, stage_idx);
     // O = b_t Q S0^T + Mq D with the gated RMSNorm: rows t = TMEM lanes 0-63 (warps 0, 1, 4, 5; each
     // warp owns 64 of the 128 columns).  Every lane runs the warp-collective TMEM loads; rows t < n are stored.
     const int half = warp >> 2;
@@ -515,10 +553,12 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
         }
       }
     }
-    {  // state rows v = TMEM lanes (all warps, 64 columns each): bf16 S0 of the next chunk; fp32 to
-       // global after the last chunk
+    {  // state rows v = TMEM lanes (all warps, 64 columns each): bf16 S0 of the next chunk and the state
+       // pre-scaled by the next chunk's total decay b_C (the S_C = b_C S0 + ... term); fp32 to global after
+       // the last chunk
       const int v = 32 * quarter + lane;
       const bool last = ci == nchunks - 1;
+      const float bnext = last ? 1.f : bv_all[((ci + 1) & 1) * 64 + 63];
       float* srow = p.state + ((slot * p.HV + hv) * K + v) * K;
 #pragma unroll 1
       for (int c = 64 * half; c < 64 * half + 64; c += 16) {
@@ -530,9 +570,15 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(GdnParams p) {
 #pragma unroll
           for (int e = 0; e < 16; e += 4)
             *reinterpret_cast<float4*>(srow + c + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) x[e] *= bnext;
+          tmem_st16(tmem + TM_X + lane_off + c, x);
         }
       }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
+    if (stager) asm volatile("cp.async.wait_group 0;" ::: "memory");  // the next chunk's rows have landed
     fence_proxy();
     fence_before();
     __syncthreads();
