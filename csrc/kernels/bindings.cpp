@@ -377,6 +377,32 @@ void gemm_nvfp4(torch::Tensor y, torch::Tensor x, torch::Tensor packed, torch::T
 
 // NVFP4 activation quantiser (see sh_nvfp4_quant_act): x bf16 [rows, K] ->
 // xq uint8 [rows, K/2], x_sf uint8 [tiles, kc4, 512], a_scale fp32 [rows].
+void nvfp4_gather_act(torch::Tensor codes, torch::Tensor scales, torch::Tensor ascale, torch::Tensor token,
+                      torch::Tensor groups, torch::Tensor num_groups, torch::Tensor xq, torch::Tensor x_sf,
+                      torch::Tensor a_scale) {
+  TORCH_CHECK(codes.is_cuda() && codes.scalar_type() == at::kByte && codes.is_contiguous() && codes.dim() == 2,
+              "nvfp4_gather_act: codes uint8 [rows, K/2]");
+  const int64_t K = codes.size(1) * 2, rows = token.numel();
+  TORCH_CHECK(scales.scalar_type() == at::kByte && scales.is_contiguous() && scales.size(1) * 16 == K &&
+                  scales.size(0) == codes.size(0), "nvfp4_gather_act: scales uint8 [rows, K/16]");
+  TORCH_CHECK(ascale.scalar_type() == at::kFloat && ascale.numel() >= codes.size(0), "nvfp4_gather_act: ascale");
+  TORCH_CHECK(token.scalar_type() == at::kInt && token.is_contiguous(), "nvfp4_gather_act: token int32");
+  TORCH_CHECK(groups.scalar_type() == at::kInt && groups.size(1) == 4 && num_groups.scalar_type() == at::kInt,
+              "nvfp4_gather_act: groups");
+  TORCH_CHECK(xq.scalar_type() == at::kByte && xq.is_contiguous() && xq.size(0) >= rows && xq.size(1) * 2 == K,
+              "nvfp4_gather_act: xq uint8 [pairs, K/2]");
+  const int64_t kc4 = (K + 255) / 256 * 4;
+  TORCH_CHECK(x_sf.element_size() == 1 && x_sf.is_contiguous() && x_sf.size(1) == kc4 && x_sf.size(2) == 512 &&
+                  x_sf.size(0) >= groups.size(0), "nvfp4_gather_act: x_sf [tiles, kc4, 512]");
+  TORCH_CHECK(a_scale.scalar_type() == at::kFloat && a_scale.numel() >= rows, "nvfp4_gather_act: a_scale");
+  const int r = sh_nvfp4_gather_act(codes.data_ptr<uint8_t>(), scales.data_ptr<uint8_t>(), ascale.data_ptr<float>(),
+                                    token.data_ptr<int>(), static_cast<int>(rows), static_cast<int>(K),
+                                    reinterpret_cast<const int4*>(groups.data_ptr<int>()), num_groups.data_ptr<int>(),
+                                    xq.data_ptr<uint8_t>(), reinterpret_cast<uint8_t*>(x_sf.data_ptr()),
+                                    a_scale.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_nvfp4_gather_act failed with code ", r);
+}
+
 void nvfp4_quant_act(torch::Tensor x, torch::Tensor xq, torch::Tensor x_sf, torch::Tensor a_scale, int64_t tile_rows,
                      double static_g, c10::optional<torch::Tensor> groups, c10::optional<torch::Tensor> num_groups,
                      bool swiglu) {
@@ -596,7 +622,8 @@ static EpParams ep_params(torch::Tensor ids, std::vector<int64_t> peer_x, std::v
 void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor w, std::vector<int64_t> peer_x,
                  std::vector<int64_t> peer_ids, std::vector<int64_t> peer_w, std::vector<int64_t> peer_y,
                  std::vector<int64_t> peer_flags, torch::Tensor counters, torch::Tensor err, int64_t rank,
-                 int64_t e_local, int64_t max_T, int64_t num_blocks) {
+                 int64_t e_local, int64_t max_T, int64_t num_blocks, std::vector<int64_t> peer_q,
+                 std::vector<int64_t> peer_s, std::vector<int64_t> peer_a) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.size(0) == ids.size(0),
               "ep_dispatch: x");
   TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.sizes() == ids.sizes(), "ep_dispatch: w");
@@ -604,6 +631,16 @@ void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor w, std::vecto
                          max_T);
   p.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   p.w = w.data_ptr<float>();
+  if (!peer_q.empty()) {  // NVFP4 dispatch
+    TORCH_CHECK(peer_q.size() == peer_x.size() && peer_s.size() == peer_x.size() && peer_a.size() == peer_x.size(),
+                "ep_dispatch: quantised peer lists");
+    p.quant = 1;
+    for (size_t i = 0; i < peer_q.size(); ++i) {
+      p.peer_q[i] = reinterpret_cast<uint8_t*>(peer_q[i]);
+      p.peer_s[i] = reinterpret_cast<uint8_t*>(peer_s[i]);
+      p.peer_a[i] = reinterpret_cast<float*>(peer_a[i]);
+    }
+  }
   SH_CHECK_RC(sh_ep_dispatch(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream()), "sh_ep_dispatch");
 }
 
@@ -775,6 +812,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_nvfp4", &gemm_nvfp4, py::arg("y"), py::arg("x"), py::arg("packed"), py::arg("scales"),
         py::arg("gscale"), py::arg("bn"), py::arg("groups") = py::none(), py::arg("num_groups") = py::none(),
         py::arg("rows_p") = 0, py::arg("err") = py::none(), py::arg("splits") = 1, py::arg("ws") = py::none());
+  m.def("nvfp4_gather_act", &nvfp4_gather_act);
   m.def("nvfp4_quant_act", &nvfp4_quant_act, py::arg("x"), py::arg("xq"), py::arg("x_sf"), py::arg("a_scale"),
         py::arg("tile_rows"), py::arg("static_g") = 0.0, py::arg("groups") = py::none(),
         py::arg("num_groups") = py::none(), py::arg("swiglu") = false);

@@ -7,7 +7,10 @@
 // dispatch (rank r, block b, tokens i = b, b + nblocks, ...):
 //   for every rank d: route row (local expert id or -1, weight or 0) ->
 //   d.ids / d.w [r*T + i]; for the ranks d hosting one of the token's experts:
-//   x[i] -> d.x[r*T + i]; then a cross-rank barrier between same-index blocks.
+//   x[i] -> d.x[r*T + i] (bf16), or with quant the row quantised once to
+//   NVFP4 -> d.q / d.s / d.a [r*T + i] (3.55x fewer bytes; the receiving W4A4
+//   expert GEMMs gather these codes directly); then a cross-rank barrier
+//   between same-index blocks.
 //   When the kernel finishes on d, every rank's rows have landed in d's buffers.
 // experts: the grouped expert GEMMs of this rank over the [world*T, H] rows
 //   (rows routed elsewhere have only -1 ids and are skipped).
@@ -32,10 +35,13 @@
 #include <stdint.h>
 
 #include "ep_a2a.h"
+#include "nvfp4_act.cuh"
 #include "pdl.cuh"
 
 namespace shk {
 namespace ep {
+
+using namespace shk::nvq;
 
 constexpr uint64_t kTimeoutNs = 5000000000ull;  // 5 s
 constexpr int kThreads = 512;
@@ -86,6 +92,45 @@ __device__ __forceinline__ uint32_t dest_mask(const EpParams& p, int64_t i) {
   return m;
 }
 
+// Quantises token row i to NVFP4 in shared memory (codes then scales) and
+// stores it into every destination rank's receive rows with 16-byte stores.
+__device__ void quant_send(const EpParams& p, int64_t i, int64_t row, uint32_t m) {
+  extern __shared__ __align__(16) uint8_t qsm[];  // [H/2 codes][H/16 scales]
+  __shared__ float red[kThreads / 32];
+  const int nblk = p.H / 16;
+  const __nv_bfloat16* xr = p.x + i * p.H;
+  float amax = 0.f;
+  for (int b = threadIdx.x; b < nblk; b += kThreads) {
+    float v[16];
+    load16(xr + b * 16, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __syncthreads();  // the previous row's stores read qsm
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = 0.f;
+  for (int w = 0; w < kThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+  const float g = row_g(amax), g6 = __fdiv_rn(g, 6.f);
+  for (int b = threadIdx.x; b < nblk; b += kThreads) {
+    float v[16];
+    load16(xr + b * 16, v);
+    qsm[p.H / 2 + b] = quant16(v, g, g6, qsm + b * 8);
+  }
+  __syncthreads();
+  const int nq = p.H / 32, ns = p.H / 256;  // 16-byte chunks of codes and of scales
+  for (int d = 0; d < p.world; ++d) {
+    if (!((m >> d) & 1u)) continue;
+    uint4* dq = reinterpret_cast<uint4*>(p.peer_q[d] + row * (p.H / 2));
+    uint4* ds = reinterpret_cast<uint4*>(p.peer_s[d] + row * (p.H / 16));
+    for (int v = threadIdx.x; v < nq; v += kThreads) dq[v] = reinterpret_cast<const uint4*>(qsm)[v];
+    for (int v = threadIdx.x; v < ns; v += kThreads) ds[v] = reinterpret_cast<const uint4*>(qsm + p.H / 2)[v];
+    if (threadIdx.x == 0) p.peer_a[d][row] = __fdiv_rn(1.f, g);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(EpParams p) {
   shk::pdl_trigger();
   shk::pdl_wait();
@@ -109,6 +154,10 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(EpParams p) {
       p.peer_w[d][row * p.k + j] = mine ? p.w[i * p.k + j] : 0.f;
     }
     const uint32_t m = dest_mask(p, i);
+    if (p.quant) {
+      quant_send(p, i, row, m);
+      continue;
+    }
     const uint4* src = reinterpret_cast<const uint4*>(p.x + i * p.H);
     for (int d = 0; d < p.world; ++d) {
       if (!((m >> d) & 1u)) continue;
@@ -180,6 +229,7 @@ using namespace shk::ep;
 static int ep_check(const EpParams& p) {
   if (p.world < 1 || p.world > SH_EP_MAX_WORLD || p.H % 8 != 0 || p.T < 0 || p.T > p.max_T) return -1;
   if (p.k < 1 || p.k > SH_EP_MAX_K || p.world * p.k > kThreads || p.e_local < 1) return -2;
+  if (p.quant && (p.H % 256 != 0 || p.H / 2 + p.H / 16 > 48 * 1024)) return -3;  // 16-byte scale rows
   return 0;
 }
 
@@ -188,7 +238,8 @@ extern "C" int sh_ep_dispatch(const EpParams* params, int num_blocks, cudaStream
   if (rc) return rc;
   if (params->T == 0) return 0;
   num_blocks = num_blocks < 1 ? 1 : (num_blocks > SH_EP_MAX_BLOCKS ? SH_EP_MAX_BLOCKS : num_blocks);
-  shk::launch(ep_dispatch_kernel, dim3(num_blocks), dim3(kThreads), 0, stream, *params);
+  const size_t smem = params->quant ? static_cast<size_t>(params->H / 2 + params->H / 16) : 0;
+  shk::launch(ep_dispatch_kernel, dim3(num_blocks), dim3(kThreads), smem, stream, *params);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -26,6 +26,12 @@ struct EpParams {
   uint32_t* counters;                      // [SH_EP_MAX_BLOCKS] local epochs (dispatch advances them)
   int* err;                                // nonzero after a timed-out wait
   int rank, world, T, H, k, e_local, max_T;
+  // quant = 1: the dispatch quantises each row to NVFP4 once (per-row g = 2688 / amax, e4m3 scale per 16,
+  // e2m1 codes: the activation quantiser's math) and sends codes, scales and 1 / g instead of bf16 rows.
+  int quant;
+  uint8_t* peer_q[SH_EP_MAX_WORLD];  // per rank: [world*max_T][H/2] e2m1 codes
+  uint8_t* peer_s[SH_EP_MAX_WORLD];  // per rank: [world*max_T][H/16] e4m3 scales
+  float* peer_a[SH_EP_MAX_WORLD];    // per rank: [world*max_T] 1 / g
 };
 
 #ifdef __cplusplus

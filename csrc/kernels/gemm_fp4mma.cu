@@ -31,12 +31,14 @@
 #include <stdint.h>
 
 #include "gemm_fp4mma.h"
+#include "nvfp4_act.cuh"
 #include "pdl.cuh"
 #include "tcgen05_common.cuh"
 
 namespace shk {
 namespace fp4mma {
 using namespace shk::tc;
+using namespace shk::nvq;
 
 constexpr int BM = 128;
 constexpr int KB = 256;         // NVFP4: k elements per pipeline stage (128 bytes per row)
@@ -466,38 +468,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ---------------------------------------------------------------- activation quantiser
-// Eight values -> eight e2m1 codes (round to nearest even, saturating at 6; the
-// sign bit is kept for negative values that round to zero), element 2i in the
-// low nibble of byte i.
-__device__ __forceinline__ uint32_t e2m1x8(const float* v) {
-  uint32_t out;
-  asm("{\n .reg .b8 b0, b1, b2, b3;\n"
-      " cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
-      " cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
-      " cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
-      " cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
-      " mov.b32 %0, {b0, b1, b2, b3};\n}"
-      : "=r"(out)
-      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
-  return out;
-}
-
-__device__ __forceinline__ void load16(const __nv_bfloat16* p, float* v) {
-  const uint4 u0 = *reinterpret_cast<const uint4*>(p);
-  const uint4 u1 = *reinterpret_cast<const uint4*>(p + 8);
-  const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
-  const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 a = __bfloat1622float2(h0[j]);
-    const float2 c = __bfloat1622float2(h1[j]);
-    v[2 * j] = a.x;
-    v[2 * j + 1] = a.y;
-    v[8 + 2 * j] = c.x;
-    v[8 + 2 * j + 1] = c.y;
-  }
-}
-
 constexpr int QUANT_THREADS = 512;
 
 // Block b (16 values) of an activation row.  SWIGLU: the row is a fused
@@ -563,7 +533,7 @@ __global__ void __launch_bounds__(QUANT_THREADS) quant_act_kernel(
     __syncthreads();
     amax = 0.f;
     for (int i = 0; i < static_cast<int>((blockDim.x + 31) >> 5); ++i) amax = fmaxf(amax, red[i]);
-    g = amax > 0.f ? __fdiv_rn(2688.f, amax) : 1.f;
+    g = row_g(amax);
   }
   const float g6 = __fdiv_rn(g, 6.f);
   if (threadIdx.x == 0) a_scale[r] = __fdiv_rn(1.f, g);
@@ -574,19 +544,46 @@ __global__ void __launch_bounds__(QUANT_THREADS) quant_act_kernel(
     if (b < nblk) {
       float v[16];
       load_act<SWIGLU>(xr, K, b, v);
-      float am = 0.f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) am = fmaxf(am, fabsf(v[j]));
-      const __nv_fp8_e4m3 s(fminf(am * g6, 448.f));  // round to nearest even, saturating
-      s8 = s.__x;
-      const float sfv = static_cast<float>(s);
-      const float inv = sfv > 0.f ? __fdiv_rn(g, sfv) : 0.f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] *= inv;
-      *reinterpret_cast<uint2*>(q + b * 8) = make_uint2(e2m1x8(v), e2m1x8(v + 8));
+      s8 = quant16(v, g, g6, q + b * 8);
     }
     sf[(b >> 2) * SF_CHUNK + (b & 3)] = s8;
   }
+}
+
+// Rows already quantised to NVFP4 in the linear layout (codes [rows][K/2],
+// e4m3 scales [rows][K/16], a_scale [rows], as the quantising expert-parallel
+// dispatch sends them) gathered into the grouped W4A4 GEMM's operand layout:
+// row r of group entry e takes source row token[r]; its scales land in the
+// entry's scale tile exactly where quant_act_kernel puts them.
+__global__ void __launch_bounds__(256) gather_nvfp4_kernel(const uint8_t* __restrict__ codes,
+                                                           const uint8_t* __restrict__ scales,
+                                                           const float* __restrict__ ascale,
+                                                           const int* __restrict__ token, int K,
+                                                           const int4* __restrict__ groups,
+                                                           const int* __restrict__ num_groups, uint8_t* __restrict__ xq,
+                                                           uint8_t* __restrict__ x_sf, float* __restrict__ a_scale) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  const int r = blockIdx.x;
+  int lo = 0, hi = *num_groups - 1;
+  if (hi < 0) return;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (groups[mid].x <= r) lo = mid;
+    else hi = mid - 1;
+  }
+  const int4 e = groups[lo];
+  if (r < e.x || r >= e.x + e.y) return;
+  const int slot = r - e.x;
+  const int64_t src = token[r];
+  const uint4* s4 = reinterpret_cast<const uint4*>(codes + src * (K / 2));
+  uint4* d4 = reinterpret_cast<uint4*>(xq + static_cast<int64_t>(r) * (K / 2));
+  for (int i = threadIdx.x; i < K / 32; i += blockDim.x) d4[i] = s4[i];
+  if (threadIdx.x == 0) a_scale[r] = ascale[src];
+  const int nblk = K / 16, kc4 = ((K + KB - 1) / KB) * 4;
+  uint8_t* sf = x_sf + static_cast<int64_t>(lo) * kc4 * SF_CHUNK + (slot & 31) * 16 + ((slot >> 5) & 3) * 4;
+  const uint8_t* ss = scales + src * nblk;
+  for (int b = threadIdx.x; b < kc4 * 4; b += blockDim.x) sf[(b >> 2) * SF_CHUNK + (b & 3)] = b < nblk ? ss[b] : 0;
 }
 
 // MXFP8 activations: per 32 values s = 2^e (ue8m0 byte e + 127) with e the smallest exponent that keeps
@@ -716,6 +713,17 @@ extern "C" int sh_nvfp4_quant_act(const void* x, int64_t ldx, int rows, int K, c
   shk::launch(swiglu ? quant_act_kernel<true> : quant_act_kernel<false>, dim3(rows), dim3(threads), 0, stream,
               static_cast<const __nv_bfloat16*>(x), ldx, rows, K, groups, num_groups, tile_rows, static_g, xq, x_sf,
               a_scale);
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int sh_nvfp4_gather_act(const uint8_t* codes, const uint8_t* scales, const float* ascale, const int* token,
+                                   int rows, int K, const int4* groups, const int* num_groups, uint8_t* xq,
+                                   uint8_t* x_sf, float* a_scale, cudaStream_t stream) {
+  if (K % 64 != 0 || K <= 0 || !groups || !num_groups) return -2;
+  if ((reinterpret_cast<uintptr_t>(codes) & 15) || (reinterpret_cast<uintptr_t>(xq) & 15)) return -3;
+  if (rows <= 0) return 0;
+  shk::launch(gather_nvfp4_kernel, dim3(rows), dim3(256), 0, stream, codes, scales, ascale, token, K, groups,
+              num_groups, xq, x_sf, a_scale);
   return static_cast<int>(cudaGetLastError());
 }
 

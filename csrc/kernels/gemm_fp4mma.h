@@ -49,6 +49,11 @@ extern "C" {
 int sh_nvfp4_quant_act(const void* x, int64_t ldx, int rows, int K, const int4* groups, const int* num_groups,
                        int max_tiles, int tile_rows, float static_g, uint8_t* xq, uint8_t* x_sf, float* a_scale,
                        int swiglu, cudaStream_t stream);
+// Pre-quantised NVFP4 rows (codes [*, K/2], e4m3 scales [*, K/16], a_scale [*]) gathered by token[r] into
+// the grouped operand layout of rows [0, rows) (the layout sh_nvfp4_quant_act writes with groups).
+int sh_nvfp4_gather_act(const uint8_t* codes, const uint8_t* scales, const float* ascale, const int* token, int rows,
+                        int K, const int4* groups, const int* num_groups, uint8_t* xq, uint8_t* x_sf, float* a_scale,
+                        cudaStream_t stream);
 // out[t, n] = alpha_w * a_scale[t] * sum_k e2m1(xq[t, k]) sx(t, k) e2m1(w[n, k]) sw(n, k); bn in {64, 128}.
 // splits > 1 (dense mode) needs ws (splits * tiles_p * tiles_q * 128 * bn floats) and zeroed counters.
 int sh_gemm_fp4mma(Fp4MmaParams* g, const void* xq, int rows_q, int bn, int splits, int num_sms,

@@ -104,11 +104,41 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             ref = _reference(x, ids, w, w13_all, w2_all, F)
             results[f"graph{rep}"] = ((og.float().cpu() - ref).abs().max().item() / ref.abs().max().item(), 0.0)
+        del graph
+        # NVFP4 (W4A4) experts: the quantising dispatch must reproduce the bf16 dispatch bit for bit (the rows
+        # are quantised once by the dispatch instead of by the receiver, with the same math).
+        from vllm_suffix_hybrid_b200.ops import reference as ref
+
+        def quant(wt, rows):
+            ps, ss, gs = [], [], []
+            for e in range(e_local):
+                gsc = ref.nvfp4_global_scale(wt[e * rows:(e + 1) * rows])
+                pk, sc = ref.nvfp4_quantize(wt[e * rows:(e + 1) * rows], gsc)
+                ps.append(pk), ss.append(sc), gs.append(gsc.reshape(1).float())
+            return tuple(t.cuda() for t in (torch.cat(ps), torch.cat(ss), torch.cat(gs)))
+
+        H4 = 256
+        w13_4 = (torch.randn(E * 2 * F, H4, generator=g) * 0.05).to(torch.bfloat16)
+        w2_4 = (torch.randn(E * H4, F, generator=g) * 0.05).to(torch.bfloat16)
+        moe4 = _Moe(None, None, e_local, F)
+        moe4.fp4 = (quant(w13_4[e0 * 2 * F:(e0 + e_local) * 2 * F], 2 * F), quant(w2_4[e0 * H4:(e0 + e_local) * H4], H4))
+        for call, T in enumerate([21, 3, 40]):
+            gi = torch.Generator().manual_seed(300 + 10 * call + rank)
+            x = torch.randn(T, H4, generator=gi).to(torch.bfloat16).cuda()
+            ids = torch.stack([torch.randperm(E, generator=gi)[:k] for _ in range(T)]).to(torch.int32).cuda()
+            w = torch.rand(T, k, generator=gi).cuda()
+            os.environ["SH_EP_A2A_FP4"] = "1"
+            got = ep.dp_dispatch_combine(moe4, x, ids, w)
+            os.environ["SH_EP_A2A_FP4"] = "0"
+            base = ep.dp_dispatch_combine(moe4, x, ids, w)
+            torch.cuda.synchronize()
+            results[f"fp4:{call}:T{T}"] = (0.0 if torch.equal(got, base) else 1.0, 0.0)
+        os.environ["SH_EP_A2A_FP4"] = "1"
         from vllm_suffix_hybrid_b200.parallel import ep_a2a
 
+        assert any(c.quant for c in ep_a2a._comms.values())
         for c in ep_a2a._comms.values():
             c.check()
-        del graph
         q.put((rank, results))
     finally:
         torch.cuda.synchronize()

@@ -135,6 +135,27 @@ def test_quant_act_swiglu_fusion_equals_silu_mul_then_quant(rows, F, tile):
     assert torch.equal(_deswizzle(f_sf, rows, tile, F // 16), _deswizzle(x_sf, rows, tile, F // 16))
 
 
+def test_gather_of_prequantised_rows_equals_quantising_the_gathered_rows():
+    """Rows quantised once (the NVFP4 expert-parallel dispatch's linear layout) and gathered into the grouped
+    W4A4 operand must equal quantising the gathered bf16 rows: codes, scale tiles and token scales."""
+    torch.manual_seed(9)
+    R, K = 50, 1024
+    x = (torch.randn(R, K) * 2).to(torch.bfloat16)
+    x[3] = 0  # a zero row
+    codes, scales, ascale = ref.nvfp4_quant_act(x)
+    groups = torch.tensor([[0, 40, 0, 0], [40, 30, 0, 0], [70, 37, 0, 0]], dtype=torch.int32).cuda()
+    ngroups = torch.tensor([3], dtype=torch.int32).cuda()
+    pairs = 107
+    token = torch.randint(0, R, (pairs,), dtype=torch.int32)
+    xq_r, sf_r, a_r = [t.clone() for t in ops.nvfp4_quant_act(x.cuda()[token.long().cuda()], 64, 0.0, groups,
+                                                               ngroups)]
+    xq, sf, a = ops.nvfp4_gather_act(codes.cuda(), scales.cuda(), ascale.float().cuda(), token.cuda(), groups, ngroups)
+    torch.cuda.synchronize()
+    assert torch.equal(xq[:pairs], xq_r[:pairs])
+    assert torch.equal(a[:pairs], a_r[:pairs])
+    assert torch.equal(sf[:3], sf_r[:3])
+
+
 def test_scale_tiles_match_the_swizzled_layout():
     """nvfp4_scale_tiles == the 128x4 layout byte (row/128)*kb_pad*128 + (kb/4)*512 + (row%32)*16 +
     ((row/32)%4)*4 + kb%4 for K a multiple of 256 (reference: kernels/nvfp4_gemm.py sf_offset)."""

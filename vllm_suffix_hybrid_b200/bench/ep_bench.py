@@ -8,6 +8,7 @@ CUDA events; the per-call time is the max over ranks.  Exchange only (the expert
 both paths and are replaced by a copy of the received rows):
   a2a  : ep_dispatch (rows only to the ranks hosting one of the token's experts, route rows to all)
          + ep_combine (expert outputs back to the owner, summed in rank order);
+  a2a_fp4: the same with the rows quantised to NVFP4 inside the dispatch (the W4A4 expert path);
   nccl : all-gather of x, ids, weights + reduce-scatter of the [N*T, H] partials (the path with
          SH_EP_A2A=0).
 Roofline of the a2a: the bytes this rank sends over NVLink (rows to remote expert ranks in the
@@ -53,6 +54,12 @@ def main():
             xs, ids_l, w_l = comm.dispatch(x, ids, w)
             return comm.combine(xs, ids)  # the received rows stand in for the expert outputs
 
+        comm_q = ep_a2a.get(H, ep.A2A_MAX_TOKENS, k, e_local, True) if H % 256 == 0 else None
+
+        def a2a_fp4():  # NVFP4 rows (the W4A4 expert path); bf16 expert outputs come back
+            comm_q.dispatch(x, ids, w)
+            return comm_q.combine(comm_q.x_buf[: W * T * H].view(W * T, H), ids)
+
         def nccl():
             xs = ep._all_gather(x)
             ids_a = ep._all_gather(ids)
@@ -60,7 +67,8 @@ def main():
             return ep._reduce_scatter(xs)
 
         res = {}
-        for name, fn in (("a2a", a2a), ("nccl", nccl)):
+        paths = [("a2a", a2a), ("nccl", nccl)] + ([("a2a_fp4", a2a_fp4)] if comm_q is not None else [])
+        for name, fn in paths:
             for _ in range(3):
                 fn()
             torch.cuda.synchronize()
@@ -86,6 +94,8 @@ def main():
             res[name] = t.item()
             del graph
         comm.check()
+        if comm_q is not None:
+            comm_q.check()
         # bytes this rank sends over NVLink in the a2a (dispatch rows to remote expert ranks + returned rows)
         dests = torch.zeros(T, W, dtype=torch.bool, device=dev)
         dests.scatter_(1, (ids.long() // e_local), True)
@@ -94,6 +104,7 @@ def main():
         dist.all_reduce(sent, op=dist.ReduceOp.MAX)
         link_us = 2 * sent.item() / (LINK_GBS * 1e3)  # dispatch + combine, per direction
         rows.append({"T_per_rank": T, "a2a_us": round(res["a2a"], 2), "nccl_us": round(res["nccl"], 2),
+                     "a2a_fp4_dispatch_us": round(res.get("a2a_fp4", 0.0), 2),
                      "speedup": round(res["nccl"] / res["a2a"], 2), "link_bound_us": round(link_us, 2),
                      "frac_of_link_roofline": round(link_us / res["a2a"], 3)})
     if rank == 0:

@@ -644,6 +644,17 @@ def nvfp4_quant_act(x: torch.Tensor, tile_rows: int, static_g: float = 0.0, grou
     return xq, x_sf, a_scale
 
 
+def nvfp4_gather_act(codes: torch.Tensor, scales: torch.Tensor, ascale: torch.Tensor, token: torch.Tensor,
+                     groups: torch.Tensor, num_groups: torch.Tensor):
+    """(xq, x_sf tiles, a_scale) of the grouped W4A4 operand built from rows already quantised to NVFP4
+    (codes [R, K/2], e4m3 scales [R, K/16], a_scale [R]; reference.nvfp4_quant_act's layout): row r takes
+    source row token[r].  Equal to nvfp4_quant_act of the gathered bf16 rows."""
+    pairs, K = token.numel(), codes.shape[1] * 2
+    xq, x_sf, a_scale = _fp4_act_buffers(codes.device, pairs, K, groups.shape[0])
+    native().nvfp4_gather_act(codes, scales, ascale, token, groups, num_groups, xq, x_sf, a_scale)
+    return xq, x_sf, a_scale
+
+
 def nvfp4_linear_w4a4(x: torch.Tensor, packed: torch.Tensor, w_sf: torch.Tensor, scales: torch.Tensor,
                       global_scale: torch.Tensor, static_g: float = 0.0, out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x W^T with NVFP4 W and per-token NVFP4-quantised x (block-scaled tcgen05 MMA on CUDA; the fp32
@@ -844,28 +855,35 @@ def moe_experts_mxfp8(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
     xq, x_sf, a_sc = mxfp8_quant_act(a, bn, groups, ngroups)
     C.gemm_fp4mma(ys, xq, x_sf, a_sc, w2q[0], t2, ones, bn, groups2, ngroups, H, fp8=True)
     if out is None:
-        out = torch.empty(T, H, dtype=x.dtype, device=dev)
+        out = torch.empty(T, H, dtype=dt, device=dev)
     C.moe_combine(out, ys, sorted_pos, weights, False)
     return out
 
 
-def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
+def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None, prequant=None):
     """moe_experts with NVFP4 expert weights: w13q = (packed [E*2F, H/2], scales [E*2F, H/16], global [E],
     optional k-block-major scales, optional block-scaled MMA scale tiles), w2q likewise for [E*H, F].
     The grouped GEMMs run the block-scaled W4A4 tcgen05 kernel on per-token NVFP4 activations (or the
     W4A16 kernel with SH_NVFP4_ACT=bf16), each expert's rows scaled by its global scale.  On CPU the
-    W4A4 mode quantises the activations like the kernel and multiplies dequantised values in fp32."""
-    T, H = x.shape
-    if not x.is_cuda and nvfp4_act_mode() == "fp4":
+    W4A4 mode quantises the activations like the kernel and multiplies dequantised values in fp32.
+    prequant = (codes [T, H/2], scales [T, H/16], a_scale [T]): the rows arrive already quantised (the
+    quantising expert-parallel dispatch); x is then unused (W4A4 on CUDA only)."""
+    if prequant is not None:
+        if not ids.is_cuda or nvfp4_act_mode() != "fp4":
+            raise ValueError("pre-quantised expert input needs the CUDA W4A4 path")
+        T, H = ids.shape[0], prequant[0].shape[1] * 2
+    else:
+        T, H = x.shape
+    if prequant is None and not x.is_cuda and nvfp4_act_mode() == "fp4":
         return _moe_w4a4_cpu(x, ids, weights, w13q, w2q, E, F, out)
-    if not x.is_cuda:
+    if prequant is None and not x.is_cuda:
         w13 = torch.cat([ref.nvfp4_dequantize(w13q[0][e * 2 * F:(e + 1) * 2 * F], w13q[1][e * 2 * F:(e + 1) * 2 * F],
                                               w13q[2][e:e + 1]) for e in range(E)]).to(x.dtype)
         w2 = torch.cat([ref.nvfp4_dequantize(w2q[0][e * H:(e + 1) * H], w2q[1][e * H:(e + 1) * H], w2q[2][e:e + 1])
                         for e in range(E)]).to(x.dtype)
         return moe_experts(x, ids, weights, w13, w2, E, F, out=out)
     k = ids.shape[1]
-    dev = x.device
+    dev = ids.device
     pairs = T * k
     bn = 64 if pairs <= E * 64 else 128
     max_groups = E + pairs // bn + 1
@@ -877,17 +895,22 @@ def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
     groups = torch.empty(max_groups, 4, dtype=torch.int32, device=dev)
     ngroups = torch.empty(1, dtype=torch.int32, device=dev)
     C.moe_align(ids, rank, offsets, sorted_pos, sorted_token, groups, ngroups, E, bn, 2 * F)
-    xs = torch.empty(pairs, H, dtype=x.dtype, device=dev)
-    C.moe_gather(xs, x, sorted_token, offsets[E:])
-    gu = torch.empty(pairs, 2 * F, dtype=x.dtype, device=dev)
+    dt = torch.bfloat16
+    if prequant is None:
+        xs = torch.empty(pairs, H, dtype=dt, device=dev)
+        C.moe_gather(xs, x, sorted_token, offsets[E:])
+    gu = torch.empty(pairs, 2 * F, dtype=dt, device=dev)
     groups2 = groups.clone()
     groups2[:, 2] = groups[:, 3] * H
-    ys = torch.empty(pairs, H, dtype=x.dtype, device=dev)
+    ys = torch.empty(pairs, H, dtype=dt, device=dev)
     if nvfp4_act_mode() == "fp4":
         # W4A4: each group entry's activation rows are quantised into the entry's own scale tile
         t13 = w13q[4] if len(w13q) > 4 else nvfp4_scale_tiles(w13q[1], 2 * F)
         t2 = w2q[4] if len(w2q) > 4 else nvfp4_scale_tiles(w2q[1], H)
-        xq, x_sf, a_sc = nvfp4_quant_act(xs, bn, 0.0, groups, ngroups)
+        if prequant is not None:
+            xq, x_sf, a_sc = nvfp4_gather_act(prequant[0], prequant[1], prequant[2], sorted_token, groups, ngroups)
+        else:
+            xq, x_sf, a_sc = nvfp4_quant_act(xs, bn, 0.0, groups, ngroups)
         C.gemm_fp4mma(gu, xq, x_sf, a_sc, w13q[0], t13, w13q[2], bn, groups, ngroups, 2 * F)
         xq, x_sf, a_sc = nvfp4_quant_act(gu, bn, 0.0, groups, ngroups, swiglu=True)  # SwiGLU fused into the quantiser
         C.gemm_fp4mma(ys, xq, x_sf, a_sc, w2q[0], t2, w2q[2], bn, groups2, ngroups, H)
@@ -898,6 +921,6 @@ def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
         a = silu_mul(gu)
         C.gemm_nvfp4(ys, a, w2q[0], sk2, w2q[2], bn, groups2, ngroups, H)
     if out is None:
-        out = torch.empty(T, H, dtype=x.dtype, device=dev)
+        out = torch.empty(T, H, dtype=dt, device=dev)
     C.moe_combine(out, ys, sorted_pos, weights, False)
     return out

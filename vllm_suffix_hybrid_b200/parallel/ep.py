@@ -101,9 +101,15 @@ def dp_dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor
     if a2a_enabled(x):
         from . import ep_a2a
 
-        comm = ep_a2a.get(x.shape[1], A2A_MAX_TOKENS, ids.shape[1], moe.E_local)
-        xs, ids_l, w_l = comm.dispatch(x, ids, w)
-        return comm.combine(_experts(moe, xs, ids_l, w_l), ids)
+        quant = (moe.fp4 is not None and ops.nvfp4_act_mode() == "fp4" and x.shape[1] % 256 == 0
+                 and os.environ.get("SH_EP_A2A_FP4", "1") != "0")
+        comm = ep_a2a.get(x.shape[1], A2A_MAX_TOKENS, ids.shape[1], moe.E_local, quant)
+        rows, ids_l, w_l = comm.dispatch(x, ids, w)
+        if quant:  # NVFP4 rows: the W4A4 experts gather the received codes directly
+            y = ops.moe_experts_nvfp4(None, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F, prequant=rows)
+        else:
+            y = _experts(moe, rows, ids_l, w_l)
+        return comm.combine(y, ids)
     xs = _all_gather(x)
     ids_a = _all_gather(ids)
     w_a = _all_gather(w)

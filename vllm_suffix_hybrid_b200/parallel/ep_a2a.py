@@ -5,7 +5,9 @@ experts.  One MoE call:
 
 1. ``ep_dispatch`` (csrc/kernels/ep_a2a.cu): each token row is stored into the receive buffer of
    every rank that hosts one of its top-k experts (P2P stores from the kernel), with a route row
-   (local expert ids, -1 for experts elsewhere) on every rank;
+   (local expert ids, -1 for experts elsewhere) on every rank.  For NVFP4 (W4A4) experts the row is
+   quantised once in the dispatch kernel and sent as e2m1 codes + e4m3 scales + 1 / g (3.55x fewer
+   bytes); the receiving expert GEMMs gather the codes straight into their operand layout;
 2. this rank's grouped expert GEMMs over the received ``[world*T, H]`` rows;
 3. ``ep_combine``: the expert outputs go back to the token owners, which sum them in rank order.
 
@@ -30,7 +32,7 @@ MAX_WORLD = 8
 
 
 class EpA2A:
-    def __init__(self, hidden: int, max_tokens: int, k: int, e_local: int, group=None):
+    def __init__(self, hidden: int, max_tokens: int, k: int, e_local: int, group=None, quant: bool = False):
         import torch.distributed._symmetric_memory as symm_mem
 
         st = state.get()
@@ -50,12 +52,24 @@ class EpA2A:
         self.flag_buf = symm_mem.empty(2 * MAX_BLOCKS * MAX_WORLD, dtype=torch.int32, device=dev)
         self.flag_buf.zero_()
         self.ids_buf.fill_(-1)
+        # NVFP4 dispatch: codes [rows, H/2], e4m3 scales [rows, H/16], 1 / g [rows]
+        self.quant = quant
+        if quant:
+            if hidden % 256:
+                raise ValueError("NVFP4 dispatch needs hidden % 256 == 0")
+            self.q_buf = symm_mem.empty(rows * hidden // 2, dtype=torch.uint8, device=dev)
+            self.s_buf = symm_mem.empty(rows * hidden // 16, dtype=torch.uint8, device=dev)
+            self.a_buf = symm_mem.empty(rows, dtype=torch.float32, device=dev)
         torch.cuda.synchronize()
         name = self.group.group_name if hasattr(self.group, "group_name") else dist.group.WORLD.group_name
-        hs = [symm_mem.rendezvous(b, name) for b in (self.x_buf, self.ids_buf, self.w_buf, self.y_buf, self.flag_buf)]
+        bufs = [self.x_buf, self.ids_buf, self.w_buf, self.y_buf, self.flag_buf]
+        if quant:
+            bufs += [self.q_buf, self.s_buf, self.a_buf]
+        hs = [symm_mem.rendezvous(b, name) for b in bufs]
         self._handles = hs
-        self.peer_x, self.peer_ids, self.peer_w, self.peer_y, self.peer_flags = (
-            [int(p) for p in h.buffer_ptrs] for h in hs)
+        ptrs = [[int(p) for p in h.buffer_ptrs] for h in hs]
+        self.peer_x, self.peer_ids, self.peer_w, self.peer_y, self.peer_flags = ptrs[:5]
+        self.peer_q, self.peer_s, self.peer_a = ptrs[5:] if quant else ([], [], [])
         self.counters = torch.zeros(MAX_BLOCKS, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -67,17 +81,24 @@ class EpA2A:
                 self.rank, self.e_local, self.max_tokens, self.blocks)
 
     def dispatch(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor):
-        """-> (rows [world*T, H], local ids [world*T, k], weights [world*T, k]) received by this rank."""
+        """-> (rows, local ids [world*T, k], weights [world*T, k]) received by this rank; rows are bf16
+        [world*T, H], or with an NVFP4 communicator (codes [world*T, H/2], scales [world*T, H/16],
+        1 / g [world*T])."""
         from .. import ops
 
         T = x.shape[0]
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens exceed the EP receive buffers ({self.max_tokens})")
         ids = ids.to(torch.int32).contiguous()
-        ops.native().ep_dispatch(x.contiguous(), ids, w.float().contiguous(), *self._args())
-        n = self.world * T
-        return (self.x_buf[: n * self.hidden].view(n, self.hidden), self.ids_buf[: n * self.k].view(n, self.k),
-                self.w_buf[: n * self.k].view(n, self.k))
+        ops.native().ep_dispatch(x.contiguous(), ids, w.float().contiguous(), *self._args(), self.peer_q,
+                                 self.peer_s, self.peer_a)
+        n, H = self.world * T, self.hidden
+        if self.quant:
+            rows = (self.q_buf[: n * H // 2].view(n, H // 2), self.s_buf[: n * H // 16].view(n, H // 16),
+                    self.a_buf[:n])
+        else:
+            rows = self.x_buf[: n * H].view(n, H)
+        return rows, self.ids_buf[: n * self.k].view(n, self.k), self.w_buf[: n * self.k].view(n, self.k)
 
     def combine(self, y: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
         """y [world*T, H] expert outputs of the received rows -> [T, H] sums for this rank's tokens."""
@@ -94,13 +115,13 @@ class EpA2A:
             raise RuntimeError(f"EP all-to-all timed out or failed (code {code}) on rank {self.rank}")
 
 
-_comms: Dict[Tuple[int, int, int, int], EpA2A] = {}
+_comms: Dict[Tuple[int, int, int, int, bool], EpA2A] = {}
 
 
-def get(hidden: int, max_tokens: int, k: int, e_local: int) -> Optional[EpA2A]:
+def get(hidden: int, max_tokens: int, k: int, e_local: int, quant: bool = False) -> Optional[EpA2A]:
     """The process's EP communicator for these sizes (created on first use; every rank must call)."""
-    key = (hidden, max_tokens, k, e_local)
+    key = (hidden, max_tokens, k, e_local, quant)
     c = _comms.get(key)
     if c is None:
-        c = _comms[key] = EpA2A(hidden, max_tokens, k, e_local)
+        c = _comms[key] = EpA2A(hidden, max_tokens, k, e_local, quant=quant)
     return c
