@@ -623,7 +623,9 @@ void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor w, std::vecto
                  std::vector<int64_t> peer_ids, std::vector<int64_t> peer_w, std::vector<int64_t> peer_y,
                  std::vector<int64_t> peer_flags, torch::Tensor counters, torch::Tensor err, int64_t rank,
                  int64_t e_local, int64_t max_T, int64_t num_blocks, std::vector<int64_t> peer_q,
-                 std::vector<int64_t> peer_s, std::vector<int64_t> peer_a) {
+                 std::vector<int64_t> peer_s, std::vector<int64_t> peer_a, c10::optional<torch::Tensor> logits,
+                 c10::optional<torch::Tensor> bias, bool sigmoid_grouped, int64_t n_groups, int64_t topk_groups,
+                 bool renorm, double scale) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.size(0) == ids.size(0),
               "ep_dispatch: x");
   TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.sizes() == ids.sizes(), "ep_dispatch: w");
@@ -631,6 +633,30 @@ void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor w, std::vecto
                          max_T);
   p.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   p.w = w.data_ptr<float>();
+  if (logits.has_value()) {  // the dispatch routes its tokens; ids / w are written, not read
+    TORCH_CHECK(logits->is_cuda() && logits->is_contiguous() && logits->dim() == 2 &&
+                    logits->size(0) == ids.size(0) &&
+                    (logits->scalar_type() == at::kFloat || logits->scalar_type() == at::kBFloat16),
+                "ep_dispatch: logits fp32/bf16 [T, E]");
+    RouteParams& r = p.route;
+    r.logits = logits->data_ptr();
+    r.logits_bf16 = logits->scalar_type() == at::kBFloat16 ? 1 : 0;
+    if (bias.has_value()) {
+      TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == logits->size(1), "ep_dispatch: bias");
+      r.bias = bias->data_ptr<float>();
+    }
+    r.ids = ids.data_ptr<int32_t>();
+    r.weights = w.data_ptr<float>();
+    r.T = static_cast<int>(ids.size(0));
+    r.E = static_cast<int>(logits->size(1));
+    r.k = static_cast<int>(ids.size(1));
+    r.sigmoid_grouped = sigmoid_grouped ? 1 : 0;
+    r.n_groups = static_cast<int>(n_groups);
+    r.topk_groups = static_cast<int>(topk_groups);
+    r.renorm = renorm ? 1 : 0;
+    r.scale = static_cast<float>(scale);
+    p.fused_route = 1;
+  }
   if (!peer_q.empty()) {  // NVFP4 dispatch
     TORCH_CHECK(peer_q.size() == peer_x.size() && peer_s.size() == peer_x.size() && peer_a.size() == peer_x.size(),
                 "ep_dispatch: quantised peer lists");

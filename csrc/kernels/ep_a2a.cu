@@ -4,7 +4,9 @@
 // all-gather of every token to every rank + reduce-scatter of the partials:
 // a token row crosses NVLink only to ranks that host one of its top-k experts).
 //
-// dispatch (rank r, block b, tokens i = b, b + nblocks, ...):
+// dispatch (rank r, block b, tokens i = b, b + nblocks, ...): optionally
+//   routes the token first from its router logits (the standalone router's
+//   selection, moe_route.cuh; ids / weights also written for the combine);
 //   for every rank d: route row (local expert id or -1, weight or 0) ->
 //   d.ids / d.w [r*T + i]; for the ranks d hosting one of the token's experts:
 //   x[i] -> d.x[r*T + i] (bf16), or with quant the row quantised once to
@@ -35,6 +37,7 @@
 #include <stdint.h>
 
 #include "ep_a2a.h"
+#include "moe_route.cuh"
 #include "nvfp4_act.cuh"
 #include "pdl.cuh"
 
@@ -94,8 +97,8 @@ __device__ __forceinline__ uint32_t dest_mask(const EpParams& p, int64_t i) {
 
 // Quantises token row i to NVFP4 in shared memory (codes then scales) and
 // stores it into every destination rank's receive rows with 16-byte stores.
-__device__ void quant_send(const EpParams& p, int64_t i, int64_t row, uint32_t m) {
-  extern __shared__ __align__(16) uint8_t qsm[];  // [H/2 codes][H/16 scales]
+// qsm: H/2 + H/16 bytes of 16-byte aligned shared memory ([codes][scales]).
+__device__ void quant_send(const EpParams& p, int64_t i, int64_t row, uint32_t m, uint8_t* qsm) {
   __shared__ float red[kThreads / 32];
   const int nblk = p.H / 16;
   const __nv_bfloat16* xr = p.x + i * p.H;
@@ -134,8 +137,12 @@ __device__ void quant_send(const EpParams& p, int64_t i, int64_t row, uint32_t m
 __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(EpParams p) {
   shk::pdl_trigger();
   shk::pdl_wait();
+  extern __shared__ __align__(16) uint8_t dsm[];  // [router scores 2E floats][NVFP4 row staging]
   __shared__ uint32_t s_epoch;
   __shared__ volatile int bail;
+  __shared__ shk::route::Scratch rsc;
+  __shared__ int tok_ids[SH_EP_MAX_K];
+  __shared__ float tok_w[SH_EP_MAX_K];
   if (threadIdx.x == 0) {
     s_epoch = ++p.counters[blockIdx.x];
     bail = 0;
@@ -144,18 +151,35 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(EpParams p) {
   const uint32_t epoch = s_epoch;
   const int nv = p.H / 8;
   const int64_t T = p.T;
+  const int route_bytes = p.fused_route ? ((2 * p.route.E * 4 + 15) & ~15) : 0;
   for (int64_t i = blockIdx.x; i < T; i += gridDim.x) {
     const int64_t row = static_cast<int64_t>(p.rank) * T + i;  // this token's row on every rank
+    __syncthreads();  // the previous token is done with tok_ids / tok_w and the staging
+    if (p.fused_route) {  // route the token here: the same selection as the standalone router
+      shk::route::route_token(p.route, i, shk::route::threads_for(p.route.E), reinterpret_cast<float*>(dsm), rsc);
+      if (threadIdx.x < p.k) {
+        tok_ids[threadIdx.x] = rsc.chosen_i[threadIdx.x];
+        tok_w[threadIdx.x] = rsc.chosen_w[threadIdx.x];
+        p.route.ids[i * p.k + threadIdx.x] = rsc.chosen_i[threadIdx.x];
+        p.route.weights[i * p.k + threadIdx.x] = rsc.chosen_w[threadIdx.x];
+      }
+    } else if (threadIdx.x < p.k) {
+      tok_ids[threadIdx.x] = p.ids[i * p.k + threadIdx.x];
+      tok_w[threadIdx.x] = p.w[i * p.k + threadIdx.x];
+    }
+    __syncthreads();
     if (threadIdx.x < p.world * p.k) {
       const int d = threadIdx.x / p.k, j = threadIdx.x % p.k;
-      const int id = p.ids[i * p.k + j];
+      const int id = tok_ids[j];
       const bool mine = id >= 0 && id / p.e_local == d;
       p.peer_ids[d][row * p.k + j] = mine ? id - d * p.e_local : -1;
-      p.peer_w[d][row * p.k + j] = mine ? p.w[i * p.k + j] : 0.f;
+      p.peer_w[d][row * p.k + j] = mine ? tok_w[j] : 0.f;
     }
-    const uint32_t m = dest_mask(p, i);
+    uint32_t m = 0;
+    for (int j = 0; j < p.k; ++j)
+      if (tok_ids[j] >= 0) m |= 1u << (tok_ids[j] / p.e_local);
     if (p.quant) {
-      quant_send(p, i, row, m);
+      quant_send(p, i, row, m, dsm + route_bytes);
       continue;
     }
     const uint4* src = reinterpret_cast<const uint4*>(p.x + i * p.H);
@@ -229,7 +253,12 @@ using namespace shk::ep;
 static int ep_check(const EpParams& p) {
   if (p.world < 1 || p.world > SH_EP_MAX_WORLD || p.H % 8 != 0 || p.T < 0 || p.T > p.max_T) return -1;
   if (p.k < 1 || p.k > SH_EP_MAX_K || p.world * p.k > kThreads || p.e_local < 1) return -2;
-  if (p.quant && (p.H % 256 != 0 || p.H / 2 + p.H / 16 > 48 * 1024)) return -3;  // 16-byte scale rows
+  if (p.quant && (p.H % 256 != 0 || p.H / 2 + p.H / 16 > 24 * 1024)) return -3;  // 16-byte scale rows
+  if (p.fused_route) {
+    const RouteParams& r = p.route;
+    if (r.k != p.k || r.E < r.k || r.E > 2048 || !r.logits || !r.ids || !r.weights || r.ids != p.ids) return -4;
+    if (r.sigmoid_grouped && (r.n_groups < 1 || r.E % r.n_groups || r.n_groups > 64)) return -4;
+  }
   return 0;
 }
 
@@ -238,7 +267,8 @@ extern "C" int sh_ep_dispatch(const EpParams* params, int num_blocks, cudaStream
   if (rc) return rc;
   if (params->T == 0) return 0;
   num_blocks = num_blocks < 1 ? 1 : (num_blocks > SH_EP_MAX_BLOCKS ? SH_EP_MAX_BLOCKS : num_blocks);
-  const size_t smem = params->quant ? static_cast<size_t>(params->H / 2 + params->H / 16) : 0;
+  const size_t smem = (params->fused_route ? ((2 * params->route.E * 4 + 15) & ~15) : 0) +
+                      (params->quant ? static_cast<size_t>(params->H / 2 + params->H / 16) : 0);
   shk::launch(ep_dispatch_kernel, dim3(num_blocks), dim3(kThreads), smem, stream, *params);
   return static_cast<int>(cudaGetLastError());
 }

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "moe.h"
+
 #define SH_EP_MAX_WORLD 8
 #define SH_EP_MAX_BLOCKS 160
 #define SH_EP_MAX_K 16
@@ -32,6 +34,11 @@ struct EpParams {
   uint8_t* peer_q[SH_EP_MAX_WORLD];  // per rank: [world*max_T][H/2] e2m1 codes
   uint8_t* peer_s[SH_EP_MAX_WORLD];  // per rank: [world*max_T][H/16] e4m3 scales
   float* peer_a[SH_EP_MAX_WORLD];    // per rank: [world*max_T] 1 / g
+  // fused_route = 1: the dispatch routes its own tokens from the router logits (route.logits [T, E]) with
+  // the standalone router's selection and writes route.ids / route.weights [T, k] (ids must equal
+  // route.ids: the combine reads them); `w` is then unused.
+  int fused_route;
+  RouteParams route;
 };
 
 #ifdef __cplusplus

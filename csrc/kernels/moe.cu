@@ -1,12 +1,8 @@
 // Mixture-of-experts routing and token movement.
 //
-//  * route_softmax_topk: softmax over E router logits, top-k, optional
-//    renormalisation of the k weights (Qwen3-Next router).
-//  * route_sigmoid_grouped: sigmoid scores; selection on score + correction
-//    bias, restricted to the top `topk_groups` of `n_groups` expert groups
-//    (group score = sum of its two best biased scores); weights = unbiased
-//    scores of the chosen experts, renormalised and scaled (DeepSeek-V3 /
-//    Kimi-K2 router).
+//  * route: one token per block; softmax top-k (Qwen3-Next) or sigmoid
+//    group-limited (DeepSeek-V3 / Kimi-K2) selection, shared with the
+//    expert-parallel dispatch through moe_route.cuh.
 //  * align: counting sort of the (token, slot) pairs by expert, exclusive
 //    offsets, and the device-side tile list (sorted row start, rows, expert
 //    weight row offset) the grouped tcgen05 GEMM consumes -- no host sync.
@@ -17,168 +13,24 @@
 #include <stdint.h>
 
 #include "moe.h"
+#include "moe_route.cuh"
 #include "pdl.cuh"
 
 namespace shk {
 namespace moe {
 
-__device__ __forceinline__ float load_f(const void* p, int64_t i, int is_bf16) {
-  return is_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]) : reinterpret_cast<const float*>(p)[i];
-}
-
-// Block argmax over s[0:E) (ties -> lowest index); returns the index.
-__device__ int block_argmax(const float* s, int E, float* rv, int* ri) {
-  float best = -INFINITY;
-  int idx = 0x7fffffff;
-  for (int e = threadIdx.x; e < E; e += blockDim.x)
-    if (s[e] > best || (s[e] == best && e < idx)) {
-      best = s[e];
-      idx = e;
-    }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (ob > best || (ob == best && oi < idx)) {
-      best = ob;
-      idx = oi;
-    }
-  }
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  __syncthreads();
-  if (lane == 0) {
-    rv[w] = best;
-    ri[w] = idx;
-  }
-  __syncthreads();
-  best = rv[0];
-  idx = ri[0];
-  for (int i = 1; i < static_cast<int>(blockDim.x >> 5); ++i)
-    if (rv[i] > best || (rv[i] == best && ri[i] < idx)) {
-      best = rv[i];
-      idx = ri[i];
-    }
-  return idx;
-}
-
-__global__ void route_softmax_kernel(RouteParams p) {
+// One token per block; the selection itself is shk::route::route_token
+// (moe_route.cuh), which the expert-parallel dispatch also runs per token.
+__global__ void route_kernel(RouteParams p) {
   shk::pdl_trigger();
   shk::pdl_wait();
-  extern __shared__ float s[];
-  __shared__ float rv[32];
-  __shared__ int ri[32];
-  __shared__ float red[32];
+  extern __shared__ float s[];  // [E] scores (softmax) or [E] scores + [E] biased (sigmoid_grouped)
+  __shared__ shk::route::Scratch sc;
   const int64_t t = blockIdx.x;
-  float mx = -INFINITY;
-  for (int e = threadIdx.x; e < p.E; e += blockDim.x) {
-    s[e] = load_f(p.logits, t * p.E + e, p.logits_bf16);
-    mx = fmaxf(mx, s[e]);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  mx = red[0];
-  for (int i = 1; i < static_cast<int>(blockDim.x >> 5); ++i) mx = fmaxf(mx, red[i]);
-  __syncthreads();
-  float sum = 0.f;
-  for (int e = threadIdx.x; e < p.E; e += blockDim.x) {
-    s[e] = __expf(s[e] - mx);
-    sum += s[e];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
-  __syncthreads();
-  sum = 0.f;
-  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) sum += red[i];
-  __shared__ float chosen_w[64];
-  __shared__ int chosen_i[64];
-  for (int j = 0; j < p.k; ++j) {
-    const int e = block_argmax(s, p.E, rv, ri);
-    if (threadIdx.x == 0) {
-      chosen_i[j] = e;
-      chosen_w[j] = s[e] / sum;
-      s[e] = -INFINITY;
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    float tot = 0.f;
-    for (int j = 0; j < p.k; ++j) tot += chosen_w[j];
-    for (int j = 0; j < p.k; ++j) {
-      p.ids[t * p.k + j] = chosen_i[j];
-      p.weights[t * p.k + j] = (p.renorm ? chosen_w[j] / tot : chosen_w[j]) * p.scale;
-    }
-  }
-}
-
-__global__ void route_sigmoid_grouped_kernel(RouteParams p) {
-  shk::pdl_trigger();
-  shk::pdl_wait();
-  extern __shared__ float s[];  // [E] scores, [E] biased
-  float* sb = s + p.E;
-  __shared__ float rv[32];
-  __shared__ int ri[32];
-  __shared__ float gscore[64];
-  __shared__ float chosen_w[64];
-  __shared__ int chosen_i[64];
-  const int64_t t = blockIdx.x;
-  for (int e = threadIdx.x; e < p.E; e += blockDim.x) {
-    const float x = load_f(p.logits, t * p.E + e, p.logits_bf16);
-    const float sc = 1.f / (1.f + __expf(-x));
-    s[e] = sc;
-    sb[e] = sc + (p.bias ? p.bias[e] : 0.f);
-  }
-  __syncthreads();
-  const int per = p.E / p.n_groups;
-  if (p.n_groups > 1) {
-    // Group score: sum of the two best biased scores in the group.
-    for (int gi = threadIdx.x; gi < p.n_groups; gi += blockDim.x) {
-      float b1 = -INFINITY, b2 = -INFINITY;
-      for (int e = gi * per; e < (gi + 1) * per; ++e) {
-        const float v = sb[e];
-        if (v > b1) {
-          b2 = b1;
-          b1 = v;
-        } else if (v > b2) {
-          b2 = v;
-        }
-      }
-      gscore[gi] = b1 + (per > 1 ? b2 : 0.f);
-    }
-    __syncthreads();
-    __shared__ int kept[64];
-    if (threadIdx.x == 0) {  // keep the top `topk_groups` groups (ties -> lower index), mask the rest
-      for (int gi = 0; gi < p.n_groups; ++gi) kept[gi] = 0;
-      for (int j = 0; j < p.topk_groups; ++j) {
-        int best = -1;
-        for (int gi = 0; gi < p.n_groups; ++gi)
-          if (!kept[gi] && (best < 0 || gscore[gi] > gscore[best])) best = gi;
-        if (best >= 0) kept[best] = 1;
-      }
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < p.E; e += blockDim.x)
-      if (!kept[e / per]) sb[e] = -INFINITY;
-    __syncthreads();
-  }
-  for (int j = 0; j < p.k; ++j) {
-    const int e = block_argmax(sb, p.E, rv, ri);
-    if (threadIdx.x == 0) {
-      chosen_i[j] = e;
-      chosen_w[j] = s[e];
-      sb[e] = -INFINITY;
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    float tot = 0.f;
-    for (int j = 0; j < p.k; ++j) tot += chosen_w[j];
-    for (int j = 0; j < p.k; ++j) {
-      p.ids[t * p.k + j] = chosen_i[j];
-      p.weights[t * p.k + j] = (p.renorm && tot > 0.f ? chosen_w[j] / tot : chosen_w[j]) * p.scale;
-    }
+  shk::route::route_token(p, t, blockDim.x, s, sc);
+  if (threadIdx.x < p.k) {
+    p.ids[t * p.k + threadIdx.x] = sc.chosen_i[threadIdx.x];
+    p.weights[t * p.k + threadIdx.x] = sc.chosen_w[threadIdx.x];
   }
 }
 
@@ -270,13 +122,10 @@ using namespace shk::moe;
 extern "C" int sh_moe_route(const RouteParams* p, cudaStream_t stream) {
   if (p->T <= 0) return 0;
   if (p->k > 64 || p->k < 1 || p->E < p->k) return -1;
-  const int threads = p->E >= 512 ? 512 : (p->E >= 256 ? 256 : 128);
-  if (p->sigmoid_grouped) {
-    if (p->n_groups < 1 || p->E % p->n_groups || p->n_groups > 64) return -2;
-    shk::launch(route_sigmoid_grouped_kernel, dim3(p->T), dim3(threads), 2 * p->E * sizeof(float), stream, *p);
-  } else {
-    shk::launch(route_softmax_kernel, dim3(p->T), dim3(threads), p->E * sizeof(float), stream, *p);
-  }
+  const int threads = shk::route::threads_for(p->E);
+  if (p->sigmoid_grouped && (p->n_groups < 1 || p->E % p->n_groups || p->n_groups > 64)) return -2;
+  const size_t smem = (p->sigmoid_grouped ? 2 : 1) * p->E * sizeof(float);
+  shk::launch(route_kernel, dim3(p->T), dim3(threads), smem, stream, *p);
   return static_cast<int>(cudaGetLastError());
 }
 

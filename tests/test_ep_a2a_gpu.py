@@ -3,7 +3,9 @@
 Every rank routes its own tokens over all experts; the device all-to-all path must match the fp32
 sum over the routed experts computed from all ranks' weights, agree with the NCCL all-gather /
 reduce-scatter path, survive consecutive calls of different sizes (single receive buffers ordered by
-the epoch barriers) and replay correctly from a CUDA graph.  Skipped with fewer than two GPUs.
+the epoch barriers) and replay correctly from a CUDA graph.  The NVFP4-quantising dispatch and the
+dispatch that runs the router top-k itself must be bit-identical to the unfused paths.  Skipped with
+fewer than two GPUs.
 """
 import os
 import socket
@@ -134,6 +136,26 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             results[f"fp4:{call}:T{T}"] = (0.0 if torch.equal(got, base) else 1.0, 0.0)
         os.environ["SH_EP_A2A_FP4"] = "1"
+        # Router top-k inside the dispatch kernel: bit-identical to ops.moe_route + the same dispatch, for the
+        # softmax and the sigmoid group-limited routers, with bf16 and NVFP4 experts.
+        from vllm_suffix_hybrid_b200 import ops
+
+        bias = (torch.randn(E, generator=g) * 0.1).cuda()
+        routers = (dict(sigmoid_grouped=False, bias=None, n_groups=1, topk_groups=1, renorm=True, scale=1.0),
+                   dict(sigmoid_grouped=True, bias=bias, n_groups=2, topk_groups=1, renorm=True, scale=2.5))
+        for mi, (mdl, HH) in enumerate(((moe, H), (moe4, H4))):
+            mdl.k = k
+            for ri, args in enumerate(routers):
+                mdl.route_args = lambda a=args: a
+                for call, T in enumerate([19, 2]):
+                    gi = torch.Generator().manual_seed(700 + 10 * call + rank)
+                    x = torch.randn(T, HH, generator=gi).to(torch.bfloat16).cuda()
+                    logits = torch.randn(T, E, generator=gi).to(torch.bfloat16).cuda()
+                    got = ep.dp_route_dispatch_combine(mdl, x, logits)
+                    ids, w = ops.moe_route(logits, k, **args)
+                    base = ep.dp_dispatch_combine(mdl, x, ids, w)
+                    torch.cuda.synchronize()
+                    results[f"route:{mi}:{ri}:{call}"] = (0.0 if torch.equal(got, base) else 1.0, 0.0)
         from vllm_suffix_hybrid_b200.parallel import ep_a2a
 
         assert any(c.quant for c in ep_a2a._comms.values())

@@ -93,26 +93,42 @@ class MoEBlock:
             self.fp4 = tuple(q[:3] + (ops.nvfp4_kmajor_scales(q[1]), ops.nvfp4_scale_tiles(q[1], r))
                              for q, r in zip(self.fp4, rows))
 
-    def route(self, x: torch.Tensor):
-        logits = ops.linear(x, self.gate).float() if not x.is_cuda else ops.linear(x, self.gate)
+    def router_logits(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.linear(x, self.gate).float() if not x.is_cuda else ops.linear(x, self.gate)
+
+    def route_args(self) -> dict:
+        """Selection parameters of ops.moe_route (besides logits and k)."""
         if self.cfg.router == "sigmoid_grouped":
-            return ops.moe_route(logits, self.k, True, self.bias, self.cfg.n_groups, self.cfg.topk_groups, True,
-                                 self.cfg.routed_scale)
-        return ops.moe_route(logits, self.k, False, renorm=True)
+            return dict(sigmoid_grouped=True, bias=self.bias, n_groups=self.cfg.n_groups,
+                        topk_groups=self.cfg.topk_groups, renorm=True, scale=self.cfg.routed_scale)
+        return dict(sigmoid_grouped=False, bias=None, n_groups=1, topk_groups=1, renorm=True, scale=1.0)
+
+    def route(self, x: torch.Tensor):
+        return ops.moe_route(self.router_logits(x), self.k, **self.route_args())
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         """x: normalised input [T, H]; returns the (TP-partial-free) FFN output [T, H]."""
-        ids, w = self.route(x)
-        if self.ep > 1:
+        if self.ep > 1 and st_dp() > 1:
             from ..parallel import ep
 
-            out = ep.dp_dispatch_combine(self, x, ids, w) if st_dp() > 1 else ep.dispatch_combine(self, x, ids, w)
-        elif self.fp4 is not None:
-            out = ops.moe_experts_nvfp4(x, ids, w, self.fp4[0], self.fp4[1], self.E, self.F)
-        elif self.fp8 is not None:
-            out = ops.moe_experts_mxfp8(x, ids, w, self.fp8[0], self.fp8[1], self.E, self.F)
+            if ep.a2a_enabled(x):  # the dispatch kernel runs the router top-k itself
+                out = ep.dp_route_dispatch_combine(self, x, self.router_logits(x))
+            else:
+                ids, w = self.route(x)
+                out = ep.dp_dispatch_combine(self, x, ids, w)
+        elif self.ep > 1:
+            from ..parallel import ep
+
+            ids, w = self.route(x)
+            out = ep.dispatch_combine(self, x, ids, w)
         else:
-            out = ops.moe_experts(x, ids, w, self.w13, self.w2, self.E, self.F)
+            ids, w = self.route(x)
+            if self.fp4 is not None:
+                out = ops.moe_experts_nvfp4(x, ids, w, self.fp4[0], self.fp4[1], self.E, self.F)
+            elif self.fp8 is not None:
+                out = ops.moe_experts_mxfp8(x, ids, w, self.fp8[0], self.fp8[1], self.E, self.F)
+            else:
+                out = ops.moe_experts(x, ids, w, self.w13, self.w2, self.E, self.F)
         if self.shared is not None:
             s = self.shared(x)
             if state.get().tp > 1:

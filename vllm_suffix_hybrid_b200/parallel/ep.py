@@ -93,6 +93,28 @@ def a2a_enabled(x: torch.Tensor) -> bool:
             and x.shape[0] <= A2A_MAX_TOKENS)
 
 
+def _quant_dispatch(moe, x: torch.Tensor) -> bool:
+    return (moe.fp4 is not None and ops.nvfp4_act_mode() == "fp4" and x.shape[1] % 256 == 0
+            and os.environ.get("SH_EP_A2A_FP4", "1") != "0")
+
+
+def _a2a_experts(moe, quant: bool, rows, ids_l: torch.Tensor, w_l: torch.Tensor) -> torch.Tensor:
+    if quant:  # NVFP4 rows: the W4A4 experts gather the received codes directly
+        return ops.moe_experts_nvfp4(None, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F, prequant=rows)
+    return _experts(moe, rows, ids_l, w_l)
+
+
+def dp_route_dispatch_combine(moe, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+    """dp_dispatch_combine with the router top-k run inside the dispatch kernel (CUDA all-to-all only):
+    logits [T, E] -> [T, H].  Bit-identical to ops.moe_route followed by dp_dispatch_combine."""
+    from . import ep_a2a
+
+    quant = _quant_dispatch(moe, x)
+    comm = ep_a2a.get(x.shape[1], A2A_MAX_TOKENS, moe.k, moe.E_local, quant)
+    rows, ids_l, w_l, ids, _ = comm.dispatch_routed(x, logits, **moe.route_args())
+    return comm.combine(_a2a_experts(moe, quant, rows, ids_l, w_l), ids)
+
+
 def dp_dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Data-parallel attention: every rank's tokens through this rank's experts; each rank keeps its own rows.
 
@@ -101,15 +123,10 @@ def dp_dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor
     if a2a_enabled(x):
         from . import ep_a2a
 
-        quant = (moe.fp4 is not None and ops.nvfp4_act_mode() == "fp4" and x.shape[1] % 256 == 0
-                 and os.environ.get("SH_EP_A2A_FP4", "1") != "0")
+        quant = _quant_dispatch(moe, x)
         comm = ep_a2a.get(x.shape[1], A2A_MAX_TOKENS, ids.shape[1], moe.E_local, quant)
         rows, ids_l, w_l = comm.dispatch(x, ids, w)
-        if quant:  # NVFP4 rows: the W4A4 experts gather the received codes directly
-            y = ops.moe_experts_nvfp4(None, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F, prequant=rows)
-        else:
-            y = _experts(moe, rows, ids_l, w_l)
-        return comm.combine(y, ids)
+        return comm.combine(_a2a_experts(moe, quant, rows, ids_l, w_l), ids)
     xs = _all_gather(x)
     ids_a = _all_gather(ids)
     w_a = _all_gather(w)

@@ -7,7 +7,8 @@ experts.  One MoE call:
    every rank that hosts one of its top-k experts (P2P stores from the kernel), with a route row
    (local expert ids, -1 for experts elsewhere) on every rank.  For NVFP4 (W4A4) experts the row is
    quantised once in the dispatch kernel and sent as e2m1 codes + e4m3 scales + 1 / g (3.55x fewer
-   bytes); the receiving expert GEMMs gather the codes straight into their operand layout;
+   bytes); the receiving expert GEMMs gather the codes straight into their operand layout.  With
+   ``dispatch_routed`` the kernel also runs the router top-k of each token from its logits;
 2. this rank's grouped expert GEMMs over the received ``[world*T, H]`` rows;
 3. ``ep_combine``: the expert outputs go back to the token owners, which sum them in rank order.
 
@@ -91,7 +92,26 @@ class EpA2A:
             raise ValueError(f"{T} tokens exceed the EP receive buffers ({self.max_tokens})")
         ids = ids.to(torch.int32).contiguous()
         ops.native().ep_dispatch(x.contiguous(), ids, w.float().contiguous(), *self._args(), self.peer_q,
-                                 self.peer_s, self.peer_a)
+                                 self.peer_s, self.peer_a, None, None, False, 1, 1, True, 1.0)
+        return self._received(T)
+
+    def dispatch_routed(self, x: torch.Tensor, logits: torch.Tensor, sigmoid_grouped: bool = False, bias=None,
+                        n_groups: int = 1, topk_groups: int = 1, renorm: bool = True, scale: float = 1.0):
+        """Routes the tokens inside the dispatch kernel (the router top-k of ops.moe_route, bit for bit)
+        from the router logits [T, E] -> (received rows, local ids, local weights, ids [T, k], weights
+        [T, k]); the combine takes the returned ids."""
+        from .. import ops
+
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the EP receive buffers ({self.max_tokens})")
+        ids = torch.empty(T, self.k, dtype=torch.int32, device=x.device)
+        w = torch.empty(T, self.k, dtype=torch.float32, device=x.device)
+        ops.native().ep_dispatch(x.contiguous(), ids, w, *self._args(), self.peer_q, self.peer_s, self.peer_a,
+                                 logits.contiguous(), bias, sigmoid_grouped, n_groups, topk_groups, renorm, scale)
+        return self._received(T) + (ids, w)
+
+    def _received(self, T: int):
         n, H = self.world * T, self.hidden
         if self.quant:
             rows = (self.q_buf[: n * H // 2].view(n, H // 2), self.s_buf[: n * H // 16].view(n, H // 16),
