@@ -855,7 +855,7 @@ def moe_experts_mxfp8(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
     xq, x_sf, a_sc = mxfp8_quant_act(a, bn, groups, ngroups)
     C.gemm_fp4mma(ys, xq, x_sf, a_sc, w2q[0], t2, ones, bn, groups2, ngroups, H, fp8=True)
     if out is None:
-        out = torch.empty(T, H, dtype=dt, device=dev)
+        out = torch.empty(T, H, dtype=x.dtype, device=dev)
     C.moe_combine(out, ys, sorted_pos, weights, False)
     return out
 
