@@ -715,6 +715,43 @@ void gdn_chunk_prefill(torch::Tensor qkv, torch::Tensor z, torch::Tensor ba, tor
               "sh_gdn_chunk_prefill");
 }
 
+void ep_combine_push(torch::Tensor ys, torch::Tensor sorted_pos, torch::Tensor w_local, torch::Tensor ids_local,
+                     int64_t T, std::vector<int64_t> peer_x, std::vector<int64_t> peer_ids, std::vector<int64_t> peer_w,
+                     std::vector<int64_t> peer_y, std::vector<int64_t> peer_flags, torch::Tensor counters,
+                     torch::Tensor err, int64_t rank, int64_t e_local, int64_t max_T, int64_t num_blocks) {
+  const int64_t world = static_cast<int64_t>(peer_x.size());
+  TORCH_CHECK(ys.is_cuda() && ys.scalar_type() == at::kBFloat16 && ys.is_contiguous() && ys.dim() == 2,
+              "ep_combine_push: ys bf16 [pairs, H]");
+  TORCH_CHECK(ids_local.scalar_type() == at::kInt && ids_local.dim() == 2 && ids_local.size(0) == world * T,
+              "ep_combine_push: ids_local [world*T, k]");
+  TORCH_CHECK(sorted_pos.scalar_type() == at::kInt && sorted_pos.is_contiguous() &&
+                  sorted_pos.numel() == ids_local.numel(), "ep_combine_push: sorted_pos [world*T*k]");
+  TORCH_CHECK(w_local.scalar_type() == at::kFloat && w_local.is_contiguous() && w_local.numel() == ids_local.numel(),
+              "ep_combine_push: w_local [world*T, k]");
+  // ids of T tokens only give T and k here; the kernel reads the received local ids from peer_ids[rank].
+  torch::Tensor shape_ids = ids_local.narrow(0, 0, T);
+  EpParams p = ep_params(shape_ids.contiguous(), peer_x, peer_ids, peer_w, peer_y, peer_flags, counters, err, rank,
+                         ys.size(1), e_local, max_T);
+  p.ys = reinterpret_cast<const __nv_bfloat16*>(ys.data_ptr());
+  p.sorted_pos = sorted_pos.data_ptr<int32_t>();
+  p.w_local = w_local.data_ptr<float>();
+  SH_CHECK_RC(sh_ep_combine_push(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream()),
+              "sh_ep_combine_push");
+}
+
+void ep_combine_sum(torch::Tensor ids, torch::Tensor out, std::vector<int64_t> peer_x, std::vector<int64_t> peer_ids,
+                    std::vector<int64_t> peer_w, std::vector<int64_t> peer_y, std::vector<int64_t> peer_flags,
+                    torch::Tensor counters, torch::Tensor err, int64_t rank, int64_t e_local, int64_t max_T,
+                    int64_t num_blocks) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(0) == ids.size(0),
+              "ep_combine_sum: out [T, H]");
+  EpParams p = ep_params(ids, peer_x, peer_ids, peer_w, peer_y, peer_flags, counters, err, rank, out.size(1), e_local,
+                         max_T);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.pushed = 1;
+  SH_CHECK_RC(sh_ep_combine(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream()), "sh_ep_combine");
+}
+
 // --- MoE -------------------------------------------------------------------------
 void moe_route(torch::Tensor logits, c10::optional<torch::Tensor> bias, torch::Tensor ids, torch::Tensor weights,
                int64_t k, bool sigmoid_grouped, int64_t n_groups, int64_t topk_groups, bool renorm, double scale) {
@@ -855,6 +892,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_recurrent", &gdn_recurrent);
   m.def("gdn_chunk_prefill", &gdn_chunk_prefill, "Chunked (64-token, tensor-core) GDN prefill from zero state");
   m.def("ep_dispatch", &ep_dispatch, "Expert-parallel dispatch of token rows over NVLink peer memory");
+  m.def("ep_combine_push", &ep_combine_push, "Experts' weighted per-token sum stored into the owners' return rows");
+  m.def("ep_combine_sum", &ep_combine_sum, "Owner-side sum of the rows pushed by ep_combine_push");
   m.def("ep_combine", &ep_combine, "Expert-parallel combine of expert outputs over NVLink peer memory");
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);

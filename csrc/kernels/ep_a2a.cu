@@ -206,8 +206,9 @@ __global__ void __launch_bounds__(kThreads) ep_combine_kernel(EpParams p) {
   const int nv = p.H / 8;
   const int64_t T = p.T;
   const int32_t* my_ids = p.peer_ids[p.rank];
-  // Push: row r*T + i of y goes back to its owner r when a local expert served it.
-  for (int64_t i = blockIdx.x; i < T; i += gridDim.x) {
+  // Push: row r*T + i of y goes back to its owner r when a local expert served it (unless the experts'
+  // weighted sum already stored it there: ep_combine_push_kernel).
+  for (int64_t i = blockIdx.x; i < T && !p.pushed; i += gridDim.x) {
     for (int r = 0; r < p.world; ++r) {
       const int64_t row = static_cast<int64_t>(r) * T + i;
       bool served = false;
@@ -245,6 +246,42 @@ __global__ void __launch_bounds__(kThreads) ep_combine_kernel(EpParams p) {
   }
 }
 
+// The experts' weighted per-token sum of the received rows, stored straight into
+// the owners' return rows: the same arithmetic as moe.cu combine_kernel (fp32
+// accumulation in slot order, one bf16 rounding), so the owner's sum is
+// bit-identical to combine_kernel followed by ep_combine_kernel's push.  Rows
+// no local expert served are not stored.  Every thread fences at system
+// scope after its stores, and the following ep_combine_kernel (pushed = 1)
+// starts after this grid has completed, so its barrier orders these stores
+// before the owners read them.
+__global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(EpParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  const int64_t T = p.T;
+  const int32_t* my_ids = p.peer_ids[p.rank];
+  for (int64_t row = blockIdx.x; row < static_cast<int64_t>(p.world) * T; row += gridDim.x) {
+    bool served = false;
+    for (int j = 0; j < p.k; ++j) served |= my_ids[row * p.k + j] >= 0;
+    if (!served) continue;
+    const int r = static_cast<int>(row / T);
+    const int64_t i = row % T;
+    __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(p.peer_y[r] + (static_cast<int64_t>(p.rank) * T + i) * p.H);
+    for (int e = threadIdx.x; e < p.H / 2; e += kThreads) {
+      float2 acc = make_float2(0.f, 0.f);
+      for (int j = 0; j < p.k; ++j) {
+        const int pos = p.sorted_pos[row * p.k + j];
+        if (pos < 0) continue;
+        const float wj = p.w_local[row * p.k + j];
+        const float2 v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(p.ys + static_cast<int64_t>(pos) * p.H)[e]);
+        acc.x += wj * v.x;
+        acc.y += wj * v.y;
+      }
+      dst[e] = __floats2bfloat162_rn(acc.x, acc.y);
+    }
+  }
+  __threadfence_system();  // this thread's peer stores are visible system-wide before the grid completes
+}
+
 }  // namespace ep
 }  // namespace shk
 
@@ -279,5 +316,15 @@ extern "C" int sh_ep_combine(const EpParams* params, int num_blocks, cudaStream_
   if (params->T == 0) return 0;
   num_blocks = num_blocks < 1 ? 1 : (num_blocks > SH_EP_MAX_BLOCKS ? SH_EP_MAX_BLOCKS : num_blocks);
   shk::launch(ep_combine_kernel, dim3(num_blocks), dim3(kThreads), 0, stream, *params);
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int sh_ep_combine_push(const EpParams* params, int num_blocks, cudaStream_t stream) {
+  const int rc = ep_check(*params);
+  if (rc) return rc;
+  if (!params->ys || !params->sorted_pos || !params->w_local) return -5;
+  if (params->T == 0) return 0;
+  num_blocks = num_blocks < 1 ? 1 : (num_blocks > SH_EP_MAX_BLOCKS ? SH_EP_MAX_BLOCKS : num_blocks);
+  shk::launch(ep_combine_push_kernel, dim3(num_blocks), dim3(kThreads), 0, stream, *params);
   return static_cast<int>(cudaGetLastError());
 }

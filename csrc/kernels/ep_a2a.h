@@ -39,6 +39,13 @@ struct EpParams {
   // route.ids: the combine reads them); `w` is then unused.
   int fused_route;
   RouteParams route;
+  // Combine fused with the experts' weighted per-token sum (sh_ep_combine_push): row r*T + i of the
+  // received rows = sum_j w_local[row, j] * ys[sorted_pos[row * k + j]] (pairs with sorted_pos < 0 skipped),
+  // stored straight into owner r's return rows; sh_ep_combine with pushed = 1 then only meets and sums.
+  const __nv_bfloat16* ys;   // [pairs][H] expert outputs in sorted pair order
+  const int32_t* sorted_pos;  // [world*T][k]
+  const float* w_local;       // [world*T][k] local route weights (0 for other ranks' experts)
+  int pushed;
 };
 
 #ifdef __cplusplus
@@ -47,6 +54,7 @@ extern "C" {
 // Both use the same grid on every rank and for every call of a communicator.
 int sh_ep_dispatch(const EpParams* p, int num_blocks, cudaStream_t stream);
 int sh_ep_combine(const EpParams* p, int num_blocks, cudaStream_t stream);
+int sh_ep_combine_push(const EpParams* p, int num_blocks, cudaStream_t stream);
 #ifdef __cplusplus
 }
 #endif

@@ -156,6 +156,20 @@ def _worker(rank, world, port, q):
                     base = ep.dp_dispatch_combine(mdl, x, ids, w)
                     torch.cuda.synchronize()
                     results[f"route:{mi}:{ri}:{call}"] = (0.0 if torch.equal(got, base) else 1.0, 0.0)
+        # The experts' weighted sum stored straight into the owners' return rows (default) must equal the
+        # local combine + copy (SH_EP_COMBINE_PUSH=0) bit for bit.
+        for mi, (mdl, HH) in enumerate(((moe, H), (moe4, H4))):
+            mdl.route_args = lambda a=routers[1]: a
+            for call, T in enumerate([23, 1]):
+                gi = torch.Generator().manual_seed(900 + 10 * call + rank)
+                x = torch.randn(T, HH, generator=gi).to(torch.bfloat16).cuda()
+                logits = torch.randn(T, E, generator=gi).to(torch.bfloat16).cuda()
+                os.environ["SH_EP_COMBINE_PUSH"] = "0"
+                base = ep.dp_route_dispatch_combine(mdl, x, logits)
+                os.environ["SH_EP_COMBINE_PUSH"] = "1"
+                got = ep.dp_route_dispatch_combine(mdl, x, logits)
+                torch.cuda.synchronize()
+                results[f"push:{mi}:{call}"] = (0.0 if torch.equal(got, base) else 1.0, 0.0)
         from vllm_suffix_hybrid_b200.parallel import ep_a2a
 
         assert any(c.quant for c in ep_a2a._comms.values())

@@ -371,7 +371,7 @@ def moe_route(logits, k: int, sigmoid_grouped: bool = False, bias=None, n_groups
     return ids.int(), (w * scale).float()
 
 
-def moe_experts(x, ids, weights, w13, w2, E: int, F: int, out=None, accumulate: bool = False):
+def moe_experts(x, ids, weights, w13, w2, E: int, F: int, out=None, accumulate: bool = False, push=None):
     """sum_j weights[t, j] * FFN_{ids[t, j]}(x[t]) with SwiGLU experts.
 
     w13: stacked [E*2F, H] (gate rows then up rows per expert), w2: [E*H, F]."""
@@ -416,6 +416,9 @@ def moe_experts(x, ids, weights, w13, w2, E: int, F: int, out=None, accumulate: 
     groups2[:, 2] = groups[:, 3] * H  # down-projection weight row offsets
     ys = torch.empty(pairs, H, dtype=x.dtype, device=dev)
     C.gemm_grouped(ys, a, w2, H, groups2, ngroups, bn)
+    if push is not None:  # the caller's combine takes the per-pair rows (expert-parallel combine push)
+        push(ys, sorted_pos)
+        return None
     if out is None:
         out = torch.empty(T, H, dtype=x.dtype, device=dev)
         accumulate = False
@@ -807,7 +810,7 @@ def mxfp8_linear(x: torch.Tensor, codes: torch.Tensor, w_sf: torch.Tensor, scale
     return y.view(*lead, N)
 
 
-def moe_experts_mxfp8(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
+def moe_experts_mxfp8(x, ids, weights, w13q, w2q, E: int, F: int, out=None, push=None):
     """MoE experts with MXFP8 weights: w13q = (codes [E*2F, H], scales [E*2F, H/32], scale tiles), w2q likewise
     for [E*H, F]; grouped block-scaled W8A8 GEMMs (CPU: fp32 oracle per pair)."""
     T, H = x.shape
@@ -854,13 +857,16 @@ def moe_experts_mxfp8(x, ids, weights, w13q, w2q, E: int, F: int, out=None):
     a = silu_mul(gu)
     xq, x_sf, a_sc = mxfp8_quant_act(a, bn, groups, ngroups)
     C.gemm_fp4mma(ys, xq, x_sf, a_sc, w2q[0], t2, ones, bn, groups2, ngroups, H, fp8=True)
+    if push is not None:
+        push(ys, sorted_pos)
+        return None
     if out is None:
         out = torch.empty(T, H, dtype=x.dtype, device=dev)
     C.moe_combine(out, ys, sorted_pos, weights, False)
     return out
 
 
-def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None, prequant=None):
+def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None, prequant=None, push=None):
     """moe_experts with NVFP4 expert weights: w13q = (packed [E*2F, H/2], scales [E*2F, H/16], global [E],
     optional k-block-major scales, optional block-scaled MMA scale tiles), w2q likewise for [E*H, F].
     The grouped GEMMs run the block-scaled W4A4 tcgen05 kernel on per-token NVFP4 activations (or the
@@ -920,6 +926,9 @@ def moe_experts_nvfp4(x, ids, weights, w13q, w2q, E: int, F: int, out=None, preq
         C.gemm_nvfp4(gu, xs, w13q[0], sk13, w13q[2], bn, groups, ngroups, 2 * F)
         a = silu_mul(gu)
         C.gemm_nvfp4(ys, a, w2q[0], sk2, w2q[2], bn, groups2, ngroups, H)
+    if push is not None:
+        push(ys, sorted_pos)
+        return None
     if out is None:
         out = torch.empty(T, H, dtype=dt, device=dev)
     C.moe_combine(out, ys, sorted_pos, weights, False)

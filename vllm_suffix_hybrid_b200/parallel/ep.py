@@ -98,10 +98,31 @@ def _quant_dispatch(moe, x: torch.Tensor) -> bool:
             and os.environ.get("SH_EP_A2A_FP4", "1") != "0")
 
 
-def _a2a_experts(moe, quant: bool, rows, ids_l: torch.Tensor, w_l: torch.Tensor) -> torch.Tensor:
-    if quant:  # NVFP4 rows: the W4A4 experts gather the received codes directly
-        return ops.moe_experts_nvfp4(None, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F, prequant=rows)
-    return _experts(moe, rows, ids_l, w_l)
+def _a2a_experts_combine(moe, comm, quant: bool, rows, ids_l: torch.Tensor, w_l: torch.Tensor,
+                         ids: torch.Tensor) -> torch.Tensor:
+    """Experts over the received rows, then the combine.  By default the experts' weighted per-token sum
+    stores its rows straight into the owners' return rows (one launch, no local output; bit-identical);
+    SH_EP_COMBINE_PUSH=0 writes the local output and lets ep_combine copy it."""
+    if os.environ.get("SH_EP_COMBINE_PUSH", "1") == "0":
+        if quant:  # NVFP4 rows: the W4A4 experts gather the received codes directly
+            y = ops.moe_experts_nvfp4(None, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F, prequant=rows)
+        else:
+            y = _experts(moe, rows, ids_l, w_l)
+        return comm.combine(y, ids)
+    T = ids.shape[0]
+
+    def push(ys, sorted_pos):
+        comm.combine_push(ys, sorted_pos, w_l, ids_l, T)
+
+    if quant:
+        ops.moe_experts_nvfp4(None, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F, prequant=rows, push=push)
+    elif moe.fp4 is not None:
+        ops.moe_experts_nvfp4(rows, ids_l, w_l, moe.fp4[0], moe.fp4[1], moe.E_local, moe.F, push=push)
+    elif getattr(moe, "fp8", None) is not None:
+        ops.moe_experts_mxfp8(rows, ids_l, w_l, moe.fp8[0], moe.fp8[1], moe.E_local, moe.F, push=push)
+    else:
+        ops.moe_experts(rows, ids_l, w_l, moe.w13, moe.w2, moe.E_local, moe.F, push=push)
+    return comm.combine_sum(ids)
 
 
 def dp_route_dispatch_combine(moe, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
@@ -112,7 +133,7 @@ def dp_route_dispatch_combine(moe, x: torch.Tensor, logits: torch.Tensor) -> tor
     quant = _quant_dispatch(moe, x)
     comm = ep_a2a.get(x.shape[1], A2A_MAX_TOKENS, moe.k, moe.E_local, quant)
     rows, ids_l, w_l, ids, _ = comm.dispatch_routed(x, logits, **moe.route_args())
-    return comm.combine(_a2a_experts(moe, quant, rows, ids_l, w_l), ids)
+    return _a2a_experts_combine(moe, comm, quant, rows, ids_l, w_l, ids)
 
 
 def dp_dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -126,7 +147,7 @@ def dp_dispatch_combine(moe, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor
         quant = _quant_dispatch(moe, x)
         comm = ep_a2a.get(x.shape[1], A2A_MAX_TOKENS, ids.shape[1], moe.E_local, quant)
         rows, ids_l, w_l = comm.dispatch(x, ids, w)
-        return comm.combine(_a2a_experts(moe, quant, rows, ids_l, w_l), ids)
+        return _a2a_experts_combine(moe, comm, quant, rows, ids_l, w_l, ids)
     xs = _all_gather(x)
     ids_a = _all_gather(ids)
     w_a = _all_gather(w)

@@ -10,7 +10,9 @@ experts.  One MoE call:
    bytes); the receiving expert GEMMs gather the codes straight into their operand layout.  With
    ``dispatch_routed`` the kernel also runs the router top-k of each token from its logits;
 2. this rank's grouped expert GEMMs over the received ``[world*T, H]`` rows;
-3. ``ep_combine``: the expert outputs go back to the token owners, which sum them in rank order.
+3. ``ep_combine``: the expert outputs go back to the token owners, which sum them in rank order.  By
+   default the experts' weighted per-token sum (``ep_combine_push``) stores its rows straight into the
+   owners' return rows, and the owners only meet and sum (``ep_combine_sum``).
 
 This replaces the NCCL all-gather of every token to every rank + reduce-scatter of the partials
 (``parallel/ep.py`` ``dp_dispatch_combine`` with ``SH_EP_A2A=0``): a row crosses NVLink only to the
@@ -127,6 +129,22 @@ class EpA2A:
         T = ids.shape[0]
         out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=y.device)
         ops.native().ep_combine(y.contiguous(), ids.to(torch.int32).contiguous(), out, *self._args())
+        return out
+
+    def combine_push(self, ys: torch.Tensor, sorted_pos: torch.Tensor, w_l: torch.Tensor, ids_l: torch.Tensor,
+                     T: int) -> None:
+        """The experts' weighted per-token sum of the received rows (ys [pairs, H] per sorted pair), stored
+        straight into the owners' return rows; finish with combine_sum."""
+        from .. import ops
+
+        ops.native().ep_combine_push(ys, sorted_pos, w_l.contiguous(), ids_l, T, *self._args())
+
+    def combine_sum(self, ids: torch.Tensor) -> torch.Tensor:
+        """[T, H] sums of the rows combine_push returned to this rank, in rank order."""
+        from .. import ops
+
+        out = torch.empty(ids.shape[0], self.hidden, dtype=torch.bfloat16, device=ids.device)
+        ops.native().ep_combine_sum(ids.to(torch.int32).contiguous(), out, *self._args())
         return out
 
     def check(self) -> None:
