@@ -142,7 +142,18 @@ std::vector<std::vector<int64_t>> to_token_lists(const py::handle& obj) {
 
 // Request ids: zero-copy UTF-8 views into the caller's str objects (valid
 // for the duration of the call; the caller's list keeps them alive).
-void to_ids_into(const py::handle& obj, py::list* keep, std::vector<std::string_view>& ids) {
+// Owns the sequences PySequence_Fast returns while one call uses views into
+// them (a few per call; no Python allocation, unlike a list).
+struct Keep {
+  py::object objs[4];
+  int n = 0;
+  void append(py::object o) {
+    if (n >= 4) throw std::runtime_error("internal: too many kept sequences");
+    objs[n++] = std::move(o);
+  }
+};
+
+void to_ids_into(const py::handle& obj, Keep* keep, std::vector<std::string_view>& ids) {
   PyObject* seq = PySequence_Fast(obj.ptr(), "request ids must be a sequence of str");
   if (!seq) throw py::error_already_set();
   const Py_ssize_t n = PySequence_Fast_GET_SIZE(seq);
@@ -164,7 +175,7 @@ void to_ids_into(const py::handle& obj, py::list* keep, std::vector<std::string_
   keep->append(py::reinterpret_steal<py::object>(seq));
 }
 
-std::vector<std::string_view> to_ids(const py::handle& obj, py::list* keep) {
+std::vector<std::string_view> to_ids(const py::handle& obj, Keep* keep) {
   std::vector<std::string_view> ids;
   to_ids_into(obj, keep, ids);
   return ids;
@@ -194,7 +205,7 @@ struct DraftRows {
 
 // Fills `out` in place: its vectors keep their capacity across calls, so a
 // warm call allocates nothing for the draft rows.
-void to_draft_rows(const py::handle& obj, py::list* keep, DraftRows& out) {
+void to_draft_rows(const py::handle& obj, Keep* keep, DraftRows& out) {
   PyObject* seq = PySequence_Fast(obj.ptr(), "native drafts must be a sequence of token lists");
   if (!seq) throw py::error_already_set();
   keep->append(py::reinterpret_steal<py::object>(seq));
@@ -384,7 +395,7 @@ PYBIND11_MODULE(_native, m) {
           [](HybridMixer& x, py::handle request_ids, py::handle contexts, py::handle native_drafts,
              py::object accepted_lengths, py::object step_time_ns) {
             (void)step_time_ns;
-            py::list keep;
+            Keep keep;
             DraftRows& nat = draft_scratch();
             const auto& drafts = guard("mix", [&]() -> const std::vector<std::vector<int64_t>>& {
               std::vector<std::string_view> ids = to_ids(request_ids, &keep);
@@ -404,7 +415,7 @@ PYBIND11_MODULE(_native, m) {
           [](HybridMixer& x, py::handle request_ids, py::handle counts, py::handle tokens, py::handle native_drafts,
              py::object accepted_lengths, py::object step_time_ns) {
             (void)step_time_ns;
-            py::list keep;
+            Keep keep;
             DraftRows& nat = draft_scratch();
             static thread_local std::vector<std::string_view> ids;
             static thread_local std::vector<int64_t> acc;
@@ -455,7 +466,7 @@ PYBIND11_MODULE(_native, m) {
           "propose_suffix_only",
           [](V2SuffixProposer& p, py::handle request_ids, py::handle indices, py::handle totals, py::handle tokens) {
             const uint64_t t0 = now_ns();
-            py::list keep;
+            Keep keep;
             std::vector<int64_t> packed, widths;
             size_t n = 0;
             guard("propose_suffix_only", [&] {
