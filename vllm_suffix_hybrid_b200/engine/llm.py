@@ -435,13 +435,13 @@ class LLMEngine:
         elif method == "suffix":
             packed, widths = self.proposer.propose_suffix_only(ids, np.arange(n, dtype=np.int64), counts,
                                                                self.tokens)
-            drafts = [list(packed[i, : widths[i]]) for i in range(n)]
+            drafts = [packed[i, : widths[i]].tolist() for i in range(n)]
         elif method == "external":
             drafts = self.external_proposer(self.running) if self.external_proposer else [[] for _ in range(n)]
         else:  # ngram
             drafts = self.proposer.propose([[1]] * n, counts, self.tokens)
-        for r, d in zip(self.running, drafts):
-            r.drafts = [int(x) for x in d]
+        for r, d in zip(self.running, drafts):  # the native proposers return fresh lists of Python ints
+            r.drafts = d if type(d) is list else [int(x) for x in d]
         return (time.perf_counter_ns() - t0) / 1e3
 
     def _decode_step(self, nb_min: int = 0) -> StepStats:
