@@ -59,6 +59,7 @@ class Request:
     max_new_tokens: int
     output: List[int] = field(default_factory=list)
     blocks: List[int] = field(default_factory=list)
+    blocks_np: np.ndarray = field(default_factory=lambda: np.zeros(0, dtype=np.int32))  # int32 mirror of blocks
     committed: int = 0  # KV positions written and verified
     next_token: int = -1  # bonus token waiting for the next window
     drafts: List[int] = field(default_factory=list)
@@ -353,6 +354,8 @@ class LLMEngine:
         need = blocks_for(upto_tokens, self.block_size) - len(r.blocks)
         if need > 0:
             r.blocks.extend(self.pool.allocate(need))
+        if r.blocks_np.shape[0] != len(r.blocks):  # the block-table row the decode steps copy
+            r.blocks_np = np.asarray(r.blocks, dtype=np.int32)
 
     def _select_prefill(self, free_rows: int) -> list:
         batch, budget = [], self.cfg.max_prefill_tokens
@@ -457,13 +460,14 @@ class LLMEngine:
         slots = np.fromiter((r.slot for r in self.running), dtype=np.int64, count=n)
         for i, r in enumerate(self.running):
             self._ensure_blocks(r, r.committed + 2 * k + 2)
-            win[i, 0] = r.next_token
-            d = r.drafts[:k]
-            win[i, 1:1 + len(d)] = d
-            if len(d) < k:
-                win[i, 1 + len(d):] = -1
-            seq[i] = r.committed
-            bt[i, :len(r.blocks)] = r.blocks
+            b = r.blocks_np
+            bt[i, :b.shape[0]] = b
+        if n:
+            win[:, 0] = np.fromiter((r.next_token for r in self.running), dtype=np.int64, count=n)
+            seq[:] = np.fromiter((r.committed for r in self.running), dtype=np.int64, count=n)
+            if k:
+                win[:, 1:] = [r.drafts[:k] if len(r.drafts) >= k else r.drafts + [-1] * (k - len(r.drafts))
+                              for r in self.running]
         t1 = time.perf_counter()
         out, acc, nat = self.runner.decode(n, win, seq, bt, slots, nb_min=nb_min)
         t2 = time.perf_counter()
@@ -553,7 +557,8 @@ class LLMEngine:
         slots = np.fromiter((r.slot for r in self.running), dtype=np.int64, count=n)
         for i, r in enumerate(self.running):
             self._ensure_blocks(r, r.committed + 2 * k + 2 + 2 * self._lag)
-            bt[i, :len(r.blocks)] = r.blocks
+            b = r.blocks_np
+            bt[i, :b.shape[0]] = b
         if self._pipe is None:  # pipeline start: host window (drafts from the synchronous proposer)
             win = np.full((n, W), -1, dtype=np.int64)
             seq = np.fromiter((r.committed for r in self.running), dtype=np.int64, count=n)
