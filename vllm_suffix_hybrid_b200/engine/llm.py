@@ -473,16 +473,18 @@ class LLMEngine:
         t2 = time.perf_counter()
         emitted = 0
         accepted = 0
+        acc_l, out_l = acc[:n].tolist(), out[:n].tolist()  # one conversion per step, not per row
+        nat_l = nat[:n, :k].tolist() if self.draft is not None and k > 0 else None
         for i, r in enumerate(self.running):
-            a = int(acc[i])
-            toks = out[i, : a + 1].tolist()
+            a = acc_l[i]
+            toks = out_l[i][: a + 1]
             r.committed += a + 1
             r.accepted_prev = a
             self._emit(r, i, toks)
             emitted += min(a + 1, len(toks))
             accepted += a
-            if self.draft is not None and k > 0:
-                r.drafts = nat[i, :k].tolist()
+            if nat_l is not None:
+                r.drafts = nat_l[i]
         prop_us = self._propose(batch_native=False)
         self._retire()
         t3 = time.perf_counter()
