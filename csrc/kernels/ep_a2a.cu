@@ -257,6 +257,10 @@ __global__ void __launch_bounds__(kThreads) ep_combine_kernel(EpParams p) {
 __global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(EpParams p) {
   shk::pdl_trigger();
   shk::pdl_wait();
+  // A dispatch barrier of this call that timed out leaves the peers' state
+  // unknown (one may still be reading the previous call's return rows):
+  // store nothing into peer memory then.  The error is already recorded.
+  if (p.err && *reinterpret_cast<volatile const int*>(p.err) != 0) return;
   const int64_t T = p.T;
   const int32_t* my_ids = p.peer_ids[p.rank];
   for (int64_t row = blockIdx.x; row < static_cast<int64_t>(p.world) * T; row += gridDim.x) {

@@ -584,7 +584,10 @@ extern "C" int sh_paged_attention(const AttnParams* params, int ntiles, int num_
 // until the process exits.  Its device address is looked up with
 // cudaGetSymbolAddress on the first call made on each device (with that
 // device current); make that first call before any CUDA-graph stream
-// capture.  Every call reuses the same array: calls that overlap on the GPU
+// capture.  The address is cached together with the device's current
+// context: after a cudaDeviceReset the module is loaded again in a new
+// context, the change is seen and the address is looked up again (that
+// lookup is again a first call: keep it outside a capture).  Every call reuses the same array: calls that overlap on the GPU
 // (two streams, two threads) race on it and must be serialised by the
 // caller.  Nothing in it needs to start at zero -- every partial slot the
 // merge reads is written earlier in the same call.
@@ -596,15 +599,22 @@ __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kMaxDevices] = {};
+CUcontext g_noalloc_ctx[kMaxDevices] = {};
 
 int noalloc_scratch(float** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return SH_NOALLOC_ERR_DEVICE;
+  // The context may not exist yet before the first lookup (the runtime
+  // creates it lazily), so it is read again after cudaGetSymbolAddress.
+  CUcontext ctx = nullptr;
+  (void)cuCtxGetCurrent(&ctx);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || ctx == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return SH_NOALLOC_ERR_SYMBOL;
+    if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS || ctx == nullptr) return SH_NOALLOC_ERR_SYMBOL;
     g_noalloc_ptr[dev] = static_cast<float*>(p);
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return 0;
@@ -620,14 +630,15 @@ extern "C" __attribute__((visibility("default"))) int sh_paged_attention_noalloc
                                                                                    int max_rows, cudaStream_t stream) {
   if (params == nullptr) return SH_NOALLOC_ERR_ARGS;
   AttnParams p = *params;
-  if (p.nsplit < 1 || head_dim <= 0) return SH_NOALLOC_ERR_ARGS;
+  if (p.nsplit < 1 || head_dim <= 0 || p.hq <= 0 || p.num_tokens < 0) return SH_NOALLOC_ERR_ARGS;
   p.part_o = nullptr;
   p.part_ml = nullptr;
   if (p.nsplit > 1) {
-    // Partials: [rows * nsplit, head_dim] then [rows * nsplit, 2] floats.
-    const int64_t slots = p.num_tokens * p.hq * p.nsplit;
-    const int64_t need = slots * (head_dim + 2);
-    if (p.num_tokens < 0 || slots < 0 || need > kNoAllocFloats) return SH_NOALLOC_ERR_TOO_LARGE;
+    // Partials: [rows * nsplit, head_dim] then [rows * nsplit, 2] floats.  The
+    // bound is checked by division first, so no product below can overflow.
+    const int64_t per_token = static_cast<int64_t>(p.hq) * p.nsplit * (head_dim + 2);
+    if (static_cast<int64_t>(p.num_tokens) > kNoAllocFloats / per_token) return SH_NOALLOC_ERR_TOO_LARGE;
+    const int64_t slots = static_cast<int64_t>(p.num_tokens) * p.hq * p.nsplit;
     float* base = nullptr;
     const int r = noalloc_scratch(&base);
     if (r) return r;

@@ -1,4 +1,14 @@
-"""Hybrid mixer (legacy split): learned native budget + conditioned suffix tail."""
+"""Hybrid mixer (legacy split): learned native budget + conditioned suffix tail.
+
+Conformance data.  The first nine tests (fresh row .. cache tokens on
+departure) restate cases of the reference's own mixer suite
+(reference: tests/test_mixer.py:6-110) with the same literal token
+vectors, so this implementation and the reference give the same drafts and
+counters on the same inputs; they are kept as a conformance table, not as
+independent design.  The tests after them (incremental NumPy rows, id
+reuse, shrinking rows, boundary windows, int32 rows, default split) and the
+randomized tests in test_mixer_diverge.py are this package's own.
+"""
 import os
 
 import numpy as np

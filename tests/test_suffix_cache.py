@@ -1,4 +1,13 @@
-"""Suffix corpus semantics: lookup, back-extension, voting, caps, eviction."""
+"""Suffix corpus semantics: lookup, back-extension, voting, caps, eviction.
+
+Conformance data.  The tests from the empty corpus through the lookback
+window, plus the tuple/NumPy input and concurrency tests, restate cases of
+the reference's corpus suite (reference: tests/test_suffix_cache.py:31-180)
+with its literal token vectors, so both implementations agree on the same
+inputs; they form a conformance table.  The token-budget, churn,
+positions-cap and re-index tests and the randomized comparison against a
+Python oracle of the documented semantics are this package's own.
+"""
 import os
 import threading
 

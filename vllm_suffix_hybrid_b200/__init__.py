@@ -14,7 +14,10 @@ Layers (bottom up):
 * ``engine``    -- config, weight loading, paged KV cache, scheduler, model
   runner, speculative-decoding loop.
 * ``proposer``  -- Python surface of the proposer (HybridProposer ABI).
-* ``serving``   -- OpenAI-style HTTP server and warm-start endpoint.
+* ``serve``     -- OpenAI-style HTTP server, async engine front end, warm-start,
+  SFT and decider routes.
+* ``tune``      -- online MTP-head tuning and in-place SFT of the served model.
+* ``bench``     -- microbenchmarks of the kernels, comm paths and proposer.
 """
 
 __version__ = "0.3.0"

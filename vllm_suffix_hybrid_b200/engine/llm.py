@@ -441,6 +441,10 @@ class LLMEngine:
             drafts = [packed[i, : widths[i]].tolist() for i in range(n)]
         elif method == "external":
             drafts = self.external_proposer(self.running) if self.external_proposer else [[] for _ in range(n)]
+            # A caller's lists may be reused or mutated later and may hold NumPy ints: copy them.
+            for r, d in zip(self.running, drafts):
+                r.drafts = [int(x) for x in d]
+            return (time.perf_counter_ns() - t0) / 1e3
         else:  # ngram
             drafts = self.proposer.propose([[1]] * n, counts, self.tokens)
         for r, d in zip(self.running, drafts):  # the native proposers return fresh lists of Python ints

@@ -1,54 +1,76 @@
-"""Weight-free custom-class proposer (suffix corpus + in-request n-gram).
+"""vLLM custom-class drafter backed by the native weight-free Engine.
 
-Same positional contract as the reference's custom-class proposer
+The class keeps the reference's constructor and call signature, so a vLLM
+speculative config that names it as ``custom_class`` works unchanged
 (reference: suffix_hybrid/hybrid_proposer.py:22-55):
-``propose(sampled_token_ids, num_tokens_no_spec, token_ids_cpu, *,
-slot_mappings=None)``.  The CPU rows already contain the sampled tokens; the
-native Engine reads them in place.  Telemetry: a JSON stats line every
-``SUFFIX_HYBRID_LOG_INTERVAL`` calls and, when ``SUFFIX_HYBRID_STATS_FILE``
-is set, a JSONL record every ``SUFFIX_HYBRID_STATS_INTERVAL`` calls.
+
+    HybridProposer(vllm_config)
+    propose(sampled_token_ids, num_tokens_no_spec, token_ids_cpu, *, slot_mappings=None)
+        -> list[list[int]]       one draft (possibly empty) per batch row
+
+Everything behind the signature is this package's own: the C++ ``Engine``
+(row identity, suffix corpus, in-request n-gram index) does the work, and
+``engine.telemetry.CallTelemetry`` owns the stats-line / JSONL cadence.
+``token_ids_cpu`` rows already hold the sampled tokens; ``sampled_token_ids``
+is only read for which rows sampled anything this step.  ``slot_mappings``
+is accepted for interface compatibility and unused (the proposer is host
+only).
 """
-import json
+from __future__ import annotations
+
 import logging
-import os
 import time
 
 from vllm_suffix_hybrid_b200._native import VERSION, Engine
+from vllm_suffix_hybrid_b200.engine.telemetry import CallTelemetry
 
 logger = logging.getLogger("suffix_hybrid")
+
+_DEFAULT_K = 8
+_DEFAULT_MAX_LEN = 32768
+
+
+def _shape_from_config(vllm_config):
+    """(draft length k, max context length) from a vLLM-style config object, with defaults."""
+    spec = getattr(vllm_config, "speculative_config", None)
+    model = getattr(vllm_config, "model_config", None)
+    k = getattr(spec, "num_speculative_tokens", None)
+    max_len = getattr(model, "max_model_len", None)
+    k = _DEFAULT_K if k is None else k
+    max_len = _DEFAULT_MAX_LEN if max_len is None else max_len
+    return int(k), int(max_len)
 
 
 class HybridProposer:
     def __init__(self, vllm_config=None):
-        spec = getattr(vllm_config, "speculative_config", None)
-        model = getattr(vllm_config, "model_config", None)
-        self._engine = Engine(getattr(spec, "num_speculative_tokens", 8),
-                              getattr(model, "max_model_len", 32768))
-        self.suffix_cache = self._engine.suffix_cache
-        self.num_speculative_tokens = self._engine.num_speculative_tokens
-        self.use_ngram = self._engine.use_ngram
-        self.stats_file = os.environ.get("SUFFIX_HYBRID_STATS_FILE", "").strip()
-        logger.info("suffix_hybrid version=%s backend=native-cpp", VERSION)
+        k, max_len = _shape_from_config(vllm_config)
+        self._engine = Engine(k, max_len)
+        self._telemetry = CallTelemetry.from_env(self._engine.get_stats, self._engine.record_total)
+        logger.info("suffix_hybrid %s: native C++ proposer, k=%d, max_model_len=%d", VERSION,
+                    self._engine.num_speculative_tokens, max_len)
+
+    # Attributes a vLLM drafter wrapper reads.
+    @property
+    def suffix_cache(self):
+        return self._engine.suffix_cache
+
+    @property
+    def num_speculative_tokens(self) -> int:
+        return self._engine.num_speculative_tokens
+
+    @property
+    def use_ngram(self) -> bool:
+        return self._engine.use_ngram
+
+    @property
+    def stats_file(self) -> str:
+        return self._telemetry.stats_file
 
     def propose(self, sampled_token_ids, num_tokens_no_spec, token_ids_cpu, *, slot_mappings=None):
-        started = time.perf_counter_ns()
+        t0 = time.perf_counter_ns()
         drafts = self._engine.propose(sampled_token_ids, num_tokens_no_spec, token_ids_cpu)
-        elapsed = time.perf_counter_ns() - started
-        log_due, stats_due = self._engine.record_total(elapsed)
-        if log_due or (stats_due and self.stats_file):
-            stats = self.get_stats()
-            stats["ts"] = time.time()
-            line = json.dumps(stats, sort_keys=True)
-            if log_due:
-                logger.info("suffix_hybrid %s", line)
-            if stats_due and self.stats_file:
-                try:
-                    with open(self.stats_file, "a", encoding="utf-8") as stream:
-                        stream.write(line + "\n")
-                except OSError:
-                    logger.exception("suffix_hybrid cannot write telemetry")
-            self._engine.record_total(time.perf_counter_ns() - started - elapsed)
+        self._telemetry.after_call(time.perf_counter_ns() - t0)
         return drafts
 
-    def get_stats(self):
+    def get_stats(self) -> dict:
         return self._engine.get_stats()
