@@ -8,7 +8,10 @@ span-reuse structure, vocab 128256), up to 512 output tokens each.  On N GPUs
 the model runs tensor-parallel over N ranks (one process per GPU, NCCL).
 
 Timed region: K decode steps after W warm-up steps, bracketed by a barrier
-and a device synchronize.  `value` is output tokens / summed device time of
+and a device synchronize.  Before the warm-up the generation is advanced
+(untimed) so that the W + K steps are centred on the middle of the
+max-new-token generation: the timed steps see the mean context length of the
+run, not the shortest one right after prefill.  `value` is output tokens / summed device time of
 the steps (CUDA events from the H2D of a step's inputs to the D2H of its
 results, max over ranks).  `e2e` is the same tokens over the wall clock of
 the K `LLMEngine.step()` calls, which include the host proposer, the H2D of
@@ -86,6 +89,9 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--max-new", type=int, default=512)
     ap.add_argument("--k", type=int, default=5)
+    ap.add_argument("--timed-from", type=int, default=-1,
+                    help="generated tokens per request before the warm-up steps start (default: the timed window "
+                         "is centred on the middle of the max-new-token generation, the mean context length)")
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="TP collectives: own NVLink kernels (fused) or the NCCL baseline")
@@ -138,6 +144,14 @@ def main():
         if world > 1:
             dist.barrier(group=st.cpu_group)
 
+    # Untimed decode up to the start of the window: attention cost grows with the context, so the timed
+    # steps sit around the middle of the generation instead of right after prefill.  Every rank runs the
+    # same steps (the engine state is replicated), so the loop ends on the same step everywhere.
+    start_at = args.timed_from if args.timed_from >= 0 else max(0, args.max_new // 2 - (args.warmup + args.steps) // 2)
+    advanced = 0
+    while eng.running and min(len(r.output) for r in eng.running) < start_at:
+        eng.step()
+        advanced += 1
     for _ in range(args.warmup):
         eng.step()
     if args.profile:
@@ -166,6 +180,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     first = len(eng.stats)
+    ctx0 = min(len(r.prompt) + len(r.output) for r in eng.running) if eng.running else 0
     t0 = time.perf_counter()
     dev_ms = 0.0
     h2d = d2h = 0
@@ -212,6 +227,7 @@ def main():
                        "l2": "working set (weights + KV) >> 126 MB L2; no flush",
                        "layers": mcfg.layers},
             "mean_accept_len": round(tokens / rows, 4),
+            "timed_window": {"untimed_steps_before_warmup": advanced, "min_context_at_first_timed_step": ctx0},
             "proposer_us_per_step": round(prop_us, 2),
             "prefill_s": round(prefill_s, 2),
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d // args.steps,

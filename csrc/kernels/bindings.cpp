@@ -108,6 +108,73 @@ void gemm_bf16(torch::Tensor y, torch::Tensor x, torch::Tensor w, bool swap, int
   TORCH_CHECK(r == 0, pair ? "sh_gemm_bf16_pair" : "sh_gemm_bf16_tcgen05", " failed with code ", r);
 }
 
+// Limit of every cross-rank wait of the comm and EP kernels launched from here
+// (ns; 0 = each kernel's default of 5 s).  set_wait_ns changes it for the
+// process: serving keeps the default, tests shorten it to make a wait run out.
+static unsigned long long g_wait_ns = 0;
+void set_wait_ns(int64_t ns) { g_wait_ns = ns > 0 ? static_cast<unsigned long long>(ns) : 0ull; }
+int64_t get_wait_ns() { return static_cast<int64_t>(g_wait_ns); }
+
+// y[M, N] = x[M, K] @ w[N, K]^T via the stream-K CTA-pair kernel (weights on
+// the MMA M side, ns*nsub tokens per tile).  ws / cnt: see sh_gemm_bf16_sk.
+void gemm_bf16_sk(torch::Tensor y, torch::Tensor x, torch::Tensor w, int64_t ns, int64_t nsub, int64_t clusters,
+                  torch::Tensor ws, torch::Tensor cnt, c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && y.is_cuda() && ws.is_cuda() && cnt.is_cuda(), "gemm_bf16_sk: CUDA tensors");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
+              "gemm_bf16_sk: bf16 tensors");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && y.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 && y.stride(1) == 1,
+              "gemm_bf16_sk: row-major 2-D operands");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && y.size(0) == M && y.size(1) == N, "gemm_bf16_sk: shape mismatch");
+  int64_t tiles = 0, need = 0;
+  TORCH_CHECK(sh_gemm_sk_shape(static_cast<int>(N), static_cast<int>(M), static_cast<int>(K), static_cast<int>(ns),
+                               static_cast<int>(nsub), static_cast<int>(clusters), &tiles, &need) == 0,
+              "gemm_bf16_sk: bad shape");
+  TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= need, "gemm_bf16_sk: workspace too small");
+  TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.numel() >= 2 * tiles, "gemm_bf16_sk: counter array too small");
+  int* errp = err.has_value() ? err->data_ptr<int>() : nullptr;
+  const int r = sh_gemm_bf16_sk(w.data_ptr(), static_cast<int>(N), w.stride(0), x.data_ptr(), static_cast<int>(M),
+                                x.stride(0), static_cast<int>(K), y.data_ptr(), y.stride(0), static_cast<int>(ns),
+                                static_cast<int>(nsub), static_cast<int>(clusters), ws.data_ptr<float>(),
+                                cnt.data_ptr<int>(), errp, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_gemm_bf16_sk failed with code ", r);
+}
+
+int64_t gemm_sk_max_clusters(int64_t ns, int64_t nsub) {
+  return sh_gemm_sk_max_clusters(static_cast<int>(ns), static_cast<int>(nsub));
+}
+
+// Vocab-parallel greedy argmax over NVLink peer memory (one kernel; see ArgmaxParams).
+void argmax_tp(torch::Tensor out, torch::Tensor logits, std::vector<int64_t> peer_keys,
+               std::vector<int64_t> peer_flags, torch::Tensor counters, torch::Tensor err, int64_t rank,
+               int64_t max_T, int64_t vocab_offset, int64_t num_blocks) {
+  const int world = static_cast<int>(peer_keys.size());
+  TORCH_CHECK(world >= 1 && world <= SH_COMM_MAX_WORLD && peer_flags.size() == peer_keys.size(), "argmax_tp: peers");
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1,
+              "argmax_tp: bf16 logits [T, V_local]");
+  TORCH_CHECK(out.scalar_type() == at::kLong && out.is_contiguous() && out.numel() == logits.size(0), "argmax_tp: out");
+  TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= SH_COMM_MAX_BLOCKS, "argmax_tp: counters");
+  ArgmaxParams p{};
+  p.logits = reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr());
+  p.ld = logits.stride(0);
+  for (int i = 0; i < world; ++i) {
+    p.peer_keys[i] = reinterpret_cast<unsigned long long*>(peer_keys[i]);
+    p.peer_flags[i] = reinterpret_cast<uint32_t*>(peer_flags[i]);
+  }
+  p.counters = reinterpret_cast<uint32_t*>(counters.data_ptr<int>());
+  p.out = out.data_ptr<int64_t>();
+  p.err = err.data_ptr<int>();
+  p.rank = static_cast<int>(rank);
+  p.world = world;
+  p.T = static_cast<int>(logits.size(0));
+  p.V_local = static_cast<int>(logits.size(1));
+  p.max_T = static_cast<int>(max_T);
+  p.vocab_offset = vocab_offset;
+  p.wait_ns = g_wait_ns;
+  const int r = sh_argmax_tp(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_argmax_tp failed with code ", r);
+}
+
 // Fused NVLink all-reduce (+ residual add + RMSNorm).  peer_* are device
 // addresses (ints) of every rank's symmetric receive / gather buffers and
 // flag arrays; `partial` is this rank's [T, H] partial in local memory.
@@ -155,6 +222,7 @@ void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std:
   }
   p.prefetch = reinterpret_cast<const void*>(prefetch_ptr);
   p.prefetch_bytes = static_cast<unsigned long long>(prefetch_bytes > 0 ? prefetch_bytes : 0);
+  p.wait_ns = g_wait_ns;
   const int r = sh_allreduce(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_allreduce failed with code ", r);
 }
@@ -232,6 +300,7 @@ void rs_norm_ag(int64_t recv, std::vector<int64_t> peer_gather, std::vector<int6
   if (timing.has_value()) p.timing = reinterpret_cast<unsigned long long*>(timing->data_ptr<int64_t>());
   p.prefetch = reinterpret_cast<const void*>(prefetch_ptr);
   p.prefetch_bytes = static_cast<unsigned long long>(prefetch_bytes > 0 ? prefetch_bytes : 0);
+  p.wait_ns = g_wait_ns;
   const int r = sh_rs_norm_ag(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_rs_norm_ag failed with code ", r);
 }
@@ -616,6 +685,7 @@ static EpParams ep_params(torch::Tensor ids, std::vector<int64_t> peer_x, std::v
   p.H = static_cast<int>(H);
   p.e_local = static_cast<int>(e_local);
   p.max_T = static_cast<int>(max_T);
+  p.wait_ns = g_wait_ns;
   return p;
 }
 
@@ -863,6 +933,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("two_shot"), py::arg("num_blocks"), py::arg("timing") = py::none(), py::arg("prefetch_ptr") = 0,
         py::arg("prefetch_bytes") = 0);
   m.def("gemm_bf16_push", &gemm_bf16_push);
+  m.def("set_wait_ns", &set_wait_ns, "limit of every cross-rank wait of the comm / EP kernels (ns, 0 = 5 s)");
+  m.def("get_wait_ns", &get_wait_ns);
+  m.def("argmax_tp", &argmax_tp, "vocab-parallel greedy argmax over NVLink peer memory", py::arg("out"),
+        py::arg("logits"), py::arg("peer_keys"), py::arg("peer_flags"), py::arg("counters"), py::arg("err"),
+        py::arg("rank"), py::arg("max_T"), py::arg("vocab_offset"), py::arg("num_blocks"));
   m.def("rs_norm_ag", &rs_norm_ag, py::arg("recv"), py::arg("peer_gather"), py::arg("peer_gather_res"),
         py::arg("peer_flags"), py::arg("rs_cnt"), py::arg("targets"), py::arg("counters"), py::arg("residual"),
         py::arg("out"), py::arg("weight"), py::arg("err"), py::arg("rank"), py::arg("T"), py::arg("H"),
@@ -902,6 +977,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped);
   m.def("nvfp4_dequant", &nvfp4_dequant);
   m.def("nvfp4_quant", &nvfp4_quant);
+  m.def("gemm_bf16_sk", &gemm_bf16_sk, "stream-K tcgen05 CTA-pair linear", py::arg("y"), py::arg("x"), py::arg("w"),
+        py::arg("ns"), py::arg("nsub"), py::arg("clusters"), py::arg("ws"), py::arg("cnt"),
+        py::arg("err") = py::none());
+  m.def("gemm_sk_max_clusters", &gemm_sk_max_clusters, "co-resident CTA pairs of the stream-K kernel",
+        py::arg("ns"), py::arg("nsub"));
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM", py::arg("y"), py::arg("x"), py::arg("w"), py::arg("swap"),
         py::arg("bn"), py::arg("splits"), py::arg("ws") = py::none(), py::arg("err") = py::none(), py::arg("pair") = false);
 }

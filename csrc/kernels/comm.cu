@@ -57,7 +57,8 @@ __device__ __forceinline__ uint32_t* flag_slot(uint32_t* pad, int phase, int blo
 
 // Cross-rank barrier between same-index blocks. Returns false on timeout.
 __device__ bool barrier_flags(uint32_t* const* peer_flags, int world, int rank, int* err, int phase, uint32_t epoch,
-                              volatile int* bail) {
+                              volatile int* bail, unsigned long long wait_ns) {
+  const uint64_t limit = wait_ns ? wait_ns : kTimeoutNs;
   __syncthreads();
   if (threadIdx.x < world) {
     // st.release orders every store the block made before the bar.sync above
@@ -68,7 +69,7 @@ __device__ bool barrier_flags(uint32_t* const* peer_flags, int world, int rank, 
     const uint32_t* f = flag_slot(peer_flags[rank], phase, blockIdx.x, threadIdx.x);
     const uint64_t t0 = now_ns();
     while (static_cast<int32_t>(ld_acquire(f) - epoch) < 0) {
-      if (*bail || now_ns() - t0 > kTimeoutNs) {
+      if (*bail || now_ns() - t0 > limit) {
         *bail = 1;
         if (err) atomicCAS(err, 0, 100 + phase);
         break;
@@ -80,7 +81,7 @@ __device__ bool barrier_flags(uint32_t* const* peer_flags, int world, int rank, 
 }
 
 __device__ __forceinline__ bool barrier(const ArParams& p, int phase, uint32_t epoch, volatile int* bail) {
-  return barrier_flags(p.peer_flags, p.world, p.rank, p.err, phase, epoch, bail);
+  return barrier_flags(p.peer_flags, p.world, p.rank, p.err, phase, epoch, bail, p.wait_ns);
 }
 
 __device__ __forceinline__ void add8(float* acc, uint4 v) {
@@ -365,7 +366,7 @@ __global__ void __launch_bounds__(512) rs_norm_ag_kernel(RsParams p) {
     const uint32_t* cnt = p.rs_cnt + par;
     const uint64_t t0 = now_ns();
     while (static_cast<int32_t>(ld_acquire(cnt) - s_target) < 0) {
-      if (now_ns() - t0 > kTimeoutNs) {
+      if (now_ns() - t0 > (p.wait_ns ? p.wait_ns : kTimeoutNs)) {
         bail = 1;
         if (p.err) atomicCAS(p.err, 0, 200);
         break;
@@ -450,7 +451,7 @@ __global__ void __launch_bounds__(512) rs_norm_ag_kernel(RsParams p) {
     }
   }
   if (stamp) stamp[2] = now_ns();
-  if (!barrier_flags(p.peer_flags, W, p.rank, p.err, 2, epoch, &bail)) return;  // every owner's rows landed
+  if (!barrier_flags(p.peer_flags, W, p.rank, p.err, 2, epoch, &bail, p.wait_ns)) return;  // every owner's rows landed
   for (int o = 0; o < W; ++o) {
     const int64_t e1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(o + 1) * p.Tc);
     for (int64_t r = static_cast<int64_t>(o) * p.Tc + slot0; r < e1; r += slots) {
@@ -476,10 +477,124 @@ __global__ void __launch_bounds__(512) rs_norm_ag_kernel(RsParams p) {
   if (stamp) stamp[3] = now_ns();
 }
 
+// Monotone 64-bit key of (value, global id): larger value first, then the
+// lower id (first-occurrence argmax).  Float bits are mapped to an unsigned
+// order (negative values bit-flipped, positive values with the sign bit set).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int64_t id) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(b) << 32) | (0xFFFFFFFFull - static_cast<unsigned long long>(id));
+}
+
+__global__ void __launch_bounds__(512) argmax_tp_kernel(ArgmaxParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  __shared__ float sb[16];
+  __shared__ int si[16];
+  __shared__ uint32_t s_epoch;
+  __shared__ volatile int bail;
+  if (threadIdx.x == 0) {
+    s_epoch = ++p.counters[blockIdx.x];
+    bail = 0;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const size_t par = epoch & 1u;
+  const int W = p.world;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // 1. local argmax of each of this block's rows, key pushed to every rank
+  for (int r = blockIdx.x; r < p.T; r += gridDim.x) {
+    const __nv_bfloat16* row = p.logits + static_cast<int64_t>(r) * p.ld;
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    const int nvec = p.V_local / 8;
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+      const uint4 u = reinterpret_cast<const uint4*>(row)[v];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        if (f.x > best) {
+          best = f.x;
+          idx = v * 8 + 2 * j;
+        }
+        if (f.y > best) {
+          best = f.y;
+          idx = v * 8 + 2 * j + 1;
+        }
+      }
+    }
+    for (int v = nvec * 8 + threadIdx.x; v < p.V_local; v += blockDim.x) {
+      const float f = __bfloat162float(row[v]);
+      if (f > best) {
+        best = f;
+        idx = v;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ob > best || (ob == best && oi < idx)) {
+        best = ob;
+        idx = oi;
+      }
+    }
+    if (lane == 0) {
+      sb[warp] = best;
+      si[warp] = idx;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int nw = blockDim.x >> 5;
+      best = lane < nw ? sb[lane] : -INFINITY;
+      idx = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ob > best || (ob == best && oi < idx)) {
+          best = ob;
+          idx = oi;
+        }
+      }
+      // A row without a finite maximum keeps id 0 of this slice, as argmax_rows does.
+      const unsigned long long key = argmax_key(best, p.vocab_offset + (idx == 0x7fffffff ? 0 : idx));
+      if (lane < W) p.peer_keys[lane][(par * W + p.rank) * p.max_T + r] = key;
+    }
+    __syncthreads();
+  }
+  // 2. every rank's keys for this block's rows have landed here
+  if (!barrier_flags(p.peer_flags, W, p.rank, p.err, 0, epoch, &bail, p.wait_ns)) return;
+  // 3. best key over the ranks
+  const unsigned long long* keys = p.peer_keys[p.rank] + par * W * static_cast<size_t>(p.max_T);
+  for (int r = blockIdx.x; r < p.T; r += gridDim.x) {
+    if (threadIdx.x == 0) {
+      unsigned long long k = 0;
+      for (int s = 0; s < W; ++s) {
+        const unsigned long long ks = keys[static_cast<size_t>(s) * p.max_T + r];
+        k = ks > k ? ks : k;
+      }
+      p.out[r] = static_cast<int64_t>(0xFFFFFFFFull - (k & 0xFFFFFFFFull));
+    }
+  }
+}
+
 }  // namespace comm
 }  // namespace shk
 
 using namespace shk::comm;
+
+extern "C" int sh_argmax_tp(const ArgmaxParams* params, int num_blocks, cudaStream_t stream) {
+  const ArgmaxParams& p = *params;
+  if (p.world < 1 || p.world > SH_COMM_MAX_WORLD || p.T < 0 || p.T > p.max_T || p.V_local < 1) return -1;
+  if ((reinterpret_cast<uintptr_t>(p.logits) & 15) || (p.ld * 2) % 16) return -2;
+  if (p.vocab_offset < 0 || p.vocab_offset + p.V_local > 0xFFFFFFFFll) return -3;
+  if (num_blocks < 1) num_blocks = 1;
+  if (num_blocks > SH_COMM_MAX_BLOCKS) num_blocks = SH_COMM_MAX_BLOCKS;
+  shk::launch(argmax_tp_kernel, dim3(num_blocks), dim3(512), 0, stream, p);
+  return static_cast<int>(cudaGetLastError());
+}
 
 extern "C" int sh_allreduce(const ArParams* params, int num_blocks, cudaStream_t stream) {
   const ArParams& p = *params;

@@ -30,6 +30,9 @@ struct ArParams {
   // each other (every block takes a slice; nullptr / 0 = none).
   const void* prefetch;
   unsigned long long prefetch_bytes;
+  // Limit of each cross-rank wait in ns (0: the default, 5 s).  On expiry the
+  // kernel records 100 + phase in *err and returns.
+  unsigned long long wait_ns;
 };
 
 // Reduce-scatter tail of a row-parallel GEMM whose epilogue pushed its output
@@ -58,11 +61,34 @@ struct RsParams {
   unsigned long long* timing;  // optional [64][4] phase stamps of block 0
   const void* prefetch;        // optional L2 prefetch of the next GEMM's weights (as ArParams)
   unsigned long long prefetch_bytes;
+  unsigned long long wait_ns;  // wait limit (0: 5 s); 200 = arrivals, 102 = the gather barrier
+};
+
+// Vocab-parallel greedy argmax in one kernel: every rank reduces each row of
+// its logits slice to a (value, global id) key, stores the key into every
+// peer's key slots, meets the peers at a same-block barrier and takes the best
+// key over the ranks (max value, lowest id on ties; the key order makes one
+// unsigned max do both).  Keys are double-buffered by epoch parity like the
+// all-reduce's receive slots.
+struct ArgmaxParams {
+  const __nv_bfloat16* logits;                     // [T, V_local] (row stride ld)
+  int64_t ld;
+  unsigned long long* peer_keys[SH_COMM_MAX_WORLD];  // per rank: [2][world][max_T] keys
+  uint32_t* peer_flags[SH_COMM_MAX_WORLD];         // per rank: [SH_COMM_MAX_BLOCKS][MAX_WORLD] flags
+  uint32_t* counters;                              // [SH_COMM_MAX_BLOCKS] local epoch counters
+  int64_t* out;                                    // [T] global token ids
+  int* err;
+  int rank, world;
+  int T, V_local, max_T;
+  int64_t vocab_offset;
+  unsigned long long wait_ns;  // wait limit (0: 5 s); expiry records 100 in *err
 };
 
 #ifdef __cplusplus
 extern "C" {
 #endif
+// Launch of the fused argmax (every call of a communicator uses the same grid).
+int sh_argmax_tp(const ArgmaxParams* p, int num_blocks, cudaStream_t stream);
 // Sum of the world ranks' [T, H] partials, optionally fused with
 // residual += sum; out = rms_norm(residual) * weight.  All ranks must call it
 // with identical T, H, mode and grid (every call of a communicator uses the

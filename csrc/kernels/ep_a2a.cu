@@ -74,7 +74,7 @@ __device__ bool barrier(const EpParams& p, int phase, uint32_t epoch, volatile i
     const uint32_t* f = flag_slot(p.peer_flags[p.rank], phase, blockIdx.x, threadIdx.x);
     const uint64_t t0 = now_ns();
     while (static_cast<int32_t>(ld_acquire(f) - epoch) < 0) {
-      if (*bail || now_ns() - t0 > kTimeoutNs) {
+      if (*bail || now_ns() - t0 > (p.wait_ns ? p.wait_ns : kTimeoutNs)) {
         *bail = 1;
         if (p.err) atomicCAS(p.err, 0, 200 + phase);
         break;

@@ -26,7 +26,8 @@ struct EpParams {
   __nv_bfloat16* out;                      // combine: [T, H] sum over the expert ranks in rank order
   uint32_t* peer_flags[SH_EP_MAX_WORLD];   // per rank: [2 phases][SH_EP_MAX_BLOCKS][SH_EP_MAX_WORLD]
   uint32_t* counters;                      // [SH_EP_MAX_BLOCKS] local epochs (dispatch advances them)
-  int* err;                                // nonzero after a timed-out wait
+  int* err;                                // nonzero after a timed-out wait (200 + barrier phase)
+  unsigned long long wait_ns;              // limit of each cross-rank wait in ns (0: the default, 5 s)
   int rank, world, T, H, k, e_local, max_T;
   // quant = 1: the dispatch quantises each row to NVFP4 once (per-row g = 2688 / amax, e4m3 scale per 16,
   // e2m1 codes: the activation quantiser's math) and sends codes, scales and 1 / g instead of bf16 rows.

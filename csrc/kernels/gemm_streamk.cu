@@ -1,0 +1,537 @@
+// Stream-K BF16 linear on CTA pairs (tcgen05 cta_group::2), weights on the MMA M side.
+//
+//   y[j, i] = sum_k W[i, k] X[j, k]      W: [rows_w, K] weights, X: [rows_x, K] tokens, y: [rows_x, ldy]
+//
+// This is the decode / verify linear of the serving step (rows_x = a few
+// dozen to a few hundred tokens).  The design follows from three facts:
+//
+// * Tile = 256 weight rows (128 per CTA of the pair) x NT tokens, with NT up to
+//   512 as one or two MMAs of N = NS per 16-wide k-step (NSUB = 1 or 2).  With
+//   every token of the call in one tile, each weight byte is read from HBM by
+//   exactly one CTA, and each SM pulls only 128 + NT/2 operand rows per 64-wide
+//   k-block for 128 x NT x 64 MACs (NT = 384: 77 MAC per byte of L2 traffic).
+// * Stream-K: the tiles x k-blocks iteration space is cut into one contiguous
+//   range per cluster (G ranges), so every SM has the same amount of MMA work
+//   whatever the tile count (no partial last wave).  A tile cut by a range
+//   boundary is summed by the LAST cluster to finish a piece of it: every
+//   piece stores its fp32 partial in a fixed slot, bumps the tile's arrival
+//   counter, and the piece that sees the final count adds all partials in
+//   cluster order (fixed order: the result does not depend on timing) and
+//   stores the tile.  No CTA waits for another, so there is no co-residency
+//   requirement.  The counter goes back to zero after each tile, so the
+//   counter array stays zero between calls (after a timed-out wait, *err is
+//   set and the caller must clear the counters before the next call).
+// * Epilogue through shared memory: each thread owns one weight row (TMEM
+//   lane) and writes its bf16 values of 32 tokens into a [32][128] staging
+//   tile; one thread stores it with a TMA tensor store (clipped at the
+//   tensor's bounds), so the output leaves the SM as 256-byte row segments.
+//   Two staging tiles alternate.
+//
+// Roles (192 threads per CTA): warp 0 = TMA producer (both CTAs; both CTAs'
+// bytes counted on the leader's full barrier; no multicast), warp 1 = TMEM
+// allocator + MMA issuer (leader CTA only), warps 2-5 = epilogue (both CTAs,
+// one 32-lane TMEM quadrant each).  Accumulators are double-buffered when two
+// fit in TMEM (NT <= 256).  Every wait is bounded; on a timeout the kernel
+// records an error code in *err, mirrors the abort into the peer CTA, lets
+// in-flight copies land, frees TMEM and returns.
+//
+// Reference parity: the reference's decode linears go to its skinny-GEMM
+// lane or the library GEMM (reference: suffix_hybrid/kernels/bf16_skinny.py:1-60);
+// this kernel is the B200 replacement for both.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gemm_tcgen05.h"
+#include "pdl.cuh"
+#include "tcgen05_common.cuh"
+
+namespace shk {
+namespace sk {
+
+using namespace shk::tc;
+
+constexpr int BK = 64;        // k-block (one 128-byte swizzle row of bf16)
+constexpr int ROWS = 128;     // weight rows per CTA (MMA M = 256 per pair)
+constexpr int STG_T = 32;     // tokens per staging tile
+constexpr int EPI_THREADS = 128;
+constexpr int kMaxParts = 16;  // partials a fix-up may add
+
+__host__ __device__ constexpr int pow2ceil(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+template <int NS, int NSUB>
+struct Cfg {
+  static constexpr int NT = NS * NSUB;                    // tokens per tile
+  static constexpr int SUB_COLS = pow2ceil(NS);           // TMEM columns between sub-accumulators
+  static constexpr int ACC_COLS = SUB_COLS * NSUB;        // TMEM columns of one accumulator
+  static constexpr int NACC = (2 * ACC_COLS <= 512) ? 2 : 1;
+  static constexpr int TCOLS = NACC * ACC_COLS;
+  static constexpr int A_BYTES = ROWS * BK * 2;           // 16 KB of weight rows
+  static constexpr int B_SUB_BYTES = (NS / 2) * BK * 2;   // this CTA's half of one MMA's token rows
+  static constexpr int STAGE_BYTES = A_BYTES + NSUB * B_SUB_BYTES;
+  static constexpr int STG_BYTES = STG_T * ROWS * 2;      // one [32][128] bf16 staging tile
+  static constexpr int RING = 200 * 1024;
+  static constexpr int STAGES = (RING / STAGE_BYTES) > 10 ? 10 : (RING / STAGE_BYTES);
+  static constexpr int STG_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = STG_OFF + 2 * STG_BYTES;
+  static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 2 * NACC + 1) * 8 + 16 + 1024;
+  static_assert(NS % 32 == 0 && NS >= 64 && NS <= 256, "MMA N per instruction");
+  static_assert(B_SUB_BYTES % 1024 == 0, "token half-tiles keep the 1024-byte swizzle alignment");
+  static_assert(TCOLS <= 512, "TMEM columns");
+  static_assert(TOTAL <= 227 * 1024, "shared memory budget");
+};
+
+struct Seg {
+  int tile, k0, k1;  // k-blocks [k0, k1) of tile `tile`
+  bool whole;        // the segment covers the tile's whole K range
+};
+
+// The iteration range of cluster c: [c * I / G, (c + 1) * I / G).
+__device__ __forceinline__ int64_t range_start(int64_t c, const SkParams& g) { return c * g.iters / g.clusters; }
+// The cluster whose range holds iteration it (largest c with range_start(c) <= it).
+__device__ __forceinline__ int cluster_of(int64_t it, const SkParams& g) {
+  return static_cast<int>(((it + 1) * g.clusters + g.iters - 1) / g.iters - 1);
+}
+
+template <int NS, int NSUB>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_sk_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                   const __grid_constant__ CUtensorMap tmY, SkParams g) {
+  using C = Cfg<NS, NSUB>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + C::NACC;
+  uint64_t* mma_done = tempty + C::NACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* bcast = const_cast<int*>(abort_flag) + 1;  // epilogue: broadcast of the arrival count
+
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < C::NACC; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmY)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(C::TCOLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers are initialised before any remote arrive / complete_tx
+  fence_after();
+  shk::pdl_trigger();
+  shk::pdl_wait();  // the previous kernel's outputs (our inputs) are complete from here on
+  const uint32_t tmem_base = *tmem_slot;
+  const int cid = blockIdx.x >> 1;
+  const int64_t it_begin = range_start(cid, g), it_end = range_start(cid + 1, g);
+  const uint32_t peer_abort = map_to_rank(const_cast<int*>(abort_flag), rank ^ 1);
+  auto raise = [&](int code) {
+    if (g.err) atomicCAS(g.err, 0, code);
+    *abort_flag = 1;
+    st_cluster_u32(peer_abort, 1);
+  };
+  // Segments of this cluster's range, in order.
+  auto next_seg = [&](int64_t& it, Seg& s) -> bool {
+    if (it >= it_end) return false;
+    s.tile = static_cast<int>(it / g.kb);
+    const int64_t t0 = static_cast<int64_t>(s.tile) * g.kb;
+    s.k0 = static_cast<int>(it - t0);
+    s.k1 = static_cast<int>((it_end - t0) < g.kb ? (it_end - t0) : g.kb);
+    s.whole = s.k0 == 0 && s.k1 == g.kb;
+    it = t0 + s.k1;
+    return true;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t it = it_begin;
+      Seg s;
+      bool stop = false;
+      while (!stop && next_seg(it, s)) {
+        const int tw = s.tile / g.tiles_x, tx = s.tile % g.tiles_x;
+        int w_y = tw * (2 * ROWS) + static_cast<int>(rank) * ROWS;
+        if (w_y >= g.rows_w) w_y = 0;  // wholly outside: load valid rows whose results are never stored
+        int x_y[NSUB];
+#pragma unroll
+        for (int u = 0; u < NSUB; ++u) {
+          x_y[u] = tx * C::NT + u * NS + static_cast<int>(rank) * (NS / 2);
+          if (x_y[u] >= g.rows_x) x_y[u] = 0;
+        }
+        for (int kb = s.k0; kb < s.k1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            raise(1);
+            stop = true;
+            break;
+          }
+          if (leader) mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          uint8_t* sp = smem + stage * C::STAGE_BYTES;
+          const uint32_t bar = map_to_rank(&full[stage], 0);
+          tma_load_2d_pair(sp, &tmW, kb * BK, w_y, bar);
+#pragma unroll
+          for (int u = 0; u < NSUB; ++u)
+            tma_load_2d_pair(sp + C::A_BYTES + u * C::B_SUB_BYTES, &tmX, kb * BK, x_y[u], bar);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t IDESC = idesc_bf16_mn(2 * ROWS, NS);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      int64_t it = it_begin;
+      Seg s;
+      while (next_seg(it, s)) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
+          raise(2);
+          break;
+        }
+        fence_after();
+        const uint32_t tmem_d = tmem_base + acc * C::ACC_COLS;
+        bool ok = true;
+        for (int kb = s.k0; kb < s.k1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t sa = smem_addr(smem + stage * C::STAGE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+#pragma unroll
+            for (int u = 0; u < NSUB; ++u)
+              mma_bf16_pair(tmem_d + u * C::SUB_COLS, sw128_desc(sa + kk * 32),
+                            sw128_desc(sa + C::A_BYTES + u * C::B_SUB_BYTES + kk * 32), IDESC,
+                            (kb > s.k0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit_pair_both(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) {
+          raise(3);
+          mma_commit_pair_local(mma_done);
+          (void)mbar_wait_drain(mma_done, 0);
+          break;
+        }
+        mma_commit_pair_both(&tfull[acc]);
+        if (++acc == C::NACC) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;       // weight row within this CTA's 128
+    const int et = threadIdx.x - 64;        // 0..127 within the epilogue warps
+    const bool elected = et == 0;
+    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::STG_OFF);
+    const int64_t slot_elems = static_cast<int64_t>(C::NT) * ROWS;
+    const int first_tile = static_cast<int>(it_begin / g.kb);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int chunk = 0;  // staging tiles used so far (alternating buffers)
+    int64_t it = it_begin;
+    Seg s;
+    while (next_seg(it, s)) {
+      const int tw = s.tile / g.tiles_x, tx = s.tile % g.tiles_x;
+      const int y_w = tw * (2 * ROWS) + static_cast<int>(rank) * ROWS;  // output column of row 0
+      const int y_x0 = tx * C::NT;                                        // output row of token 0
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+        if (lane == 0) raise(4);
+        break;
+      }
+      fence_after();
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * C::ACC_COLS;
+      bool store = true;
+      const float* parts[kMaxParts];
+      int nparts = 0;
+      if (!s.whole) {
+        // Partial tile: park this piece's fp32 sums in the cluster's slot, then
+        // count it.  Slot = (cluster, rank, first tile of the range ? 0 : 1).
+        float* mine = g.ws + ((static_cast<int64_t>(cid) * 2 + rank) * 2 + (s.tile == first_tile ? 0 : 1)) * slot_elems;
+#pragma unroll 1
+        for (int c = 0; c < C::NT; c += 16) {
+          float v[16];
+          __syncwarp();
+          tmem_ld16(tacc + (c / NS) * C::SUB_COLS + (c % NS), v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) __stcg(mine + static_cast<int64_t>(c + i) * ROWS + row, v[i]);
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_rank(&tempty[acc], 0));  // TMEM is free again
+        __threadfence();
+        named_barrier(1, EPI_THREADS);
+        if (elected) {
+          const int c_first = cluster_of(static_cast<int64_t>(s.tile) * g.kb, g);
+          const int c_last = cluster_of(static_cast<int64_t>(s.tile + 1) * g.kb - 1, g);
+          int* cnt = g.cnt + s.tile * 2 + rank;
+          const int old = atomicAdd(cnt, 1);
+          const bool last = old == c_last - c_first;
+          if (last) *cnt = 0;  // every piece has arrived: reset for the next call
+          *bcast = last ? (c_last - c_first + 1) : 0;
+        }
+        named_barrier(1, EPI_THREADS);
+        nparts = *bcast;
+        if (nparts > kMaxParts) {  // excluded by the host's cluster clamp
+          if (elected) raise(5);
+          nparts = 0;
+        }
+        store = nparts > 0;
+        if (store) {
+          __threadfence();  // acquire side of the counter: the other pieces' partials are visible
+          const int c_first = cluster_of(static_cast<int64_t>(s.tile) * g.kb, g);
+          for (int j = 0; j < nparts; ++j) {
+            const int cj = c_first + j;
+            const int fj = static_cast<int>(range_start(cj, g) / g.kb);
+            parts[j] = g.ws + ((static_cast<int64_t>(cj) * 2 + rank) * 2 + (s.tile == fj ? 0 : 1)) * slot_elems;
+          }
+        }
+      }
+      if (store) {
+#pragma unroll 1
+        for (int c = 0; c < C::NT; c += STG_T) {
+          __nv_bfloat16* buf = stg + (chunk & 1) * (STG_T * ROWS);
+          // The store issued from this buffer two chunks ago has read it.
+          if (elected && chunk >= 2) bulk_wait_read<1>();
+          named_barrier(1, EPI_THREADS);
+#pragma unroll
+          for (int h = 0; h < STG_T; h += 16) {
+            float v[16];
+            if (s.whole) {
+              __syncwarp();
+              tmem_ld16(tacc + ((c + h) / NS) * C::SUB_COLS + ((c + h) % NS), v);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = 0.f;
+              for (int j = 0; j < nparts; ++j) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] += __ldcg(parts[j] + static_cast<int64_t>(c + h + i) * ROWS + row);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) buf[(h + i) * ROWS + row] = __float2bfloat16_rn(v[i]);
+          }
+          fence_proxy_async_smem();
+          named_barrier(1, EPI_THREADS);
+          if (elected && y_w < g.rows_w && y_x0 + c < g.rows_x) {
+            tma_store_2d(&tmY, buf, y_w, y_x0 + c);
+          }
+          if (elected) bulk_commit();
+          ++chunk;
+        }
+      }
+      if (s.whole) {
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_rank(&tempty[acc], 0));
+      }
+      if (++acc == C::NACC) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (elected) bulk_wait_all();
+  }
+  if (warp == 0 && lane == 0 && *abort_flag) {
+    // Loads issued before the abort complete within microseconds; give them 200 us.
+    const uint64_t t0 = now_ns();
+    while (now_ns() - t0 < 200000) {
+    }
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TCOLS));
+  }
+}
+
+}  // namespace sk
+}  // namespace shk
+
+namespace {
+
+using namespace shk::sk;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// bf16 matrix [rows][cols] (row stride in elements), box {box_cols, box_rows}.
+int encode(CUtensorMap* m, const void* base, int rows, int cols, int64_t stride, int box_cols, int box_rows,
+           bool swizzle128) {
+  auto enc = encode_fn();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
+}
+
+constexpr int kMaxDevices = 64;
+
+// Index of a compiled (MMA N, MMAs per k-step) variant, -1 if none.
+int variant(int ns, int nsub) {
+  if (nsub == 1) return ns == 64 ? 0 : ns == 128 ? 1 : ns == 192 ? 2 : ns == 256 ? 3 : -1;
+  if (nsub == 2) return ns == 192 ? 4 : ns == 256 ? 5 : -1;
+  return -1;
+}
+
+template <int NS, int NSUB>
+int launch_sk(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& my, const SkParams& g,
+              cudaStream_t st) {
+  using C = Cfg<NS, NSUB>;
+  auto k = gemm_sk_kernel<NS, NSUB>;
+  static bool ready[kMaxDevices] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+  if (!ready[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    ready[dev] = true;
+  }
+  shk::launch(k, dim3(2 * g.clusters), dim3(192), C::TOTAL, st, mw, mx, my, g);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" int sh_gemm_sk_max_clusters(int ns, int nsub) {
+  static int cached[kMaxDevices][6] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  const int which = variant(ns, nsub);
+  if (which < 0) return 0;
+  if (cached[dev][which]) return cached[dev][which];
+  int sms = 0;
+  (void)cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int n = sms / 2;
+  auto query = [&](auto k, int bytes) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * n, 1, 1);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = bytes;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, k, &cfg) == cudaSuccess && c > 0 && c < n) n = c;
+  };
+  switch (which) {
+    case 0: query(gemm_sk_kernel<64, 1>, Cfg<64, 1>::TOTAL); break;
+    case 1: query(gemm_sk_kernel<128, 1>, Cfg<128, 1>::TOTAL); break;
+    case 2: query(gemm_sk_kernel<192, 1>, Cfg<192, 1>::TOTAL); break;
+    case 3: query(gemm_sk_kernel<256, 1>, Cfg<256, 1>::TOTAL); break;
+    case 4: query(gemm_sk_kernel<192, 2>, Cfg<192, 2>::TOTAL); break;
+    default: query(gemm_sk_kernel<256, 2>, Cfg<256, 2>::TOTAL); break;
+  }
+  (void)cudaGetLastError();
+  cached[dev][which] = n;
+  return n;
+}
+
+extern "C" int sh_gemm_sk_shape(int rows_w, int rows_x, int K, int ns, int nsub, int clusters, int64_t* tiles,
+                                int64_t* ws_floats) {
+  if (K % BK != 0 || K <= 0 || rows_w <= 0 || rows_x <= 0 || clusters <= 0) return -2;
+  const int nt = ns * nsub;
+  const int64_t t = static_cast<int64_t>((rows_w + 2 * ROWS - 1) / (2 * ROWS)) * ((rows_x + nt - 1) / nt);
+  if (tiles) *tiles = t;
+  if (ws_floats) *ws_floats = static_cast<int64_t>(clusters) * 2 * 2 * nt * ROWS;
+  return 0;
+}
+
+extern "C" int sh_gemm_bf16_sk(const void* W, int rows_w, int64_t ldw, const void* X, int rows_x, int64_t ldx,
+                               int K, void* Y, int64_t ldy, int ns, int nsub, int clusters, float* ws, int* cnt,
+                               int* err, cudaStream_t stream) {
+  if (K % BK != 0 || K <= 0) return -2;
+  if (rows_w <= 0 || rows_x <= 0) return 0;
+  if ((reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(X) & 15) ||
+      (reinterpret_cast<uintptr_t>(Y) & 15) || (ldw * 2) % 16 || (ldx * 2) % 16 || (ldy * 2) % 16)
+    return -3;  // TMA: 16-byte aligned bases and row strides
+  if (clusters < 1 || !ws || !cnt) return -5;
+  const int which = variant(ns, nsub);
+  if (which < 0) return -4;
+  const int nt = ns * nsub;
+  SkParams g{};
+  g.rows_w = rows_w;
+  g.rows_x = rows_x;
+  g.tiles_w = (rows_w + 2 * ROWS - 1) / (2 * ROWS);
+  g.tiles_x = (rows_x + nt - 1) / nt;
+  g.kb = K / BK;
+  g.iters = static_cast<int64_t>(g.tiles_w) * g.tiles_x * g.kb;
+  // Every range is at least ceil(kb / 15) iterations long, so a tile of kb
+  // iterations meets at most 16 ranges (the fix-up adds at most 16 partials).
+  const int64_t min_range = (g.kb + kMaxParts - 2) / (kMaxParts - 1);
+  const int64_t gmax = g.iters / min_range;
+  g.clusters = static_cast<int>(clusters < gmax ? clusters : gmax);
+  g.ws = ws;
+  g.cnt = cnt;
+  g.err = err;
+  CUtensorMap mw, mx, my;
+  int r = encode(&mw, W, rows_w, K, ldw, BK, ROWS, true);
+  if (r) return 1000 + r;
+  r = encode(&mx, X, rows_x, K, ldx, BK, ns / 2, true);
+  if (r) return 2000 + r;
+  r = encode(&my, Y, rows_x, rows_w, ldy, ROWS, STG_T, false);
+  if (r) return 5000 + r;
+  switch (which) {
+    case 0: r = launch_sk<64, 1>(mw, mx, my, g, stream); break;
+    case 1: r = launch_sk<128, 1>(mw, mx, my, g, stream); break;
+    case 2: r = launch_sk<192, 1>(mw, mx, my, g, stream); break;
+    case 3: r = launch_sk<256, 1>(mw, mx, my, g, stream); break;
+    case 4: r = launch_sk<192, 2>(mw, mx, my, g, stream); break;
+    default: r = launch_sk<256, 2>(mw, mx, my, g, stream); break;
+  }
+  return r ? 3000 + r : 0;
+}

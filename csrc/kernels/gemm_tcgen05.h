@@ -33,9 +33,36 @@ struct GemmParams {
   int push_rank, push_world, push_rows, push_max_T, push_n;
 };
 
+// Stream-K linear on CTA pairs (gemm_streamk.cu): y[j, i] = sum_k W[i, k] X[j, k].
+struct SkParams {
+  int rows_w, rows_x;
+  int tiles_w, tiles_x;  // 256-row weight tiles x NT-token tiles; tile = tw * tiles_x + tx
+  int kb;                // 64-wide k-blocks per tile
+  int64_t iters;         // tiles * kb: the stream-K iteration space
+  int clusters;          // CTA pairs; pair c runs iterations [c*iters/clusters, (c+1)*iters/clusters)
+  float* ws;             // fp32 partial slots [clusters][2 ranks][2][NT][128]
+  int* cnt;              // [tiles][2] arrival counters, zero between calls
+  int* err;
+};
+
 #ifdef __cplusplus
 extern "C" {
 #endif
+// Stream-K linear y = X W^T on tcgen05 CTA pairs, weights on the MMA M side:
+// W [rows_w, K] (row stride ldw), X [rows_x, K], y [rows_x, ldy] bf16; K % 64 == 0,
+// 16-byte aligned bases and row strides.  One tile = 256 weight rows x
+// ns*nsub tokens ((ns, nsub) in {(64,1), (128,1), (192,1), (256,1), (192,2), (256,2)}).
+// `clusters` CTA pairs share the iteration space evenly (clamped so that a
+// tile is split into at most 16 pieces).  ws: >= the floats reported by
+// sh_gemm_sk_shape; cnt: >= 2 * tiles ints, zero before the first call (the
+// kernel leaves them zero).  One call at a time per (ws, cnt) pair.
+int sh_gemm_bf16_sk(const void* W, int rows_w, int64_t ldw, const void* X, int rows_x, int64_t ldx, int K, void* Y,
+                    int64_t ldy, int ns, int nsub, int clusters, float* ws, int* cnt, int* err, cudaStream_t stream);
+// Tile count and workspace floats of a stream-K call (0 on success).
+int sh_gemm_sk_shape(int rows_w, int rows_x, int K, int ns, int nsub, int clusters, int64_t* tiles,
+                     int64_t* ws_floats);
+// Co-resident CTA pairs of the stream-K kernel on the current device.
+int sh_gemm_sk_max_clusters(int ns, int nsub);
 // D[i, j] = sum_k P[i, k] Q[j, k] (bf16 in, fp32 accumulate, bf16 out).
 //   trans = 0: out[i * ldo + j];  trans = 1: out[j * ldo + i].
 //   bn in {64, 128, 256}: Q tile rows (MMA N).  splits > 1 needs a workspace

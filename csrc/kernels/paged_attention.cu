@@ -601,18 +601,34 @@ std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kMaxDevices] = {};
 CUcontext g_noalloc_ctx[kMaxDevices] = {};
 
+// cuCtxGetCurrent through the runtime's driver entry point (the library does
+// not link libcuda directly, so it loads on machines without a driver).
+CUresult current_context(CUcontext* ctx) {
+  using Fn = CUresult (*)(CUcontext*);
+  static Fn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || p == nullptr)
+      return CUDA_ERROR_NOT_FOUND;
+    fn = reinterpret_cast<Fn>(p);
+  }
+  return fn(ctx);
+}
+
 int noalloc_scratch(float** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return SH_NOALLOC_ERR_DEVICE;
   // The context may not exist yet before the first lookup (the runtime
   // creates it lazily), so it is read again after cudaGetSymbolAddress.
   CUcontext ctx = nullptr;
-  (void)cuCtxGetCurrent(&ctx);
+  (void)current_context(&ctx);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (g_noalloc_ptr[dev] == nullptr || ctx == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return SH_NOALLOC_ERR_SYMBOL;
-    if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS || ctx == nullptr) return SH_NOALLOC_ERR_SYMBOL;
+    if (current_context(&ctx) != CUDA_SUCCESS || ctx == nullptr) return SH_NOALLOC_ERR_SYMBOL;
     g_noalloc_ptr[dev] = static_cast<float*>(p);
     g_noalloc_ctx[dev] = ctx;
   }

@@ -56,7 +56,9 @@ def cuda_ext():
         srcs,
         include_dirs=[os.path.join(ROOT, "csrc", "kernels")],
         extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": nvcc},
-        libraries=["cuda"],
+        # No -lcuda: driver entry points are fetched through the runtime
+        # (cudaGetDriverEntryPointByVersion), so the module imports on a
+        # machine without a GPU driver (the build check).
     )
 
 

@@ -127,3 +127,25 @@ def test_spec_verify_matches_reference():
     ops.spec_verify(d_c, t_c, s_c, out, acc, nxt)
     assert torch.equal(out.cpu(), o_ref) and torch.equal(acc.cpu(), a_ref)
     assert torch.equal(nxt.cpu(), n_ref) and torch.equal(s_c.cpu(), s_ref)
+
+
+@pytest.mark.parametrize("T,V,offset", [(1, 16032, 0), (384, 16032, 48096), (77, 1001, 5)])
+def test_argmax_tp_single_rank_layout(T, V, offset):
+    """The fused vocab-parallel argmax in a one-rank layout (keys and flags in this GPU's memory):
+    global id = local first-occurrence argmax + the shard's vocab offset, over repeated calls."""
+    torch.manual_seed(T + V)
+    logits = torch.randn(T, V, device="cuda").to(torch.bfloat16)
+    logits[0, 3] = 50.0
+    logits[0, 7] = 50.0  # tie: the lower id wins
+    keys = torch.zeros(2 * 1 * 512 * 2 + 160 * 8, dtype=torch.int32, device="cuda")
+    base = keys.data_ptr()
+    counters = torch.zeros(160, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.empty(T, dtype=torch.int64, device="cuda")
+    want = logits.float().argmax(1) + offset
+    for _ in range(3):  # both key parities
+        ops.native().argmax_tp(out, logits, [base], [base + 2 * 512 * 8], counters, err, 0, 512, offset, 64)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert torch.equal(out, want)
+    assert int(out[0].item()) == 3 + offset

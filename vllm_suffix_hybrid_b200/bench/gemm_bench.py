@@ -18,6 +18,8 @@ SHAPES = [  # (name, M, N, K) -- Llama-3-8B decode with a k=5 verify window over
     ("down_m384", 384, 4096, 14336),
     ("lm_head_m384", 384, 128256, 4096),
     ("qkv_m64", 64, 6144, 4096),
+    ("o_m64", 64, 4096, 4096),
+    ("fc_m64", 64, 4096, 8192),  # EAGLE head input projection [embedding | hidden] -> hidden
     ("gate_up_m64", 64, 28672, 4096),
     ("down_m64", 64, 4096, 14336),
     ("lm_head_m64", 64, 128256, 4096),
@@ -61,23 +63,23 @@ def time_fn(fn, flush, iters=20, warmup=5):
 
 
 def sweep(name, x, w, y, flush, iters):
-    """Every (pair, swap, bn, splits) configuration of the tcgen05 kernels on one shape."""
-    from vllm_suffix_hybrid_b200 import ops
-    from vllm_suffix_hybrid_b200.ops.gemm import workspace
+    """Every candidate configuration of the autotuner on one shape (cuBLAS included)."""
+    from vllm_suffix_hybrid_b200.ops.gemm import LIB, _runner, candidates
 
     M, K = x.shape
     N = w.shape[0]
     rows = []
-    for pair in (False, True):
-        for swap in (False, True):
-            for bn in ((128, 192, 256) if pair else (64, 128, 256)):
-                for splits in (1, 2, 4):
-                    ws = workspace(x.device, splits * M * N) if splits > 1 else None
-                    fn = lambda: ops.native().gemm_bf16(y, x, w, swap, bn, splits, ws, None, pair)
-                    rows.append((time_fn(fn, flush, iters, 2), pair, swap, bn, splits))
-    rows.sort()
-    print(json.dumps({"sweep": name, "best": [dict(us=round(t, 2), pair=p, swap=s, bn=b, splits=k)
-                                              for t, p, s, b, k in rows[:6]]}))
+    for cfg in [LIB] + [c for c in candidates(M, N, K) if c.kind != "lib"]:
+        fn = _runner(cfg, x, w, y)
+        try:
+            fn()
+        except RuntimeError:
+            continue
+        rows.append((time_fn(fn, flush, iters, 2), cfg))
+    rows.sort(key=lambda r: r[0])
+    print(json.dumps({"sweep": name, "M": M, "N": N, "K": K,
+                      "cublas_us": round(next(t for t, c in rows if c.kind == "lib"), 2),
+                      "best": [dict(us=round(t, 2), **c._asdict()) for t, c in rows[:8]]}), flush=True)
 
 
 NVFP4_SHAPES = [  # (name, M, N, K): DeepSeek-V3-style decode projections and one expert
@@ -157,7 +159,7 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="time every kernel configuration per shape")
     ap.add_argument("--once", action="store_true",
                     help="no timing: two eager launches of ours then cuBLAS per shape (for ncu captures)")
-    ap.add_argument("--config", default="", help="force pair,swap,bn,splits (e.g. 1,0,256,1)")
+    ap.add_argument("--config", default="", help="force kind,swap,bn,splits,clusters (e.g. sk,1,192,2,74 or pair,0,256,1,0)")
     ap.add_argument("--w4a4", action="store_true", help="with --nvfp4 --once: launch the W4A4 kernel")
     ap.add_argument("--nvfp4", action="store_true",
                     help="NVFP4-weight (W4A16) kernel vs the bf16 paths on decode shapes (packed-weight GB/s)")
@@ -179,12 +181,10 @@ def main():
             sweep(name, x, w, y, flush, a.iters)
         ours = lambda: tcgen05_linear(x, w, y)
         if a.config:
-            from vllm_suffix_hybrid_b200 import ops
-            from vllm_suffix_hybrid_b200.ops.gemm import workspace
+            from vllm_suffix_hybrid_b200.ops.gemm import Cfg, _runner
 
-            pr, sw, bn, sp = (int(v) for v in a.config.split(","))
-            ws = workspace(x.device, sp * M * N) if sp > 1 else None
-            ours = lambda: ops.native().gemm_bf16(y, x, w, bool(sw), bn, sp, ws, None, bool(pr))
+            kind, sw, bn, sp, cl = a.config.split(",")
+            ours = _runner(Cfg(kind, bool(int(sw)), int(bn), int(sp), int(cl)), x, w, y)
         if a.once:
             for _ in range(2):
                 flush.zero_()
@@ -201,7 +201,7 @@ def main():
         err = (y.float() - ref).abs().max().item()
         flops = 2.0 * M * N * K
         wbytes = N * K * 2
-        r = {"shape": name, "M": M, "N": N, "K": K, "plan": list(plan(M, N, K, x, w, y)), "tcgen05_us": round(t_ours, 2),
+        r = {"shape": name, "M": M, "N": N, "K": K, "plan": plan(M, N, K, x, w, y)._asdict(), "tcgen05_us": round(t_ours, 2),
              "cublas_us": round(t_lib, 2), "speedup": round(t_lib / t_ours, 3),
              "tcgen05_tflops": round(flops / t_ours / 1e6, 1), "tcgen05_weight_gbs": round(wbytes / t_ours / 1e3, 1),
              "max_abs_err": err}

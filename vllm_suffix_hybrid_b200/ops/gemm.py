@@ -1,33 +1,41 @@
 """Dispatcher of the tcgen05 GEMMs: y = x @ w^T for bf16 x [M, K], w [N, K].
 
-Two kernels (csrc/kernels/gemm_tcgen05.cu): one CTA per 128-row tile, and a
-CTA pair (cta_group::2) per 256-row tile that halves each SM's share of the
-B operand.  A configuration is (pair, swap, bn, splits):
+Three kernel families, all on the 5th-generation tensor cores:
 
-* swap: the weight rows take the MMA's M side and the tokens become the MMA
-  N dimension (bn), so a decode batch pays no padding to 128 rows;
-* bn: MMA N tile (one CTA: 64/128/256, pair: 128/192/256);
-* splits: split-K factor (fp32 partials + a deterministic reduce pass).
+* ``tc``   -- one CTA per 128-row tile (csrc/kernels/gemm_tcgen05.cu);
+* ``pair`` -- a CTA pair (cta_group::2) per 256-row tile, same file;
+* ``sk``   -- stream-K on CTA pairs with the weights on the MMA M side and
+  every token of the call in one wide N tile (csrc/kernels/gemm_streamk.cu):
+  each weight byte crosses HBM once and all SMs get equal MMA work.
 
-By default every new (M, N, K) is autotuned once, on its first eager call:
-the candidate configurations are timed on the device with a cold L2 and the
-fastest is kept for the process (SH_GEMM_TUNE=0 uses the static heuristic;
+A configuration is ``Cfg(kind, swap, bn, splits, clusters)``:
+
+* tc / pair: swap puts the weight rows on the MMA M side (tokens become N),
+  bn is the MMA N tile (tc 64/128/256, pair 128/192/256) and splits the
+  split-K factor (fp32 partials + a deterministic reduce pass);
+* sk: bn is the MMA N per instruction (64/128/192/256), splits the number of
+  MMAs per 16-wide k-step (1 or 2; tokens per tile = bn * splits) and
+  clusters the number of CTA pairs sharing the iteration space;
+* lib: cuBLAS (torch.matmul), only a candidate when SH_GEMM_LIB=1.
+
+Every new (M, N, K) is autotuned once, on its first eager call: the
+candidates are timed on the device with a cold L2 and the fastest is kept
+for the process (SH_GEMM_TUNE=0 uses the static heuristic;
 SH_GEMM_TUNE_FILE=path loads and saves the choices as JSON, which pins them
-across runs).  Calls during CUDA-graph capture never tune: they use the
-recorded choice or the heuristic.  For these plain (unfused) linears cuBLAS is
-one more candidate (configuration "lib"; SH_GEMM_LIB=0 leaves it out); the
-fused GEMMs -- grouped MoE experts and the NVFP4 paths -- always run this
-framework's kernels.
+across runs and across processes of a multi-GPU job).  Calls during
+CUDA-graph capture never tune: they use the recorded choice or the
+heuristic.
 
 Batch-invariant mode (SH_BATCH_INVARIANT=1): the split-K factor -- the only
-choice that changes a row's fp32 summation order -- becomes a function of
-(N, K) alone, so a token's output does not depend on how many other tokens
-share the call (a k+1-token verify window gives the same logits as plain
-decoding).  Orientation, pair and N tile do not change the per-element
-order and stay free.
+tc/pair choice that changes a row's fp32 summation order -- becomes a
+function of (N, K) alone, so a token's output does not depend on how many
+other tokens share the call (a k+1-token verify window gives the same logits
+as plain decoding).  Stream-K pieces depend on the tile count, so sk is left
+out in that mode.
 
-Split-K partials go to one fp32 workspace per device that grows on demand
-and is reused by every call on that device's stream.
+Split-K partials, stream-K partial slots and stream-K arrival counters live
+in per-device buffers that grow on demand and are reused by every call on
+that device's stream (one GEMM at a time per device).
 """
 from __future__ import annotations
 
@@ -35,7 +43,7 @@ import functools
 import json
 import math
 import os
-from typing import Dict, Optional, Tuple
+from typing import Dict, NamedTuple, Optional, Tuple
 
 import torch
 
@@ -43,17 +51,44 @@ from . import native
 
 NUM_SMS = 148
 _WS: Dict[int, torch.Tensor] = {}
+_SK_WS: Dict[int, torch.Tensor] = {}
+_SK_CNT: Dict[int, torch.Tensor] = {}
+_RETIRED: list = []
+
+
+class Cfg(NamedTuple):
+    kind: str        # "tc" | "pair" | "sk" | "lib"
+    swap: bool = False
+    bn: int = 0
+    splits: int = 1
+    clusters: int = 0
+
+
+LIB = Cfg("lib")
+SK_SHAPES = ((64, 1), (128, 1), (192, 1), (256, 1), (192, 2), (256, 2))  # (MMA N, MMAs per k-step)
+
+
+def sk_tokens(bn: int, nsub: int) -> int:
+    return bn * nsub
+
+
+@functools.lru_cache(maxsize=64)
+def sk_max_clusters(bn: int, nsub: int) -> int:
+    return int(native().gemm_sk_max_clusters(bn, nsub)) or NUM_SMS // 2
 
 
 @functools.lru_cache(maxsize=4096)
-def heuristic(M: int, N: int, K: int) -> Tuple[bool, bool, int, int]:
-    """(pair, swap, bn, splits) without measurement.
+def heuristic(M: int, N: int, K: int) -> Cfg:
+    """Configuration without measurement.
 
-    Decode sizes (M <= 256) are weight-streaming: one-CTA swap-AB tiles,
-    split-K only while it at most fills one wave.  Larger M is bound by the
-    L2 -> SM operand stream, where the CTA pair's 256 x 256 tile moves the
+    Up to 512 tokens: stream-K with every token in one tile (the narrowest
+    tile that holds them) on all co-resident CTA pairs.  Larger M is bound by
+    the L2 -> SM operand stream, where the CTA pair's 256 x 256 tile moves the
     fewest bytes per MAC.
     """
+    if M <= 512 and N % 8 == 0 and not batch_invariant():
+        bn, nsub = next((b, u) for b, u in SK_SHAPES if sk_tokens(b, u) >= M)
+        return Cfg("sk", True, bn, nsub, NUM_SMS // 2)
     kb = max(K // 64, 1)
     if M <= 256:
         bn = next(b for b in (64, 128, 256) if b >= M)
@@ -61,12 +96,12 @@ def heuristic(M: int, N: int, K: int) -> Tuple[bool, bool, int, int]:
         splits = 1
         while tiles * splits * 2 <= NUM_SMS and kb // (splits * 2) >= 8 and splits < 8:
             splits *= 2
-        return False, True, bn, splits
+        return Cfg("tc", True, bn, splits)
     tiles = math.ceil(M / 256) * math.ceil(N / 256)
     splits = 1
     while tiles * splits < NUM_SMS // 4 and kb // (splits * 2) >= 16 and splits < 4:
         splits *= 2
-    return True, False, 256, splits
+    return Cfg("pair", False, 256, splits)
 
 
 def batch_invariant() -> bool:
@@ -76,15 +111,27 @@ def batch_invariant() -> bool:
 @functools.lru_cache(maxsize=4096)
 def invariant_splits(N: int, K: int) -> int:
     """Split-K factor of (N, K) used for every M in batch-invariant mode (the decode-size choice)."""
-    return heuristic(64, N, K)[3]
-
-
-LIB = (False, False, 0, 0)  # configuration tag of the cuBLAS candidate
+    kb = max(K // 64, 1)
+    tiles = math.ceil(N / 128)
+    splits = 1
+    while tiles * splits * 2 <= NUM_SMS and kb // (splits * 2) >= 8 and splits < 8:
+        splits *= 2
+    return splits
 
 
 def candidates(M: int, N: int, K: int, splits_only: Optional[int] = None):
     kb = max(K // 64, 1)
-    out = [LIB] if os.environ.get("SH_GEMM_LIB", "1") != "0" and splits_only is None else []
+    out = [LIB] if os.environ.get("SH_GEMM_LIB", "0") == "1" and splits_only is None else []
+    if splits_only is None and N % 8 == 0 and os.environ.get("SH_GEMM_SK", "1") != "0":
+        tiles_w = math.ceil(N / 256)
+        fits = [(b, u) for b, u in SK_SHAPES if sk_tokens(b, u) >= M]
+        # the narrowest single tile over all tokens, and narrower tiles that split the tokens
+        shapes = fits[:1] + [(b, u) for b, u in SK_SHAPES if sk_tokens(b, u) < M and sk_tokens(b, u) >= M / 4]
+        for b, u in shapes:
+            tiles = tiles_w * math.ceil(M / sk_tokens(b, u))
+            gmax = sk_max_clusters(b, u)
+            for g in sorted({gmax, min(gmax, tiles), min(gmax, 2 * tiles)}):
+                out.append(Cfg("sk", True, b, u, g))
     for pair in (False, True):
         for swap in (False, True):
             for bn in ((128, 192, 256) if pair else (64, 128, 256)):
@@ -93,11 +140,11 @@ def candidates(M: int, N: int, K: int, splits_only: Optional[int] = None):
                 for splits in ((splits_only,) if splits_only else (1, 2, 4)):
                     if splits_only is None and splits > 1 and kb // splits < 4:
                         continue
-                    out.append((pair, swap, bn, splits))
+                    out.append(Cfg("pair" if pair else "tc", swap, bn, splits))
     return out
 
 
-_CHOICE: Dict[Tuple[int, int, int], Tuple[bool, bool, int, int]] = {}
+_CHOICE: Dict[Tuple[int, int, int], Cfg] = {}
 _FLUSH: Dict[int, torch.Tensor] = {}
 _LOADED = [False]
 
@@ -115,7 +162,8 @@ def _load():
         with open(f) as fh:
             for key, val in json.load(fh).items():
                 M, N, K = (int(v) for v in key.split(","))
-                _CHOICE[(M, N, K)] = (bool(val[0]), bool(val[1]), int(val[2]), int(val[3]))
+                if isinstance(val, list) and len(val) == 5 and isinstance(val[0], str):
+                    _CHOICE[(M, N, K)] = Cfg(val[0], bool(val[1]), int(val[2]), int(val[3]), int(val[4]))
 
 
 def _save():
@@ -129,8 +177,7 @@ def _save():
     os.replace(tmp, f)
 
 
-def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor,
-              splits_only: Optional[int] = None) -> Tuple[bool, bool, int, int]:
+def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor, splits_only: Optional[int] = None) -> Cfg:
     M, K = x2.shape
     N = w.shape[0]
     dev = x2.device
@@ -138,12 +185,15 @@ def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor,
     flush = _FLUSH.get(idx)
     if flush is None:
         flush = _FLUSH[idx] = torch.empty(160 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
-    lib = native()
     cands = candidates(M, N, K, splits_only)
     times = []
     for cfg in cands:
         run = _runner(cfg, x2, w, y)
-        run()  # first launch: no timing
+        try:
+            run()  # first launch: no timing
+        except RuntimeError:  # a configuration this shape cannot use (alignment, size)
+            times.append(float("inf"))
+            continue
         t = float("inf")
         for _ in range(2):
             flush.zero_()  # cold L2, and keeps the GPU busy while the timed launch is enqueued
@@ -159,13 +209,33 @@ def _autotune(x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor,
     return cands[min(range(len(cands)), key=times.__getitem__)]
 
 
-def _runner(cfg, x2, w, y):
-    pair, swap, bn, splits = cfg
-    if bn == 0:
+def _sk_buffers(device: torch.device, ws_floats: int, counters: int):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws, cnt = _SK_WS.get(idx), _SK_CNT.get(idx)
+    if ws is None or ws.numel() < ws_floats or cnt is None or cnt.numel() < counters:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("stream-K GEMM buffers must be sized before CUDA-graph capture (run once eagerly)")
+        # Replaced buffers stay alive: CUDA graphs captured earlier still point at them.
+        if ws is None or ws.numel() < ws_floats:
+            _RETIRED.append(ws)
+            ws = _SK_WS[idx] = torch.empty(max(ws_floats, 1 << 20), dtype=torch.float32, device=device)
+        if cnt is None or cnt.numel() < counters:
+            _RETIRED.append(cnt)
+            cnt = _SK_CNT[idx] = torch.zeros(max(counters, 4096), dtype=torch.int32, device=device)
+    return ws, cnt
+
+
+def _runner(cfg: Cfg, x2, w, y):
+    if cfg.kind == "lib":
         return lambda: torch.matmul(x2, w.t(), out=y)
     M, N = x2.shape[0], w.shape[0]
-    ws = workspace(x2.device, splits * M * N) if splits > 1 else None
-    return lambda: native().gemm_bf16(y, x2, w, swap, bn, splits, ws, None, pair)
+    if cfg.kind == "sk":
+        nt = cfg.bn * cfg.splits
+        tiles = math.ceil(N / 256) * math.ceil(M / nt)
+        ws, cnt = _sk_buffers(x2.device, cfg.clusters * 4 * nt * 128, 2 * tiles)
+        return lambda: native().gemm_bf16_sk(y, x2, w, cfg.bn, cfg.splits, cfg.clusters, ws, cnt)
+    ws = workspace(x2.device, cfg.splits * M * N) if cfg.splits > 1 else None
+    return lambda: native().gemm_bf16(y, x2, w, cfg.swap, cfg.bn, cfg.splits, ws, None, cfg.kind == "pair")
 
 
 def _agree(times):
@@ -191,7 +261,7 @@ def _agree(times):
 
 
 def plan(M: int, N: int, K: int, x2: Optional[torch.Tensor] = None, w: Optional[torch.Tensor] = None,
-         y: Optional[torch.Tensor] = None) -> Tuple[bool, bool, int, int]:
+         y: Optional[torch.Tensor] = None) -> Cfg:
     """Configuration for y[M, N] = x[M, K] w[N, K]^T (see the module docstring)."""
     _load()
     inv = batch_invariant()
@@ -202,7 +272,7 @@ def plan(M: int, N: int, K: int, x2: Optional[torch.Tensor] = None, w: Optional[
     fixed = invariant_splits(N, K) if inv else None
     if (x2 is None or os.environ.get("SH_GEMM_TUNE", "1") == "0" or torch.cuda.is_current_stream_capturing()):
         h = heuristic(M, N, K)
-        return h if fixed is None else (h[0], h[1], h[2], fixed)
+        return h if fixed is None else h._replace(splits=fixed)
     got = _autotune(x2, w, y, fixed)
     _CHOICE[key] = got
     if not inv:
@@ -228,7 +298,7 @@ def plan_push(x2: torch.Tensor, w: torch.Tensor) -> Tuple[bool, int]:
     if torch.cuda.is_current_stream_capturing() or os.environ.get("SH_GEMM_TUNE", "1") == "0":
         return (M > 128, 256 if M > 128 else 128)
     y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
-    cands = [(False, False, bn, 1) for bn in (64, 128, 256)] + [(True, False, bn, 1) for bn in (128, 192, 256)]
+    cands = [Cfg("tc", False, bn, 1) for bn in (64, 128, 256)] + [Cfg("pair", False, bn, 1) for bn in (128, 192, 256)]
     dev = x2.device
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     flush = _FLUSH.get(idx)
@@ -251,15 +321,16 @@ def plan_push(x2: torch.Tensor, w: torch.Tensor) -> Tuple[bool, int]:
         times.append(t)
     times = _agree(times)
     best = cands[min(range(len(cands)), key=times.__getitem__)]
-    _PUSH[key] = (best[0], best[2])
+    _PUSH[key] = (best.kind == "pair", best.bn)
     return _PUSH[key]
 
 
 def choice_summary() -> dict:
     """How many tuned shapes run which kernel family (for benchmark reports)."""
-    out = {"tcgen05_one_cta": 0, "tcgen05_pair": 0, "cublas": 0}
+    names = {"tc": "tcgen05_one_cta", "pair": "tcgen05_pair", "sk": "tcgen05_streamk", "lib": "cublas"}
+    out = {v: 0 for v in names.values()}
     for cfg in _CHOICE.values():
-        out["cublas" if cfg[2] == 0 else ("tcgen05_pair" if cfg[0] else "tcgen05_one_cta")] += 1
+        out[names[cfg.kind]] += 1
     return out
 
 
@@ -269,6 +340,7 @@ def workspace(device: torch.device, numel: int) -> torch.Tensor:
     if ws is None or ws.numel() < numel:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("GEMM split-K workspace must be sized before CUDA-graph capture (run once eagerly)")
+        _RETIRED.append(ws)  # graphs captured earlier may still point at it
         ws = torch.empty(max(numel, 1 << 20), dtype=torch.float32, device=device)
         _WS[idx] = ws
     return ws

@@ -4,7 +4,9 @@
 kernels (one-shot / two-shot, fused with residual-add + RMSNorm where the
 caller asks for it) when the fused runtime is up, else NCCL (the baseline).
 ``vocab_parallel_argmax`` never gathers logits: every rank reduces its vocab
-slice to (max, index) pairs and only those pairs cross the links.
+slice to (max, index) keys and only those keys cross the links -- in one
+kernel over NVLink peer memory when the fused runtime is up (``_C.argmax_tp``),
+else as an NCCL all-gather of (value, id) pairs (the baseline).
 """
 from __future__ import annotations
 
@@ -93,6 +95,8 @@ def vocab_parallel_argmax(local_logits: torch.Tensor, vocab_offset: int, out: Op
     from .. import ops
 
     st = state.get()
+    if st.tp > 1 and _FUSED is not None and _FUSED.can_argmax(local_logits):
+        return _FUSED.argmax(local_logits, vocab_offset, out)
     idx = ops.argmax(local_logits, out=None if st.tp > 1 else out)
     if st.tp == 1:
         return idx

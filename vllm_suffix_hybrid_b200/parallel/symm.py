@@ -62,7 +62,17 @@ class SymmComm:
         self.peer_flags = [int(x) for x in h_f.buffer_ptrs]
         cnt_off = PHASES * MAX_BLOCKS * MAX_WORLD * 4
         self.peer_rs_cnt = [p + cnt_off for p in self.peer_flags]
-        self._handles = (h_r, h_g, h_f, h_gr)
+        # Vocab-parallel argmax: keys [2][world][max_tokens] (u64) then flags [MAX_BLOCKS][MAX_WORLD] (u32).
+        self.key_words = 2 * self.world * max_tokens
+        self.argmax_buf = symm_mem.empty(self.key_words * 2 + MAX_BLOCKS * MAX_WORLD, dtype=torch.int32, device=dev)
+        self.argmax_buf.zero_()
+        torch.cuda.synchronize()
+        h_a = symm_mem.rendezvous(self.argmax_buf, name)
+        self.peer_keys = [int(x) for x in h_a.buffer_ptrs]
+        self.peer_argmax_flags = [p + self.key_words * 8 for p in self.peer_keys]
+        self.argmax_counters = torch.zeros(MAX_BLOCKS, dtype=torch.int32, device=dev)
+        self.argmax_blocks = min(MAX_BLOCKS, 64)
+        self._handles = (h_r, h_g, h_f, h_gr, h_a)
         self.targets = torch.zeros(2 * MAX_BLOCKS, dtype=torch.int32, device=dev)
         # Row-parallel GEMMs push their rows straight to the owners (reduce-scatter in
         # the GEMM epilogue) and rs_norm_ag finishes; SH_TP_PUSH=0 keeps the
@@ -171,6 +181,25 @@ class SymmComm:
                                 self.rank, pp.T, self.hidden, self.max_tokens, self.owner_rows(pp.T), pp.expected,
                                 eps, gather_residual, self.blocks, self.timing, pf, pf_bytes)
         return out
+
+    # -- vocab-parallel argmax --------------------------------------------------
+    def can_argmax(self, logits: torch.Tensor) -> bool:
+        return (logits.is_cuda and logits.dtype == torch.bfloat16 and logits.dim() == 2 and logits.stride(1) == 1
+                and logits.shape[0] <= self.max_tokens and (logits.stride(0) * 2) % 16 == 0
+                and logits.data_ptr() % 16 == 0)
+
+    def argmax(self, logits: torch.Tensor, vocab_offset: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Global greedy ids of vocab-sharded logits [T, V/tp] in one kernel (keys over NVLink)."""
+        from .. import ops
+
+        dst = out if out is not None and out.is_contiguous() and out.dtype == torch.int64 else \
+            torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+        ops.native().argmax_tp(dst, logits, self.peer_keys, self.peer_argmax_flags, self.argmax_counters, self.err,
+                               self.rank, self.max_tokens, vocab_offset, self.argmax_blocks)
+        if out is not None and dst is not out:
+            out.copy_(dst)
+            return out
+        return dst
 
     def check(self) -> None:
         code = int(self.err.item())
