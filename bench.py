@@ -106,6 +106,16 @@ def main():
     if args.impl == "reference":
         reference_arm(args)
         return
+    import faulthandler
+
+    t_start = time.perf_counter()
+
+    def progress(msg):  # stderr breadcrumbs: a run that is killed still shows how far it got
+        print(f"[bench +{time.perf_counter() - t_start:7.1f}s rank {os.environ.get('RANK', '0')}] {msg}",
+              file=sys.stderr, flush=True)
+
+    if os.environ.get("SH_BENCH_STACKS_AFTER_S"):  # dump every thread's stack if still running after N s
+        faulthandler.dump_traceback_later(float(os.environ["SH_BENCH_STACKS_AFTER_S"]), exit=False)
 
     import numpy as np
     import torch
@@ -130,7 +140,9 @@ def main():
                        max_num_seqs=args.batch, device="cuda", cuda_graphs=not args.no_graphs)
     if args.split == "diverge":
         os.environ["SUFFIX_HYBRID_SPLIT"] = "diverge"
+    progress("building the engine")
     eng = LLMEngine(cfg)
+    progress("engine ready; prefill")
     prompts = make_streams(args.batch, args.prompt_len, mcfg.vocab, seed=1234)
     for p in prompts:
         eng.add_request(p, args.max_new)
@@ -148,12 +160,17 @@ def main():
     # steps sit around the middle of the generation instead of right after prefill.  Every rank runs the
     # same steps (the engine state is replicated), so the loop ends on the same step everywhere.
     start_at = args.timed_from if args.timed_from >= 0 else max(0, args.max_new // 2 - (args.warmup + args.steps) // 2)
+    progress(f"prefill done in {prefill_s:.1f}s; advancing to {start_at} generated tokens")
     advanced = 0
     while eng.running and min(len(r.output) for r in eng.running) < start_at:
         eng.step()
         advanced += 1
+        if advanced % 50 == 0:
+            progress(f"advanced {advanced} steps")
+    progress(f"advanced {advanced} steps; warm-up")
     for _ in range(args.warmup):
         eng.step()
+    progress("timed steps")
     if args.profile:
         eng.runner.use_graphs = False
         torch.cuda.synchronize()
@@ -169,7 +186,8 @@ def main():
     if cfg.cuda_graphs:
         r = eng.runner
         ctr = ops.count_launches(True)
-        r._decode_body(len(eng.running) if len(eng.running) in r.graphs else max(r.graphs))
+        nb, wd = max(r.graphs, key=lambda kw: (kw[0] == len(eng.running), kw[1]))
+        r._decode_body(nb, wd)
         ops.count_launches(False)
         n_launch_step = ctr.count
     torch.cuda.synchronize()

@@ -274,8 +274,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       const int tw = s.tile / g.tiles_x, tx = s.tile % g.tiles_x;
       const int y_w = tw * (2 * ROWS) + static_cast<int>(rank) * ROWS;  // output column of row 0
       const int y_x0 = tx * C::NT;                                        // output row of token 0
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
-        if (lane == 0) raise(4);
+      // The epilogue warps leave together (they meet at named barriers below).
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag);
+      if (named_barrier_any(1, EPI_THREADS, !ok)) {
+        if (elected) raise(4);
         break;
       }
       fence_after();

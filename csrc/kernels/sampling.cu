@@ -83,19 +83,21 @@ __global__ void argmax_rows_kernel(int64_t* __restrict__ out, const T* __restric
   }
 }
 
-// One thread per request.
+// One thread per request.  Row strides (elements) let the step verify the
+// first W columns of wider static buffers.
 __global__ void spec_verify_kernel(const int64_t* __restrict__ draft, const int64_t* __restrict__ target,
                                    int64_t* __restrict__ seq_lens, int64_t* __restrict__ out_tokens,
-                                   int32_t* __restrict__ accept, int64_t* __restrict__ next_token, int batch, int k) {
+                                   int32_t* __restrict__ accept, int64_t* __restrict__ next_token, int batch, int k,
+                                   int64_t ld_d, int64_t ld_t, int64_t ld_o) {
   shk::pdl_trigger();
   shk::pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
-  const int64_t* d = draft + (int64_t)b * k;
-  const int64_t* t = target + (int64_t)b * (k + 1);
+  const int64_t* d = draft + (int64_t)b * ld_d;
+  const int64_t* t = target + (int64_t)b * ld_t;
   int a = 0;
   while (a < k && d[a] >= 0 && d[a] == t[a]) ++a;
-  int64_t* o = out_tokens + (int64_t)b * (k + 1);
+  int64_t* o = out_tokens + (int64_t)b * ld_o;
   for (int i = 0; i < a; ++i) o[i] = d[i];
   o[a] = t[a];
   for (int i = a + 1; i <= k; ++i) o[i] = -1;
@@ -206,13 +208,16 @@ void spec_verify(torch::Tensor draft, torch::Tensor target, torch::Tensor seq_le
                  torch::Tensor accept, torch::Tensor next_token) {
   TORCH_CHECK(draft.scalar_type() == at::kLong && target.scalar_type() == at::kLong, "spec_verify: int64 tokens");
   TORCH_CHECK(seq_lens.scalar_type() == at::kLong && accept.scalar_type() == at::kInt, "spec_verify: dtypes");
-  TORCH_CHECK(draft.is_contiguous() && target.is_contiguous() && out_tokens.is_contiguous(), "contiguous");
+  TORCH_CHECK(draft.dim() == 2 && target.dim() == 2 && out_tokens.dim() == 2 && draft.stride(1) == 1 &&
+                  target.stride(1) == 1 && out_tokens.stride(1) == 1, "spec_verify: row-major [B, *] views");
   const int batch = draft.size(0), k = draft.size(1);
   TORCH_CHECK(target.size(0) == batch && target.size(1) == k + 1, "target must be [B, k+1]");
+  TORCH_CHECK(out_tokens.size(0) >= batch && out_tokens.size(1) == k + 1, "out_tokens must be [B, k+1]");
   if (batch == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   shk::launch(spec_verify_kernel, dim3((batch + 127) / 128), dim3(128), 0, stream, 
       draft.data_ptr<int64_t>(), target.data_ptr<int64_t>(), seq_lens.data_ptr<int64_t>(),
-      out_tokens.data_ptr<int64_t>(), accept.data_ptr<int32_t>(), next_token.data_ptr<int64_t>(), batch, k);
+      out_tokens.data_ptr<int64_t>(), accept.data_ptr<int32_t>(), next_token.data_ptr<int64_t>(), batch, k,
+      draft.stride(0), target.stride(0), out_tokens.stride(0));
   SH_CUDA_CHECK(cudaGetLastError());
 }

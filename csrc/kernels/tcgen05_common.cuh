@@ -145,6 +145,18 @@ __device__ __forceinline__ void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Barrier over a subset of warps that also ORs a predicate over its threads:
+// every participant gets the same answer.
+__device__ __forceinline__ bool named_barrier_any(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %3, 0;\n bar.red.or.pred q, %1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(id), "r"(count), "r"(pred ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
 // ----------------------------------------------------------------- clusters
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;

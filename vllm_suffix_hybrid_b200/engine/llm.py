@@ -100,6 +100,7 @@ class LLMEngine:
         mcfg = cfg.model
         spec = cfg.spec
         self.k = spec.k if spec.method != "none" else 0
+        self.adaptive_width = bool(getattr(spec, "adaptive_width", True))
         self.model, self.draft = build_model(mcfg, dev, cfg.seed, with_draft=spec.method in ("hybrid", "native"))
         if (st.tp > 1 or st.ep > 1) and cfg.parallel.comm == "fused" and torch.device(dev).type == "cuda":
             from ..parallel import comm as pcomm
@@ -204,6 +205,68 @@ class LLMEngine:
         self.waiting.append(Request(rid, p, max_new_tokens, arrival=time.time(),
                                     stop_ids=frozenset(int(t) for t in (stop_token_ids or ()))))
         return rid
+
+    def admit_prefilled(self, prompts, max_new_tokens: int = 128, seed: int = 0) -> List[str]:
+        """Benchmark helper: admit requests as if their prompts had been prefilled, without the prefill pass.
+
+        Decode throughput at long contexts (32k-128k tokens per request) is measured on a cache of the
+        right size; a real prefill of millions of prompt tokens would dominate the run.  The requests get
+        their blocks, slot and token history (the proposers see the full prompt), the cache contents are
+        set once to random values of the cache's format (finite bf16 / fp8 / NVFP4 codes; recurrent
+        states zero), and each request's first output token is drawn at random.  Every decode step after
+        this does its full work; only the prefill forward is skipped.
+        """
+        rng = np.random.default_rng(seed)
+        if not getattr(self, "_synthetic_cache", False):
+            self._fill_caches_random(seed)
+            self._synthetic_cache = True
+        rids = []
+        for p in prompts:
+            if len(self.running) >= self.cfg.max_num_seqs:
+                raise RuntimeError("admit_prefilled: more requests than max_num_seqs")
+            rid = self.add_request(p, max_new_tokens)
+            r = self.waiting.pop()
+            self._ensure_blocks(r, len(r.prompt) + 2 * self.k + 2)
+            r.slot = self._free_slots.pop()
+            row = len(self.running)
+            self.running.append(r)
+            self.tokens[row, :len(r.prompt)] = r.prompt
+            r.committed = len(r.prompt)
+            self._emit(r, row, [int(rng.integers(0, self.cfg.model.vocab))])
+            r.drafts = []
+            rids.append(rid)
+        self._propose(batch_native=True)
+        return rids
+
+    def _fill_caches_random(self, seed: int) -> None:
+        gen = torch.Generator(device=self.device).manual_seed(seed) if torch.device(self.device).type == "cuda" \
+            else torch.Generator().manual_seed(seed)
+
+        def fill(x):
+            if isinstance(x, torch.Tensor):
+                if x.dtype in (torch.bfloat16, torch.float16, torch.float32):
+                    x.normal_(0.0, 1.0, generator=gen)
+                elif x.dtype == torch.uint8:  # packed rows (e2m1 / e4m3 / bf16 bytes): small finite values
+                    x.random_(0, 0x40, generator=gen)
+                elif x.dtype == torch.float8_e4m3fn:
+                    x.view(torch.uint8).random_(0, 0x40, generator=gen)
+            elif isinstance(x, dict):
+                for v in x.values():
+                    fill(v)
+            elif isinstance(x, (list, tuple)):
+                for v in x:
+                    fill(v)
+            elif hasattr(x, "__dict__"):
+                for name, v in vars(x).items():
+                    if "state" in name:  # recurrent (GDN) states start from zero, as after a real prefill reset
+                        if isinstance(v, torch.Tensor):
+                            v.zero_()
+                        continue
+                    fill(v)
+
+        fill(self.caches)
+        if self.dcaches is not None:
+            fill(self.dcaches)
 
     def abort_request(self, rid: str) -> bool:
         """Stop a request; a running one leaves at this step boundary. False if unknown or done."""
@@ -466,14 +529,19 @@ class LLMEngine:
             self._ensure_blocks(r, r.committed + 2 * k + 2)
             b = r.blocks_np
             bt[i, :b.shape[0]] = b
+        width = W
         if n:
             win[:, 0] = np.fromiter((r.next_token for r in self.running), dtype=np.int64, count=n)
             seq[:] = np.fromiter((r.committed for r in self.running), dtype=np.int64, count=n)
             if k:
                 win[:, 1:] = [r.drafts[:k] if len(r.drafts) >= k else r.drafts + [-1] * (k - len(r.drafts))
                               for r in self.running]
+                if self.adaptive_width and nb_min == 0:
+                    # Verify only as wide as the longest real draft (-1 pads never match a target token).
+                    real = (win[:, 1:] >= 0).cumprod(axis=1).sum(axis=1)
+                    width = 1 + int(real.max())
         t1 = time.perf_counter()
-        out, acc, nat = self.runner.decode(n, win, seq, bt, slots, nb_min=nb_min)
+        out, acc, nat = self.runner.decode(n, win, seq, bt, slots, nb_min=nb_min, width=width)
         t2 = time.perf_counter()
         emitted = 0
         accepted = 0

@@ -10,9 +10,16 @@ Decode step for a batch of B requests, each with a verify window
      tokens = the verified next tokens) -> first native draft from row a;
   5. k-1 single-token draft steps -> native drafts [B, k].
 
-Everything after the host upload is static-shape per batch bucket, so the
-whole step is captured once per bucket as a CUDA graph and replayed.
-Padded rows of a bucket point at the reserved scratch block 0.
+Everything after the host upload is static-shape per (batch bucket, verify
+width), so the whole step is captured once per pair as a CUDA graph and
+replayed.  The verify width W of a step is 1 + the longest draft any row
+publishes (at most k + 1): when every row's drafts are short -- suffix-only
+or n-gram misses, EWMA-gated widths -- the step verifies fewer tokens per
+row, and a step with no drafts at all is a plain 1-token decode (reference
+behaviour: ragged widths, width-0 rows cost a plain decode,
+suffix_hybrid/wrap_v2.py:1503-1569).  Rows with fewer drafts than W - 1 are
+padded with -1, which never matches a target token.  Padded rows of a
+bucket point at the reserved scratch block 0.
 """
 from __future__ import annotations
 
@@ -76,12 +83,13 @@ class Runner:
         self.h_nat = torch.zeros(B, max(k, 1), dtype=torch.long, pin_memory=pin)
         self.h_slots = torch.zeros(B, dtype=torch.long, pin_memory=pin)
         self._tiles: Dict[tuple, tuple] = {}
-        self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}  # (bucket, verify width) -> graph
         self.event = torch.cuda.Event() if pin else None
         # Device time of the last decode step (H2D of its inputs .. D2H of its results).
         self.ev0 = torch.cuda.Event(enable_timing=True) if pin else None
         self.ev1 = torch.cuda.Event(enable_timing=True) if pin else None
         self.last_device_ms = 0.0
+        self.last_width = self.W
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self._async = None  # buffers of the pipelined (async-scheduling) step, made on first use
@@ -146,7 +154,7 @@ class Runner:
         A["h_used"][parity][:nb].copy_(self.win[:nb], non_blocking=True)
         A["h_real"][parity][:nb].copy_(A["real"][:nb], non_blocking=True)
         if self.use_graphs:
-            g = self.graphs.get(nb)
+            g = self.graphs.get((nb, self.W))
             if g is None:
                 raise RuntimeError("capture the bucket's graph with a synchronous step first")
             g.replay()
@@ -172,7 +180,7 @@ class Runner:
                 A["h_real"][parity][:nb_real].numpy())
 
     def has_graph(self, nb_real: int) -> bool:
-        return not self.use_graphs or bucket_for(nb_real, self.max_batch) in self.graphs
+        return not self.use_graphs or (bucket_for(nb_real, self.max_batch), self.W) in self.graphs
 
     # ------------------------------------------------------------------ helpers
     def _tile_tensors(self, nb: int, qlen: int):
@@ -210,28 +218,28 @@ class Runner:
         return torch.stack(drafts, 1)
 
     # ------------------------------------------------------------------ decode
-    def _decode_body(self, nb: int) -> None:
-        W = self.W
-        win, L, bt = self.win[:nb], self.seq[:nb], self.bt[:nb]
-        pos = L[:, None] + self.ar_w[None, :]
+    def _decode_body(self, nb: int, W: Optional[int] = None) -> None:
+        W = self.W if W is None else W
+        win, L, bt = self.win[:nb, :W], self.seq[:nb], self.bt[:nb]
+        pos = L[:, None] + self.ar_w[None, :W]
         meta = self._meta(nb, W, pos, bt, L + W)
         meta.state_slots, meta.pending, meta.window = self.slots[:nb], self.pending, W
         hid, pre = self.model.forward(win.reshape(-1), meta, self.caches)
-        self.target[:nb].copy_(self.model.greedy(hid).view(nb, W))
+        target = self.target[:nb, :W]
+        target.copy_(self.model.greedy(hid).view(nb, W))
         lnew = self.seq_new[:nb]
         lnew.copy_(L)
-        if self.k > 0:
-            ops.spec_verify(win[:, 1:].contiguous(), self.target[:nb], lnew, self.out_tokens[:nb],
-                            self.accept[:nb], self.next_tok[:nb])
+        if W > 1:
+            ops.spec_verify(win[:, 1:], target, lnew, self.out_tokens[:nb, :W], self.accept[:nb], self.next_tok[:nb])
         else:
-            self.out_tokens[:nb].copy_(self.target[:nb])
+            self.out_tokens[:nb, :1].copy_(target)
             self.accept[:nb].zero_()
-            self.next_tok[:nb].copy_(self.target[:nb, 0])
+            self.next_tok[:nb].copy_(target[:, 0])
             lnew.add_(1)
         if self.recurrent:  # deferred commit: the next window replays accept+1 records
             self.pending.index_copy_(0, self.slots[:nb], (self.accept[:nb] + 1).to(torch.int32))
         if self.draft is not None and self.k > 0:
-            tok_in = self.out_tokens[:nb].clamp_min(0)
+            tok_in = self.out_tokens[:nb, :W].clamp_min(0)
             dh, dpre = self.draft.forward(tok_in.reshape(-1), pre, meta, self.dcaches)
             sel = self.ar_b[:nb] * W + self.accept[:nb].long()
             d1 = self.model.greedy(dh.index_select(0, sel))
@@ -239,10 +247,14 @@ class Runner:
             self.native[:nb].copy_(self._draft_steps(d1, f1, lnew, bt, nb))
 
     def decode(self, nb_real: int, win: np.ndarray, seq: np.ndarray, bt: np.ndarray, slots: np.ndarray = None,
-               nb_min: int = 0):
+               nb_min: int = 0, width: Optional[int] = None):
         """Run one decode step; returns host views (out_tokens, accept, native).  nb_min raises the batch
-        bucket (data-parallel ranks run the same bucket; rows past nb_real are scratch padding)."""
+        bucket (data-parallel ranks run the same bucket; rows past nb_real are scratch padding).  width:
+        the step's verify width (1..k+1, default k+1); win columns past it are not read."""
         nb = bucket_for(max(nb_real, nb_min, 1), self.max_batch)
+        W = self.W if width is None else int(width)
+        if not 1 <= W <= self.W:
+            raise ValueError(f"verify width {W} outside 1..{self.W}")
         self.h_win[:nb_real].numpy()[:] = win
         self.h_seq[:nb_real].numpy()[:] = seq
         self.h_bt[:nb_real].numpy()[:, :bt.shape[1]] = bt
@@ -260,12 +272,12 @@ class Runner:
         self.bt[:nb, :nbt].copy_(self.h_bt[:nb, :nbt], non_blocking=True)
         self.slots[:nb].copy_(self.h_slots[:nb], non_blocking=True)
         if self.use_graphs:
-            g = self.graphs.get(nb)
+            g = self.graphs.get((nb, W))
             if g is None:
-                g = self._capture(nb)
+                g = self._capture(nb, W)
             g.replay()
         else:
-            self._decode_body(nb)
+            self._decode_body(nb, W)
         self.h_out[:nb].copy_(self.out_tokens[:nb], non_blocking=True)
         self.h_acc[:nb].copy_(self.accept[:nb], non_blocking=True)
         if self.draft is not None and self.k > 0:
@@ -276,9 +288,10 @@ class Runner:
             self.last_device_ms = self.ev0.elapsed_time(self.ev1)
         self.h2d_bytes = nb * (self.W * 8 + 8 + 8 + self.max_blocks * 4)
         self.d2h_bytes = nb * (self.W * 8 + 4 + (self.k * 8 if self.draft is not None and self.k > 0 else 0))
+        self.last_width = W
         return self.h_out[:nb_real].numpy(), self.h_acc[:nb_real].numpy(), self.h_nat[:nb_real].numpy()
 
-    def _capture(self, nb: int):
+    def _capture(self, nb: int, W: Optional[int] = None):
         # Warm-up and capture run on scratch rows only (block 0, state slot 0):
         # a warm-up iteration really executes, and state that is committed
         # rather than rewritten (deferred recurrent commit) must not see it.
@@ -288,14 +301,15 @@ class Runner:
         self.slots[:nb].zero_()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
+        W = self.W if W is None else W
         with torch.cuda.stream(s):
             for _ in range(2):
-                self._decode_body(nb)
+                self._decode_body(nb, W)
         torch.cuda.current_stream().wait_stream(s)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            self._decode_body(nb)
-        self.graphs[nb] = g
+            self._decode_body(nb, W)
+        self.graphs[(nb, W)] = g
         # Restore this step's real inputs (still in the pinned staging buffers).
         nbt = self.max_blocks
         self.win[:nb].copy_(self.h_win[:nb], non_blocking=True)
