@@ -31,6 +31,16 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 
+# Per-config workload: requests, prompt and output lengths, layout.
+CONFIG_DEFAULTS = {
+    "llama3-8b": dict(batch=64, prompt_len=2048, max_new=512, layout="tp", synthetic_prefill=False),
+    "qwen3-next": dict(batch=32, prompt_len=8192, max_new=1024, layout="dp-ep", synthetic_prefill=True),
+    "deepseek-v3.2": dict(batch=32, prompt_len=32768, max_new=1024, layout="dp-ep", synthetic_prefill=True),
+    "kimi-k2": dict(batch=64, prompt_len=131072, max_new=1024, layout="dp-ep", synthetic_prefill=True,
+                    streams=dict(p_copy=0.6, corpus_n=256), env={"SUFFIX_HYBRID_NGRAM_WINDOW": "8192"}),
+}
+
+
 def reference_arm(args):
     why = ("reference build backend unavailable offline: the reference is a maturin (Rust/PyO3) package and "
            "neither maturin nor cargo is installed; its native module suffix_hybrid._native cannot be built, "
@@ -85,9 +95,15 @@ def main():
     ap.add_argument("--config", default="llama3-8b")
     ap.add_argument("--method", default="hybrid")
     ap.add_argument("--split", default="legacy")
-    ap.add_argument("--batch", type=int, default=64)
-    ap.add_argument("--prompt-len", type=int, default=2048)
-    ap.add_argument("--max-new", type=int, default=512)
+    ap.add_argument("--batch", type=int, default=0, help="global requests (default: the config's)")
+    ap.add_argument("--prompt-len", type=int, default=0, help="prompt tokens (default: the config's)")
+    ap.add_argument("--max-new", type=int, default=0, help="output tokens per request (default: the config's)")
+    ap.add_argument("--layout", default="", choices=["", "tp", "dp-ep"],
+                    help="tp: tensor parallel over the N GPUs; dp-ep: data-parallel attention (each rank serves "
+                         "its own requests) with the MoE experts split over the N ranks (default: the config's)")
+    ap.add_argument("--synthetic-prefill", default="", choices=["", "0", "1"],
+                    help="1: admit the prompts with a randomly filled KV cache instead of running the prefill "
+                         "forward (long-context decode benches; default: on for the 32k/128k configs)")
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--timed-from", type=int, default=-1,
                     help="generated tokens per request before the warm-up steps start (default: the timed window "
@@ -128,27 +144,48 @@ def main():
     from vllm_suffix_hybrid_b200.parallel import state as pstate
     from vllm_suffix_hybrid_b200.utils.clocks import ClockSampler
 
-    st = pstate.init(tp=args.gpus)
+    d = CONFIG_DEFAULTS[args.config]
+    args.batch = args.batch or d["batch"]
+    args.prompt_len = args.prompt_len or d["prompt_len"]
+    args.max_new = args.max_new or d["max_new"]
+    layout = args.layout or d["layout"]
+    synthetic = (args.synthetic_prefill or ("1" if d["synthetic_prefill"] else "0")) == "1"
+    for key, val in d.get("env", {}).items():
+        os.environ.setdefault(key, val)
+    n = args.gpus
+    if layout == "dp-ep" and n > 1:
+        st = pstate.init(ep=n, dp=n)
+    else:
+        st = pstate.init(tp=n)
     rank, world = st.rank, st.world
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
+    if layout == "dp-ep" and args.batch % max(world, 1):
+        raise SystemExit(f"--batch {args.batch} must split evenly over {world} data-parallel ranks")
+    local_batch = args.batch // world if layout == "dp-ep" else args.batch
     mcfg = PRESETS[args.config]()
     if args.layers:
         mcfg.layers = args.layers
+    par = (ParallelConfig(ep=n, dp=n, comm=args.comm) if layout == "dp-ep" and n > 1
+           else ParallelConfig(tp=n, comm=args.comm))
     cfg = EngineConfig(model=mcfg, spec=SpecConfig(method=args.method, k=args.k, split=args.split),
-                       parallel=ParallelConfig(tp=args.gpus, comm=args.comm),
+                       parallel=par,
                        cache=CacheConfig(max_model_len=args.prompt_len + args.max_new + 4 * args.k + 64),
-                       max_num_seqs=args.batch, device="cuda", cuda_graphs=not args.no_graphs)
+                       max_num_seqs=local_batch, device="cuda", cuda_graphs=not args.no_graphs)
     if args.split == "diverge":
         os.environ["SUFFIX_HYBRID_SPLIT"] = "diverge"
     progress("building the engine")
     eng = LLMEngine(cfg)
     progress("engine ready; prefill")
-    prompts = make_streams(args.batch, args.prompt_len, mcfg.vocab, seed=1234)
-    for p in prompts:
-        eng.add_request(p, args.max_new)
+    prompts = make_streams(args.batch, args.prompt_len, mcfg.vocab, seed=1234, **d.get("streams", {}))
+    mine = prompts[rank::world] if layout == "dp-ep" else prompts
     t_pf = time.perf_counter()
-    while eng.waiting:
-        eng.step()
+    if synthetic:
+        eng.admit_prefilled(mine, args.max_new, seed=1234 + rank)
+    else:
+        for p in mine:
+            eng.add_request(p, args.max_new)
+        while eng.waiting:
+            eng.step()
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t_pf
 
@@ -161,8 +198,17 @@ def main():
     # same steps (the engine state is replicated), so the loop ends on the same step everywhere.
     start_at = args.timed_from if args.timed_from >= 0 else max(0, args.max_new // 2 - (args.warmup + args.steps) // 2)
     progress(f"prefill done in {prefill_s:.1f}s; advancing to {start_at} generated tokens")
+    def below_start() -> bool:
+        """Whether any request (on any rank, in the data-parallel layout) is short of the window start."""
+        mine = bool(eng.running) and min(len(r.output) for r in eng.running) < start_at
+        if layout == "dp-ep" and world > 1:  # ranks step in lockstep: agree on the loop's end
+            flag = torch.tensor([1 if mine else 0], dtype=torch.int32)
+            dist.all_reduce(flag, group=st.cpu_group)
+            return int(flag.item()) > 0
+        return mine
+
     advanced = 0
-    while eng.running and min(len(r.output) for r in eng.running) < start_at:
+    while below_start():
         eng.step()
         advanced += 1
         if advanced % 50 == 0:
@@ -220,6 +266,10 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=st.group)
     dev_ms, wall = float(t[0]), float(t[1])
+    if layout == "dp-ep" and world > 1:  # every rank emits for its own requests: the box's output is the sum
+        c = torch.tensor([tokens, rows], dtype=torch.float64, device="cuda")
+        dist.all_reduce(c, group=st.group)
+        tokens, rows = int(c[0]), int(c[1])
     from vllm_suffix_hybrid_b200.ops import gemm as _gemm
 
     gemm_choices = _gemm.choice_summary()
@@ -238,12 +288,16 @@ def main():
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": "bf16",
-            "data": "synthetic (config-0 span-reuse token streams, vocab 128256); random-init weights N(0,0.02)",
-            "config": {"model": "llama3-8b-shape" if args.config == "llama3-8b" else args.config,
+            "data": (f"synthetic (span-reuse token streams, vocab {mcfg.vocab}); random-init weights "
+                     f"({mcfg.weight_format})" + ("; prompts admitted with a random-filled KV cache (prefill "
+                                                  "forward skipped, every decode step complete)" if synthetic else "")),
+            "config": {"model": "llama3-8b-shape" if args.config == "llama3-8b" else f"{args.config}-shape",
                        "global_batch": args.batch, "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
-                       "k": args.k, "method": args.method, "split": args.split, "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
+                       "k": args.k, "method": args.method, "split": args.split,
+                       "parallelism": (f"dp{world}-ep{world}" if layout == "dp-ep" and world > 1 else f"tp{world}"),
+                       "comm": args.comm if world > 1 else "none",
                        "l2": "working set (weights + KV) >> 126 MB L2; no flush",
-                       "layers": mcfg.layers},
+                       "layers": mcfg.layers, "weights": mcfg.weight_format, "kv_cache": mcfg.kv_format},
             "mean_accept_len": round(tokens / rows, 4),
             "timed_window": {"untimed_steps_before_warmup": advanced, "min_context_at_first_timed_step": ctx0},
             "proposer_us_per_step": round(prop_us, 2),

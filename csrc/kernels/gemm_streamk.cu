@@ -10,17 +10,25 @@
 //   every token of the call in one tile, each weight byte is read from HBM by
 //   exactly one CTA, and each SM pulls only 128 + NT/2 operand rows per 64-wide
 //   k-block for 128 x NT x 64 MACs (NT = 384: 77 MAC per byte of L2 traffic).
-// * Stream-K: the tiles x k-blocks iteration space is cut into one contiguous
-//   range per cluster (G ranges), so every SM has the same amount of MMA work
-//   whatever the tile count (no partial last wave).  A tile cut by a range
-//   boundary is summed by the LAST cluster to finish a piece of it: every
-//   piece stores its fp32 partial in a fixed slot, bumps the tile's arrival
-//   counter, and the piece that sees the final count adds all partials in
-//   cluster order (fixed order: the result does not depend on timing) and
-//   stores the tile.  No CTA waits for another, so there is no co-residency
+// * Stream-K with the split pieces first: with U tiles on G clusters, every
+//   cluster owns q = U / G whole tiles, and the k-blocks of the remaining
+//   r = U % G tiles are cut into one contiguous range per cluster (over the
+//   first G_sk clusters), so every SM gets the same MMA work whatever the
+//   tile count (no partial last wave).  Each cluster runs its split piece
+//   FIRST and its whole tiles after it: a split tile is summed by the LAST
+//   cluster to finish a piece of it (every piece stores its fp32 partial in a
+//   fixed slot and bumps the tile's arrival counter; the piece that sees the
+//   final count adds all partials in cluster order -- a fixed order, so the
+//   result does not depend on timing -- and stores the tile), and that sum
+//   runs on the epilogue warps while the MMA warp already works on the whole
+//   tiles.  No CTA waits for another, so there is no co-residency
 //   requirement.  The counter goes back to zero after each tile, so the
 //   counter array stays zero between calls (after a timed-out wait, *err is
 //   set and the caller must clear the counters before the next call).
+// * Weights before the dependency wait: the weights do not depend on the
+//   previous kernel, so under programmatic dependent launch the producer
+//   fills the ring's weight halves before griddepcontrol.wait and only the
+//   token halves (the previous kernel's output) wait for it.
 // * Epilogue through shared memory: each thread owns one weight row (TMEM
 //   lane) and writes its bf16 values of 32 tokens into a [32][128] staging
 //   tile; one thread stores it with a TMA tensor store (clipped at the
@@ -90,14 +98,53 @@ struct Cfg {
 struct Seg {
   int tile, k0, k1;  // k-blocks [k0, k1) of tile `tile`
   bool whole;        // the segment covers the tile's whole K range
+  bool split;        // the tile is one of the split (stream-K) tiles
 };
 
-// The iteration range of cluster c: [c * I / G, (c + 1) * I / G).
-__device__ __forceinline__ int64_t range_start(int64_t c, const SkParams& g) { return c * g.iters / g.clusters; }
-// The cluster whose range holds iteration it (largest c with range_start(c) <= it).
-__device__ __forceinline__ int cluster_of(int64_t it, const SkParams& g) {
-  return static_cast<int>(((it + 1) * g.clusters + g.iters - 1) / g.iters - 1);
+// Split iterations: sk_iters = (U % G) * kb, cut over the first sk_clusters clusters;
+// split tile j is tile (U / G) * G + j.  Range of cluster c: [c * I / Gs, (c + 1) * I / Gs).
+__device__ __forceinline__ int64_t sk_start(int64_t c, const SkParams& g) {
+  return c >= g.sk_clusters ? g.sk_iters : c * g.sk_iters / g.sk_clusters;
 }
+// The cluster whose split range holds split iteration it.
+__device__ __forceinline__ int sk_cluster_of(int64_t it, const SkParams& g) {
+  return static_cast<int>(((it + 1) * g.sk_clusters + g.sk_iters - 1) / g.sk_iters - 1);
+}
+
+// The segments of one cluster, in order: its split piece(s), then its whole tiles.
+struct SegIter {
+  int64_t sk_it, sk_end;
+  int dp_next, dp_end, sk_base;
+  __device__ __forceinline__ SegIter(int c, const SkParams& g) {
+    sk_it = sk_start(c, g);
+    sk_end = sk_start(c + 1, g);
+    dp_next = c * g.q;
+    dp_end = dp_next + g.q;
+    sk_base = g.q * g.clusters;
+  }
+  __device__ __forceinline__ bool next(Seg& s, const SkParams& g) {
+    if (sk_it < sk_end) {
+      const int j = static_cast<int>(sk_it / g.kb);
+      const int64_t t0 = static_cast<int64_t>(j) * g.kb;
+      s.tile = sk_base + j;
+      s.k0 = static_cast<int>(sk_it - t0);
+      s.k1 = static_cast<int>((sk_end - t0) < g.kb ? (sk_end - t0) : g.kb);
+      s.whole = s.k0 == 0 && s.k1 == g.kb;
+      s.split = true;
+      sk_it = t0 + s.k1;
+      return true;
+    }
+    if (dp_next < dp_end) {
+      s.tile = dp_next++;
+      s.k0 = 0;
+      s.k1 = g.kb;
+      s.whole = true;
+      s.split = false;
+      return true;
+    }
+    return false;
+  }
+};
 
 template <int NS, int NSUB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
@@ -144,47 +191,69 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   cluster_sync();  // the peer's barriers are initialised before any remote arrive / complete_tx
   fence_after();
   shk::pdl_trigger();
-  shk::pdl_wait();  // the previous kernel's outputs (our inputs) are complete from here on
+  // griddepcontrol.wait: the producer waits after issuing its first weight loads (below); every
+  // other role waits here (the epilogue writes y and the split partials, which the previous kernel
+  // may still read).
+  if (warp != 0) shk::pdl_wait();
   const uint32_t tmem_base = *tmem_slot;
   const int cid = blockIdx.x >> 1;
-  const int64_t it_begin = range_start(cid, g), it_end = range_start(cid + 1, g);
   const uint32_t peer_abort = map_to_rank(const_cast<int*>(abort_flag), rank ^ 1);
   auto raise = [&](int code) {
     if (g.err) atomicCAS(g.err, 0, code);
     *abort_flag = 1;
     st_cluster_u32(peer_abort, 1);
   };
-  // Segments of this cluster's range, in order.
-  auto next_seg = [&](int64_t& it, Seg& s) -> bool {
-    if (it >= it_end) return false;
-    s.tile = static_cast<int>(it / g.kb);
-    const int64_t t0 = static_cast<int64_t>(s.tile) * g.kb;
-    s.k0 = static_cast<int>(it - t0);
-    s.k1 = static_cast<int>((it_end - t0) < g.kb ? (it_end - t0) : g.kb);
-    s.whole = s.k0 == 0 && s.k1 == g.kb;
-    it = t0 + s.k1;
-    return true;
-  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int64_t it = it_begin;
+      // Row coordinates of a tile's weight half-tile and token sub-tiles.
+      auto w_row = [&](int tile) {
+        const int y = (tile / g.tiles_x) * (2 * ROWS) + static_cast<int>(rank) * ROWS;
+        return y < g.rows_w ? y : 0;  // wholly outside: load valid rows whose results are never stored
+      };
+      auto x_row = [&](int tile, int u) {
+        const int y = (tile % g.tiles_x) * C::NT + u * NS + static_cast<int>(rank) * (NS / 2);
+        return y < g.rows_x ? y : 0;
+      };
+      // 1. Before the dependency wait: the weight halves of the first STAGES k-blocks.
+      int pre_tile[C::STAGES], pre_kb[C::STAGES];
+      int npre = 0;
+      {
+        SegIter itp(cid, g);
+        Seg s;
+        while (npre < C::STAGES && itp.next(s, g))
+          for (int kb = s.k0; kb < s.k1 && npre < C::STAGES; ++kb) {
+            pre_tile[npre] = s.tile;
+            pre_kb[npre] = kb;
+            if (leader) mbar_expect_tx(&full[npre], 2 * C::STAGE_BYTES);
+            tma_load_2d_pair(smem + npre * C::STAGE_BYTES, &tmW, kb * BK, w_row(s.tile),
+                             map_to_rank(&full[npre], 0));
+            ++npre;
+          }
+      }
+      shk::pdl_wait();  // the tokens are the previous kernel's output
+      for (int i = 0; i < npre; ++i) {
+        const uint32_t bar = map_to_rank(&full[i], 0);
+#pragma unroll
+        for (int u = 0; u < NSUB; ++u)
+          tma_load_2d_pair(smem + i * C::STAGE_BYTES + C::A_BYTES + u * C::B_SUB_BYTES, &tmX, pre_kb[i] * BK,
+                           x_row(pre_tile[i], u), bar);
+      }
+      // 2. The rest of the k-blocks, each into the next free stage.
+      int stage = npre % C::STAGES;
+      uint32_t phase = npre == C::STAGES ? 1u : 0u;
+      int done = 0;
+      SegIter it(cid, g);
       Seg s;
       bool stop = false;
-      while (!stop && next_seg(it, s)) {
-        const int tw = s.tile / g.tiles_x, tx = s.tile % g.tiles_x;
-        int w_y = tw * (2 * ROWS) + static_cast<int>(rank) * ROWS;
-        if (w_y >= g.rows_w) w_y = 0;  // wholly outside: load valid rows whose results are never stored
+      while (!stop && it.next(s, g)) {
+        const int w_y = w_row(s.tile);
         int x_y[NSUB];
 #pragma unroll
-        for (int u = 0; u < NSUB; ++u) {
-          x_y[u] = tx * C::NT + u * NS + static_cast<int>(rank) * (NS / 2);
-          if (x_y[u] >= g.rows_x) x_y[u] = 0;
-        }
+        for (int u = 0; u < NSUB; ++u) x_y[u] = x_row(s.tile, u);
         for (int kb = s.k0; kb < s.k1; ++kb) {
+          if (done++ < npre) continue;  // issued above
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             raise(1);
             stop = true;
@@ -203,6 +272,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           }
         }
       }
+    } else {
+      shk::pdl_wait();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader only)
@@ -212,9 +283,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      int64_t it = it_begin;
+      SegIter it(cid, g);
       Seg s;
-      while (next_seg(it, s)) {
+      while (it.next(s, g)) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
           raise(2);
           break;
@@ -264,13 +335,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const bool elected = et == 0;
     __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::STG_OFF);
     const int64_t slot_elems = static_cast<int64_t>(C::NT) * ROWS;
-    const int first_tile = static_cast<int>(it_begin / g.kb);
+    const int first_split = static_cast<int>(sk_start(cid, g) / g.kb);  // this cluster's first split tile j
     int acc = 0;
     uint32_t acc_phase = 0;
     int chunk = 0;  // staging tiles used so far (alternating buffers)
-    int64_t it = it_begin;
+    SegIter it(cid, g);
     Seg s;
-    while (next_seg(it, s)) {
+    while (it.next(s, g)) {
       const int tw = s.tile / g.tiles_x, tx = s.tile % g.tiles_x;
       const int y_w = tw * (2 * ROWS) + static_cast<int>(rank) * ROWS;  // output column of row 0
       const int y_x0 = tx * C::NT;                                        // output row of token 0
@@ -288,7 +359,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       if (!s.whole) {
         // Partial tile: park this piece's fp32 sums in the cluster's slot, then
         // count it.  Slot = (cluster, rank, first tile of the range ? 0 : 1).
-        float* mine = g.ws + ((static_cast<int64_t>(cid) * 2 + rank) * 2 + (s.tile == first_tile ? 0 : 1)) * slot_elems;
+        const int j = s.tile - g.q * g.clusters;  // split tile index
+        float* mine = g.ws + ((static_cast<int64_t>(cid) * 2 + rank) * 2 + (j == first_split ? 0 : 1)) * slot_elems;
 #pragma unroll 1
         for (int c = 0; c < C::NT; c += 16) {
           float v[16];
@@ -302,9 +374,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         if (lane == 0) mbar_arrive_cluster(map_to_rank(&tempty[acc], 0));  // TMEM is free again
         __threadfence();
         named_barrier(1, EPI_THREADS);
+        const int c_first = sk_cluster_of(static_cast<int64_t>(j) * g.kb, g);
         if (elected) {
-          const int c_first = cluster_of(static_cast<int64_t>(s.tile) * g.kb, g);
-          const int c_last = cluster_of(static_cast<int64_t>(s.tile + 1) * g.kb - 1, g);
+          const int c_last = sk_cluster_of(static_cast<int64_t>(j + 1) * g.kb - 1, g);
           int* cnt = g.cnt + s.tile * 2 + rank;
           const int old = atomicAdd(cnt, 1);
           const bool last = old == c_last - c_first;
@@ -320,11 +392,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         store = nparts > 0;
         if (store) {
           __threadfence();  // acquire side of the counter: the other pieces' partials are visible
-          const int c_first = cluster_of(static_cast<int64_t>(s.tile) * g.kb, g);
-          for (int j = 0; j < nparts; ++j) {
-            const int cj = c_first + j;
-            const int fj = static_cast<int>(range_start(cj, g) / g.kb);
-            parts[j] = g.ws + ((static_cast<int64_t>(cj) * 2 + rank) * 2 + (s.tile == fj ? 0 : 1)) * slot_elems;
+          for (int pj = 0; pj < nparts; ++pj) {
+            const int cj = c_first + pj;
+            const int fj = static_cast<int>(sk_start(cj, g) / g.kb);
+            parts[pj] = g.ws + ((static_cast<int64_t>(cj) * 2 + rank) * 2 + (j == fj ? 0 : 1)) * slot_elems;
           }
         }
       }
@@ -342,11 +413,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
               __syncwarp();
               tmem_ld16(tacc + ((c + h) / NS) * C::SUB_COLS + ((c + h) % NS), v);
             } else {
+              // Sum in cluster order; two pieces' loads in flight at a time.
 #pragma unroll
               for (int i = 0; i < 16; ++i) v[i] = 0.f;
-              for (int j = 0; j < nparts; ++j) {
+              int pj = 0;
+              for (; pj + 1 < nparts; pj += 2) {
+                float a[16], b[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] += __ldcg(parts[j] + static_cast<int64_t>(c + h + i) * ROWS + row);
+                for (int i = 0; i < 16; ++i) {
+                  a[i] = __ldcg(parts[pj] + static_cast<int64_t>(c + h + i) * ROWS + row);
+                  b[i] = __ldcg(parts[pj + 1] + static_cast<int64_t>(c + h + i) * ROWS + row);
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = (v[i] + a[i]) + b[i];
+              }
+              if (pj < nparts) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] += __ldcg(parts[pj] + static_cast<int64_t>(c + h + i) * ROWS + row);
               }
             }
 #pragma unroll
@@ -511,12 +594,18 @@ extern "C" int sh_gemm_bf16_sk(const void* W, int rows_w, int64_t ldw, const voi
   g.tiles_w = (rows_w + 2 * ROWS - 1) / (2 * ROWS);
   g.tiles_x = (rows_x + nt - 1) / nt;
   g.kb = K / BK;
-  g.iters = static_cast<int64_t>(g.tiles_w) * g.tiles_x * g.kb;
-  // Every range is at least ceil(kb / 15) iterations long, so a tile of kb
+  const int tiles = g.tiles_w * g.tiles_x;
+  g.clusters = clusters;
+  g.q = tiles / g.clusters;
+  g.sk_iters = static_cast<int64_t>(tiles % g.clusters) * g.kb;
+  // Every split range is at least ceil(kb / 15) iterations long, so a split tile of kb
   // iterations meets at most 16 ranges (the fix-up adds at most 16 partials).
   const int64_t min_range = (g.kb + kMaxParts - 2) / (kMaxParts - 1);
-  const int64_t gmax = g.iters / min_range;
-  g.clusters = static_cast<int>(clusters < gmax ? clusters : gmax);
+  int64_t gs = g.sk_iters / min_range;
+  if (gs > g.clusters) gs = g.clusters;
+  if (gs < 1) gs = 1;
+  g.sk_clusters = static_cast<int>(gs);
+  if (g.q == 0) g.clusters = g.sk_clusters;  // fewer tiles than clusters: only the split pieces, no idle pairs
   g.ws = ws;
   g.cnt = cnt;
   g.err = err;

@@ -38,8 +38,10 @@ struct SkParams {
   int rows_w, rows_x;
   int tiles_w, tiles_x;  // 256-row weight tiles x NT-token tiles; tile = tw * tiles_x + tx
   int kb;                // 64-wide k-blocks per tile
-  int64_t iters;         // tiles * kb: the stream-K iteration space
-  int clusters;          // CTA pairs; pair c runs iterations [c*iters/clusters, (c+1)*iters/clusters)
+  int clusters;          // CTA pairs launched
+  int q;                 // whole tiles per cluster: cluster c owns tiles [c*q, c*q + q)
+  int64_t sk_iters;      // k-blocks of the split tiles (tiles % clusters of them, after the whole ones)
+  int sk_clusters;       // clusters sharing the split k-blocks evenly (their pieces run first)
   float* ws;             // fp32 partial slots [clusters][2 ranks][2][NT][128]
   int* cnt;              // [tiles][2] arrival counters, zero between calls
   int* err;
@@ -52,8 +54,8 @@ extern "C" {
 // W [rows_w, K] (row stride ldw), X [rows_x, K], y [rows_x, ldy] bf16; K % 64 == 0,
 // 16-byte aligned bases and row strides.  One tile = 256 weight rows x
 // ns*nsub tokens ((ns, nsub) in {(64,1), (128,1), (192,1), (256,1), (192,2), (256,2)}).
-// `clusters` CTA pairs share the iteration space evenly (clamped so that a
-// tile is split into at most 16 pieces).  ws: >= the floats reported by
+// `clusters` CTA pairs each own tiles / clusters whole tiles and share the
+// k-blocks of the remaining tiles (a split tile has at most 16 pieces).  ws: >= the floats reported by
 // sh_gemm_sk_shape; cnt: >= 2 * tiles ints, zero before the first call (the
 // kernel leaves them zero).  One call at a time per (ws, cnt) pair.
 int sh_gemm_bf16_sk(const void* W, int rows_w, int64_t ldw, const void* X, int rows_x, int64_t ldx, int K, void* Y,

@@ -71,8 +71,10 @@ __device__ __forceinline__ bool mbar_try_sleep(uint64_t* b, uint32_t par, uint32
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t par, volatile int* abort_flag) {
   if (mbar_try(b, par)) return true;
   const uint64_t t0 = now_ns();
-  while (true) {
-    if (mbar_try_sleep(b, par, 10000)) return true;
+  while (true) {  // poll without a suspend hint (a suspended warp can wake up late); checks every 64 polls
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try(b, par)) return true;
     if (*abort_flag) return false;
     if (now_ns() - t0 > kTimeoutNs) return false;
   }

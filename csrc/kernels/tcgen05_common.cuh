@@ -51,12 +51,16 @@ __device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity, u
   return ok != 0;
 }
 // Bounded wait: false on timeout or when another role already aborted.  The
-// loop sleeps in try_wait (10 us hint) between the abort / timer checks.
+// loop polls with try_wait (no suspend hint: a suspended thread can wake up
+// late, and these waits sit on the MMA pipeline's critical path) and checks
+// the abort flag and the timer every 64 polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = now_ns();
   while (true) {
-    if (mbar_try_sleep(bar, parity, 10000)) return true;
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try(bar, parity)) return true;
     if (*abort_flag) return false;
     if (now_ns() - t0 > kTimeoutNs) return false;
   }

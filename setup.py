@@ -62,7 +62,23 @@ def cuda_ext():
     )
 
 
+def use_system_compiler():
+    """Compile with the system GCC when the environment points CC/CXX at a wrapper toolchain.
+
+    The /opt/gcc wrapper of this image (a relocated copy of GCC 13 with its own
+    assembler) produces objects in which a C++ exception carrying a formatted
+    message (TORCH_CHECK(cond, "...", value)) crashes during unwinding; the
+    system GCC 13 (/usr/bin) does not.  Set SH_KEEP_CXX=1 to keep CC/CXX.
+    """
+    if os.environ.get("SH_KEEP_CXX") == "1":
+        return
+    for var, path in (("CC", "/usr/bin/gcc"), ("CXX", "/usr/bin/g++")):
+        if os.path.exists(path) and os.environ.get(var, "").startswith("/opt/gcc"):
+            os.environ[var] = path
+
+
 def main():
+    use_system_compiler()
     exts = [native_ext()]
     cmdclass = {}
     if os.environ.get("SKIP_CUDA", "0") != "1":

@@ -67,6 +67,21 @@ def _worker(rank, world, port, q):
             dist.all_gather(gathered, x)
             same = all(torch.equal(gathered[0], t) for t in gathered)
             results[f"{i}:{mode}:{T}"] = (err_x, err_r, same)
+        # Fused vocab-parallel argmax: each rank holds a V/world slice; the kernel's global ids must equal
+        # the first-occurrence argmax of the full (all-gathered) logits, ties across ranks included.
+        V = 16032 * world
+        for i, T in enumerate((1, 64, 384, 7, 384)):
+            g = torch.Generator(device="cuda").manual_seed(500 + i)
+            full_logits = torch.randn(T, V, device="cuda", generator=g).to(torch.bfloat16)
+            full_logits[0, 5] = 40.0
+            full_logits[0, V - 3] = 40.0  # tie between the first and the last rank's slices
+            lo = rank * (V // world)
+            local = full_logits[:, lo:lo + V // world].contiguous()
+            got = comm.argmax(local, lo)
+            want = full_logits.float().argmax(1)
+            torch.cuda.synchronize()
+            comm.check()
+            results[f"argmax{i}:{T}"] = (0.0 if torch.equal(got, want) else 1.0, 0.0, True)
         q.put((rank, results))
     finally:
         torch.cuda.synchronize()

@@ -159,6 +159,7 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="time every kernel configuration per shape")
     ap.add_argument("--once", action="store_true",
                     help="no timing: two eager launches of ours then cuBLAS per shape (for ncu captures)")
+    ap.add_argument("--lib-only", action="store_true", help="with --once: launch only cuBLAS (profiling the library)")
     ap.add_argument("--config", default="", help="force kind,swap,bn,splits,clusters (e.g. sk,1,192,2,74 or pair,0,256,1,0)")
     ap.add_argument("--w4a4", action="store_true", help="with --nvfp4 --once: launch the W4A4 kernel")
     ap.add_argument("--nvfp4", action="store_true",
@@ -188,7 +189,8 @@ def main():
         if a.once:
             for _ in range(2):
                 flush.zero_()
-                ours()
+                if not a.lib_only:
+                    ours()
                 flush.zero_()
                 torch.matmul(x, w.t(), out=y)
             torch.cuda.synchronize()

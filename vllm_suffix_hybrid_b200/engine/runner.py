@@ -24,6 +24,7 @@ bucket point at the reserved scratch block 0.
 from __future__ import annotations
 
 import math
+import os
 from typing import Dict, List, Optional
 
 import numpy as np
@@ -34,6 +35,15 @@ from ..models.common import AttnMeta
 from .kv_cache import blocks_for
 
 BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+
+
+def _max_rows(rows: int) -> int:
+    """Query rows per attention tile the kernel is specialised for (it picks its in-CTA key split from this).
+    Batch-invariant mode always reports a full tile, so the key split -- which changes the softmax merge
+    order -- does not depend on the verify width."""
+    if os.environ.get("SH_BATCH_INVARIANT", "0") == "1":
+        return 64
+    return min(64, rows)
 
 
 def bucket_for(n: int, max_batch: int) -> int:
@@ -203,7 +213,7 @@ class Runner:
         nsplit = ops.attention_splits(tr.numel(), kvh, self.max_blocks)
         return AttnMeta(positions=pos.reshape(-1), slot_mapping=self._slots(bt, pos).reshape(-1), block_tables=bt,
                         seq_lens=seq_lens, q_start=qs, tile_req=tr, tile_row0=t0, num_tokens=nb * qlen,
-                        nsplit=nsplit, max_rows=min(64, qlen * self.group))
+                        nsplit=nsplit, max_rows=_max_rows(qlen * self.group))
 
     def _draft_steps(self, d1: torch.Tensor, f1: torch.Tensor, lnew: torch.Tensor, bt: torch.Tensor, nb: int):
         """Draft tokens 2..k at positions lnew + s - 2 (s = 2..k)."""
@@ -345,7 +355,7 @@ class Runner:
                         tile_req=torch.tensor(tr, dtype=torch.int32, device=dev),
                         tile_row0=torch.tensor(t0, dtype=torch.int32, device=dev), num_tokens=int(sum(lens)),
                         nsplit=ops.attention_splits(len(tr), self.model.kv_heads_local, mb),
-                        max_rows=min(64, max(lens) * self.group))
+                        max_rows=_max_rows(max(lens) * self.group))
         slot_t = torch.tensor(state_slots if state_slots is not None else [0] * n, dtype=torch.long, device=dev)
         meta.state_slots, meta.pending, meta.window = slot_t, self.pending, 0
         hid, pre = self.model.forward(ids, meta, self.caches)

@@ -26,12 +26,13 @@ across runs and across processes of a multi-GPU job).  Calls during
 CUDA-graph capture never tune: they use the recorded choice or the
 heuristic.
 
-Batch-invariant mode (SH_BATCH_INVARIANT=1): the split-K factor -- the only
-tc/pair choice that changes a row's fp32 summation order -- becomes a
-function of (N, K) alone, so a token's output does not depend on how many
-other tokens share the call (a k+1-token verify window gives the same logits
-as plain decoding).  Stream-K pieces depend on the tile count, so sk is left
-out in that mode.
+Batch-invariant mode (SH_BATCH_INVARIANT=1): no autotuning; every call with
+M <= 256 runs the one-CTA swap-AB kernel with a 64-token N tile and every
+larger call the CTA-pair kernel, with the split-K factor a function of
+(N, K) alone, so a token's output does not depend on how many other tokens
+share the call (a k+1-token verify window gives the same logits as plain
+decoding).  Stream-K pieces depend on the tile count, so sk is not used in
+that mode.
 
 Split-K partials, stream-K partial slots and stream-K arrival counters live
 in per-device buffers that grow on demand and are reused by every call on
@@ -269,11 +270,16 @@ def plan(M: int, N: int, K: int, x2: Optional[torch.Tensor] = None, w: Optional[
     got = _CHOICE.get(key)
     if got is not None:
         return got
-    fixed = invariant_splits(N, K) if inv else None
+    if inv:
+        # One kernel family per M range and split-K from (N, K) alone: nothing about a row's
+        # arithmetic depends on how many rows share the call.
+        fixed = invariant_splits(N, K)
+        got = Cfg("tc", True, 64, fixed) if M <= 256 else Cfg("pair", False, 256, fixed)
+        _CHOICE[key] = got
+        return got
     if (x2 is None or os.environ.get("SH_GEMM_TUNE", "1") == "0" or torch.cuda.is_current_stream_capturing()):
-        h = heuristic(M, N, K)
-        return h if fixed is None else h._replace(splits=fixed)
-    got = _autotune(x2, w, y, fixed)
+        return heuristic(M, N, K)
+    got = _autotune(x2, w, y, None)
     _CHOICE[key] = got
     if not inv:
         _save()
