@@ -108,6 +108,9 @@ def main():
     ap.add_argument("--timed-from", type=int, default=-1,
                     help="generated tokens per request before the warm-up steps start (default: the timed window "
                          "is centred on the middle of the max-new-token generation, the mean context length)")
+    ap.add_argument("--adaptive-width", action="store_true",
+                    help="verify only as wide as the longest real draft (off for the headline: every step "
+                         "verifies k + 1 tokens per row)")
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="TP collectives: own NVLink kernels (fused) or the NCCL baseline")
@@ -167,7 +170,8 @@ def main():
         mcfg.layers = args.layers
     par = (ParallelConfig(ep=n, dp=n, comm=args.comm) if layout == "dp-ep" and n > 1
            else ParallelConfig(tp=n, comm=args.comm))
-    cfg = EngineConfig(model=mcfg, spec=SpecConfig(method=args.method, k=args.k, split=args.split),
+    cfg = EngineConfig(model=mcfg, spec=SpecConfig(method=args.method, k=args.k, split=args.split,
+                                                   adaptive_width=args.adaptive_width),
                        parallel=par,
                        cache=CacheConfig(max_model_len=args.prompt_len + args.max_new + 4 * args.k + 64),
                        max_num_seqs=local_batch, device="cuda", cuda_graphs=not args.no_graphs)
@@ -248,10 +252,12 @@ def main():
     t0 = time.perf_counter()
     dev_ms = 0.0
     h2d = d2h = 0
+    width_sum = 0
     for _ in range(args.steps):
         s = eng.step()
         assert s.kind == "decode", s
         dev_ms += eng.runner.last_device_ms
+        width_sum += eng.runner.last_width
         h2d += eng.runner.h2d_bytes
         d2h += eng.runner.d2h_bytes
     torch.cuda.synchronize()
@@ -299,6 +305,8 @@ def main():
                        "l2": "working set (weights + KV) >> 126 MB L2; no flush",
                        "layers": mcfg.layers, "weights": mcfg.weight_format, "kv_cache": mcfg.kv_format},
             "mean_accept_len": round(tokens / rows, 4),
+            "mean_verify_width": round(width_sum / args.steps, 3),
+            "adaptive_width": bool(args.adaptive_width),
             "timed_window": {"untimed_steps_before_warmup": advanced, "min_context_at_first_timed_step": ctx0},
             "proposer_us_per_step": round(prop_us, 2),
             "prefill_s": round(prefill_s, 2),

@@ -295,7 +295,8 @@ void silu_mul(torch::Tensor out, torch::Tensor x) {
 }
 
 void embedding(torch::Tensor out, torch::Tensor ids, torch::Tensor table) {
-  TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.scalar_type() == at::kLong, "embedding args");
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.scalar_type() == at::kLong && ids.is_contiguous(),
+              "embedding: contiguous int64 ids, table and out");
   const int64_t rows = ids.numel();
   if (rows == 0) return;
   const int hidden = table.size(1);

@@ -216,6 +216,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         const int y = (tile % g.tiles_x) * C::NT + u * NS + static_cast<int>(rank) * (NS / 2);
         return y < g.rows_x ? y : 0;
       };
+      const uint64_t pol_w = policy_evict_first();  // weights: read once
+      const uint64_t pol_x = policy_evict_last();   // tokens: read by every cluster
       // 1. Before the dependency wait: the weight halves of the first STAGES k-blocks.
       int pre_tile[C::STAGES], pre_kb[C::STAGES];
       int npre = 0;
@@ -227,8 +229,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
             pre_tile[npre] = s.tile;
             pre_kb[npre] = kb;
             if (leader) mbar_expect_tx(&full[npre], 2 * C::STAGE_BYTES);
-            tma_load_2d_pair(smem + npre * C::STAGE_BYTES, &tmW, kb * BK, w_row(s.tile),
-                             map_to_rank(&full[npre], 0));
+            tma_load_2d_pair_hint(smem + npre * C::STAGE_BYTES, &tmW, kb * BK, w_row(s.tile),
+                                  map_to_rank(&full[npre], 0), pol_w);
             ++npre;
           }
       }
@@ -237,8 +239,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         const uint32_t bar = map_to_rank(&full[i], 0);
 #pragma unroll
         for (int u = 0; u < NSUB; ++u)
-          tma_load_2d_pair(smem + i * C::STAGE_BYTES + C::A_BYTES + u * C::B_SUB_BYTES, &tmX, pre_kb[i] * BK,
-                           x_row(pre_tile[i], u), bar);
+          tma_load_2d_pair_hint(smem + i * C::STAGE_BYTES + C::A_BYTES + u * C::B_SUB_BYTES, &tmX, pre_kb[i] * BK,
+                                x_row(pre_tile[i], u), bar, pol_x);
       }
       // 2. The rest of the k-blocks, each into the next free stage.
       int stage = npre % C::STAGES;
@@ -262,10 +264,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           if (leader) mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
           uint8_t* sp = smem + stage * C::STAGE_BYTES;
           const uint32_t bar = map_to_rank(&full[stage], 0);
-          tma_load_2d_pair(sp, &tmW, kb * BK, w_y, bar);
+          tma_load_2d_pair_hint(sp, &tmW, kb * BK, w_y, bar, pol_w);
 #pragma unroll
           for (int u = 0; u < NSUB; ++u)
-            tma_load_2d_pair(sp + C::A_BYTES + u * C::B_SUB_BYTES, &tmX, kb * BK, x_y[u], bar);
+            tma_load_2d_pair_hint(sp + C::A_BYTES + u * C::B_SUB_BYTES, &tmX, kb * BK, x_y[u], bar, pol_x);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;

@@ -153,6 +153,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int64_t issued = 0;
       bool aborted = false;
+      const uint64_t pol_p = g.p_is_weight ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_q = g.p_is_weight ? policy_evict_last() : policy_evict_first();
       for (int w = blockIdx.x; w < total_work && !aborted; w += gridDim.x) {
         const Work wk = decode_work(w, g, BN);
         const int kb0 = wk.sp * g.kb_per_split;
@@ -166,8 +168,8 @@ __global__ void __launch_bounds__(192, 1)
           }
           mbar_expect_tx(&full[stage], S::STAGE_BYTES);
           uint8_t* sp = smem + stage * S::STAGE_BYTES;
-          tma_load_2d(sp, &tmP, kb * BK, wk.p_y, &full[stage]);
-          tma_load_2d(sp + S::P_BYTES, &tmQ, kb * BK, wk.q_y, &full[stage]);
+          tma_load_2d_hint(sp, &tmP, kb * BK, wk.p_y, &full[stage], pol_p);
+          tma_load_2d_hint(sp + S::P_BYTES, &tmQ, kb * BK, wk.q_y, &full[stage], pol_q);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -462,6 +464,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      const uint64_t pol_p = g.p_is_weight ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_q = g.p_is_weight ? policy_evict_last() : policy_evict_first();
       for (int w = cid; w < total_work; w += ncl) {
         const Work wk = decode_work(w, g, BN);
         int p_y = wk.tp * (2 * PAIR_ROWS) + static_cast<int>(rank) * PAIR_ROWS;
@@ -480,8 +484,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           if (leader) mbar_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
           uint8_t* sp = smem + stage * S::STAGE_BYTES;
           const uint32_t bar = map_to_rank(&full[stage], 0);
-          tma_load_2d_pair(sp, &tmP, kb * BK, p_y, bar);
-          tma_load_2d_pair(sp + S::A_BYTES, &tmQ, kb * BK, q_y, bar);
+          tma_load_2d_pair_hint(sp, &tmP, kb * BK, p_y, bar, pol_p);
+          tma_load_2d_pair_hint(sp + S::A_BYTES, &tmQ, kb * BK, q_y, bar, pol_q);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -865,6 +869,7 @@ extern "C" int sh_gemm_bf16_tcgen05(const void* P, int rows_p, int64_t ldp, cons
   g.ws = ws;
   g.err = err;
   g.p_fast = trans ? 0 : 1;  // consecutive work units share the weight tile
+  g.p_is_weight = trans ? 1 : 0;
   const int work = g.tiles_p * g.tiles_q * splits;
   const int grid = work < num_sms ? work : num_sms;
   const bool split = splits > 1;
@@ -912,6 +917,7 @@ extern "C" int sh_gemm_bf16_grouped(const void* P, int p_total_rows, int rows_p,
   g.ldo = static_cast<int>(ldo);
   g.err = err;
   g.p_fast = 1;
+  g.p_is_weight = 1;  // expert weights
   g.groups = groups;
   g.num_groups = num_groups;
   const int work = max_groups * g.tiles_p;
@@ -958,6 +964,7 @@ extern "C" int sh_gemm_bf16_pair(const void* P, int rows_p, int64_t ldp, const v
   g.ws = ws;
   g.err = err;
   g.p_fast = trans ? 0 : 1;
+  g.p_is_weight = trans ? 1 : 0;
   const int work = g.tiles_p * g.tiles_q * splits;
   const int clusters = pair_clusters(num_sms);
   const int grid = 2 * (work < clusters ? work : clusters);
@@ -1012,6 +1019,7 @@ extern "C" int sh_gemm_bf16_push(const void* P, int rows_p, int64_t ldp, const v
   g.ws = nullptr;
   g.err = err;
   g.p_fast = trans ? 0 : 1;
+  g.p_is_weight = trans ? 1 : 0;
   g.groups = nullptr;
   g.num_groups = nullptr;
   const int work = g.tiles_p * g.tiles_q;

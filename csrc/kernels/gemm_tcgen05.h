@@ -13,6 +13,7 @@ struct GemmParams {
   float* ws;
   int* err;
   int p_fast;
+  int p_is_weight;  // P holds the weights (read once: L2 evict-first), Q the activations (evict-last); else swapped
   // Grouped (MoE) mode when groups != nullptr: work unit = (group entry, P
   // tile).  Entry = {q_row0, q_rows, p_row_offset, unused}: the Q tile starts at
   // sorted row q_row0 and holds q_rows valid rows; P tiles start at row

@@ -183,7 +183,7 @@ class SpecConfig:
     min_len: int = 1  # SUFFIX_HYBRID_SUFFIX_MIN
     async_scheduling: bool = False  # SUFFIX_HYBRID_ASYNC: lag-1 host candidates, drafts resolved on the device
     async_hyb_min: int = 0  # SUFFIX_HYBRID_ASYNC_HYB_MIN (0 = k): real suffix drafts that replace native ones
-    # Verify only as wide as the longest real draft of the step (SUFFIX_HYBRID_ADAPTIVE_WIDTH=0: always k + 1).
+    # Verify only as wide as the longest real draft of the step (SUFFIX_HYBRID_ADAPTIVE_WIDTH=0 / 1 overrides).
     adaptive_width: bool = True
 
 
@@ -230,8 +230,8 @@ def apply_env(cfg: EngineConfig) -> EngineConfig:
         cfg.spec.method = "suffix"
     if _env("UNIFORM_K") is not None:
         cfg.spec.uniform_k = _env("UNIFORM_K") == "1"
-    if _env("ADAPTIVE_WIDTH") == "0":
-        cfg.spec.adaptive_width = False
+    if _env("ADAPTIVE_WIDTH") in ("0", "1"):
+        cfg.spec.adaptive_width = _env("ADAPTIVE_WIDTH") == "1"
     if _env("EWMA_WIDTH") == "1":
         cfg.spec.width_gate = True
     v = _env("SUFFIX_MIN")

@@ -234,7 +234,9 @@ class Runner:
         pos = L[:, None] + self.ar_w[None, :W]
         meta = self._meta(nb, W, pos, bt, L + W)
         meta.state_slots, meta.pending, meta.window = self.slots[:nb], self.pending, W
-        hid, pre = self.model.forward(win.reshape(-1), meta, self.caches)
+        # win is a column slice of the static [B, k + 1] buffer: copy it into one contiguous id vector
+        # (for W = 1 a reshape would return a strided view, which the embedding kernel must not get).
+        hid, pre = self.model.forward(win.contiguous().view(-1), meta, self.caches)
         target = self.target[:nb, :W]
         target.copy_(self.model.greedy(hid).view(nb, W))
         lnew = self.seq_new[:nb]

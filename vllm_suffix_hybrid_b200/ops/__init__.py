@@ -185,7 +185,7 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None =
         return r
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
-    native().embedding(out, ids.reshape(-1), table)
+    native().embedding(out, ids.reshape(-1).contiguous(), table)
     return out
 
 
