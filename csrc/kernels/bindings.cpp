@@ -118,7 +118,8 @@ int64_t get_wait_ns() { return static_cast<int64_t>(g_wait_ns); }
 // y[M, N] = x[M, K] @ w[N, K]^T via the stream-K CTA-pair kernel (weights on
 // the MMA M side, ns*nsub tokens per tile).  ws / cnt: see sh_gemm_bf16_sk.
 void gemm_bf16_sk(torch::Tensor y, torch::Tensor x, torch::Tensor w, int64_t ns, int64_t nsub, int64_t clusters,
-                  torch::Tensor ws, torch::Tensor cnt, c10::optional<torch::Tensor> err) {
+                  torch::Tensor ws, torch::Tensor cnt, c10::optional<torch::Tensor> err,
+                  c10::optional<torch::Tensor> stamps) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && y.is_cuda() && ws.is_cuda() && cnt.is_cuda(), "gemm_bf16_sk: CUDA tensors");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
               "gemm_bf16_sk: bf16 tensors");
@@ -133,10 +134,16 @@ void gemm_bf16_sk(torch::Tensor y, torch::Tensor x, torch::Tensor w, int64_t ns,
   TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= need, "gemm_bf16_sk: workspace too small");
   TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.numel() >= 2 * tiles, "gemm_bf16_sk: counter array too small");
   int* errp = err.has_value() ? err->data_ptr<int>() : nullptr;
+  unsigned long long* st = nullptr;
+  if (stamps.has_value()) {
+    TORCH_CHECK(stamps->scalar_type() == at::kLong && stamps->is_cuda() && stamps->numel() >= 2 * clusters * 64,
+                "gemm_bf16_sk: stamps int64 [2 * clusters, 64]");
+    st = reinterpret_cast<unsigned long long*>(stamps->data_ptr<int64_t>());
+  }
   const int r = sh_gemm_bf16_sk(w.data_ptr(), static_cast<int>(N), w.stride(0), x.data_ptr(), static_cast<int>(M),
                                 x.stride(0), static_cast<int>(K), y.data_ptr(), y.stride(0), static_cast<int>(ns),
                                 static_cast<int>(nsub), static_cast<int>(clusters), ws.data_ptr<float>(),
-                                cnt.data_ptr<int>(), errp, at::cuda::getCurrentCUDAStream());
+                                cnt.data_ptr<int>(), errp, st, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_gemm_bf16_sk failed with code ", r);
 }
 
@@ -979,7 +986,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_quant", &nvfp4_quant);
   m.def("gemm_bf16_sk", &gemm_bf16_sk, "stream-K tcgen05 CTA-pair linear", py::arg("y"), py::arg("x"), py::arg("w"),
         py::arg("ns"), py::arg("nsub"), py::arg("clusters"), py::arg("ws"), py::arg("cnt"),
-        py::arg("err") = py::none());
+        py::arg("err") = py::none(), py::arg("stamps") = py::none());
   m.def("gemm_sk_max_clusters", &gemm_sk_max_clusters, "co-resident CTA pairs of the stream-K kernel",
         py::arg("ns"), py::arg("nsub"));
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM", py::arg("y"), py::arg("x"), py::arg("w"), py::arg("swap"),

@@ -30,10 +30,13 @@
 //   fills the ring's weight halves before griddepcontrol.wait and only the
 //   token halves (the previous kernel's output) wait for it.
 // * Epilogue through shared memory: each thread owns one weight row (TMEM
-//   lane) and writes its bf16 values of 32 tokens into a [32][128] staging
-//   tile; one thread stores it with a TMA tensor store (clipped at the
-//   tensor's bounds), so the output leaves the SM as 256-byte row segments.
-//   Two staging tiles alternate.
+//   lane), reads 32 token columns per tcgen05.ld and writes their bf16 values
+//   into a [32][128] staging tile; one thread stores it with a TMA tensor
+//   store (clipped at the tensor's bounds), so the output leaves the SM as
+//   256-byte row segments.  Three staging tiles rotate, and the next chunk's
+//   TMEM read is in flight while the current chunk is staged.  Split-tile partials
+//   are stored as float4 ([token / 4][row][4]), so every partial store and
+//   fix-up load moves 512 contiguous bytes per warp instruction.
 //
 // Roles (192 threads per CTA): warp 0 = TMA producer (both CTAs; both CTAs'
 // bytes counted on the leader's full barrier; no multicast), warp 1 = TMEM
@@ -63,7 +66,8 @@ using namespace shk::tc;
 
 constexpr int BK = 64;        // k-block (one 128-byte swizzle row of bf16)
 constexpr int ROWS = 128;     // weight rows per CTA (MMA M = 256 per pair)
-constexpr int STG_T = 32;     // tokens per staging tile
+constexpr int kMaxPiecesPerTile = 3;  // split pieces per split tile (the fix-up reads them all)
+constexpr int STG_T = 32;              // tokens per staging tile of the TMA-store epilogue
 constexpr int EPI_THREADS = 128;
 constexpr int kMaxParts = 16;  // partials a fix-up may add
 
@@ -84,16 +88,60 @@ struct Cfg {
   static constexpr int B_SUB_BYTES = (NS / 2) * BK * 2;   // this CTA's half of one MMA's token rows
   static constexpr int STAGE_BYTES = A_BYTES + NSUB * B_SUB_BYTES;
   static constexpr int STG_BYTES = STG_T * ROWS * 2;      // one [32][128] bf16 staging tile
+  static constexpr int NSTG = 3;                          // staging tiles in flight
   static constexpr int RING = 200 * 1024;
   static constexpr int STAGES = (RING / STAGE_BYTES) > 10 ? 10 : (RING / STAGE_BYTES);
   static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-  static constexpr int BAR_OFF = STG_OFF + 2 * STG_BYTES;
+  static constexpr int BAR_OFF = STG_OFF + NSTG * STG_BYTES;
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 2 * NACC + 1) * 8 + 16 + 1024;
   static_assert(NS % 32 == 0 && NS >= 64 && NS <= 256, "MMA N per instruction");
   static_assert(B_SUB_BYTES % 1024 == 0, "token half-tiles keep the 1024-byte swizzle alignment");
   static_assert(TCOLS <= 512, "TMEM columns");
   static_assert(TOTAL <= 227 * 1024, "shared memory budget");
 };
+
+// Phase stamps (SkParams::stamps, [grid][64] u64 ns), for profiling the pipeline without a profiler:
+//   [0] CTA start  [1] producer: first weight loads issued  [2] producer: dependency wait passed
+//   [3] producer: ns waiting for free stages  [4] MMA: ns waiting for loaded stages
+//   [5] MMA: ns waiting for a free accumulator  [6] epilogue: CTA end
+//   [8 + 4i .. 11 + 4i] segment i < 8: MMA start, MMA issue end, epilogue saw the accumulator, TMEM freed
+constexpr int kStampSlots = 64;
+__device__ __forceinline__ void stamp(const SkParams& g, int slot, unsigned long long v) {
+  if (g.stamps) g.stamps[blockIdx.x * kStampSlots + slot] = v;
+}
+
+// 32 consecutive TMEM columns of this thread's lane, without waiting: the
+// registers are valid after the next tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.wait::ld that also names the 32 registers of an outstanding load as its operands, so the
+// compiler cannot move their uses above the wait.
+__device__ __forceinline__ void tmem_wait_ld32(float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+// 32 consecutive TMEM columns of this thread's lane (one tcgen05.ld, one wait).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  tmem_ld32_nowait(taddr, v);
+  tmem_wait_ld32(v);
+}
 
 struct Seg {
   int tile, k0, k1;  // k-blocks [k0, k1) of tile `tile`
@@ -194,6 +242,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   // griddepcontrol.wait: the producer waits after issuing its first weight loads (below); every
   // other role waits here (the epilogue writes y and the split partials, which the previous kernel
   // may still read).
+  if (g.stamps && threadIdx.x == 0) stamp(g, 0, now_ns());
   if (warp != 0) shk::pdl_wait();
   const uint32_t tmem_base = *tmem_slot;
   const int cid = blockIdx.x >> 1;
@@ -216,7 +265,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         const int y = (tile % g.tiles_x) * C::NT + u * NS + static_cast<int>(rank) * (NS / 2);
         return y < g.rows_x ? y : 0;
       };
-      const uint64_t pol_w = policy_evict_first();  // weights: read once
+      // Weights read by one tile only are evict-first; with several token tiles the next tile of the
+      // same cluster reads the same weight rows again, so they stay (evict-last, like the tokens).
+      const uint64_t pol_w = g.tiles_x == 1 ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_x = policy_evict_last();   // tokens: read by every cluster
       // 1. Before the dependency wait: the weight halves of the first STAGES k-blocks.
       int pre_tile[C::STAGES], pre_kb[C::STAGES];
@@ -234,7 +285,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
             ++npre;
           }
       }
+      if (g.stamps) stamp(g, 1, now_ns());
       shk::pdl_wait();  // the tokens are the previous kernel's output
+      if (g.stamps) stamp(g, 2, now_ns());
       for (int i = 0; i < npre; ++i) {
         const uint32_t bar = map_to_rank(&full[i], 0);
 #pragma unroll
@@ -246,6 +299,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       int stage = npre % C::STAGES;
       uint32_t phase = npre == C::STAGES ? 1u : 0u;
       int done = 0;
+      unsigned long long wait_empty_ns = 0;
       SegIter it(cid, g);
       Seg s;
       bool stop = false;
@@ -256,11 +310,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         for (int u = 0; u < NSUB; ++u) x_y[u] = x_row(s.tile, u);
         for (int kb = s.k0; kb < s.k1; ++kb) {
           if (done++ < npre) continue;  // issued above
+          const uint64_t tw0 = g.stamps ? now_ns() : 0;
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             raise(1);
             stop = true;
             break;
           }
+          if (g.stamps) wait_empty_ns += now_ns() - tw0;
           if (leader) mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
           uint8_t* sp = smem + stage * C::STAGE_BYTES;
           const uint32_t bar = map_to_rank(&full[stage], 0);
@@ -274,6 +330,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           }
         }
       }
+      if (g.stamps) stamp(g, 3, wait_empty_ns);
     } else {
       shk::pdl_wait();
     }
@@ -287,19 +344,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       uint32_t acc_phase = 0;
       SegIter it(cid, g);
       Seg s;
+      int seg = 0;
+      unsigned long long wait_full_ns = 0, wait_acc_ns = 0;
       while (it.next(s, g)) {
+        const uint64_t ta = g.stamps ? now_ns() : 0;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
           raise(2);
           break;
+        }
+        if (g.stamps) {
+          const uint64_t t = now_ns();
+          wait_acc_ns += t - ta;
+          if (seg < 8) stamp(g, 8 + 4 * seg, t);
         }
         fence_after();
         const uint32_t tmem_d = tmem_base + acc * C::ACC_COLS;
         bool ok = true;
         for (int kb = s.k0; kb < s.k1; ++kb) {
+          const uint64_t tf = g.stamps ? now_ns() : 0;
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
             break;
           }
+          if (g.stamps) wait_full_ns += now_ns() - tf;
           fence_after();
           const uint32_t sa = smem_addr(smem + stage * C::STAGE_BYTES);
 #pragma unroll
@@ -323,10 +390,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           break;
         }
         mma_commit_pair_both(&tfull[acc]);
+        if (g.stamps && seg < 8) stamp(g, 9 + 4 * seg, now_ns());
+        ++seg;
         if (++acc == C::NACC) {
           acc = 0;
           acc_phase ^= 1;
         }
+      }
+      if (g.stamps) {
+        stamp(g, 4, wait_full_ns);
+        stamp(g, 5, wait_acc_ns);
       }
     }
   } else {
@@ -335,17 +408,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const int row = quad * 32 + lane;       // weight row within this CTA's 128
     const int et = threadIdx.x - 64;        // 0..127 within the epilogue warps
     const bool elected = et == 0;
-    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::STG_OFF);
     const int64_t slot_elems = static_cast<int64_t>(C::NT) * ROWS;
     const int first_split = static_cast<int>(sk_start(cid, g) / g.kb);  // this cluster's first split tile j
+    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::STG_OFF);
+    int chunk = 0;  // staging tiles used so far (alternating buffers)
     int acc = 0;
     uint32_t acc_phase = 0;
-    int chunk = 0;  // staging tiles used so far (alternating buffers)
+    int eseg = 0;
     SegIter it(cid, g);
     Seg s;
+    // One 32-token chunk of this thread's weight row (v[32], fp32) -> bf16 staging tile -> TMA tensor store
+    // of [32 tokens][128 weights] (clipped at the tensor's bounds).  Two staging tiles alternate.
+    auto store_chunk = [&](const float* v, int y_w, int y_t) {
+      __nv_bfloat16* buf = stg + (chunk % C::NSTG) * (STG_T * ROWS);
+      // The store issued from this buffer NSTG chunks ago has read it (at most NSTG - 1 stores still reading).
+      if (elected && chunk >= C::NSTG) bulk_wait_read<C::NSTG - 1>();
+      named_barrier(1, EPI_THREADS);
+#pragma unroll
+      for (int i = 0; i < STG_T; ++i) buf[i * ROWS + row] = __float2bfloat16_rn(v[i]);
+      fence_proxy_async_smem();
+      named_barrier(1, EPI_THREADS);
+      if (elected) {
+        if (y_w < g.rows_w && y_t < g.rows_x) tma_store_2d(&tmY, buf, y_w, y_t);
+        bulk_commit();
+      }
+      ++chunk;
+    };
     while (it.next(s, g)) {
       const int tw = s.tile / g.tiles_x, tx = s.tile % g.tiles_x;
-      const int y_w = tw * (2 * ROWS) + static_cast<int>(rank) * ROWS;  // output column of row 0
+      const int y_w = tw * (2 * ROWS) + static_cast<int>(rank) * ROWS;  // output column of weight row 0
       const int y_x0 = tx * C::NT;                                        // output row of token 0
       // The epilogue warps leave together (they meet at named barriers below).
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag);
@@ -353,27 +444,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         if (elected) raise(4);
         break;
       }
+      if (g.stamps && elected && eseg < 8) stamp(g, 10 + 4 * eseg, now_ns());
       fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * C::ACC_COLS;
-      bool store = true;
-      const float* parts[kMaxParts];
-      int nparts = 0;
-      if (!s.whole) {
-        // Partial tile: park this piece's fp32 sums in the cluster's slot, then
-        // count it.  Slot = (cluster, rank, first tile of the range ? 0 : 1).
-        const int j = s.tile - g.q * g.clusters;  // split tile index
-        float* mine = g.ws + ((static_cast<int64_t>(cid) * 2 + rank) * 2 + (j == first_split ? 0 : 1)) * slot_elems;
+      if (s.whole) {
+        // TMEM reads one chunk ahead of the staging writes (two register sets, one wait per chunk);
+        // NT is a multiple of 64.
+        static_assert(C::NT % (2 * STG_T) == 0, "two chunks per step");
+        auto tcol = [&](int c) { return tacc + (c / NS) * C::SUB_COLS + (c % NS); };
+        float va[STG_T], vb[STG_T];
+        tmem_ld32(tcol(0), va);
 #pragma unroll 1
-        for (int c = 0; c < C::NT; c += 16) {
-          float v[16];
-          __syncwarp();
-          tmem_ld16(tacc + (c / NS) * C::SUB_COLS + (c % NS), v);
+        for (int c = 0; c < C::NT; c += 2 * STG_T) {
+          tmem_ld32_nowait(tcol(c + STG_T), vb);
+          store_chunk(va, y_w, y_x0 + c);
+          tmem_wait_ld32(vb);
+          if (c + 2 * STG_T < C::NT) tmem_ld32_nowait(tcol(c + 2 * STG_T), va);
+          store_chunk(vb, y_w, y_x0 + c + STG_T);
+          tmem_wait_ld32(va);
+        }
+      } else {
+        // Partial tile: park this piece's fp32 sums in the cluster's slot, then
+        // count it.  Slot = (cluster, rank, first split tile of the range ? 0 : 1).
+        const int j = s.tile - g.q * g.clusters;  // split tile index
+        float4* mine = reinterpret_cast<float4*>(
+            g.ws + ((static_cast<int64_t>(cid) * 2 + rank) * 2 + (j == first_split ? 0 : 1)) * slot_elems);
+#pragma unroll 1
+        for (int c = 0; c < C::NT; c += 32) {
+          float v[32];
+          tmem_ld32(tacc + (c / NS) * C::SUB_COLS + (c % NS), v);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) __stcg(mine + static_cast<int64_t>(c + i) * ROWS + row, v[i]);
+          for (int i4 = 0; i4 < 8; ++i4)
+            __stcg(mine + static_cast<int64_t>(c / 4 + i4) * ROWS + row,
+                   make_float4(v[4 * i4], v[4 * i4 + 1], v[4 * i4 + 2], v[4 * i4 + 3]));
         }
         fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(map_to_rank(&tempty[acc], 0));  // TMEM is free again
+        if (g.stamps && elected && eseg < 8) stamp(g, 11 + 4 * eseg, now_ns());
         __threadfence();
         named_barrier(1, EPI_THREADS);
         const int c_first = sk_cluster_of(static_cast<int64_t>(j) * g.kb, g);
@@ -386,77 +494,70 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           *bcast = last ? (c_last - c_first + 1) : 0;
         }
         named_barrier(1, EPI_THREADS);
-        nparts = *bcast;
+        int nparts = *bcast;
         if (nparts > kMaxParts) {  // excluded by the host's cluster clamp
           if (elected) raise(5);
           nparts = 0;
         }
-        store = nparts > 0;
-        if (store) {
+        if (nparts > 0) {
           __threadfence();  // acquire side of the counter: the other pieces' partials are visible
+          const float4* parts[kMaxParts];
           for (int pj = 0; pj < nparts; ++pj) {
             const int cj = c_first + pj;
             const int fj = static_cast<int>(sk_start(cj, g) / g.kb);
-            parts[pj] = g.ws + ((static_cast<int64_t>(cj) * 2 + rank) * 2 + (j == fj ? 0 : 1)) * slot_elems;
+            parts[pj] = reinterpret_cast<const float4*>(
+                g.ws + ((static_cast<int64_t>(cj) * 2 + rank) * 2 + (j == fj ? 0 : 1)) * slot_elems);
           }
-        }
-      }
-      if (store) {
 #pragma unroll 1
-        for (int c = 0; c < C::NT; c += STG_T) {
-          __nv_bfloat16* buf = stg + (chunk & 1) * (STG_T * ROWS);
-          // The store issued from this buffer two chunks ago has read it.
-          if (elected && chunk >= 2) bulk_wait_read<1>();
-          named_barrier(1, EPI_THREADS);
+          for (int c = 0; c < C::NT; c += STG_T) {
+            // Sum the pieces in cluster order; three pieces' loads in flight at a time.
+            float4 sum[8];
 #pragma unroll
-          for (int h = 0; h < STG_T; h += 16) {
-            float v[16];
-            if (s.whole) {
-              __syncwarp();
-              tmem_ld16(tacc + ((c + h) / NS) * C::SUB_COLS + ((c + h) % NS), v);
-            } else {
-              // Sum in cluster order; two pieces' loads in flight at a time.
+            for (int i4 = 0; i4 < 8; ++i4) sum[i4] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int pj = 0; pj < nparts; pj += 3) {
+              float4 ld[3][8];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = 0.f;
-              int pj = 0;
-              for (; pj + 1 < nparts; pj += 2) {
-                float a[16], b[16];
+              for (int u = 0; u < 3; ++u)
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                  a[i] = __ldcg(parts[pj] + static_cast<int64_t>(c + h + i) * ROWS + row);
-                  b[i] = __ldcg(parts[pj + 1] + static_cast<int64_t>(c + h + i) * ROWS + row);
-                }
+                for (int i4 = 0; i4 < 8; ++i4)
+                  if (pj + u < nparts) ld[u][i4] = __ldcg(parts[pj + u] + static_cast<int64_t>(c / 4 + i4) * ROWS + row);
 #pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] = (v[i] + a[i]) + b[i];
-              }
-              if (pj < nparts) {
+              for (int u = 0; u < 3; ++u)
+                if (pj + u < nparts)
 #pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] += __ldcg(parts[pj] + static_cast<int64_t>(c + h + i) * ROWS + row);
-              }
+                  for (int i4 = 0; i4 < 8; ++i4) {
+                    sum[i4].x += ld[u][i4].x;
+                    sum[i4].y += ld[u][i4].y;
+                    sum[i4].z += ld[u][i4].z;
+                    sum[i4].w += ld[u][i4].w;
+                  }
             }
+            float v[STG_T];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) buf[(h + i) * ROWS + row] = __float2bfloat16_rn(v[i]);
+            for (int i4 = 0; i4 < 8; ++i4) {
+              v[4 * i4] = sum[i4].x;
+              v[4 * i4 + 1] = sum[i4].y;
+              v[4 * i4 + 2] = sum[i4].z;
+              v[4 * i4 + 3] = sum[i4].w;
+            }
+            store_chunk(v, y_w, y_x0 + c);
           }
-          fence_proxy_async_smem();
-          named_barrier(1, EPI_THREADS);
-          if (elected && y_w < g.rows_w && y_x0 + c < g.rows_x) {
-            tma_store_2d(&tmY, buf, y_w, y_x0 + c);
-          }
-          if (elected) bulk_commit();
-          ++chunk;
         }
       }
       if (s.whole) {
         fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(map_to_rank(&tempty[acc], 0));
+        if (g.stamps && elected && eseg < 8) stamp(g, 11 + 4 * eseg, now_ns());
       }
+      ++eseg;
       if (++acc == C::NACC) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
     if (elected) bulk_wait_all();
+    if (g.stamps && elected) stamp(g, 6, now_ns());
   }
   if (warp == 0 && lane == 0 && *abort_flag) {
     // Loads issued before the abort complete within microseconds; give them 200 us.
@@ -580,7 +681,7 @@ extern "C" int sh_gemm_sk_shape(int rows_w, int rows_x, int K, int ns, int nsub,
 
 extern "C" int sh_gemm_bf16_sk(const void* W, int rows_w, int64_t ldw, const void* X, int rows_x, int64_t ldx,
                                int K, void* Y, int64_t ldy, int ns, int nsub, int clusters, float* ws, int* cnt,
-                               int* err, cudaStream_t stream) {
+                               int* err, unsigned long long* stamps, cudaStream_t stream) {
   if (K % BK != 0 || K <= 0) return -2;
   if (rows_w <= 0 || rows_x <= 0) return 0;
   if ((reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(X) & 15) ||
@@ -604,6 +705,9 @@ extern "C" int sh_gemm_bf16_sk(const void* W, int rows_w, int64_t ldw, const voi
   // iterations meets at most 16 ranges (the fix-up adds at most 16 partials).
   const int64_t min_range = (g.kb + kMaxParts - 2) / (kMaxParts - 1);
   int64_t gs = g.sk_iters / min_range;
+  // At most kMaxPiecesPerTile pieces per split tile: the last piece's fix-up reads all of them.
+  const int64_t cap = static_cast<int64_t>(tiles % g.clusters) * kMaxPiecesPerTile;
+  if (gs > cap) gs = cap;
   if (gs > g.clusters) gs = g.clusters;
   if (gs < 1) gs = 1;
   g.sk_clusters = static_cast<int>(gs);
@@ -611,6 +715,9 @@ extern "C" int sh_gemm_bf16_sk(const void* W, int rows_w, int64_t ldw, const voi
   g.ws = ws;
   g.cnt = cnt;
   g.err = err;
+  g.stamps = stamps;
+  g.y = static_cast<__nv_bfloat16*>(Y);
+  g.ldy = ldy;
   CUtensorMap mw, mx, my;
   int r = encode(&mw, W, rows_w, K, ldw, BK, ROWS, true);
   if (r) return 1000 + r;

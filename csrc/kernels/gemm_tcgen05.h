@@ -46,6 +46,10 @@ struct SkParams {
   float* ws;             // fp32 partial slots [clusters][2 ranks][2][NT][128]
   int* cnt;              // [tiles][2] arrival counters, zero between calls
   int* err;
+  // Optional phase timestamps (%globaltimer ns) per CTA, [grid][64] (nullptr: off); see gemm_streamk.cu.
+  unsigned long long* stamps;
+  __nv_bfloat16* y;      // output [rows_x][ldy]
+  int64_t ldy;
 };
 
 #ifdef __cplusplus
@@ -53,14 +57,15 @@ extern "C" {
 #endif
 // Stream-K linear y = X W^T on tcgen05 CTA pairs, weights on the MMA M side:
 // W [rows_w, K] (row stride ldw), X [rows_x, K], y [rows_x, ldy] bf16; K % 64 == 0,
-// 16-byte aligned bases and row strides.  One tile = 256 weight rows x
+// 16-byte aligned bases and row strides, rows_w % 8 == 0.  One tile = 256 weight rows x
 // ns*nsub tokens ((ns, nsub) in {(64,1), (128,1), (192,1), (256,1), (192,2), (256,2)}).
 // `clusters` CTA pairs each own tiles / clusters whole tiles and share the
-// k-blocks of the remaining tiles (a split tile has at most 16 pieces).  ws: >= the floats reported by
+// k-blocks of the remaining tiles (a split tile has at most 3 pieces).  ws: >= the floats reported by
 // sh_gemm_sk_shape; cnt: >= 2 * tiles ints, zero before the first call (the
 // kernel leaves them zero).  One call at a time per (ws, cnt) pair.
 int sh_gemm_bf16_sk(const void* W, int rows_w, int64_t ldw, const void* X, int rows_x, int64_t ldx, int K, void* Y,
-                    int64_t ldy, int ns, int nsub, int clusters, float* ws, int* cnt, int* err, cudaStream_t stream);
+                    int64_t ldy, int ns, int nsub, int clusters, float* ws, int* cnt, int* err,
+                    unsigned long long* stamps, cudaStream_t stream);
 // Tile count and workspace floats of a stream-K call (0 on success).
 int sh_gemm_sk_shape(int rows_w, int rows_x, int K, int ns, int nsub, int clusters, int64_t* tiles,
                      int64_t* ws_floats);

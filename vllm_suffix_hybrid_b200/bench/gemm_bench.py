@@ -150,6 +150,48 @@ def nvfp4_main(a):
                           "w4a16_max_abs_err_vs_dequantised": err, "w4a4_max_abs_err_vs_fp32_oracle": err44}))
 
 
+def stamps_main(a):
+    """Phase timeline of the stream-K kernel (in-kernel %globaltimer stamps, no profiler) for one config."""
+    import statistics
+
+    from vllm_suffix_hybrid_b200 import ops
+    from vllm_suffix_hybrid_b200.ops.gemm import _sk_buffers
+
+    kind, sw, bn, sp, cl = a.config.split(",")
+    bn, nsub, cl = int(bn), int(sp), int(cl)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for name, M, N, K in SHAPES:
+        if a.only and name not in a.only.split(","):
+            continue
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        nt = bn * nsub
+        tiles = -(-N // 256) * -(-M // nt)
+        ws, cnt = _sk_buffers(x.device, cl * 4 * nt * 128, 2 * tiles)
+        st = torch.zeros(2 * cl, 64, dtype=torch.int64, device="cuda")
+        for _ in range(3):
+            flush.zero_()
+            ops.native().gemm_bf16_sk(y, x, w, bn, nsub, cl, ws, cnt, None, st)
+        torch.cuda.synchronize()
+        t = st.cpu()
+        t0 = int(t[:, 0].min())
+        rel = lambda v: (int(v) - t0) / 1e3  # noqa: E731
+        ends = [rel(t[i, 6]) for i in range(t.shape[0]) if t[i, 6] > 0]
+        lead = [i for i in range(0, t.shape[0], 2)]
+        summary = {
+            "shape": name, "config": a.config, "tiles": tiles,
+            "cta_end_us": {"min": round(min(ends), 2), "median": round(statistics.median(ends), 2), "max": round(max(ends), 2)},
+            "dep_wait_done_us_median": round(statistics.median(rel(t[i, 2]) for i in range(t.shape[0])), 2),
+            "producer_wait_free_stage_us_median": round(statistics.median(int(t[i, 3]) for i in range(t.shape[0])) / 1e3, 2),
+            "mma_wait_loaded_stage_us_median": round(statistics.median(int(t[i, 4]) for i in lead) / 1e3, 2),
+            "mma_wait_free_accumulator_us_median": round(statistics.median(int(t[i, 5]) for i in lead) / 1e3, 2),
+            "segments_cta0": [[round(rel(t[0, 8 + 4 * j + q]), 2) if t[0, 8 + 4 * j + q] > 0 else None for q in range(4)]
+                              for j in range(8) if t[0, 8 + 4 * j] > 0],
+        }
+        print(json.dumps(summary), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", action="store_true")
@@ -160,6 +202,8 @@ def main():
     ap.add_argument("--once", action="store_true",
                     help="no timing: two eager launches of ours then cuBLAS per shape (for ncu captures)")
     ap.add_argument("--lib-only", action="store_true", help="with --once: launch only cuBLAS (profiling the library)")
+    ap.add_argument("--stamps", action="store_true",
+                    help="with --config sk,...: print the stream-K kernel's in-kernel phase timeline")
     ap.add_argument("--config", default="", help="force kind,swap,bn,splits,clusters (e.g. sk,1,192,2,74 or pair,0,256,1,0)")
     ap.add_argument("--w4a4", action="store_true", help="with --nvfp4 --once: launch the W4A4 kernel")
     ap.add_argument("--nvfp4", action="store_true",
@@ -167,6 +211,8 @@ def main():
     a = ap.parse_args()
     if a.nvfp4:
         return nvfp4_main(a)
+    if a.stamps:
+        return stamps_main(a)
     from vllm_suffix_hybrid_b200.ops.gemm import plan, tcgen05_linear
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
