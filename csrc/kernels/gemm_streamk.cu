@@ -238,7 +238,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   __syncthreads();
   cluster_sync();  // the peer's barriers are initialised before any remote arrive / complete_tx
   fence_after();
-  shk::pdl_trigger();
+  {  // Dependents may launch once this CTA's MMAs are done (triggered by the epilogue at its last
+     // segment); a CTA without work lets them launch now.
+    SegIter any(blockIdx.x >> 1, g);
+    Seg first;
+    if (!any.next(first, g)) shk::pdl_trigger();
+  }
   // griddepcontrol.wait: the producer waits after issuing its first weight loads (below); every
   // other role waits here (the epilogue writes y and the split partials, which the previous kernel
   // may still read).
@@ -445,6 +450,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         break;
       }
       if (g.stamps && elected && eseg < 8) stamp(g, 10 + 4 * eseg, now_ns());
+      if (elected) {  // the last segment's MMAs are done: the next kernel may start launching
+        SegIter peek = it;
+        Seg nxt;
+        if (!peek.next(nxt, g)) shk::pdl_trigger();
+      }
       fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * C::ACC_COLS;
       if (s.whole) {

@@ -141,10 +141,11 @@ __global__ void __launch_bounds__(192, 1)
   fence_before();
   __syncthreads();
   fence_after();
-  shk::pdl_trigger();
   shk::pdl_wait();  // inputs of the previous kernel are complete from here on
   const uint32_t tmem_base = *tmem_slot;
   const int total_work = g.groups ? (*g.num_groups) * g.tiles_p : g.tiles_p * g.tiles_q * g.splits;
+  // Dependents may launch once this CTA's last tile is accumulated (triggered by the epilogue).
+  if (static_cast<int>(blockIdx.x) >= total_work) shk::pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -251,6 +252,7 @@ __global__ void __launch_bounds__(192, 1)
         *abort_flag = 1;
         break;
       }
+      if (warp == 2 && lane == 0 && w + static_cast<int>(gridDim.x) >= total_work) shk::pdl_trigger();
       fence_after();
       const int p = wk.tp * BM + row;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
@@ -447,11 +449,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   __syncthreads();
   cluster_sync();  // the peer's barriers are initialised before any remote arrive / complete_tx
   fence_after();
-  shk::pdl_trigger();
   shk::pdl_wait();  // inputs of the previous kernel are complete from here on
   const uint32_t tmem_base = *tmem_slot;
   const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
   const int total_work = g.tiles_p * g.tiles_q * g.splits;
+  // Dependents may launch once this CTA's last tile is accumulated (triggered by the epilogue).
+  if (cid >= total_work) shk::pdl_trigger();
   const uint32_t peer_abort = map_to_rank(const_cast<int*>(abort_flag), rank ^ 1);
   auto raise = [&](int code) {
     if (g.err) atomicCAS(g.err, 0, code);
@@ -557,6 +560,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         if (lane == 0) raise(4);
         break;
       }
+      if (warp == 2 && lane == 0 && w + ncl >= total_work) shk::pdl_trigger();
       fence_after();
       const int p = wk.tp * (2 * PAIR_ROWS) + static_cast<int>(rank) * PAIR_ROWS + row;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * pair_acc_cols<BN>();

@@ -190,7 +190,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  shk::pdl_trigger();
+  // Dependents may launch once this CTA works on its last unit (triggered below), not at its start:
+  // their CTAs would otherwise sit on the SMs for the whole kernel.
+  if (blockIdx.x >= units) shk::pdl_trigger();
   shk::pdl_wait();  // inputs of the previous kernel are complete from here on
 
   if (warp == 0) {
@@ -239,6 +241,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int key0 = kpart * (KEYS / KS);
   int it = 0;  // pages consumed by this CTA so far (ring position)
   for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    if (u + static_cast<int>(gridDim.x) >= units && threadIdx.x == 32) shk::pdl_trigger();
     const Unit w = unit_of(p, u, ntiles);
     // Query rows of this unit -> smem (compute warps only; sQ is free once
     // every compute warp has copied its fragments of the previous unit).

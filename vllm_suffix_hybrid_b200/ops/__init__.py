@@ -116,7 +116,13 @@ _ATTN_WS = {}
 
 
 def attention_splits(num_tiles: int, kv_heads: int, max_pages: int, sms: int = 148) -> int:
-    """KV splits per request so the grid covers ~4 waves of SMs (1..16).
+    """KV splits per request (1..16).
+
+    Splitting the keys lets short batches fill the SMs but costs a merge pass
+    over fp32 partials (about a fifth of the attention time at decode sizes).
+    With at least two waves of (tile, kv head) units the persistent kernel
+    balances well enough unsplit, so splits are used only below that, sized
+    for about four waves.  SH_ATTN_SPLITS forces a count.
 
     In batch-invariant mode (SH_BATCH_INVARIANT=1) the count depends on
     max_pages only, so a query row's merge order does not change with the
@@ -124,7 +130,12 @@ def attention_splits(num_tiles: int, kv_heads: int, max_pages: int, sms: int = 1
     """
     if os.environ.get("SH_BATCH_INVARIANT", "0") == "1":
         return int(max(1, min(8, max_pages // 2)))
+    forced = os.environ.get("SH_ATTN_SPLITS")
+    if forced:
+        return int(max(1, min(16, int(forced), max(1, max_pages // 2))))
     units = max(num_tiles * kv_heads, 1)
+    if units >= 2 * sms:
+        return 1
     want = -(-4 * sms // units)
     return int(max(1, min(16, want, max(1, max_pages // 2))))
 
