@@ -8,6 +8,7 @@
 #include "gdn.h"
 #include "moe.h"
 #include "mla.h"
+#include "dsa_indexer.h"
 #include "gemm_fp4mma.h"
 #include "gemm_nvfp4.h"
 #include "paged_attention.h"
@@ -383,31 +384,81 @@ void mla_cache_write(torch::Tensor latent, torch::Tensor c, torch::Tensor kpe, t
   TORCH_CHECK(r == 0, "sh_mla_cache_write failed with code ", r);
 }
 
-void dsa_topk(torch::Tensor topk, torch::Tensor logits, torch::Tensor q, torch::Tensor w, torch::Tensor kcache,
-              torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start) {
-  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.is_contiguous(), "dsa: q [T, IH, ID]");
-  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "dsa: w [T, IH] fp32");
-  TORCH_CHECK(kcache.scalar_type() == at::kBFloat16 && kcache.dim() == 3 && kcache.size(1) == 64, "dsa: kcache");
-  TORCH_CHECK(topk.scalar_type() == at::kInt && topk.is_contiguous() && logits.scalar_type() == at::kFloat,
-              "dsa: outputs");
-  DsaParams p{};
-  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
-  p.w = w.data_ptr<float>();
-  p.kcache = reinterpret_cast<const __nv_bfloat16*>(kcache.data_ptr());
+// Indexer key cache: page [64 x 128 e4m3 | 64 f32 scales] (8448 bytes) per 64 slots.
+void dsa_cache_write(torch::Tensor cache, torch::Tensor k, torch::Tensor slots) {
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.dim() == 2 && cache.size(1) == SH_DSA_PAGE_BYTES &&
+                  cache.is_contiguous() && cache.is_cuda(),
+              "dsa_cache_write: cache [pages, 8448] uint8");
+  TORCH_CHECK(k.scalar_type() == at::kBFloat16 && k.dim() == 2 && k.size(1) == SH_DSA_DIM && k.stride(1) == 1,
+              "dsa_cache_write: k [T, 128] bf16 with unit inner stride");
+  TORCH_CHECK(slots.scalar_type() == at::kLong && slots.is_contiguous() && slots.numel() == k.size(0),
+              "dsa_cache_write: slots [T] int64");
+  const int r = sh_dsa_cache_write(cache.data_ptr<uint8_t>(), reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()),
+                                   k.stride(0), slots.data_ptr<int64_t>(), static_cast<int>(k.size(0)),
+                                   at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_dsa_cache_write failed with code ", r);
+}
+
+// q8 = e4m3 queries, wq = w * per-row query scale (rows of 128 values).
+void dsa_quant_q(torch::Tensor q8, torch::Tensor wq, torch::Tensor q, torch::Tensor w) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.size(2) == SH_DSA_DIM && q.is_contiguous(),
+              "dsa_quant_q: q [T, IH, 128] bf16 contiguous");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.numel() == q.size(0) * q.size(1),
+              "dsa_quant_q: w [T, IH] fp32");
+  TORCH_CHECK(q8.scalar_type() == at::kByte && q8.is_contiguous() && q8.numel() == q.numel(), "dsa_quant_q: q8");
+  TORCH_CHECK(wq.scalar_type() == at::kFloat && wq.is_contiguous() && wq.numel() == w.numel(), "dsa_quant_q: wq");
+  const int r = sh_dsa_quant_q(q8.data_ptr<uint8_t>(), wq.data_ptr<float>(),
+                               reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), w.data_ptr<float>(),
+                               static_cast<int>(w.numel()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_dsa_quant_q failed with code ", r);
+}
+
+// Indexer logits into `logits` rows and (unless score_only) the top-K positions per query row.
+void dsa_index(torch::Tensor topk, torch::Tensor logits, torch::Tensor q8, torch::Tensor wq, torch::Tensor cache,
+               torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start, int64_t grid,
+               c10::optional<torch::Tensor> err, bool score_only) {
+  TORCH_CHECK(q8.scalar_type() == at::kByte && q8.dim() == 3 && q8.size(2) == SH_DSA_DIM && q8.is_contiguous(),
+              "dsa_index: q8 [T, IH, 128] uint8");
+  TORCH_CHECK(wq.scalar_type() == at::kFloat && wq.is_contiguous() && wq.numel() == q8.size(0) * q8.size(1),
+              "dsa_index: wq [T, IH] fp32");
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.dim() == 2 && cache.size(1) == SH_DSA_PAGE_BYTES &&
+                  cache.is_contiguous(),
+              "dsa_index: cache [pages, 8448] uint8");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1 &&
+                  logits.size(0) >= q8.size(0) && logits.stride(0) % 4 == 0 &&
+                  logits.size(1) >= block_tables.size(1) * SH_DSA_PAGE_KEYS,
+              "dsa_index: logits [T, >= max_keys] fp32 rows (row stride a multiple of 4)");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2 && block_tables.stride(1) == 1,
+              "dsa_index: block_tables int32 [B, W]");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kLong && q_start.scalar_type() == at::kLong &&
+                  q_start.numel() == seq_lens.numel() + 1 && block_tables.size(0) >= seq_lens.numel(),
+              "dsa_index: seq_lens [B], q_start [B + 1] int64");
+  if (!score_only)
+    TORCH_CHECK(topk.scalar_type() == at::kInt && topk.dim() == 2 && topk.is_contiguous() &&
+                    topk.size(0) == q8.size(0),
+                "dsa_index: topk [T, K] int32");
+  if (err) TORCH_CHECK(err->scalar_type() == at::kInt && err->numel() >= 1, "dsa_index: err int32");
+  DsaIndexParams p{};
+  p.q8 = q8.data_ptr<uint8_t>();
+  p.wq = wq.data_ptr<float>();
+  p.kcache = cache.data_ptr<uint8_t>();
+  p.num_pages = static_cast<int>(cache.size(0));
   p.block_tables = block_tables.data_ptr<int32_t>();
   p.bt_stride = block_tables.stride(0);
   p.seq_lens = seq_lens.data_ptr<int64_t>();
   p.q_start = q_start.data_ptr<int64_t>();
-  p.B = static_cast<int>(seq_lens.size(0));
+  p.B = static_cast<int>(seq_lens.numel());
+  p.T = static_cast<int>(q8.size(0));
+  p.IH = static_cast<int>(q8.size(1));
+  p.K = score_only ? 0 : static_cast<int>(topk.size(1));
   p.logits = logits.data_ptr<float>();
-  p.topk = topk.data_ptr<int32_t>();
-  p.T = static_cast<int>(q.size(0));
-  p.IH = static_cast<int>(q.size(1));
-  p.ID = static_cast<int>(q.size(2));
-  p.K = static_cast<int>(topk.size(1));
-  p.max_keys = static_cast<int>(logits.size(1));
-  const int r = sh_dsa_topk(&p, at::cuda::getCurrentCUDAStream());
-  TORCH_CHECK(r == 0, "sh_dsa_topk failed with code ", r, " (IH=", p.IH, ", ID=", p.ID, ")");
+  p.ld = logits.stride(0);
+  p.topk = score_only ? nullptr : topk.data_ptr<int32_t>();
+  p.err = err ? err->data_ptr<int>() : nullptr;
+  p.grid = static_cast<int>(grid);
+  const int r = score_only ? sh_dsa_score(&p, at::cuda::getCurrentCUDAStream())
+                           : sh_dsa_index(&p, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_dsa_index failed with code ", r, " (IH=", p.IH, ")");
 }
 
 // NVFP4-weight GEMM (W4A16): y[t, n] = x[t] . dequant(W[n]); grouped MoE mode with `groups`.
@@ -953,7 +1004,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("prefetch_bytes") = 0);
   m.def("mla_decode", &mla_decode);
   m.def("mla_cache_write", &mla_cache_write);
-  m.def("dsa_topk", &dsa_topk);
+  m.def("dsa_cache_write", &dsa_cache_write);
+  m.def("dsa_quant_q", &dsa_quant_q);
+  m.def("dsa_index", &dsa_index);
   m.def("gemm_nvfp4", &gemm_nvfp4, py::arg("y"), py::arg("x"), py::arg("packed"), py::arg("scales"),
         py::arg("gscale"), py::arg("bn"), py::arg("groups") = py::none(), py::arg("num_groups") = py::none(),
         py::arg("rows_p") = 0, py::arg("err") = py::none(), py::arg("splits") = 1, py::arg("ws") = py::none());

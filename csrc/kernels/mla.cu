@@ -458,164 +458,6 @@ __global__ void cache_write_fp4_kernel(uint8_t* __restrict__ cache, const __nv_b
   for (int i = threadIdx.x; i < R; i += blockDim.x) rope[i] = kpe[t * kpe_stride + i];
 }
 
-// ------------------------------------------------------------------------- DSA indexer
-constexpr int IDX_KEYS = 64;     // keys per indexer tile
-constexpr int IDX_THREADS = 512;  // 16 warps: 4 head groups x 4 key quarters
-
-__device__ __forceinline__ uint32_t ordered_bits(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // larger float -> larger unsigned
-}
-
-// One CTA per query token: logits over its causal keys, then the top-K positions.
-template <int IH, int ID>
-__global__ void __launch_bounds__(IDX_THREADS, 1) dsa_topk_kernel(DsaParams p) {
-  shk::pdl_trigger();
-  shk::pdl_wait();
-  static_assert(IH % 16 == 0 && IH <= 64 && ID % 64 == 0, "indexer geometry");
-  constexpr int CH = ID / 8;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  const uint32_t sQ = saddr(smem);                       // [64][ID] (rows >= IH zero)
-  const uint32_t sK = sQ + 64 * ID * 2;                  // [IDX_KEYS][ID]
-  float* sW = reinterpret_cast<float*>(smem + 64 * ID * 2 + IDX_KEYS * ID * 2);  // [64] head weights
-  float* sPart = sW + 64;                                 // [4 head groups][IDX_KEYS]
-  uint32_t* hist = reinterpret_cast<uint32_t*>(sPart + 4 * IDX_KEYS);  // [256]
-  uint32_t* misc = hist + 256;                           // [8]
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t = blockIdx.x;
-  const int b = request_of(p.q_start, p.B, t);
-  const int64_t qs = p.q_start[b], ql = p.q_start[b + 1] - qs, seq = p.seq_lens[b];
-  const int64_t qpos = seq - ql + (t - qs);
-  const int nkeys = static_cast<int>(qpos + 1);
-  int32_t* out = p.topk + static_cast<int64_t>(t) * p.K;
-  if (nkeys <= p.K) {  // every causal key is selected
-    for (int i = tid; i < p.K; i += IDX_THREADS) out[i] = i < nkeys ? i : -1;
-    return;
-  }
-  const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
-  float* lg = p.logits + static_cast<int64_t>(t) * p.max_keys;
-  for (int c = tid; c < 64 * CH; c += IDX_THREADS) {
-    const int r = c / CH, cc = c % CH;
-    const bool ok = r < IH;
-    cp_async16(sQ + swz<64>(r, cc), p.q + (static_cast<int64_t>(t) * IH + (ok ? r : 0)) * ID + cc * 8, ok);
-  }
-  if (tid < 64) sW[tid] = tid < IH ? p.w[static_cast<int64_t>(t) * IH + tid] : 0.f;
-  asm volatile("cp.async.commit_group;\n" ::);
-  const int hg = warp & 3, kq = warp >> 2;  // 16 heads x 16 keys per warp
-  for (int k0 = 0; k0 < nkeys; k0 += IDX_KEYS) {
-    __syncthreads();
-    for (int c = tid; c < IDX_KEYS * CH; c += IDX_THREADS) {
-      const int key = c / CH, cc = c % CH;
-      const int pos = k0 + key;
-      const bool ok = pos < nkeys;
-      const int64_t row = ok ? static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63) : 0;
-      cp_async16(sK + swz<IDX_KEYS>(key, cc), p.kcache + row * ID + cc * 8, ok);
-    }
-    asm volatile("cp.async.commit_group;\n" ::);
-    asm volatile("cp.async.wait_group 0;\n" ::);
-    __syncthreads();
-    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    if (hg * 16 < IH) {
-#pragma unroll
-      for (int kk = 0; kk < ID / 16; ++kk) {
-        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-        ldsm_x4(sQ + swz<64>(hg * 16 + (lane & 15), 2 * kk + (lane >> 4)), a0, a1, a2, a3);
-        ldsm_x4(sK + swz<IDX_KEYS>(kq * 16 + (lane & 7) + ((lane >> 4) << 3), 2 * kk + ((lane >> 3) & 1)), b0, b1, b2,
-                b3);
-        mma16816(sc[0], a0, a1, a2, a3, b0, b1);
-        mma16816(sc[1], a0, a1, a2, a3, b2, b3);
-      }
-    }
-    // relu * w over this warp's 16 heads, summed over the heads -> per key partial
-    const float wa = sW[hg * 16 + (lane >> 2)], wb = sW[hg * 16 + (lane >> 2) + 8];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float v = fmaxf(sc[nt][e], 0.f) * wa + fmaxf(sc[nt][2 + e], 0.f) * wb;
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        v += __shfl_xor_sync(0xffffffffu, v, 8);
-        v += __shfl_xor_sync(0xffffffffu, v, 16);
-        if ((lane >> 2) == 0) sPart[hg * IDX_KEYS + kq * 16 + nt * 8 + 2 * (lane & 3) + e] = v;
-      }
-    __syncthreads();
-    for (int key = tid; key < IDX_KEYS; key += IDX_THREADS) {
-      const int pos = k0 + key;
-      if (pos < nkeys)
-        lg[pos] = sPart[key] + sPart[IDX_KEYS + key] + sPart[2 * IDX_KEYS + key] + sPart[3 * IDX_KEYS + key];
-    }
-  }
-  __syncthreads();
-  // radix select of the K-th largest ordered key (4 passes of 8 bits, most significant first)
-  uint32_t prefix = 0, mask = 0;
-  int remaining = p.K;  // how many of the top K lie at or below the current prefix bucket
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += IDX_THREADS) hist[i] = 0;
-    __syncthreads();
-    for (int i = tid; i < nkeys; i += IDX_THREADS) {
-      const uint32_t u = ordered_bits(lg[i]);
-      if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 255], 1u);
-    }
-    __syncthreads();
-    if (tid == 0) {
-      int acc = 0, d = 255;
-      for (; d > 0; --d) {
-        if (acc + static_cast<int>(hist[d]) >= remaining) break;
-        acc += hist[d];
-      }
-      misc[0] = static_cast<uint32_t>(d);
-      misc[1] = static_cast<uint32_t>(remaining - acc);
-    }
-    __syncthreads();
-    prefix |= misc[0] << shift;
-    mask |= 255u << shift;
-    remaining = static_cast<int>(misc[1]);
-    __syncthreads();
-  }
-  // threshold = prefix: take every key above it and the `remaining` latest keys equal to it
-  // (skip the first eq_total - remaining equal keys in position order), written in ascending order
-  const uint32_t thr = prefix;
-  if (tid == 0) misc[2] = 0;
-  __syncthreads();
-  {
-    uint32_t eq = 0;
-    for (int i = tid; i < nkeys; i += IDX_THREADS) eq += ordered_bits(lg[i]) == thr ? 1u : 0u;
-    if (eq) atomicAdd(&misc[2], eq);
-  }
-  __syncthreads();
-  const int skip = static_cast<int>(misc[2]) - remaining;
-  uint32_t* wsel = misc + 8;        // [16] per-warp selected counts
-  uint32_t* weq = wsel + 16;        // [16] per-warp equal counts
-  const uint32_t lt_mask = (1u << lane) - 1u;
-  int base = 0, base_eq = 0;
-  for (int c0 = 0; c0 < nkeys; c0 += IDX_THREADS) {
-    const int i = c0 + tid;
-    const uint32_t u = i < nkeys ? ordered_bits(lg[i]) : 0u;
-    const bool gt = i < nkeys && u > thr, eqk = i < nkeys && u == thr;
-    const uint32_t beq = __ballot_sync(0xffffffffu, eqk);
-    if (lane == 0) weq[warp] = __popc(beq);
-    __syncthreads();
-    int eq_before = base_eq;
-    for (int w = 0; w < warp; ++w) eq_before += weq[w];
-    eq_before += __popc(beq & lt_mask);
-    const bool sel = gt || (eqk && eq_before >= skip);
-    const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
-    if (lane == 0) wsel[warp] = __popc(bsel);
-    __syncthreads();
-    int pos = base;
-    for (int w = 0; w < warp; ++w) pos += wsel[w];
-    pos += __popc(bsel & lt_mask);
-    if (sel && pos < p.K) out[pos] = i;
-    for (int w = 0; w < IDX_THREADS / 32; ++w) {
-      base += wsel[w];
-      base_eq += weq[w];
-    }
-    __syncthreads();
-  }
-  for (int i = base + tid; i < p.K; i += IDX_THREADS) out[i] = -1;
-}
-
 }  // namespace mla
 }  // namespace shk
 
@@ -642,19 +484,6 @@ int launch_mla(const MlaParams& p, cudaStream_t st) {
   return static_cast<int>(cudaGetLastError());
 }
 
-template <int IH, int ID>
-int launch_dsa(const DsaParams& p, cudaStream_t st) {
-  const int smem = 64 * ID * 2 + IDX_KEYS * ID * 2 + (64 + 4 * IDX_KEYS) * 4 + (256 + 8 + 32) * 4 + 128;
-  auto k = dsa_topk_kernel<IH, ID>;
-  static bool ready = false;
-  if (!ready) {
-    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    ready = true;
-  }
-  shk::launch(k, dim3(p.T), dim3(IDX_THREADS), smem, st, p);
-  return static_cast<int>(cudaGetLastError());
-}
 }  // namespace
 
 extern "C" int sh_mla_decode(const MlaParams* p, int C, int V, cudaStream_t stream) {
@@ -686,10 +515,3 @@ extern "C" int sh_mla_cache_write(__nv_bfloat16* latent, const __nv_bfloat16* c,
   return static_cast<int>(cudaGetLastError());
 }
 
-extern "C" int sh_dsa_topk(const DsaParams* p, cudaStream_t stream) {
-  if (p->T <= 0) return 0;
-  if (p->K <= 0 || !p->topk || !p->logits) return -1;
-  if (p->IH == 64 && p->ID == 128) return launch_dsa<64, 128>(*p, stream);
-  if (p->IH == 16 && p->ID == 64) return launch_dsa<16, 64>(*p, stream);
-  return -2;
-}

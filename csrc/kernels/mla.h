@@ -23,19 +23,6 @@ struct MlaParams {
   float scale_log2;             // softmax scale * log2(e)
 };
 
-struct DsaParams {
-  const __nv_bfloat16* q;       // [T, IH, ID] indexer queries
-  const float* w;               // [T, IH] head weights (scales folded in)
-  const __nv_bfloat16* kcache;  // paged [num_blocks, 64, ID] indexer keys
-  const int32_t* block_tables;
-  int64_t bt_stride;
-  const int64_t* seq_lens;
-  const int64_t* q_start;
-  int B;
-  float* logits;                // scratch [T, max_keys]
-  int32_t* topk;                // [T, K] selected positions in ascending order, -1 padded
-  int T, IH, ID, K, max_keys;
-};
 
 #ifdef __cplusplus
 extern "C" {
@@ -52,7 +39,6 @@ int sh_mla_cache_write_fp4(uint8_t* cache, const __nv_bfloat16* c, int64_t c_str
 // latent[slot[t]] = cat(c[t], kpe[t]) for slot[t] >= 0 (C = Cl + R).
 int sh_mla_cache_write(__nv_bfloat16* latent, const __nv_bfloat16* c, int64_t c_stride, const __nv_bfloat16* kpe,
                        int64_t kpe_stride, const int64_t* slots, int T, int Cl, int R, cudaStream_t stream);
-int sh_dsa_topk(const DsaParams* p, cudaStream_t stream);
 #ifdef __cplusplus
 }
 #endif

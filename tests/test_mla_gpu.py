@@ -57,27 +57,76 @@ def test_mla_decode_matches_reference(C, V, H, sparse, nsplit):
     assert err < 2e-2 * (1 + want.abs().max().item()), err
 
 
-@pytest.mark.parametrize("IH,ID", [(64, 128), (16, 64)])
-def test_dsa_topk_matches_reference(IH, ID):
-    gen = torch.Generator().manual_seed(IH)
-    seqs, qlens = [700, 50, 1300], [3, 1, 2]
-    kc, bt = _paged(seqs, ID, gen)
+def _dsa_case(seqs, qlens, IH, gen):
+    """Index-key page cache (written by the host reference) with shuffled page ids, queries and weights."""
+    nb = [(s + 63) // 64 for s in seqs]
+    pages = sum(nb) + 2
+    perm = torch.randperm(pages - 1, generator=gen) + 1
+    bt = torch.zeros(len(seqs), max(nb) + 1, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(nb):
+        bt[i, :n] = perm[o:o + n].int()
+        o += n
+    cache = torch.zeros(pages, ops.DSA_PAGE_BYTES, dtype=torch.uint8)
+    for i, s in enumerate(seqs):
+        pos = torch.arange(s)
+        slots = bt[i, pos // 64].long() * 64 + pos % 64
+        k = (torch.randn(s, 128, generator=gen) * torch.rand(s, 1, generator=gen)).to(torch.bfloat16)
+        ref.dsa_cache_write(cache, k, slots)
     T = sum(qlens)
-    qi = (torch.randn(T, IH, ID, generator=gen) * 0.3).to(torch.bfloat16)
+    qi = (torch.randn(T, IH, 128, generator=gen) * 0.3).to(torch.bfloat16)
     w = torch.randn(T, IH, generator=gen)
     q_start = torch.tensor(np.cumsum([0] + qlens), dtype=torch.long)
-    seq_lens = torch.tensor(seqs, dtype=torch.long)
-    K = 128
-    want = ref.dsa_topk(qi.float(), w, kc.float(), bt, seq_lens, q_start, K)
-    got = ops.dsa_topk(qi.cuda(), w.cuda(), kc.cuda(), bt.cuda(), seq_lens.cuda(), q_start.cuda(), K)
-    torch.cuda.synchronize()
-    got = got.cpu().long()
-    for t in range(T):
-        g = set(x for x in got[t].tolist() if x >= 0)
-        r = set(x for x in want[t].tolist() if x >= 0)
-        # the kernel sums in bf16 tensor-core tiles: allow a few near-threshold swaps
-        assert len(g) == len(r) and len(g ^ r) <= 4, (t, len(g ^ r))
-        assert got[t][: len(g)].tolist() == sorted(g)  # ascending positions, then -1
+    return cache, bt, qi, w, q_start, torch.tensor(seqs, dtype=torch.long)
+
+
+@pytest.mark.parametrize("IH", [64, 16])
+@pytest.mark.parametrize("seqs,qlens", [([700, 50, 1300], [3, 1, 2]), ([2100, 333, 4097, 64], [6, 6, 6, 6]),
+                                        ([900, 1500], [13, 40])])
+def test_dsa_index_fp8_matches_reference(IH, seqs, qlens):
+    """tcgen05 scoring over the fp8 page cache + radix top-k against the float64 host indexer: logits within
+    fp32 rounding, selected sets equal up to near-threshold swaps, positions ascending."""
+    gen = torch.Generator().manual_seed(IH + sum(seqs))
+    cache, bt, qi, w, q_start, seq_lens = _dsa_case(seqs, qlens, IH, gen)
+    dev = [x.cuda() for x in (qi, w, cache, bt, seq_lens, q_start)]
+    lg = ops.dsa_topk(*dev, 0, score_only=True).cpu()
+    want_lg = ref.dsa_logits(qi, w, cache, bt, seq_lens, q_start)
+    for t, r in enumerate(want_lg):
+        got = lg[t, : r.shape[0]]
+        tol = 1e-4 * (1 + r.abs().max().item())
+        assert torch.allclose(got, r, atol=tol, rtol=1e-4), (t, (got - r).abs().max().item())
+    K = 256
+    got = ops.dsa_topk(*dev, K).cpu()
+    want = ref.dsa_topk(qi, w, cache, bt, seq_lens, q_start, K)
+    assert ops._MLA_WS[("dsa", torch.cuda.current_device())]["err"].item() == 0
+    for t in range(got.shape[0]):
+        g = [x for x in got[t].tolist() if x >= 0]
+        r = [x for x in want[t].tolist() if x >= 0]
+        assert len(g) == len(r) and len(set(g) ^ set(r)) <= 4, (t, len(set(g) ^ set(r)))
+        assert g == sorted(g) and got[t][len(g):].eq(-1).all()
+
+
+def test_dsa_cache_write_and_quant_match_host():
+    """Device quantisation (keys into pages, queries) is bit-identical to the host reference."""
+    gen = torch.Generator().manual_seed(5)
+    T = 77
+    k = (torch.randn(T, 128, generator=gen) * torch.rand(T, 1, generator=gen) * 3).to(torch.bfloat16)
+    k[3] = 0  # an all-zero key (scale 1)
+    slots = torch.randperm(6 * 64, generator=gen)[:T].long()
+    slots[5] = -1
+    host = torch.zeros(6, ops.DSA_PAGE_BYTES, dtype=torch.uint8)
+    ref.dsa_cache_write(host, k, slots)
+    dev = torch.zeros_like(host).cuda()
+    ops.dsa_cache_write(dev, k.cuda(), slots.cuda())
+    assert torch.equal(dev.cpu(), host)
+    q = (torch.randn(T, 16, 128, generator=gen)).to(torch.bfloat16)
+    w = torch.randn(T, 16, generator=gen)
+    q8 = torch.empty(T, 16, 128, dtype=torch.uint8, device="cuda")
+    wq = torch.empty(T, 16, dtype=torch.float32, device="cuda")
+    ops.native().dsa_quant_q(q8, wq, q.cuda(), w.cuda())
+    codes, s = ref.dsa_quant(q)
+    assert torch.equal(q8.cpu(), codes.to(torch.float8_e4m3fn).view(torch.uint8))
+    assert torch.equal(wq.cpu(), w * s[..., 0])
 
 
 @pytest.mark.parametrize("name", ["deepseek_v32", "kimi_k2"])

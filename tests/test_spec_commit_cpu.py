@@ -28,7 +28,11 @@ def _model(name):
 
 
 @pytest.mark.parametrize("name", ["llama", "qwen3_next", "deepseek_v32", "kimi_k2"])
-def test_oracle_drafts_match_plain_decode(name):
+def test_oracle_drafts_match_plain_decode(name, monkeypatch):
+    # Batch-invariant mode: a verify window computes its rows in larger matmuls than plain decode, and the
+    # DeepSeek indexer quantises its queries to e4m3, so a last-bit difference in a query can move a code and
+    # change the selected keys.  Invariant mode makes every row independent of the batch.
+    monkeypatch.setenv("SH_BATCH_INVARIANT", "1")
     rng = np.random.default_rng(3)
     prompts = [rng.integers(0, 512, int(rng.integers(8, 30))) for _ in range(3)]
     base_cfg = EngineConfig(model=_model(name), spec=SpecConfig(method="none"), cache=CacheConfig(max_model_len=256),

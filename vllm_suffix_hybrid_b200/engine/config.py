@@ -164,11 +164,11 @@ def shrink(cfg: ModelConfig, layers: int = 2, hidden: int = 256, vocab: int = 10
         c.layers = max(layers, 4)
     if cfg.arch in ("deepseek_v32", "kimi_k2"):
         c.heads = 4
-        # kernel-supported test geometry: latent 64 + rope 64 (C = 128), indexer 16 heads x 64
+        # kernel-supported test geometry: latent 64 + rope 64 (C = 128), indexer 16 heads x 128
         c.q_lora, c.kv_lora, c.qk_nope, c.qk_rope, c.v_head = 64, 64, 32, 64, 32
         c.head_dim = c.qk_nope + c.qk_rope
         if cfg.dsa_heads:
-            c.dsa_heads, c.dsa_head_dim, c.dsa_topk = 16, 64, 32
+            c.dsa_heads, c.dsa_head_dim, c.dsa_topk = 16, 128, 32
     c.max_position = 8192
     return c
 

@@ -4,9 +4,10 @@
   (kv_lora) and the rotary key k_pe (rope) per token; queries are projected
   into the latent space with W_UK, attention runs over the latent rows, and
   W_UV maps the latent output back to per-head values.
-* DSA lightning indexer (V3.2): per-token index keys are cached; every query
-  scores its context with sum_h relu(q_h . k) * w_h and attends only to the
-  top-k positions.
+* DSA lightning indexer (V3.2): per-token index keys are cached in fp8 pages
+  (64 e4m3 keys of 128 bytes + 64 f32 key scales, 132 B per key); every query
+  (quantised to e4m3 per head) scores its context with
+  k_scale * sum_h relu(q_h . k) * w_h and attends only to the top-k positions.
 * MoE: sigmoid group-limited router with score-correction bias, routed
   scaling, one shared expert; the first `first_dense_layers` layers are dense.
 * Weights may be NVFP4 (ModelOpt layout: packed e2m1, e4m3 block-16 scales,
@@ -153,7 +154,7 @@ class MLAttention:
         if self.dsa:
             qi = self.idx_q(qa).view(T, self.ih, self.idim)
             ki = self.idx_k(x)
-            ops.mla_cache_write(icache, ki.contiguous(), ki[:, :0], meta.slot_mapping)
+            ops.dsa_cache_write(icache, ki.contiguous(), meta.slot_mapping)
             wt = ops.linear(x, self.idx_w).float() * (self.ih ** -0.5) * (self.idim ** -0.5)
             topk = ops.dsa_topk(qi, wt, icache, meta.block_tables, meta.seq_lens, meta.q_start, self.itopk)
         if x.is_cuda:
@@ -222,8 +223,7 @@ class DeepseekModel:
             else:
                 lat = torch.zeros(num_blocks, block_size, self.cfg.kv_lora + self.cfg.qk_rope, dtype=self.dtype,
                                   device=self.device)
-            idx = (torch.zeros(num_blocks, block_size, self.cfg.dsa_head_dim, dtype=self.dtype, device=self.device)
-                   if self.cfg.dsa_topk else None)
+            idx = ops.dsa_cache_alloc(num_blocks, block_size, self.device) if self.cfg.dsa_topk else None
             caches.append((lat, idx))
         return caches
 

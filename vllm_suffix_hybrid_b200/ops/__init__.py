@@ -254,13 +254,19 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) ->
     """y = x @ w.T for w [N, K].
 
     bf16 on a CUDA device runs the tcgen05 GEMM (K must be a multiple of 64);
-    other dtypes (the fp32 toy model) and the CPU use the library matmul.
+    other dtypes (the fp32 toy model) and the CPU use the library matmul
+    (fp32 on the CPU in batch-invariant mode: float64 accumulation).
     """
     if x.is_cuda and x.dtype == torch.bfloat16 and _GEMM_BACKEND == "tcgen05":
         from .gemm import tcgen05_linear
 
         return tcgen05_linear(x, w, out)
-    y = torch.matmul(x, w.t())
+    if not x.is_cuda and x.dtype == torch.float32 and os.environ.get("SH_BATCH_INVARIANT", "0") == "1":
+        # a row's result must not depend on the other rows of the call: float64 accumulation makes the
+        # library's batch-size-dependent summation order invisible after rounding to fp32
+        y = torch.matmul(x.double(), w.double().t()).to(x.dtype)
+    else:
+        y = torch.matmul(x, w.t())
     if out is not None:
         out.copy_(y)
         return out
@@ -535,24 +541,68 @@ def mla_splits(num_tokens: int, heads: int, max_keys: int, sms: int = 148) -> in
     return int(max(1, min(16, -(-sms // units), max(1, max_keys // 64))))
 
 
-def dsa_topk(qi: torch.Tensor, w: torch.Tensor, kcache: torch.Tensor, block_tables, seq_lens, q_start,
-             k: int) -> torch.Tensor:
-    """Lightning-indexer top-k positions per query token ([T, k], -1 padded)."""
-    if not qi.is_cuda:
-        return ref.dsa_topk(qi, w, kcache, block_tables, seq_lens, q_start, k)
-    T = qi.shape[0]
-    max_keys = block_tables.shape[1] * kcache.shape[1]
-    idx = qi.device.index if qi.device.index is not None else torch.cuda.current_device()
+DSA_PAGE_KEYS = 64
+DSA_DIM = 128
+DSA_PAGE_BYTES = DSA_PAGE_KEYS * (DSA_DIM + 4)  # 64 e4m3 keys of 128 B, then 64 f32 key scales
+_SMS = {}
+
+
+def _num_sms(device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
+
+
+def dsa_cache_alloc(num_blocks: int, block_size: int, device) -> torch.Tensor:
+    """Indexer key cache: one 8448-byte page (64 e4m3 keys + 64 f32 scales, 132 B per key) per block."""
+    if block_size != DSA_PAGE_KEYS:
+        raise ValueError(f"the indexer key cache needs {DSA_PAGE_KEYS}-token blocks, got {block_size}")
+    return torch.zeros(num_blocks, DSA_PAGE_BYTES, dtype=torch.uint8, device=device)
+
+
+def dsa_cache_write(cache: torch.Tensor, k: torch.Tensor, slots: torch.Tensor) -> None:
+    """cache page slot // 64, row slot % 64 <- e4m3(k / s) with s = amax|k| / 448 stored as the key's scale."""
+    if not cache.is_cuda:
+        ref.dsa_cache_write(cache, k, slots)
+        return
+    native().dsa_cache_write(cache, k, slots)
+
+
+def _dsa_ws(device, T: int, IH: int, max_keys: int):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
     key = ("dsa", idx)
     ws = _MLA_WS.get(key)
-    if ws is None or ws.shape[0] < T or ws.shape[1] < max_keys:
+    if ws is None or ws["q8"].shape[0] < T or ws["q8"].shape[1] != IH or ws["logits"].shape[1] < max_keys:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("indexer scratch must be sized before CUDA-graph capture")
-        ws = torch.empty(max(T, 64), max_keys, dtype=torch.float32, device=qi.device)
+        rows = max(T, 64)
+        cols = -(-max(max_keys, 64) // 4) * 4
+        ws = {"q8": torch.empty(rows, IH, DSA_DIM, dtype=torch.uint8, device=device),
+              "wq": torch.empty(rows, IH, dtype=torch.float32, device=device),
+              "logits": torch.empty(rows, cols, dtype=torch.float32, device=device),
+              "err": torch.zeros(1, dtype=torch.int32, device=device)}
         _MLA_WS[key] = ws
-    out = torch.empty(T, k, dtype=torch.int32, device=qi.device)
-    native().dsa_topk(out, ws[:T, :max_keys], qi.contiguous(), w.float().contiguous(), kcache, block_tables,
-                      seq_lens, q_start)
+    return ws
+
+
+def dsa_topk(qi: torch.Tensor, w: torch.Tensor, kcache: torch.Tensor, block_tables, seq_lens, q_start,
+             k: int, score_only: bool = False):
+    """Lightning-indexer top-k positions per query token ([T, k] int32 ascending, -1 padded).
+
+    qi [T, IH, 128] queries (quantised to e4m3 per (token, head) row here), w [T, IH] head weights, kcache
+    the fp8 page cache of dsa_cache_alloc.  score_only returns the logits rows instead ([T, >= max_keys]
+    fp32 scratch, row t valid on [0, pos_t]; a view of a reused buffer)."""
+    if not qi.is_cuda:
+        return ref.dsa_topk(qi, w, kcache, block_tables, seq_lens, q_start, k)
+    T, IH = qi.shape[0], qi.shape[1]
+    max_keys = block_tables.shape[1] * DSA_PAGE_KEYS
+    ws = _dsa_ws(qi.device, T, IH, max_keys)
+    q8, wq, logits = ws["q8"][:T], ws["wq"][:T], ws["logits"][:T]
+    native().dsa_quant_q(q8, wq, qi.contiguous(), w.float().contiguous())
+    out = logits if score_only else torch.empty(T, k, dtype=torch.int32, device=qi.device)
+    native().dsa_index(out, logits, q8, wq, kcache, block_tables, seq_lens, q_start, _num_sms(qi.device), ws["err"],
+                       score_only)
     return out
 
 

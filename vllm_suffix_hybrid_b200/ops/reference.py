@@ -398,26 +398,77 @@ def mla_attention(q_lat, q_pe, latent, block_tables, seq_lens, q_start, scale, k
     return out
 
 
-def dsa_topk(qi, w, kcache, block_tables, seq_lens, q_start, k):
-    """Lightning indexer: logits[t, s] = sum_h relu(qi[t,h] . k[s]) * w[t,h]; causal top-k positions
-    per query ([T, k] int64, -1 padded; equal logits prefer the later position)."""
-    bs = kcache.shape[1]
-    T = qi.shape[0]
-    out = torch.full((T, k), -1, dtype=torch.long, device=qi.device)
+DSA_PAGE_KEYS, DSA_DIM = 64, 128
+DSA_KEY_BYTES = DSA_PAGE_KEYS * DSA_DIM  # key bytes of a page; the 64 f32 scales follow
+
+
+def dsa_quant(x):
+    """Per-row e4m3 quantisation of [..., 128] values: s = amax / 448 (1 for a zero row), codes = e4m3(x / s)
+    rounded to nearest even.  Returns (codes as float32, s [..., 1])."""
+    x = x.float()
+    am = x.abs().amax(-1, keepdim=True)
+    s = torch.where(am > 0, am / 448.0, torch.ones_like(am))
+    return (x / s).to(torch.float8_e4m3fn).float(), s
+
+
+def dsa_cache_write(cache, k, slots):
+    """Write keys into the indexer page cache ([pages, 8448] uint8): page slot // 64, row slot % 64."""
+    ok = slots >= 0
+    if not bool(ok.any()):
+        return
+    x = k[ok].float()
+    s_all = slots[ok].long()
+    codes, sc = dsa_quant(x)
+    cb = codes.to(torch.float8_e4m3fn).view(torch.uint8)
+    sb = sc[:, 0].contiguous().view(torch.uint8).view(-1, 4)
+    pg, r = s_all // DSA_PAGE_KEYS, s_all % DSA_PAGE_KEYS
+    cols = torch.arange(DSA_DIM, device=cache.device)
+    cache[pg[:, None], (r * DSA_DIM)[:, None] + cols[None]] = cb
+    c4 = torch.arange(4, device=cache.device)
+    cache[pg[:, None], (DSA_KEY_BYTES + r * 4)[:, None] + c4[None]] = sb
+
+
+def dsa_keys(cache):
+    """Dequantised keys [pages, 64, 128] (e4m3 codes) and scales [pages, 64] of the indexer page cache."""
+    keys = cache[:, :DSA_KEY_BYTES].contiguous().view(torch.float8_e4m3fn).float().view(-1, DSA_PAGE_KEYS, DSA_DIM)
+    scales = cache[:, DSA_KEY_BYTES:].contiguous().view(torch.float32).view(-1, DSA_PAGE_KEYS)
+    return keys, scales
+
+
+def dsa_logits(qi, w, kcache, block_tables, seq_lens, q_start):
+    """Per-token indexer logits over the causal keys: logits[t][p] = ks[p] * sum_h relu(q8[t,h] . k8[p]) *
+    w[t,h] * qs[t,h] (fp32, float64 accumulation), one tensor per query token."""
+    keys, ks = dsa_keys(kcache)
+    q8, qs = dsa_quant(qi)
+    wq = w.float() * qs[..., 0]
+    out = []
     for b in range(seq_lens.shape[0]):
         s0, s1 = int(q_start[b]), int(q_start[b + 1])
         ql, sl = s1 - s0, int(seq_lens[b])
         if ql == 0:
             continue
-        nblk = (sl + bs - 1) // bs
-        Kc = kcache[block_tables[b, :nblk].long()].reshape(nblk * bs, -1)[:sl].float()
-        lg = (torch.relu(torch.einsum("thd,sd->ths", qi[s0:s1].float(), Kc)) * w[s0:s1].float()[..., None]).sum(1)
-        qpos = torch.arange(sl - ql, sl, device=qi.device)
-        lg = lg.masked_fill(torch.arange(sl, device=qi.device)[None, :] > qpos[:, None], float("-inf"))
-        kk = min(k, sl)
-        # Ties (relu makes exact zeros common) prefer the most recent position: sort the reversed row stably.
-        vals, idx = torch.sort(lg.flip(-1), dim=-1, descending=True, stable=True)
-        vals, idx = vals[:, :kk], sl - 1 - idx[:, :kk]
-        idx = torch.where(torch.isinf(vals), torch.full_like(idx, -1), idx)
-        out[s0:s1, :kk] = idx
+        nblk = (sl + DSA_PAGE_KEYS - 1) // DSA_PAGE_KEYS
+        pages = block_tables[b, :nblk].long()
+        Kc = keys[pages].reshape(-1, DSA_DIM)[:sl].double()
+        KS = ks[pages].reshape(-1)[:sl].double()
+        lg = (torch.relu(torch.einsum("thd,sd->ths", q8[s0:s1].double(), Kc)) * wq[s0:s1].double()[..., None]).sum(1)
+        lg = lg * KS[None]
+        for j in range(ql):
+            out.append(lg[j, : sl - ql + j + 1].float())
+    return out
+
+
+def dsa_topk(qi, w, kcache, block_tables, seq_lens, q_start, k):
+    """Lightning indexer over the fp8 page cache: the k largest causal logits per query token, positions in
+    ascending order, -1 padded ([T, k] int32).  Equal logits prefer the later position."""
+    T = qi.shape[0]
+    out = torch.full((T, k), -1, dtype=torch.int32, device=qi.device)
+    for t, lg in enumerate(dsa_logits(qi, w, kcache, block_tables, seq_lens, q_start)):
+        n = lg.shape[0]
+        if n <= k:
+            out[t, :n] = torch.arange(n, dtype=torch.int32)
+            continue
+        # stable sort of the reversed row: among equal logits the later position comes first
+        idx = torch.sort(lg.flip(-1), descending=True, stable=True).indices[:k]
+        out[t] = torch.sort(n - 1 - idx).values.to(torch.int32)
     return out
