@@ -15,7 +15,9 @@
 // all of those rows.  Each CTA takes an equal contiguous share of the list.
 //   warp 0      TMA producer: the row group's fp8 queries and head weights into
 //               one of two query buffers, the key tiles (two pages each) into a
-//               5-stage ring (L2 evict-first: keys are streamed once);
+//               5-stage ring and their per-key scales into a ring of 8 scale
+//               slots, on the same barrier (L2 evict-first: keys are streamed
+//               once);
 //   warp 1      MMA issuer: D[key, token x head] = K_tile (M = 128 keys) x
 //               Q_group^T (N = tokens x IH <= 256) with tcgen05.mma kind::f8f6f4
 //               (e4m3 x e4m3 -> f32) into one of two TMEM accumulators, so the
@@ -25,9 +27,11 @@
 //               of each token in registers -- no cross-lane reduction -- then
 //               writes the logit with an L2 evict-last hint (the scratch rows,
 //               a few tens of MB at decode sizes, stay in L2 for the select).
-// Selection (dsa_topk_kernel): one CTA per query token, a three-pass radix
-// select (11 / 11 / 10 bits) with warp-aggregated shared-memory histograms,
-// then one ordered compaction.  Equal logits prefer the later position.
+// Selection (dsa_topk_kernel): one CTA per query token; the row is read once
+// from L2 into shared memory, a radix select over 11-bit digits that starts
+// below the bits common to the whole row finds the K-th largest logit, and
+// one ordered compaction writes the positions.  Equal logits prefer the later
+// position.
 //
 // Every wait is bounded (2 s); a timed-out wait records 400 + phase in *err,
 // raises the CTA's abort flag so the other roles leave their loops, and the
@@ -60,13 +64,20 @@ constexpr int kQBoxRows = 128;                // rows per query TMA box
 constexpr int kStages = 5;
 constexpr int kThreads = 320;                 // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int kAccCols = 256;                 // TMEM columns per accumulator (two accumulators)
+// Key scales ride with the key tiles (same full barrier) into a ring of their own.  Slot reuse needs no
+// barrier: the producer loads tile g only after the MMA finished tile g - kStages, whose first item waited
+// for the epilogue to release the item two items earlier (two accumulators, at most two items per tile),
+// so every item of tile g - kStages - 1 had been released; the epilogue reads an item's scales before it
+// releases the item, and kScaleSlots > kStages + 1.
+constexpr int kScaleSlots = 8;
 
 struct Smem {
   static constexpr int RING = 0;
   static constexpr int QBUF = RING + kStages * kTileBytes;
   static constexpr int QBYTES = kQRows * kDim;
   static constexpr int WQ = QBUF + 2 * QBYTES;
-  static constexpr int BAR = WQ + 2 * kQRows * 4;
+  static constexpr int SCALE = WQ + 2 * kQRows * 4;  // [kScaleSlots][128] key scales, one slot per tile
+  static constexpr int BAR = SCALE + kScaleSlots * kTile * 4;
   static constexpr int NBAR = 2 * kStages + 8;
   static constexpr int MISC = BAR + NBAR * 8;
   static constexpr int TOTAL = MISC + 64 + 1024;  // + alignment slack
@@ -222,7 +233,7 @@ __device__ int64_t request_tiles(const DsaIndexParams& p, int b) {
 template <int IH>
 __global__ void __launch_bounds__(kThreads, 1)
     dsa_score_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
-                     DsaIndexParams p) {
+                     const __grid_constant__ CUtensorMap tmS, DsaIndexParams p) {
   static_assert(IH == 16 || IH == 64, "indexer heads");
   constexpr int TPG = kAccCols / IH;  // tokens per MMA group (N <= 256)
   extern __shared__ uint8_t smem_raw[];
@@ -253,6 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmS)) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
@@ -321,12 +333,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* ring = smem + Smem::RING;
   uint8_t* qbuf = smem + Smem::QBUF;
   float* wqbuf = reinterpret_cast<float*>(smem + Smem::WQ);
+  float* sscale = reinterpret_cast<float*>(smem + Smem::SCALE);
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t pol_k = policy_evict_first(), pol_q = policy_evict_last();
       int stage = 0, phase = 0, si = 0;
+      uint32_t g = 0;  // tiles loaded by this CTA (scale slot g % kScaleSlots)
       Seg s;
       bool ok = true;
       while (ok && walk.next(s, p)) {
@@ -350,10 +364,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int pg = 2 * tile;
           const bool two = static_cast<int64_t>(pg + 1) * kPage <= s.last;
-          mbar_expect_tx(&full[stage], (two ? 2 : 1) * kPageKeyBytes);
+          mbar_expect_tx(&full[stage], (two ? 2 : 1) * (kPageKeyBytes + kPage * 4));
           uint8_t* dst = ring + stage * kTileBytes;
+          float* sdst = sscale + (g % kScaleSlots) * kTile;
           tma_load_3d_hint(dst, &tmK, 0, 0, bt[pg], &full[stage], pol_k);
-          if (two) tma_load_3d_hint(dst + kPageKeyBytes, &tmK, 0, 0, bt[pg + 1], &full[stage], pol_k);
+          tma_load_2d_hint(sdst, &tmS, 0, bt[pg], &full[stage], pol_k);
+          if (two) {
+            tma_load_3d_hint(dst + kPageKeyBytes, &tmK, 0, 0, bt[pg + 1], &full[stage], pol_k);
+            tma_load_2d_hint(sdst + kPage, &tmS, 0, bt[pg + 1], &full[stage], pol_k);
+          }
+          ++g;
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1;
@@ -422,39 +442,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t pol_l = policy_evict_last();
     int si = 0;
     uint32_t j = 0;
+    uint32_t gt = 0;  // tiles of this CTA before the current one (scale slot gt % kScaleSlots)
     Seg s;
     bool ok = true;
     while (ok && walk.next(s, p)) {
       const int qb = si & 1;
       const int ng = (s.nt + TPG - 1) / TPG, tpg = (s.nt + ng - 1) / ng;
-      const int32_t* bt = p.block_tables + static_cast<int64_t>(s.b) * p.bt_stride;
       const float* wq = wqbuf + qb * kQRows;
-      // per-key scales, loaded one tile ahead (page id two tiles ahead)
-      auto page_of = [&](int tile) -> int {
-        const int64_t pos = static_cast<int64_t>(tile) * kTile + row;
-        return (tile < s.te && pos <= s.last) ? bt[pos >> 6] : -1;
-      };
-      auto scale_of = [&](int page, int tile) -> float {
-        if (page < 0) return 0.f;
-        return *reinterpret_cast<const float*>(p.kcache + static_cast<int64_t>(page) * kPageBytes + kPageKeyBytes +
-                                               ((static_cast<int64_t>(tile) * kTile + row) & 63) * 4);
-      };
-      float ks_next = scale_of(page_of(s.tb), s.tb);
-      int page_next = page_of(s.tb + 1);
-      for (int tile = s.tb; tile < s.te && ok; ++tile) {
-        const float ks = ks_next;
-        ks_next = scale_of(page_next, tile + 1);
-        page_next = page_of(tile + 2);
+      for (int tile = s.tb; tile < s.te && ok; ++tile, ++gt) {
         const int64_t pos = static_cast<int64_t>(tile) * kTile + row;
         for (int g = 0; g < ng; ++g, ++j) {
           if ((j & 1) != static_cast<uint32_t>(e)) continue;
           const uint32_t use = j >> 1;
-          if (!mbar_wait(&accf[e], use & 1, abort_flag)) {
+          // the warp agrees on the outcome: the TMEM loads below (.sync.aligned) run on all lanes or none
+          if (!__all_sync(0xffffffffu, mbar_wait(&accf[e], use & 1, abort_flag))) {
             raise(406);
             ok = false;
             break;
           }
           fence_after();
+          // this key's scale (pages past the group's last key were not loaded: their keys are never stored)
+          const float ks = sscale[(gt % kScaleSlots) * kTile + row];
           const int ntok = min(tpg, s.nt - g * tpg);
           const uint32_t tb = tmem_base + (static_cast<uint32_t>(qtr * 32) << 16) + e * kAccCols;
           const float* w = wq + g * tpg * IH;
@@ -516,8 +524,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------------------ top-k select
-constexpr int kSelThreads = 512;
+constexpr int kSelThreads = 1024;
 constexpr int kBins = 2048;
+constexpr int kSelMaxStaged = 40960;  // rows of up to this many keys are staged in shared memory (160 KB)
 
 __device__ __forceinline__ uint32_t ordered_bits(float f) {
   const uint32_t u = __float_as_uint(f);
@@ -557,11 +566,20 @@ __device__ __forceinline__ int block_excl_scan(int v, int* warp_sums, int* total
   return before + inc - v;
 }
 
-__global__ void __launch_bounds__(kSelThreads) dsa_topk_kernel(DsaIndexParams p) {
+// One CTA per query row.  Pass 0 reads the logits row once (float4, L2) into shared memory as orderable
+// keys (rows longer than `staged` keys are re-read from global memory instead) and finds the row's
+// smallest and largest key.  The radix select then starts at the highest bit in which those two differ
+// (the bits above it are common to every key), so the first 11-bit digit already spreads the keys over
+// the histogram instead of piling them into a few exponent bins; at most three digit passes follow.  One
+// ordered compaction writes the selected positions.
+__global__ void __launch_bounds__(kSelThreads) dsa_topk_kernel(DsaIndexParams p, int staged) {
   shk::pdl_trigger();
   shk::pdl_wait();
+  extern __shared__ uint4 sel_smem[];
+  uint32_t* skeys = reinterpret_cast<uint32_t*>(sel_smem);
   __shared__ uint32_t hist[kBins];
   __shared__ int warp_sums[kSelThreads / 32];
+  __shared__ uint32_t red[2][kSelThreads / 32];
   __shared__ uint32_t pick[4];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t = blockIdx.x;
@@ -575,37 +593,79 @@ __global__ void __launch_bounds__(kSelThreads) dsa_topk_kernel(DsaIndexParams p)
     return;
   }
   const float* row = p.logits + static_cast<int64_t>(t) * p.ld;
-  // radix select of the K-th largest ordered key, most significant digits first
-  uint32_t prefix = 0, mask = 0, eq_total = 0;
+  const bool in_smem = n <= staged;
+  auto key_at = [&](int i) -> uint32_t { return in_smem ? skeys[i] : ordered_bits(__ldcg(row + i)); };
+
+  uint32_t kmin = 0xffffffffu, kmax = 0u;
+  for (int i0 = 4 * tid; i0 < n; i0 += 4 * kSelThreads) {
+    uint32_t u[4];
+    if (i0 + 3 < n) {
+      const float4 f = __ldcg(reinterpret_cast<const float4*>(row + i0));
+      u[0] = ordered_bits(f.x);
+      u[1] = ordered_bits(f.y);
+      u[2] = ordered_bits(f.z);
+      u[3] = ordered_bits(f.w);
+      if (in_smem) *reinterpret_cast<uint4*>(skeys + i0) = make_uint4(u[0], u[1], u[2], u[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        u[e] = i0 + e < n ? ordered_bits(__ldcg(row + i0 + e)) : 0u;
+        if (in_smem && i0 + e < n) skeys[i0 + e] = u[e];
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (i0 + e < n) {
+        kmin = min(kmin, u[e]);
+        kmax = max(kmax, u[e]);
+      }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+  }
+  if (lane == 0) {
+    red[0][warp] = kmin;
+    red[1][warp] = kmax;
+  }
+  __syncthreads();  // also publishes the staged keys
+  kmin = 0xffffffffu;
+  kmax = 0u;
+#pragma unroll
+  for (int w = 0; w < kSelThreads / 32; ++w) {
+    kmin = min(kmin, red[0][w]);
+    kmax = max(kmax, red[1][w]);
+  }
+  const uint32_t diff = kmin ^ kmax;
+  int hb = diff ? 31 - __clz(diff) : -1;  // highest bit not common to every key
+  uint32_t mask = hb >= 31 ? 0u : ~((2u << hb) - 1u);
+  if (hb < 0) mask = 0xffffffffu;
+  uint32_t prefix = kmax & mask, eq_total = static_cast<uint32_t>(n);
   int remaining = p.K;
-#pragma unroll 1
-  for (int pass = 0; pass < 3; ++pass) {  // digits: bits 31..21, 20..10, 9..0
-    const int shift = pass == 0 ? 21 : pass == 1 ? 10 : 0, nb = pass == 2 ? 1024 : kBins;
+  while (hb >= 0) {  // 11-bit digits from bit hb down
+    const int shift = hb >= 10 ? hb - 10 : 0, nb = 1 << (hb - shift + 1);
     for (int i = tid; i < nb; i += kSelThreads) hist[i] = 0;
     __syncthreads();
-    for (int base = 0; base < n; base += kSelThreads) {
-      const int i = base + tid;
-      const bool valid = i < n;
-      const uint32_t u = valid ? ordered_bits(__ldcg(row + i)) : 0u;
-      const bool m = valid && (u & mask) == prefix;
-      const uint32_t d = (u >> shift) & (nb - 1);
-      const uint32_t key = m ? d : (0x10000u | lane);  // non-matching lanes never share a key
-      const unsigned peers = __match_any_sync(0xffffffffu, key);
-      if (m && lane == __ffs(peers) - 1) atomicAdd(&hist[d], static_cast<uint32_t>(__popc(peers)));
+    for (int i = tid; i < n; i += kSelThreads) {
+      const uint32_t u = key_at(i);
+      if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & (nb - 1)], 1u);
     }
     __syncthreads();
-    if (warp == 0) {  // lane l sums bins [nb - (l + 1) * per, nb - l * per): counts from the top
-      const int per = nb / 32;
+    if (warp == 0) {  // lane l sums bins [nb - (l + 1) * per, nb - l * per) (counts from the top)
+      const int per = nb >= 32 ? nb / 32 : 1;
       const int hi = nb - lane * per;
       uint32_t v = 0;
-      for (int d = hi - 1; d >= hi - per; --d) v += hist[d];
+      if (hi > 0)
+        for (int d = hi - 1; d >= hi - per; --d) v += hist[d];
       uint32_t inc = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const uint32_t u = __shfl_up_sync(0xffffffffu, inc, o);
         if (lane >= o) inc += u;
       }
-      const bool cross = inc >= static_cast<uint32_t>(remaining) && inc - v < static_cast<uint32_t>(remaining);
+      const bool cross = hi > 0 && inc >= static_cast<uint32_t>(remaining) &&
+                         inc - v < static_cast<uint32_t>(remaining);
       if (cross) {
         uint32_t above = inc - v;
         int d = hi - 1;
@@ -623,36 +683,40 @@ __global__ void __launch_bounds__(kSelThreads) dsa_topk_kernel(DsaIndexParams p)
     mask |= static_cast<uint32_t>(nb - 1) << shift;
     remaining = static_cast<int>(pick[1]);
     eq_total = pick[2];
+    hb = shift - 1;
     __syncthreads();
   }
-  // prefix is the K-th largest key: take every key above it and the `remaining` latest keys equal to it.
+  // prefix is the K-th largest key: take every key above it and the `remaining` latest keys equal to it,
+  // in ascending position order (chunks of 8 consecutive keys per thread).
   const int skip = static_cast<int>(eq_total) - remaining;
-  const int per = (n + kSelThreads - 1) / kSelThreads;
-  const int lo = min(n, tid * per), hi = min(n, lo + per);
-  int ngt = 0, neq = 0;
-  for (int i = lo; i < hi; ++i) {
-    const uint32_t u = ordered_bits(__ldcg(row + i));
-    ngt += u > prefix;
-    neq += u == prefix;
-  }
-  int tot;
-  int eq_before = block_excl_scan(neq, warp_sums, &tot);
-  int nsel = ngt;
-  {
-    int e = eq_before;
-    for (int i = lo; i < hi; ++i) {  // selected equal keys of this thread's range
-      const uint32_t u = ordered_bits(__ldcg(row + i));
-      if (u == prefix) nsel += (e++ >= skip);
+  int base_pos = 0, base_eq = 0;
+  for (int c0 = 0; c0 < n; c0 += 8 * kSelThreads) {
+    const int i0 = c0 + 8 * tid;
+    uint32_t gt = 0, eq = 0;  // bit e: key i0 + e above / equal to the threshold
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t u = i0 + e < n ? key_at(i0 + e) : 0u;
+      gt |= static_cast<uint32_t>(i0 + e < n && u > prefix) << e;
+      eq |= static_cast<uint32_t>(i0 + e < n && u == prefix) << e;
     }
+    int tot_eq, tot_sel;
+    const int eq_before = base_eq + block_excl_scan(__popc(eq), warp_sums, &tot_eq);
+    uint32_t sel = gt;
+    int e_cnt = eq_before;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if ((eq >> e) & 1u) sel |= static_cast<uint32_t>(e_cnt++ >= skip) << e;
+    int pos = base_pos + block_excl_scan(__popc(sel), warp_sums, &tot_sel);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if ((sel >> e) & 1u) {
+        if (pos < p.K) out[pos] = i0 + e;
+        ++pos;
+      }
+    base_pos += tot_sel;
+    base_eq += tot_eq;
   }
-  int pos = block_excl_scan(nsel, warp_sums, &tot);
-  for (int i = lo; i < hi; ++i) {
-    const uint32_t u = ordered_bits(__ldcg(row + i));
-    bool sel = u > prefix;
-    if (u == prefix) sel = eq_before++ >= skip;
-    if (sel && pos < p.K) out[pos++] = i;
-  }
-  for (int i = tot + tid; i < p.K; i += kSelThreads) out[i] = -1;
+  for (int i = base_pos + tid; i < p.K; i += kSelThreads) out[i] = -1;
 }
 
 // ------------------------------------------------------------------------------ quantisation
@@ -756,6 +820,17 @@ int launch_score(const DsaIndexParams& p, cudaStream_t st) {
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return 2000 + static_cast<int>(r);
   }
+  CUtensorMap ms;
+  {  // key scales: {64 floats, pages}, starting after each page's key bytes
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(kPage), static_cast<cuuint64_t>(p.num_pages)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kPageBytes)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kPage), 1};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<uint8_t*>(p.kcache + kPageKeyBytes),
+                           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return 3000 + static_cast<int>(r);
+  }
   auto k = dsa_score_kernel<IH>;
   static bool ready[kMaxDevices] = {false};
   int dev = 0;
@@ -765,7 +840,7 @@ int launch_score(const DsaIndexParams& p, cudaStream_t st) {
     if (e != cudaSuccess) return static_cast<int>(e);
     ready[dev] = true;
   }
-  shk::launch(k, dim3(p.grid), dim3(kThreads), Smem::TOTAL, st, mk, mq, p);
+  shk::launch(k, dim3(p.grid), dim3(kThreads), Smem::TOTAL, st, mk, mq, ms, p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -810,6 +885,17 @@ extern "C" int sh_dsa_index(const DsaIndexParams* p, cudaStream_t stream) {
   if (p->K <= 0 || !p->topk) return -1;
   const int r = sh_dsa_score(p, stream);
   if (r) return r;
-  shk::launch(dsa_topk_kernel, dim3(p->T), dim3(kSelThreads), 0, stream, *p);
+  // rows of up to max_keys keys are staged in shared memory (capped at 160 KB)
+  const int staged = static_cast<int>(p->ld < kSelMaxStaged ? p->ld : kSelMaxStaged);
+  static bool ready[kMaxDevices] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+  if (!ready[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(dsa_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSelMaxStaged * 4);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    ready[dev] = true;
+  }
+  shk::launch(dsa_topk_kernel, dim3(p->T), dim3(kSelThreads), static_cast<size_t>(staged) * 4, stream, *p, staged);
   return static_cast<int>(cudaGetLastError());
 }

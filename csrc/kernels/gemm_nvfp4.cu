@@ -302,7 +302,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t acc_phase = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x) {
       const Work wk = decode_work(w, g, BN);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+      // the warp agrees on the outcome: its TMEM loads (.sync.aligned) run on all lanes or none
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) {
         if (g.err && lane == 0) atomicCAS(g.err, 0, 25);
         *abort_flag = 1;
         break;

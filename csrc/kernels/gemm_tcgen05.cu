@@ -247,7 +247,8 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t push_par = g.push ? ((*g.push_epoch + 1u) & 1u) : 0u;
     for (int w = blockIdx.x; w < total_work; w += gridDim.x) {
       const Work wk = decode_work(w, g, BN);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+      // the warp agrees on the outcome: its TMEM loads (.sync.aligned) run on all lanes or none
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) {
         if (g.err && lane == 0) atomicCAS(g.err, 0, 4);
         *abort_flag = 1;
         break;
@@ -556,7 +557,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const uint32_t push_par = PUSH ? ((*g.push_epoch + 1u) & 1u) : 0u;
     for (int w = cid; w < total_work; w += ncl) {
       const Work wk = decode_work(w, g, BN);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+      // the warp agrees on the outcome: its TMEM loads (.sync.aligned) run on all lanes or none
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) {
         if (lane == 0) raise(4);
         break;
       }
