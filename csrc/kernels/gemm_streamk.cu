@@ -21,7 +21,11 @@
 //   final count adds all partials in cluster order -- a fixed order, so the
 //   result does not depend on timing -- and stores the tile), and that sum
 //   runs on the epilogue warps while the MMA warp already works on the whole
-//   tiles.  No CTA waits for another, so there is no co-residency
+//   tiles.  When a cluster's split range ends in a second split piece, a
+//   fix-up owed for the first waits until that piece is parked: the second
+//   piece's MMAs need the (single) accumulator, which only its park frees.
+//   Partials of the next 32-token chunk load while the current chunk is
+//   staged.  No CTA waits for another, so there is no co-residency
 //   requirement.  The counter goes back to zero after each tile, so the
 //   counter array stays zero between calls (after a timed-out wait, *err is
 //   set and the caller must clear the counters before the next call).
@@ -103,8 +107,9 @@ struct Cfg {
 // Phase stamps (SkParams::stamps, [grid][64] u64 ns), for profiling the pipeline without a profiler:
 //   [0] CTA start  [1] producer: first weight loads issued  [2] producer: dependency wait passed
 //   [3] producer: ns waiting for free stages  [4] MMA: ns waiting for loaded stages
-//   [5] MMA: ns waiting for a free accumulator  [6] epilogue: CTA end
+//   [5] MMA: ns waiting for a free accumulator  [6] epilogue: CTA end  [7] epilogue: last fix-up done
 //   [8 + 4i .. 11 + 4i] segment i < 8: MMA start, MMA issue end, epilogue saw the accumulator, TMEM freed
+//   [40] ns in fix-ups  [41] ns of it in the staged output stores  [42] partials summed
 constexpr int kStampSlots = 64;
 __device__ __forceinline__ void stamp(const SkParams& g, int slot, unsigned long long v) {
   if (g.stamps) g.stamps[blockIdx.x * kStampSlots + slot] = v;
@@ -424,7 +429,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     Seg s;
     // One 32-token chunk of this thread's weight row (v[32], fp32) -> bf16 staging tile -> TMA tensor store
     // of [32 tokens][128 weights] (clipped at the tensor's bounds).  Two staging tiles alternate.
+    unsigned long long fix_store_ns = 0, fix_ns = 0, fix_parts = 0;  // stamps of the fix-ups (elected thread)
+    bool in_fix = false;
     auto store_chunk = [&](const float* v, int y_w, int y_t) {
+      const uint64_t ts = (g.stamps && elected && in_fix) ? now_ns() : 0;
       __nv_bfloat16* buf = stg + (chunk % C::NSTG) * (STG_T * ROWS);
       // The store issued from this buffer NSTG chunks ago has read it (at most NSTG - 1 stores still reading).
       if (elected && chunk >= C::NSTG) bulk_wait_read<C::NSTG - 1>();
@@ -438,7 +446,116 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         bulk_commit();
       }
       ++chunk;
+      if (ts) fix_store_ns += now_ns() - ts;
     };
+    // Sums a split tile's parked partials (nparts pieces starting at cluster c_first, cluster order) and
+    // stores the tile.  Run by every epilogue thread together (named barriers inside store_chunk).
+    auto fixup = [&](int j, int c_first, int nparts, int y_w, int y_x0) {
+      const uint64_t tf = (g.stamps && elected) ? now_ns() : 0;
+      in_fix = true;
+      fix_parts += nparts;
+      __threadfence();  // acquire side of the counter: the other pieces' partials are visible
+      if (nparts <= 2) {
+        // One or two pieces: the next chunk's partials load while the current chunk is summed and
+        // staged (two chunks of loads in flight per thread).  Same summation order as below.
+        auto part_of = [&](int pj) {
+          const int cj = c_first + pj;
+          const int fj = static_cast<int>(sk_start(cj, g) / g.kb);
+          return reinterpret_cast<const float4*>(
+              g.ws + ((static_cast<int64_t>(cj) * 2 + rank) * 2 + (j == fj ? 0 : 1)) * slot_elems);
+        };
+        const float4* p0 = part_of(0);
+        const float4* p1 = part_of(nparts - 1);
+        const bool two = nparts == 2;
+        float4 a0[8], a1[8], b0[8], b1[8];
+        auto load = [&](float4* d0, float4* d1, int c) {
+#pragma unroll
+          for (int i4 = 0; i4 < 8; ++i4) d0[i4] = __ldcg(p0 + static_cast<int64_t>(c / 4 + i4) * ROWS + row);
+          if (two)
+#pragma unroll
+            for (int i4 = 0; i4 < 8; ++i4) d1[i4] = __ldcg(p1 + static_cast<int64_t>(c / 4 + i4) * ROWS + row);
+        };
+        auto sum_store = [&](float4* d0, const float4* d1, int c) {
+#pragma unroll
+          for (int i4 = 0; i4 < 8; ++i4) {
+            d0[i4].x = 0.f + d0[i4].x;
+            d0[i4].y = 0.f + d0[i4].y;
+            d0[i4].z = 0.f + d0[i4].z;
+            d0[i4].w = 0.f + d0[i4].w;
+            if (two) {
+              d0[i4].x += d1[i4].x;
+              d0[i4].y += d1[i4].y;
+              d0[i4].z += d1[i4].z;
+              d0[i4].w += d1[i4].w;
+            }
+          }
+          store_chunk(reinterpret_cast<const float*>(d0), y_w, y_x0 + c);
+        };
+        load(a0, a1, 0);
+#pragma unroll 1
+        for (int c = 0; c < C::NT; c += 2 * STG_T) {
+          load(b0, b1, c + STG_T);
+          sum_store(a0, a1, c);
+          if (c + 2 * STG_T < C::NT) load(a0, a1, c + 2 * STG_T);
+          sum_store(b0, b1, c + STG_T);
+        }
+      } else {
+      const float4* parts[kMaxParts];
+      for (int pj = 0; pj < nparts; ++pj) {
+        const int cj = c_first + pj;
+        const int fj = static_cast<int>(sk_start(cj, g) / g.kb);
+        parts[pj] = reinterpret_cast<const float4*>(
+            g.ws + ((static_cast<int64_t>(cj) * 2 + rank) * 2 + (j == fj ? 0 : 1)) * slot_elems);
+      }
+#pragma unroll 1
+      for (int c = 0; c < C::NT; c += STG_T) {
+        // Sum the pieces in cluster order; three pieces' loads in flight at a time.
+        float4 sum[8];
+#pragma unroll
+        for (int i4 = 0; i4 < 8; ++i4) sum[i4] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int pj = 0; pj < nparts; pj += 3) {
+          float4 ld[3][8];
+#pragma unroll
+          for (int u = 0; u < 3; ++u)
+#pragma unroll
+            for (int i4 = 0; i4 < 8; ++i4)
+              if (pj + u < nparts) ld[u][i4] = __ldcg(parts[pj + u] + static_cast<int64_t>(c / 4 + i4) * ROWS + row);
+#pragma unroll
+          for (int u = 0; u < 3; ++u)
+            if (pj + u < nparts)
+#pragma unroll
+              for (int i4 = 0; i4 < 8; ++i4) {
+                sum[i4].x += ld[u][i4].x;
+                sum[i4].y += ld[u][i4].y;
+                sum[i4].z += ld[u][i4].z;
+                sum[i4].w += ld[u][i4].w;
+              }
+        }
+        float v[STG_T];
+#pragma unroll
+        for (int i4 = 0; i4 < 8; ++i4) {
+          v[4 * i4] = sum[i4].x;
+          v[4 * i4 + 1] = sum[i4].y;
+          v[4 * i4 + 2] = sum[i4].z;
+          v[4 * i4 + 3] = sum[i4].w;
+        }
+        store_chunk(v, y_w, y_x0 + c);
+      }
+      }
+      if (g.stamps && elected) {
+        stamp(g, 7, now_ns());
+        fix_ns += now_ns() - tf;
+        stamp(g, 40, fix_ns);
+        stamp(g, 41, fix_store_ns);
+        stamp(g, 42, fix_parts);
+      }
+      in_fix = false;
+    };
+    struct Fix {
+      int j, c_first, nparts, y_w, y_x0;
+    };
+    Fix pend[2];
+    int npend = 0;
     while (it.next(s, g)) {
       const int tw = s.tile / g.tiles_x, tx = s.tile % g.tiles_x;
       const int y_w = tw * (2 * ROWS) + static_cast<int>(rank) * ROWS;  // output column of weight row 0
@@ -479,14 +596,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         const int j = s.tile - g.q * g.clusters;  // split tile index
         float4* mine = reinterpret_cast<float4*>(
             g.ws + ((static_cast<int64_t>(cid) * 2 + rank) * 2 + (j == first_split ? 0 : 1)) * slot_elems);
-#pragma unroll 1
-        for (int c = 0; c < C::NT; c += 32) {
-          float v[32];
-          tmem_ld32(tacc + (c / NS) * C::SUB_COLS + (c % NS), v);
+        {  // TMEM reads one chunk ahead of the stores (NT is a multiple of 64)
+          auto tcol = [&](int c) { return tacc + (c / NS) * C::SUB_COLS + (c % NS); };
+          auto park = [&](const float* v, int c) {
 #pragma unroll
-          for (int i4 = 0; i4 < 8; ++i4)
-            __stcg(mine + static_cast<int64_t>(c / 4 + i4) * ROWS + row,
-                   make_float4(v[4 * i4], v[4 * i4 + 1], v[4 * i4 + 2], v[4 * i4 + 3]));
+            for (int i4 = 0; i4 < 8; ++i4)
+              __stcg(mine + static_cast<int64_t>(c / 4 + i4) * ROWS + row,
+                     make_float4(v[4 * i4], v[4 * i4 + 1], v[4 * i4 + 2], v[4 * i4 + 3]));
+          };
+          float va[32], vb[32];
+          tmem_ld32(tcol(0), va);
+#pragma unroll 1
+          for (int c = 0; c < C::NT; c += 64) {
+            tmem_ld32_nowait(tcol(c + 32), vb);
+            park(va, c);
+            tmem_wait_ld32(vb);
+            if (c + 64 < C::NT) tmem_ld32_nowait(tcol(c + 64), va);
+            park(vb, c + 32);
+            tmem_wait_ld32(va);
+          }
         }
         fence_before();
         __syncwarp();
@@ -509,49 +637,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           if (elected) raise(5);
           nparts = 0;
         }
-        if (nparts > 0) {
-          __threadfence();  // acquire side of the counter: the other pieces' partials are visible
-          const float4* parts[kMaxParts];
-          for (int pj = 0; pj < nparts; ++pj) {
-            const int cj = c_first + pj;
-            const int fj = static_cast<int>(sk_start(cj, g) / g.kb);
-            parts[pj] = reinterpret_cast<const float4*>(
-                g.ws + ((static_cast<int64_t>(cj) * 2 + rank) * 2 + (j == fj ? 0 : 1)) * slot_elems);
-          }
-#pragma unroll 1
-          for (int c = 0; c < C::NT; c += STG_T) {
-            // Sum the pieces in cluster order; three pieces' loads in flight at a time.
-            float4 sum[8];
-#pragma unroll
-            for (int i4 = 0; i4 < 8; ++i4) sum[i4] = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int pj = 0; pj < nparts; pj += 3) {
-              float4 ld[3][8];
-#pragma unroll
-              for (int u = 0; u < 3; ++u)
-#pragma unroll
-                for (int i4 = 0; i4 < 8; ++i4)
-                  if (pj + u < nparts) ld[u][i4] = __ldcg(parts[pj + u] + static_cast<int64_t>(c / 4 + i4) * ROWS + row);
-#pragma unroll
-              for (int u = 0; u < 3; ++u)
-                if (pj + u < nparts)
-#pragma unroll
-                  for (int i4 = 0; i4 < 8; ++i4) {
-                    sum[i4].x += ld[u][i4].x;
-                    sum[i4].y += ld[u][i4].y;
-                    sum[i4].z += ld[u][i4].z;
-                    sum[i4].w += ld[u][i4].w;
-                  }
-            }
-            float v[STG_T];
-#pragma unroll
-            for (int i4 = 0; i4 < 8; ++i4) {
-              v[4 * i4] = sum[i4].x;
-              v[4 * i4 + 1] = sum[i4].y;
-              v[4 * i4 + 2] = sum[i4].z;
-              v[4 * i4 + 3] = sum[i4].w;
-            }
-            store_chunk(v, y_w, y_x0 + c);
-          }
+        if (nparts > 0) pend[npend++] = Fix{j, c_first, nparts, y_w, y_x0};
+        // A last piece's fix-up waits while the next segment is another split piece: that piece's MMAs
+        // need the accumulator, which only its own park frees, so the MMA would idle for the whole
+        // fix-up.  Pending fix-ups run once the next segment is a whole tile (its MMAs overlap them)
+        // or there is none.
+        SegIter peek = it;
+        Seg nxt;
+        const bool more_split = peek.next(nxt, g) && nxt.split;
+        if (!more_split || npend == 2) {
+          for (int f = 0; f < npend; ++f) fixup(pend[f].j, pend[f].c_first, pend[f].nparts, pend[f].y_w, pend[f].y_x0);
+          npend = 0;
         }
       }
       if (s.whole) {

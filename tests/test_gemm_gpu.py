@@ -97,6 +97,7 @@ def _sk_buffers(M, N, ns, nsub, clusters):
     (300, 520, 1536, 74),    # ragged token and weight edges, pieces of partial tiles
     (37, 1000, 512, 3),      # few clusters: several whole tiles per cluster
     (200, 2056, 1024, 9),    # weight rows not a multiple of the 256-row tile
+    (384, 28672, 1024, 74),  # 1.5 waves: split ranges span two tiles, a fix-up waits behind the next piece
 ])
 def test_gemm_streamk(ns, nsub, M, N, K, clusters):
     """Stream-K CTA-pair kernel against fp32; output outside the problem untouched, counters left zero."""

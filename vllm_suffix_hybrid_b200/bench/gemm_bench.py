@@ -189,6 +189,21 @@ def stamps_main(a):
             "segments_cta0": [[round(rel(t[0, 8 + 4 * j + q]), 2) if t[0, 8 + 4 * j + q] > 0 else None for q in range(4)]
                               for j in range(8) if t[0, 8 + 4 * j] > 0],
         }
+        # the three CTAs that end last, with their segment timelines
+        slow = sorted((i for i in range(t.shape[0]) if t[i, 6] > 0), key=lambda i: -int(t[i, 6]))[:3]
+        summary["slowest"] = [{"cta": i, "end": round(rel(t[i, 6]), 2), "start": round(rel(t[i, 0]), 2),
+                               "segments": [[round(rel(t[i, 8 + 4 * j + q]), 2) if t[i, 8 + 4 * j + q] > 0 else None
+                                             for q in range(4)] for j in range(8) if (t[i, 8 + 4 * j:12 + 4 * j] > 0).any()],
+                               "fixup_end": round(rel(t[i, 7]), 2) if t[i, 7] > 0 else None,
+                               "fixup_us": round(int(t[i, 40]) / 1e3, 2), "fixup_store_us": round(int(t[i, 41]) / 1e3, 2),
+                               "fixup_parts": int(t[i, 42])}
+                              for i in slow]
+        fx = [i for i in range(t.shape[0]) if t[i, 42] > 0]
+        if fx:
+            summary["fixups"] = {"ctas": len(fx), "parts_median": statistics.median(int(t[i, 42]) for i in fx),
+                                 "us_median": round(statistics.median(int(t[i, 40]) for i in fx) / 1e3, 2),
+                                 "us_max": round(max(int(t[i, 40]) for i in fx) / 1e3, 2),
+                                 "store_us_median": round(statistics.median(int(t[i, 41]) for i in fx) / 1e3, 2)}
         print(json.dumps(summary), flush=True)
 
 
