@@ -317,7 +317,7 @@ void rs_norm_ag(int64_t recv, std::vector<int64_t> peer_gather, std::vector<int6
 void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor latent, torch::Tensor block_tables,
                 torch::Tensor seq_lens, torch::Tensor q_start, c10::optional<torch::Tensor> topk, int64_t nsplit,
                 c10::optional<torch::Tensor> part_o, c10::optional<torch::Tensor> part_ml, double scale,
-                torch::Tensor err) {
+                torch::Tensor err, int64_t impl, c10::optional<torch::Tensor> stamps) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.is_contiguous(), "mla: q [T,H,C]");
   const bool fp4 = latent.scalar_type() == at::kByte;
   TORCH_CHECK((fp4 || latent.scalar_type() == at::kBFloat16) && latent.dim() == 3 && latent.size(1) == 64 &&
@@ -355,6 +355,11 @@ void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor latent, torch:
   p.T = static_cast<int>(q.size(0));
   p.H = static_cast<int>(q.size(1));
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  p.impl = static_cast<int>(impl);
+  if (stamps) {
+    TORCH_CHECK(stamps->scalar_type() == at::kLong && stamps->is_cuda(), "mla: stamps int64");
+    p.stamps = reinterpret_cast<unsigned long long*>(stamps->data_ptr<int64_t>());
+  }
   const int r = sh_mla_decode(&p, C, V, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_mla_decode failed with code ", r, " (C=", C, ", V=", V, ")");
 }

@@ -416,11 +416,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_after();
             const int n = min(tpg, s.nt - g * tpg) * IH;
             const uint32_t idesc = idesc_e4m3(kTile, n);
-            const uint32_t baddr = qaddr + g * tpg * IH * kDim;
+            // descriptors built once and advanced by (32 bytes / 16) per k-step
+            const uint64_t adesc = sw128_desc(kaddr), bdesc = sw128_desc(qaddr + g * tpg * IH * kDim);
 #pragma unroll
             for (int k = 0; k < kDim / 32; ++k)
-              mma_e4m3(tmem_base + buf * kAccCols, sw128_desc(kaddr + k * 32), sw128_desc(baddr + k * 32), idesc,
-                       k > 0 ? 1u : 0u);
+              mma_e4m3(tmem_base + buf * kAccCols, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k),
+                       idesc, k > 0 ? 1u : 0u);
             mma_commit(&accf[buf]);
           }
           if (!ok) break;

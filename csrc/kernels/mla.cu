@@ -474,8 +474,13 @@ int launch_mla(const MlaParams& p, cudaStream_t st) {
     if (e != cudaSuccess) return static_cast<int>(e);
     ready = true;
   }
-  shk::launch(k, dim3(p.T, (p.H + ROWS - 1) / ROWS, p.nsplit), dim3(THREADS), S::TOTAL, st, p);
-  int r = static_cast<int>(cudaGetLastError());
+  int r = -2;
+  if constexpr (C == 576 && V == 512 && !FP4)
+    if (p.impl != 1) r = sh_mla_decode_tc(&p, st);  // -2: the tcgen05 kernel does not apply
+  if (r == -2) {
+    shk::launch(k, dim3(p.T, (p.H + ROWS - 1) / ROWS, p.nsplit), dim3(THREADS), S::TOTAL, st, p);
+    r = static_cast<int>(cudaGetLastError());
+  }
   if (r || p.nsplit == 1) return r;
   const int64_t rows = static_cast<int64_t>(p.T) * p.H;
   const int64_t n = rows * (V / 2);

@@ -21,6 +21,8 @@ struct MlaParams {
   int* err;
   int T, H, nsplit;
   float scale_log2;             // softmax scale * log2(e)
+  int impl;                     // 0: tcgen05 kernel where it applies, 1: the mma.sync kernel only
+  unsigned long long* stamps;   // optional per-CTA cycle counters of the tcgen05 kernel ([grid][8]; profiling)
 };
 
 
@@ -28,7 +30,10 @@ struct MlaParams {
 extern "C" {
 #endif
 // C % 64 == 0 and V % 64 == 0 (V <= C); supported (C, V): (576, 512), (128, 64).
+// Uses the tcgen05 kernel (mla_tc.cu) for C = 576, V = 512, H % 128 == 0 and a bf16 cache unless impl == 1.
 int sh_mla_decode(const MlaParams* p, int C, int V, cudaStream_t stream);
+// The tcgen05 kernel alone (no split merge): -2 when it does not apply to p.
+int sh_mla_decode_tc(const MlaParams* p, cudaStream_t stream);
 // NVFP4 latent cache row (Cl latent + R rope values): Cl/2 bytes of e2m1 pairs (low nibble first), Cl/16
 // e4m3 block scales at byte Cl/2, the R rope values in bf16 at the next 16-byte boundary; rows padded
 // to 16 bytes (Cl 512, R 64: 416 bytes against 1152 in bf16).  Block scale s = e4m3(amax16 / 6),

@@ -36,6 +36,7 @@ def main():
     ap.add_argument("--nsplit", type=int, default=0)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--once", action="store_true", help="two eager launches, no timing (for ncu)")
+    ap.add_argument("--stamps", action="store_true", help="per-CTA cycle counters of the tcgen05 kernel")
     a = ap.parse_args()
     from vllm_suffix_hybrid_b200 import ops
     from vllm_suffix_hybrid_b200.bench.gemm_bench import time_fn
@@ -62,6 +63,19 @@ def main():
         latent = packed
     nsplit = a.nsplit or ops.mla_splits(T, a.heads, K)
     run = lambda: ops.mla_decode(q, latent, bt, seq, qs, 1.0 / math.sqrt(192), V, topk, nsplit)
+    if a.stamps:
+        ctas = T * (a.heads // 128) * 2 * nsplit
+        st = torch.zeros(ctas * 8, dtype=torch.long, device="cuda")
+        for _ in range(2):
+            st.zero_()
+            ops.mla_decode(q, latent, bt, seq, qs, 1.0 / math.sqrt(192), V, topk, nsplit, stamps=st)
+        torch.cuda.synchronize()
+        st = st.view(ctas, 8).double().cpu()
+        names = ["prod_wait_free", "prod_issue", "mma_wait_keys", "mma_wait_p", "softmax_wait_s", "rescales",
+                 "cta_cycles", "tiles"]
+        print(json.dumps({"stamps_median": {n: float(st[:, i].median()) for i, n in enumerate(names)},
+                          "stamps_max": {n: float(st[:, i].max()) for i, n in enumerate(names)}}))
+        return
     if a.once:
         run()
         run()

@@ -508,7 +508,7 @@ def mla_fp4_row_bytes(kv_lora: int, rope: int) -> int:
 
 
 def mla_decode(q: torch.Tensor, latent: torch.Tensor, block_tables, seq_lens, q_start, scale: float, kv_lora: int,
-               topk: torch.Tensor | None = None, nsplit: int = 1) -> torch.Tensor:
+               topk: torch.Tensor | None = None, nsplit: int = 1, stamps: torch.Tensor | None = None) -> torch.Tensor:
     """Absorbed MLA over the latent cache: q [T, H, C] -> o_lat [T, H, kv_lora] (bf16 on CUDA)."""
     if not q.is_cuda:
         return ref.mla_attention(q[..., :kv_lora], q[..., kv_lora:], latent, block_tables, seq_lens, q_start, scale,
@@ -530,7 +530,7 @@ def mla_decode(q: torch.Tensor, latent: torch.Tensor, block_tables, seq_lens, q_
     err = torch.zeros(1, dtype=torch.int32, device=q.device)
     native().mla_decode(out, q.contiguous(), latent, block_tables, seq_lens, q_start,
                         None if topk is None else topk.to(torch.int32).contiguous(), nsplit, part_o, part_ml, scale,
-                        err)
+                        err, 1 if os.environ.get("SH_MLA_TC", "1") == "0" else 0, stamps)
     return out
 
 
