@@ -191,7 +191,7 @@ void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std:
                      c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, torch::Tensor err,
                      int64_t rank, int64_t T, int64_t H, int64_t max_T, double eps, bool two_shot,
                      int64_t num_blocks, c10::optional<torch::Tensor> timing, int64_t prefetch_ptr,
-                     int64_t prefetch_bytes) {
+                     int64_t prefetch_bytes, int64_t quant) {
   const int world = static_cast<int>(peer_recv.size());
   TORCH_CHECK(world >= 1 && world <= SH_COMM_MAX_WORLD && peer_gather.size() == peer_recv.size() &&
                   peer_flags.size() == peer_recv.size(), "allreduce_fused: peer lists");
@@ -231,6 +231,7 @@ void allreduce_fused(torch::Tensor partial, std::vector<int64_t> peer_recv, std:
   p.prefetch = reinterpret_cast<const void*>(prefetch_ptr);
   p.prefetch_bytes = static_cast<unsigned long long>(prefetch_bytes > 0 ? prefetch_bytes : 0);
   p.wait_ns = g_wait_ns;
+  p.quant = static_cast<int>(quant);
   const int r = sh_allreduce(&p, static_cast<int>(num_blocks), at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_allreduce failed with code ", r);
 }
@@ -994,7 +995,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("peer_flags"), py::arg("counters"), py::arg("out"), py::arg("residual"), py::arg("weight"),
         py::arg("err"), py::arg("rank"), py::arg("T"), py::arg("H"), py::arg("max_T"), py::arg("eps"),
         py::arg("two_shot"), py::arg("num_blocks"), py::arg("timing") = py::none(), py::arg("prefetch_ptr") = 0,
-        py::arg("prefetch_bytes") = 0);
+        py::arg("prefetch_bytes") = 0, py::arg("quant") = 0);
   m.def("gemm_bf16_push", &gemm_bf16_push);
   m.def("set_wait_ns", &set_wait_ns, "limit of every cross-rank wait of the comm / EP kernels (ns, 0 = 5 s)");
   m.def("get_wait_ns", &get_wait_ns);

@@ -26,8 +26,11 @@
 // while it waits.  Each wait gives up after a time limit, records an error
 // code in *err and skips the remaining data phases (no trap, no hang).
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <type_traits>
 
 #include "comm.h"
 #include "pdl.cuh"
@@ -239,7 +242,99 @@ __device__ __forceinline__ void push_row(const uint4* src, uint4* const* dst, in
     }
 }
 
+// ---- compressed rows (ArParams::quant): [H codes | H / 128 fp32 scales] in a bf16 row slot ----------
+// A block of 128 elements is 16 consecutive 8-element vectors, i.e. one half-warp of a row group (thread t
+// of a group owns vectors t + k * 128), so a block's amax is a 4-step shuffle reduction.
+constexpr int kQBlock = 128;
+
+__device__ __forceinline__ float half_warp_max(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// 8 values -> 8 codes (int8: round(x / s) in [-127, 127]; fp8: e4m3(x / s)) with s = amax / qmax.
+__device__ __forceinline__ uint2 encode8(const float* x, float amax, int quant, float* scale) {
+  const float qmax = quant == 1 ? 127.f : 448.f;
+  *scale = amax / qmax;
+  const float inv = amax > 0.f ? qmax / amax : 0.f;
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    uint32_t c;
+    if (quant == 1) {
+      const float q = fminf(fmaxf(rintf(x[i] * inv), -127.f), 127.f);
+      c = static_cast<uint32_t>(static_cast<int32_t>(q)) & 0xFFu;
+    } else {
+      __nv_fp8_e4m3 f(fminf(fmaxf(x[i] * inv, -448.f), 448.f));
+      c = f.__x;
+    }
+    w[i >> 2] |= c << (8 * (i & 3));
+  }
+  return make_uint2(w[0], w[1]);
+}
+__device__ __forceinline__ void decode8_add(float* acc, uint2 code, float scale, int quant) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t c = ((i < 4 ? code.x : code.y) >> (8 * (i & 3))) & 0xFFu;
+    float v;
+    if (quant == 1) {
+      v = static_cast<float>(static_cast<int8_t>(c));
+    } else {
+      __nv_fp8_e4m3 f;
+      f.__x = static_cast<__nv_fp8_storage_t>(c);
+      v = static_cast<float>(f);
+    }
+    acc[i] += v * scale;
+  }
+}
+// Encode this thread's vectors of one row (fp32 values in x) and store codes + block scales into every dst.
 template <int VPT>
+__device__ __forceinline__ void push_row_q(float (*x)[8], char* const* dst, int ndst, int nv, int quant) {
+  const int lt = threadIdx.x % kGroupThreads;
+  const bool lead = (threadIdx.x & 15) == 0;
+  uint2 code[VPT];
+  float scale[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(x[k][i]));
+    code[k] = encode8(x[k], half_warp_max(am), quant, &scale[k]);
+  }
+  const size_t H = static_cast<size_t>(nv) * 8;
+  for (int d = 0; d < ndst; ++d)
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int v = lt + k * kGroupThreads;
+      if (v >= nv) continue;
+      reinterpret_cast<uint2*>(dst[d])[v] = code[k];
+      if (lead) reinterpret_cast<float*>(dst[d] + H)[v >> 4] = scale[k];
+    }
+}
+// acc += the dequantised row (all loads issued before any use).
+template <int VPT>
+__device__ __forceinline__ void add_row_q(float (*acc)[8], const char* src, int nv, int quant) {
+  const int lt = threadIdx.x % kGroupThreads;
+  const size_t H = static_cast<size_t>(nv) * 8;
+  uint2 code[VPT];
+  float scale[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int v = lt + k * kGroupThreads;
+    code[k] = v < nv ? reinterpret_cast<const uint2*>(src)[v] : make_uint2(0u, 0u);
+    scale[k] = v < nv ? reinterpret_cast<const float*>(src + H)[v >> 4] : 0.f;
+  }
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) decode8_add(acc[k], code[k], scale[k], quant);
+}
+// This thread's vectors of a bf16 row as fp32 (zero past the row end).
+template <int VPT>
+__device__ __forceinline__ void load_row_f32(float (*x)[8], const uint4* src, int nv) {
+  zero_acc<VPT>(x);
+  add_row<VPT>(x, src, nv);
+}
+
+template <int VPT, bool QUANT>
 __global__ void __launch_bounds__(512) allreduce_kernel(ArParams p) {
   shk::pdl_trigger();
   l2_prefetch_slice(p.prefetch, p.prefetch_bytes);
@@ -272,6 +367,69 @@ __global__ void __launch_bounds__(512) allreduce_kernel(ArParams p) {
   };
   const uint4* partial = reinterpret_cast<const uint4*>(p.partial);
   uint4* dsts[SH_COMM_MAX_WORLD];
+
+  if constexpr (QUANT) {
+    // Compressed rows.  Every contribution is encoded once and written to its readers' slots, its own
+    // rank's included, so all ranks decode the same bytes.
+    auto qrecv = [&](int dst, int src, int64_t r) { return reinterpret_cast<char*>(recv_row(dst, src, r)); };
+    auto qgather = [&](int dst, int64_t r) { return reinterpret_cast<char*>(gather_row(dst, r)); };
+    char* qd[SH_COMM_MAX_WORLD];
+    if (!p.two_shot) {
+      for (int64_t r = slot0; r < p.T; r += slots) {
+        float x[VPT][8];
+        load_row_f32<VPT>(x, partial + r * (H / 8), nv);
+        for (int d = 0; d < W; ++d) qd[d] = qrecv(d, p.rank, r);
+        push_row_q<VPT>(x, qd, W, nv, p.quant);
+      }
+      if (stamp) stamp[1] = now_ns();
+      if (!barrier(p, 0, epoch, &bail)) return;
+      if (stamp) stamp[2] = now_ns();
+      for (int64_t r = slot0; r < p.T; r += slots) {
+        float acc[VPT][8];
+        zero_acc<VPT>(acc);
+        for (int src = 0; src < W; ++src) add_row_q<VPT>(acc, qrecv(p.rank, src, r), nv, p.quant);
+        finish_row<VPT>(p, r, acc, red);
+      }
+      if (stamp) stamp[3] = now_ns();
+      return;
+    }
+    const int Tc = (p.T + W - 1) / W;
+    for (int i = 0; i < W; ++i) {  // chunk rows to their owners (this rank's own chunk included)
+      const int o = (p.rank + i) % W;
+      const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(o + 1) * Tc);
+      for (int64_t r = static_cast<int64_t>(o) * Tc + slot0; r < r1; r += slots) {
+        float x[VPT][8];
+        load_row_f32<VPT>(x, partial + r * (H / 8), nv);
+        qd[0] = qrecv(o, p.rank, r);
+        push_row_q<VPT>(x, qd, 1, nv, p.quant);
+      }
+    }
+    if (stamp) stamp[1] = now_ns();
+    if (!barrier(p, 0, epoch, &bail)) return;
+    if (stamp) stamp[2] = now_ns();
+    {  // owner: decode and sum in rank order, requantise the sum into every rank's gather slot
+      const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(p.rank + 1) * Tc);
+      for (int64_t r = static_cast<int64_t>(p.rank) * Tc + slot0; r < r1; r += slots) {
+        float acc[VPT][8];
+        zero_acc<VPT>(acc);
+        for (int src = 0; src < W; ++src) add_row_q<VPT>(acc, qrecv(p.rank, src, r), nv, p.quant);
+        for (int d = 0; d < W; ++d) qd[d] = qgather(d, r);
+        push_row_q<VPT>(acc, qd, W, nv, p.quant);
+      }
+    }
+    if (!barrier(p, 1, epoch, &bail)) return;
+    for (int o = 0; o < W; ++o) {
+      const int64_t r1 = min(static_cast<int64_t>(p.T), static_cast<int64_t>(o + 1) * Tc);
+      for (int64_t r = static_cast<int64_t>(o) * Tc + slot0; r < r1; r += slots) {
+        float acc[VPT][8];
+        zero_acc<VPT>(acc);
+        add_row_q<VPT>(acc, qgather(p.rank, r), nv, p.quant);
+        finish_row<VPT>(p, r, acc, red);
+      }
+    }
+    if (stamp) stamp[3] = now_ns();
+    return;
+  }
 
   if (!p.two_shot) {
     for (int64_t r = slot0; r < p.T; r += slots) {
@@ -600,20 +758,28 @@ extern "C" int sh_allreduce(const ArParams* params, int num_blocks, cudaStream_t
   const ArParams& p = *params;
   if (p.world < 1 || p.world > SH_COMM_MAX_WORLD || p.H % 8 != 0 || p.T < 0 || p.T > p.max_T) return -1;
   if (p.fuse_norm && (p.residual == nullptr || p.weight == nullptr)) return -2;
+  if (p.quant < 0 || p.quant > 2 || (p.quant && p.H % kQBlock != 0)) return -4;
   if (p.T == 0) return 0;
   if (num_blocks < 1) num_blocks = 1;
   if (num_blocks > SH_COMM_MAX_BLOCKS) num_blocks = SH_COMM_MAX_BLOCKS;
   const int nv = p.H / 8;
   const int vpt = (nv + kGroupThreads - 1) / kGroupThreads;
   const int threads = 4 * kGroupThreads;  // four rows per block
+  auto run = [&](auto vpt_c) {
+    constexpr int V = decltype(vpt_c)::value;
+    if (p.quant)
+      shk::launch(allreduce_kernel<V, true>, dim3(num_blocks), dim3(threads), 0, stream, p);
+    else
+      shk::launch(allreduce_kernel<V, false>, dim3(num_blocks), dim3(threads), 0, stream, p);
+  };
   if (vpt == 1)
-    shk::launch(allreduce_kernel<1>, dim3(num_blocks), dim3(threads), 0, stream, p);
+    run(std::integral_constant<int, 1>{});
   else if (vpt == 2)
-    shk::launch(allreduce_kernel<2>, dim3(num_blocks), dim3(threads), 0, stream, p);
+    run(std::integral_constant<int, 2>{});
   else if (vpt <= 4)
-    shk::launch(allreduce_kernel<4>, dim3(num_blocks), dim3(threads), 0, stream, p);
+    run(std::integral_constant<int, 4>{});
   else if (vpt <= 8)
-    shk::launch(allreduce_kernel<8>, dim3(num_blocks), dim3(threads), 0, stream, p);
+    run(std::integral_constant<int, 8>{});
   else
     return -3;  // H > 8192
   return static_cast<int>(cudaGetLastError());

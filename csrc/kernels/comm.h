@@ -33,6 +33,11 @@ struct ArParams {
   // Limit of each cross-rank wait in ns (0: the default, 5 s).  On expiry the
   // kernel records 100 + phase in *err and returns.
   unsigned long long wait_ns;
+  // Compressed transfer (H % 128 == 0): 0 = bf16 rows; 1 = int8, 2 = fp8 e4m3 codes with one fp32 scale
+  // per 128 elements (amax / 127 or amax / 448), a row packed as [H codes | H / 128 scales] in its bf16
+  // slot.  Every rank sums the same dequantised bytes in rank order, so the results stay bit-identical;
+  // the two-shot form requantises the owner's sum for the gather (two roundings, like the reference).
+  int quant;
 };
 
 // Reduce-scatter tail of a row-parallel GEMM whose epilogue pushed its output

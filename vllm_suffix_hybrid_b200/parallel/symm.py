@@ -31,6 +31,41 @@ PHASES = 3
 MAX_WORLD = 8
 
 
+def qar_mode(name: str) -> int:
+    """Compressed all-reduce mode of the kernel: 0 off, 1 int8, 2 fp8 e4m3."""
+    name = (name or "").strip().lower()
+    if name in ("", "0", "off", "none"):
+        return 0
+    if name not in ("int8", "fp8"):
+        raise ValueError(f"SUFFIX_NCCL_QAR must be int8 or fp8, got {name!r}")
+    return 1 if name == "int8" else 2
+
+
+def qar_reference(parts, mode: int, two_shot: bool = False, world_chunks: int = 1) -> torch.Tensor:
+    """CPU statement of the compressed all-reduce for a list of per-rank fp32 partials [T, H]: every
+    partial is encoded per 128-value block (scale = amax / 127 for int8 or amax / 448 for fp8 e4m3, codes
+    round(x / scale) clamped to [-127, 127] or e4m3(x / scale)) and decoded, the decoded rows are summed
+    in rank order, and with ``two_shot`` the sum is encoded and decoded once more (the owner's gather)."""
+
+    def roundtrip(x: torch.Tensor) -> torch.Tensor:
+        T, H = x.shape
+        blk = x.float().view(T, H // 128, 128)
+        amax = blk.abs().amax(-1, keepdim=True)
+        qmax = 127.0 if mode == 1 else 448.0
+        scale = amax / qmax
+        inv = torch.where(amax > 0, qmax / amax, torch.zeros_like(amax))
+        if mode == 1:
+            codes = torch.clamp(torch.round(blk * inv), -127, 127)
+        else:
+            codes = torch.clamp(blk * inv, -448, 448).to(torch.float8_e4m3fn).float()
+        return (codes * scale).view(T, H)
+
+    acc = torch.zeros_like(parts[0], dtype=torch.float32)
+    for x in parts:
+        acc = acc + roundtrip(x)
+    return roundtrip(acc) if two_shot else acc
+
+
 class SymmComm:
     def __init__(self, hidden: int, max_tokens: int, dtype=torch.bfloat16, group=None,
                  one_shot_max_bytes: Optional[int] = None):
@@ -87,6 +122,13 @@ class SymmComm:
         self.one_shot_max_bytes = int(env) if env else (one_shot_max_bytes or (4 << 20))
         # L2 prefetch of the next GEMM's weights from the collective kernels (SH_L2_PREFETCH_MAX_BYTES=0: off)
         self.l2_prefetch_max_bytes = int(os.environ.get("SH_L2_PREFETCH_MAX_BYTES", str(24 << 20)))
+        # Compressed all-reduce (off by default; lossy): SUFFIX_NCCL_QAR=int8|fp8 sends every partial as
+        # 1-byte codes + one fp32 scale per 128 values for bf16 messages of SUFFIX_NCCL_QAR_MIN_BYTES
+        # (4 MiB) up to SUFFIX_NCCL_QAR_MAX_BYTES (no limit) -- the reference's knobs and band (reference:
+        # suffix_hybrid/nccl_split.py:37-39, suffix_hybrid/nccl_qar.py:1-25).
+        self.qar_mode = qar_mode(os.environ.get("SUFFIX_NCCL_QAR", ""))
+        self.qar_min_bytes = int(os.environ.get("SUFFIX_NCCL_QAR_MIN_BYTES", str(4 << 20)))
+        self.qar_max_bytes = int(os.environ.get("SUFFIX_NCCL_QAR_MAX_BYTES", str(1 << 62)))
         dist.barrier(group=self.group)
 
     # -- buffers --------------------------------------------------------------
@@ -120,9 +162,12 @@ class SymmComm:
         sent = (self.world - 1) * T * H * x.element_size()
         two_shot = sent > self.one_shot_max_bytes and T >= self.world
         pf, pf_bytes = self._prefetch(prefetch)
+        msg = T * H * x.element_size()
+        quant = self.qar_mode if (self.qar_mode and H % 128 == 0 and
+                                  self.qar_min_bytes <= msg < self.qar_max_bytes) else 0
         ops.native().allreduce_fused(x, self.peer_recv, self.peer_gather, self.peer_flags, self.counters, out,
                                      residual, weight, self.err, self.rank, T, H, self.max_tokens, eps, two_shot,
-                                     self.blocks, self.timing, pf, pf_bytes)
+                                     self.blocks, self.timing, pf, pf_bytes, quant)
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         out = torch.empty_like(x)
