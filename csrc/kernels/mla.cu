@@ -475,7 +475,7 @@ int launch_mla(const MlaParams& p, cudaStream_t st) {
     ready = true;
   }
   int r = -2;
-  if constexpr (C == 576 && V == 512 && !FP4)
+  if constexpr (C == 576 && V == 512)
     if (p.impl != 1) r = sh_mla_decode_tc(&p, st);  // -2: the tcgen05 kernel does not apply
   if (r == -2) {
     shk::launch(k, dim3(p.T, (p.H + ROWS - 1) / ROWS, p.nsplit), dim3(THREADS), S::TOTAL, st, p);

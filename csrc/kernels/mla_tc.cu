@@ -44,12 +44,19 @@
 // and frees its TMEM before it returns.  The one TMA load (Q) reads this GPU's
 // memory without multicast.
 //
+// NVFP4 latent cache (416-byte rows: e2m1 pairs, e4m3 scales per 16 values,
+// bf16 rope): the producers load a key's packed row with 16-byte loads, decode
+// each block into bf16 chunks of the swizzled tile in registers (exact) and
+// copy the rope chunks with cp.async, then fence the shared-memory writes to
+// the tensor cores before they arrive; no staging buffer is needed.
+//
 // Reference parity: the reference's sparse MLA decode over its FP8 / NVFP4
 // caches (reference: kernels-oxide/nvfp4_ds_mla/src/main.rs:1-45) computes the
-// same absorbed attention; this kernel serves the bf16 latent cache.
+// same absorbed attention over the bf16 or NVFP4 latent cache.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -78,6 +85,9 @@ constexpr int COPIES = SLABS * (KT / 4);  // warp-wide 16-byte copies per tile (
 constexpr int COPIES_PER_WARP = COPIES / PROD_WARPS;
 static_assert(COPIES % PROD_WARPS == 0, "copies split evenly over the producer warps");
 constexpr uint32_t T_O = 0, T_S = 256, T_P = 320, T_Q = 352, T_COLS = 512;
+// NVFP4 latent row (kv_lora 512 + rope 64): 256 bytes of e2m1 pairs (low nibble first), 32 e4m3 scales (one
+// per 16 values), the 64 rope values in bf16 at the next 16-byte boundary; 416 bytes.
+constexpr int kFp4Scales = 256, kFp4Rope = 288, kFp4Row = 416;
 
 struct Smem {
   static constexpr int Q = 0;
@@ -156,6 +166,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+// e2m1 code in bits 0-3 (sign bit 3): 0, 0.5, 1, 1.5, 2, 3, 4, 6 and their negatives.
+__device__ __forceinline__ float e2m1_value(uint32_t c) {
+  const uint32_t e = (c >> 1) & 3u, m = c & 1u;
+  const float mag = e == 0 ? 0.5f * static_cast<float>(m) : __uint_as_float(((e + 126u) << 23) | (m << 22));
+  return (c & 8u) ? -mag : mag;
+}
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -200,6 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
   const int per = (tiles_all + p.nsplit - 1) / p.nsplit;
   const int tg0 = min(split * per, tiles_all), tg1 = min(tg0 + per, tiles_all);
   const int n = tg1 - tg0;  // key tiles of this unit
+  const bool fp4 = p.latent_fp4 != nullptr;  // NVFP4 latent rows, decoded by the producers
 
   if (threadIdx.x == 0) {
     mbar_init(qfull, 1);
@@ -265,6 +282,51 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
       const uint32_t mask = __ballot_sync(0xffffffffu, ok);
       if (warp == 0 && lane == 0) valid[st] = mask;  // published by the barrier's completion
       uint8_t* kdst = smem + Smem::K + st * K_BYTES;
+      if (fp4) {
+        // NVFP4 rows: 4 lanes per key, each decodes 8 blocks of 16 latent values (its quarter of the row)
+        // into bf16 chunks of the swizzled tile and copies 2 of the key's 8 rope chunks.  A code times its
+        // block scale has at most 5 significant bits, so the bf16 values are exact.
+        const int r = 8 * pw + (lane >> 2), q4 = lane & 3;
+        const int64_t rr = __shfl_sync(0xffffffffu, row, r);
+        const uint8_t* src = p.latent_fp4 + rr * kFp4Row;
+        uint8_t* krow = kdst + r * 128;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * q4 + cc;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                           smem_addr(krow + 8 * K_SLAB + ((c ^ (r & 7)) << 4))),
+                       "l"(src + kFp4Rope + c * 16)
+                       : "memory");
+        }
+        const uint4* pk = reinterpret_cast<const uint4*>(src + q4 * 64);
+        const uint4 w0 = __ldg(pk), w1 = __ldg(pk + 1), w2 = __ldg(pk + 2), w3 = __ldg(pk + 3);
+        const uint2 scb = __ldg(reinterpret_cast<const uint2*>(src + kFp4Scales + q4 * 8));
+        const uint32_t words[16] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w,
+                                    w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
+#pragma unroll
+        for (int blk = 0; blk < 8; ++blk) {
+          const int bidx = q4 * 8 + blk;  // block of latent dims [16 bidx, 16 bidx + 16)
+          __nv_fp8_e4m3 f8;
+          f8.__x = static_cast<__nv_fp8_storage_t>(((blk < 4 ? scb.x : scb.y) >> (8 * (blk & 3))) & 0xFFu);
+          const float sc = static_cast<float>(f8);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {  // two 16-byte chunks of 8 values
+            const uint32_t word = words[2 * blk + h];
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              o[e] = pack_bf16(e2m1_value(word >> (8 * e)) * sc, e2m1_value(word >> (8 * e + 4)) * sc);
+            const int slab = bidx >> 2, c = (bidx & 3) * 2 + h;
+            *reinterpret_cast<uint4*>(krow + slab * K_SLAB + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+        // decoded chunks (generic stores) and rope copies must be visible to the tensor cores
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&kfull[st]);
+        cyc[1] += clock64() - c1;
+        continue;
+      }
       // Copy `it` moves 4 keys x one 128-byte slab row: 8 lanes per key, one 16-byte chunk each.
 #pragma unroll 2
       for (int k = 0; k < COPIES_PER_WARP; ++k) {
@@ -540,9 +602,11 @@ constexpr int kMaxDevices = 64;
 }  // namespace
 
 extern "C" int sh_mla_decode_tc(const MlaParams* p, cudaStream_t stream) {
-  if (p->latent_fp4 || !p->latent || p->H % ROWS != 0) return -2;
+  if ((!p->latent && !p->latent_fp4) || p->H % ROWS != 0) return -2;
   if (p->T <= 0) return 0;
-  if ((reinterpret_cast<uintptr_t>(p->q) & 15) || (reinterpret_cast<uintptr_t>(p->latent) & 15)) return -2;
+  if ((reinterpret_cast<uintptr_t>(p->q) & 15) || (reinterpret_cast<uintptr_t>(p->latent) & 15) ||
+      (reinterpret_cast<uintptr_t>(p->latent_fp4) & 15))
+    return -2;
   CUtensorMap mq;
   const int r = encode_rows(&mq, p->q, static_cast<int64_t>(p->T) * p->H, ROWS);
   if (r) return 1000 + r;

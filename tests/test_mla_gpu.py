@@ -221,13 +221,14 @@ def test_deepseek_nvfp4_spec_is_exact_in_batch_invariant_mode(monkeypatch, fmt, 
         assert got == base, (key, got, base)
 
 
-@pytest.mark.parametrize("C,V", [(576, 512), (128, 64)])
+@pytest.mark.parametrize("C,V,H", [(576, 512, 64), (576, 512, 128), (128, 64, 16)])
 @pytest.mark.parametrize("sparse", [False, True])
-def test_mla_decode_over_nvfp4_cache(C, V, sparse):
+def test_mla_decode_over_nvfp4_cache(C, V, H, sparse):
     """NVFP4 latent rows written by the cache kernel and read by the decode kernel == the fp32 oracle
-    over the quantise-dequantised latent (the values the cache stores)."""
-    torch.manual_seed(C + int(sparse))
-    B, q, H, ctx = 3, 4, 64 if C == 576 else 16, 300
+    over the quantise-dequantised latent (the values the cache stores).  128 heads run the tcgen05 kernel,
+    whose producers decode the rows; 64 and 16 heads the mma.sync kernel."""
+    torch.manual_seed(C + H + int(sparse))
+    B, q, ctx = 3, 4, 300
     T = B * q
     bs = 64
     nb = -(-ctx // bs)

@@ -8,6 +8,8 @@ max over ranks.  Paths:
   ours : SymmComm.all_reduce_add_rms_norm (push one-/two-shot over NVLink,
          residual add + RMSNorm in the same kernel);
   nccl : dist.all_reduce (NCCL) followed by the fused_add_rms_norm kernel.
+With SUFFIX_NCCL_QAR=int8|fp8 (and SUFFIX_NCCL_QAR_MIN_BYTES=0) `ours` is the compressed all-reduce; its
+max_abs_diff_vs_nccl is then the quantisation error.
 Roofline: an all-reduce must move 2 (N-1)/N * T*H*2 bytes through each GPU's
 NVLink port per direction; target time = those bytes / 770 GB/s (measured
 peer-copy bandwidth per direction).  `frac` = target / measured.
@@ -116,7 +118,8 @@ def main():
         target_us = link / (LINK_GBS * 1e3)
         sent = (W - 1) * nbytes
         mode = "two_shot" if (sent > comm.one_shot_max_bytes and T >= W) else "one_shot"
-        rows.append({"world": W, "T": T, "H": H, "bytes": nbytes, "mode": mode, "ours_us": round(t_ours, 2),
+        qar = {0: "bf16", 1: "int8", 2: "fp8"}[comm.qar_mode if comm.qar_min_bytes <= nbytes < comm.qar_max_bytes else 0]
+        rows.append({"world": W, "T": T, "H": H, "bytes": nbytes, "mode": mode, "transfer": qar, "ours_us": round(t_ours, 2),
                      "nccl_us": round(t_nccl, 2), "speedup_vs_nccl": round(t_nccl / max(t_ours, 1e-9), 2),
                      "roofline_us": round(target_us, 2), "frac_ours": round(target_us / max(t_ours, 1e-9), 3),
                      "frac_nccl": round(target_us / max(t_nccl, 1e-9), 3), "max_abs_diff_vs_nccl": err,
