@@ -166,11 +166,25 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
-// e2m1 code in bits 0-3 (sign bit 3): 0, 0.5, 1, 1.5, 2, 3, 4, 6 and their negatives.
-__device__ __forceinline__ float e2m1_value(uint32_t c) {
-  const uint32_t e = (c >> 1) & 3u, m = c & 1u;
-  const float mag = e == 0 ? 0.5f * static_cast<float>(m) : __uint_as_float(((e + 126u) << 23) | (m << 22));
-  return (c & 8u) ? -mag : mag;
+// 8 e2m1 codes (nibble k = value k) -> 4 bf16 pairs times the block scale.  Byte-permute tables give the
+// two bytes of each magnitude's bf16 encoding (0, 0.5, 1, 1.5, 2, 3, 4, 6), the code's bit 3 becomes the
+// sign, and one bf16x2 multiply applies the scale (exact: at most 5 significant bits).
+__device__ __forceinline__ void e2m1x8_to_bf16(uint32_t w, __nv_bfloat162 s2, uint32_t* out) {
+  constexpr uint32_t kLo0 = 0xC0800000u, kLo1 = 0xC0804000u;  // low bytes of codes 0-3, 4-7
+  constexpr uint32_t kHi0 = 0x3F3F3F00u, kHi1 = 0x40404040u;  // high bytes of codes 0-3, 4-7
+  const uint32_t mag = w & 0x77777777u;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t sel = (mag >> (16 * h)) & 0xFFFFu;
+    const uint32_t lo = __byte_perm(kLo0, kLo1, sel), hi = __byte_perm(kHi0, kHi1, sel);
+    const uint32_t sg = (w >> (16 * h)) & 0x8888u;
+    const uint32_t p01 = __byte_perm(lo, hi, 0x5140) | ((sg & 0x8u) << 12) | ((sg & 0x80u) << 24);
+    const uint32_t p23 = __byte_perm(lo, hi, 0x7362) | ((sg & 0x800u) << 4) | ((sg & 0x8000u) << 16);
+    const __nv_bfloat162 a = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&p01), s2);
+    const __nv_bfloat162 c = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&p23), s2);
+    out[2 * h] = *reinterpret_cast<const uint32_t*>(&a);
+    out[2 * h + 1] = *reinterpret_cast<const uint32_t*>(&c);
+  }
 }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -267,28 +281,41 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
     for (int j = 0; j < n; ++j) {
       const int st = j % STAGES;
       const unsigned long long c0 = clock64();
-      if (j >= STAGES && !__all_sync(0xffffffffu, mbar_wait(&kempty[st], ((j / STAGES) - 1) & 1, abort_flag))) {
-        if (lane == 0) raise(501);
-        break;
-      }
-      const unsigned long long c1 = clock64();
-      cyc[0] += c1 - c0;
-      // this lane's key: its cache row (row 0 for a masked key, whose scores are dropped)
+      // this lane's key: its cache row (row 0 for a masked key, whose scores are dropped); computed before
+      // the free-stage wait, like the NVFP4 path's packed-row loads, so their latency overlaps it
       const int64_t kp = static_cast<int64_t>(tg0 + j) * KT + lane;
       int64_t pos = -1;
       if (kp < nkeys) pos = p.topk ? static_cast<int64_t>(p.topk[static_cast<int64_t>(t) * p.topk_k + kp]) : kp;
       const bool ok = pos >= 0 && pos <= qpos;
       const int64_t row = ok ? static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63) : 0;
       const uint32_t mask = __ballot_sync(0xffffffffu, ok);
+      // NVFP4: 4 lanes per key, each with a quarter of the packed row (8 blocks of 16 latent values)
+      const int fr = 8 * pw + (lane >> 2), q4 = lane & 3;
+      const int64_t frr = __shfl_sync(0xffffffffu, row, fr);
+      const uint8_t* fsrc = fp4 ? p.latent_fp4 + frr * kFp4Row : nullptr;
+      uint4 w0, w1, w2, w3;
+      uint2 scb;
+      if (fp4) {
+        const uint4* pk = reinterpret_cast<const uint4*>(fsrc + q4 * 64);
+        w0 = __ldg(pk);
+        w1 = __ldg(pk + 1);
+        w2 = __ldg(pk + 2);
+        w3 = __ldg(pk + 3);
+        scb = __ldg(reinterpret_cast<const uint2*>(fsrc + kFp4Scales + q4 * 8));
+      }
+      if (j >= STAGES && !__all_sync(0xffffffffu, mbar_wait(&kempty[st], ((j / STAGES) - 1) & 1, abort_flag))) {
+        if (lane == 0) raise(501);
+        break;
+      }
+      const unsigned long long c1 = clock64();
+      cyc[0] += c1 - c0;
       if (warp == 0 && lane == 0) valid[st] = mask;  // published by the barrier's completion
       uint8_t* kdst = smem + Smem::K + st * K_BYTES;
       if (fp4) {
-        // NVFP4 rows: 4 lanes per key, each decodes 8 blocks of 16 latent values (its quarter of the row)
-        // into bf16 chunks of the swizzled tile and copies 2 of the key's 8 rope chunks.  A code times its
-        // block scale has at most 5 significant bits, so the bf16 values are exact.
-        const int r = 8 * pw + (lane >> 2), q4 = lane & 3;
-        const int64_t rr = __shfl_sync(0xffffffffu, row, r);
-        const uint8_t* src = p.latent_fp4 + rr * kFp4Row;
+        // Decode into bf16 chunks of the swizzled tile and copy 2 of the key's 8 rope chunks.  A code
+        // times its block scale has at most 5 significant bits, so the bf16 values are exact.
+        const int r = fr;
+        const uint8_t* src = fsrc;
         uint8_t* krow = kdst + r * 128;
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
@@ -298,9 +325,6 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
                        "l"(src + kFp4Rope + c * 16)
                        : "memory");
         }
-        const uint4* pk = reinterpret_cast<const uint4*>(src + q4 * 64);
-        const uint4 w0 = __ldg(pk), w1 = __ldg(pk + 1), w2 = __ldg(pk + 2), w3 = __ldg(pk + 3);
-        const uint2 scb = __ldg(reinterpret_cast<const uint2*>(src + kFp4Scales + q4 * 8));
         const uint32_t words[16] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w,
                                     w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
 #pragma unroll
@@ -308,14 +332,11 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
           const int bidx = q4 * 8 + blk;  // block of latent dims [16 bidx, 16 bidx + 16)
           __nv_fp8_e4m3 f8;
           f8.__x = static_cast<__nv_fp8_storage_t>(((blk < 4 ? scb.x : scb.y) >> (8 * (blk & 3))) & 0xFFu);
-          const float sc = static_cast<float>(f8);
+          const __nv_bfloat162 sc2 = __float2bfloat162_rn(static_cast<float>(f8));  // exact: 4 significant bits
 #pragma unroll
           for (int h = 0; h < 2; ++h) {  // two 16-byte chunks of 8 values
-            const uint32_t word = words[2 * blk + h];
             uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              o[e] = pack_bf16(e2m1_value(word >> (8 * e)) * sc, e2m1_value(word >> (8 * e + 4)) * sc);
+            e2m1x8_to_bf16(words[2 * blk + h], sc2, o);
             const int slab = bidx >> 2, c = (bidx & 3) * 2 + h;
             *reinterpret_cast<uint4*>(krow + slab * K_SLAB + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
