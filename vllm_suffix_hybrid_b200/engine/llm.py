@@ -181,6 +181,10 @@ class LLMEngine:
 
     # ------------------------------------------------------------------ sizing
     def _auto_blocks(self) -> int:
+        """KV blocks from the memory budget: at most 4x what max_num_seqs full-length requests could hold,
+        at least one full-length request.  Requests are admitted against their own reservations
+        (`_select_prefill`), so a pool smaller than max_num_seqs full-length requests never runs dry; it
+        only admits fewer long requests at once."""
         c = self.cfg
         need = c.max_num_seqs * (self.max_blocks_per_seq + 1) + 8
         if torch.device(self.device).type != "cuda":
@@ -191,7 +195,7 @@ class LLMEngine:
         kv_layers = getattr(m, "num_kv_layers", c.model.layers)
         per_block *= kv_layers + (1 if self.draft is not None else 0)
         budget = int(free * c.cache.gpu_memory_fraction) - (4 << 30)
-        return max(need, min(budget // per_block, 4 * need))
+        return max(self.max_blocks_per_seq + 9, min(budget // per_block, 4 * need))
 
     # ------------------------------------------------------------------ API
     def add_request(self, prompt, max_new_tokens: int = 128, rid: Optional[str] = None,
@@ -226,6 +230,8 @@ class LLMEngine:
                 raise RuntimeError("admit_prefilled: more requests than max_num_seqs")
             rid = self.add_request(p, max_new_tokens)
             r = self.waiting.pop()
+            if self._reservation(r) > self._unclaimed_blocks():
+                raise MemoryError(f"admit_prefilled: request {rid} does not fit the KV blocks left unpromised")
             self._ensure_blocks(r, len(r.prompt) + 2 * self.k + 2)
             r.slot = self._free_slots.pop()
             row = len(self.running)
@@ -383,9 +389,14 @@ class LLMEngine:
         if self.dp > 1:
             return self._dp_step()
         free_rows = self.cfg.max_num_seqs - len(self.running)
-        if self.waiting and free_rows > 0:
+        # a waiting request is prefilled once a row is free and the KV blocks not promised to running requests
+        # cover it (otherwise the running ones decode on, without breaking the decode pipeline, until they do)
+        if self.waiting and free_rows > 0 and (not self.running or
+                                               self._reservation(self.waiting[0]) <= self._unclaimed_blocks()):
             self._drain()
-            return self._prefill_step(self.cfg.max_num_seqs - len(self.running))
+            batch = self._select_prefill(self.cfg.max_num_seqs - len(self.running))
+            if batch:
+                return self._prefill_step(0, batch)
         decode = self._decode_step_async if self._async else self._decode_step
         sp = self.step_profiler
         if sp is not None:
@@ -420,15 +431,35 @@ class LLMEngine:
         if r.blocks_np.shape[0] != len(r.blocks):  # the block-table row the decode steps copy
             r.blocks_np = np.asarray(r.blocks, dtype=np.int32)
 
+    def _reservation(self, r: Request) -> int:
+        """Blocks request r can ever hold: its prompt and every output token, plus the verify window's
+        look-ahead (the decode step keeps blocks for committed + 2k + 2 positions)."""
+        return blocks_for(len(r.prompt) + r.max_new_tokens + 2 * self.k + 2, self.block_size)
+
+    def _unclaimed_blocks(self) -> int:
+        """Free blocks not yet promised to a running request's remaining growth."""
+        owed = sum(max(0, self._reservation(r) - len(r.blocks)) for r in self.running)
+        return self.pool.free - owed
+
     def _select_prefill(self, free_rows: int) -> list:
+        """Waiting requests to prefill, in arrival order, within the prefill token budget and the KV blocks
+        that are not promised to running requests (each admitted request reserves its own maximum, so the
+        pool never runs dry mid-generation; a request that does not fit waits for others to finish)."""
         batch, budget = [], self.cfg.max_prefill_tokens
+        blocks = self._unclaimed_blocks()
         while self.waiting and len(batch) < free_rows:
             r = self.waiting[0]
             if batch and len(r.prompt) > budget:
                 break
+            need = self._reservation(r)
+            if need > blocks:
+                if not batch and not self.running:
+                    raise MemoryError(f"request {r.rid} needs {need} KV blocks, the pool has {self.pool.free} free")
+                break
             self.waiting.pop(0)
             batch.append(r)
             budget -= len(r.prompt)
+            blocks -= need
         return batch
 
     def _prefill_step(self, free_rows: int, batch: Optional[list] = None, pad: Optional[tuple] = None) -> StepStats:
