@@ -19,9 +19,9 @@
 // ring of 32-key tiles (36 KB each).  TMEM: O [0, 256), S [256, 320) (two
 // buffers), P [320, 352) (two buffers, bf16 pairs), Q [352, 480).
 //
-// Roles (288 threads):
-//   warps 0, 6-8  producers: each computes the tile's 32 cache rows (top-k
-//                 position -> block table) and issues a quarter of the tile's
+// Roles (416 threads):
+//   warps 0, 6-12 producers: each computes the tile's 32 cache rows (top-k
+//                 position -> block table) and issues an eighth of the tile's
 //                 72 warp-wide 16-byte cp.async copies (4 keys x one 128-byte
 //                 row of a 64-dim slab each), stored at the swizzled positions
 //                 the MMA descriptors expect; every lane's arrival on the
@@ -79,8 +79,8 @@ constexpr int Q_SLAB = ROWS * 128;  // 16 KB
 constexpr int K_SLAB = KT * 128;    // 4 KB
 constexpr int K_BYTES = SLABS * K_SLAB;  // 36 KB per key tile
 constexpr int STAGES = 4;
-constexpr int PROD_WARPS = 4;       // warps 0, 6, 7, 8
-constexpr int THREADS = 288;
+constexpr int PROD_WARPS = 8;       // warps 0, 6-12
+constexpr int THREADS = 416;
 constexpr int COPIES = SLABS * (KT / 4);  // warp-wide 16-byte copies per tile (72)
 constexpr int COPIES_PER_WARP = COPIES / PROD_WARPS;
 static_assert(COPIES % PROD_WARPS == 0, "copies split evenly over the producer warps");
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
     if (p.err) atomicCAS(p.err, 0, code);
     *abort_flag = 1;
   };
-  const int pw = warp == 0 ? 0 : warp - 5;  // producer index of warps 0, 6, 7, 8
+  const int pw = warp == 0 ? 0 : warp - 5;  // producer index of warps 0, 6-12
 
   if (warp == 0 || warp >= 6) {
     // ------------------------------------------------------------------ producers
@@ -278,30 +278,43 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
     }
     const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
     const char* lat = reinterpret_cast<const char*>(p.latent);
+    // This lane's key of tile jj: its top-k position (-1: none) and its cache row (row 0 for a masked key,
+    // whose scores are dropped).  The two dependent loads run ahead of the tile that uses them: tile j + 2's
+    // position and tile j + 1's row are fetched while tile j is processed.
+    auto pos_of = [&](int jj) -> int64_t {
+      const int64_t kp = static_cast<int64_t>(tg0 + jj) * KT + lane;
+      if (jj >= n || kp >= nkeys) return -1;
+      return p.topk ? static_cast<int64_t>(p.topk[static_cast<int64_t>(t) * p.topk_k + kp]) : kp;
+    };
+    auto row_of = [&](int64_t pos) -> int64_t {
+      return (pos >= 0 && pos <= qpos) ? static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63) : 0;
+    };
+    int64_t pos_c = pos_of(0), row_c = row_of(pos_c), pos_n = pos_of(1), row_n = 0, pos_nn = -1;
+    // NVFP4: 8 lanes per key, lane q8 with one 64-dim slab of the packed row (4 blocks of 16 values); a
+    // tile's packed bytes are loaded before its free-stage wait.
+    const int fr = 4 * pw + (lane >> 3), q8 = lane & 7;
     for (int j = 0; j < n; ++j) {
       const int st = j % STAGES;
       const unsigned long long c0 = clock64();
-      // this lane's key: its cache row (row 0 for a masked key, whose scores are dropped); computed before
-      // the free-stage wait, like the NVFP4 path's packed-row loads, so their latency overlaps it
-      const int64_t kp = static_cast<int64_t>(tg0 + j) * KT + lane;
-      int64_t pos = -1;
-      if (kp < nkeys) pos = p.topk ? static_cast<int64_t>(p.topk[static_cast<int64_t>(t) * p.topk_k + kp]) : kp;
-      const bool ok = pos >= 0 && pos <= qpos;
-      const int64_t row = ok ? static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63) : 0;
+      if (j > 0) {
+        pos_c = pos_n;
+        row_c = row_n;
+        pos_n = pos_nn;
+      }
+      const bool ok = pos_c >= 0 && pos_c <= qpos;
+      const int64_t row = row_c;
       const uint32_t mask = __ballot_sync(0xffffffffu, ok);
-      // NVFP4: 4 lanes per key, each with a quarter of the packed row (8 blocks of 16 latent values)
-      const int fr = 8 * pw + (lane >> 2), q4 = lane & 3;
-      const int64_t frr = __shfl_sync(0xffffffffu, row, fr);
-      const uint8_t* fsrc = fp4 ? p.latent_fp4 + frr * kFp4Row : nullptr;
-      uint4 w0, w1, w2, w3;
-      uint2 scb;
+      row_n = row_of(pos_n);   // used by the next tile
+      pos_nn = pos_of(j + 2);  // used two tiles from now
+      const uint8_t* fsrc = nullptr;
+      uint4 w0, w1;
+      uint32_t scw;
       if (fp4) {
-        const uint4* pk = reinterpret_cast<const uint4*>(fsrc + q4 * 64);
+        fsrc = p.latent_fp4 + __shfl_sync(0xffffffffu, row, fr) * kFp4Row;
+        const uint4* pk = reinterpret_cast<const uint4*>(fsrc + q8 * 32);
         w0 = __ldg(pk);
         w1 = __ldg(pk + 1);
-        w2 = __ldg(pk + 2);
-        w3 = __ldg(pk + 3);
-        scb = __ldg(reinterpret_cast<const uint2*>(fsrc + kFp4Scales + q4 * 8));
+        scw = __ldg(reinterpret_cast<const uint32_t*>(fsrc + kFp4Scales + q8 * 4));
       }
       if (j >= STAGES && !__all_sync(0xffffffffu, mbar_wait(&kempty[st], ((j / STAGES) - 1) & 1, abort_flag))) {
         if (lane == 0) raise(501);
@@ -312,33 +325,26 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
       if (warp == 0 && lane == 0) valid[st] = mask;  // published by the barrier's completion
       uint8_t* kdst = smem + Smem::K + st * K_BYTES;
       if (fp4) {
-        // Decode into bf16 chunks of the swizzled tile and copy 2 of the key's 8 rope chunks.  A code
+        // Decode slab q8 into bf16 chunks of the swizzled tile and copy the key's rope chunk q8.  A code
         // times its block scale has at most 5 significant bits, so the bf16 values are exact.
         const int r = fr;
-        const uint8_t* src = fsrc;
         uint8_t* krow = kdst + r * 128;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(krow + 8 * K_SLAB + ((q8 ^ (r & 7)) << 4))),
+                     "l"(fsrc + kFp4Rope + q8 * 16)
+                     : "memory");
+        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint8_t* kslab = krow + q8 * K_SLAB;
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = 2 * q4 + cc;
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                           smem_addr(krow + 8 * K_SLAB + ((c ^ (r & 7)) << 4))),
-                       "l"(src + kFp4Rope + c * 16)
-                       : "memory");
-        }
-        const uint32_t words[16] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w,
-                                    w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
-#pragma unroll
-        for (int blk = 0; blk < 8; ++blk) {
-          const int bidx = q4 * 8 + blk;  // block of latent dims [16 bidx, 16 bidx + 16)
+        for (int blk = 0; blk < 4; ++blk) {  // block of latent dims [64 q8 + 16 blk, + 16)
           __nv_fp8_e4m3 f8;
-          f8.__x = static_cast<__nv_fp8_storage_t>(((blk < 4 ? scb.x : scb.y) >> (8 * (blk & 3))) & 0xFFu);
+          f8.__x = static_cast<__nv_fp8_storage_t>((scw >> (8 * blk)) & 0xFFu);
           const __nv_bfloat162 sc2 = __float2bfloat162_rn(static_cast<float>(f8));  // exact: 4 significant bits
 #pragma unroll
           for (int h = 0; h < 2; ++h) {  // two 16-byte chunks of 8 values
             uint32_t o[4];
             e2m1x8_to_bf16(words[2 * blk + h], sc2, o);
-            const int slab = bidx >> 2, c = (bidx & 3) * 2 + h;
-            *reinterpret_cast<uint4*>(krow + slab * K_SLAB + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            const int c = blk * 2 + h;
+            *reinterpret_cast<uint4*>(kslab + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
         // decoded chunks (generic stores) and rope copies must be visible to the tensor cores
