@@ -55,3 +55,17 @@ def test_request_larger_than_the_pool_is_refused_not_deadlocked():
     eng.add_request(np.arange(200) % 512, max_new_tokens=40)
     with pytest.raises(MemoryError):
         eng.step()
+
+
+def test_rope_table_covers_max_model_len():
+    """A 128k prompt plus its output runs past a 131072-entry RoPE table: the engine extends the table to
+    every position a max_model_len request can write (the Kimi-K2 benchmark layout)."""
+    m = shrink(llama3_8b_config(), layers=1, hidden=64, vocab=256)
+    m.dtype = "float32"
+    m.max_position = 300
+    cfg = EngineConfig(model=m, spec=SpecConfig(method="none", k=0), device="cpu", cuda_graphs=False,
+                       cache=CacheConfig(max_model_len=512, block_size=16), max_num_seqs=2)
+    eng = LLMEngine(cfg)
+    assert eng.model.cos_sin.shape[0] >= 512 + 2
+    out = eng.generate([np.arange(400) % 256], max_new_tokens=100)  # positions 400..499 exist in the table
+    assert len(out[0]) == 100

@@ -101,6 +101,14 @@ class LLMEngine:
         spec = cfg.spec
         self.k = spec.k if spec.method != "none" else 0
         self.adaptive_width = bool(getattr(spec, "adaptive_width", True))
+        # The RoPE tables are indexed by position on the device: they must cover every position a request of
+        # max_model_len can write (its prompt, its output and the verify look-ahead), or a decode step reads
+        # past the table.  Rotary embeddings are defined for any position, so the table is extended.
+        reach = cfg.cache.max_model_len + 2 * self.k + 2
+        if mcfg.max_position < reach:
+            logger.warning("RoPE table extended from %d to %d positions (max_model_len %d)", mcfg.max_position,
+                           reach, cfg.cache.max_model_len)
+            mcfg.max_position = reach
         self.model, self.draft = build_model(mcfg, dev, cfg.seed, with_draft=spec.method in ("hybrid", "native"))
         if (st.tp > 1 or st.ep > 1) and cfg.parallel.comm == "fused" and torch.device(dev).type == "cuda":
             from ..parallel import comm as pcomm
