@@ -84,9 +84,11 @@ __device__ __forceinline__ int request_of(const int64_t* q_start, int B, int t) 
 }
 __device__ __forceinline__ void bar_pair(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
 
-__host__ __device__ constexpr int fp4_sc_off(int Cl) { return Cl / 2; }
-__host__ __device__ constexpr int fp4_rope_off(int Cl) { return (Cl / 2 + Cl / 16 + 15) / 16 * 16; }
-__host__ __device__ constexpr int fp4_row_bytes(int Cl, int R) { return (fp4_rope_off(Cl) + 2 * R + 15) / 16 * 16; }
+// NVFP4 row (mla.h): e2m1 pairs, R e4m3 rope bytes, Cl/16 permuted e4m3 block scales, padded to 16 bytes.
+__host__ __device__ constexpr int fp4_rope_off(int Cl) { return Cl / 2; }
+__host__ __device__ constexpr int fp4_sc_off(int Cl, int R) { return Cl / 2 + R; }
+__host__ __device__ constexpr int fp4_sc_pos(int Cl, int s) { return (Cl / 64) * (s & 3) + (s >> 2); }
+__host__ __device__ constexpr int fp4_row_bytes(int Cl, int R) { return (Cl / 2 + R + Cl / 16 + 15) / 16 * 16; }
 
 template <int C, int V, bool FP4>
 struct MlaSmem {
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(THREADS, 1) mla_decode_kernel(MlaParams p) {
       const uint8_t* r = raw + key * S::ROWB;
       const uint2 pk = *reinterpret_cast<const uint2*>(r + blk * 8);
       __nv_fp8_e4m3 s8;
-      s8.__x = r[fp4_sc_off(V) + blk];
+      s8.__x = r[fp4_sc_off(V, C - V) + fp4_sc_pos(V, blk)];
       const float sc = static_cast<float>(s8) * 9.223372036854775808e18f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -199,11 +201,12 @@ __global__ void __launch_bounds__(THREADS, 1) mla_decode_kernel(MlaParams p) {
         *reinterpret_cast<uint4*>(kvp + swz<KEYS>(key, blk * 2 + h)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
       }
     }
-    constexpr int RC = (C - V) * 2 / 16;
+    constexpr int RC = (C - V) / 8;  // 16-byte bf16 chunks of the rope, 8 e4m3 bytes each
     for (int i = tid; i < KEYS * RC; i += THREADS) {
       const int key = i / RC, rc = i % RC;
-      *reinterpret_cast<uint4*>(kvp + swz<KEYS>(key, V / 8 + rc)) =
-          *reinterpret_cast<const uint4*>(raw + key * S::ROWB + fp4_rope_off(V) + rc * 16);
+      uint32_t w[4];
+      e4m3x8_to_bf16(*reinterpret_cast<const uint2*>(raw + key * S::ROWB + fp4_rope_off(V) + rc * 8), w);
+      *reinterpret_cast<uint4*>(kvp + swz<KEYS>(key, V / 8 + rc)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   };
 
@@ -414,7 +417,7 @@ __global__ void cache_write_kernel(__nv_bfloat16* __restrict__ latent, const __n
 }
 
 // NVFP4 latent row writer (layout: sh_mla_fp4_row_bytes): one CTA of 64 threads per token; thread i
-// quantises latent block i (16 values) and threads copy the rope values.
+// quantises latent block i (16 values) and the threads round the rope values to e4m3.
 __device__ __forceinline__ uint32_t e2m1x8(const float* v) {
   uint32_t out;
   asm("{\n .reg .b8 b0, b1, b2, b3;\n"
@@ -446,16 +449,16 @@ __global__ void cache_write_fp4_kernel(uint8_t* __restrict__ cache, const __nv_b
       v[j] = __bfloat162float(c[t * c_stride + blk * 16 + j]);
       am = fmaxf(am, fabsf(v[j]));
     }
-    const __nv_fp8_e4m3 s(am / 6.f);  // round to nearest even, saturating
-    const float sv = static_cast<float>(s);
-    const float inv = sv > 0.f ? 1.f / sv : 0.f;
+    // round to nearest even, saturating; the 2^-9 floor (the smallest e4m3 subnormal) keeps the scale nonzero
+    const __nv_fp8_e4m3 s(fmaxf(__fdiv_rn(am, 6.f), 1.953125e-3f));
+    const float inv = __frcp_rn(static_cast<float>(s));  // correctly rounded, as the CPU statement
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] *= inv;
     *reinterpret_cast<uint2*>(row + blk * 8) = make_uint2(e2m1x8(v), e2m1x8(v + 8));
-    row[fp4_sc_off(Cl) + blk] = s.__x;
+    row[fp4_sc_off(Cl, R) + fp4_sc_pos(Cl, blk)] = s.__x;
   }
-  __nv_bfloat16* rope = reinterpret_cast<__nv_bfloat16*>(row + fp4_rope_off(Cl));
-  for (int i = threadIdx.x; i < R; i += blockDim.x) rope[i] = kpe[t * kpe_stride + i];
+  for (int i = threadIdx.x; i < R; i += blockDim.x)
+    row[fp4_rope_off(Cl) + i] = __nv_fp8_e4m3(__bfloat162float(kpe[t * kpe_stride + i])).__x;
 }
 
 }  // namespace mla
@@ -506,7 +509,7 @@ extern "C" int sh_mla_cache_write_fp4(uint8_t* cache, const __nv_bfloat16* c, in
                                       const __nv_bfloat16* kpe, int64_t kpe_stride, const int64_t* slots, int T,
                                       int Cl, int R, cudaStream_t stream) {
   if (T <= 0) return 0;
-  if (Cl % 16 != 0 || Cl / 16 > 64) return -2;
+  if (Cl % 64 != 0 || Cl / 16 > 64) return -2;
   shk::launch(cache_write_fp4_kernel, dim3(T), dim3(64), 0, stream, cache, c, c_stride, kpe, kpe_stride, slots, Cl,
               R);
   return static_cast<int>(cudaGetLastError());

@@ -44,11 +44,11 @@
 // and frees its TMEM before it returns.  The one TMA load (Q) reads this GPU's
 // memory without multicast.
 //
-// NVFP4 latent cache (416-byte rows: e2m1 pairs, e4m3 scales per 16 values,
-// bf16 rope): the producers load a key's packed row with 16-byte loads, decode
-// each block into bf16 chunks of the swizzled tile in registers (exact) and
-// copy the rope chunks with cp.async, then fence the shared-memory writes to
-// the tensor cores before they arrive; no staging buffer is needed.
+// NVFP4 latent cache (352-byte rows: e2m1 pairs, e4m3 rope, permuted e4m3
+// scales per 16 values): the producers load a key's packed row with 16-, 8- and
+// 4-byte loads, decode each block and the rope into bf16 chunks of the swizzled
+// tile in registers (exact), then fence the shared-memory writes to the tensor
+// cores before they arrive; no staging buffer is needed.
 //
 // Reference parity: the reference's sparse MLA decode over its FP8 / NVFP4
 // caches (reference: kernels-oxide/nvfp4_ds_mla/src/main.rs:1-45) computes the
@@ -85,9 +85,9 @@ constexpr int COPIES = SLABS * (KT / 4);  // warp-wide 16-byte copies per tile (
 constexpr int COPIES_PER_WARP = COPIES / PROD_WARPS;
 static_assert(COPIES % PROD_WARPS == 0, "copies split evenly over the producer warps");
 constexpr uint32_t T_O = 0, T_S = 256, T_P = 320, T_Q = 352, T_COLS = 512;
-// NVFP4 latent row (kv_lora 512 + rope 64): 256 bytes of e2m1 pairs (low nibble first), 32 e4m3 scales (one
-// per 16 values), the 64 rope values in bf16 at the next 16-byte boundary; 416 bytes.
-constexpr int kFp4Scales = 256, kFp4Rope = 288, kFp4Row = 416;
+// NVFP4 latent row (kv_lora 512 + rope 64, mla.h): 256 bytes of e2m1 pairs (low nibble first), the 64 rope
+// values as e4m3, 32 e4m3 scales (one per 16 values; block s at byte 8 (s % 4) + s / 4); 352 bytes.
+constexpr int kFp4Rope = 256, kFp4Scales = 320, kFp4Row = 352;
 
 struct Smem {
   static constexpr int Q = 0;
@@ -306,15 +306,24 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
       const uint32_t mask = __ballot_sync(0xffffffffu, ok);
       row_n = row_of(pos_n);   // used by the next tile
       pos_nn = pos_of(j + 2);  // used two tiles from now
-      const uint8_t* fsrc = nullptr;
       uint4 w0, w1;
-      uint32_t scw;
+      uint32_t scw = 0, ro[4];
       if (fp4) {
-        fsrc = p.latent_fp4 + __shfl_sync(0xffffffffu, row, fr) * kFp4Row;
+        const uint8_t* fsrc = p.latent_fp4 + __shfl_sync(0xffffffffu, row, fr) * kFp4Row;
         const uint4* pk = reinterpret_cast<const uint4*>(fsrc + q8 * 32);
         w0 = __ldg(pk);
         w1 = __ldg(pk + 1);
-        scw = __ldg(reinterpret_cast<const uint32_t*>(fsrc + kFp4Scales + q8 * 4));
+        const uint2 rw = __ldg(reinterpret_cast<const uint2*>(fsrc + kFp4Rope + q8 * 8));
+        const uint32_t sw = __ldg(reinterpret_cast<const uint32_t*>(fsrc + kFp4Scales + q8 * 4));  // scale word q8
+        // Before the free-stage wait: block 4 q8 + blk's scale sits at byte 8 blk + q8 of the scale region
+        // (word 2 blk + q8 / 4, loaded by that lane of the key's eight; byte q8 % 4), and rope chunk q8 is
+        // converted to bf16.
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+          const uint32_t wd = __shfl_sync(0xffffffffu, sw, (lane & ~7) | (2 * blk + (q8 >> 2)));
+          scw |= ((wd >> (8 * (q8 & 3))) & 0xFFu) << (8 * blk);
+        }
+        e4m3x8_to_bf16(rw, ro);
       }
       if (j >= STAGES && !__all_sync(0xffffffffu, mbar_wait(&kempty[st], ((j / STAGES) - 1) & 1, abort_flag))) {
         if (lane == 0) raise(501);
@@ -325,13 +334,11 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
       if (warp == 0 && lane == 0) valid[st] = mask;  // published by the barrier's completion
       uint8_t* kdst = smem + Smem::K + st * K_BYTES;
       if (fp4) {
-        // Decode slab q8 into bf16 chunks of the swizzled tile and copy the key's rope chunk q8.  A code
-        // times its block scale has at most 5 significant bits, so the bf16 values are exact.
+        // Decode slab q8 into bf16 chunks of the swizzled tile and store rope chunk q8.  A code times its block
+        // scale has at most 5 significant bits and an e4m3 value 4, so the bf16 values are exact.
         const int r = fr;
         uint8_t* krow = kdst + r * 128;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(krow + 8 * K_SLAB + ((q8 ^ (r & 7)) << 4))),
-                     "l"(fsrc + kFp4Rope + q8 * 16)
-                     : "memory");
+        *reinterpret_cast<uint4*>(krow + 8 * K_SLAB + ((q8 ^ (r & 7)) << 4)) = make_uint4(ro[0], ro[1], ro[2], ro[3]);
         const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         uint8_t* kslab = krow + q8 * K_SLAB;
 #pragma unroll
@@ -347,8 +354,7 @@ __global__ void __launch_bounds__(THREADS, 1) mla_tc_kernel(const __grid_constan
             *reinterpret_cast<uint4*>(kslab + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
-        // decoded chunks (generic stores) and rope copies must be visible to the tensor cores
-        asm volatile("cp.async.wait_all;" ::: "memory");
+        // the decoded chunks (generic stores) must be visible to the tensor cores
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(&kfull[st]);
         cyc[1] += clock64() - c1;

@@ -221,6 +221,29 @@ def test_deepseek_nvfp4_spec_is_exact_in_batch_invariant_mode(monkeypatch, fmt, 
         assert got == base, (key, got, base)
 
 
+@pytest.mark.parametrize("Cl,R", [(512, 64), (64, 64)])
+def test_nvfp4_cache_writer_bytes_match_statement(Cl, R):
+    """The cache kernel's NVFP4 rows are byte-identical to the CPU statement `mla_fp4_pack` (vLLM's
+    nvfp4_ds_mla row: e2m1 pairs, e4m3 rope, permuted e4m3 block scales); unwritten slots stay zero."""
+    torch.manual_seed(Cl + R)
+    N, bs = 150, 64
+    c = (torch.randn(N, Cl) * torch.rand(N, 1) * 3).to(torch.bfloat16)
+    c[0, :16] = 0
+    c[1, 16:32] = 1e-6
+    c[2, 32:48] = 4000.0  # block scale saturates at 448
+    kpe = (torch.randn(N, R) * 30).to(torch.bfloat16)
+    kpe[3, :4] = 1000.0  # rope saturates at 448
+    slots = torch.randperm(3 * bs)[:N]
+    slots[5] = -1
+    cache = torch.zeros(3, bs, ops.mla_fp4_row_bytes(Cl, R), dtype=torch.uint8, device="cuda")
+    ops.mla_cache_write(cache, c.cuda(), kpe.cuda(), slots.cuda())
+    torch.cuda.synchronize()
+    want = torch.zeros(3 * bs, cache.shape[2], dtype=torch.uint8)
+    keep = slots >= 0
+    want[slots[keep]] = ref.mla_fp4_pack(c[keep], kpe[keep])
+    assert torch.equal(cache.view(3 * bs, -1).cpu(), want)
+
+
 @pytest.mark.parametrize("C,V,H", [(576, 512, 64), (576, 512, 128), (128, 64, 16)])
 @pytest.mark.parametrize("sparse", [False, True])
 def test_mla_decode_over_nvfp4_cache(C, V, H, sparse):

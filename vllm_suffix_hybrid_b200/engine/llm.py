@@ -199,9 +199,15 @@ class LLMEngine:
             return need
         free, _ = torch.cuda.mem_get_info()
         m = self.model
-        per_block = 2 * self.block_size * m.kv_heads_local * c.model.head_dim * m.embed.element_size()
         kv_layers = getattr(m, "num_kv_layers", c.model.layers)
-        per_block *= kv_layers + (1 if self.draft is not None else 0)
+        if hasattr(m, "kv_block_bytes"):  # latent-cache models size their own rows (MLA: NVFP4 or bf16 + indexer)
+            per_block = m.kv_block_bytes(self.block_size) * kv_layers
+            if self.draft is not None:
+                per_block += (self.draft.kv_block_bytes(self.block_size) if hasattr(self.draft, "kv_block_bytes")
+                              else m.kv_block_bytes(self.block_size))
+        else:
+            per_block = 2 * self.block_size * m.kv_heads_local * c.model.head_dim * m.embed.element_size()
+            per_block *= kv_layers + (1 if self.draft is not None else 0)
         budget = int(free * c.cache.gpu_memory_fraction) - (4 << 30)
         return max(self.max_blocks_per_seq + 9, min(budget // per_block, 4 * need))
 

@@ -213,11 +213,24 @@ class DeepseekModel:
     def kv_cache_shape(self, num_blocks: int, block_size: int):
         return (num_blocks, block_size, self.cfg.kv_lora + self.cfg.qk_rope)
 
-    def allocate_caches(self, num_blocks: int, block_size: int, slots: int, window: int) -> List:
+    def _kv_fp4(self) -> bool:
+        return self.cfg.kv_format == "nvfp4" and torch.device(self.device).type == "cuda"
+
+    def kv_block_bytes(self, block_size: int) -> int:
+        """Device bytes one KV block takes in one layer: the latent rows (NVFP4 or model dtype) and, with the
+        DSA indexer, its key page."""
+        if self._kv_fp4():
+            row = ops.mla_fp4_row_bytes(self.cfg.kv_lora, self.cfg.qk_rope)
+        else:
+            row = (self.cfg.kv_lora + self.cfg.qk_rope) * self.embed.element_size()
+        return block_size * row + (ops.DSA_PAGE_BYTES if self.cfg.dsa_topk else 0)
+
+    def allocate_caches(self, num_blocks: int, block_size: int, slots: int, window: int,
+                        n_layers: int | None = None) -> List:
         caches = []
-        fp4 = self.cfg.kv_format == "nvfp4" and torch.device(self.device).type == "cuda"
-        for _ in self.layers:
-            if fp4:  # NVFP4 latent rows (2.8x smaller than bf16 at kv_lora 512)
+        fp4 = self._kv_fp4()
+        for _ in range(len(self.layers) if n_layers is None else n_layers):
+            if fp4:  # NVFP4 latent rows (3.3x smaller than bf16 at kv_lora 512)
                 lat = torch.zeros(num_blocks, block_size, ops.mla_fp4_row_bytes(self.cfg.kv_lora, self.cfg.qk_rope),
                                   dtype=torch.uint8, device=self.device)
             else:
@@ -260,8 +273,11 @@ class DeepseekMtp:
         self.layer = DeepseekLayer(cfg, cfg.layers, dt, device, gen, target.cos_sin, fmt)
         self.norm = RMSNorm(cfg.hidden, cfg.norm_eps, dt, device)
 
+    def kv_block_bytes(self, block_size: int) -> int:
+        return self.target.kv_block_bytes(block_size)
+
     def allocate_caches(self, num_blocks: int, block_size: int):
-        return self.target.allocate_caches(num_blocks, block_size, 0, 0)[0]
+        return self.target.allocate_caches(num_blocks, block_size, 0, 0, n_layers=1)[0]
 
     def forward(self, tokens, feature, meta, cache):
         e = self.enorm(ops.embedding(tokens, self.target.embed))

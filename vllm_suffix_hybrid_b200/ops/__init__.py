@@ -496,15 +496,16 @@ def mla_cache_write(latent: torch.Tensor, c: torch.Tensor, kpe: torch.Tensor, sl
         ok = slots >= 0
         s = slots[ok]
         cc = ref.mla_fp4_qdq(c).to(c.dtype) if fp4 else c
-        latent[s // bs, s % bs] = torch.cat([cc, kpe.to(c.dtype)], -1)[ok].to(latent.dtype)
+        kk = ref.e4m3_qdq(kpe).to(c.dtype) if fp4 else kpe.to(c.dtype)
+        latent[s // bs, s % bs] = torch.cat([cc, kk], -1)[ok].to(latent.dtype)
         return
     native().mla_cache_write(latent, c, kpe, slots)
 
 
 def mla_fp4_row_bytes(kv_lora: int, rope: int) -> int:
-    """Bytes of one NVFP4 latent cache row (kv_lora e2m1 values + e4m3 scales + rope in bf16, 16-aligned)."""
-    r0 = (kv_lora // 2 + kv_lora // 16 + 15) // 16 * 16
-    return (r0 + 2 * rope + 15) // 16 * 16
+    """Bytes of one NVFP4 latent cache row: kv_lora e2m1 values, the rope values in e4m3, kv_lora / 16 e4m3
+    block scales, padded to 16 bytes (352 at kv_lora 512, rope 64; `reference.mla_fp4_pack` writes it)."""
+    return (kv_lora // 2 + rope + kv_lora // 16 + 15) // 16 * 16
 
 
 def mla_decode(q: torch.Tensor, latent: torch.Tensor, block_tables, seq_lens, q_start, scale: float, kv_lora: int,

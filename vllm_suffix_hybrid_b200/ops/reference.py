@@ -329,17 +329,60 @@ def nvfp4_w4a4_linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tenso
     return (xa @ wv.t()) * a_scale[:, None] * float(global_scale.reshape(-1)[0])
 
 
+def e4m3_qdq(x: torch.Tensor) -> torch.Tensor:
+    """Values rounded to e4m3 (nearest even, saturating at +-448), as fp32."""
+    return x.float().clamp(-448.0, 448.0).to(torch.float8_e4m3fn).float()
+
+
+def _mla_fp4_blocks(c: torch.Tensor):
+    """Block scales (e4m3, [N, 16-value blocks]) and e2m1 codes ([N, Cl]) of latent rows c [N, Cl]:
+    s = e4m3(max(amax16 / 6, 2^-9)), code = e2m1_rne(x * (1 / s))."""
+    x = c.float().reshape(c.shape[0], -1, 16)
+    s = (x.abs().amax(-1) / 6.0).clamp(2.0 ** -9, 448.0).to(torch.float8_e4m3fn)
+    codes = e2m1_codes(x * (1.0 / s.float())[..., None])
+    return s, codes.reshape(c.shape[0], -1)
+
+
 def mla_fp4_qdq(c: torch.Tensor) -> torch.Tensor:
-    """Latent values as the NVFP4 latent cache returns them: per 16 values s = e4m3(amax / 6), code =
-    e2m1_rne(x * (1 / s)), value = code * s (fp32)."""
+    """Latent values as the NVFP4 latent cache returns them (code * s, fp32)."""
     shape = c.shape
-    x = c.float().reshape(-1, 16)
-    s = (x.abs().amax(-1) / 6.0).to(torch.float8_e4m3fn).float()
-    inv = torch.where(s > 0, 1.0 / torch.where(s > 0, s, torch.ones_like(s)), torch.zeros_like(s))
-    codes = e2m1_codes(x * inv[:, None])
+    s, codes = _mla_fp4_blocks(c.reshape(-1, shape[-1]))
     mag = E2M1.to(c.device)[(codes & 7).long()]
-    val = torch.where(codes & 8 > 0, -mag, mag) * s[:, None]
+    val = torch.where(codes & 8 > 0, -mag, mag).view(codes.shape[0], -1, 16) * s.float()[..., None]
     return val.reshape(shape)
+
+
+def mla_fp4_scale_pos(kv_lora: int) -> torch.Tensor:
+    """Byte of block scale s inside the row's scale region: (kv_lora / 64) * (s % 4) + s // 4 (a bijection
+    on the kv_lora / 16 scales; 8 * (s % 4) + s // 4 at kv_lora 512)."""
+    s = torch.arange(kv_lora // 16)
+    return (kv_lora // 64) * (s % 4) + s // 4
+
+
+def mla_fp4_pack(c: torch.Tensor, kpe: torch.Tensor) -> torch.Tensor:
+    """NVFP4 latent cache rows [N, row_bytes] (uint8) of latent c [N, Cl] and rope kpe [N, R]: e2m1 pairs
+    (low nibble = even dim), the rope values in e4m3, the permuted block scales, zero padding to 16 bytes.
+    The row of vLLM's nvfp4_ds_mla cache (reference: kernels-oxide/nvfp4_ds_mla/src/main.rs:11-20)."""
+    N, Cl = c.shape
+    R = kpe.shape[1]
+    s, codes = _mla_fp4_blocks(c)
+    rows = torch.zeros(N, (Cl // 2 + R + Cl // 16 + 15) // 16 * 16, dtype=torch.uint8)
+    rows[:, :Cl // 2] = codes[:, 0::2] | (codes[:, 1::2] << 4)
+    rows[:, Cl // 2:Cl // 2 + R] = e4m3_qdq(kpe).to(torch.float8_e4m3fn).view(torch.uint8)
+    rows[:, Cl // 2 + R + mla_fp4_scale_pos(Cl)] = s.view(torch.uint8)
+    return rows
+
+
+def mla_fp4_unpack(rows: torch.Tensor, kv_lora: int, rope: int) -> torch.Tensor:
+    """Values [N, kv_lora + rope] (fp32) that NVFP4 latent rows hold."""
+    N = rows.shape[0]
+    codes = torch.stack([rows[:, :kv_lora // 2] & 15, rows[:, :kv_lora // 2] >> 4], -1).view(N, kv_lora).long()
+    mag = E2M1[codes & 7]
+    base = kv_lora // 2 + rope
+    s = rows[:, base + mla_fp4_scale_pos(kv_lora)].contiguous().view(torch.float8_e4m3fn).float()
+    lat = (torch.where(codes & 8 > 0, -mag, mag).view(N, -1, 16) * s[..., None]).view(N, kv_lora)
+    pe = rows[:, kv_lora // 2:base].contiguous().view(torch.float8_e4m3fn).float()
+    return torch.cat([lat, pe], -1)
 
 
 # ----------------------------------------------------------------------------- MXFP8 (W8A8, block 32)
