@@ -1,5 +1,7 @@
 // Python bindings of the sm_100a kernel library (module `_C`).
 #include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAFunctions.h>
+#include <cstring>
 #include <torch/extension.h>
 
 #include "gemm_tcgen05.h"
@@ -8,6 +10,7 @@
 #include "gdn.h"
 #include "moe.h"
 #include "mla.h"
+#include "hisparse.h"
 #include "dsa_indexer.h"
 #include "gemm_fp4mma.h"
 #include "gemm_nvfp4.h"
@@ -363,6 +366,103 @@ void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor latent, torch:
   }
   const int r = sh_mla_decode(&p, C, V, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(r == 0, "sh_mla_decode failed with code ", r, " (C=", C, ", V=", V, ")");
+}
+
+// Pinned host memory mapped into the device address space, as a CUDA uint8 tensor over the device-side
+// pointer: kernels read and write it over the host link (zero-copy).  Zero-filled; freed with the tensor.
+torch::Tensor mapped_host_buffer(int64_t nbytes) {
+  TORCH_CHECK(nbytes > 0, "mapped_host_buffer: size");
+  void* h = nullptr;
+  cudaError_t e = cudaHostAlloc(&h, static_cast<size_t>(nbytes), cudaHostAllocMapped | cudaHostAllocPortable);
+  TORCH_CHECK(e == cudaSuccess, "cudaHostAlloc(", nbytes, " bytes) failed: ", cudaGetErrorString(e));
+  void* d = nullptr;
+  e = cudaHostGetDevicePointer(&d, h, 0);
+  if (e != cudaSuccess) {
+    cudaFreeHost(h);
+    TORCH_CHECK(false, "cudaHostGetDevicePointer failed: ", cudaGetErrorString(e));
+  }
+  std::memset(h, 0, static_cast<size_t>(nbytes));
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, c10::cuda::current_device());
+  return torch::from_blob(d, {nbytes}, [h](void*) { cudaFreeHost(h); }, opts);
+}
+
+void hisparse_resolve(torch::Tensor topk, torch::Tensor topk_out, torch::Tensor q_start, torch::Tensor seq_lens,
+                      torch::Tensor state_slots, torch::Tensor positions, torch::Tensor slot_mapping,
+                      torch::Tensor block_tables, torch::Tensor cold, torch::Tensor hot, torch::Tensor pos2slot,
+                      torch::Tensor slot2pos, torch::Tensor stamp, torch::Tensor clock, torch::Tensor hot_bt,
+                      torch::Tensor hot_seq, torch::Tensor err, c10::optional<torch::Tensor> stats) {
+  const int64_t B = seq_lens.size(0), T = topk.size(0);
+  TORCH_CHECK(topk.scalar_type() == at::kInt && topk_out.scalar_type() == at::kInt && topk.is_contiguous() &&
+                  topk_out.is_contiguous() && topk_out.size(0) >= T && topk_out.size(1) == topk.size(1),
+              "hisparse: top-k lists int32 [T, K]");
+  TORCH_CHECK(q_start.scalar_type() == at::kLong && seq_lens.scalar_type() == at::kLong &&
+                  state_slots.scalar_type() == at::kLong && positions.scalar_type() == at::kLong &&
+                  slot_mapping.scalar_type() == at::kLong && q_start.size(0) == B + 1 && state_slots.size(0) >= B &&
+                  positions.size(0) >= T && slot_mapping.size(0) >= T,
+              "hisparse: int64 batch metadata");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.stride(1) == 1 && block_tables.size(0) >= B,
+              "hisparse: block tables int32");
+  const int64_t row_bytes = cold.numel() / (cold.size(0) * cold.size(1)) * cold.element_size();
+  TORCH_CHECK(cold.is_contiguous() && hot.is_contiguous() && cold.size(1) == 64 && hot.size(1) == 64 &&
+                  cold.scalar_type() == hot.scalar_type() && hot.numel() * hot.element_size() % row_bytes == 0 &&
+                  hot.numel() / (hot.size(0) * hot.size(1)) * hot.element_size() == row_bytes,
+              "hisparse: cold and hot caches [blocks, 64, row] of one row format");
+  TORCH_CHECK(pos2slot.scalar_type() == at::kInt && slot2pos.scalar_type() == at::kInt &&
+                  stamp.scalar_type() == at::kInt && clock.scalar_type() == at::kInt && pos2slot.is_contiguous() &&
+                  slot2pos.is_contiguous() && stamp.is_contiguous() && pos2slot.dim() == 2 && slot2pos.dim() == 2 &&
+                  stamp.sizes() == slot2pos.sizes() && clock.size(0) == slot2pos.size(0) &&
+                  pos2slot.size(0) == slot2pos.size(0),
+              "hisparse: residency maps int32 [slots, P], [slots, H]");
+  const int64_t H = slot2pos.size(1);
+  TORCH_CHECK(hot.size(0) * 64 >= slot2pos.size(0) * H, "hisparse: hot rows < slots x H");
+  TORCH_CHECK(hot_bt.scalar_type() == at::kInt && hot_bt.is_contiguous() && hot_bt.numel() >= B * (H / 64) &&
+                  hot_seq.scalar_type() == at::kLong && hot_seq.size(0) >= B && err.scalar_type() == at::kInt,
+              "hisparse: outputs");
+  HsParams p{};
+  p.topk = topk.data_ptr<int32_t>();
+  p.topk_out = topk_out.data_ptr<int32_t>();
+  p.q_start = q_start.data_ptr<int64_t>();
+  p.seq_lens = seq_lens.data_ptr<int64_t>();
+  p.state_slots = state_slots.data_ptr<int64_t>();
+  p.positions = positions.data_ptr<int64_t>();
+  p.slot_mapping = slot_mapping.data_ptr<int64_t>();
+  p.block_tables = block_tables.data_ptr<int32_t>();
+  p.bt_stride = block_tables.stride(0);
+  p.cold = reinterpret_cast<const uint8_t*>(cold.data_ptr());
+  p.hot = reinterpret_cast<uint8_t*>(hot.data_ptr());
+  p.pos2slot = pos2slot.data_ptr<int32_t>();
+  p.slot2pos = slot2pos.data_ptr<int32_t>();
+  p.stamp = stamp.data_ptr<int32_t>();
+  p.clock = clock.data_ptr<int32_t>();
+  p.hot_bt = hot_bt.data_ptr<int32_t>();
+  p.hot_seq = hot_seq.data_ptr<int64_t>();
+  p.err = err.data_ptr<int>();
+  if (stats) {
+    TORCH_CHECK(stats->scalar_type() == at::kLong && stats->numel() >= 2, "hisparse: stats int64 [2]");
+    p.stats = stats->data_ptr<int64_t>();
+  }
+  p.B = static_cast<int>(B);
+  p.K = static_cast<int>(topk.size(1));
+  p.H = static_cast<int>(H);
+  p.P = static_cast<int>(pos2slot.size(1));
+  p.row_bytes = static_cast<int>(row_bytes);
+  const int r = sh_hisparse_resolve(&p, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_hisparse_resolve failed with code ", r);
+}
+
+void hisparse_reset(torch::Tensor pos2slot, torch::Tensor slot2pos, torch::Tensor stamp, torch::Tensor clock,
+                    torch::Tensor slots) {
+  TORCH_CHECK(pos2slot.dim() == 3 && slot2pos.dim() == 3 && pos2slot.is_contiguous() && slot2pos.is_contiguous() &&
+                  stamp.is_contiguous() && clock.is_contiguous() && stamp.sizes() == slot2pos.sizes() &&
+                  clock.size(0) == pos2slot.size(0) && clock.size(1) == pos2slot.size(1) &&
+                  slots.scalar_type() == at::kLong && pos2slot.scalar_type() == at::kInt,
+              "hisparse_reset: maps [layers, slots, P] / [layers, slots, H] int32, slots int64");
+  const int r = sh_hisparse_reset(pos2slot.data_ptr<int32_t>(), slot2pos.data_ptr<int32_t>(), stamp.data_ptr<int32_t>(),
+                                  clock.data_ptr<int32_t>(), slots.data_ptr<int64_t>(), static_cast<int>(slots.numel()),
+                                  static_cast<int>(pos2slot.size(0)), static_cast<int>(pos2slot.size(1)),
+                                  static_cast<int>(slot2pos.size(2)), static_cast<int>(pos2slot.size(2)),
+                                  at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(r == 0, "sh_hisparse_reset failed with code ", r);
 }
 
 void mla_cache_write(torch::Tensor latent, torch::Tensor c, torch::Tensor kpe, torch::Tensor slots) {
@@ -1010,6 +1110,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("prefetch_bytes") = 0);
   m.def("mla_decode", &mla_decode);
   m.def("mla_cache_write", &mla_cache_write);
+  m.def("mapped_host_buffer", &mapped_host_buffer);
+  m.def("hisparse_resolve", &hisparse_resolve, py::arg("topk"), py::arg("topk_out"), py::arg("q_start"),
+        py::arg("seq_lens"), py::arg("state_slots"), py::arg("positions"), py::arg("slot_mapping"),
+        py::arg("block_tables"), py::arg("cold"), py::arg("hot"), py::arg("pos2slot"), py::arg("slot2pos"),
+        py::arg("stamp"), py::arg("clock"), py::arg("hot_bt"), py::arg("hot_seq"), py::arg("err"),
+        py::arg("stats") = py::none());
+  m.def("hisparse_reset", &hisparse_reset);
   m.def("dsa_cache_write", &dsa_cache_write);
   m.def("dsa_quant_q", &dsa_quant_q);
   m.def("dsa_index", &dsa_index);

@@ -201,6 +201,11 @@ class CacheConfig:
     num_blocks: int = 0  # 0: size from free memory
     gpu_memory_fraction: float = 0.85
     max_model_len: int = 4096
+    # host KV tier (DSA sparse-attention models on CUDA): latent rows in mapped host memory, hot rows on the
+    # device (engine/host_tier.py); hot_rows 0 = (k + 2) x top-k; host_kv_gb caps the host pool
+    host_kv: bool = False
+    host_kv_hot_rows: int = 0
+    host_kv_gb: float = 64.0
 
 
 @dataclass
@@ -245,4 +250,9 @@ def apply_env(cfg: EngineConfig) -> EngineConfig:
     v = _env("MAX_SPEC_TOKENS")
     if v is not None and v.isdigit() and int(v) > 0:
         cfg.spec.k = int(v)
+    if _env("HOST_KV") == "1":
+        cfg.cache.host_kv = True
+    v = _env("HOST_KV_HOT_ROWS")
+    if v is not None and v.isdigit():
+        cfg.cache.host_kv_hot_rows = int(v)
     return cfg

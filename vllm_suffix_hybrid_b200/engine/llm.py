@@ -129,10 +129,19 @@ class LLMEngine:
         self.block_size = bs
         self.max_model_len = cfg.cache.max_model_len
         self.max_blocks_per_seq = blocks_for(self.max_model_len + 2 * self.k + 2, bs)
+        self.host_tier = None
+        if cfg.cache.host_kv:
+            from .host_tier import hot_rows_for
+
+            if not hasattr(self.model, "enable_host_kv"):
+                raise ValueError("the host KV tier needs a DSA sparse-attention model (DeepSeek-V3.2 shape)")
+            self.model.enable_host_kv(cfg.cache.host_kv_hot_rows or hot_rows_for(self.k, mcfg.dsa_topk),
+                                      self.max_model_len + 2 * self.k + 2, cfg.max_num_seqs * (self.k + 1))
         num_blocks = cfg.cache.num_blocks or self._auto_blocks()
         self.pool = BlockPool(num_blocks)
         if hasattr(self.model, "allocate_caches"):
             self.caches = self.model.allocate_caches(num_blocks, bs, cfg.max_num_seqs + 1, self.k + 1)
+            self.host_tier = getattr(self.model, "host_tier", None)
         else:
             self.caches = allocate_caches(mcfg.layers, self.model.kv_cache_shape(num_blocks, bs), self.model.dtype,
                                           dev)
@@ -209,6 +218,11 @@ class LLMEngine:
             per_block = 2 * self.block_size * m.kv_heads_local * c.model.head_dim * m.embed.element_size()
             per_block *= kv_layers + (1 if self.draft is not None else 0)
         budget = int(free * c.cache.gpu_memory_fraction) - (4 << 30)
+        if c.cache.host_kv and hasattr(m, "latent_block_bytes"):  # latent rows in host memory, hot rows on device
+            hot = m.host_kv[0] * (c.max_num_seqs + 1) * m.latent_block_bytes(1) * kv_layers
+            budget -= hot
+            host = int(c.cache.host_kv_gb * (1 << 30)) // (m.latent_block_bytes(self.block_size) * kv_layers)
+            return max(self.max_blocks_per_seq + 9, min(budget // max(per_block, 1), host, 4 * need))
         return max(self.max_blocks_per_seq + 9, min(budget // per_block, 4 * need))
 
     # ------------------------------------------------------------------ API

@@ -139,7 +139,8 @@ class MLAttention:
         return self.lora + self.rope
 
     def __call__(self, x: torch.Tensor, meta: AttnMeta, cache) -> torch.Tensor:
-        latent, icache = cache
+        latent, icache = cache[0], cache[1]
+        tier = cache[2] if len(cache) > 2 else None  # host KV tier: `latent` is the host-resident cache
         T = x.shape[0]
         qa = self.q_a_norm(self.q_a(x)) if self.q_a is not None else x
         q = self.q_b(qa).view(T, self.H, self.nope + self.rope)
@@ -163,8 +164,12 @@ class MLAttention:
             q_lat = torch.bmm(q[..., : self.nope].transpose(0, 1), w_uk).transpose(0, 1)
             qf = torch.cat([q_lat, q_pe.to(q_lat.dtype)], -1).contiguous()
             keys = meta.block_tables.shape[1] * latent.shape[1]
-            o_lat = ops.mla_decode(qf, latent, meta.block_tables, meta.seq_lens, meta.q_start, self.scale, self.lora,
-                                   topk, ops.mla_splits(T, self.H, self.itopk if self.dsa else keys))
+            lat, bt, seq, tk = latent, meta.block_tables, meta.seq_lens, topk
+            if tier is not None and topk is not None and meta.window > 0:
+                # decode: the selected keys' rows are resolved into this layer's hot rows on the device
+                lat, bt, seq, tk = tier.resolve(topk.to(torch.int32).contiguous(), meta)
+            o_lat = ops.mla_decode(qf, lat, bt, seq, meta.q_start, self.scale, self.lora, tk,
+                                   ops.mla_splits(T, self.H, self.itopk if self.dsa else keys))
             o = torch.bmm(o_lat.transpose(0, 1), w_uv.transpose(1, 2)).transpose(0, 1)
             return self.o(o.reshape(T, self.H * self.vd).contiguous())
         q_lat = torch.einsum("thn,hnc->thc", q[..., : self.nope].float(), w_uk.float())
@@ -205,6 +210,8 @@ class DeepseekModel:
         self.lm_head = Linear(cfg.hidden, cfg.vocab, self.dtype, device, gen)
         self.vocab_offset = 0
         self.num_kv_layers = cfg.layers
+        self.host_kv = None  # (hot rows, max positions, max decode tokens) with the host KV tier
+        self.host_tier = None
 
     @property
     def kv_heads_local(self) -> int:
@@ -216,17 +223,41 @@ class DeepseekModel:
     def _kv_fp4(self) -> bool:
         return self.cfg.kv_format == "nvfp4" and torch.device(self.device).type == "cuda"
 
-    def kv_block_bytes(self, block_size: int) -> int:
-        """Device bytes one KV block takes in one layer: the latent rows (NVFP4 or model dtype) and, with the
-        DSA indexer, its key page."""
+    def _latent_row(self):
+        """(row shape, dtype) of one latent cache row: NVFP4 bytes or kv_lora + rope values."""
         if self._kv_fp4():
-            row = ops.mla_fp4_row_bytes(self.cfg.kv_lora, self.cfg.qk_rope)
-        else:
-            row = (self.cfg.kv_lora + self.cfg.qk_rope) * self.embed.element_size()
-        return block_size * row + (ops.DSA_PAGE_BYTES if self.cfg.dsa_topk else 0)
+            return (ops.mla_fp4_row_bytes(self.cfg.kv_lora, self.cfg.qk_rope),), torch.uint8
+        return (self.cfg.kv_lora + self.cfg.qk_rope,), self.dtype
+
+    def latent_block_bytes(self, block_size: int) -> int:
+        shape, dt = self._latent_row()
+        return block_size * shape[0] * torch.empty(0, dtype=dt).element_size()
+
+    def kv_block_bytes(self, block_size: int) -> int:
+        """Device bytes one KV block takes in one layer: the latent rows (NVFP4 or model dtype; on the host
+        with the host KV tier) and, with the DSA indexer, its key page."""
+        lat = 0 if self.host_kv is not None else self.latent_block_bytes(block_size)
+        return lat + (ops.DSA_PAGE_BYTES if self.cfg.dsa_topk else 0)
+
+    def enable_host_kv(self, hot_rows: int, max_positions: int, max_tokens: int) -> None:
+        """Keep the target layers' latent caches in host memory with `hot_rows` device rows per request slot
+        and layer (engine/host_tier.py); needs the DSA indexer (the hot rows hold each step's top-k keys)."""
+        if not self.cfg.dsa_topk or torch.device(self.device).type != "cuda":
+            raise ValueError("the host KV tier needs a DSA sparse-attention model on CUDA")
+        self.host_kv = (hot_rows, max_positions, max_tokens)
 
     def allocate_caches(self, num_blocks: int, block_size: int, slots: int, window: int,
                         n_layers: int | None = None) -> List:
+        if self.host_kv is not None and n_layers is None:  # the target's layers (the MTP layer stays on device)
+            from ..engine.host_tier import HostKVTier
+
+            hot_rows, max_pos, max_tok = self.host_kv
+            shape, dt = self._latent_row()
+            tier = HostKVTier(len(self.layers), num_blocks, block_size, shape, dt, slots, hot_rows, max_pos, max_tok,
+                              self.cfg.dsa_topk, self.device)
+            self.host_tier = tier
+            return [(tier.cold[i], ops.dsa_cache_alloc(num_blocks, block_size, self.device), tier.layer(i))
+                    for i in range(len(self.layers))]
         caches = []
         fp4 = self._kv_fp4()
         for _ in range(len(self.layers) if n_layers is None else n_layers):
@@ -241,6 +272,8 @@ class DeepseekModel:
         return caches
 
     def forward(self, ids, meta: AttnMeta, caches, embeds=None):
+        if self.host_tier is not None and meta.window == 0 and meta.state_slots is not None:
+            self.host_tier.reset(meta.state_slots)  # prefill: these slots start new requests
         residual = ops.embedding(ids, self.embed) if embeds is None else embeds
         x = ops.rms_norm(residual, self.layers[0].input_norm.weight, self.cfg.norm_eps)
         for i, layer in enumerate(self.layers):
@@ -274,7 +307,9 @@ class DeepseekMtp:
         self.norm = RMSNorm(cfg.hidden, cfg.norm_eps, dt, device)
 
     def kv_block_bytes(self, block_size: int) -> int:
-        return self.target.kv_block_bytes(block_size)
+        # the MTP layer's cache is on the device even with the target's host KV tier
+        t = self.target
+        return t.latent_block_bytes(block_size) + (ops.DSA_PAGE_BYTES if self.cfg.dsa_topk else 0)
 
     def allocate_caches(self, num_blocks: int, block_size: int):
         return self.target.allocate_caches(num_blocks, block_size, 0, 0, n_layers=1)[0]
