@@ -216,6 +216,9 @@ class EngineConfig:
     cache: CacheConfig = field(default_factory=CacheConfig)
     max_num_seqs: int = 64
     max_prefill_tokens: int = 16384
+    # a prompt longer than max_prefill_tokens is prefilled in chunks of that size, alternating with decode
+    # steps of the running requests (attention-only models; recurrent-state models prefill it whole)
+    chunked_prefill: bool = True
     device: str = "cuda"
     seed: int = 0
     cuda_graphs: bool = True
@@ -250,6 +253,8 @@ def apply_env(cfg: EngineConfig) -> EngineConfig:
     v = _env("MAX_SPEC_TOKENS")
     if v is not None and v.isdigit() and int(v) > 0:
         cfg.spec.k = int(v)
+    if _env("CHUNKED_PREFILL") in ("0", "1"):
+        cfg.chunked_prefill = _env("CHUNKED_PREFILL") == "1"
     if _env("HOST_KV") == "1":
         cfg.cache.host_kv = True
     v = _env("HOST_KV_HOT_ROWS")

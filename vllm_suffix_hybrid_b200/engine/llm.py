@@ -1,8 +1,11 @@
 """Public engine API: add requests, step, generate.
 
-A step either prefills newly admitted requests (all of them, in chunks of
-``max_prefill_tokens``) or runs one speculative decode step for every
-running request.  After each step the proposer picks the next drafts:
+A step either prefills newly admitted requests (batched up to
+``max_prefill_tokens`` prompt tokens), prefills the next ``max_prefill_tokens``
+chunk of one longer prompt (such chunks alternate with decode steps, so a long
+prompt does not stall the running requests), or runs one speculative decode
+step for every running request.  After each step the proposer picks the next
+drafts:
 
 * ``hybrid``  -- native drafts (EAGLE/MTP head) mixed with the suffix corpus
   by the native HybridMixer (legacy split or diverge), fed the verified
@@ -70,6 +73,7 @@ class Request:
     stop_ids: frozenset = frozenset()  # generation ends after the first of these tokens
     finish_reason: str = ""  # "length" | "stop" | "abort"
     polled: int = 0  # output tokens already handed out by poll()
+    prefilled: int = 0  # prompt tokens in the cache while a long prompt is prefilled in chunks
 
     @property
     def history_len(self) -> int:
@@ -157,6 +161,8 @@ class LLMEngine:
         self.tokens = np.zeros((cfg.max_num_seqs, self.max_model_len + 2 * self.k + 2), dtype=np.int64)
         self.running: List[Request] = []
         self.waiting: List[Request] = []
+        self.prefilling: Optional[Request] = None  # a long prompt being prefilled in chunks
+        self._last_kind = ""  # "chunk" after a chunked-prefill step, "decode" after a decode step
         self.finished: Dict[str, Request] = {}
         self._ids = itertools.count()
         self.stats: List[StepStats] = []
@@ -232,7 +238,8 @@ class LLMEngine:
         p = np.asarray(prompt, dtype=np.int64)
         if len(p) == 0 or len(p) + max_new_tokens > self.max_model_len:
             raise ValueError("prompt empty or prompt + max_new_tokens exceeds max_model_len")
-        if rid in self.finished or any(r.rid == rid for r in self.running) or any(r.rid == rid for r in self.waiting):
+        if (rid in self.finished or any(r.rid == rid for r in self.running) or any(r.rid == rid for r in self.waiting)
+                or (self.prefilling is not None and self.prefilling.rid == rid)):
             raise ValueError(f"duplicate request id {rid}")
         self.waiting.append(Request(rid, p, max_new_tokens, arrival=time.time(),
                                     stop_ids=frozenset(int(t) for t in (stop_token_ids or ()))))
@@ -304,6 +311,18 @@ class LLMEngine:
 
     def abort_request(self, rid: str) -> bool:
         """Stop a request; a running one leaves at this step boundary. False if unknown or done."""
+        r = self.prefilling
+        if r is not None and r.rid == rid:
+            self._drain()
+            self.prefilling = None
+            self.pool.release(r.blocks)
+            r.blocks = []
+            if r.slot:
+                self._free_slots.append(r.slot)
+                r.slot = 0
+            r.finished, r.finish_reason = True, "abort"
+            self.finished[rid] = r
+            return True
         for i, r in enumerate(self.waiting):
             if r.rid == rid:
                 self.waiting.pop(i)
@@ -325,6 +344,8 @@ class LLMEngine:
             r = next((q for q in self.running if q.rid == rid), None)
         if r is None:
             r = next((q for q in self.waiting if q.rid == rid), None)
+        if r is None and self.prefilling is not None and self.prefilling.rid == rid:
+            r = self.prefilling
         if r is None:
             raise KeyError(rid)
         new = r.output[r.polled:]
@@ -384,7 +405,7 @@ class LLMEngine:
         return dict(get()) if get else {}
 
     def has_work(self) -> bool:
-        local = bool(self.waiting or self.running or self._pipe is not None)
+        local = bool(self.waiting or self.running or self.prefilling is not None or self._pipe is not None)
         if self.dp > 1:  # data-parallel attention: every rank steps while any rank has work
             return bool(self._dp_gather([int(local)]).max())
         return local
@@ -416,15 +437,29 @@ class LLMEngine:
     def step(self) -> StepStats:
         if self.dp > 1:
             return self._dp_step()
-        free_rows = self.cfg.max_num_seqs - len(self.running)
+        # a long prompt's chunks alternate with decode steps of the running requests
+        if self.prefilling is not None and (not self.running or self._last_kind != "chunk"):
+            return self._chunk_step()
+        free_rows = self.cfg.max_num_seqs - len(self.running) - (self.prefilling is not None)
         # a waiting request is prefilled once a row is free and the KV blocks not promised to running requests
         # cover it (otherwise the running ones decode on, without breaking the decode pipeline, until they do)
         if self.waiting and free_rows > 0 and (not self.running or
                                                self._reservation(self.waiting[0]) <= self._unclaimed_blocks()):
-            self._drain()
-            batch = self._select_prefill(self.cfg.max_num_seqs - len(self.running))
-            if batch:
-                return self._prefill_step(0, batch)
+            if self._chunkable(self.waiting[0]):
+                r0 = self.waiting[0]
+                if not self.running and self._reservation(r0) > self._unclaimed_blocks():
+                    raise MemoryError(f"request {r0.rid} needs {self._reservation(r0)} KV blocks, the pool has "
+                                      f"{self.pool.free} free")
+                if self.prefilling is None:
+                    self._drain()
+                    self.prefilling = self.waiting.pop(0)
+                    return self._chunk_step()
+            else:
+                self._drain()
+                batch = self._select_prefill(free_rows)
+                if batch:
+                    return self._prefill_step(0, batch)
+        self._last_kind = "decode"
         decode = self._decode_step_async if self._async else self._decode_step
         sp = self.step_profiler
         if sp is not None:
@@ -467,7 +502,47 @@ class LLMEngine:
     def _unclaimed_blocks(self) -> int:
         """Free blocks not yet promised to a running request's remaining growth."""
         owed = sum(max(0, self._reservation(r) - len(r.blocks)) for r in self.running)
+        if self.prefilling is not None:
+            owed += max(0, self._reservation(self.prefilling) - len(self.prefilling.blocks))
         return self.pool.free - owed
+
+    def _chunkable(self, r: Request) -> bool:
+        """Whether r's prompt is prefilled in chunks (longer than the prefill budget, attention-only model,
+        no data-parallel lockstep)."""
+        return (self.cfg.chunked_prefill and len(r.prompt) > self.cfg.max_prefill_tokens and self.dp == 1
+                and not self.runner.recurrent)
+
+    def _chunk_step(self) -> StepStats:
+        """Prefill the next max_prefill_tokens of the long prompt; its last chunk makes it a running request."""
+        t0 = time.perf_counter()
+        r = self.prefilling
+        self._drain()
+        if not r.slot:
+            r.slot = self._free_slots.pop()
+        s = r.prefilled
+        e = min(len(r.prompt), s + self.cfg.max_prefill_tokens)
+        final = e == len(r.prompt)
+        self._ensure_blocks(r, e + (2 * self.k + 2 if final else 0))
+        first, natives = self.runner.prefill([r.prompt[s:e]], [r.blocks], [r.slot], starts=[s],
+                                             follow=[None if final else int(r.prompt[e])], drafts=final)
+        r.prefilled = e
+        self._last_kind = "chunk"
+        prop_us = 0.0
+        if final:
+            self.prefilling = None
+            row = len(self.running)
+            self.running.append(r)
+            self.tokens[row, :len(r.prompt)] = r.prompt
+            r.committed = len(r.prompt)
+            self._emit(r, row, [int(first[0])])
+            r.drafts = [int(x) for x in natives[0][: self.k]]
+        t1 = time.perf_counter()
+        if final:
+            prop_us = self._propose(batch_native=True)
+            self._retire()
+        st = StepStats("prefill", 1, 1 if final else 0, 0, (t1 - t0) * 1e3, 0.0, prop_us)
+        self.stats.append(st)
+        return st
 
     def _select_prefill(self, free_rows: int) -> list:
         """Waiting requests to prefill, in arrival order, within the prefill token budget and the KV blocks

@@ -332,16 +332,26 @@ class Runner:
 
     # ------------------------------------------------------------------ prefill
     def prefill(self, prompts: List[np.ndarray], block_tables: List[List[int]],
-                state_slots: Optional[List[int]] = None, hidden_only: bool = False, features: bool = False):
-        """Prefill a batch of prompts (each fully). Returns (first tokens [n], native drafts [n, k]); with
+                state_slots: Optional[List[int]] = None, hidden_only: bool = False, features: bool = False,
+                starts: Optional[List[int]] = None, follow: Optional[List[Optional[int]]] = None,
+                drafts: bool = True):
+        """Prefill a batch of prompts. Returns (first tokens [n], native drafts [n, k]); with
         hidden_only the final normalised hidden state at each prompt's last position [n, H] (scoring);
         with features the target's pre-norm hidden state at every prompt position [sum(len), H] (the draft
-        head's input features, for its training replay)."""
+        head's input features, for its training replay).
+
+        Chunked prefill: prompts[i] may be the chunk of a longer prompt whose first starts[i] tokens are
+        already in the cache (attention-only models); follow[i] is then the prompt token after the chunk
+        (the draft head's input at the chunk's last position), or None for a chunk that ends the prompt.
+        drafts=False skips the native draft steps (a chunk that does not end its prompt)."""
         dev = self.device
         n = len(prompts)
         lens = [len(p) for p in prompts]
+        starts = [0] * n if starts is None else [int(s) for s in starts]
+        if self.recurrent and any(starts):
+            raise ValueError("chunked prefill needs an attention-only model (recurrent states prefill whole)")
         ids = torch.from_numpy(np.concatenate(prompts).astype(np.int64)).to(dev, non_blocking=True)
-        pos = torch.from_numpy(np.concatenate([np.arange(l) for l in lens]).astype(np.int64)).to(dev)
+        pos = torch.from_numpy(np.concatenate([np.arange(s, s + l) for s, l in zip(starts, lens)]).astype(np.int64)).to(dev)
         mb = max(len(b) for b in block_tables)
         btn = np.zeros((n, mb), dtype=np.int32)
         for i, b in enumerate(block_tables):
@@ -350,7 +360,7 @@ class Runner:
         req_of_tok = torch.from_numpy(np.concatenate([np.full(l, i) for i, l in enumerate(lens)])).to(dev)
         blk = bt.long()[req_of_tok, torch.div(pos, self.bs, rounding_mode="floor")]
         slots = blk * self.bs + pos % self.bs
-        seq_lens = torch.tensor(lens, dtype=torch.long, device=dev)
+        seq_lens = torch.tensor([s + l for s, l in zip(starts, lens)], dtype=torch.long, device=dev)
         qs = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.long, device=dev)
         tr, t0 = ops.plan_attention_tiles(lens, self.group)
         meta = AttnMeta(positions=pos, slot_mapping=slots, block_tables=bt, seq_lens=seq_lens, q_start=qs,
@@ -374,8 +384,14 @@ class Runner:
             nxt = torch.empty_like(ids)
             nxt[:-1] = ids[1:]
             nxt[last] = first  # the token after each prompt's last position
+            if follow is not None and any(f is not None for f in follow):
+                ends = qs[1:].cpu().numpy() - 1
+                for i, f in enumerate(follow):
+                    if f is not None:
+                        nxt[int(ends[i])] = int(f)
             dh, dpre = self.draft.forward(nxt, pre, meta, self.dcaches)
-            d1 = self.model.greedy(dh.index_select(0, last))
-            f1 = dpre.index_select(0, last)
-            natives = self._draft_steps(d1, f1, seq_lens, bt, n)
+            if drafts:
+                d1 = self.model.greedy(dh.index_select(0, last))
+                f1 = dpre.index_select(0, last)
+                natives = self._draft_steps(d1, f1, seq_lens, bt, n)
         return first.cpu().numpy(), natives.cpu().numpy()
