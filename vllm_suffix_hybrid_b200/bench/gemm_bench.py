@@ -109,10 +109,17 @@ def nvfp4_main(a):
         run = lambda: ops.nvfp4_linear(x, p, s, g, out=y)
         run44 = lambda: ops.nvfp4_linear_w4a4(x, p, w_sf, s, g, out=y)
         if a.once:
-            (run44 if a.w4a4 else run)()
-            (run44 if a.w4a4 else run)()
+            if a.mxfp8:
+                c8, s8 = ops.mxfp8_quantize(w)
+                t8sf = ops.mxfp8_scale_tiles(s8)
+                run8 = lambda: ops.mxfp8_linear(x, c8, t8sf, s8, out=y)
+                run8()
+                run8()
+            else:
+                (run44 if a.w4a4 else run)()
+                (run44 if a.w4a4 else run)()
             torch.cuda.synchronize()
-            print(json.dumps({"once": name, "w4a4": bool(a.w4a4)}))
+            print(json.dumps({"once": name, "w4a4": bool(a.w4a4), "mxfp8": bool(a.mxfp8)}))
             continue
         t4 = time_fn(run, flush, a.iters)
         t44 = time_fn(run44, flush, a.iters)  # includes the activation quantiser launch
@@ -221,6 +228,7 @@ def main():
                     help="with --config sk,...: print the stream-K kernel's in-kernel phase timeline")
     ap.add_argument("--config", default="", help="force kind,swap,bn,splits,clusters (e.g. sk,1,192,2,74 or pair,0,256,1,0)")
     ap.add_argument("--w4a4", action="store_true", help="with --nvfp4 --once: launch the W4A4 kernel")
+    ap.add_argument("--mxfp8", action="store_true", help="with --nvfp4 --once: launch the MXFP8 W8A8 kernel")
     ap.add_argument("--nvfp4", action="store_true",
                     help="NVFP4-weight (W4A16) kernel vs the bf16 paths on decode shapes (packed-weight GB/s)")
     a = ap.parse_args()
