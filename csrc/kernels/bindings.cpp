@@ -673,7 +673,7 @@ void gemm_fp4mma(torch::Tensor y, torch::Tensor xq, torch::Tensor x_sf, torch::T
                  torch::Tensor w_sf, torch::Tensor alpha_w, int64_t bn, c10::optional<torch::Tensor> groups,
                  c10::optional<torch::Tensor> num_groups, int64_t rows_p, c10::optional<torch::Tensor> err,
                  int64_t splits, c10::optional<torch::Tensor> ws, c10::optional<torch::Tensor> counters,
-                 bool fp8) {
+                 bool fp8, c10::optional<torch::Tensor> stamps) {
   TORCH_CHECK(xq.is_cuda() && xq.scalar_type() == at::kByte && xq.is_contiguous() && xq.dim() == 2, "gemm_fp4mma: xq");
   TORCH_CHECK(w.scalar_type() == at::kByte && w.is_contiguous() && w.size(1) == xq.size(1), "gemm_fp4mma: w");
   // NVFP4: two codes per byte, 4 scale chunks per 256 k; MXFP8: one code per byte, one chunk per 128 k
@@ -719,6 +719,11 @@ void gemm_fp4mma(torch::Tensor y, torch::Tensor xq, torch::Tensor x_sf, torch::T
                 "gemm_fp4mma: split tickets (zeroed int32 per output tile)");
     g.ws = ws->data_ptr<float>();
     g.counters = counters->data_ptr<int>();
+  }
+  if (stamps) {
+    TORCH_CHECK(stamps->scalar_type() == at::kLong && stamps->is_cuda() && stamps->numel() >= 8 * num_sms,
+                "gemm_fp4mma: stamps int64 [num_sms * 8]");
+    g.stamps = reinterpret_cast<unsigned long long*>(stamps->data_ptr<int64_t>());
   }
   const int r = (fp8 ? sh_gemm_mxfp8 : sh_gemm_fp4mma)(&g, xq.data_ptr(), static_cast<int>(xq.size(0)),
                                                        static_cast<int>(bn), static_cast<int>(splits), num_sms,
@@ -1131,7 +1136,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("w_sf"), py::arg("alpha_w"), py::arg("bn"), py::arg("groups") = py::none(),
         py::arg("num_groups") = py::none(), py::arg("rows_p") = 0, py::arg("err") = py::none(),
         py::arg("splits") = 1, py::arg("ws") = py::none(), py::arg("counters") = py::none(),
-        py::arg("fp8") = false);
+        py::arg("fp8") = false, py::arg("stamps") = py::none());
   m.def("mxfp8_quant_act", &mxfp8_quant_act, py::arg("x"), py::arg("xq"), py::arg("x_sf"), py::arg("a_scale"),
         py::arg("tile_rows"), py::arg("groups") = py::none(), py::arg("num_groups") = py::none());
   m.def("spec_advance", &spec_advance);

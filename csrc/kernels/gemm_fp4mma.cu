@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* epi_flag = abort_flag + 1;  // epilogue broadcast word
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t t_entry = g.stamps ? now_ns() : 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -223,8 +224,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   fence_before();
   __syncthreads();
   fence_after();
+  const uint64_t t_setup = g.stamps ? now_ns() : 0;
   shk::pdl_trigger();
   shk::pdl_wait();
+  const uint64_t t_wait = g.stamps ? now_ns() : 0;
+  unsigned long long* stamp = g.stamps ? g.stamps + static_cast<int64_t>(blockIdx.x) * 8 : nullptr;
+  if (stamp && threadIdx.x == 0) {
+    stamp[0] = t_setup - t_entry;
+    stamp[1] = t_wait - t_setup;
+  }
   const uint32_t tmem_base = *tmem_slot;
   const int nkb = (g.K + KB - 1) / KB;
   const int kc4 = nkb * CPB;  // scale chunks per tile
@@ -282,6 +290,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ok = false;
             break;
           }
+          if (stamp && kcount == 0) stamp[2] = now_ns() - t_wait;
           fence_after();
           const uint32_t sa = smem_addr(smem + s * S::STAGE);
           const uint32_t sb = sa + S::A_BYTES;
@@ -339,9 +348,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int tiles = g.tiles_p * g.tiles_q;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint64_t e_wait = 0, e_part = 0, e_store = 0, e_first = 0, tq0 = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x) {
       const Work wk = decode_work(w, g, BN, nkb);
       const int nq = min(BN, wk.q_lim - wk.q_base);  // valid tokens of the tile
+      if (stamp) tq0 = now_ns();
       // token scales of the tile, fetched while the mainloop runs (the previous tile's readers passed
       // the last barrier of its iteration)
       if (et < BN) tok[et] = et < nq ? g.alpha_w[wk.expert] * g.a_scale[wk.q_base + et] : 0.f;
@@ -357,19 +368,27 @@ __global__ void __launch_bounds__(THREADS, 1)
       epi_sync();
       if (!*epi_flag) break;
       fence_after();
+      uint64_t tq1 = 0;
+      if (stamp) {
+        tq1 = now_ns();
+        e_wait += tq1 - tq0;
+        if (!e_first) e_first = tq1 - t_wait;
+      }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
       const int tile = wk.tq_tile;
       bool store = true;
       if (g.splits > 1) {
-        float* part = g.ws + (static_cast<int64_t>(wk.sp) * tiles + tile) * (BM * BN) + row * BN;
+        // Partial tiles are stored chunk-major: 16-column chunk cc of row r at floats (cc * BM + r) * 16, so a
+        // warp writes 2 KB contiguously per chunk and the reducer reads consecutive float4s across its threads.
+        const int ncc = (nq + 15) >> 4;  // column chunks holding valid tokens
+        float* part = g.ws + (static_cast<int64_t>(wk.sp) * tiles + tile) * (BM * BN);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          if (c >= nq) break;  // warp-uniform
+        for (int cc = 0; cc < ncc; ++cc) {
           float v[16];
-          tmem_ld16(tbase + c, v);
+          tmem_ld16(tbase + cc * 16, v);
+          float4* dst = reinterpret_cast<float4*>(part + (cc * BM + row) * 16);
 #pragma unroll
-          for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4*>(part + c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
         }
         fence_before();
         mbar_arrive(&tempty[acc]);
@@ -382,39 +401,54 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         epi_sync();
         store = *epi_flag != 0;
+        if (stamp) {
+          const uint64_t t2 = now_ns();
+          e_part += t2 - tq1;
+          tq1 = t2;
+        }
         if (store) {
+          // float4 f = et + 128 j of the tile (j < 4 ncc), summed over the splits in split order; eight f per
+          // round trip with up to four splits' loads in flight (32 independent loads)
+          const float4* wsv = reinterpret_cast<const float4*>(g.ws + static_cast<int64_t>(tile) * (BM * BN));
+          const int64_t sstride = static_cast<int64_t>(tiles) * (BM * BN) / 4;  // float4s between splits
+          const int nf = ncc * 4;
 #pragma unroll 1
-          for (int c = 0; c < BN; c += 16) {
-            if (c >= nq) break;
-            float v[16];
+          for (int j0 = 0; j0 < nf; j0 += 8) {
+            float4 acc4[8];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.f;
-            // four splits' 16-float slices in flight per round trip; summed in split order
+            for (int u = 0; u < 8; ++u) acc4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int s0 = 0; s0 < g.splits; s0 += 4) {
-              // unconditional loads (clamped split index) so all sixteen issue back to back
-              float4 t4[4][4];
+              float4 t4[4][8];  // [split][f]
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int su = min(s0 + u, g.splits - 1);
-                const float4* src = reinterpret_cast<const float4*>(
-                    g.ws + (static_cast<int64_t>(su) * tiles + tile) * (BM * BN) + row * BN + c);
+              for (int sp = 0; sp < 4; ++sp) {
+                const int su = min(s0 + sp, g.splits - 1);  // clamped: all loads issue back to back
 #pragma unroll
-                for (int i = 0; i < 4; ++i) t4[u][i] = __ldcg(src + i);
+                for (int u = 0; u < 8; ++u) {
+                  const int j = min(j0 + u, nf - 1);
+                  t4[sp][u] = __ldcg(wsv + su * sstride + et + 128 * j);
+                }
               }
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const float m = s0 + u < g.splits ? 1.f : 0.f;
+              for (int sp = 0; sp < 4; ++sp) {
+                const float m = s0 + sp < g.splits ? 1.f : 0.f;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  v[4 * i] += m * t4[u][i].x;
-                  v[4 * i + 1] += m * t4[u][i].y;
-                  v[4 * i + 2] += m * t4[u][i].z;
-                  v[4 * i + 3] += m * t4[u][i].w;
+                for (int u = 0; u < 8; ++u) {
+                  acc4[u].x += m * t4[sp][u].x;
+                  acc4[u].y += m * t4[sp][u].y;
+                  acc4[u].z += m * t4[sp][u].z;
+                  acc4[u].w += m * t4[sp][u].w;
                 }
               }
             }
 #pragma unroll
-            for (int i = 0; i < 16; ++i) stage[(c + i) * BM + row] = __float2bfloat16(v[i] * tok[c + i]);
+            for (int u = 0; u < 8; ++u) {
+              if (j0 + u >= nf) break;
+              const int q = 4 * (et + 128 * (j0 + u));  // float index in the chunk-major tile
+              const int cc = q >> 11, rr = (q & 2047) >> 4, col = cc * 16 + (q & 15);
+              const float a4[4] = {acc4[u].x, acc4[u].y, acc4[u].z, acc4[u].w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) stage[(col + e) * BM + rr] = __float2bfloat16(a4[e] * tok[col + e]);
+            }
           }
         }
       } else {
@@ -447,10 +481,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         epi_sync();  // the staging tile may be overwritten
       }
+      if (stamp) e_store += now_ns() - tq1;
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
+    }
+    if (stamp && et == 0) {
+      stamp[3] = e_first;
+      stamp[4] = e_wait;
+      stamp[5] = e_part;
+      stamp[6] = e_store;
+      stamp[7] = now_ns() - t_entry;
     }
   }
   if (*abort_flag && warp == 0 && lane == 0) {

@@ -32,6 +32,9 @@ struct Fp4MmaParams {
   const int4* groups;            // grouped (MoE) entries {q_row0, q_rows, p_row_offset, expert} or nullptr
   const int* num_groups;
   int max_groups;
+  unsigned long long* stamps;    // optional per-CTA timings, ns ([grid][8]; profiling): setup, PDL wait, first
+                                 // stage landed, first accumulator ready, accumulator waits, split partial
+                                 // writes + ticket, reduce + store, whole CTA
 };
 
 #ifdef __cplusplus

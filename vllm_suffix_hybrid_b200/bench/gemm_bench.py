@@ -121,6 +121,30 @@ def nvfp4_main(a):
             torch.cuda.synchronize()
             print(json.dumps({"once": name, "w4a4": bool(a.w4a4), "mxfp8": bool(a.mxfp8)}))
             continue
+        if a.stamps:  # per-CTA timings of the W4A4 kernel at 1, 2, 4 and 8 K splits (cold L2)
+            from vllm_suffix_hybrid_b200.ops.gemm import workspace
+            bn44 = 64 if M <= 64 else 128
+            xq, x_sf, a_sc = ops.nvfp4_quant_act(x, bn44)
+            gsc = g.float().reshape(-1)
+            nsm = torch.cuda.get_device_properties(0).multi_processor_count
+            ntile = -(-N // 128) * -(-M // bn44)
+            wsp = workspace(x.device, 8 * ntile * 128 * bn44)
+            cnt = ops.split_tickets(x.device, ntile)
+            keys = ["setup", "pdl_wait", "first_stage", "first_acc", "acc_waits", "split_part", "store", "cta"]
+            for sp in (1, 2, 4, 8):
+                st = torch.zeros(nsm * 8, dtype=torch.long, device="cuda")
+                for _ in range(3):
+                    flush.zero_()
+                    st.zero_()
+                    ops.native().gemm_fp4mma(y, xq, x_sf, a_sc, p, w_sf, gsc, bn44, splits=sp, ws=wsp, counters=cnt,
+                                             stamps=st)
+                torch.cuda.synchronize()
+                v = st.view(nsm, 8).cpu()
+                used = v[:, 7] > 0
+                print(json.dumps({"stamps": name, "splits": sp, "ctas": int(used.sum()),
+                                  "median_ns": dict(zip(keys, v[used].median(0).values.tolist())),
+                                  "max_ns": dict(zip(keys, v[used].max(0).values.tolist()))}))
+            continue
         t4 = time_fn(run, flush, a.iters)
         t44 = time_fn(run44, flush, a.iters)  # includes the activation quantiser launch
         bn44 = 64 if M <= 64 else 128

@@ -734,29 +734,33 @@ def nvfp4_linear_w4a4(x: torch.Tensor, packed: torch.Tensor, w_sf: torch.Tensor,
     M, K = x2.shape
     y = out.view(M, N) if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
     if M:
-        from .gemm import batch_invariant
-
         bn = 64 if M <= 64 else 128
         xq, x_sf, a_scale = nvfp4_quant_act(x2, bn, static_g)
-        tiles = -(-N // 128) * -(-M // bn)
-        nkb = -(-K // 256)
-        # split-K (SH_FP4_SPLITK=1): while the grid covers under half the SMs (batch-invariant mode: the
-        # one-token-tile choice for every M).  Off by default: on B200 the last-split reduction tail
-        # measured neutral to slower than one split on every decode shape tried.
-        t_split = -(-N // 128) if batch_invariant() else tiles
-        splits = 1
-        while os.environ.get("SH_FP4_SPLITK", "0") == "1" and t_split * splits * 2 <= 148 \
-                and nkb // (splits * 2) >= 2 and splits < 16:
-            splits *= 2
-        ws = cnt = None
-        if splits > 1:
-            from .gemm import workspace
-
-            ws = workspace(x.device, splits * tiles * 128 * bn)
-            cnt = split_tickets(x.device, tiles)
+        splits, ws, cnt = _blockscaled_split(x.device, N, M, K, bn)
         native().gemm_fp4mma(y, xq, x_sf, a_scale, packed, w_sf, global_scale.float().reshape(-1), bn,
                              splits=splits, ws=ws, counters=cnt)
     return y.view(*lead, N)
+
+
+def _blockscaled_split(dev, N: int, M: int, K: int, bn: int):
+    """(splits, workspace, tickets) of a dense block-scaled GEMM (W4A4 / MXFP8) of reduction length K.
+
+    K is split (in-kernel, the last split of a tile sums the fp32 partials in split order) while the tiles x
+    splits cover at most half the SMs and every split keeps at least 1536 of K: below that the last split's
+    reduction tail (about 5 us on B200) costs more than the shorter K loop saves (measured: a 7168-long K
+    gains from 4 splits, a 2048-long K loses from 2).  Batch-invariant mode counts weight tiles only, so the
+    split does not depend on M.  SH_FP4_SPLITK=0 turns splitting off."""
+    from .gemm import batch_invariant, workspace
+
+    tiles = -(-N // 128) * -(-M // bn)
+    splits = 1
+    if os.environ.get("SH_FP4_SPLITK", "1") != "0":
+        t_split = -(-N // 128) if batch_invariant() else tiles
+        while t_split * splits * 2 <= _num_sms(dev) and K // (splits * 2) >= 1536 and splits < 16:
+            splits *= 2
+    if splits == 1:
+        return 1, None, None
+    return splits, workspace(dev, splits * tiles * 128 * bn), split_tickets(dev, tiles)
 
 
 _TICKETS: dict = {}
@@ -868,7 +872,9 @@ def mxfp8_linear(x: torch.Tensor, codes: torch.Tensor, w_sf: torch.Tensor, scale
     if M:
         bn = 64 if M <= 64 else 128
         xq, x_sf, a_sc = mxfp8_quant_act(x2, bn)
-        native().gemm_fp4mma(y, xq, x_sf, a_sc, codes, w_sf, _ones(x.device, 1), bn, fp8=True)
+        splits, ws, cnt = _blockscaled_split(x.device, N, M, x2.shape[1], bn)
+        native().gemm_fp4mma(y, xq, x_sf, a_sc, codes, w_sf, _ones(x.device, 1), bn, splits=splits, ws=ws,
+                             counters=cnt, fp8=True)
     return y.view(*lead, N)
 
 
