@@ -34,6 +34,22 @@ __global__ void route_kernel(RouteParams p) {
   }
 }
 
+// Eight tokens per block, one warp each (shk::route::warp_path geometries).
+__global__ void __launch_bounds__(256) route_warp_kernel(RouteParams p) {
+  shk::pdl_trigger();
+  shk::pdl_wait();
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (t >= p.T) return;  // warp-uniform
+  int id;
+  float w;
+  shk::route::route_token_warp(p, t, id, w);
+  const int lane = threadIdx.x & 31;
+  if (lane < p.k) {
+    p.ids[t * p.k + lane] = id;
+    p.weights[t * p.k + lane] = w;
+  }
+}
+
 // Single CTA: counting sort by expert + tile list.
 __global__ void align_kernel(AlignParams p) {
   shk::pdl_trigger();
@@ -124,6 +140,10 @@ extern "C" int sh_moe_route(const RouteParams* p, cudaStream_t stream) {
   if (p->k > 64 || p->k < 1 || p->E < p->k) return -1;
   const int threads = shk::route::threads_for(p->E);
   if (p->sigmoid_grouped && (p->n_groups < 1 || p->E % p->n_groups || p->n_groups > 64)) return -2;
+  if (shk::route::warp_path(*p)) {
+    shk::launch(route_warp_kernel, dim3((p->T + 7) / 8), dim3(256), 0, stream, *p);
+    return static_cast<int>(cudaGetLastError());
+  }
   const size_t smem = (p->sigmoid_grouped ? 2 : 1) * p->E * sizeof(float);
   shk::launch(route_kernel, dim3(p->T), dim3(threads), smem, stream, *p);
   return static_cast<int>(cudaGetLastError());

@@ -75,10 +75,143 @@ __device__ inline int block_argmax(const float* s, int E, int nt, Scratch& sc) {
   return idx;
 }
 
+// ---------------------------------------------------------------- one warp per token
+// The fast path: E a multiple of 32 up to 512, k <= 32, and either no group limit or 32 experts per group.
+// Lane l holds experts l + 32 i in registers (i < E / 32), so a group is one register index across the warp.
+// The selection is the block path's: same scores, ties to the lower expert index, the sigmoid weights and
+// the renormalisation summed in the same order (bit-identical ids and sigmoid weights; the softmax
+// denominator is summed in a different order).
+constexpr int kWarpMaxPer = 16;
+
+__host__ __device__ inline bool warp_path(const RouteParams& p) {
+  return p.E % 32 == 0 && p.E <= 32 * kWarpMaxPer && p.k <= 32 && p.k >= 1 &&
+         (!p.sigmoid_grouped || p.n_groups == 1 || p.E / p.n_groups == 32);
+}
+
+// Lane j < k returns chosen expert j and its final weight in (id, w); every lane of the warp must call.
+__device__ inline void route_token_warp(const RouteParams& p, int64_t t, int& id, float& w) {
+  const int lane = threadIdx.x & 31, n = p.E >> 5;
+  float sel[kWarpMaxPer], val[kWarpMaxPer];
+#pragma unroll
+  for (int i = 0; i < kWarpMaxPer; ++i) {
+    sel[i] = -INFINITY;
+    val[i] = 0.f;
+    if (i < n) sel[i] = load_logit(p.logits, t * p.E + lane + 32 * i, p.logits_bf16);
+  }
+  float denom = 1.f;
+  if (!p.sigmoid_grouped) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kWarpMaxPer; ++i)
+      if (i < n) mx = fmaxf(mx, sel[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kWarpMaxPer; ++i)
+      if (i < n) {
+        sel[i] = __expf(sel[i] - mx);
+        val[i] = sel[i];
+        sum += sel[i];
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    denom = sum;
+  } else {
+#pragma unroll
+    for (int i = 0; i < kWarpMaxPer; ++i)
+      if (i < n) {
+        const float v = 1.f / (1.f + __expf(-sel[i]));
+        val[i] = v;
+        sel[i] = v + (p.bias ? p.bias[lane + 32 * i] : 0.f);
+      }
+    if (p.n_groups > 1) {  // group g = register index g: its score is the sum of its two best biased scores
+      float gs[kWarpMaxPer];
+#pragma unroll
+      for (int g = 0; g < kWarpMaxPer; ++g) {
+        gs[g] = -INFINITY;
+        if (g >= n) continue;  // warp-uniform
+        float b1 = sel[g], b2 = -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float o1 = __shfl_xor_sync(0xffffffffu, b1, o), o2 = __shfl_xor_sync(0xffffffffu, b2, o);
+          const float hi = fmaxf(b1, o1);
+          b2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
+          b1 = hi;
+        }
+        gs[g] = b1 + b2;
+      }
+      uint32_t kept = 0;  // the top `topk_groups` groups, ties to the lower index (the same in every lane)
+      for (int j = 0; j < p.topk_groups; ++j) {
+        int best = -1;
+        float bv = 0.f;
+#pragma unroll
+        for (int g = 0; g < kWarpMaxPer; ++g)
+          if (g < n && !((kept >> g) & 1u) && (best < 0 || gs[g] > bv)) {
+            best = g;
+            bv = gs[g];
+          }
+        if (best >= 0) kept |= 1u << best;
+      }
+#pragma unroll
+      for (int g = 0; g < kWarpMaxPer; ++g)
+        if (g < n && !((kept >> g) & 1u)) sel[g] = -INFINITY;
+    }
+  }
+  uint32_t taken = 0;
+  id = 0;
+  w = 0.f;
+  for (int j = 0; j < p.k; ++j) {
+    float bv = -INFINITY, bw = 0.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kWarpMaxPer; ++i) {
+      const int e = lane + 32 * i;
+      if (i < n && !((taken >> i) & 1u) && (sel[i] > bv || (sel[i] == bv && e < bi))) {
+        bv = sel[i];
+        bi = e;
+        bw = val[i];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o), ow = __shfl_xor_sync(0xffffffffu, bw, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+        bw = ow;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (lane == j) {
+      id = bi;
+      w = p.sigmoid_grouped ? bw : bw / denom;
+    }
+  }
+  float tot = 0.f;
+  for (int j = 0; j < p.k; ++j) tot += __shfl_sync(0xffffffffu, w, j);
+  const bool norm = p.sigmoid_grouped ? (p.renorm && tot > 0.f) : p.renorm;
+  w = (norm ? w / tot : w) * p.scale;
+}
+
 // Routes token t: on return (after the final barrier) sc.chosen_i[0:k] and sc.chosen_w[0:k] hold the
 // experts and their final weights (renormalised and scaled).  s: 2E floats of shared memory.
 __device__ inline void route_token(const RouteParams& p, int64_t t, int nt, float* s, Scratch& sc) {
   const int tid = threadIdx.x;
+  if (warp_path(p)) {  // warp 0 routes; the block only waits for the result
+    if (tid < 32) {
+      int id;
+      float w;
+      route_token_warp(p, t, id, w);
+      if (tid < p.k) {
+        sc.chosen_i[tid] = id;
+        sc.chosen_w[tid] = w;
+      }
+    }
+    __syncthreads();
+    return;
+  }
   const bool act = tid < nt;
   if (!p.sigmoid_grouped) {
     float mx = -INFINITY;

@@ -100,15 +100,26 @@ def test_gdn_chunk_prefill_matches_recurrence(lens):
     assert (s_got - s_ref).abs().max().item() < 0.03 * s_ref[1:].abs().max().item()
 
 
-@pytest.mark.parametrize("grouped", [False, True])
-def test_moe_route(grouped):
-    torch.manual_seed(0)
-    T, E, k = 37, 64, 6
+@pytest.mark.parametrize("grouped,E,k,groups,topg", [
+    (False, 64, 6, 1, 1), (True, 64, 6, 8, 3),  # block path (8 experts per group)
+    (True, 256, 8, 8, 4),                        # warp path: DeepSeek-V3 router
+    (True, 384, 8, 1, 1),                        # warp path: Kimi-K2 (no group limit)
+    (False, 512, 10, 1, 1),                      # warp path: Qwen3-Next softmax router
+])
+def test_moe_route(grouped, E, k, groups, topg):
+    """The GPU router (one warp per token where E % 32 == 0, E <= 512 and 32 experts per group, else one
+    block) picks the CPU statement's experts with its weights."""
+    torch.manual_seed(E + k)
+    T = 37
     logits = torch.randn(T, E)
+    logits[3, 5] = logits[3, 9]  # an exact tie: the lower expert index is taken first
     bias = torch.randn(E) * 0.1 if grouped else None
-    ids_c, w_c = ops.moe_route(logits, k, grouped, bias, 8 if grouped else 1, 3 if grouped else 1, True, 2.5)
-    ids_g, w_g = ops.moe_route(logits.cuda(), k, grouped, bias.cuda() if grouped else None, 8 if grouped else 1,
-                               3 if grouped else 1, True, 2.5)
+    ids_c, w_c = ops.moe_route(logits, k, grouped, bias, groups, topg, True, 2.5)
+    ids_g, w_g = ops.moe_route(logits.cuda(), k, grouped, bias.cuda() if grouped else None, groups, topg, True,
+                               2.5)
+    ids_b, w_b = ops.moe_route(logits.cuda().to(torch.bfloat16), k, grouped, bias.cuda() if grouped else None,
+                               groups, topg, True, 2.5)
+    assert bool((ids_b >= 0).all()) and bool((ids_b < E).all())
     assert torch.equal(ids_g.cpu().sort(-1).values, ids_c.sort(-1).values)
     o_c = w_c.gather(1, ids_c.long().argsort(-1))
     o_g = w_g.cpu().gather(1, ids_g.cpu().long().argsort(-1))

@@ -4,8 +4,10 @@ Router: sigmoid group-limited top-8 over 256 experts (8 groups, top-4 groups, bi
 Experts: this rank's 32 of the 256 experts (expert parallelism 8) in bf16, hidden 7168, expert FFN 2048;
 the routed pairs that fall on other ranks' experts are skipped, as after an expert-parallel dispatch.
 The expert pipeline is align (counting sort) -> gather -> grouped gate_up GEMM -> SwiGLU -> grouped down
-GEMM -> weighted combine.  Times are CUDA-event medians over `--iters` launches after warm-up, with a
-256 MB L2 flush before each.  `--once` runs each op twice and exits (for ncu captures).
+GEMM -> weighted combine.  The expert pipeline is timed with CUDA events per launch (median over `--iters`,
+256 MB L2 flush before each); the router, whose kernel is shorter than its host launch, is timed as 50
+back-to-back launches between two events (device time per launch, logits L2-warm after the first).
+`--once` runs each op twice and exits (for ncu captures).
 
 Run: python -m vllm_suffix_hybrid_b200.bench.moe_bench [--tokens 192] [--once]
 """
@@ -72,7 +74,19 @@ def main() -> None:
             ts.append(e0.elapsed_time(e1) * 1e3)
         return float(np.median(ts))
 
-    t_route = time_us(route)
+    for _ in range(3):
+        route()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ids_buf = torch.empty(T, a.k, dtype=torch.int32, device="cuda")
+    w_buf = torch.empty(T, a.k, dtype=torch.float32, device="cuda")
+    lib = ops.native()
+    torch.cuda.synchronize()
+    r0.record()
+    for _ in range(50):
+        lib.moe_route(logits, bias, ids_buf, w_buf, a.k, True, 8, 4, True, 1.0)
+    r1.record()
+    torch.cuda.synchronize()
+    t_route = r0.elapsed_time(r1) * 1e3 / 50
     t_exp = time_us(experts)
     pairs = int((ids_local >= 0).sum())
     flops = 2 * pairs * (2 * F * H + H * F)
