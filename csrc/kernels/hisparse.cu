@@ -9,7 +9,7 @@
 //   2. victims are chosen least recently used first among rows no key of this step uses (free rows
 //      first), through a 256-bin histogram of row ages;
 //   3. each claimed position takes a victim row, whose old position loses residency;
-//   4. one warp per fetched row copies it from host memory with 16-byte loads;
+//   4. the fetched rows are copied from host memory with 16-byte loads, four rows per warp in flight;
 //   5. the request's top-k list is rewritten as hot-row indices, in the same order, and its hot
 //      block-table row and a causal-safe length are written, so the MLA kernel reads the hot rows as an
 //      ordinary paged cache.
@@ -31,6 +31,7 @@ namespace hs {
 
 constexpr int THREADS = 1024;
 constexpr int BINS = 256;
+constexpr int UNROLL = 4;  // independent entries (or rows) per thread (or warp) and pass
 
 __device__ __forceinline__ int row_age(int32_t owner, int32_t stamp, int tick) {
   return owner < 0 ? BINS - 1 : min(BINS - 1, max(1, tick - stamp));
@@ -68,23 +69,36 @@ __global__ void __launch_bounds__(THREADS) resolve_kernel(HsParams p) {
   const int64_t n = ql * p.K;
   const int32_t* tk = p.topk + qs * p.K;
   int my_hits = 0;
-  for (int64_t e = tid; e < n; e += THREADS) {
-    const int64_t qpos = seq - ql + e / p.K;
-    const int32_t pos = tk[e];
-    if (pos < 0 || pos > qpos || pos >= p.P) continue;
-    const int32_t h = p2s[pos];
-    if (h >= 0) {
-      stp[h] = tick;
-      ++my_hits;
-      continue;
+  // UNROLL entries per thread per pass: their positions, then their residency entries, load back to back
+  for (int64_t e0 = tid; e0 < n; e0 += UNROLL * THREADS) {
+    int32_t pos[UNROLL], h[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int64_t e = e0 + u * THREADS;
+      pos[u] = -1;
+      if (e < n) {
+        const int32_t q = tk[e];
+        if (q >= 0 && q <= seq - ql + e / p.K && q < p.P) pos[u] = q;
+      }
     }
-    if (atomicCAS(&p2s[pos], -1, -2) == -1) {
-      const int j = atomicAdd(&nmiss, 1);
-      if (j < p.H) {
-        miss[j] = pos;
-      } else {
-        p2s[pos] = -1;
-        overflow = 1;
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) h[u] = pos[u] >= 0 ? p2s[pos[u]] : -1;
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      if (pos[u] < 0) continue;
+      if (h[u] >= 0) {
+        stp[h[u]] = tick;
+        ++my_hits;
+        continue;
+      }
+      if (atomicCAS(&p2s[pos[u]], -1, -2) == -1) {
+        const int j = atomicAdd(&nmiss, 1);
+        if (j < p.H) {
+          miss[j] = pos[u];
+        } else {
+          p2s[pos[u]] = -1;
+          overflow = 1;
+        }
       }
     }
   }
@@ -93,10 +107,17 @@ __global__ void __launch_bounds__(THREADS) resolve_kernel(HsParams p) {
   const int need = min(nmiss, p.H);
   // 2. victims: all rows older than the threshold age, then enough rows of that age
   if (need > 0) {
-    for (int h = tid; h < p.H; h += THREADS) {
-      const int32_t o = s2p[h], s = stp[h];
-      if (o >= 0 && s == tick) continue;
-      atomicAdd(&hist[row_age(o, s, tick)], 1);
+    for (int h0 = tid; h0 < p.H; h0 += UNROLL * THREADS) {
+      int32_t o[UNROLL], st[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int h = h0 + u * THREADS;
+        o[u] = h < p.H ? s2p[h] : 0;
+        st[u] = h < p.H ? stp[h] : tick;
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u)
+        if (!(o[u] >= 0 && st[u] == tick)) atomicAdd(&hist[row_age(o[u], st[u], tick)], 1);
     }
     __syncthreads();
     if (tid == 0) {
@@ -109,13 +130,22 @@ __global__ void __launch_bounds__(THREADS) resolve_kernel(HsParams p) {
       tb_need = need - acc;
     }
     __syncthreads();
-    for (int h = tid; h < p.H; h += THREADS) {
-      const int32_t o = s2p[h], s = stp[h];
-      if (o >= 0 && s == tick) continue;
-      const int age = row_age(o, s, tick);
-      if (age > tb || (age == tb && atomicAdd(&tb_taken, 1) < tb_need)) {
-        const int j = atomicAdd(&nvict, 1);
-        if (j < need) vict[j] = h;
+    for (int h0 = tid; h0 < p.H; h0 += UNROLL * THREADS) {
+      int32_t o[UNROLL], st[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int h = h0 + u * THREADS;
+        o[u] = h < p.H ? s2p[h] : 0;
+        st[u] = h < p.H ? stp[h] : tick;
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        if (o[u] >= 0 && st[u] == tick) continue;  // in use this step, or past the rows (o 0, stamp tick)
+        const int age = row_age(o[u], st[u], tick);
+        if (age > tb || (age == tb && atomicAdd(&tb_taken, 1) < tb_need)) {
+          const int j = atomicAdd(&nvict, 1);
+          if (j < need) vict[j] = h0 + u * THREADS;
+        }
       }
     }
     __syncthreads();
@@ -141,22 +171,49 @@ __global__ void __launch_bounds__(THREADS) resolve_kernel(HsParams p) {
   {
     const int warp = tid >> 5, lane = tid & 31, chunks = p.row_bytes >> 4;
     const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
-    for (int j = warp; j < nv; j += THREADS / 32) {
-      const int32_t pos = miss[j];
-      const int64_t crow = static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63);
-      const uint4* src = reinterpret_cast<const uint4*>(p.cold + crow * p.row_bytes);
-      uint4* dst = reinterpret_cast<uint4*>(p.hot + (slot * p.H + vict[j]) * p.row_bytes);
-      for (int c = lane; c < chunks; c += 32) dst[c] = src[c];
+    // a warp moves UNROLL rows per pass: their block-table entries, then all their 16-byte chunks, in flight
+    // together (host-memory reads are the longest latency here)
+    for (int j0 = warp; j0 < nv; j0 += UNROLL * (THREADS / 32)) {
+      int64_t crow[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const int j = j0 + u * (THREADS / 32);
+        crow[u] = -1;
+        if (j < nv) {
+          const int32_t pos = miss[j];
+          crow[u] = static_cast<int64_t>(bt[pos >> 6]) * 64 + (pos & 63);
+        }
+      }
+      for (int c = lane; c < chunks; c += 32) {
+        uint4 v[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u)
+          if (crow[u] >= 0) v[u] = reinterpret_cast<const uint4*>(p.cold + crow[u] * p.row_bytes)[c];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u)
+          if (crow[u] >= 0)
+            reinterpret_cast<uint4*>(p.hot + (slot * p.H + vict[j0 + u * (THREADS / 32)]) * p.row_bytes)[c] = v[u];
+      }
     }
   }
   // 5. rewritten top-k, hot block-table row, causal-safe length
   int32_t* out = p.topk_out + qs * p.K;
-  for (int64_t e = tid; e < n; e += THREADS) {
-    const int64_t qpos = seq - ql + e / p.K;
-    const int32_t pos = tk[e];
-    int32_t h = -1;
-    if (pos >= 0 && pos <= qpos && pos < p.P) h = max(p2s[pos], -1);
-    out[e] = h;
+  for (int64_t e0 = tid; e0 < n; e0 += UNROLL * THREADS) {
+    int32_t pos[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int64_t e = e0 + u * THREADS;
+      pos[u] = -1;
+      if (e < n) {
+        const int32_t q = tk[e];
+        if (q >= 0 && q <= seq - ql + e / p.K && q < p.P) pos[u] = q;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int64_t e = e0 + u * THREADS;
+      if (e < n) out[e] = pos[u] >= 0 ? max(p2s[pos[u]], -1) : -1;
+    }
   }
   const int hb = p.H / 64;
   for (int j = tid; j < hb; j += THREADS) p.hot_bt[static_cast<int64_t>(b) * hb + j] = static_cast<int32_t>(slot * hb + j);
