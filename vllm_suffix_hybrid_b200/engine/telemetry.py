@@ -97,6 +97,7 @@ class Telemetry(_Sink):
                "window_steps": w[0], "mean_accept_len": w[2] / w[1] if w[1] else 0.0,
                "device_ms_per_step": w[3] / w[0], "host_ms_per_step": w[4] / w[0],
                "proposer_us_per_step": w[5] / w[0], "running": len(engine.running), "waiting": len(engine.waiting),
+               "prefilling": int(getattr(engine, "prefilling", None) is not None),
                "proposer": engine.proposer_stats()}
         self.write(rec, to_log, to_file)
         self._window = [0, 0, 0, 0.0, 0.0, 0.0]

@@ -128,7 +128,11 @@ class AsyncEngine:
     def stats(self) -> dict:
         e = self.engine
         out = dict(self.metrics)
-        out.update({"running": len(e.running), "waiting": len(e.waiting)})
+        out.update({"running": len(e.running), "waiting": len(e.waiting),
+                    "prefilling": int(getattr(e, "prefilling", None) is not None)})
+        tier = getattr(e, "host_tier", None)
+        if tier is not None:
+            out["host_kv_hit_rate"] = tier.hit_rate()
         out.update(e.spec_stats())
         out["proposer"] = e.proposer_stats()
         return out
