@@ -119,6 +119,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int TCOLS = (2 * BN <= 128) ? 128 : (2 * BN <= 256 ? 256 : 512);
   if (threadIdx.x == 0) {
+    // fetch the tensor-map descriptors while the barriers and TMEM are set up
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmPK)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
     for (int s = 0; s < PS; ++s) {
       mbar_init(&pfull[s], 1);
       mbar_init(&pempty[s], 1);

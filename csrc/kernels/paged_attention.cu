@@ -182,6 +182,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int G = p.hq / p.hk;
   const int units = ntiles * p.hk * p.nsplit;
   if (threadIdx.x == 0) {
+    // fetch the tensor-map descriptors while the barriers are set up
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
     for (int st = 0; st < STAGES; ++st) {
       mbar_init(&full[st], 1);
       mbar_init(&empty[st], 4);
