@@ -328,6 +328,30 @@ PYBIND11_MODULE(_native, m) {
              std::lock_guard<std::mutex> lock(s.c->mu);
              s.c->corpus.set_n(n);
            })
+      .def("save",
+           [](PySuffixCache& s, const std::string& path) {
+             std::string err;
+             int64_t r;
+             {
+               std::lock_guard<std::mutex> lock(s.c->mu);
+               r = save_corpus(s.c->corpus, path, &err);
+             }
+             if (r < 0) throw std::runtime_error("suffix corpus snapshot: " + err);
+             return r;
+           },
+           "Write the corpus (its sequences, oldest first) to a snapshot file; returns the sequence count.")
+      .def("load",
+           [](PySuffixCache& s, const std::string& path) {
+             std::string err;
+             int64_t r;
+             {
+               std::lock_guard<std::mutex> lock(s.c->mu);
+               r = load_corpus(s.c->corpus, path, &err);
+             }
+             if (r < 0) throw std::runtime_error("suffix corpus restore: " + err);
+             return r;
+           },
+           "Add a snapshot's sequences (checked whole before any is added); returns the sequence count.")
       .def("stats", [](PySuffixCache& s) { return corpus_stats(s.c); });
 
   py::class_<Engine>(m, "Engine")

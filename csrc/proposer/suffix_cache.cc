@@ -1,5 +1,8 @@
 #include "suffix_cache.h"
 
+#include <cstdio>
+#include <cstring>
+
 #include <algorithm>
 #include <cmath>
 #include <stdexcept>
@@ -289,6 +292,107 @@ std::map<std::string, size_t> SuffixCorpus::stats() const {
       {"max_cached_requests", cfg_.sequences},
       {"max_cached_tokens", cfg_.tokens},
   };
+}
+
+namespace {
+
+constexpr char kSnapMagic[8] = {'S', 'H', 'C', 'O', 'R', 'P', '0', '1'};
+constexpr uint32_t kSnapVersion = 1;
+
+// FNV-1a, 64-bit (offset basis 14695981039346656037, prime 1099511628211).
+struct Fnv {
+  uint64_t h = 14695981039346656037ull;
+  void feed(const void* p, size_t n) {
+    const unsigned char* b = static_cast<const unsigned char*>(p);
+    for (size_t i = 0; i < n; ++i) h = (h ^ b[i]) * 1099511628211ull;
+  }
+};
+
+}  // namespace
+
+int64_t save_corpus(const SuffixCorpus& c, const std::string& path, std::string* err) {
+  const std::string tmp = path + ".tmp";
+  FILE* f = std::fopen(tmp.c_str(), "wb");
+  if (!f) {
+    if (err) *err = "cannot open " + tmp + " for writing";
+    return -1;
+  }
+  Fnv fnv;
+  bool ok = std::fwrite(kSnapMagic, 1, sizeof(kSnapMagic), f) == sizeof(kSnapMagic);
+  auto put = [&](const void* p, size_t n) {
+    if (!ok) return;
+    ok = std::fwrite(p, 1, n, f) == n;
+    fnv.feed(p, n);
+  };
+  const uint32_t version = kSnapVersion, n = static_cast<uint32_t>(c.cfg().n);
+  const uint64_t count = c.sequences().size();
+  put(&version, sizeof(version));
+  put(&n, sizeof(n));
+  put(&count, sizeof(count));
+  for (const auto& seq : c.sequences()) {
+    const uint64_t len = seq.size();
+    put(&len, sizeof(len));
+    put(seq.data(), len * sizeof(int64_t));
+  }
+  if (ok) ok = std::fwrite(&fnv.h, 1, sizeof(fnv.h), f) == sizeof(fnv.h);
+  ok = (std::fclose(f) == 0) && ok;
+  if (!ok || std::rename(tmp.c_str(), path.c_str()) != 0) {
+    std::remove(tmp.c_str());
+    if (err) *err = "cannot write " + path;
+    return -1;
+  }
+  return static_cast<int64_t>(count);
+}
+
+int64_t load_corpus(SuffixCorpus& c, const std::string& path, std::string* err) {
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) {
+    if (err) *err = "cannot open " + path;
+    return -1;
+  }
+  std::vector<unsigned char> buf;
+  unsigned char chunk[1 << 16];
+  size_t got;
+  while ((got = std::fread(chunk, 1, sizeof(chunk), f)) > 0) buf.insert(buf.end(), chunk, chunk + got);
+  std::fclose(f);
+  auto fail = [&](const char* why) -> int64_t {
+    if (err) *err = path + ": " + why;
+    return -1;
+  };
+  const size_t head = sizeof(kSnapMagic) + 4 + 4 + 8;
+  if (buf.size() < head + 8 || std::memcmp(buf.data(), kSnapMagic, sizeof(kSnapMagic)) != 0)
+    return fail("not a corpus snapshot");
+  Fnv fnv;
+  fnv.feed(buf.data() + sizeof(kSnapMagic), buf.size() - sizeof(kSnapMagic) - 8);
+  uint64_t sum;
+  std::memcpy(&sum, buf.data() + buf.size() - 8, 8);
+  if (sum != fnv.h) return fail("checksum mismatch");
+  uint32_t version;
+  uint64_t count;
+  std::memcpy(&version, buf.data() + sizeof(kSnapMagic), 4);
+  std::memcpy(&count, buf.data() + sizeof(kSnapMagic) + 8, 8);
+  if (version != kSnapVersion) return fail("unsupported snapshot version");
+  // walk the sequence table once to check every length before anything is added
+  std::vector<std::pair<size_t, uint64_t>> spans;  // (byte offset of the tokens, length)
+  size_t off = head;
+  const size_t end = buf.size() - 8;
+  for (uint64_t i = 0; i < count; ++i) {
+    if (end - off < 8) return fail("truncated sequence table");
+    uint64_t len;
+    std::memcpy(&len, buf.data() + off, 8);
+    off += 8;
+    if (len > (end - off) / sizeof(int64_t)) return fail("truncated sequence");
+    spans.emplace_back(off, len);
+    off += len * sizeof(int64_t);
+  }
+  if (off != end) return fail("trailing bytes");
+  std::vector<int64_t> toks;
+  for (const auto& sp : spans) {
+    toks.resize(sp.second);
+    std::memcpy(toks.data(), buf.data() + sp.first, sp.second * sizeof(int64_t));
+    c.add(toks);
+  }
+  return static_cast<int64_t>(count);
 }
 
 }  // namespace sh

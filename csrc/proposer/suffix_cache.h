@@ -48,6 +48,8 @@ class SuffixCorpus {
 
   std::map<std::string, size_t> stats() const;
   size_t cached_tokens() const { return tokens_; }
+  // The held sequences in FIFO order, oldest first (what a snapshot stores).
+  const std::deque<std::vector<int64_t>>& sequences() const { return seqs_; }
   const CacheConfig& cfg() const { return cfg_; }
   CacheConfig& mutable_cfg() { return cfg_; }
 
@@ -94,5 +96,16 @@ struct SharedCorpus {
 
 // Window hashing shared with the in-request n-gram index.
 uint64_t window_hash(const int64_t* w, size_t n);
+
+// Corpus snapshot, so the corpus survives a restart.  File layout (little-endian):
+//   "SHCORP01" | u32 version (1) | u32 window n at save | u64 sequence count |
+//   per sequence: u64 length, length x i64 tokens | u64 FNV-1a 64 of every byte after the magic
+// save writes `path`.tmp and renames it over `path` (a crash leaves the old snapshot whole) and returns the
+// number of sequences written.  load reads and checks the whole file before it touches the corpus, then adds
+// the sequences oldest first through the normal ingest path (the corpus bounds and eviction apply) and
+// returns how many it added; a missing, truncated or corrupt file leaves the corpus unchanged and reports
+// the reason in *err (return -1).
+int64_t save_corpus(const SuffixCorpus& c, const std::string& path, std::string* err);
+int64_t load_corpus(SuffixCorpus& c, const std::string& path, std::string* err);
 
 }  // namespace sh

@@ -25,6 +25,7 @@ from __future__ import annotations
 
 import itertools
 import logging
+import os
 import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
@@ -198,6 +199,12 @@ class LLMEngine:
         from ..tune.mtp_tune import MtpTuner
 
         self.tuner = MtpTuner.from_env(self)  # SUFFIX_MTP_TUNE=1: adapters attach before any graph capture
+        # SUFFIX_HYBRID_CORPUS_FILE: the suffix corpus is restored from this snapshot at start (when it exists)
+        # and written back by save_corpus() (the HTTP server does so at shutdown)
+        self.corpus_file = os.environ.get("SUFFIX_HYBRID_CORPUS_FILE") or None
+        if self.corpus_file and os.path.exists(self.corpus_file) and self._corpus_caches():
+            n = self.load_corpus(self.corpus_file)
+            logger.warning("suffix corpus restored from %s: %d sequences", self.corpus_file, n)
         from ..tune.sft import SftTrainer
 
         self.sft = SftTrainer.from_env(self)  # SUFFIX_SFT=1: adapters on the served model, before capture
@@ -352,10 +359,34 @@ class LLMEngine:
         r.polled = len(r.output)
         return new, r.finished, r.finish_reason
 
+    def _corpus_caches(self) -> list:
+        return [c for c in (getattr(self.proposer, "suffix_cache", None),
+                            getattr(self.async_proposer, "suffix_cache", None)) if c is not None]
+
+    def save_corpus(self, path: Optional[str] = None) -> int:
+        """Snapshot the proposer's suffix corpus (every held sequence, oldest first) to `path` (default:
+        SUFFIX_HYBRID_CORPUS_FILE), written to a temporary file and renamed over it; returns the count."""
+        path = path or self.corpus_file
+        caches = self._corpus_caches()
+        if not path or not caches:
+            raise RuntimeError("save_corpus needs a path and a suffix-corpus proposer")
+        return int(caches[0].save(path))
+
+    def load_corpus(self, path: Optional[str] = None) -> int:
+        """Add a snapshot's sequences to every suffix corpus of the proposers (the file is checked whole
+        before anything is added; the corpus bounds apply); returns the count."""
+        path = path or self.corpus_file
+        caches = self._corpus_caches()
+        if not path or not caches:
+            raise RuntimeError("load_corpus needs a path and a suffix-corpus proposer")
+        n = 0
+        for c in caches:
+            n = int(c.load(path))
+        return n
+
     def warm_start(self, sequences) -> int:
         """Pre-fill the proposer's suffix corpus with token histories (same path as a departing request)."""
-        caches = [c for c in (getattr(self.proposer, "suffix_cache", None),
-                              getattr(self.async_proposer, "suffix_cache", None)) if c is not None]
+        caches = self._corpus_caches()
         if not caches:
             raise RuntimeError(f"warm start needs a suffix-corpus proposer (method {self.cfg.spec.method!r})")
         n = 0

@@ -61,6 +61,12 @@ class AsyncEngine:
         self._ops.put(EngineOp("stop"))
         if self._thread is not None:
             self._thread.join(timeout=60)
+        e = self.engine
+        if getattr(e, "corpus_file", None) and e._corpus_caches():  # keep the corpus for the next start
+            try:
+                logger.warning("suffix corpus saved to %s: %d sequences", e.corpus_file, e.save_corpus())
+            except RuntimeError as err:
+                logger.warning("suffix corpus not saved: %s", err)
 
     def new_rid(self) -> str:
         with self._lock:
