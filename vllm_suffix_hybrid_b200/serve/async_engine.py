@@ -47,6 +47,10 @@ class AsyncEngine:
         self._thread: Optional[threading.Thread] = None
         self._running = False
         self._counter = 0
+        from ..parallel.health import RankHealth
+
+        # lockstep ranks share a failure flag in the rendezvous store, tested between steps
+        self.health = RankHealth.from_process_group() if world > 1 else RankHealth()
         self.metrics = {"requests_total": 0, "requests_finished": 0, "requests_aborted": 0,
                         "generated_tokens_total": 0, "decode_steps_total": 0, "prefill_steps_total": 0,
                         "step_seconds_total": 0.0, "warm_start_sequences_total": 0}
@@ -159,8 +163,12 @@ class AsyncEngine:
             return ops
         import torch.distributed as dist
 
+        self.health.check()  # a peer that recorded a failure is not waited for
         box = [ops]
-        dist.broadcast_object_list(box, src=0, group=self.cpu_group)
+        try:
+            dist.broadcast_object_list(box, src=0, group=self.cpu_group)
+        except Exception as err:  # a peer left: the collective's timeout or a closed connection
+            raise self.health.explain(err) from err
         return box[0]
 
     def _apply(self, ops: List[EngineOp]) -> bool:
@@ -281,6 +289,7 @@ class AsyncEngine:
                 st = e.step()
             except Exception as ex:  # a failed step fails every live request
                 logger.exception("engine step failed")
+                self.health.report(f"engine step failed: {ex!r}")  # the peers stop instead of waiting
                 with self._lock:
                     rids = list(self._streams)
                 for rid in rids:
