@@ -49,8 +49,9 @@ class AsyncEngine:
         self._counter = 0
         from ..parallel.health import RankHealth
 
-        # lockstep ranks share a failure flag in the rendezvous store, tested between steps
-        self.health = RankHealth.from_process_group() if world > 1 else RankHealth()
+        # lockstep ranks share a failure flag in the rendezvous store, tested every 8th step (one store round
+        # trip); a failed collective in between is explained from the same flag
+        self.health = RankHealth.from_process_group(every=8) if world > 1 else RankHealth()
         self.metrics = {"requests_total": 0, "requests_finished": 0, "requests_aborted": 0,
                         "generated_tokens_total": 0, "decode_steps_total": 0, "prefill_steps_total": 0,
                         "step_seconds_total": 0.0, "warm_start_sequences_total": 0}
