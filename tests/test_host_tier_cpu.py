@@ -34,3 +34,47 @@ def test_tier_is_refused_where_it_cannot_apply(name):
                        max_num_seqs=2, device="cpu")
     with pytest.raises(ValueError, match="host KV tier"):
         LLMEngine(cfg)
+
+
+def _state(P=2048, H=128):
+    import numpy as np
+
+    return np.full(P, -1, dtype=np.int64), np.full(H, -1, dtype=np.int64), np.zeros(H, dtype=np.int64)
+
+
+def test_reference_resolver_lru_and_rewrite():
+    """The policy the kernel implements (same scenario as the GPU test): C evicts A, the least recently used,
+    not B; B is then all hits; a rewritten resident position is fetched again."""
+    import numpy as np
+
+    from vllm_suffix_hybrid_b200.engine.host_tier import resolve_reference
+
+    p2s, s2p, stp = _state()
+    A, B, C = np.arange(0, 64), np.arange(100, 164), np.arange(200, 264)
+    q = np.array([999])
+    for tick, keys in ((1, A), (2, B)):
+        out, hits, fetched, ovf = resolve_reference(p2s, s2p, stp, tick, keys[None], q)
+        assert hits == 0 and len(fetched) == 64 and not ovf
+        assert (s2p[out[0]] == keys).all()  # every key's row holds it
+    out, hits, fetched, ovf = resolve_reference(p2s, s2p, stp, 3, C[None], q)
+    assert fetched == C.tolist() and (p2s[A] == -1).all() and (p2s[B] >= 0).all()
+    out, hits, fetched, ovf = resolve_reference(p2s, s2p, stp, 4, B[None], q)
+    assert hits == 64 and fetched == []
+    out, hits, fetched, ovf = resolve_reference(p2s, s2p, stp, 5, B[None], np.array([120]), written=[120])
+    assert fetched == [120] and hits == 20  # keys 100..120 are causal; 120 was rewritten
+    assert (out[0][B > 120] == -1).all()
+
+
+def test_reference_resolver_dedups_and_flags_overflow():
+    import numpy as np
+
+    from vllm_suffix_hybrid_b200.engine.host_tier import resolve_reference
+
+    p2s, s2p, stp = _state(H=64)
+    keys = np.stack([np.arange(0, 64), np.arange(32, 96)])  # 96 distinct keys over two query tokens
+    out, hits, fetched, ovf = resolve_reference(p2s, s2p, stp, 1, keys, np.array([500, 501]))
+    assert ovf and len(fetched) == 64 and len(set(fetched)) == 64
+    p2s, s2p, stp = _state(H=64)
+    keys = np.stack([np.arange(0, 64), np.arange(0, 64)[::-1]])  # shared keys fetch once
+    out, hits, fetched, ovf = resolve_reference(p2s, s2p, stp, 1, keys, np.array([500, 501]))
+    assert not ovf and len(fetched) == 64 and (out[0] == out[1][::-1]).all()

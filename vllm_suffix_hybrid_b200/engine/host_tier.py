@@ -31,6 +31,49 @@ def hot_rows_for(k: int, topk: int) -> int:
     return int(min(MAX_HOT_ROWS, -(-need // 64) * 64))
 
 
+def resolve_reference(pos2slot, slot2pos, stamp, tick: int, topk, qpos, written=()):
+    """CPU statement of one request's resolve, the policy of `csrc/kernels/hisparse.cu` (numpy int arrays of
+    one request slot, updated in place).
+
+    topk [T, K] key positions of the request's T query tokens (-1: none), qpos [T] their positions, written
+    the positions the step writes.  Returns (hot [T, K] hot-row indices or -1, hits, fetched positions in
+    claim order, overflow).  Victims are the rows no key of this step uses, free rows first, then by age
+    (tick - stamp) capped at 255 steps, oldest first; the kernel takes rows of the threshold age in any
+    order, this statement by row index."""
+    import numpy as np
+
+    H = slot2pos.shape[0]
+    for p in written:  # rewritten positions lose their hot copy
+        if 0 <= p < pos2slot.shape[0] and pos2slot[p] >= 0:
+            slot2pos[pos2slot[p]] = -1
+            pos2slot[p] = -1
+    topk = np.asarray(topk)
+    valid = (topk >= 0) & (topk <= np.asarray(qpos)[:, None]) & (topk < pos2slot.shape[0])
+    hits, miss = 0, []
+    claimed = set()
+    for p in topk[valid].tolist():
+        h = pos2slot[p]
+        if h >= 0:
+            stamp[h] = tick
+            hits += 1
+        elif p not in claimed:
+            claimed.add(p)
+            miss.append(p)
+    used = (slot2pos >= 0) & (stamp == tick)
+    age = np.where(slot2pos < 0, 255, np.clip(tick - stamp, 1, 255))
+    order = [h for h in sorted(range(H), key=lambda h: (-int(age[h]), h)) if not used[h]]
+    overflow = len(miss) > len(order)
+    fetched = []
+    for p, h in zip(miss, order):
+        if slot2pos[h] >= 0:
+            pos2slot[slot2pos[h]] = -1
+        slot2pos[h], stamp[h], pos2slot[p] = p, tick, h
+        fetched.append(p)
+    out = np.full(topk.shape, -1, dtype=np.int64)
+    out[valid] = np.maximum(pos2slot[topk[valid]], -1)
+    return out, hits, fetched, overflow
+
+
 class HostTierLayer:
     """One layer's view of the tier: its host cache, hot rows, residency maps and resolve outputs."""
 
