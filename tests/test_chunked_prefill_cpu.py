@@ -61,3 +61,16 @@ def test_abort_during_chunked_prefill_frees_its_blocks():
     assert eng.prefilling is None and eng.pool.free == free0
     assert eng.poll(rid)[1:] == (True, "abort")
     assert not eng.has_work()
+
+
+def test_recurrent_models_prefill_whole_and_data_parallel_is_excluded():
+    from vllm_suffix_hybrid_b200.engine.config import qwen3_next_config
+
+    m = shrink(qwen3_next_config(), layers=2, hidden=128, vocab=256)
+    eng = LLMEngine(_cfg(m, "none", True, budget=32))
+    rid = eng.add_request(np.arange(100) % 256, max_new_tokens=4)
+    assert not eng._chunkable(eng.waiting[0])  # GDN states prefill from the empty state only
+    st = eng.step()
+    assert st.kind == "prefill" and eng.prefilling is None and eng.running[0].rid == rid
+    with pytest.raises(ValueError, match="attention-only"):
+        eng.runner.prefill([np.arange(8)], [eng.running[0].blocks], [eng.running[0].slot], starts=[4])
