@@ -75,7 +75,8 @@ std::vector<std::vector<int64_t>> Engine::propose(const std::vector<char>& sampl
       row.index = NgramIndex(ngram_min_);
     }
     const size_t have = row.ctx.size();
-    row.ctx.reserve(n);
+    // geometric growth: a row that grows by a few tokens per call must not be copied whole every call
+    if (row.ctx.capacity() < n) row.ctx.reserve(std::max(n, row.ctx.capacity() + row.ctx.capacity() / 2));
     if (fast) {
       row.ctx.insert(row.ctx.end(), fast + have, fast + n);
     } else {
