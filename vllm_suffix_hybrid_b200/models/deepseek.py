@@ -17,7 +17,7 @@
 from __future__ import annotations
 
 import math
-from typing import List, Optional
+from typing import List
 
 import torch
 
