@@ -1,6 +1,6 @@
 """Headline benchmark: decode output tokens/s per box with k=5 hybrid speculation.
 
-Workload: Llama-3-8B-shaped decoder, bf16 random init
+Workload (benchmark config 1): Llama-3-8B-shaped decoder, bf16 random init
 N(0, 0.02), a 1-layer EAGLE-style draft head of the same width, k = 5 greedy
 hybrid speculation (native drafts mixed with the suffix corpus by the native
 mixer), 64 concurrent requests with synthetic 2048-token prompts (config-0

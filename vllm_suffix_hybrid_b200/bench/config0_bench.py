@@ -1,6 +1,6 @@
 """Config 0: the proposer loop on the CPU with a toy target that verifies.
 
-Workload: 16 rows of 8192-token histories built by the
+Workload (benchmark config 0): 16 rows of 8192-token histories built by the
 span-reuse generator (``bench.synthetic.make_streams``: segments that copy a
 U[16, 256] span from earlier in the row or from a shared 64-sequence corpus
 of 4096 Zipf(1.1) tokens with p = 0.4, else 32-128 i.i.d. Zipf tokens),
