@@ -111,6 +111,20 @@ def test_warm_start_and_metrics(server):
     assert st["requests_finished"] >= 1 and "proposer" in st
 
 
+def test_corpus_save_route(server, tmp_path):
+    from vllm_suffix_hybrid_b200 import _native
+
+    client, aeng = server
+    client.post("/debug/warm-start", json={"sequences": [[3, 1, 4, 1, 5, 9, 2, 6] * 4]})
+    path = str(tmp_path / "corpus.bin")
+    r = client.post("/debug/corpus-save", json={"path": path})
+    n = aeng.engine.proposer.suffix_cache.stats()["num_sequences"]
+    assert r.status_code == 200 and r.json() == {"saved": n, "path": path} and n >= 1
+    assert _native.SuffixCache().load(path) == n
+    assert client.post("/debug/corpus-save", json={}).status_code == 400  # no path and no default file
+    assert client.post("/debug/corpus-save", json={"path": str(tmp_path / "no" / "dir.bin")}).status_code == 409
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

@@ -9,6 +9,8 @@ Routes:
   POST /debug/warm-start      {"sequences": [[ids...], ...]} -> {"ingested": N}; only with
                               SUFFIX_HYBRID_WARMSTART=1 (the reference's route and gate,
                               reference: suffix_hybrid/warmstart.py)
+  POST /debug/corpus-save     {"path": optional} -> {"saved": N, "path": p}: snapshot of the suffix
+                              corpus (default path SUFFIX_HYBRID_CORPUS_FILE); same gate
 Decoding is greedy (the verify step is the greedy accept run); a request
 with temperature > 0 is rejected with 400.
 """
@@ -162,6 +164,21 @@ def build_app(aeng, tokenizer, model_name: str) -> FastAPI:
             except Exception as ex:
                 return JSONResponse(status_code=409, content={"error": str(ex)})
             return {"ingested": n}
+
+        @app.post("/debug/corpus-save")
+        async def corpus_save(request: Request):
+            try:
+                body = await request.json()
+            except Exception:
+                body = {}
+            path = (body or {}).get("path") or getattr(aeng.engine, "corpus_file", None)
+            if not isinstance(path, str) or not path:
+                return JSONResponse(status_code=400, content={"error": "no path (body or SUFFIX_HYBRID_CORPUS_FILE)"})
+            try:
+                n = await aeng.save_corpus(path)
+            except Exception as ex:
+                return JSONResponse(status_code=409, content={"error": str(ex)})
+            return {"saved": n, "path": path}
 
     if getattr(aeng.engine, "sft", None) is not None:
         from .sft_api import attach as attach_sft

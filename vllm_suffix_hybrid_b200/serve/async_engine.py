@@ -27,7 +27,7 @@ logger = logging.getLogger("suffix_hybrid.serve")
 
 @dataclass
 class EngineOp:
-    kind: str  # "add" | "abort" | "warm" | "readout" | "stop"
+    kind: str  # "add" | "abort" | "warm" | "corpus_save" | "readout" | "stop"
     rid: str = ""
     prompt: List[int] = field(default_factory=list)
     max_new_tokens: int = 0
@@ -111,6 +111,16 @@ class AsyncEngine:
         with self._lock:
             self._futures[key] = (loop, fut)
         self._ops.put(EngineOp("warm", key, sequences=[[int(t) for t in s] for s in sequences]))
+        return await fut
+
+    async def save_corpus(self, path: Optional[str] = None) -> int:
+        """Snapshot the suffix corpus on the engine thread (rank 0 writes the file); returns the count."""
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        key = f"corpus-{self.new_rid()}"
+        with self._lock:
+            self._futures[key] = (loop, fut)
+        self._ops.put(EngineOp("corpus_save", key, payload=path))
         return await fut
 
     async def readout(self, prompt: List[int], rows) -> List[float]:
@@ -211,6 +221,11 @@ class AsyncEngine:
                     n = e.warm_start(op.sequences)
                     self.metrics["warm_start_sequences_total"] += n
                     self._resolve(op.rid, n)
+                except Exception as ex:
+                    self._resolve(op.rid, ex)
+            elif op.kind == "corpus_save" and self.rank == 0:  # the ranks' corpora are identical in lockstep
+                try:
+                    self._resolve(op.rid, e.save_corpus(op.payload))
                 except Exception as ex:
                     self._resolve(op.rid, ex)
         return True
