@@ -268,7 +268,7 @@ class LLMEngine:
             self._synthetic_cache = True
         rids = []
         for p in prompts:
-            if len(self.running) >= self.cfg.max_num_seqs:
+            if len(self.running) + (self.prefilling is not None) >= self.cfg.max_num_seqs:
                 raise RuntimeError("admit_prefilled: more requests than max_num_seqs")
             rid = self.add_request(p, max_new_tokens)
             r = self.waiting.pop()
